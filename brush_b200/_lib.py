@@ -1,0 +1,205 @@
+"""ctypes binding of the C ABI declared in ``include/bsx.h``.
+
+The shared library is loaded from the package directory (``brush_b200/libbsx.so``,
+built by ``brush_b200/build.py``). There is no fallback: if the library is
+missing or cannot be loaded, every entry point raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libbsx.so"
+
+BSX_COMPACT_GRAD_LANES = 11
+BSX_GRAD_STRIDE = 12
+BSX_PROJECTED_LANES = 12
+BSX_TILE_WIDTH = 16
+
+STATUS_NAMES = {
+    0: "BSX_OK",
+    1: "BSX_ERR_INVALID_ARG",
+    2: "BSX_ERR_SHAPE",
+    3: "BSX_ERR_CAPACITY",
+    4: "BSX_ERR_DEVICE_TIMEOUT",
+    5: "BSX_ERR_CUDA",
+    6: "BSX_ERR_STATE",
+    7: "BSX_ERR_UNSUPPORTED",
+}
+
+RENDER_DEFAULT, RENDER_MIP = 0, 1
+PASS_FORWARD, PASS_BACKWARD, PASS_BACKWARD_SMOOTH_CUTOFF = 0, 1, 2
+
+
+class BsxError(RuntimeError):
+    """A bsx entry point returned a non-OK status."""
+
+    def __init__(self, status: int, message: str):
+        self.status = status
+        super().__init__(f"{STATUS_NAMES.get(status, status)}: {message}")
+
+
+class Camera(C.Structure):
+    _fields_ = [
+        ("fov_x", C.c_double),
+        ("fov_y", C.c_double),
+        ("center_uv", C.c_float * 2),
+        ("position", C.c_float * 3),
+        ("rotation", C.c_float * 4),
+        ("camera_model", C.c_int32),
+    ]
+
+
+class ProjectUniforms(C.Structure):
+    _fields_ = [
+        ("viewmat", C.c_float * 12),
+        ("fx", C.c_float),
+        ("fy", C.c_float),
+        ("cx", C.c_float),
+        ("cy", C.c_float),
+        ("camera_pos", C.c_float * 3),
+        ("half_max_render_fov", C.c_float),
+        ("lim_pos_x", C.c_float),
+        ("lim_pos_y", C.c_float),
+        ("lim_neg_x", C.c_float),
+        ("lim_neg_y", C.c_float),
+        ("img_w", C.c_uint32),
+        ("img_h", C.c_uint32),
+        ("tile_bw", C.c_uint32),
+        ("tile_bh", C.c_uint32),
+        ("sh_degree", C.c_uint32),
+        ("total_splats", C.c_uint32),
+        ("num_visible", C.c_uint32),
+    ]
+
+
+class RenderOut(C.Structure):
+    _fields_ = [
+        ("d_image", C.c_void_p),
+        ("d_image_packed", C.c_void_p),
+        ("d_visible", C.c_void_p),
+        ("d_max_radius", C.c_void_p),
+        ("d_tile_offsets", C.c_void_p),
+        ("d_projected", C.c_void_p),
+        ("d_isect_gid", C.c_void_p),
+        ("d_isect_tile", C.c_void_p),
+        ("d_depth_order", C.c_void_p),
+        ("d_tile_counts", C.c_void_p),
+        ("d_cum_counts", C.c_void_p),
+        ("num_visible", C.c_uint32),
+        ("num_intersections", C.c_uint32),
+        ("tile_bw", C.c_uint32),
+        ("tile_bh", C.c_uint32),
+        ("uniforms", ProjectUniforms),
+    ]
+
+
+class LossCfg(C.Structure):
+    _fields_ = [
+        ("l1_weight", C.c_float),
+        ("ssim_weight", C.c_float),
+        ("composite_bg", C.c_int32),
+        ("bg", C.c_float * 3),
+        ("mask", C.c_int32),
+    ]
+
+
+class AdamGroup(C.Structure):
+    _fields_ = [
+        ("d_param", C.c_void_p),
+        ("d_grad", C.c_void_p),
+        ("d_m", C.c_void_p),
+        ("d_v", C.c_void_p),
+        ("rows", C.c_uint32),
+        ("cols", C.c_uint32),
+        ("lr", C.c_float),
+        ("h_col_scale", C.POINTER(C.c_float)),
+        ("reduce_moment_2", C.c_int32),
+    ]
+
+
+class AdamCfg(C.Structure):
+    _fields_ = [
+        ("beta_1", C.c_float),
+        ("beta_2", C.c_float),
+        ("epsilon", C.c_float),
+        ("step", C.c_uint32),
+        ("grad_scale", C.c_float),
+    ]
+
+
+# name -> (restype, argtypes); exactly the functions include/bsx.h declares.
+SIGNATURES = {
+    "bsx_create": (C.c_int, [C.c_int, C.POINTER(C.c_void_p)]),
+    "bsx_destroy": (C.c_int, [C.c_void_p]),
+    "bsx_set_stream": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "bsx_sync": (C.c_int, [C.c_void_p]),
+    "bsx_last_error": (C.c_char_p, [C.c_void_p]),
+    "bsx_status_string": (C.c_char_p, [C.c_int]),
+    "bsx_abi_version": (C.c_int, []),
+    "bsx_launch_count": (C.c_uint64, [C.c_void_p]),
+    "bsx_profile_enable": (C.c_int, [C.c_void_p, C.c_int32]),
+    "bsx_profile_collect": (C.c_int, [C.c_void_p]),
+    "bsx_profile_count": (C.c_int32, [C.c_void_p]),
+    "bsx_profile_entry": (
+        C.c_int, [C.c_void_p, C.c_int32, C.POINTER(C.c_char_p), C.POINTER(C.c_double), C.POINTER(C.c_uint64)]
+    ),
+    "bsx_profile_reset": (C.c_int, [C.c_void_p]),
+    "bsx_make_project_uniforms": (
+        C.c_int,
+        [C.POINTER(Camera), C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.POINTER(ProjectUniforms)],
+    ),
+    "bsx_render_fwd": (
+        C.c_int,
+        [C.c_void_p, C.POINTER(Camera), C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32,
+         C.c_uint32, C.c_int32, C.c_int32, C.POINTER(C.c_float), C.POINTER(RenderOut)],
+    ),
+    "bsx_rasterize_bwd": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p]),
+    "bsx_project_bwd": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "bsx_loss_fwd": (
+        C.c_int,
+        [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32, C.POINTER(LossCfg), C.c_void_p],
+    ),
+    "bsx_loss_bwd": (
+        C.c_int,
+        [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32, C.POINTER(LossCfg), C.c_void_p,
+         C.c_void_p],
+    ),
+    "bsx_loss_fused": (
+        C.c_int,
+        [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.POINTER(LossCfg), C.c_void_p, C.c_void_p],
+    ),
+    "bsx_adam_step": (C.c_int, [C.c_void_p, C.POINTER(AdamGroup), C.c_int32, C.POINTER(AdamCfg)]),
+    "bsx_radix_argsort_u32": (
+        C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p]
+    ),
+    "bsx_prefix_sum_u32": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32, C.c_void_p]),
+    "bsx_get_tile_offsets": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p]),
+}
+
+_LIB = None
+
+
+def lib() -> C.CDLL:
+    """Load ``libbsx.so`` once; raise if it is absent (there is no CPU path)."""
+    global _LIB
+    if _LIB is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(
+                f"{LIB_PATH} is missing: build it with `python brush_b200/build.py` "
+                "(the B200 CUDA library is required; there is no fallback)"
+            )
+        handle = C.CDLL(os.fspath(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        _LIB = handle
+    return _LIB
+
+
+def check(status: int, ctx=None) -> None:
+    if status != 0:
+        msg = lib().bsx_last_error(ctx).decode() if ctx else lib().bsx_status_string(status).decode()
+        raise BsxError(status, msg)

@@ -1,0 +1,207 @@
+// project_fwd.cu - fused cull / project / SH colour / visible compaction.
+//
+// One thread per splat, 256 splats per block. Restates, in one pass,
+// project_forward_kernel (crates/brush-render/src/kernels/project_forward.rs:20-144)
+// and project_visible_kernel (kernels/project_visible.rs:22-89): the cull
+// predicates, the EWA covariance, the StopThePop per-tile count, and the SH
+// colour of every surviving splat. Where the reference appends visible ids
+// with an atomic counter (order depends on scheduling), blocks here take
+// tickets and compact with a decoupled look-back, so the visible list is in
+// global-id order on every run.
+//
+// Outputs (global-id indexed unless noted):
+//   projected[N,12]  rows {x, y, conic00, conic01, conic11, opacity, r, g, b,
+//                    depth, ln(255*opacity), 0}; written for visible splats only
+//   counts[N]        contributing-tile count (0 when culled)
+//   max_radius[N]    max(ex/W, ey/H) (0 when culled)
+//   vis_gid[V], depth_key[V]  compacted visible ids and depth bits, id order
+//   scalars[0] = V, scalars[1] = total intersections (u32, wraps as the reference)
+#include "lookback.cuh"
+#include "sh.cuh"
+
+namespace bsx {
+
+namespace {
+
+constexpr int kProjThreads = 256;
+
+struct ProjArgs {
+    const float* transforms;
+    const float* sh;
+    const float* raw_opac;
+    uint32_t n;
+    uint32_t coeffs;
+    int mip;
+    Uni u;
+    float* projected;
+    uint32_t* counts;
+    float* max_radius;
+    uint32_t* vis_gid;
+    uint32_t* depth_key;
+    uint32_t* scalars;
+    uint64_t* status;
+    uint32_t* ticket;
+    int* err;
+};
+
+template <int DEG>
+__global__ void __launch_bounds__(kProjThreads) project_fwd_kernel(const ProjArgs a) {
+    __shared__ uint32_t s_tile;
+    __shared__ uint32_t s_warp_vis[kProjThreads / 32];
+    __shared__ uint32_t s_warp_hits[kProjThreads / 32];
+    __shared__ uint32_t s_base;
+    if (threadIdx.x == 0) s_tile = atomicAdd(a.ticket, 1u);
+    __syncthreads();
+    const uint32_t tile = s_tile;
+    const uint32_t g = tile * kProjThreads + threadIdx.x;
+    const Uni& u = a.u;
+
+    bool visible = false;
+    uint32_t hits = 0;
+    float depth = 0.0f;
+    float radius = 0.0f;
+    if (g < a.n) {
+        do {
+            const float* t = a.transforms + (size_t)g * 10;
+            V3 mean = v3(__ldg(t), __ldg(t + 1), __ldg(t + 2));
+            V3 mean_c = vadd(mmul(u.rot, mean), u.trans);
+            if (!(vfinite(mean_c) && mean_c.z <= 1.0e10f)) break;
+            if (mean_c.z < 0.01f) break;
+            V3 scl = v3(bsx_expf(__ldg(t + 7)), bsx_expf(__ldg(t + 8)), bsx_expf(__ldg(t + 9)));
+            if (!vfinite(scl)) break;
+            Q4 qu{__ldg(t + 3), __ldg(t + 4), __ldg(t + 5), __ldg(t + 6)};
+            float qn = qdot(qu, qu);
+            if (!(qn >= 1.0e-6f && bsx_is_finite(qn))) break;
+            float ro = __ldg(a.raw_opac + g);
+            if (!bsx_is_finite(ro)) break;
+            Q4 q = qnormalize(qu);
+            S2 raw = calc_cov2d(scl, q, mean_c, u);
+            float fc;
+            S2 cov = compensate_cov2d(raw, a.mip != 0, &fc);
+            float opac = bsx_sigmoid(ro) * fc;
+            if (!s2finite(cov)) break;
+            float inv_z = 1.0f / mean_c.z;
+            float m2x = u.fx * mean_c.x * inv_z + u.cx;
+            float m2y = u.fy * mean_c.y * inv_z + u.cy;
+            if (!(opac >= 1.0f / 255.0f)) break;
+            float pt = bsx_logf(opac * 255.0f);
+            S2 conic = sym2_inverse(cov);
+            float ex, ey;
+            bbox_extent(conic, pt, &ex, &ey);
+            if (!(ex >= 0.0f && ey >= 0.0f)) break;
+            float wf = (float)u.w, hf = (float)u.h;
+            bool on_screen = m2x + ex > 0.0f && m2x - ex < wf && m2y + ey > 0.0f && m2y - ey < hf;
+            if (!on_screen) break;
+            TileBox bb = tile_bbox(m2x, m2y, ex, ey, u.tbw, u.tbh);
+            for (uint32_t ty = bb.min_y; ty < bb.max_y; ++ty)
+                for (uint32_t tx = bb.min_x; tx < bb.max_x; ++tx)
+                    if (tile_contrib(tx, ty, m2x, m2y, conic, pt)) ++hits;
+            visible = true;
+            depth = mean_c.z;
+            radius = bsx_max(ex / wf, ey / hf);
+            // SH colour at the normalised view direction (project_visible.rs:56-71).
+            V3 dv = vsub(mean, u.cam);
+            V3 vdir = vscale(dv, 1.0f / sqrtf(vdot(dv, dv)));
+            V3 col = sh_to_color<DEG>(a.sh + (size_t)g * a.coeffs * 3, vdir);
+            float cr = col.x + 0.5f, cg = col.y + 0.5f, cb = col.z + 0.5f;
+            cr = bsx_clamp(bsx_is_finite(cr) ? cr : 0.0f, -100.0f, 100.0f);
+            cg = bsx_clamp(bsx_is_finite(cg) ? cg : 0.0f, -100.0f, 100.0f);
+            cb = bsx_clamp(bsx_is_finite(cb) ? cb : 0.0f, -100.0f, 100.0f);
+            float4* row = reinterpret_cast<float4*>(a.projected + (size_t)g * BSX_PROJECTED_LANES);
+            row[0] = make_float4(m2x, m2y, conic.c00, conic.c01);
+            row[1] = make_float4(conic.c11, opac, cr, cg);
+            row[2] = make_float4(cb, mean_c.z, pt, 0.0f);
+        } while (false);
+        a.counts[g] = hits;
+        a.max_radius[g] = radius;
+    }
+
+    // Block-level compaction of visible ids + intersection total.
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint32_t vmask = __ballot_sync(0xffffffffu, visible);
+    uint32_t whits = hits;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) whits += __shfl_xor_sync(0xffffffffu, whits, o);
+    if (lane == 0) {
+        s_warp_vis[warp] = __popc(vmask);
+        s_warp_hits[warp] = whits;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        uint32_t wv = lane < kProjThreads / 32 ? s_warp_vis[lane] : 0u;
+        uint32_t wh = lane < kProjThreads / 32 ? s_warp_hits[lane] : 0u;
+        uint32_t inc = wv;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            uint32_t tv = __shfl_up_sync(0xffffffffu, inc, o);
+            if (lane >= o) inc += tv;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) wh += __shfl_xor_sync(0xffffffffu, wh, o);
+        uint32_t block_vis = __shfl_sync(0xffffffffu, inc, 31);
+        if (lane < kProjThreads / 32) s_warp_vis[lane] = inc - wv;
+        uint32_t prefix = lookback_publish(a.status, tile, block_vis, a.err);
+        if (lane == 0) {
+            s_base = prefix;
+            if (wh) atomicAdd(a.scalars + 1, wh);
+            if ((uint64_t)(tile + 1) * kProjThreads >= a.n) a.scalars[0] = prefix + block_vis;
+        }
+    }
+    __syncthreads();
+    if (visible) {
+        uint32_t pos = s_base + s_warp_vis[warp] + __popc(vmask & ((1u << lane) - 1u));
+        if (pos < a.n) {
+            a.vis_gid[pos] = g;
+            a.depth_key[pos] = bsx_f32_to_bits(depth);
+        } else {
+            set_error(a.err, kDevOutOfRange);
+        }
+    }
+}
+
+}  // namespace
+
+bsx_status launch_project_fwd(bsx_ctx* ctx, const bsx_project_uniforms& uni, const float* transforms,
+                              const float* sh, const float* raw_opac, uint32_t n, uint32_t coeffs, int degree,
+                              int mip, float* projected, uint32_t* counts, float* max_radius, uint32_t* vis_gid,
+                              uint32_t* depth_key, uint32_t* scalars) {
+    const uint32_t tiles = (n + kProjThreads - 1) / kProjThreads;
+    bsx_status s = ensure(ctx, ctx->scan_status, scan_status_words(tiles) * sizeof(uint64_t));
+    if (s != BSX_OK) return s;
+    uint64_t* status = ctx->scan_status.as<uint64_t>();
+    s = check_cuda(ctx, cudaMemsetAsync(status, 0, scan_status_words(tiles) * sizeof(uint64_t), ctx->stream),
+                   "memset projection status");
+    if (s != BSX_OK) return s;
+    s = check_cuda(ctx, cudaMemsetAsync(scalars, 0, 2 * sizeof(uint32_t), ctx->stream), "memset scalars");
+    if (s != BSX_OK) return s;
+    ProjArgs a;
+    a.transforms = transforms;
+    a.sh = sh;
+    a.raw_opac = raw_opac;
+    a.n = n;
+    a.coeffs = coeffs;
+    a.mip = mip;
+    a.u = make_uni(uni);
+    a.projected = projected;
+    a.counts = counts;
+    a.max_radius = max_radius;
+    a.vis_gid = vis_gid;
+    a.depth_key = depth_key;
+    a.scalars = scalars;
+    a.status = status;
+    a.ticket = reinterpret_cast<uint32_t*>(status + tiles);
+    a.err = ctx->d_err;
+    if (degree < 0 || degree > 4) return fail(ctx, BSX_ERR_SHAPE, "sh coefficient count must be (degree+1)^2 with degree <= 4");
+    prof_begin(ctx);
+    switch (degree) {
+        case 0: project_fwd_kernel<0><<<tiles, kProjThreads, 0, ctx->stream>>>(a); break;
+        case 1: project_fwd_kernel<1><<<tiles, kProjThreads, 0, ctx->stream>>>(a); break;
+        case 2: project_fwd_kernel<2><<<tiles, kProjThreads, 0, ctx->stream>>>(a); break;
+        case 3: project_fwd_kernel<3><<<tiles, kProjThreads, 0, ctx->stream>>>(a); break;
+        case 4: project_fwd_kernel<4><<<tiles, kProjThreads, 0, ctx->stream>>>(a); break;
+        default: return fail(ctx, BSX_ERR_SHAPE, "sh coefficient count must be (degree+1)^2 with degree <= 4");
+    }
+    return post_launch(ctx, "project_fwd_kernel");
+}
+
+}  // namespace bsx

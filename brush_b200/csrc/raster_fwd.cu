@@ -1,0 +1,176 @@
+// raster_fwd.cu - tile rasterizer, forward.
+//
+// Restates rasterize_kernel (crates/brush-render/src/kernels/rasterize.rs:24-200):
+// one 256-thread block per 16x16 tile, one pixel per thread in the
+// reference's Morton order (helpers.rs:54-81, so each warp covers an 8x4
+// patch), front-to-back compositing over the tile's depth-sorted splats in
+// batches of 256 staged in shared memory. Per pair:
+//   sigma = 0.5*(c00 dx^2 + c11 dy^2) + c01 dx dy,  alpha = min(0.999, o e^-sigma)
+//   accept iff sigma >= 0 and alpha >= 1/255; stop before accumulating once
+//   T*(1-alpha) <= 1e-4.
+// B200 specifics: the block-wide early-out is a __syncthreads_count vote;
+// pairs whose sigma exceeds ln(255*o) + margin (where alpha < 1/255 is
+// certain) skip the exponential, which leaves every decision and every
+// accumulated value bit-identical; visibility marks are collected per batch
+// in shared memory and written once per splat instead of once per pixel.
+#include "splat_math.cuh"
+
+namespace bsx {
+
+namespace {
+
+constexpr int kRasterThreads = 256;
+// Rejection margin on sigma for the exponential-free pre-filter. With the
+// hard cutoff the exact test is sigma <= ln(255 o) up to a few ulp of the
+// shared exp/ln; the smooth ramp starts at alpha = 1/255 - 5e-4, i.e.
+// ln(255 o) + 0.137.
+constexpr float kMarginHard = 1.0e-3f;
+constexpr float kMarginSmooth = 0.25f;
+
+__device__ __forceinline__ uint32_t compact_bits_16(uint32_t v) {
+    uint32_t x = v & 0x55555555u;
+    x = (x | (x >> 1)) & 0x33333333u;
+    x = (x | (x >> 2)) & 0x0F0F0F0Fu;
+    x = (x | (x >> 4)) & 0x00FF00FFu;
+    x = (x | (x >> 8)) & 0x0000FFFFu;
+    return x;
+}
+
+__device__ __forceinline__ float cutoff_weight(float a) {
+    const float mid = 1.0f / 255.0f, band = 1.0e-3f;
+    float t = bsx_clamp((a - (mid - 0.5f * band)) / band, 0.0f, 1.0f);
+    return t * t * (3.0f - 2.0f * t);
+}
+
+struct FwdArgs {
+    const uint32_t* isect_gid;
+    uint32_t* tile_offsets;
+    const float* projected;
+    float* image;            // [H,W,4] when bwd_info
+    uint32_t* image_packed;  // [H,W] otherwise
+    float* visible;          // [N] when bwd_info
+    uint32_t tbw, w, h;
+    float bg_r, bg_g, bg_b;
+};
+
+template <bool BWD, bool SMOOTH>
+__global__ void __launch_bounds__(kRasterThreads) raster_fwd_kernel(const FwdArgs a) {
+    __shared__ float4 s_a[kRasterThreads];  // x, y, c00, c01
+    __shared__ float4 s_b[kRasterThreads];  // c11, opacity, r, g
+    __shared__ float4 s_c[kRasterThreads];  // b, depth, ln(255 o), 0
+    __shared__ uint32_t s_gid[BWD ? kRasterThreads : 1];
+    __shared__ int s_used[BWD ? kRasterThreads : 1];
+    __shared__ uint32_t s_max_useful;
+
+    const uint32_t tile = blockIdx.x;
+    const uint32_t tx = tile % a.tbw, ty = tile / a.tbw;
+    const uint32_t px = tx * kTile + compact_bits_16(threadIdx.x);
+    const uint32_t py = ty * kTile + compact_bits_16(threadIdx.x >> 1);
+    const bool inside = px < a.w && py < a.h;
+    const float pcx = (float)px + 0.5f, pcy = (float)py + 0.5f;
+    const uint32_t lo = a.tile_offsets[tile * 2], hi = a.tile_offsets[tile * 2 + 1];
+    if (BWD) {
+        if (threadIdx.x == 0) s_max_useful = lo;
+        __syncthreads();
+    }
+
+    float T = 1.0f, cr = 0.0f, cg = 0.0f, cb = 0.0f;
+    bool done = !inside;
+    uint32_t last = lo;
+    const float margin = SMOOTH ? kMarginSmooth : kMarginHard;
+
+    for (uint32_t batch = lo; batch < hi; batch += kRasterThreads) {
+        if (__syncthreads_count(done) == kRasterThreads) break;
+        const uint32_t n = min((uint32_t)kRasterThreads, hi - batch);
+        if (threadIdx.x < n) {
+            const uint32_t g = __ldg(a.isect_gid + batch + threadIdx.x);
+            const float4* row = reinterpret_cast<const float4*>(a.projected + (size_t)g * BSX_PROJECTED_LANES);
+            s_a[threadIdx.x] = __ldg(row);
+            s_b[threadIdx.x] = __ldg(row + 1);
+            s_c[threadIdx.x] = __ldg(row + 2);
+            if (BWD) {
+                s_gid[threadIdx.x] = g;
+                s_used[threadIdx.x] = 0;
+            }
+        }
+        __syncthreads();
+        if (!done) {
+            for (uint32_t t = 0; t < n; ++t) {
+                const float4 A = s_a[t];
+                const float c11 = s_b[t].x;
+                const float sigma = calc_sigma(pcx, pcy, A.z, A.w, c11, A.x, A.y);
+                if (sigma > s_c[t].z + margin) continue;
+                const float4 B = s_b[t];
+                const float alpha = bsx_min(0.999f, B.y * bsx_expf(-sigma));
+                const float wc = SMOOTH ? cutoff_weight(alpha) : (alpha >= 1.0f / 255.0f ? 1.0f : 0.0f);
+                if (sigma >= 0.0f && wc > 0.0f) {
+                    const float ae = alpha * wc;
+                    const float next_t = T * (1.0f - ae);
+                    if (next_t <= 1.0e-4f) {
+                        done = true;
+                        break;
+                    }
+                    if (BWD) s_used[t] = 1;
+                    const float vis = ae * T;
+                    cr += bsx_max(B.z, 0.0f) * vis;
+                    cg += bsx_max(B.w, 0.0f) * vis;
+                    cb += bsx_max(s_c[t].x, 0.0f) * vis;
+                    T = next_t;
+                    last = batch + t + 1;
+                }
+            }
+        }
+        if (BWD) {
+            __syncthreads();
+            if (threadIdx.x < n && s_used[threadIdx.x]) a.visible[s_gid[threadIdx.x]] = 1.0f;
+        }
+    }
+
+    if (inside) {
+        const float fr = cr + T * a.bg_r, fg = cg + T * a.bg_g, fb = cb + T * a.bg_b;
+        const float fa = 1.0f - T;
+        const size_t pid = (size_t)py * a.w + px;
+        if (BWD) {
+            reinterpret_cast<float4*>(a.image)[pid] = make_float4(fr, fg, fb, fa);
+        } else {
+            const uint32_t r8 = (uint32_t)bsx_clamp(fr * 255.0f, 0.0f, 255.0f);
+            const uint32_t g8 = (uint32_t)bsx_clamp(fg * 255.0f, 0.0f, 255.0f);
+            const uint32_t b8 = (uint32_t)bsx_clamp(fb * 255.0f, 0.0f, 255.0f);
+            const uint32_t a8 = (uint32_t)bsx_clamp(fa * 255.0f, 0.0f, 255.0f);
+            a.image_packed[pid] = r8 | (g8 << 8) | (b8 << 16) | (a8 << 24);
+        }
+    }
+    if (BWD) {
+        atomicMax(&s_max_useful, last);
+        __syncthreads();
+        if (threadIdx.x == 0) a.tile_offsets[tile * 2 + 1] = s_max_useful;
+    }
+}
+
+}  // namespace
+
+bsx_status launch_raster_fwd(bsx_ctx* ctx, const uint32_t* isect_gid, uint32_t* tile_offsets, const float* projected,
+                             float* image, uint32_t* image_packed, float* visible, const bsx_project_uniforms& u,
+                             const float bg[3], int bwd_info, int smooth) {
+    FwdArgs a;
+    a.isect_gid = isect_gid;
+    a.tile_offsets = tile_offsets;
+    a.projected = projected;
+    a.image = image;
+    a.image_packed = image_packed;
+    a.visible = visible;
+    a.tbw = u.tile_bw;
+    a.w = u.img_w;
+    a.h = u.img_h;
+    a.bg_r = bg[0];
+    a.bg_g = bg[1];
+    a.bg_b = bg[2];
+    const uint32_t tiles = u.tile_bw * u.tile_bh;
+    prof_begin(ctx);
+    if (!bwd_info) raster_fwd_kernel<false, false><<<tiles, kRasterThreads, 0, ctx->stream>>>(a);
+    else if (!smooth) raster_fwd_kernel<true, false><<<tiles, kRasterThreads, 0, ctx->stream>>>(a);
+    else raster_fwd_kernel<true, true><<<tiles, kRasterThreads, 0, ctx->stream>>>(a);
+    return post_launch(ctx, "raster_fwd_kernel");
+}
+
+}  // namespace bsx

@@ -1,0 +1,163 @@
+// scan.cu - single-pass inclusive prefix sum with decoupled look-back.
+//
+// Replaces brush-prefix-sum's three-level Hillis-Steele scan
+// (crates/brush-prefix-sum/src/lib.rs:11-87, kernels.rs:22-76) with one
+// kernel: each 4096-element tile takes a ticket (so tiles wait only on tiles
+// that are already running), reduces itself, publishes its aggregate, then
+// warp 0 looks back over predecessors' published aggregates / inclusive
+// prefixes (Merrill & Garland, "Single-pass Parallel Prefix Scan with
+// Decoupled Look-back", 2016). Every wait is bounded: on expiry the tile
+// records a device error and carries on, so the grid always terminates.
+// Sums are u32 and wrap, as the reference's.
+#include "common.cuh"
+#include "lookback.cuh"
+
+namespace bsx {
+
+namespace {
+
+constexpr int kScanThreads = 256;
+constexpr int kScanItems = 16;
+constexpr uint32_t kScanTile = kScanThreads * kScanItems;
+
+__device__ __forceinline__ uint32_t warp_incl_scan(uint32_t v) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        uint32_t t = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += t;
+    }
+    return v;
+}
+
+// Block-wide exclusive scan of one value per thread; returns the exclusive
+// prefix and writes the block total to *total.
+__device__ __forceinline__ uint32_t block_excl_scan(uint32_t v, uint32_t* s_warp, uint32_t* total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint32_t incl = warp_incl_scan(v);
+    if (lane == 31) s_warp[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        uint32_t w = lane < (kScanThreads / 32) ? s_warp[lane] : 0u;
+        uint32_t wi = warp_incl_scan(w);
+        if (lane < (kScanThreads / 32)) s_warp[lane] = wi - w;
+        if (lane == (kScanThreads / 32) - 1) s_warp[kScanThreads / 32] = wi;
+    }
+    __syncthreads();
+    uint32_t excl = s_warp[warp] + incl - v;
+    *total = s_warp[kScanThreads / 32];
+    return excl;
+}
+
+}  // namespace
+
+namespace {
+
+__global__ void __launch_bounds__(kScanThreads) scan_kernel(const uint32_t* __restrict__ in,
+                                                            const uint32_t* __restrict__ gather, uint32_t n,
+                                                            uint32_t* __restrict__ out, uint64_t* status,
+                                                            uint32_t* ticket, uint32_t* total_out, int* err,
+                                                            int vec_in, int vec_out) {
+    __shared__ uint32_t s_tile;
+    __shared__ uint32_t s_warp[kScanThreads / 32 + 1];
+    __shared__ uint32_t s_prefix;
+    if (threadIdx.x == 0) s_tile = atomicAdd(ticket, 1u);
+    __syncthreads();
+    const uint32_t tile = s_tile;
+    const uint64_t base = (uint64_t)tile * kScanTile + (uint64_t)threadIdx.x * kScanItems;
+    uint32_t items[kScanItems];
+    if (vec_in && !gather && base + kScanItems <= n) {
+        const uint4* src = reinterpret_cast<const uint4*>(in + base);
+#pragma unroll
+        for (int q = 0; q < kScanItems / 4; ++q) {
+            uint4 v = __ldg(src + q);
+            items[4 * q] = v.x;
+            items[4 * q + 1] = v.y;
+            items[4 * q + 2] = v.z;
+            items[4 * q + 3] = v.w;
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < kScanItems; ++k) {
+            uint64_t i = base + k;
+            items[k] = i < n ? (gather ? in[gather[i]] : in[i]) : 0u;
+        }
+    }
+    uint32_t sum = 0;
+#pragma unroll
+    for (int k = 0; k < kScanItems; ++k) sum += items[k];
+    uint32_t total;
+    uint32_t excl = block_excl_scan(sum, s_warp, &total);
+    if (threadIdx.x < 32) {
+        uint32_t prefix = 0;
+        if (tile == 0) {
+            if (threadIdx.x == 0) st_relaxed_u64(status + tile, kFlagIncl | total);
+        } else {
+            if (threadIdx.x == 0) st_relaxed_u64(status + tile, kFlagAgg | total);
+            prefix = lookback_exclusive(status, tile, err);
+            if (threadIdx.x == 0) st_relaxed_u64(status + tile, kFlagIncl | (uint32_t)(prefix + total));
+        }
+        if (threadIdx.x == 0) {
+            s_prefix = prefix;
+            if (total_out && (uint64_t)(tile + 1) * kScanTile >= n) *total_out = prefix + total;
+        }
+    }
+    __syncthreads();
+    uint32_t run = s_prefix + excl;
+    if (vec_out && base + kScanItems <= n) {
+        uint4* dst = reinterpret_cast<uint4*>(out + base);
+#pragma unroll
+        for (int q = 0; q < kScanItems / 4; ++q) {
+            uint4 v;
+            run += items[4 * q];
+            v.x = run;
+            run += items[4 * q + 1];
+            v.y = run;
+            run += items[4 * q + 2];
+            v.z = run;
+            run += items[4 * q + 3];
+            v.w = run;
+            dst[q] = v;
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < kScanItems; ++k) {
+            run += items[k];
+            if (base + k < n) out[base + k] = run;
+        }
+    }
+}
+
+}  // namespace
+
+size_t scan_status_words(uint32_t n_tiles) { return (size_t)n_tiles + 2; }
+
+bsx_status scan_inclusive_u32(bsx_ctx* ctx, const uint32_t* d_in, const uint32_t* d_gather, uint32_t n,
+                              uint32_t* d_out, uint32_t* d_total) {
+    if (n == 0) {
+        if (d_total) return check_cuda(ctx, cudaMemsetAsync(d_total, 0, 4, ctx->stream), "memset total");
+        return BSX_OK;
+    }
+    const uint32_t tiles = (uint32_t)(((uint64_t)n + kScanTile - 1) / kScanTile);
+    bsx_status s = ensure(ctx, ctx->scan_status, scan_status_words(tiles) * sizeof(uint64_t));
+    if (s != BSX_OK) return s;
+    uint64_t* status = ctx->scan_status.as<uint64_t>();
+    s = check_cuda(ctx, cudaMemsetAsync(status, 0, scan_status_words(tiles) * sizeof(uint64_t), ctx->stream),
+                   "memset scan status");
+    if (s != BSX_OK) return s;
+    uint32_t* ticket = reinterpret_cast<uint32_t*>(status + tiles);
+    const int vec_in = ((uintptr_t)d_in % 16) == 0;
+    const int vec_out = ((uintptr_t)d_out % 16) == 0;
+    prof_begin(ctx);
+    scan_kernel<<<tiles, kScanThreads, 0, ctx->stream>>>(d_in, d_gather, n, d_out, status, ticket, d_total,
+                                                           ctx->d_err, vec_in, vec_out);
+    return post_launch(ctx, "scan_kernel");
+}
+
+}  // namespace bsx
+
+extern "C" bsx_status bsx_prefix_sum_u32(bsx_ctx* ctx, const uint32_t* d_in, uint32_t n, uint32_t* d_out) {
+    if (!ctx || (n && (!d_in || !d_out))) return BSX_ERR_INVALID_ARG;
+    cudaSetDevice(ctx->device);
+    return bsx::scan_inclusive_u32(ctx, d_in, nullptr, n, d_out, nullptr);
+}

@@ -1,0 +1,233 @@
+/*
+ * bsx.h - C ABI of the B200 splat-training hot path.
+ *
+ * Every entry point is `extern "C"`, takes plain pointers and sizes, never
+ * throws or unwinds, and returns a bsx_status. Pointers named d_* are CUDA
+ * device pointers owned by the caller; h_* are host pointers. All GPU work
+ * is enqueued asynchronously on the context's stream (bsx_set_stream); the
+ * only host synchronisation inside the library is the one read of the
+ * visible/intersection counts per forward render (the reference performs
+ * the same read, crates/brush-render/src/render.rs:308-330).
+ *
+ * Layouts are the reference's (crates/brush-render/src/gaussian_splats.rs:110-127):
+ *   transforms [N,10] = mean xyz, quaternion (w,x,y,z) unnormalised, log-scale xyz
+ *   sh_coeffs  [N,C,3] coefficient-major, RGB-minor, C = (degree+1)^2
+ *   raw_opac   [N]     opacity logits
+ *   image      [H,W,4] RGBA float (backward passes) or [H,W] packed RGBA8 (forward pass)
+ *   gt         [H,W]   packed RGBA8, r in the low byte
+ */
+#ifndef BSX_H
+#define BSX_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define BSX_API __attribute__((visibility("default")))
+#else
+#define BSX_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BSX_ABI_VERSION 1
+/* Gradient lanes per splat written by the raster backward:
+ * xy(2) conic(3) rgb(3) alpha refine depth. Reference:
+ * crates/brush-render-bwd/src/kernels/rasterize_backwards.rs:40 */
+#define BSX_COMPACT_GRAD_LANES 11
+/* Row stride of the gradient buffer exchanged between bsx_rasterize_bwd and
+ * bsx_project_bwd: the 11 reference lanes plus one pad lane, so each row is
+ * three 16-byte words (the raster backward accumulates with vector atomics). */
+#define BSX_GRAD_STRIDE 12
+/* Row stride (floats) of the projected-splat buffer: xy, conic(3), opacity,
+ * rgb, depth, then two pad lanes so each row is three aligned 16-byte words.
+ * The reference packs the same first ten lanes (kernels/helpers.rs:48-52). */
+#define BSX_PROJECTED_LANES 12
+#define BSX_TILE_WIDTH 16
+
+typedef enum bsx_status {
+    BSX_OK = 0,
+    BSX_ERR_INVALID_ARG = 1,   /* null pointer, bad enum, size out of range */
+    BSX_ERR_SHAPE = 2,         /* inconsistent tensor sizes (reference DimCheck) */
+    BSX_ERR_CAPACITY = 3,      /* an internal size limit was exceeded */
+    BSX_ERR_DEVICE_TIMEOUT = 4,/* a bounded device-side wait gave up */
+    BSX_ERR_CUDA = 5,          /* a CUDA runtime call failed */
+    BSX_ERR_STATE = 6,         /* call order violated (e.g. backward without forward) */
+    BSX_ERR_UNSUPPORTED = 7    /* valid request this build does not implement */
+} bsx_status;
+
+typedef enum bsx_render_mode { BSX_RENDER_DEFAULT = 0, BSX_RENDER_MIP = 1 } bsx_render_mode;
+
+/* crates/brush-render/src/gaussian_splats.rs:46-66 */
+typedef enum bsx_raster_pass {
+    BSX_PASS_FORWARD = 0,               /* packed RGBA8 output, no bookkeeping */
+    BSX_PASS_BACKWARD = 1,              /* RGBA f32 + visible + shortened tile ranges */
+    BSX_PASS_BACKWARD_SMOOTH_CUTOFF = 2 /* as BACKWARD with the C^1 alpha-cutoff ramp */
+} bsx_raster_pass;
+
+typedef enum bsx_camera_model { BSX_CAMERA_PINHOLE = 0 } bsx_camera_model;
+
+/* crates/brush-render/src/camera.rs:11-19 */
+typedef struct bsx_camera {
+    double fov_x;          /* radians */
+    double fov_y;
+    float center_uv[2];    /* principal point as a fraction of the image size */
+    float position[3];     /* camera centre, world space */
+    float rotation[4];     /* camera-to-world rotation quaternion (x, y, z, w) */
+    int32_t camera_model;  /* bsx_camera_model */
+} bsx_camera;
+
+/* crates/brush-render/src/kernels/types.rs:53-83 (ProjectUniforms). */
+typedef struct bsx_project_uniforms {
+    float viewmat[12];     /* world-to-camera 3x4, column-major: 3 rotation columns + translation */
+    float fx, fy, cx, cy;  /* pinhole intrinsics in pixels */
+    float camera_pos[3];
+    float half_max_render_fov;
+    float lim_pos_x, lim_pos_y, lim_neg_x, lim_neg_y; /* projection-Jacobian clamp */
+    uint32_t img_w, img_h;
+    uint32_t tile_bw, tile_bh;
+    uint32_t sh_degree;
+    uint32_t total_splats;
+    uint32_t num_visible;
+} bsx_project_uniforms;
+
+/* Device outputs of one forward render (crates/brush-render/src/render_aux.rs:16-68).
+ * All pointers reference context-owned memory valid until the next render on
+ * the same context. Projected rows, visibility, radii and gradients are
+ * indexed by the global splat id, so global_from_compact_gid is the identity
+ * and compact_gid_from_isect holds global ids. */
+typedef struct bsx_render_out {
+    float* d_image;                 /* [H,W,4] f32 (backward passes) */
+    uint32_t* d_image_packed;       /* [H,W] RGBA8 (forward pass) */
+    float* d_visible;               /* [N] 1.0 where a splat was composited (backward passes) */
+    float* d_max_radius;            /* [N] max(ex/W, ey/H) for visible splats, else 0 */
+    uint32_t* d_tile_offsets;       /* [ty,tx,2] start/end per tile (end shortened in backward passes) */
+    float* d_projected;             /* [N, BSX_PROJECTED_LANES] */
+    uint32_t* d_isect_gid;          /* [num_intersections] splat id per intersection, tile-major, front-to-back */
+    uint32_t* d_isect_tile;         /* [num_intersections] sorted tile id per intersection */
+    uint32_t* d_depth_order;        /* [num_visible] visible splat ids sorted by depth */
+    uint32_t* d_tile_counts;        /* [N] contributing-tile count per splat */
+    uint32_t* d_cum_counts;         /* [num_visible] inclusive scan of counts in depth order */
+    uint32_t num_visible;
+    uint32_t num_intersections;
+    uint32_t tile_bw, tile_bh;
+    bsx_project_uniforms uniforms;
+} bsx_render_out;
+
+/* crates/brush-loss/src/lib.rs:935-941 (ImageLossConfig). */
+typedef struct bsx_loss_cfg {
+    float l1_weight;
+    float ssim_weight;
+    int32_t composite_bg;  /* 1: gt_eff = gt + (1 - gt.a) * bg */
+    float bg[3];
+    int32_t mask;          /* 1: multiply the loss map by gt.a */
+} bsx_loss_cfg;
+
+/* One parameter tensor for the fused Adam update
+ * (crates/brush-train/src/adam_scaled.rs:216-383). Rows x cols elements,
+ * row-major. col_scale (cols entries, host) multiplies the learning rate per
+ * column; reduce_moment_2 keeps one second moment per row (mean of g^2 over
+ * the row) as the reference does for the SH coefficients. */
+typedef struct bsx_adam_group {
+    float* d_param;
+    const float* d_grad;
+    float* d_m;            /* [rows, cols] */
+    float* d_v;            /* [rows, cols] or [rows] when reduce_moment_2 */
+    uint32_t rows, cols;
+    float lr;
+    const float* h_col_scale;  /* may be NULL (all ones); at most 64 entries */
+    int32_t reduce_moment_2;
+} bsx_adam_group;
+
+typedef struct bsx_adam_cfg {
+    float beta_1;          /* 0.9 */
+    float beta_2;          /* 0.999 */
+    float epsilon;         /* 1e-15 in the reference trainer */
+    uint32_t step;         /* time step AFTER this update (1 for the first update) */
+    float grad_scale;      /* multiplies every gradient first (1/world_size after a sum all-reduce) */
+} bsx_adam_cfg;
+
+/* ---- context ----------------------------------------------------------- */
+typedef struct bsx_ctx bsx_ctx;
+
+BSX_API bsx_status bsx_create(int device, bsx_ctx** out);
+BSX_API bsx_status bsx_destroy(bsx_ctx* ctx);
+BSX_API bsx_status bsx_set_stream(bsx_ctx* ctx, void* cuda_stream);
+BSX_API bsx_status bsx_sync(bsx_ctx* ctx);
+BSX_API const char* bsx_last_error(const bsx_ctx* ctx);
+BSX_API const char* bsx_status_string(bsx_status s);
+BSX_API int bsx_abi_version(void);
+/* Number of kernel launches this context has enqueued since creation. */
+BSX_API uint64_t bsx_launch_count(const bsx_ctx* ctx);
+
+/* Optional per-launch timing with CUDA events on the context's stream.
+ * While enabled, every kernel launch is bracketed by two events;
+ * bsx_profile_collect synchronises the stream and accumulates the elapsed
+ * time per kernel name; entries are read with bsx_profile_entry. */
+BSX_API bsx_status bsx_profile_enable(bsx_ctx* ctx, int32_t on);
+BSX_API bsx_status bsx_profile_collect(bsx_ctx* ctx);
+BSX_API int32_t bsx_profile_count(const bsx_ctx* ctx);
+BSX_API bsx_status bsx_profile_entry(const bsx_ctx* ctx, int32_t i, const char** name, double* total_ms,
+                                     uint64_t* launches);
+BSX_API bsx_status bsx_profile_reset(bsx_ctx* ctx);
+
+/* Host-only: camera -> uniforms, following crates/brush-render/src/camera.rs:49-101,200-254
+ * and render.rs:116-136. Needs no GPU. */
+BSX_API bsx_status bsx_make_project_uniforms(const bsx_camera* cam, uint32_t img_w, uint32_t img_h,
+                                     uint32_t sh_degree, uint32_t total_splats,
+                                     bsx_project_uniforms* out);
+
+/* ---- forward render: SplatOps::render (crates/brush-render/src/lib.rs:69-88) ---- */
+BSX_API bsx_status bsx_render_fwd(bsx_ctx* ctx, const bsx_camera* cam, uint32_t img_w, uint32_t img_h,
+                          const float* d_transforms, const float* d_sh_coeffs,
+                          const float* d_raw_opac, uint32_t num_splats, uint32_t sh_coeffs_per_splat,
+                          int32_t render_mode, int32_t raster_pass, const float background[3],
+                          bsx_render_out* out);
+
+/* ---- backward: SplatBwdOps (crates/brush-render-bwd/src/burn_glue.rs:80-172) ----
+ * Both consume the state of the last backward-pass forward render on ctx. */
+/* rasterize_bwd: v_output [H,W,4] -> d_v_combined [N, BSX_GRAD_STRIDE]
+ * (zeroed, then accumulated). Both buffers 16-byte aligned. */
+BSX_API bsx_status bsx_rasterize_bwd(bsx_ctx* ctx, const float* d_v_output, int32_t compute_refine_weight,
+                             float* d_v_combined);
+/* project_bwd: d_v_combined -> dense gradients (all N rows written). */
+BSX_API bsx_status bsx_project_bwd(bsx_ctx* ctx, const float* d_v_combined, float* d_v_transforms,
+                           float* d_v_sh_coeffs, float* d_v_raw_opac, float* d_v_refine_weight);
+
+/* ---- image loss: LossOps (crates/brush-loss/src/lib.rs:955-970) ----
+ * pred/map/dl_dpred are [C,H,W] planar like the reference (C = 3, or 4 with
+ * alpha matching in channel 3). */
+BSX_API bsx_status bsx_loss_fwd(bsx_ctx* ctx, const float* d_pred, const uint32_t* d_gt_packed, uint32_t img_w,
+                        uint32_t img_h, uint32_t channels, const bsx_loss_cfg* cfg, float* d_loss_map);
+BSX_API bsx_status bsx_loss_bwd(bsx_ctx* ctx, const float* d_pred, const uint32_t* d_gt_packed, uint32_t img_w,
+                        uint32_t img_h, uint32_t channels, const bsx_loss_cfg* cfg,
+                        const float* d_dl_dmap, float* d_dl_dpred);
+/* Fused training form: reads the [H,W,4] render directly, writes mean(map)
+ * over the 3 colour channels to d_loss_mean (one float) and the gradient of
+ * that mean into d_v_output [H,W,4] (alpha lane 0). */
+BSX_API bsx_status bsx_loss_fused(bsx_ctx* ctx, const float* d_image_hwc4, const uint32_t* d_gt_packed,
+                          uint32_t img_w, uint32_t img_h, const bsx_loss_cfg* cfg, float* d_loss_mean,
+                          float* d_v_output);
+
+/* ---- optimizer: AdamScaled (crates/brush-train/src/adam_scaled.rs:216-309) ---- */
+BSX_API bsx_status bsx_adam_step(bsx_ctx* ctx, const bsx_adam_group* groups, int32_t num_groups,
+                         const bsx_adam_cfg* cfg);
+
+/* ---- primitives: brush-sort / brush-prefix-sum / get_tile_offsets ---- */
+/* Stable argsort by key & mask(bits rounded up to a multiple of 4), as
+ * crates/brush-sort/src/lib.rs:16-129. Inputs are left untouched. */
+BSX_API bsx_status bsx_radix_argsort_u32(bsx_ctx* ctx, const uint32_t* d_keys, const uint32_t* d_values, uint32_t n,
+                                 uint32_t sorting_bits, uint32_t* d_keys_out, uint32_t* d_values_out);
+/* Inclusive prefix sum (u32, wrapping), crates/brush-prefix-sum/src/lib.rs:11-87. */
+BSX_API bsx_status bsx_prefix_sum_u32(bsx_ctx* ctx, const uint32_t* d_in, uint32_t n, uint32_t* d_out);
+/* [start,end) per tile from sorted tile ids; ids >= num_tiles are sentinels
+ * (crates/brush-render/src/get_tile_offset.rs:10-62). d_offsets is zeroed first. */
+BSX_API bsx_status bsx_get_tile_offsets(bsx_ctx* ctx, const uint32_t* d_tile_ids, uint32_t n, uint32_t num_tiles,
+                                uint32_t* d_offsets);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* BSX_H */

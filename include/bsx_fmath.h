@@ -1,0 +1,154 @@
+/*
+ * bsx_fmath.h - deterministic float32 elementary functions shared by the
+ * sm_100a kernels and host code.
+ *
+ * Why this exists: the splat pipeline takes discrete decisions from float
+ * predicates (cull on opacity, intersection counts from ln(255*opacity),
+ * the alpha >= 1/255 cutoff, the T <= 1e-4 early-out). To make those
+ * decisions identical on the GPU and on a CPU restatement, every
+ * transcendental on the path is evaluated with the SAME sequence of IEEE
+ * operations on both sides: + - * / sqrt (correctly rounded by IEEE 754 on
+ * both processors), explicit fused multiply-add (also correctly rounded on
+ * both), and integer bit manipulation.
+ *
+ * The reference evaluates exp/ln with its shading language's builtins,
+ * whose accuracy its own tests bound only by tolerance; the functions here
+ * take that role.
+ *
+ * Methods (published, restated here; coefficients derived from the math):
+ *  - exp: Cody & Waite argument reduction x = k*ln2 + r with ln2 split into
+ *    a 15-bit head (exact products for |k| <= 255) and a tail, followed by
+ *    the degree-7 Taylor polynomial of e^r on |r| <= ln2/2 (truncation error
+ *    r^8/8! < 5.3e-9 relative), then exact scaling by 2^k.
+ *  - ln: x = m * 2^e with m in [sqrt(1/2), sqrt(2)), s = (m-1)/(m+1),
+ *    ln(m) = 2*atanh(s) = 2s(1 + s^2/3 + s^4/5 + ... + s^10/11)
+ *    (|s| <= 0.1716, truncation < 2e-10 relative), plus e*ln2.
+ * Accuracy against the C library is checked by the CPU test-suite.
+ *
+ * Compile the including translation units without floating-point
+ * contraction (nvcc -fmad=false, gcc -ffp-contract=off) so that expressions
+ * are evaluated exactly as written.
+ */
+#ifndef BSX_FMATH_H
+#define BSX_FMATH_H
+
+#include <stdint.h>
+
+#if defined(__CUDACC__)
+#define BSX_HD __host__ __device__ __forceinline__
+#else
+#include <math.h>
+#include <string.h>
+#define BSX_HD static inline
+#endif
+
+BSX_HD float bsx_bits_to_f32(uint32_t u) {
+#if defined(__CUDA_ARCH__)
+    return __uint_as_float(u);
+#else
+    float f;
+    memcpy(&f, &u, sizeof f);
+    return f;
+#endif
+}
+
+BSX_HD uint32_t bsx_f32_to_bits(float f) {
+#if defined(__CUDA_ARCH__)
+    return __float_as_uint(f);
+#else
+    uint32_t u;
+    memcpy(&u, &f, sizeof u);
+    return u;
+#endif
+}
+
+/* Correctly rounded a*b+c on both processors. */
+BSX_HD float bsx_fma(float a, float b, float c) {
+#if defined(__CUDA_ARCH__)
+    return __fmaf_rn(a, b, c);
+#else
+    return fmaf(a, b, c);
+#endif
+}
+
+/* Round to nearest integer, ties to even (IEEE default mode on both). */
+BSX_HD float bsx_rint(float x) {
+#if defined(__CUDA_ARCH__)
+    return rintf(x);
+#else
+    return nearbyintf(x);
+#endif
+}
+
+/* IEEE minNum/maxNum: a NaN operand yields the other operand. */
+BSX_HD float bsx_min(float a, float b) { return fminf(a, b); }
+BSX_HD float bsx_max(float a, float b) { return fmaxf(a, b); }
+BSX_HD float bsx_clamp(float x, float lo, float hi) { return fminf(fmaxf(x, lo), hi); }
+
+/* 2^k as a float for k in [-126, 127]. */
+BSX_HD float bsx_pow2i(int k) { return bsx_bits_to_f32((uint32_t)(k + 127) << 23); }
+
+/* Bit-level finiteness test (exponent field not all ones). */
+BSX_HD int bsx_is_finite(float x) { return ((bsx_f32_to_bits(x) >> 23) & 0xFFu) != 0xFFu; }
+
+/* exp(x) in float32. NaN propagates; overflow gives +inf; deep underflow 0. */
+BSX_HD float bsx_expf(float x) {
+    if (x != x) return x;
+    if (x > 88.72283935546875f) return bsx_bits_to_f32(0x7f800000u);
+    if (x < -103.97209167480469f) return 0.0f;
+    const float kLog2e = 1.4426950216293335f;
+    const float kLn2Hi = 0.693145751953125f;    /* 0x3f317200 */
+    const float kLn2Lo = 1.428606765330187e-06f; /* 0x35bfbe8e */
+    float k = bsx_rint(x * kLog2e);
+    float r = bsx_fma(-k, kLn2Hi, x);
+    r = bsx_fma(-k, kLn2Lo, r);
+    float p = 0.00019841270113829523f;       /* 1/7! */
+    p = bsx_fma(p, r, 0.0013888889225199819f); /* 1/6! */
+    p = bsx_fma(p, r, 0.008333333767950535f);  /* 1/5! */
+    p = bsx_fma(p, r, 0.0416666679084301f);    /* 1/4! */
+    p = bsx_fma(p, r, 0.1666666716337204f);    /* 1/3! */
+    p = bsx_fma(p, r, 0.5f);
+    p = bsx_fma(p, r, 1.0f);
+    p = bsx_fma(p, r, 1.0f);
+    int ki = (int)k;
+    if (ki >= -126 && ki <= 127) return p * bsx_pow2i(ki);
+    if (ki > 127) return (p * bsx_pow2i(127)) * 2.0f;
+    return (p * bsx_pow2i(ki + 64)) * 5.421010862427522e-20f; /* 2^-64 */
+}
+
+/* Natural logarithm in float32. */
+BSX_HD float bsx_logf(float x) {
+    if (x != x) return x;
+    if (x < 0.0f) return bsx_bits_to_f32(0x7fc00000u);
+    if (x == 0.0f) return bsx_bits_to_f32(0xff800000u);
+    uint32_t b = bsx_f32_to_bits(x);
+    if (b >= 0x7f800000u) return x; /* +inf */
+    int e = 0;
+    if (b < 0x00800000u) { /* subnormal: scale into the normal range */
+        x = x * 8388608.0f;  /* 2^23, exact */
+        b = bsx_f32_to_bits(x);
+        e = -23;
+    }
+    e += (int)(b >> 23) - 127;
+    float m = bsx_bits_to_f32((b & 0x007fffffu) | 0x3f800000u);
+    if (m > 1.4142135381698608f) {
+        m = m * 0.5f;
+        e += 1;
+    }
+    float s = (m - 1.0f) / (m + 1.0f);
+    float s2 = s * s;
+    float q = 0.09090909361839294f;             /* 1/11 */
+    q = bsx_fma(q, s2, 0.1111111119389534f);    /* 1/9 */
+    q = bsx_fma(q, s2, 0.1428571492433548f);    /* 1/7 */
+    q = bsx_fma(q, s2, 0.20000000298023224f);   /* 1/5 */
+    q = bsx_fma(q, s2, 0.3333333432674408f);    /* 1/3 */
+    float t = s + s;
+    float lnm = bsx_fma(t * s2, q, t);
+    float ef = (float)e;
+    return bsx_fma(ef, 0.693145751953125f, bsx_fma(ef, 1.428606765330187e-06f, lnm));
+}
+
+/* Logistic sigmoid, same expression as the reference: 1 / (1 + e^-x). */
+BSX_HD float bsx_sigmoid(float x) { return 1.0f / (1.0f + bsx_expf(-x)); }
+
+#endif /* BSX_FMATH_H */

@@ -1,0 +1,254 @@
+"""numpy front-end of the CPU oracle (``oracle/oracle.cpp``).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, by ``__graft_entry__.smoke()``
+and by ``bench.py``'s CPU-baseline leg as the checker / CPU baseline, never by
+the product path.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB = HERE / "_build" / "liboracle.so"
+
+_lib = None
+
+
+class _Camera(C.Structure):
+    _fields_ = [("fov_x", C.c_double), ("fov_y", C.c_double), ("center_uv", C.c_float * 2),
+                ("position", C.c_float * 3), ("rotation", C.c_float * 4), ("camera_model", C.c_int32)]
+
+
+class Uniforms(C.Structure):
+    _fields_ = [("viewmat", C.c_float * 12), ("fx", C.c_float), ("fy", C.c_float), ("cx", C.c_float),
+                ("cy", C.c_float), ("camera_pos", C.c_float * 3), ("half_max_render_fov", C.c_float),
+                ("lim_pos_x", C.c_float), ("lim_pos_y", C.c_float), ("lim_neg_x", C.c_float),
+                ("lim_neg_y", C.c_float), ("img_w", C.c_uint32), ("img_h", C.c_uint32),
+                ("tile_bw", C.c_uint32), ("tile_bh", C.c_uint32), ("sh_degree", C.c_uint32),
+                ("total_splats", C.c_uint32), ("num_visible", C.c_uint32)]
+
+
+class LossCfg(C.Structure):
+    _fields_ = [("l1_weight", C.c_float), ("ssim_weight", C.c_float), ("composite_bg", C.c_int32),
+                ("bg", C.c_float * 3), ("mask", C.c_int32)]
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not LIB.exists():
+            from .build import build
+
+            build()
+        _lib = C.CDLL(str(LIB))
+        f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+        u32p = np.ctypeslib.ndpointer(np.uint32, flags="C_CONTIGUOUS")
+        _lib.orc_make_project_uniforms.argtypes = [C.POINTER(_Camera), C.c_uint32, C.c_uint32, C.c_uint32,
+                                                   C.c_uint32, C.POINTER(Uniforms)]
+        _lib.orc_render.restype = C.c_void_p
+        _lib.orc_render.argtypes = [C.POINTER(Uniforms), f32p, f32p, f32p, C.c_uint32, C.c_uint32, C.c_int,
+                                    C.c_int, f32p]
+        _lib.orc_render_free.argtypes = [C.c_void_p]
+        _lib.orc_render_sizes.argtypes = [C.c_void_p, u32p]
+        _lib.orc_render_get.restype = C.c_size_t
+        _lib.orc_render_get.argtypes = [C.c_void_p, C.c_int, C.c_void_p]
+        _lib.orc_rasterize_bwd.argtypes = [C.c_void_p, f32p, C.c_int, f32p]
+        _lib.orc_project_bwd.argtypes = [C.POINTER(Uniforms), f32p, f32p, f32p, C.c_uint32, C.c_uint32, C.c_int,
+                                         f32p, f32p, f32p, f32p, f32p]
+        _lib.orc_loss_fwd.argtypes = [f32p, u32p, C.c_uint32, C.c_uint32, C.c_uint32, C.POINTER(LossCfg), f32p]
+        _lib.orc_loss_bwd.argtypes = [f32p, u32p, C.c_uint32, C.c_uint32, C.c_uint32, C.POINTER(LossCfg), f32p,
+                                      f32p]
+        _lib.orc_adam.argtypes = [f32p, f32p, f32p, f32p, C.c_uint32, C.c_uint32, C.c_float, C.c_void_p, C.c_int,
+                                  C.c_float, C.c_float, C.c_float, C.c_uint32, C.c_float]
+        _lib.orc_radix_argsort_u32.argtypes = [u32p, u32p, C.c_uint32, C.c_uint32, u32p, u32p]
+        _lib.orc_prefix_sum_u32.argtypes = [u32p, C.c_uint32, u32p]
+        _lib.orc_tile_offsets.argtypes = [u32p, C.c_uint32, C.c_uint32, u32p]
+        _lib.orc_rasterize_rows.argtypes = [f32p, C.c_uint32, C.c_uint32, C.c_uint32, f32p, C.c_int, f32p]
+        _lib.orc_gauss_taps.argtypes = [f32p]
+        _lib.orc_expf.restype = C.c_float
+        _lib.orc_expf.argtypes = [C.c_float]
+        _lib.orc_logf.restype = C.c_float
+        _lib.orc_logf.argtypes = [C.c_float]
+        _lib.orc_set_threads.argtypes = [C.c_int]
+        _lib.orc_get_threads.restype = C.c_int
+    return _lib
+
+
+def set_threads(n: int) -> None:
+    lib().orc_set_threads(int(n))
+
+
+def threads() -> int:
+    return int(lib().orc_get_threads())
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=np.float32))
+
+
+def _u32(a) -> np.ndarray:
+    a = np.asarray(a)
+    if a.dtype == np.int32:
+        a = a.view(np.uint32)
+    return np.ascontiguousarray(a.astype(np.uint32, copy=False))
+
+
+def camera_c(cam) -> _Camera:
+    c = _Camera()
+    c.fov_x, c.fov_y = float(cam.fov_x), float(cam.fov_y)
+    c.center_uv[:] = [float(v) for v in cam.center_uv]
+    c.position[:] = [float(v) for v in cam.position]
+    c.rotation[:] = [float(v) for v in cam.rotation]
+    c.camera_model = int(cam.camera_model)
+    return c
+
+
+def make_uniforms(cam, w: int, h: int, sh_degree: int = 0, total: int = 0) -> Uniforms:
+    u = Uniforms()
+    c = camera_c(cam)
+    if lib().orc_make_project_uniforms(C.byref(c), w, h, sh_degree, total, C.byref(u)) != 0:
+        raise ValueError("unsupported camera")
+    return u
+
+
+_FIELDS = {"projected": (0, np.float32), "counts": (1, np.uint32), "max_radius": (2, np.float32),
+           "depth_order": (3, np.uint32), "cum": (4, np.uint32), "isect_tile": (5, np.uint32),
+           "isect_gid": (6, np.uint32), "tile_offsets": (7, np.uint32), "image": (8, np.float32),
+           "image_packed": (9, np.uint32), "visible": (10, np.float32)}
+
+
+class RenderResult:
+    """Forward render on the CPU; holds the C++ state needed by ``rasterize_bwd``."""
+
+    def __init__(self, cam, img_size, transforms, sh, raw_opac, mip=False, raster_pass=1, bg=(0.0, 0.0, 0.0)):
+        self.w, self.h = int(img_size[0]), int(img_size[1])
+        self.transforms = _f32(transforms).reshape(-1, 10)
+        n = self.transforms.shape[0]
+        self.sh = _f32(sh).reshape(n, -1, 3)
+        self.coeffs = self.sh.shape[1]
+        self.raw_opac = _f32(raw_opac).reshape(n)
+        self.mip = int(bool(mip))
+        deg = int(round(self.coeffs ** 0.5)) - 1
+        self.uniforms = make_uniforms(cam, self.w, self.h, deg, n)
+        self.n = n
+        self._h = lib().orc_render(C.byref(self.uniforms), self.transforms, self.sh, self.raw_opac, n, self.coeffs,
+                                   self.mip, int(raster_pass), _f32(bg))
+        sizes = np.zeros(4, dtype=np.uint32)
+        lib().orc_render_sizes(self._h, sizes)
+        self.num_visible, self.num_intersections, self.tile_bw, self.tile_bh = (int(v) for v in sizes)
+        for name, (idx, dt) in _FIELDS.items():
+            count = lib().orc_render_get(self._h, idx, None)
+            arr = np.empty(count, dtype=dt)
+            if count:
+                lib().orc_render_get(self._h, idx, arr.ctypes.data)
+            setattr(self, name, arr)
+        self.projected = self.projected.reshape(n, 12)
+        if self.image.size:
+            self.image = self.image.reshape(self.h, self.w, 4)
+        if self.image_packed.size:
+            self.image_packed = self.image_packed.reshape(self.h, self.w)
+        self.tile_offsets = self.tile_offsets.reshape(self.tile_bh, self.tile_bw, 2)
+
+    def rasterize_bwd(self, v_output, compute_refine_weight=True) -> np.ndarray:
+        out = np.zeros((self.n, 11), dtype=np.float32)
+        lib().orc_rasterize_bwd(self._h, _f32(v_output).reshape(-1), int(compute_refine_weight), out)
+        return out
+
+    def project_bwd(self, v_combined):
+        n, c = self.n, self.coeffs
+        vt = np.zeros((n, 10), np.float32)
+        vs = np.zeros((n, c, 3), np.float32)
+        vo = np.zeros(n, np.float32)
+        vr = np.zeros(n, np.float32)
+        lib().orc_project_bwd(C.byref(self.uniforms), self.transforms, self.sh, self.raw_opac, n, c, self.mip,
+                              _f32(v_combined).reshape(n, 11), vt, vs, vo, vr)
+        return vt, vs, vo, vr
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h:
+            lib().orc_render_free(h)
+            self._h = None
+
+
+def loss_cfg(l1_weight=0.8, ssim_weight=-0.2, composite_bg=None, mask=False) -> LossCfg:
+    c = LossCfg()
+    c.l1_weight, c.ssim_weight = float(l1_weight), float(ssim_weight)
+    c.composite_bg = int(composite_bg is not None)
+    c.bg[:] = [float(v) for v in (composite_bg or (0.0, 0.0, 0.0))]
+    c.mask = int(mask)
+    return c
+
+
+def loss_fwd(pred_chw, gt_packed, cfg: LossCfg) -> np.ndarray:
+    p = _f32(pred_chw)
+    ch, h, w = p.shape
+    out = np.empty_like(p)
+    lib().orc_loss_fwd(p.reshape(-1), _u32(gt_packed).reshape(-1), w, h, ch, C.byref(cfg), out.reshape(-1))
+    return out
+
+
+def loss_bwd(pred_chw, gt_packed, cfg: LossCfg, dl_dmap) -> np.ndarray:
+    p = _f32(pred_chw)
+    ch, h, w = p.shape
+    out = np.empty_like(p)
+    lib().orc_loss_bwd(p.reshape(-1), _u32(gt_packed).reshape(-1), w, h, ch, C.byref(cfg),
+                       _f32(dl_dmap).reshape(-1), out.reshape(-1))
+    return out
+
+
+def adam(param, grad, m, v, lr, col_scale=None, reduce=False, beta1=0.9, beta2=0.999, eps=1e-15, step=1,
+         grad_scale=1.0):
+    """In place on param/m/v (2-D float32 arrays; v is [rows] when reduce)."""
+    rows, cols = param.shape
+    sc = None
+    if col_scale is not None:
+        sc_arr = _f32(col_scale)
+        sc = sc_arr.ctypes.data
+    lib().orc_adam(param.reshape(-1), _f32(grad).reshape(-1), m.reshape(-1), v.reshape(-1), rows, cols, float(lr),
+                   sc, int(reduce), beta1, beta2, eps, int(step), float(grad_scale))
+
+
+def radix_argsort(keys, values, bits):
+    k, v = _u32(keys), _u32(values)
+    ko, vo = np.empty_like(k), np.empty_like(v)
+    lib().orc_radix_argsort_u32(k, v, k.size, int(bits), ko, vo)
+    return ko, vo
+
+
+def prefix_sum(values):
+    v = _u32(values)
+    out = np.empty_like(v)
+    lib().orc_prefix_sum_u32(v, v.size, out)
+    return out
+
+
+def tile_offsets(ids, num_tiles):
+    ids = _u32(ids)
+    out = np.zeros(num_tiles * 2, dtype=np.uint32)
+    lib().orc_tile_offsets(ids, ids.size, num_tiles, out)
+    return out.reshape(num_tiles, 2)
+
+
+def rasterize_rows(rows10, w, h, bg=(0.0, 0.0, 0.0), smooth=False) -> np.ndarray:
+    r = _f32(rows10).reshape(-1, 10)
+    out = np.empty((h, w, 4), dtype=np.float32)
+    lib().orc_rasterize_rows(r.reshape(-1), r.shape[0], w, h, _f32(bg), int(smooth), out.reshape(-1))
+    return out
+
+
+def gauss_taps() -> np.ndarray:
+    out = np.empty(11, dtype=np.float32)
+    lib().orc_gauss_taps(out)
+    return out
+
+
+def expf(x: float) -> float:
+    return float(lib().orc_expf(float(x)))
+
+
+def logf(x: float) -> float:
+    return float(lib().orc_logf(float(x)))

@@ -1,0 +1,110 @@
+"""Pin the CPU oracle to the reference's own known answers before trusting it.
+
+- gsplat golden forward renders committed by the reference
+  (crates/brush-bench-test/src/reference.rs:28-151; tolerance 1e-5 + 1 %);
+- the raster-oracle KATs (crates/brush-render/src/tests/raster_oracle.rs:111-159);
+- sort / prefix-sum / tile-offset KATs (brush-sort/src/lib.rs:170-429,
+  brush-prefix-sum/src/lib.rs:109-191, get_tile_offset.rs:88-129);
+- the shared elementary functions against the C library.
+"""
+import math
+
+import numpy as np
+import pytest
+
+from conftest import golden_case
+
+
+@pytest.mark.parametrize("name", ["tiny_case", "basic_case"])
+def test_golden_gsplat_render(orc, name):
+    cam, size, t, sh, op, ref = golden_case(name)
+    r = orc.RenderResult(cam, size, t, sh, op)
+    err = np.abs(r.image - ref)
+    tol = 1e-5 + 1e-2 * np.abs(ref)
+    assert not np.isnan(r.image).any()
+    assert (err <= tol).all(), f"max err {err.max()}"
+
+
+def test_raster_kat_one_splat_clamps_negative_color(orc):
+    img = orc.rasterize_rows([0.5, 0.5, 1.0, 0.0, 1.0, 0.5, 1.0, 0.5, -1.0, 0.0], 1, 1, (0.2, 0.4, 0.6))
+    np.testing.assert_allclose(img.ravel(), [0.6, 0.45, 0.3, 0.5], atol=1e-6)
+
+
+def test_raster_kat_early_out_splat_not_accumulated(orc):
+    rows = [0.5, 0.5, 1.0, 0.0, 1.0, 0.999, 1.0, 0.0, 0.0, 0.0, 0.5, 0.5, 1.0, 0.0, 1.0, 0.999, 0.0, 1.0, 0.0, 0.0]
+    np.testing.assert_allclose(orc.rasterize_rows(rows, 1, 1).ravel(), [0.999, 0, 0, 0.999], atol=1e-6)
+
+
+def test_raster_kat_hard_and_smooth_cutoff(orc):
+    mid = float(np.float32(1.0 / 255.0))
+    rows = [0.5, 0.5, 1.0, 0.0, 1.0, mid, 1.0, 0.0, 0.0, 0.0]
+    np.testing.assert_allclose(orc.rasterize_rows(rows, 1, 1).ravel(), [mid, 0, 0, mid], atol=1e-7)
+    np.testing.assert_allclose(orc.rasterize_rows(rows, 1, 1, smooth=True).ravel(), [mid / 2, 0, 0, mid / 2],
+                               atol=1e-7)
+
+
+def test_tile_raster_matches_global_order_raster(orc):
+    """Binned tile rasterization equals compositing all depth-sorted splats (raster_oracle.rs:306-329, 2e-5)."""
+    from brush_b200.splats import config1_scene
+
+    splats, cam, size, _ = config1_scene("cpu", seed=7, n=2048)
+    r = orc.RenderResult(cam, size, splats.transforms.numpy(), splats.sh_coeffs.numpy(),
+                         splats.raw_opacities.numpy())
+    rows = r.projected[r.depth_order][:, :10]
+    glob = orc.rasterize_rows(rows, size[0], size[1])
+    assert np.abs(glob - r.image).max() <= 2e-5
+
+
+def test_sort_kat_stable_for_every_pass_count(orc):
+    n = 4099
+    i = np.arange(n, dtype=np.uint64)
+    group = ((i * 73) % 1021).astype(np.uint64)
+    prod = (group * 0x9E3779B9) & 0xFFFFFFFF
+    keys = ((((prod << 7) | (prod >> 25)) & 0xFFFFFFFF) ^ 0xA5A55A5A).astype(np.uint32)
+    vals = np.arange(n, dtype=np.uint32)
+    for bits in [0, 4, 8, 12, 13, 14, 15, 16, 20, 28, 32]:
+        eff = (bits + 3) // 4 * 4
+        mask = 0xFFFFFFFF if eff == 32 else (1 << eff) - 1
+        order = np.argsort(keys & np.uint32(mask), kind="stable")
+        ko, vo = orc.radix_argsort(keys, vals, bits)
+        assert (ko == keys[order]).all() and (vo == vals[order]).all(), bits
+
+
+def test_prefix_sum_kats(orc):
+    assert list(orc.prefix_sum([1, 1, 1, 1])) == [1, 2, 3, 4]
+    for n in [255, 256, 257]:
+        d = (np.arange(n) % 7).astype(np.uint32)
+        assert (orc.prefix_sum(d) == np.cumsum(d).astype(np.uint32)).all()
+    d = np.array([2, 0, 32, 512, 30965] * 100, dtype=np.uint32)
+    assert (orc.prefix_sum(d) == np.cumsum(d).astype(np.uint32)).all()
+
+
+def test_tile_offset_kat_runs_and_sentinel(orc):
+    runs = [31, 1, 223, 1, 1791, 1, 17, 0]
+    ids, exp = [], np.zeros((8, 2), np.uint32)
+    for tid, rl in enumerate(runs):
+        if rl == 0:
+            continue
+        s = len(ids)
+        ids += [tid] * rl
+        exp[tid] = (s, len(ids))
+    ids += [8] * 13
+    assert (orc.tile_offsets(np.array(ids, np.uint32), 8) == exp).all()
+
+
+def test_shared_exp_log_accuracy(orc):
+    rng = np.random.default_rng(0)
+    xs = np.concatenate([rng.uniform(-103, 88, 20000), rng.uniform(-2, 2, 20000)]).astype(np.float32)
+    for x in xs[::7]:
+        e = orc.expf(x)
+        ref = np.float32(math.exp(float(x)))
+        assert abs(np.int64(np.float32(e).view(np.int32)) - np.int64(ref.view(np.int32))) <= 1
+    for x in np.abs(xs[::7]) + np.float32(1e-3):
+        lg = orc.logf(x)
+        ref = np.float32(math.log(float(x)))
+        assert abs(np.int64(np.float32(lg).view(np.int32)) - np.int64(ref.view(np.int32))) <= 2
+
+
+def test_gauss_taps_normalised(orc):
+    w = orc.gauss_taps()
+    assert abs(float(w.sum()) - 1.0) < 1e-6 and np.allclose(w, w[::-1])
