@@ -1,26 +1,41 @@
 // raster_bwd.cu - tile rasterizer, backward.
 //
 // Restates rasterize_backwards_kernel
-// (crates/brush-render-bwd/src/kernels/rasterize_backwards.rs:79-443). One
-// warp per tile; each lane owns one splat of the current 32-splat batch and
-// accumulates that splat's 11 gradient lanes in registers. Per-pixel state
-// (residual colour C - sum(front contributions) - T_final*bg, and
-// transmittance T) lives in shared memory and is replayed front to back on a
-// diagonal wavefront: at step i lane l handles pixel i-l, so every pixel sees
-// the splats in depth order. The replay performs exactly the forward pass's
-// float operations, so T and every accept / early-out decision match the
-// forward bit-for-bit. Gradients leave registers once per (splat, tile) as
+// (crates/brush-render-bwd/src/kernels/rasterize_backwards.rs:79-443) with a
+// pixel-parallel schedule: one 256-thread block per 16x16 tile, one pixel per
+// thread in the forward's Morton order. Each thread replays its pixel front to
+// back exactly as the forward did (same float operations, so T and every
+// accept / early-out decision match the forward bit-for-bit), carrying the
+// residual colour C - T_final*bg - (front contributions) in registers as the
+// reference does. Per splat, a warp whose 8x4 pixel patch misses the splat's
+// pixel box skips it uniformly; otherwise each lane forms its pixel's
+// contribution to the splat's 10 gradient lanes, the warp sums them with a
+// 16-value butterfly (16 shuffles), the sums are accumulated per splat in
+// shared memory across the tile's 8 warps, and each (splat, tile) leaves with
 // three 16-byte vector atomics (red.global.add.v4.f32) into a 12-lane row.
+// The alpha / T chain uses exact IEEE operations; the gradient arithmetic,
+// which is tolerance-checked, uses fused multiply-adds and fast reciprocals.
 #include "splat_math.cuh"
 
 namespace bsx {
 
 namespace {
 
-constexpr int kBwdWarps = 4;  // tiles per block
-constexpr int kBwdThreads = kBwdWarps * 32;
+constexpr int kBwdThreads = 256;
 constexpr float kMarginHard = 1.0e-3f;
 constexpr float kMarginSmooth = 0.25f;
+constexpr int kGradLanes = 10;  // xy(2) conic(3) rgb(3) alpha refine
+
+struct BwdArgs {
+    const uint32_t* isect_gid;
+    const uint32_t* tile_offsets;
+    const float* projected;
+    const float* image;     // [H,W,4]
+    const float* v_output;  // [H,W,4]
+    float* v_grad;          // [N,12]
+    uint32_t tbw, num_tiles, w, h;
+    float bg_r, bg_g, bg_b;
+};
 
 __device__ __forceinline__ float cutoff_weight(float a) {
     const float mid = 1.0f / 255.0f, band = 1.0e-3f;
@@ -35,123 +50,211 @@ __device__ __forceinline__ float cutoff_weight_deriv(float a) {
     return inside ? (6.0f * t - 6.0f * t * t) / band : 0.0f;
 }
 
-struct BwdArgs {
-    const uint32_t* isect_gid;
-    const uint32_t* tile_offsets;
-    const float* projected;
-    const float* image;     // [H,W,4]
-    const float* v_output;  // [H,W,4]
-    float* v_grad;          // [N,12]
-    uint32_t tbw, num_tiles, w, h;
-    float bg_r, bg_g, bg_b;
-};
+__device__ __forceinline__ uint32_t compact_bits_16(uint32_t v) {
+    uint32_t x = v & 0x55555555u;
+    x = (x | (x >> 1)) & 0x33333333u;
+    x = (x | (x >> 2)) & 0x0F0F0F0Fu;
+    x = (x | (x >> 4)) & 0x00FF00FFu;
+    x = (x | (x >> 8)) & 0x0000FFFFu;
+    return x;
+}
+
+// Tile-local pixel masks of a splat (bit x: column x, bit 16+y: row y) that
+// can hold a pixel with sigma <= thr: exact ellipse half-extents padded by one
+// pixel. Zero when nothing can pass.
+__device__ __forceinline__ uint32_t splat_pixel_mask(float sx, float sy, float c00, float c01, float c11, float thr,
+                                                     uint32_t ox, uint32_t oy) {
+    const float det = c00 * c11 - c01 * c01;
+    if (!(det > 0.0f) || !(thr >= 0.0f)) return 0u;
+    const float inv = 1.0f / det;
+    const float ex = sqrtf(2.0f * thr * c11 * inv) + 1.0f;
+    const float ey = sqrtf(2.0f * thr * c00 * inv) + 1.0f;
+    const float lx = sx - 0.5f - (float)ox, ly = sy - 0.5f - (float)oy;
+    const int x0 = max(0, (int)floorf(fmaxf(lx - ex, -1.0f)));
+    const int x1 = min(15, (int)ceilf(fminf(lx + ex, 16.0f)));
+    const int y0 = max(0, (int)floorf(fmaxf(ly - ey, -1.0f)));
+    const int y1 = min(15, (int)ceilf(fminf(ly + ey, 16.0f)));
+    if (x0 > x1 || y0 > y1) return 0u;
+    const uint32_t xm = ((0xffffu >> (15 - x1)) >> x0) << x0;
+    const uint32_t ym = ((0xffffu >> (15 - y1)) >> y0) << y0;
+    return xm | (ym << 16);
+}
+
+// Sum 16 per-lane values over the warp. Returns, on lane l, the total of
+// value (l >> 1). Butterfly that halves the live values at each level:
+// 8 + 4 + 2 + 1 + 1 shuffles.
+__device__ __forceinline__ float warp_sum16(float (&v)[16], int lane) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const bool up = lane & 16;
+        const float send = up ? v[k] : v[k + 8];
+        const float keep = up ? v[k + 8] : v[k];
+        v[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const bool up = lane & 8;
+        const float send = up ? v[k] : v[k + 4];
+        const float keep = up ? v[k + 4] : v[k];
+        v[k] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const bool up = lane & 4;
+        const float send = up ? v[k] : v[k + 2];
+        const float keep = up ? v[k + 2] : v[k];
+        v[k] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    }
+    {
+        const bool up = lane & 2;
+        const float send = up ? v[0] : v[1];
+        const float keep = up ? v[1] : v[0];
+        v[0] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+    }
+    return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
+}
 
 template <bool SMOOTH, bool REFINE>
 __global__ void __launch_bounds__(kBwdThreads) raster_bwd_kernel(const BwdArgs a) {
-    __shared__ float4 s_state[kBwdWarps][kTilePixels];
+    __shared__ float4 s_a[kBwdThreads];  // x, y, c00, c01
+    __shared__ float4 s_b[kBwdThreads];  // c11, opacity, r, g
+    __shared__ float2 s_c[kBwdThreads];  // b, ln(255 o) + margin
+    __shared__ uint32_t s_mask[kBwdThreads];
+    __shared__ uint32_t s_gid[kBwdThreads];
+    __shared__ float s_grad[kBwdThreads][kGradLanes + 1];
+
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const uint32_t tile = blockIdx.x * kBwdWarps + warp;
-    if (tile >= a.num_tiles) return;
+    const uint32_t tile = blockIdx.x;
+    const uint32_t ox = (tile % a.tbw) * kTile, oy = (tile / a.tbw) * kTile;
+    const uint32_t lx = compact_bits_16(threadIdx.x), ly = compact_bits_16(threadIdx.x >> 1);
+    // the warp's 8x4 Morton patch as column / row masks
+    const uint32_t wcols = 0xffu << (8 * ((warp >> 1) & 1));
+    const uint32_t wrows = 0xfu << (4 * (warp & 1) + 8 * ((warp >> 2) & 1));
+    const uint32_t px = ox + lx, py = oy + ly;
+    const bool inside = px < a.w && py < a.h;
     const uint32_t lo = __ldg(a.tile_offsets + tile * 2), hi = __ldg(a.tile_offsets + tile * 2 + 1);
     if (hi <= lo) return;
-    const uint32_t ox = (tile % a.tbw) * kTile, oy = (tile / a.tbw) * kTile;
-    float4* st = s_state[warp];
-    const float4* img4 = reinterpret_cast<const float4*>(a.image);
-    const float4* vo4 = reinterpret_cast<const float4*>(a.v_output);
-    for (int p = lane; p < kTilePixels; p += 32) {
-        const uint32_t px = ox + (p % kTile), py = oy + (p / kTile);
-        float4 s = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        if (px < a.w && py < a.h) {
-            const float4 o = __ldg(img4 + (size_t)py * a.w + px);
-            const float tf = 1.0f - o.w;
-            s = make_float4(o.x - tf * a.bg_r, o.y - tf * a.bg_g, o.z - tf * a.bg_b, 1.0f);
-        }
-        st[p] = s;
-    }
-    __syncwarp();
     const float margin = SMOOTH ? kMarginSmooth : kMarginHard;
+
+    // Per-pixel constants and replay state (registers).
+    float T = 1.0f, sr = 0.0f, sg = 0.0f, sb = 0.0f;
+    float vor = 0.0f, vog = 0.0f, vob = 0.0f, vow = 0.0f, inv_fa = 0.0f;
+    bool done = !inside;
+    if (inside) {
+        const size_t pid = (size_t)py * a.w + px;
+        const float4 o = __ldg(reinterpret_cast<const float4*>(a.image) + pid);
+        const float tf = 1.0f - o.w;
+        sr = o.x - tf * a.bg_r;
+        sg = o.y - tf * a.bg_g;
+        sb = o.z - tf * a.bg_b;
+        const float4 vo = __ldg(reinterpret_cast<const float4*>(a.v_output) + pid);
+        vor = vo.x;
+        vog = vo.y;
+        vob = vo.z;
+        vow = (vo.w - (a.bg_r * vo.x + a.bg_g * vo.y + a.bg_b * vo.z)) * tf;
+        inv_fa = __frcp_rn(bsx_max(o.w, 1.0e-5f));
+    }
+    const float pcx = (float)px + 0.5f, pcy = (float)py + 0.5f;
     const float wf = (float)a.w, hf = (float)a.h;
-    const uint32_t count = hi - lo;
-    for (uint32_t b0 = 0; b0 < count; b0 += 32) {
-        const uint32_t nb = min(32u, count - b0);
-        const bool active = (uint32_t)lane < nb;
-        uint32_t g = 0;
-        float4 A = make_float4(0, 0, 0, 0), B = A, C = A;
-        if (active) {
-            g = __ldg(a.isect_gid + lo + b0 + lane);
+
+    for (uint32_t batch = lo; batch < hi; batch += kBwdThreads) {
+        if (__syncthreads_count(done) == kBwdThreads) break;
+        const uint32_t n = min((uint32_t)kBwdThreads, hi - batch);
+        if (threadIdx.x < n) {
+            const uint32_t g = __ldg(a.isect_gid + batch + threadIdx.x);
             const float4* row = reinterpret_cast<const float4*>(a.projected + (size_t)g * BSX_PROJECTED_LANES);
-            A = __ldg(row);
-            B = __ldg(row + 1);
-            C = __ldg(row + 2);
+            const float4 ra = __ldg(row), rb = __ldg(row + 1), rc = __ldg(row + 2);
+            s_a[threadIdx.x] = ra;
+            s_b[threadIdx.x] = rb;
+            s_c[threadIdx.x] = make_float2(rc.x, rc.z + margin);
+            s_mask[threadIdx.x] = splat_pixel_mask(ra.x, ra.y, ra.z, ra.w, rb.x, rc.z + margin, ox, oy);
+            s_gid[threadIdx.x] = g;
+#pragma unroll
+            for (int k = 0; k <= kGradLanes; ++k) s_grad[threadIdx.x][k] = 0.0f;
         }
-        const float sx = A.x, sy = A.y, c00 = A.z, c01 = A.w, c11 = B.x, ca = B.y;
-        const float craw = B.z, cgraw = B.w, cbraw = C.x, pt = C.z;
-        const float clr = bsx_max(craw, 0.0f), clg = bsx_max(cgraw, 0.0f), clb = bsx_max(cbraw, 0.0f);
-        float g_xy_x = 0, g_xy_y = 0, g_c0 = 0, g_c1 = 0, g_c2 = 0, g_r = 0, g_g = 0, g_b = 0, g_a = 0, g_ref = 0;
-        const uint32_t steps = nb + kTilePixels - 1;
-        for (uint32_t i = 0; i < steps; ++i) {
-            const int p = (int)i - lane;
-            if (active && p >= 0 && p < kTilePixels) {
-                float4 s = st[p];
-                if (s.w > 1.0e-4f) {
-                    const uint32_t px = ox + (p % kTile), py = oy + (p / kTile);
-                    const float dx = sx - ((float)px + 0.5f);
-                    const float dy = sy - ((float)py + 0.5f);
-                    const float sigma = 0.5f * (c00 * dx * dx + c11 * dy * dy) + c01 * dx * dy;
-                    if (sigma <= pt + margin) {
-                        const float gauss = bsx_expf(-sigma);
-                        const float alpha = bsx_min(0.999f, ca * gauss);
-                        const float wc = SMOOTH ? cutoff_weight(alpha) : (alpha >= 1.0f / 255.0f ? 1.0f : 0.0f);
-                        if (sigma >= 0.0f && wc > 0.0f) {
-                            const float ae = alpha * wc;
-                            const float next_t = s.w * (1.0f - ae);
-                            if (next_t <= 1.0e-4f) {
-                                st[p].w = 0.0f;
-                            } else {
-                                const float vis = ae * s.w;
-                                const size_t pid = (size_t)py * a.w + px;
-                                const float4 vo = __ldg(vo4 + pid);
-                                const float fa = __ldg(a.image + pid * 4 + 3);
-                                const float tf = 1.0f - fa;
-                                const float vow = (vo.w - (a.bg_r * vo.x + a.bg_g * vo.y + a.bg_b * vo.z)) * tf;
-                                g_r += craw >= 0.0f ? vis * vo.x : 0.0f;
-                                g_g += cgraw >= 0.0f ? vis * vo.y : 0.0f;
-                                g_b += cbraw >= 0.0f ? vis * vo.z : 0.0f;
-                                const float ra = 1.0f / (1.0f - ae);
-                                const float dot_rgb = ((s.w * clr - s.x) * vo.x + (s.w * clg - s.y) * vo.y +
-                                                       (s.w * clb - s.z) * vo.z) * ra;
-                                const float nrx = s.x - vis * clr, nry = s.y - vis * clg, nrz = s.z - vis * clb;
-                                const float vae = dot_rgb + vow * ra;
-                                const float dw = SMOOTH ? cutoff_weight_deriv(alpha) : 0.0f * alpha;
-                                const float valpha = vae * (wc + alpha * dw);
-                                const float vsig = -alpha * valpha;
-                                const float vxx = vsig * (c00 * dx + c01 * dy);
-                                const float vxy = vsig * (c01 * dx + c11 * dy);
-                                if (ca * gauss <= 0.999f) {
-                                    g_c0 += 0.5f * vsig * dx * dx;
-                                    g_c1 += vsig * dx * dy;
-                                    g_c2 += 0.5f * vsig * dy * dy;
-                                    g_xy_x += vxx;
-                                    g_xy_y += vxy;
-                                    g_a += valpha * gauss;
-                                    if (REFINE) {
-                                        const float len = sqrtf(vxx * wf * vxx * wf + vxy * hf * vxy * hf);
-                                        g_ref += len / bsx_max(fa, 1.0e-5f);
-                                    }
+        __syncthreads();
+        for (uint32_t t = 0; t < n; ++t) {
+            const uint32_t m = s_mask[t];
+            if (!(m & wcols) || !((m >> 16) & wrows)) continue;  // warp-uniform
+            if (__all_sync(0xffffffffu, done)) break;             // warp-uniform
+            float gv[16];
+#pragma unroll
+            for (int k = 0; k < 16; ++k) gv[k] = 0.0f;
+            bool contrib = false;
+            if (!done && ((m >> lx) & (m >> (16 + ly)) & 1u)) {
+                const float4 A = s_a[t];
+                const float4 B = s_b[t];
+                const float2 Cc = s_c[t];
+                const float sx = A.x, sy = A.y, c00 = A.z, c01 = A.w, c11 = B.x, ca = B.y;
+                // exact forward arithmetic
+                const float sigma = calc_sigma(pcx, pcy, c00, c01, c11, sx, sy);
+                if (sigma <= Cc.y) {
+                    const float gauss = bsx_expf(-sigma);
+                    const float alpha = bsx_min(0.999f, ca * gauss);
+                    const float wc = SMOOTH ? cutoff_weight(alpha) : (alpha >= 1.0f / 255.0f ? 1.0f : 0.0f);
+                    if (sigma >= 0.0f && wc > 0.0f) {
+                        const float ae = alpha * wc;
+                        const float next_t = T * (1.0f - ae);
+                        if (next_t <= 1.0e-4f) {
+                            done = true;
+                        } else {
+                            contrib = true;
+                            const float craw = B.z, cgraw = B.w, cbraw = Cc.x;
+                            const float clr = bsx_max(craw, 0.0f), clg = bsx_max(cgraw, 0.0f),
+                                        clb = bsx_max(cbraw, 0.0f);
+                            const float vis = ae * T;
+                            gv[5] = craw >= 0.0f ? vis * vor : 0.0f;
+                            gv[6] = cgraw >= 0.0f ? vis * vog : 0.0f;
+                            gv[7] = cbraw >= 0.0f ? vis * vob : 0.0f;
+                            const float ra = __fdividef(1.0f, 1.0f - ae);
+                            float dot_rgb = __fmaf_rn(T, clr, -sr) * vor;
+                            dot_rgb = __fmaf_rn(__fmaf_rn(T, clg, -sg), vog, dot_rgb);
+                            dot_rgb = __fmaf_rn(__fmaf_rn(T, clb, -sb), vob, dot_rgb);
+                            const float vae = (dot_rgb + vow) * ra;
+                            const float valpha = SMOOTH ? vae * (wc + alpha * cutoff_weight_deriv(alpha)) : vae;
+                            const float vsig = -alpha * valpha;
+                            const float dx = sx - pcx, dy = sy - pcy;
+                            const float vxx = vsig * __fmaf_rn(c00, dx, c01 * dy);
+                            const float vxy = vsig * __fmaf_rn(c01, dx, c11 * dy);
+                            if (ca * gauss <= 0.999f) {
+                                const float hv = 0.5f * vsig;
+                                gv[0] = vxx;
+                                gv[1] = vxy;
+                                gv[2] = hv * dx * dx;
+                                gv[3] = vsig * dx * dy;
+                                gv[4] = hv * dy * dy;
+                                gv[8] = valpha * gauss;
+                                if (REFINE) {
+                                    const float ax = vxx * wf, ay = vxy * hf;
+                                    const float q = __fmaf_rn(ax, ax, ay * ay);
+                                    gv[9] = q * rsqrtf(fmaxf(q, 1e-38f)) * inv_fa;
                                 }
-                                st[p] = make_float4(nrx, nry, nrz, next_t);
                             }
+                            sr = __fmaf_rn(-vis, clr, sr);
+                            sg = __fmaf_rn(-vis, clg, sg);
+                            sb = __fmaf_rn(-vis, clb, sb);
+                            T = next_t;
                         }
                     }
                 }
             }
-            __syncwarp();
+            if (__any_sync(0xffffffffu, contrib)) {
+                const float tot = warp_sum16(gv, lane);
+                const int k = lane >> 1;
+                if (!(lane & 1) && k < kGradLanes) atomicAdd(&s_grad[t][k], tot);
+            }
         }
-        if (active) {
-            float4* dst = reinterpret_cast<float4*>(a.v_grad + (size_t)g * kGradStride);
-            atomicAdd(dst, make_float4(g_xy_x, g_xy_y, g_c0, g_c1));
-            atomicAdd(dst + 1, make_float4(g_c2, g_r, g_g, g_b));
-            atomicAdd(dst + 2, make_float4(g_a, g_ref, 0.0f, 0.0f));
+        __syncthreads();
+        if (threadIdx.x < n) {
+            const float* sgr = s_grad[threadIdx.x];
+            bool any = false;
+#pragma unroll
+            for (int k = 0; k < kGradLanes; ++k) any = any || sgr[k] != 0.0f;
+            if (!any) continue;
+            float4* dst = reinterpret_cast<float4*>(a.v_grad + (size_t)s_gid[threadIdx.x] * kGradStride);
+            atomicAdd(dst, make_float4(sgr[0], sgr[1], sgr[2], sgr[3]));
+            atomicAdd(dst + 1, make_float4(sgr[4], sgr[5], sgr[6], sgr[7]));
+            atomicAdd(dst + 2, make_float4(sgr[8], sgr[9], 0.0f, 0.0f));
         }
     }
 }
@@ -175,7 +278,7 @@ bsx_status launch_raster_bwd(bsx_ctx* ctx, const uint32_t* isect_gid, const uint
     a.bg_r = bg[0];
     a.bg_g = bg[1];
     a.bg_b = bg[2];
-    const uint32_t blocks = (a.num_tiles + kBwdWarps - 1) / kBwdWarps;
+    const uint32_t blocks = a.num_tiles;
     prof_begin(ctx);
     if (smooth) {
         if (refine) raster_bwd_kernel<true, true><<<blocks, kBwdThreads, 0, ctx->stream>>>(a);

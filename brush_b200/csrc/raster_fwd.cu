@@ -42,6 +42,27 @@ __device__ __forceinline__ float cutoff_weight(float a) {
     return t * t * (3.0f - 2.0f * t);
 }
 
+// Tile-local pixel masks of a splat: bit x of the low half / bit y of the high
+// half is set when column x / row y of the tile can hold a pixel with
+// sigma <= thr (exact ellipse half-extents, padded by one pixel).
+__device__ __forceinline__ uint32_t splat_pixel_mask(float sx, float sy, float c00, float c01, float c11, float thr,
+                                                     uint32_t ox, uint32_t oy) {
+    const float det = c00 * c11 - c01 * c01;
+    if (!(det > 0.0f) || !(thr >= 0.0f)) return 0u;
+    const float inv = 1.0f / det;
+    const float ex = sqrtf(2.0f * thr * c11 * inv) + 1.0f;
+    const float ey = sqrtf(2.0f * thr * c00 * inv) + 1.0f;
+    const float lx = sx - 0.5f - (float)ox, ly = sy - 0.5f - (float)oy;
+    const int x0 = max(0, (int)floorf(fmaxf(lx - ex, -1.0f)));
+    const int x1 = min(15, (int)ceilf(fminf(lx + ex, 16.0f)));
+    const int y0 = max(0, (int)floorf(fmaxf(ly - ey, -1.0f)));
+    const int y1 = min(15, (int)ceilf(fminf(ly + ey, 16.0f)));
+    if (x0 > x1 || y0 > y1) return 0u;
+    const uint32_t xm = ((0xffffu >> (15 - x1)) >> x0) << x0;
+    const uint32_t ym = ((0xffffu >> (15 - y1)) >> y0) << y0;
+    return xm | (ym << 16);
+}
+
 struct FwdArgs {
     const uint32_t* isect_gid;
     uint32_t* tile_offsets;
@@ -58,14 +79,20 @@ __global__ void __launch_bounds__(kRasterThreads) raster_fwd_kernel(const FwdArg
     __shared__ float4 s_a[kRasterThreads];  // x, y, c00, c01
     __shared__ float4 s_b[kRasterThreads];  // c11, opacity, r, g
     __shared__ float4 s_c[kRasterThreads];  // b, depth, ln(255 o), 0
+    __shared__ uint32_t s_mask[kRasterThreads];
     __shared__ uint32_t s_gid[BWD ? kRasterThreads : 1];
     __shared__ int s_used[BWD ? kRasterThreads : 1];
     __shared__ uint32_t s_max_useful;
 
     const uint32_t tile = blockIdx.x;
     const uint32_t tx = tile % a.tbw, ty = tile / a.tbw;
-    const uint32_t px = tx * kTile + compact_bits_16(threadIdx.x);
-    const uint32_t py = ty * kTile + compact_bits_16(threadIdx.x >> 1);
+    const uint32_t lxp = compact_bits_16(threadIdx.x), lyp = compact_bits_16(threadIdx.x >> 1);
+    // the warp's 8x4 Morton patch as column / row masks (for warp-uniform skips)
+    const uint32_t wid = threadIdx.x >> 5;
+    const uint32_t wcols = 0xffu << (8 * ((wid >> 1) & 1));
+    const uint32_t wrows = 0xfu << (4 * (wid & 1) + 8 * ((wid >> 2) & 1));
+    const uint32_t px = tx * kTile + lxp;
+    const uint32_t py = ty * kTile + lyp;
     const bool inside = px < a.w && py < a.h;
     const float pcx = (float)px + 0.5f, pcy = (float)py + 0.5f;
     const uint32_t lo = a.tile_offsets[tile * 2], hi = a.tile_offsets[tile * 2 + 1];
@@ -85,9 +112,11 @@ __global__ void __launch_bounds__(kRasterThreads) raster_fwd_kernel(const FwdArg
         if (threadIdx.x < n) {
             const uint32_t g = __ldg(a.isect_gid + batch + threadIdx.x);
             const float4* row = reinterpret_cast<const float4*>(a.projected + (size_t)g * BSX_PROJECTED_LANES);
-            s_a[threadIdx.x] = __ldg(row);
-            s_b[threadIdx.x] = __ldg(row + 1);
-            s_c[threadIdx.x] = __ldg(row + 2);
+            const float4 ra = __ldg(row), rb = __ldg(row + 1), rc = __ldg(row + 2);
+            s_a[threadIdx.x] = ra;
+            s_b[threadIdx.x] = rb;
+            s_c[threadIdx.x] = rc;
+            s_mask[threadIdx.x] = splat_pixel_mask(ra.x, ra.y, ra.z, ra.w, rb.x, rc.z + margin, tx * kTile, ty * kTile);
             if (BWD) {
                 s_gid[threadIdx.x] = g;
                 s_used[threadIdx.x] = 0;
@@ -96,6 +125,9 @@ __global__ void __launch_bounds__(kRasterThreads) raster_fwd_kernel(const FwdArg
         __syncthreads();
         if (!done) {
             for (uint32_t t = 0; t < n; ++t) {
+                const uint32_t m = s_mask[t];
+                if (!(m & wcols) || !((m >> 16) & wrows)) continue;
+                if (!((m >> lxp) & (m >> (16 + lyp)) & 1u)) continue;
                 const float4 A = s_a[t];
                 const float c11 = s_b[t].x;
                 const float sigma = calc_sigma(pcx, pcy, A.z, A.w, c11, A.x, A.y);

@@ -20,6 +20,7 @@ import torch
 from . import _lib
 from .adam import AdamGroup, AdamScaled
 from .camera import Camera
+from .dist import reduce_gradients
 from .loss import ImageLossConfig, image_loss_fused
 from .render import render
 from .render_bwd import SplatGrads, project_bwd, rasterize_bwd
@@ -134,8 +135,8 @@ class SplatTrainer:
         image_loss_fused(out.out_img, gt_packed, lcfg, self.loss, self.v_output)
         rasterize_bwd(self.v_output, compute_refine_weight, self.v_combined)
         project_bwd(self.v_combined, self.n, self.c, self.grads)
-        if self.pg is not None and self.world > 1:
-            torch.distributed.all_reduce(self.flat_grad, group=self.pg)
+        grad_scale = reduce_gradients(self.flat_grad, self.grads.v_refine_weight if self.record is not None else None,
+                                      self.pg)
         lr_t, tscale, lr_sh, sh_cols, lr_op, lr_mean = self._lr_table()
         n, c = self.n, self.c
         if self.groups is None:
@@ -150,12 +151,8 @@ class SplatTrainer:
         g0.lr, g0.col_scale = lr_t, tscale
         g1.lr, g1.col_scale = lr_sh, sh_cols
         g2.lr = lr_op
-        self.adam.step(self.groups, grad_scale=1.0 / self.world)
+        self.adam.step(self.groups, grad_scale=grad_scale)
         if self.record is not None:
-            if self.pg is not None and self.world > 1:
-                # Identical densification inputs on every rank.
-                torch.distributed.all_reduce(self.grads.v_refine_weight, op=torch.distributed.ReduceOp.MAX,
-                                             group=self.pg)
             if compute_refine_weight:
                 self.record.gather_stats(self.grads.v_refine_weight, out.aux.visible, out.aux.max_radius)
         return TrainStepStats(out.aux.num_visible, out.aux.num_intersections, self.loss, lr_mean)
