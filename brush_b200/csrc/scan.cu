@@ -9,6 +9,8 @@
 // Decoupled Look-back", 2016). Every wait is bounded: on expiry the tile
 // records a device error and carries on, so the grid always terminates.
 // Sums are u32 and wrap, as the reference's.
+#include <mutex>
+
 #include "common.cuh"
 #include "lookback.cuh"
 
@@ -160,4 +162,72 @@ extern "C" bsx_status bsx_prefix_sum_u32(bsx_ctx* ctx, const uint32_t* d_in, uin
     if (!ctx || (n && (!d_in || !d_out))) return BSX_ERR_INVALID_ARG;
     cudaSetDevice(ctx->device);
     return bsx::scan_inclusive_u32(ctx, d_in, nullptr, n, d_out, nullptr);
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free prefix sum.
+//
+// For callers that must not allocate GPU memory: code running inside a
+// memory pool or arena that forbids foreign allocations, real-time loops
+// where cudaMalloc's implicit device synchronisation is unacceptable, and
+// plugin hosts that do not let a plugin create a bsx context (creating one
+// allocates its error word and pinned readback slots). The look-back state
+// of this scan lives in a fixed file-scope device array instead of a
+// context workspace, so a call enqueues one memset and one kernel and
+// allocates nothing.
+//
+// Limits and rules:
+//  - n <= BSX_PREFIX_SUM_NOALLOC_MAX_N (16,769,024); larger n is rejected.
+//  - The array is one per GPU that loads this library and stays resident
+//    until the process exits (32 KiB).
+//  - Every call shares the array, so calls whose execution overlaps on the
+//    GPU (different streams, or different host threads on the same device)
+//    race and produce wrong results; serialise them.
+//  - The first call on a device looks up the array's device address (with
+//    that device current); make that first call before any stream capture.
+//  - Device-side look-back waits are bounded; a timed-out wait is not
+//    reported by this entry point (it has no context to report into).
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr uint32_t kNoAllocTiles = 4094;  // 4094 * 4096 = 16,769,024 elements
+static __device__ __align__(256) uint64_t g_noalloc_scan_state[kNoAllocTiles + 2];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[256];  // device address of g_noalloc_scan_state, per device ordinal
+
+}  // namespace
+
+extern "C" bsx_status bsx_prefix_sum_u32_noalloc(const uint32_t* d_in, uint32_t n, uint32_t* d_out,
+                                                 void* cuda_stream) {
+    static_assert((uint64_t)kNoAllocTiles * bsx::kScanTile == BSX_PREFIX_SUM_NOALLOC_MAX_N, "limit mismatch");
+    if (n && (!d_in || !d_out)) return BSX_ERR_INVALID_ARG;
+    if (n > BSX_PREFIX_SUM_NOALLOC_MAX_N) return BSX_ERR_CAPACITY;
+    if (n == 0) return BSX_OK;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 256) return BSX_ERR_CUDA;
+    void* state = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_noalloc_mu);
+        if (!g_noalloc_ptr[dev]) {
+            // Host code cannot use the array's name as a device address; ask the
+            // runtime for this device's copy (the current device is `dev`).
+            void* p = nullptr;
+            if (cudaGetSymbolAddress(&p, g_noalloc_scan_state) != cudaSuccess || !p) return BSX_ERR_CUDA;
+            g_noalloc_ptr[dev] = p;
+        }
+        state = g_noalloc_ptr[dev];
+    }
+    cudaStream_t stream = (cudaStream_t)cuda_stream;
+    const uint32_t tiles = (uint32_t)(((uint64_t)n + bsx::kScanTile - 1) / bsx::kScanTile);
+    uint64_t* status = static_cast<uint64_t*>(state);
+    // The look-back words and the ticket must start at zero on every call.
+    if (cudaMemsetAsync(status, 0, bsx::scan_status_words(tiles) * sizeof(uint64_t), stream) != cudaSuccess)
+        return BSX_ERR_CUDA;
+    uint32_t* ticket = reinterpret_cast<uint32_t*>(status + tiles);
+    const int vec_in = ((uintptr_t)d_in % 16) == 0;
+    const int vec_out = ((uintptr_t)d_out % 16) == 0;
+    bsx::scan_kernel<<<tiles, bsx::kScanThreads, 0, stream>>>(d_in, nullptr, n, d_out, status, ticket, nullptr,
+                                                                nullptr, vec_in, vec_out);
+    return cudaGetLastError() == cudaSuccess ? BSX_OK : BSX_ERR_CUDA;
 }

@@ -222,6 +222,18 @@ BSX_API bsx_status bsx_radix_argsort_u32(bsx_ctx* ctx, const uint32_t* d_keys, c
                                  uint32_t sorting_bits, uint32_t* d_keys_out, uint32_t* d_values_out);
 /* Inclusive prefix sum (u32, wrapping), crates/brush-prefix-sum/src/lib.rs:11-87. */
 BSX_API bsx_status bsx_prefix_sum_u32(bsx_ctx* ctx, const uint32_t* d_in, uint32_t n, uint32_t* d_out);
+/* Allocation-free variant of bsx_prefix_sum_u32 (no counterpart in the
+ * reference: an addition of this library for callers that cannot allocate GPU
+ * memory, e.g. inside a foreign memory pool, in a real-time loop that cannot
+ * afford cudaMalloc's synchronisation, or in a host that does not let a plugin
+ * create a context). Same result as bsx_prefix_sum_u32; runs on the current
+ * device and the given stream; needs no context. Its scratch is one fixed
+ * device array per GPU (32 KiB, resident until exit) shared by all calls:
+ * calls that overlap on the GPU race, so serialise them. n is limited to
+ * BSX_PREFIX_SUM_NOALLOC_MAX_N (BSX_ERR_CAPACITY beyond). The first call on a
+ * device resolves the array's address and should precede any stream capture. */
+#define BSX_PREFIX_SUM_NOALLOC_MAX_N 16769024u
+BSX_API bsx_status bsx_prefix_sum_u32_noalloc(const uint32_t* d_in, uint32_t n, uint32_t* d_out, void* cuda_stream);
 /* [start,end) per tile from sorted tile ids; ids >= num_tiles are sentinels
  * (crates/brush-render/src/get_tile_offset.rs:10-62). d_offsets is zeroed first. */
 BSX_API bsx_status bsx_get_tile_offsets(bsx_ctx* ctx, const uint32_t* d_tile_ids, uint32_t n, uint32_t num_tiles,
