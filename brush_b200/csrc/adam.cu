@@ -18,7 +18,7 @@ namespace {
 
 constexpr int kAdamThreads = 256;
 constexpr int kMaxGroups = 4;
-constexpr int kMaxCols = 64;
+constexpr int kMaxCols = 80;            // SH degree 4: 25 coefficients x 3
 constexpr uint32_t kTileFloats = 4096;  // contiguous floats per block (a whole number of rows)
 
 struct AdamGroupDev {
@@ -27,6 +27,7 @@ struct AdamGroupDev {
     float* m;
     float* v;
     uint32_t rows, cols, tile_rows;
+    float inv_cols;
     float lr;
     int reduce;
     int has_scale;
@@ -38,14 +39,20 @@ struct AdamGroupDev {
 struct AdamArgs {
     AdamGroupDev g[kMaxGroups];
     int ngroups;
-    float b1, b2, eps, bc1, bc2, gscale;
+    float b1, b2, eps, inv_bc1, inv_bc2, gscale;
     int first;
 };
 
+// Row of element e of a tile (e < 4096, cols <= 80): the float quotient of
+// e + 0.5 is never within rounding distance of an integer.
+__device__ __forceinline__ uint32_t row_of(uint32_t e, float inv_cols) {
+    return (uint32_t)(((float)e + 0.5f) * inv_cols);
+}
+
 // One block = one contiguous tile of whole rows of one group. The gradient
-// tile is staged in shared memory with coalesced (float4) loads, per-row
-// second-moment means are formed there when reduce_moment_2 is set, and p, m,
-// v stream through once with coalesced loads and stores.
+// tile is staged in shared memory with coalesced float4 loads (accumulating
+// per-row sums of squares for reduce_moment_2 groups on the way), then p, m, v
+// stream through once with coalesced float4 loads and stores.
 __global__ void __launch_bounds__(kAdamThreads) adam_kernel(const __grid_constant__ AdamArgs a) {
     __shared__ __align__(16) float s_g[kTileFloats];
     __shared__ float s_v[kTileFloats];
@@ -59,84 +66,93 @@ __global__ void __launch_bounds__(kAdamThreads) adam_kernel(const __grid_constan
     const size_t base = (size_t)row0 * cols;
     const uint32_t count = nrows * cols;
     const float one_m_b1 = 1.0f - a.b1, one_m_b2 = 1.0f - a.b2;
-    if (G.vec) {
-        const float4* g4 = reinterpret_cast<const float4*>(G.grad + base);
-        for (uint32_t j = threadIdx.x; j < count / 4; j += kAdamThreads) {
-            float4 v = __ldg(g4 + j);
-            reinterpret_cast<float4*>(s_g)[j] = make_float4(v.x * a.gscale, v.y * a.gscale, v.z * a.gscale,
-                                                            v.w * a.gscale);
-        }
-        for (uint32_t j = (count / 4) * 4 + threadIdx.x; j < count; j += kAdamThreads)
-            s_g[j] = __ldg(G.grad + base + j) * a.gscale;
-    } else {
-        for (uint32_t j = threadIdx.x; j < count; j += kAdamThreads) s_g[j] = __ldg(G.grad + base + j) * a.gscale;
+    const bool vec = G.vec;
+    const uint32_t nvec = vec ? count / 4 : 0;
+    if (G.reduce)
+        for (uint32_t r = threadIdx.x; r < nrows; r += kAdamThreads) s_v[r] = 0.0f;
+    __syncthreads();
+    const bool row_quads = G.reduce && (cols % 4) == 0;  // a float4 never straddles two rows
+    for (uint32_t j = threadIdx.x; j < nvec; j += kAdamThreads) {
+        float4 v = __ldg(reinterpret_cast<const float4*>(G.grad + base) + j);
+        v = make_float4(v.x * a.gscale, v.y * a.gscale, v.z * a.gscale, v.w * a.gscale);
+        reinterpret_cast<float4*>(s_g)[j] = v;
+        if (row_quads) atomicAdd(&s_v[row_of(4 * j, G.inv_cols)], v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w);
+    }
+    for (uint32_t j = nvec * 4 + threadIdx.x; j < count; j += kAdamThreads) {
+        const float g = __ldg(G.grad + base + j) * a.gscale;
+        s_g[j] = g;
+        if (row_quads) atomicAdd(&s_v[row_of(j, G.inv_cols)], g * g);
     }
     __syncthreads();
     if (G.reduce) {
         for (uint32_t r = threadIdx.x; r < nrows; r += kAdamThreads) {
-            float s = 0.0f;
-            for (uint32_t c = 0; c < cols; ++c) {
-                const float g = s_g[r * cols + c];
-                s += g * g;
+            float s2;
+            if (row_quads) {
+                s2 = s_v[r];
+            } else {
+                s2 = 0.0f;
+                for (uint32_t c = 0; c < cols; ++c) {
+                    const float g = s_g[r * cols + c];
+                    s2 += g * g;
+                }
             }
-            const float gsq = s / (float)cols;
+            const float gsq = s2 * G.inv_cols;
             const float vr = a.first ? gsq * one_m_b2 : G.v[row0 + r] * a.b2 + gsq * one_m_b2;
             G.v[row0 + r] = vr;
             s_v[r] = vr;
         }
         __syncthreads();
     }
-    auto update = [&](uint32_t e, float p, float mm_old, float vv_old, float* p_out, float* m_out, float* v_out) {
-        const uint32_t c = e % cols;
-        const float g = s_g[e];
-        const float mm = a.first ? g * one_m_b1 : mm_old * a.b1 + g * one_m_b1;
+    // element update; c = column, r = row within the tile
+    auto upd = [&](float p, float g, float m_old, float v_old, uint32_t c, uint32_t r, float& po, float& mo,
+                   float& vo) {
+        const float mm = a.first ? g * one_m_b1 : m_old * a.b1 + g * one_m_b1;
         float vv;
         if (G.reduce) {
-            vv = s_v[e / cols];
+            vv = s_v[r];
         } else {
-            const float gsq = g * g;
-            vv = a.first ? gsq * one_m_b2 : vv_old * a.b2 + gsq * one_m_b2;
+            vv = a.first ? (g * g) * one_m_b2 : v_old * a.b2 + (g * g) * one_m_b2;
         }
-        const float upd = (mm / a.bc1) / (sqrtf(vv / a.bc2) + a.eps);
+        const float u = __fdividef(mm * a.inv_bc1, sqrtf(vv * a.inv_bc2) + a.eps);
         const float sc = G.has_scale ? G.scale[c] * G.lr : G.lr;
-        *p_out = p - upd * sc;
-        *m_out = mm;
-        *v_out = vv;
+        po = p - u * sc;
+        mo = mm;
+        vo = vv;
     };
-    if (G.vec) {
+    if (vec) {
         float4* p4 = reinterpret_cast<float4*>(G.param + base);
         float4* m4 = reinterpret_cast<float4*>(G.m + base);
         float4* v4 = reinterpret_cast<float4*>(G.v + base);
-        for (uint32_t j = threadIdx.x; j < count / 4; j += kAdamThreads) {
+        for (uint32_t j = threadIdx.x; j < nvec; j += kAdamThreads) {
+            const uint32_t e0 = 4 * j;
+            uint32_t r = row_of(e0, G.inv_cols);
+            uint32_t c = e0 - r * cols;
             const float4 p = p4[j];
+            const float4 g = reinterpret_cast<const float4*>(s_g)[j];
             const float4 m = a.first ? make_float4(0, 0, 0, 0) : m4[j];
             const float4 v = (G.reduce || a.first) ? make_float4(0, 0, 0, 0) : v4[j];
             float4 po, mo, vo;
-            update(4 * j + 0, p.x, m.x, v.x, &po.x, &mo.x, &vo.x);
-            update(4 * j + 1, p.y, m.y, v.y, &po.y, &mo.y, &vo.y);
-            update(4 * j + 2, p.z, m.z, v.z, &po.z, &mo.z, &vo.z);
-            update(4 * j + 3, p.w, m.w, v.w, &po.w, &mo.w, &vo.w);
+            upd(p.x, g.x, m.x, v.x, c, r, po.x, mo.x, vo.x);
+            if (++c == cols) { c = 0; ++r; }
+            upd(p.y, g.y, m.y, v.y, c, r, po.y, mo.y, vo.y);
+            if (++c == cols) { c = 0; ++r; }
+            upd(p.z, g.z, m.z, v.z, c, r, po.z, mo.z, vo.z);
+            if (++c == cols) { c = 0; ++r; }
+            upd(p.w, g.w, m.w, v.w, c, r, po.w, mo.w, vo.w);
             p4[j] = po;
             m4[j] = mo;
             if (!G.reduce) v4[j] = vo;
         }
-        for (uint32_t e = (count / 4) * 4 + threadIdx.x; e < count; e += kAdamThreads) {
-            float po, mo, vo;
-            update(e, G.param[base + e], a.first ? 0.0f : G.m[base + e],
-                   (G.reduce || a.first) ? 0.0f : G.v[base + e], &po, &mo, &vo);
-            G.param[base + e] = po;
-            G.m[base + e] = mo;
-            if (!G.reduce) G.v[base + e] = vo;
-        }
-    } else {
-        for (uint32_t e = threadIdx.x; e < count; e += kAdamThreads) {
-            float po, mo, vo;
-            update(e, G.param[base + e], a.first ? 0.0f : G.m[base + e],
-                   (G.reduce || a.first) ? 0.0f : G.v[base + e], &po, &mo, &vo);
-            G.param[base + e] = po;
-            G.m[base + e] = mo;
-            if (!G.reduce) G.v[base + e] = vo;
-        }
+    }
+    for (uint32_t e = nvec * 4 + threadIdx.x; e < count; e += kAdamThreads) {
+        const uint32_t r = row_of(e, G.inv_cols);
+        const uint32_t c = e - r * cols;
+        float po, mo, vo;
+        upd(G.param[base + e], s_g[e], a.first ? 0.0f : G.m[base + e], (G.reduce || a.first) ? 0.0f : G.v[base + e],
+            c, r, po, mo, vo);
+        G.param[base + e] = po;
+        G.m[base + e] = mo;
+        if (!G.reduce) G.v[base + e] = vo;
     }
 }
 
@@ -163,15 +179,15 @@ extern "C" bsx_status bsx_adam_step(bsx_ctx* ctx, const bsx_adam_group* groups, 
     a.b1 = cfg->beta_1;
     a.b2 = cfg->beta_2;
     a.eps = cfg->epsilon;
-    a.bc1 = 1.0f - powi_f32(cfg->beta_1, cfg->step);
-    a.bc2 = 1.0f - powi_f32(cfg->beta_2, cfg->step);
+    a.inv_bc1 = 1.0f / (1.0f - powi_f32(cfg->beta_1, cfg->step));
+    a.inv_bc2 = 1.0f / (1.0f - powi_f32(cfg->beta_2, cfg->step));
     a.gscale = cfg->grad_scale;
     a.first = cfg->step == 1;
     uint32_t blocks = 0;
     for (int i = 0; i < num_groups; ++i) {
         const bsx_adam_group& s = groups[i];
         if (s.rows && (!s.d_param || !s.d_grad || !s.d_m || !s.d_v)) return fail(ctx, BSX_ERR_INVALID_ARG, "null adam buffer");
-        if (s.cols == 0 || s.cols > kMaxCols) return fail(ctx, BSX_ERR_SHAPE, "adam group cols must be in [1, 64]");
+        if (s.cols == 0 || s.cols > kMaxCols) return fail(ctx, BSX_ERR_SHAPE, "adam group cols must be in [1, 80]");
         AdamGroupDev& d = a.g[i];
         d.param = s.d_param;
         d.grad = s.d_grad;
@@ -179,6 +195,7 @@ extern "C" bsx_status bsx_adam_step(bsx_ctx* ctx, const bsx_adam_group* groups, 
         d.v = s.d_v;
         d.rows = s.rows;
         d.cols = s.cols;
+        d.inv_cols = 1.0f / (float)s.cols;
         d.lr = s.lr;
         d.reduce = s.reduce_moment_2;
         d.has_scale = s.h_col_scale != nullptr;

@@ -66,6 +66,8 @@ __device__ __forceinline__ float gt_eff(const LossArgs& a, int c, uint32_t y, ui
 }
 
 struct Ssim { float val, dmu1, dsig1, dsig12; };
+// SSIM and its partials (lib.rs:193-209, :480-500). Reciprocals are fast
+// (2 ulp); the loss is checked against the host restatement by tolerance.
 __device__ __forceinline__ Ssim ssim_terms(float o0, float o1, float o2, float o3, float o4) {
     const float mu1 = o0, mu2 = o2;
     const float mu1_sq = mu1 * mu1, mu2_sq = mu2 * mu2;
@@ -76,24 +78,25 @@ __device__ __forceinline__ Ssim ssim_terms(float o0, float o1, float o2, float o
     const float b = s1 + s2 + kC2;
     const float ct = 2.0f * mu1 * mu2 + kC1;
     const float dt = 2.0f * s12 + kC2;
-    Ssim r;
-    r.val = bsx_clamp((ct * dt) / (a * b), -1.0f, 1.0f);
-    const float inv_ab = 1.0f / (a * b);
+    const float inv_a = __fdividef(1.0f, a), inv_b = __fdividef(1.0f, b);
+    const float inv_ab = inv_a * inv_b;
     const float cd = ct * dt * inv_ab;
+    Ssim r;
+    r.val = bsx_clamp(cd, -1.0f, 1.0f);
     const bool clamped = cd < -1.0f || cd > 1.0f;
-    r.dmu1 = clamped ? 0.0f : 2.0f * mu2 * inv_ab * (dt - ct) - 2.0f * mu1 * cd * (1.0f / a - 1.0f / b);
-    r.dsig1 = clamped ? 0.0f : -cd / b;
+    r.dmu1 = clamped ? 0.0f : 2.0f * mu2 * inv_ab * (dt - ct) - 2.0f * mu1 * cd * (inv_a - inv_b);
+    r.dsig1 = clamped ? 0.0f : -cd * inv_b;
     r.dsig12 = clamped ? 0.0f : 2.0f * ct * inv_ab;
     return r;
 }
 
-// Stage (pred, gt_eff) of an (ext x ext) region starting `halo` pixels before
-// the tile into s[ext*ext*2]; out-of-image samples are zero.
+// Stage pred and effective gt of an (ext x ext) region starting `halo` pixels
+// before the tile into sx / sy (planar); out-of-image samples are zero.
 template <bool HWC4>
 __device__ __forceinline__ void stage_tile(const LossArgs& a, int c, int tile_x0, int tile_y0, int ext, int halo,
-                                           float* s) {
+                                           float* sx, float* sy) {
     for (int tid = threadIdx.x; tid < ext * ext; tid += blockDim.x) {
-        const int ly = tid / ext, lx = tid % ext;
+        const int ly = tid / ext, lx = tid - ly * ext;
         const int gy = tile_y0 + ly - halo, gx = tile_x0 + lx - halo;
         float pv = 0.0f, ge = 0.0f;
         if (gy >= 0 && gx >= 0 && gy < (int)a.h && gx < (int)a.w) {
@@ -101,66 +104,68 @@ __device__ __forceinline__ void stage_tile(const LossArgs& a, int c, int tile_x0
             float ga;
             ge = gt_eff(a, c, gy, gx, &ga);
         }
-        s[tid * 2] = pv;
-        s[tid * 2 + 1] = ge;
+        sx[tid] = pv;
+        sy[tid] = ge;
     }
 }
 
-// Horizontal moment blur: rows [0,rows) of the staged region, output columns
-// [0,cols) centred at staged column col + 5.
-__device__ __forceinline__ void hblur_moments(const float* s, int ext, int rows, int cols, const float* w, float* o) {
-    for (int tid = threadIdx.x; tid < rows * cols; tid += blockDim.x) {
-        const int ry = tid / cols, cx = tid % cols;
-        const int center = cx + kHalo;
+// Horizontal moment blur: rows [0,rows) of the staged region (row stride
+// ext), output columns [0,cols) centred at staged column col + 5; output is
+// five planes of rows*cols.
+__device__ __forceinline__ void hblur_moments(const float* X, const float* Y, int ext, int rows, int cols,
+                                              const float* w, float* o) {
+    const int plane = rows * cols;
+    for (int tid = threadIdx.x; tid < plane; tid += blockDim.x) {
+        const int ry = tid / cols, cx = tid - ry * cols;
+        const int center = ry * ext + cx + kHalo;
         float sx = 0.f, sx2 = 0.f, sy = 0.f, sy2 = 0.f, sxy = 0.f;
 #pragma unroll
         for (int d = 1; d < 6; ++d) {
             const float wd = w[5 - d];
-            const int il = (ry * ext + center - d) * 2, ir = (ry * ext + center + d) * 2;
-            const float xl = s[il], yl = s[il + 1], xr = s[ir], yr = s[ir + 1];
+            const float xl = X[center - d], yl = Y[center - d], xr = X[center + d], yr = Y[center + d];
             sx += (xl + xr) * wd;
             sx2 += (xl * xl + xr * xr) * wd;
             sy += (yl + yr) * wd;
             sy2 += (yl * yl + yr * yr) * wd;
             sxy += (xl * yl + xr * yr) * wd;
         }
-        const int ic = (ry * ext + center) * 2;
-        const float xc = s[ic], yc = s[ic + 1], wc = w[5];
+        const float xc = X[center], yc = Y[center], wc = w[5];
         sx += xc * wc;
         sx2 += xc * xc * wc;
         sy += yc * wc;
         sy2 += yc * yc * wc;
         sxy += xc * yc * wc;
-        float* dst = o + (ry * cols + cx) * 5;
-        dst[0] = sx;
-        dst[1] = sx2;
-        dst[2] = sy;
-        dst[3] = sy2;
-        dst[4] = sxy;
+        o[tid] = sx;
+        o[plane + tid] = sx2;
+        o[2 * plane + tid] = sy;
+        o[3 * plane + tid] = sy2;
+        o[4 * plane + tid] = sxy;
     }
 }
 
-__device__ __forceinline__ void vblur5(const float* hb, int cols, int center_row, int col, const float* w, float o[5]) {
+// Vertical blur of the five moment planes at (center_row, col).
+__device__ __forceinline__ void vblur5(const float* hb, int plane, int cols, int center_row, int col, const float* w,
+                                       float o[5]) {
 #pragma unroll
     for (int k = 0; k < 5; ++k) o[k] = 0.0f;
 #pragma unroll
     for (int d = 1; d < 6; ++d) {
         const float wd = w[5 - d];
-        const float* t = hb + ((center_row - d) * cols + col) * 5;
-        const float* b = hb + ((center_row + d) * cols + col) * 5;
+        const int it = (center_row - d) * cols + col, ib = (center_row + d) * cols + col;
 #pragma unroll
-        for (int k = 0; k < 5; ++k) o[k] += (t[k] + b[k]) * wd;
+        for (int k = 0; k < 5; ++k) o[k] += (hb[k * plane + it] + hb[k * plane + ib]) * wd;
     }
-    const float* cc = hb + (center_row * cols + col) * 5;
+    const int ic = center_row * cols + col;
 #pragma unroll
-    for (int k = 0; k < 5; ++k) o[k] += cc[k] * w[5];
+    for (int k = 0; k < 5; ++k) o[k] += hb[k * plane + ic] * w[5];
 }
 
 // Forward loss map, reference layout [C,H,W]; grid (tx, ty, C).
 template <bool HWC4>
-__global__ void __launch_bounds__(256) loss_fwd_kernel(const LossArgs a) {
-    __shared__ float s_tile[kShared * kShared * 2];
-    __shared__ float s_h[kShared * kBlock * 5];
+__global__ void __launch_bounds__(256) loss_fwd_kernel(const __grid_constant__ LossArgs a) {
+    __shared__ float s_x[kShared * kShared];
+    __shared__ float s_y[kShared * kShared];
+    __shared__ float s_h[5 * kShared * kBlock];
     __shared__ float w[11];
     if (threadIdx.x < 11) w[threadIdx.x] = a.taps.w[threadIdx.x];
     const int c = blockIdx.z;
@@ -189,16 +194,16 @@ __global__ void __launch_bounds__(256) loss_fwd_kernel(const LossArgs a) {
         }
         return;
     }
-    stage_tile<HWC4>(a, c, tile_x0, tile_y0, kShared, kHalo, s_tile);
+    stage_tile<HWC4>(a, c, tile_x0, tile_y0, kShared, kHalo, s_x, s_y);
     __syncthreads();
-    hblur_moments(s_tile, kShared, kShared, kBlock, w, s_h);
+    hblur_moments(s_x, s_y, kShared, kShared, kBlock, w, s_h);
     __syncthreads();
     float o[5];
-    vblur5(s_h, kBlock, ty + kHalo, tx, w, o);
+    vblur5(s_h, kShared * kBlock, kBlock, ty + kHalo, tx, w, o);
     if (in) {
         const Ssim t = ssim_terms(o[0], o[1], o[2], o[3], o[4]);
-        const int ci = ((ty + kHalo) * kShared + tx + kHalo) * 2;
-        const float l1 = fabsf(s_tile[ci] - s_tile[ci + 1]);
+        const int ci = (ty + kHalo) * kShared + tx + kHalo;
+        const float l1 = fabsf(s_x[ci] - s_y[ci]);
         float v = a.l1_w * l1 + a.ssim_w * t.val;
         if (a.mask) {
             float gc, ga;
@@ -209,25 +214,33 @@ __global__ void __launch_bounds__(256) loss_fwd_kernel(const LossArgs a) {
     }
 }
 
-// Backward (and fused loss+backward). Shared layout per channel:
-//   s_a: staged (pred, gt_eff), 36x36x2
-//   s_b: first horizontal blur 36x26x5, later second horizontal blur 26x16x3
-//   s_p: chain-weighted partials 26x26x3
+// Shared buffers of the backward (and fused loss+backward), per channel:
+//   s_x, s_y: staged pred / gt_eff planes, 36x36
+//   s_h:      first horizontal blur, 5 planes of 36x26; later the second
+//             horizontal blur, 3 planes of 26x16
+//   s_p:      chain-weighted partials, 3 planes of 26x26
+struct LossSmem {
+    float x[kExtended * kExtended];
+    float y[kExtended * kExtended];
+    float h[5 * kExtended * kShared];
+    float p[3 * kShared * kShared];
+};
+
 template <bool HWC4, bool FUSED>
 __device__ __forceinline__ void loss_bwd_channel(const LossArgs& a, int c, int tile_x0, int tile_y0, const float* w,
-                                                 float* s_a, float* s_b, float* s_p, float* s_val, float* grad_out,
-                                                 float* loss_out) {
+                                                 LossSmem& S, float* s_val, float* grad_out, float* loss_out) {
     const int tx = threadIdx.x % kBlock, ty = threadIdx.x / kBlock;
     const uint32_t px = tile_x0 + tx, py = tile_y0 + ty;
     const bool in = px < a.w && py < a.h;
-    stage_tile<HWC4>(a, c, tile_x0, tile_y0, kExtended, 2 * kHalo, s_a);
+    stage_tile<HWC4>(a, c, tile_x0, tile_y0, kExtended, 2 * kHalo, S.x, S.y);
     __syncthreads();
-    hblur_moments(s_a, kExtended, kExtended, kShared, w, s_b);
+    hblur_moments(S.x, S.y, kExtended, kExtended, kShared, w, S.h);
     __syncthreads();
-    for (int tid = threadIdx.x; tid < kShared * kShared; tid += blockDim.x) {
-        const int pyl = tid / kShared, pxl = tid % kShared;
+    constexpr int kP = kShared * kShared;
+    for (int tid = threadIdx.x; tid < kP; tid += blockDim.x) {
+        const int pyl = tid / kShared, pxl = tid - pyl * kShared;
         float o[5];
-        vblur5(s_b, kShared, pyl + kHalo, pxl, w, o);
+        vblur5(S.h, kExtended * kShared, kShared, pyl + kHalo, pxl, w, o);
         const Ssim t = ssim_terms(o[0], o[1], o[2], o[3], o[4]);
         const int gy = tile_y0 + pyl - kHalo, gx = tile_x0 + pxl - kHalo;
         float chain = 0.0f;
@@ -239,33 +252,32 @@ __device__ __forceinline__ void loss_bwd_channel(const LossArgs& a, int c, int t
                 chain = chain * ga;
             }
         }
-        s_p[tid * 3] = t.dmu1 * chain;
-        s_p[tid * 3 + 1] = t.dsig1 * chain;
-        s_p[tid * 3 + 2] = t.dsig12 * chain;
+        S.p[tid] = t.dmu1 * chain;
+        S.p[kP + tid] = t.dsig1 * chain;
+        S.p[2 * kP + tid] = t.dsig12 * chain;
         if (FUSED && pyl >= kHalo && pyl < kHalo + kBlock && pxl >= kHalo && pxl < kHalo + kBlock)
             s_val[(pyl - kHalo) * kBlock + (pxl - kHalo)] = t.val;
     }
     __syncthreads();
-    // second horizontal blur: 26 rows x 16 columns x 3
-    for (int tid = threadIdx.x; tid < kShared * kBlock; tid += blockDim.x) {
-        const int ry = tid / kBlock, cx = tid % kBlock;
-        const int center = cx + kHalo;
+    // second horizontal blur: 26 rows x 16 columns x 3 planes
+    constexpr int kQ = kShared * kBlock;
+    for (int tid = threadIdx.x; tid < kQ; tid += blockDim.x) {
+        const int ry = tid / kBlock, cx = tid - ry * kBlock;
+        const int center = ry * kShared + cx + kHalo;
         float a0 = 0.f, a1 = 0.f, a2 = 0.f;
 #pragma unroll
         for (int d = 1; d < 6; ++d) {
             const float wd = w[5 - d];
-            const int il = (ry * kShared + center - d) * 3, ir = (ry * kShared + center + d) * 3;
-            a0 += (s_p[il] + s_p[ir]) * wd;
-            a1 += (s_p[il + 1] + s_p[ir + 1]) * wd;
-            a2 += (s_p[il + 2] + s_p[ir + 2]) * wd;
+            a0 += (S.p[center - d] + S.p[center + d]) * wd;
+            a1 += (S.p[kP + center - d] + S.p[kP + center + d]) * wd;
+            a2 += (S.p[2 * kP + center - d] + S.p[2 * kP + center + d]) * wd;
         }
-        const int ic = (ry * kShared + center) * 3;
-        a0 += s_p[ic] * w[5];
-        a1 += s_p[ic + 1] * w[5];
-        a2 += s_p[ic + 2] * w[5];
-        s_b[tid * 3] = a0;
-        s_b[tid * 3 + 1] = a1;
-        s_b[tid * 3 + 2] = a2;
+        a0 += S.p[center] * w[5];
+        a1 += S.p[kP + center] * w[5];
+        a2 += S.p[2 * kP + center] * w[5];
+        S.h[tid] = a0;
+        S.h[kQ + tid] = a1;
+        S.h[2 * kQ + tid] = a2;
     }
     __syncthreads();
     if (in) {
@@ -274,18 +286,20 @@ __device__ __forceinline__ void loss_bwd_channel(const LossArgs& a, int c, int t
 #pragma unroll
         for (int d = 1; d < 6; ++d) {
             const float wd = w[5 - d];
-            const int bt = ((ly - d) * kBlock + tx) * 3, bb = ((ly + d) * kBlock + tx) * 3;
-            s0 += (s_b[bt] + s_b[bb]) * wd;
-            s1 += (s_b[bt + 1] + s_b[bb + 1]) * wd;
-            s2 += (s_b[bt + 2] + s_b[bb + 2]) * wd;
+            const int bt = (ly - d) * kBlock + tx, bb = (ly + d) * kBlock + tx;
+            s0 += (S.h[bt] + S.h[bb]) * wd;
+            s1 += (S.h[kQ + bt] + S.h[kQ + bb]) * wd;
+            s2 += (S.h[2 * kQ + bt] + S.h[2 * kQ + bb]) * wd;
         }
-        const int bc = (ly * kBlock + tx) * 3;
-        s0 += s_b[bc] * w[5];
-        s1 += s_b[bc + 1] * w[5];
-        s2 += s_b[bc + 2] * w[5];
-        const float p1 = read_pred<HWC4>(a, c, py, px);
-        float ga;
-        const float ge = gt_eff(a, c, py, px, &ga);
+        const int bc = ly * kBlock + tx;
+        s0 += S.h[bc] * w[5];
+        s1 += S.h[kQ + bc] * w[5];
+        s2 += S.h[2 * kQ + bc] * w[5];
+        const int ci = (ty + 2 * kHalo) * kExtended + tx + 2 * kHalo;
+        const float p1 = S.x[ci];
+        const float ge = S.y[ci];
+        float gc_unused, ga = 1.0f;
+        if (a.mask) read_gt(a, c, py, px, &gc_unused, &ga);
         const float sg = s0 + (2.0f * p1) * s1 + ge * s2;
         const float diff = p1 - ge;
         const float sign = diff > 0.0f ? 1.0f : (diff < 0.0f ? -1.0f : 0.0f);
@@ -302,10 +316,8 @@ __device__ __forceinline__ void loss_bwd_channel(const LossArgs& a, int c, int t
 }
 
 template <bool HWC4>
-__global__ void __launch_bounds__(256) loss_bwd_kernel(const LossArgs a) {
-    __shared__ float s_a[kExtended * kExtended * 2];
-    __shared__ float s_b[kExtended * kShared * 5];
-    __shared__ float s_p[kShared * kShared * 3];
+__global__ void __launch_bounds__(256) loss_bwd_kernel(const __grid_constant__ LossArgs a) {
+    __shared__ LossSmem S;
     __shared__ float w[11];
     if (threadIdx.x < 11) w[threadIdx.x] = a.taps.w[threadIdx.x];
     const int c = blockIdx.z;
@@ -329,15 +341,13 @@ __global__ void __launch_bounds__(256) loss_bwd_kernel(const LossArgs a) {
     }
     __syncthreads();
     float g = 0.0f, unused = 0.0f;
-    loss_bwd_channel<HWC4, false>(a, c, tile_x0, tile_y0, w, s_a, s_b, s_p, nullptr, &g, &unused);
+    loss_bwd_channel<HWC4, false>(a, c, tile_x0, tile_y0, w, S, nullptr, &g, &unused);
     if (in) a.out[idx] = g;
 }
 
 // Training form: three colour channels per block, [H,W,4] in and out.
-__global__ void __launch_bounds__(256) loss_fused_kernel(const LossArgs a) {
-    __shared__ float s_a[kExtended * kExtended * 2];
-    __shared__ float s_b[kExtended * kShared * 5];
-    __shared__ float s_p[kShared * kShared * 3];
+__global__ void __launch_bounds__(256) loss_fused_kernel(const __grid_constant__ LossArgs a) {
+    __shared__ LossSmem S;
     __shared__ float s_val[kBlock * kBlock];
     __shared__ float w[11];
     __shared__ float s_red[8];
@@ -367,7 +377,7 @@ __global__ void __launch_bounds__(256) loss_fused_kernel(const LossArgs a) {
         }
     } else {
         for (int c = 0; c < 3; ++c)
-            loss_bwd_channel<true, true>(a, c, tile_x0, tile_y0, w, s_a, s_b, s_p, s_val, &g[c], &loss);
+            loss_bwd_channel<true, true>(a, c, tile_x0, tile_y0, w, S, s_val, &g[c], &loss);
     }
     if (px < a.w && py < a.h)
         reinterpret_cast<float4*>(a.out)[(size_t)py * a.w + px] = make_float4(g[0], g[1], g[2], 0.0f);

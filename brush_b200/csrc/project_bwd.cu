@@ -6,7 +6,13 @@
 // (kernels/camera_model/pinhole.rs:58-123) -> rotation/scale VJP, plus the SH
 // coefficient VJP and the view-direction VJP into the mean (kernels/sh.rs).
 // One thread per splat over all N rows; rows without gradient are written as
-// zeros here, so no separate zero-fill of the dense outputs is needed.
+// zeros, so no separate zero-fill of the dense outputs is needed.
+//
+// Memory: a block owns R consecutive splats. Their transform, SH and gradient
+// rows (contiguous in global memory) are copied into shared memory with
+// coalesced loads, each thread works on its own rows there (odd row strides
+// keep the per-thread accesses free of bank conflicts), and the gradient rows
+// go back to global memory with coalesced stores.
 #include "sh.cuh"
 
 namespace bsx {
@@ -32,145 +38,200 @@ __device__ __forceinline__ V3 s3mul(const S3& s, V3 v) {
                 vscale(v3(s.c02, s.c12, s.c22), v.z));
 }
 
+// Row index of element i of a staged block (i < 2^15, cols <= 80).
+__device__ __forceinline__ uint32_t row_of(uint32_t i, float inv_cols) {
+    return (uint32_t)(((float)i + 0.5f) * inv_cols);
+}
+
+// Copy `rows` rows of `cols` floats (contiguous in global memory) into shared
+// memory rows of stride `stride`, or back.
+__device__ __forceinline__ void stage_in(float* dst, const float* __restrict__ src, uint32_t rows, uint32_t cols,
+                                         uint32_t stride) {
+    const float inv = 1.0f / (float)cols;
+    for (uint32_t i = threadIdx.x; i < rows * cols; i += blockDim.x) {
+        const uint32_t r = row_of(i, inv);
+        dst[r * stride + (i - r * cols)] = __ldg(src + i);
+    }
+}
+__device__ __forceinline__ void stage_out(float* __restrict__ dst, const float* src, uint32_t rows, uint32_t cols,
+                                          uint32_t stride) {
+    const float inv = 1.0f / (float)cols;
+    for (uint32_t i = threadIdx.x; i < rows * cols; i += blockDim.x) {
+        const uint32_t r = row_of(i, inv);
+        dst[i] = src[r * stride + (i - r * cols)];
+    }
+}
+
 template <int DEG>
-__global__ void __launch_bounds__(256) project_bwd_kernel(const PbArgs a) {
-    const uint32_t g = blockIdx.x * blockDim.x + threadIdx.x;
-    if (g >= a.n) return;
-    constexpr int C3 = (DEG + 1) * (DEG + 1) * 3;
-    float* vt = a.v_transforms + (size_t)g * 10;
-    float* vs = a.v_sh + (size_t)g * C3;
-    const float4* rg4 = reinterpret_cast<const float4*>(a.v_grad + (size_t)g * kGradStride);
-    const float4 r0 = __ldg(rg4), r1 = __ldg(rg4 + 1), r2 = __ldg(rg4 + 2);
-    const bool any = r0.x != 0.0f || r0.y != 0.0f || r0.z != 0.0f || r0.w != 0.0f || r1.x != 0.0f ||
-                     r1.y != 0.0f || r1.z != 0.0f || r1.w != 0.0f || r2.x != 0.0f || r2.y != 0.0f || r2.z != 0.0f;
-    if (!any) {
+struct PbShape {
+    static constexpr int C3 = (DEG + 1) * (DEG + 1) * 3;
+    static constexpr int R = DEG >= 4 ? 64 : 128;  // splats per block
+    static constexpr int TS = 11;                  // transform row stride (odd)
+    static constexpr int SS = C3 | 1;              // SH row stride (odd)
+    static constexpr int GS = 13;                  // gradient row stride (odd)
+};
+
+template <int DEG>
+__global__ void __launch_bounds__(PbShape<DEG>::R) project_bwd_kernel(const PbArgs a) {
+    using S = PbShape<DEG>;
+    constexpr int C3 = S::C3;
+    __shared__ float s_t[S::R * S::TS];
+    __shared__ float s_sh[S::R * S::SS];
+    __shared__ float s_g[S::R * S::GS];
+    const uint32_t g0 = blockIdx.x * S::R;
+    const uint32_t rows = min((uint32_t)S::R, a.n - g0);
+    stage_in(s_t, a.transforms + (size_t)g0 * 10, rows, 10, S::TS);
+    stage_in(s_sh, a.sh + (size_t)g0 * C3, rows, C3, S::SS);
+    stage_in(s_g, a.v_grad + (size_t)g0 * kGradStride, rows, kGradStride, S::GS);
+    __syncthreads();
+    const uint32_t r = threadIdx.x;
+    if (r < rows) {
+        const uint32_t g = g0 + r;
+        float* t = s_t + r * S::TS;   // transform in, transform gradient out
+        float* shr = s_sh + r * S::SS;  // SH in, SH gradient out
+        const float* rg = s_g + r * S::GS;
+        bool any = false;
 #pragma unroll
-        for (int k = 0; k < 10; ++k) vt[k] = 0.0f;
+        for (int k = 0; k < BSX_COMPACT_GRAD_LANES; ++k) any = any || rg[k] != 0.0f;
+        if (!any) {
 #pragma unroll
-        for (int k = 0; k < C3; ++k) vs[k] = 0.0f;
-        a.v_opac[g] = 0.0f;
-        a.v_refine[g] = 0.0f;
-        return;
+            for (int k = 0; k < 10; ++k) t[k] = 0.0f;
+#pragma unroll
+            for (int k = 0; k < C3; ++k) shr[k] = 0.0f;
+            a.v_opac[g] = 0.0f;
+            a.v_refine[g] = 0.0f;
+        } else {
+            const Uni& u = a.u;
+            const float vmx = rg[0], vmy = rg[1], vcx = rg[2], vcy = rg[3], vcz = rg[4];
+            const V3 vcol = v3(rg[5], rg[6], rg[7]);
+            const float valpha = rg[8], vref = rg[9], vdep = rg[10];
+            const V3 mean = v3(t[0], t[1], t[2]);
+            const V3 scl = v3(bsx_expf(t[7]), bsx_expf(t[8]), bsx_expf(t[9]));
+            const Q4 qu{t[3], t[4], t[5], t[6]};
+            const Q4 q = qnormalize(qu);
+
+            // view direction + SH VJPs (read the coefficients before overwriting the row)
+            const V3 uw = vsub(mean, u.cam);
+            const float ulen = sqrtf(vdot(uw, uw));
+            const V3 vdir = vscale(uw, 1.0f / ulen);
+            const V3 vv = sh_viewdir_vjp<DEG>(shr, vdir, vcol);
+            sh_coeffs_vjp<DEG>(shr, vdir, vcol);
+            const float vdv = vdot(vdir, vv);
+            const V3 v_mean_sh = vscale(vsub(vv, vscale(vdir, vdv)), 1.0f / ulen);
+
+            const V3 mean_c = vadd(mmul(u.rot, mean), u.trans);
+            const M3 R = quat_to_mat3(q);
+            const M3 Mm = mdiag(R, scl);
+            const S2 raw = calc_cov2d(scl, q, mean_c, u);
+            float fc;
+            const S2 cov = compensate_cov2d(raw, a.mip != 0, &fc);
+            const float os = bsx_sigmoid(__ldg(a.raw_opac + g));
+            a.v_opac[g] = fc * valpha * os * (1.0f - os);
+            const float rc = bsx_is_finite(vref) ? vref : 0.0f;
+            a.v_refine[g] = bsx_clamp(rc, 0.0f, 1.0e32f);
+
+            const S2 ci = sym2_inverse(cov);
+            const S2 vi{vcx, vcy * 0.5f, vcz};
+            const float t00 = -ci.c00 * vi.c00 + -ci.c01 * vi.c01;
+            const float t01 = -ci.c01 * vi.c00 + -ci.c11 * vi.c01;
+            const float t10 = -ci.c00 * vi.c01 + -ci.c01 * vi.c11;
+            const float t11 = -ci.c01 * vi.c01 + -ci.c11 * vi.c11;
+            const S2 vcov{t00 * ci.c00 + t10 * ci.c01, t01 * ci.c00 + t11 * ci.c01, t01 * ci.c01 + t11 * ci.c11};
+
+            const V3 mr0 = mrow(Mm, 0), mr1 = mrow(Mm, 1), mr2 = mrow(Mm, 2);
+            const S3 covar{vdot(mr0, mr0), vdot(mr0, mr1), vdot(mr0, mr2),
+                           vdot(mr1, mr1), vdot(mr1, mr2), vdot(mr2, mr2)};
+            const V3 vr0 = mrow(u.rot, 0), vr1 = mrow(u.rot, 1), vr2 = mrow(u.rot, 2);
+            const V3 sr0 = s3mul(covar, vr0), sr1 = s3mul(covar, vr1), sr2 = s3mul(covar, vr2);
+            const S3 cov_c{vdot(vr0, sr0), vdot(vr0, sr1), vdot(vr0, sr2),
+                           vdot(vr1, sr1), vdot(vr1, sr2), vdot(vr2, sr2)};
+            const M23 J = pinhole_jacobian(mean_c, u);
+
+            // pinhole projection VJP (pinhole.rs:180-245)
+            const float mx = mean_c.x, my = mean_c.y, mz = mean_c.z;
+            const float inv_z = 1.0f / mz;
+            const float mxr = mx * inv_z, myr = my * inv_z;
+            const float mxc = bsx_clamp(mxr, u.lnx, u.lpx), myc = bsx_clamp(myr, u.lny, u.lpy);
+            const bool in_x = mxr <= u.lpx && mxr >= u.lnx;
+            const bool in_y = myr <= u.lpy && myr >= u.lny;
+            const float iz2 = inv_z * inv_z, iz3 = iz2 * inv_z;
+            float v_mx = u.fx * inv_z * vmx;
+            float v_my = u.fy * inv_z * vmy;
+            float v_mz = -(u.fx * mx * vmx + u.fy * my * vmy) * iz2;
+            const float jc[3][2] = {{J.c0x, J.c0y}, {J.c1x, J.c1y}, {J.c2x, J.c2y}};
+            float tmp[3][2];
+#pragma unroll
+            for (int c = 0; c < 3; ++c) {
+                tmp[c][0] = vcov.c00 * jc[c][0] + vcov.c01 * jc[c][1];
+                tmp[c][1] = vcov.c01 * jc[c][0] + vcov.c11 * jc[c][1];
+            }
+            const V3 tr0 = v3(tmp[0][0], tmp[1][0], tmp[2][0]), tr1 = v3(tmp[0][1], tmp[1][1], tmp[2][1]);
+            const V3 cr0 = v3(cov_c.c00, cov_c.c01, cov_c.c02), cr1 = v3(cov_c.c01, cov_c.c11, cov_c.c12),
+                     cr2 = v3(cov_c.c02, cov_c.c12, cov_c.c22);
+            const float vj00 = 2.0f * vdot(tr0, cr0);
+            const float vj11 = 2.0f * vdot(tr1, cr1);
+            const float vj20 = 2.0f * vdot(tr0, cr2);
+            const float vj21 = 2.0f * vdot(tr1, cr2);
+            const float txv = mz * mxc, tyv = mz * myc;
+            if (in_x) v_mx += -u.fx * iz2 * vj20;
+            else v_mz += -u.fx * iz3 * vj20 * txv;
+            if (in_y) v_my += -u.fy * iz2 * vj21;
+            else v_mz += -u.fy * iz3 * vj21 * tyv;
+            v_mz += -u.fx * iz2 * vj00 - u.fy * iz2 * vj11 + 2.0f * u.fx * txv * iz3 * vj20 +
+                    2.0f * u.fy * tyv * iz3 * vj21;
+            const V3 v_mean_c = v3(v_mx, v_my, v_mz + vdep);
+
+            // J^T v_cov2d J (Mat2x3::transpose_congruence_sym2)
+            const S3 vcc{jc[0][0] * tmp[0][0] + jc[0][1] * tmp[0][1], jc[0][0] * tmp[1][0] + jc[0][1] * tmp[1][1],
+                         jc[0][0] * tmp[2][0] + jc[0][1] * tmp[2][1], jc[1][0] * tmp[1][0] + jc[1][1] * tmp[1][1],
+                         jc[1][0] * tmp[2][0] + jc[1][1] * tmp[2][1], jc[2][0] * tmp[2][0] + jc[2][1] * tmp[2][1]};
+            const V3 v_mean = vadd(mtmul(u.rot, v_mean_c), v_mean_sh);
+            // v_M = 2 (R_view^T vcc R_view) M
+            const V3 sc0 = s3mul(vcc, u.rot.c0), sc1 = s3mul(vcc, u.rot.c1), sc2 = s3mul(vcc, u.rot.c2);
+            const S3 tc{vdot(u.rot.c0, sc0), vdot(u.rot.c0, sc1), vdot(u.rot.c0, sc2),
+                        vdot(u.rot.c1, sc1), vdot(u.rot.c1, sc2), vdot(u.rot.c2, sc2)};
+            const S3 tc2{tc.c00 * 2.0f, tc.c01 * 2.0f, tc.c02 * 2.0f, tc.c11 * 2.0f, tc.c12 * 2.0f, tc.c22 * 2.0f};
+            const M3 vM{s3mul(tc2, Mm.c0), s3mul(tc2, Mm.c1), s3mul(tc2, Mm.c2)};
+            const V3 vse = v3(vdot(R.c0, vM.c0) * scl.x, vdot(R.c1, vM.c1) * scl.y, vdot(R.c2, vM.c2) * scl.z);
+            // quat_to_mat_vjp of v_M diag(scale)
+            const M3 vr = mdiag(vM, scl);
+            const float qw = q.w, qx = q.x, qy = q.y, qz = q.z;
+            const float wg = qx * (vr.c1.z - vr.c2.y) + qy * (vr.c2.x - vr.c0.z) + qz * (vr.c0.y - vr.c1.x);
+            const float xg = -2.0f * qx * (vr.c1.y + vr.c2.z) + qy * (vr.c0.y + vr.c1.x) + qz * (vr.c0.z + vr.c2.x) +
+                             qw * (vr.c1.z - vr.c2.y);
+            const float yg = qx * (vr.c0.y + vr.c1.x) - 2.0f * qy * (vr.c0.x + vr.c2.z) + qz * (vr.c1.z + vr.c2.y) +
+                             qw * (vr.c2.x - vr.c0.z);
+            const float zg = qx * (vr.c0.z + vr.c2.x) + qy * (vr.c1.z + vr.c2.y) - 2.0f * qz * (vr.c0.x + vr.c1.y) +
+                             qw * (vr.c0.y - vr.c1.x);
+            const Q4 qg{2.0f * wg, 2.0f * xg, 2.0f * yg, 2.0f * zg};
+            // normalisation VJP on the raw quaternion
+            const float lsq = qdot(qu, qu);
+            const float l = sqrtf(lsq);
+            const float inv = 1.0f / (l * lsq);
+            const float cc0 = -qu.w * qu.x, cc1 = -qu.x * qu.y, cc2 = -qu.y * qu.w;
+            const float cs0 = -qu.w * qu.z, cs1 = -qu.x * qu.z, cs2 = -qu.y * qu.z;
+            const float sw_ = qu.w * qu.w, sx_ = qu.x * qu.x, sy_ = qu.y * qu.y, sz_ = qu.z * qu.z;
+            t[0] = v_mean.x;
+            t[1] = v_mean.y;
+            t[2] = v_mean.z;
+            t[3] = ((lsq - sw_) * qg.w + cc0 * qg.x + cc2 * qg.y + cs0 * qg.z) * inv;
+            t[4] = (cc0 * qg.w + (lsq - sx_) * qg.x + cc1 * qg.y + cs1 * qg.z) * inv;
+            t[5] = (cc2 * qg.w + cc1 * qg.x + (lsq - sy_) * qg.y + cs2 * qg.z) * inv;
+            t[6] = (cs0 * qg.w + cs1 * qg.x + cs2 * qg.y + (lsq - sz_) * qg.z) * inv;
+            t[7] = vse.x;
+            t[8] = vse.y;
+            t[9] = vse.z;
+        }
     }
-    const Uni& u = a.u;
-    const float vmx = r0.x, vmy = r0.y, vcx = r0.z, vcy = r0.w, vcz = r1.x;
-    const V3 vcol = v3(r1.y, r1.z, r1.w);
-    const float valpha = r2.x, vref = r2.y, vdep = r2.z;
-    const float* t = a.transforms + (size_t)g * 10;
-    const V3 mean = v3(__ldg(t), __ldg(t + 1), __ldg(t + 2));
-    const V3 scl = v3(bsx_expf(__ldg(t + 7)), bsx_expf(__ldg(t + 8)), bsx_expf(__ldg(t + 9)));
-    const Q4 qu{__ldg(t + 3), __ldg(t + 4), __ldg(t + 5), __ldg(t + 6)};
-    const Q4 q = qnormalize(qu);
+    __syncthreads();
+    stage_out(a.v_transforms + (size_t)g0 * 10, s_t, rows, 10, S::TS);
+    stage_out(a.v_sh + (size_t)g0 * C3, s_sh, rows, C3, S::SS);
+}
 
-    // view direction + SH VJPs
-    const V3 uw = vsub(mean, u.cam);
-    const float ulen = sqrtf(vdot(uw, uw));
-    const V3 vdir = vscale(uw, 1.0f / ulen);
-    const float* shc = a.sh + (size_t)g * C3;
-    sh_coeffs_vjp<DEG>(vs, vdir, vcol);
-    const V3 vv = sh_viewdir_vjp<DEG>(shc, vdir, vcol);
-    const float vdv = vdot(vdir, vv);
-    const V3 v_mean_sh = vscale(vsub(vv, vscale(vdir, vdv)), 1.0f / ulen);
-
-    const V3 mean_c = vadd(mmul(u.rot, mean), u.trans);
-    const M3 R = quat_to_mat3(q);
-    const M3 Mm = mdiag(R, scl);
-    const S2 raw = calc_cov2d(scl, q, mean_c, u);
-    float fc;
-    const S2 cov = compensate_cov2d(raw, a.mip != 0, &fc);
-    const float os = bsx_sigmoid(__ldg(a.raw_opac + g));
-    a.v_opac[g] = fc * valpha * os * (1.0f - os);
-    const float rc = bsx_is_finite(vref) ? vref : 0.0f;
-    a.v_refine[g] = bsx_clamp(rc, 0.0f, 1.0e32f);
-
-    const S2 ci = sym2_inverse(cov);
-    const S2 vi{vcx, vcy * 0.5f, vcz};
-    const float t00 = -ci.c00 * vi.c00 + -ci.c01 * vi.c01;
-    const float t01 = -ci.c01 * vi.c00 + -ci.c11 * vi.c01;
-    const float t10 = -ci.c00 * vi.c01 + -ci.c01 * vi.c11;
-    const float t11 = -ci.c01 * vi.c01 + -ci.c11 * vi.c11;
-    const S2 vcov{t00 * ci.c00 + t10 * ci.c01, t01 * ci.c00 + t11 * ci.c01, t01 * ci.c01 + t11 * ci.c11};
-
-    const V3 mr0 = mrow(Mm, 0), mr1 = mrow(Mm, 1), mr2 = mrow(Mm, 2);
-    const S3 covar{vdot(mr0, mr0), vdot(mr0, mr1), vdot(mr0, mr2), vdot(mr1, mr1), vdot(mr1, mr2), vdot(mr2, mr2)};
-    const V3 vr0 = mrow(u.rot, 0), vr1 = mrow(u.rot, 1), vr2 = mrow(u.rot, 2);
-    const V3 sr0 = s3mul(covar, vr0), sr1 = s3mul(covar, vr1), sr2 = s3mul(covar, vr2);
-    const S3 cov_c{vdot(vr0, sr0), vdot(vr0, sr1), vdot(vr0, sr2), vdot(vr1, sr1), vdot(vr1, sr2), vdot(vr2, sr2)};
-    const M23 J = pinhole_jacobian(mean_c, u);
-
-    // pinhole projection VJP (pinhole.rs:180-245)
-    const float mx = mean_c.x, my = mean_c.y, mz = mean_c.z;
-    const float inv_z = 1.0f / mz;
-    const float mxr = mx * inv_z, myr = my * inv_z;
-    const float mxc = bsx_clamp(mxr, u.lnx, u.lpx), myc = bsx_clamp(myr, u.lny, u.lpy);
-    const bool in_x = mxr <= u.lpx && mxr >= u.lnx;
-    const bool in_y = myr <= u.lpy && myr >= u.lny;
-    const float iz2 = inv_z * inv_z, iz3 = iz2 * inv_z;
-    float v_mx = u.fx * inv_z * vmx;
-    float v_my = u.fy * inv_z * vmy;
-    float v_mz = -(u.fx * mx * vmx + u.fy * my * vmy) * iz2;
-    const float jc[3][2] = {{J.c0x, J.c0y}, {J.c1x, J.c1y}, {J.c2x, J.c2y}};
-    float tmp[3][2];
-#pragma unroll
-    for (int c = 0; c < 3; ++c) {
-        tmp[c][0] = vcov.c00 * jc[c][0] + vcov.c01 * jc[c][1];
-        tmp[c][1] = vcov.c01 * jc[c][0] + vcov.c11 * jc[c][1];
-    }
-    const V3 tr0 = v3(tmp[0][0], tmp[1][0], tmp[2][0]), tr1 = v3(tmp[0][1], tmp[1][1], tmp[2][1]);
-    const V3 cr0 = v3(cov_c.c00, cov_c.c01, cov_c.c02), cr1 = v3(cov_c.c01, cov_c.c11, cov_c.c12),
-             cr2 = v3(cov_c.c02, cov_c.c12, cov_c.c22);
-    const float vj00 = 2.0f * vdot(tr0, cr0);
-    const float vj11 = 2.0f * vdot(tr1, cr1);
-    const float vj20 = 2.0f * vdot(tr0, cr2);
-    const float vj21 = 2.0f * vdot(tr1, cr2);
-    const float txv = mz * mxc, tyv = mz * myc;
-    if (in_x) v_mx += -u.fx * iz2 * vj20;
-    else v_mz += -u.fx * iz3 * vj20 * txv;
-    if (in_y) v_my += -u.fy * iz2 * vj21;
-    else v_mz += -u.fy * iz3 * vj21 * tyv;
-    v_mz += -u.fx * iz2 * vj00 - u.fy * iz2 * vj11 + 2.0f * u.fx * txv * iz3 * vj20 + 2.0f * u.fy * tyv * iz3 * vj21;
-    const V3 v_mean_c = v3(v_mx, v_my, v_mz + vdep);
-
-    // J^T v_cov2d J (Mat2x3::transpose_congruence_sym2)
-    const S3 vcc{jc[0][0] * tmp[0][0] + jc[0][1] * tmp[0][1], jc[0][0] * tmp[1][0] + jc[0][1] * tmp[1][1],
-                 jc[0][0] * tmp[2][0] + jc[0][1] * tmp[2][1], jc[1][0] * tmp[1][0] + jc[1][1] * tmp[1][1],
-                 jc[1][0] * tmp[2][0] + jc[1][1] * tmp[2][1], jc[2][0] * tmp[2][0] + jc[2][1] * tmp[2][1]};
-    const V3 v_mean = vadd(mtmul(u.rot, v_mean_c), v_mean_sh);
-    // v_M = 2 (R_view^T vcc R_view) M
-    const V3 sc0 = s3mul(vcc, u.rot.c0), sc1 = s3mul(vcc, u.rot.c1), sc2 = s3mul(vcc, u.rot.c2);
-    const S3 tc{vdot(u.rot.c0, sc0), vdot(u.rot.c0, sc1), vdot(u.rot.c0, sc2),
-                vdot(u.rot.c1, sc1), vdot(u.rot.c1, sc2), vdot(u.rot.c2, sc2)};
-    const S3 tc2{tc.c00 * 2.0f, tc.c01 * 2.0f, tc.c02 * 2.0f, tc.c11 * 2.0f, tc.c12 * 2.0f, tc.c22 * 2.0f};
-    const M3 vM{s3mul(tc2, Mm.c0), s3mul(tc2, Mm.c1), s3mul(tc2, Mm.c2)};
-    const V3 vse = v3(vdot(R.c0, vM.c0) * scl.x, vdot(R.c1, vM.c1) * scl.y, vdot(R.c2, vM.c2) * scl.z);
-    // quat_to_mat_vjp of v_M diag(scale)
-    const M3 vr = mdiag(vM, scl);
-    const float qw = q.w, qx = q.x, qy = q.y, qz = q.z;
-    const float wg = qx * (vr.c1.z - vr.c2.y) + qy * (vr.c2.x - vr.c0.z) + qz * (vr.c0.y - vr.c1.x);
-    const float xg = -2.0f * qx * (vr.c1.y + vr.c2.z) + qy * (vr.c0.y + vr.c1.x) + qz * (vr.c0.z + vr.c2.x) +
-                     qw * (vr.c1.z - vr.c2.y);
-    const float yg = qx * (vr.c0.y + vr.c1.x) - 2.0f * qy * (vr.c0.x + vr.c2.z) + qz * (vr.c1.z + vr.c2.y) +
-                     qw * (vr.c2.x - vr.c0.z);
-    const float zg = qx * (vr.c0.z + vr.c2.x) + qy * (vr.c1.z + vr.c2.y) - 2.0f * qz * (vr.c0.x + vr.c1.y) +
-                     qw * (vr.c0.y - vr.c1.x);
-    const Q4 qg{2.0f * wg, 2.0f * xg, 2.0f * yg, 2.0f * zg};
-    // normalisation VJP on the raw quaternion
-    const float lsq = qdot(qu, qu);
-    const float l = sqrtf(lsq);
-    const float inv = 1.0f / (l * lsq);
-    const float cc0 = -qu.w * qu.x, cc1 = -qu.x * qu.y, cc2 = -qu.y * qu.w;
-    const float cs0 = -qu.w * qu.z, cs1 = -qu.x * qu.z, cs2 = -qu.y * qu.z;
-    const float sw_ = qu.w * qu.w, sx_ = qu.x * qu.x, sy_ = qu.y * qu.y, sz_ = qu.z * qu.z;
-    vt[0] = v_mean.x;
-    vt[1] = v_mean.y;
-    vt[2] = v_mean.z;
-    vt[3] = ((lsq - sw_) * qg.w + cc0 * qg.x + cc2 * qg.y + cs0 * qg.z) * inv;
-    vt[4] = (cc0 * qg.w + (lsq - sx_) * qg.x + cc1 * qg.y + cs1 * qg.z) * inv;
-    vt[5] = (cc2 * qg.w + cc1 * qg.x + (lsq - sy_) * qg.y + cs2 * qg.z) * inv;
-    vt[6] = (cs0 * qg.w + cs1 * qg.x + cs2 * qg.y + (lsq - sz_) * qg.z) * inv;
-    vt[7] = vse.x;
-    vt[8] = vse.y;
-    vt[9] = vse.z;
+template <int DEG>
+void launch_deg(const PbArgs& a, cudaStream_t st) {
+    constexpr int R = PbShape<DEG>::R;
+    project_bwd_kernel<DEG><<<(a.n + R - 1) / R, R, 0, st>>>(a);
 }
 
 }  // namespace
@@ -192,16 +253,14 @@ bsx_status launch_project_bwd(bsx_ctx* ctx, const bsx_project_uniforms& uni, con
     a.v_sh = v_sh;
     a.v_opac = v_opac;
     a.v_refine = v_refine;
-    const uint32_t blocks = (n + 255) / 256;
     if (degree < 0 || degree > 4) return fail(ctx, BSX_ERR_SHAPE, "unsupported SH degree");
     prof_begin(ctx);
     switch (degree) {
-        case 0: project_bwd_kernel<0><<<blocks, 256, 0, ctx->stream>>>(a); break;
-        case 1: project_bwd_kernel<1><<<blocks, 256, 0, ctx->stream>>>(a); break;
-        case 2: project_bwd_kernel<2><<<blocks, 256, 0, ctx->stream>>>(a); break;
-        case 3: project_bwd_kernel<3><<<blocks, 256, 0, ctx->stream>>>(a); break;
-        case 4: project_bwd_kernel<4><<<blocks, 256, 0, ctx->stream>>>(a); break;
-        default: return fail(ctx, BSX_ERR_SHAPE, "unsupported SH degree");
+        case 0: launch_deg<0>(a, ctx->stream); break;
+        case 1: launch_deg<1>(a, ctx->stream); break;
+        case 2: launch_deg<2>(a, ctx->stream); break;
+        case 3: launch_deg<3>(a, ctx->stream); break;
+        default: launch_deg<4>(a, ctx->stream); break;
     }
     return post_launch(ctx, "project_bwd_kernel");
 }

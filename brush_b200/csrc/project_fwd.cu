@@ -32,6 +32,7 @@ struct ProjArgs {
     uint32_t n;
     uint32_t coeffs;
     int mip;
+    int sh_vec;  // SH base 16-byte aligned
     Uni u;
     float* projected;
     uint32_t* counts;
@@ -62,14 +63,17 @@ __global__ void __launch_bounds__(kProjThreads) project_fwd_kernel(const ProjArg
     float radius = 0.0f;
     if (g < a.n) {
         do {
-            const float* t = a.transforms + (size_t)g * 10;
-            V3 mean = v3(__ldg(t), __ldg(t + 1), __ldg(t + 2));
+            // one transform row = five 8-byte words
+            const float2* t2 = reinterpret_cast<const float2*>(a.transforms + (size_t)g * 10);
+            const float2 w0 = __ldg(t2), w1 = __ldg(t2 + 1), w2 = __ldg(t2 + 2), w3 = __ldg(t2 + 3), w4 = __ldg(t2 + 4);
+            const float t[10] = {w0.x, w0.y, w1.x, w1.y, w2.x, w2.y, w3.x, w3.y, w4.x, w4.y};
+            V3 mean = v3(t[0], t[1], t[2]);
             V3 mean_c = vadd(mmul(u.rot, mean), u.trans);
             if (!(vfinite(mean_c) && mean_c.z <= 1.0e10f)) break;
             if (mean_c.z < 0.01f) break;
-            V3 scl = v3(bsx_expf(__ldg(t + 7)), bsx_expf(__ldg(t + 8)), bsx_expf(__ldg(t + 9)));
+            V3 scl = v3(bsx_expf(t[7]), bsx_expf(t[8]), bsx_expf(t[9]));
             if (!vfinite(scl)) break;
-            Q4 qu{__ldg(t + 3), __ldg(t + 4), __ldg(t + 5), __ldg(t + 6)};
+            Q4 qu{t[3], t[4], t[5], t[6]};
             float qn = qdot(qu, qu);
             if (!(qn >= 1.0e-6f && bsx_is_finite(qn))) break;
             float ro = __ldg(a.raw_opac + g);
@@ -102,7 +106,23 @@ __global__ void __launch_bounds__(kProjThreads) project_fwd_kernel(const ProjArg
             // SH colour at the normalised view direction (project_visible.rs:56-71).
             V3 dv = vsub(mean, u.cam);
             V3 vdir = vscale(dv, 1.0f / sqrtf(vdot(dv, dv)));
-            V3 col = sh_to_color<DEG>(a.sh + (size_t)g * a.coeffs * 3, vdir);
+            constexpr int C3 = (DEG + 1) * (DEG + 1) * 3;
+            float shc[C3];
+            const float* srow = a.sh + (size_t)g * C3;
+            if (C3 % 4 == 0 && a.sh_vec) {
+#pragma unroll
+                for (int k = 0; k < C3 / 4; ++k) {
+                    const float4 q4 = __ldg(reinterpret_cast<const float4*>(srow) + k);
+                    shc[4 * k] = q4.x;
+                    shc[4 * k + 1] = q4.y;
+                    shc[4 * k + 2] = q4.z;
+                    shc[4 * k + 3] = q4.w;
+                }
+            } else {
+#pragma unroll
+                for (int k = 0; k < C3; ++k) shc[k] = __ldg(srow + k);
+            }
+            V3 col = sh_to_color<DEG>(shc, vdir);
             float cr = col.x + 0.5f, cg = col.y + 0.5f, cb = col.z + 0.5f;
             cr = bsx_clamp(bsx_is_finite(cr) ? cr : 0.0f, -100.0f, 100.0f);
             cg = bsx_clamp(bsx_is_finite(cg) ? cg : 0.0f, -100.0f, 100.0f);
@@ -181,6 +201,7 @@ bsx_status launch_project_fwd(bsx_ctx* ctx, const bsx_project_uniforms& uni, con
     a.n = n;
     a.coeffs = coeffs;
     a.mip = mip;
+    a.sh_vec = ((uintptr_t)sh % 16) == 0;
     a.u = make_uni(uni);
     a.projected = projected;
     a.counts = counts;

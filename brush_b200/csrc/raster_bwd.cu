@@ -21,7 +21,6 @@ namespace bsx {
 
 namespace {
 
-constexpr int kBwdThreads = 256;
 constexpr float kMarginHard = 1.0e-3f;
 constexpr float kMarginSmooth = 0.25f;
 constexpr int kGradLanes = 10;  // xy(2) conic(3) rgb(3) alpha refine
@@ -114,52 +113,128 @@ __device__ __forceinline__ float warp_sum16(float (&v)[16], int lane) {
     return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
 }
 
-template <bool SMOOTH, bool REFINE>
-__global__ void __launch_bounds__(kBwdThreads) raster_bwd_kernel(const BwdArgs a) {
-    __shared__ float4 s_a[kBwdThreads];  // x, y, c00, c01
-    __shared__ float4 s_b[kBwdThreads];  // c11, opacity, r, g
-    __shared__ float2 s_c[kBwdThreads];  // b, ln(255 o) + margin
-    __shared__ uint32_t s_mask[kBwdThreads];
-    __shared__ uint32_t s_gid[kBwdThreads];
-    __shared__ float s_grad[kBwdThreads][kGradLanes + 1];
+// Per-pixel replay state and constants.
+struct PixelBwd {
+    float T, sr, sg, sb;            // transmittance, residual colour
+    float vor, vog, vob, vow;       // v_out rgb, (v_a - bg.v_out) * T_final
+    float inv_fa;                   // 1 / max(final alpha, 1e-5)
+    float pcy;                      // pixel centre y
+    bool done;
+};
 
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const uint32_t tile = blockIdx.x;
-    const uint32_t ox = (tile % a.tbw) * kTile, oy = (tile / a.tbw) * kTile;
-    const uint32_t lx = compact_bits_16(threadIdx.x), ly = compact_bits_16(threadIdx.x >> 1);
-    // the warp's 8x4 Morton patch as column / row masks
-    const uint32_t wcols = 0xffu << (8 * ((warp >> 1) & 1));
-    const uint32_t wrows = 0xfu << (4 * (warp & 1) + 8 * ((warp >> 2) & 1));
-    const uint32_t px = ox + lx, py = oy + ly;
-    const bool inside = px < a.w && py < a.h;
-    const uint32_t lo = __ldg(a.tile_offsets + tile * 2), hi = __ldg(a.tile_offsets + tile * 2 + 1);
-    if (hi <= lo) return;
-    const float margin = SMOOTH ? kMarginSmooth : kMarginHard;
-
-    // Per-pixel constants and replay state (registers).
-    float T = 1.0f, sr = 0.0f, sg = 0.0f, sb = 0.0f;
-    float vor = 0.0f, vog = 0.0f, vob = 0.0f, vow = 0.0f, inv_fa = 0.0f;
-    bool done = !inside;
-    if (inside) {
+__device__ __forceinline__ void pixel_init(PixelBwd& P, const BwdArgs& a, uint32_t px, uint32_t py) {
+    P.T = 1.0f;
+    P.sr = P.sg = P.sb = 0.0f;
+    P.vor = P.vog = P.vob = P.vow = 0.0f;
+    P.inv_fa = 0.0f;
+    P.pcy = (float)py + 0.5f;
+    P.done = !(px < a.w && py < a.h);
+    if (!P.done) {
         const size_t pid = (size_t)py * a.w + px;
         const float4 o = __ldg(reinterpret_cast<const float4*>(a.image) + pid);
         const float tf = 1.0f - o.w;
-        sr = o.x - tf * a.bg_r;
-        sg = o.y - tf * a.bg_g;
-        sb = o.z - tf * a.bg_b;
+        P.sr = o.x - tf * a.bg_r;
+        P.sg = o.y - tf * a.bg_g;
+        P.sb = o.z - tf * a.bg_b;
         const float4 vo = __ldg(reinterpret_cast<const float4*>(a.v_output) + pid);
-        vor = vo.x;
-        vog = vo.y;
-        vob = vo.z;
-        vow = (vo.w - (a.bg_r * vo.x + a.bg_g * vo.y + a.bg_b * vo.z)) * tf;
-        inv_fa = __frcp_rn(bsx_max(o.w, 1.0e-5f));
+        P.vor = vo.x;
+        P.vog = vo.y;
+        P.vob = vo.z;
+        P.vow = (vo.w - (a.bg_r * vo.x + a.bg_g * vo.y + a.bg_b * vo.z)) * tf;
+        P.inv_fa = __frcp_rn(bsx_max(o.w, 1.0e-5f));
     }
-    const float pcx = (float)px + 0.5f, pcy = (float)py + 0.5f;
-    const float wf = (float)a.w, hf = (float)a.h;
+}
 
-    for (uint32_t batch = lo; batch < hi; batch += kBwdThreads) {
-        if (__syncthreads_count(done) == kBwdThreads) break;
-        const uint32_t n = min((uint32_t)kBwdThreads, hi - batch);
+// One pixel's step of the replay for one splat: exact forward arithmetic for
+// sigma / alpha / T, then the pixel's gradient contribution added into gv.
+template <bool SMOOTH, bool REFINE>
+__device__ __forceinline__ bool pixel_step(PixelBwd& P, float pcx, float dx0, float xx, float xy, float sx, float sy,
+                                           float c00, float c01, float c11, float ca, float thr, float craw,
+                                           float cgraw, float cbraw, float wf, float hf, float (&gv)[16]) {
+    if (P.done) return false;
+    const float dyp = P.pcy - sy;
+    const float sigma = 0.5f * (xx + c11 * dyp * dyp) + xy * dyp;
+    if (!(sigma >= 0.0f) || sigma > thr) return false;
+    const float gauss = bsx_expf_neg(-sigma);
+    const float alpha = bsx_min(0.999f, ca * gauss);
+    const float wc = SMOOTH ? cutoff_weight(alpha) : (alpha >= 1.0f / 255.0f ? 1.0f : 0.0f);
+    if (!(wc > 0.0f)) return false;
+    const float ae = alpha * wc;
+    const float next_t = P.T * (1.0f - ae);
+    if (next_t <= 1.0e-4f) {
+        P.done = true;
+        return false;
+    }
+    // gradient arithmetic (tolerance-checked): fused operations allowed
+    const float T = P.T;
+    const float clr = bsx_max(craw, 0.0f), clg = bsx_max(cgraw, 0.0f), clb = bsx_max(cbraw, 0.0f);
+    const float vis = ae * T;
+    if (craw >= 0.0f) gv[5] = __fmaf_rn(vis, P.vor, gv[5]);
+    if (cgraw >= 0.0f) gv[6] = __fmaf_rn(vis, P.vog, gv[6]);
+    if (cbraw >= 0.0f) gv[7] = __fmaf_rn(vis, P.vob, gv[7]);
+    const float ra = __fdividef(1.0f, 1.0f - ae);
+    float dot_rgb = __fmaf_rn(T, clr, -P.sr) * P.vor;
+    dot_rgb = __fmaf_rn(__fmaf_rn(T, clg, -P.sg), P.vog, dot_rgb);
+    dot_rgb = __fmaf_rn(__fmaf_rn(T, clb, -P.sb), P.vob, dot_rgb);
+    const float vae = (dot_rgb + P.vow) * ra;
+    const float valpha = SMOOTH ? vae * (wc + alpha * cutoff_weight_deriv(alpha)) : vae;
+    const float vsig = -alpha * valpha;
+    // the reference's backward uses d = splat - pixel
+    const float dx = -dx0, dy = -dyp;
+    const float vxx = vsig * __fmaf_rn(c00, dx, c01 * dy);
+    const float vxy = vsig * __fmaf_rn(c01, dx, c11 * dy);
+    if (ca * gauss <= 0.999f) {
+        const float hv = 0.5f * vsig;
+        gv[0] += vxx;
+        gv[1] += vxy;
+        gv[2] = __fmaf_rn(hv * dx, dx, gv[2]);
+        gv[3] = __fmaf_rn(vsig * dx, dy, gv[3]);
+        gv[4] = __fmaf_rn(hv * dy, dy, gv[4]);
+        gv[8] = __fmaf_rn(valpha, gauss, gv[8]);
+        if (REFINE) {
+            const float ax = vxx * wf, ay = vxy * hf;
+            const float q = __fmaf_rn(ax, ax, ay * ay);
+            gv[9] = __fmaf_rn(q * rsqrtf(fmaxf(q, 1e-38f)), P.inv_fa, gv[9]);
+        }
+    }
+    P.sr = __fmaf_rn(-vis, clr, P.sr);
+    P.sg = __fmaf_rn(-vis, clg, P.sg);
+    P.sb = __fmaf_rn(-vis, clb, P.sb);
+    P.T = next_t;
+    return true;
+}
+
+// Two pixels per thread (rows y and y + 8 of the tile), 128 threads per tile.
+constexpr int kBwdPixThreads = 128;
+
+template <bool SMOOTH, bool REFINE>
+__global__ void __launch_bounds__(kBwdPixThreads) raster_bwd_kernel(const BwdArgs a) {
+    __shared__ float4 s_a[kBwdPixThreads];  // x, y, c00, c01
+    __shared__ float4 s_b[kBwdPixThreads];  // c11, opacity, r, g
+    __shared__ float2 s_c[kBwdPixThreads];  // b, ln(255 o) + margin
+    __shared__ uint32_t s_mask[kBwdPixThreads];
+    __shared__ uint32_t s_gid[kBwdPixThreads];
+    __shared__ float s_grad[kBwdPixThreads][kGradLanes + 1];
+
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t tile = blockIdx.x;
+    const uint32_t lo = __ldg(a.tile_offsets + tile * 2), hi = __ldg(a.tile_offsets + tile * 2 + 1);
+    if (hi <= lo) return;
+    const uint32_t ox = (tile % a.tbw) * kTile, oy = (tile / a.tbw) * kTile;
+    const uint32_t lx = compact_bits_16(threadIdx.x), ly = compact_bits_16(threadIdx.x >> 1);
+    const uint32_t wcols = 0xffu << (8 * ((warp >> 1) & 1));
+    const uint32_t wrows = 0x0f0fu << (4 * (warp & 1));
+    const uint32_t px = ox + lx;
+    const float pcx = (float)px + 0.5f;
+    const float margin = SMOOTH ? kMarginSmooth : kMarginHard;
+    const float wf = (float)a.w, hf = (float)a.h;
+    PixelBwd PA, PB;
+    pixel_init(PA, a, px, oy + ly);
+    pixel_init(PB, a, px, oy + ly + 8);
+
+    for (uint32_t batch = lo; batch < hi; batch += kBwdPixThreads) {
+        if (__syncthreads_count(PA.done && PB.done) == kBwdPixThreads) break;
+        const uint32_t n = min((uint32_t)kBwdPixThreads, hi - batch);
         if (threadIdx.x < n) {
             const uint32_t g = __ldg(a.isect_gid + batch + threadIdx.x);
             const float4* row = reinterpret_cast<const float4*>(a.projected + (size_t)g * BSX_PROJECTED_LANES);
@@ -175,69 +250,21 @@ __global__ void __launch_bounds__(kBwdThreads) raster_bwd_kernel(const BwdArgs a
         __syncthreads();
         for (uint32_t t = 0; t < n; ++t) {
             const uint32_t m = s_mask[t];
-            if (!(m & wcols) || !((m >> 16) & wrows)) continue;  // warp-uniform
-            if (__all_sync(0xffffffffu, done)) break;             // warp-uniform
+            if (!(m & wcols) || !((m >> 16) & wrows)) continue;    // warp-uniform
+            if (__all_sync(0xffffffffu, PA.done && PB.done)) break;  // warp-uniform
+            const float4 A = s_a[t];
+            const float4 B = s_b[t];
+            const float2 Cc = s_c[t];
+            const float dx0 = pcx - A.x;
+            const float xx = A.z * dx0 * dx0;
+            const float xy = A.w * dx0;
             float gv[16];
 #pragma unroll
             for (int k = 0; k < 16; ++k) gv[k] = 0.0f;
-            bool contrib = false;
-            if (!done && ((m >> lx) & (m >> (16 + ly)) & 1u)) {
-                const float4 A = s_a[t];
-                const float4 B = s_b[t];
-                const float2 Cc = s_c[t];
-                const float sx = A.x, sy = A.y, c00 = A.z, c01 = A.w, c11 = B.x, ca = B.y;
-                // exact forward arithmetic
-                const float sigma = calc_sigma(pcx, pcy, c00, c01, c11, sx, sy);
-                if (sigma <= Cc.y) {
-                    const float gauss = bsx_expf(-sigma);
-                    const float alpha = bsx_min(0.999f, ca * gauss);
-                    const float wc = SMOOTH ? cutoff_weight(alpha) : (alpha >= 1.0f / 255.0f ? 1.0f : 0.0f);
-                    if (sigma >= 0.0f && wc > 0.0f) {
-                        const float ae = alpha * wc;
-                        const float next_t = T * (1.0f - ae);
-                        if (next_t <= 1.0e-4f) {
-                            done = true;
-                        } else {
-                            contrib = true;
-                            const float craw = B.z, cgraw = B.w, cbraw = Cc.x;
-                            const float clr = bsx_max(craw, 0.0f), clg = bsx_max(cgraw, 0.0f),
-                                        clb = bsx_max(cbraw, 0.0f);
-                            const float vis = ae * T;
-                            gv[5] = craw >= 0.0f ? vis * vor : 0.0f;
-                            gv[6] = cgraw >= 0.0f ? vis * vog : 0.0f;
-                            gv[7] = cbraw >= 0.0f ? vis * vob : 0.0f;
-                            const float ra = __fdividef(1.0f, 1.0f - ae);
-                            float dot_rgb = __fmaf_rn(T, clr, -sr) * vor;
-                            dot_rgb = __fmaf_rn(__fmaf_rn(T, clg, -sg), vog, dot_rgb);
-                            dot_rgb = __fmaf_rn(__fmaf_rn(T, clb, -sb), vob, dot_rgb);
-                            const float vae = (dot_rgb + vow) * ra;
-                            const float valpha = SMOOTH ? vae * (wc + alpha * cutoff_weight_deriv(alpha)) : vae;
-                            const float vsig = -alpha * valpha;
-                            const float dx = sx - pcx, dy = sy - pcy;
-                            const float vxx = vsig * __fmaf_rn(c00, dx, c01 * dy);
-                            const float vxy = vsig * __fmaf_rn(c01, dx, c11 * dy);
-                            if (ca * gauss <= 0.999f) {
-                                const float hv = 0.5f * vsig;
-                                gv[0] = vxx;
-                                gv[1] = vxy;
-                                gv[2] = hv * dx * dx;
-                                gv[3] = vsig * dx * dy;
-                                gv[4] = hv * dy * dy;
-                                gv[8] = valpha * gauss;
-                                if (REFINE) {
-                                    const float ax = vxx * wf, ay = vxy * hf;
-                                    const float q = __fmaf_rn(ax, ax, ay * ay);
-                                    gv[9] = q * rsqrtf(fmaxf(q, 1e-38f)) * inv_fa;
-                                }
-                            }
-                            sr = __fmaf_rn(-vis, clr, sr);
-                            sg = __fmaf_rn(-vis, clg, sg);
-                            sb = __fmaf_rn(-vis, clb, sb);
-                            T = next_t;
-                        }
-                    }
-                }
-            }
+            bool contrib = pixel_step<SMOOTH, REFINE>(PA, pcx, dx0, xx, xy, A.x, A.y, A.z, A.w, B.x, B.y, Cc.y, B.z,
+                                                      B.w, Cc.x, wf, hf, gv);
+            contrib |= pixel_step<SMOOTH, REFINE>(PB, pcx, dx0, xx, xy, A.x, A.y, A.z, A.w, B.x, B.y, Cc.y, B.z, B.w,
+                                                  Cc.x, wf, hf, gv);
             if (__any_sync(0xffffffffu, contrib)) {
                 const float tot = warp_sum16(gv, lane);
                 const int k = lane >> 1;
@@ -250,11 +277,12 @@ __global__ void __launch_bounds__(kBwdThreads) raster_bwd_kernel(const BwdArgs a
             bool any = false;
 #pragma unroll
             for (int k = 0; k < kGradLanes; ++k) any = any || sgr[k] != 0.0f;
-            if (!any) continue;
-            float4* dst = reinterpret_cast<float4*>(a.v_grad + (size_t)s_gid[threadIdx.x] * kGradStride);
-            atomicAdd(dst, make_float4(sgr[0], sgr[1], sgr[2], sgr[3]));
-            atomicAdd(dst + 1, make_float4(sgr[4], sgr[5], sgr[6], sgr[7]));
-            atomicAdd(dst + 2, make_float4(sgr[8], sgr[9], 0.0f, 0.0f));
+            if (any) {
+                float4* dst = reinterpret_cast<float4*>(a.v_grad + (size_t)s_gid[threadIdx.x] * kGradStride);
+                atomicAdd(dst, make_float4(sgr[0], sgr[1], sgr[2], sgr[3]));
+                atomicAdd(dst + 1, make_float4(sgr[4], sgr[5], sgr[6], sgr[7]));
+                atomicAdd(dst + 2, make_float4(sgr[8], sgr[9], 0.0f, 0.0f));
+            }
         }
     }
 }
@@ -281,11 +309,11 @@ bsx_status launch_raster_bwd(bsx_ctx* ctx, const uint32_t* isect_gid, const uint
     const uint32_t blocks = a.num_tiles;
     prof_begin(ctx);
     if (smooth) {
-        if (refine) raster_bwd_kernel<true, true><<<blocks, kBwdThreads, 0, ctx->stream>>>(a);
-        else raster_bwd_kernel<true, false><<<blocks, kBwdThreads, 0, ctx->stream>>>(a);
+        if (refine) raster_bwd_kernel<true, true><<<blocks, kBwdPixThreads, 0, ctx->stream>>>(a);
+        else raster_bwd_kernel<true, false><<<blocks, kBwdPixThreads, 0, ctx->stream>>>(a);
     } else {
-        if (refine) raster_bwd_kernel<false, true><<<blocks, kBwdThreads, 0, ctx->stream>>>(a);
-        else raster_bwd_kernel<false, false><<<blocks, kBwdThreads, 0, ctx->stream>>>(a);
+        if (refine) raster_bwd_kernel<false, true><<<blocks, kBwdPixThreads, 0, ctx->stream>>>(a);
+        else raster_bwd_kernel<false, false><<<blocks, kBwdPixThreads, 0, ctx->stream>>>(a);
     }
     return post_launch(ctx, "raster_bwd_kernel");
 }

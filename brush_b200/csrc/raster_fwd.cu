@@ -19,7 +19,6 @@ namespace bsx {
 
 namespace {
 
-constexpr int kRasterThreads = 256;
 // Rejection margin on sigma for the exponential-free pre-filter. With the
 // hard cutoff the exact test is sigma <= ln(255 o) up to a few ulp of the
 // shared exp/ln; the smooth ramp starts at alpha = 1/255 - 5e-4, i.e.
@@ -74,82 +73,104 @@ struct FwdArgs {
     float bg_r, bg_g, bg_b;
 };
 
+// Two pixels per thread: Morton index t < 128 gives (x, y) with y < 8, and
+// the thread also owns (x, y + 8). Both share dx and its products.
+constexpr int kFwdThreads = 128;
+
 template <bool BWD, bool SMOOTH>
-__global__ void __launch_bounds__(kRasterThreads) raster_fwd_kernel(const FwdArgs a) {
-    __shared__ float4 s_a[kRasterThreads];  // x, y, c00, c01
-    __shared__ float4 s_b[kRasterThreads];  // c11, opacity, r, g
-    __shared__ float4 s_c[kRasterThreads];  // b, depth, ln(255 o), 0
-    __shared__ uint32_t s_mask[kRasterThreads];
-    __shared__ uint32_t s_gid[BWD ? kRasterThreads : 1];
-    __shared__ int s_used[BWD ? kRasterThreads : 1];
+__global__ void __launch_bounds__(kFwdThreads) raster_fwd_kernel(const FwdArgs a) {
+    __shared__ float4 s_a[kFwdThreads];  // x, y, c00, c01
+    __shared__ float4 s_b[kFwdThreads];  // c11, opacity, r, g
+    __shared__ float2 s_c[kFwdThreads];  // b, ln(255 o) + margin
+    __shared__ uint32_t s_mask[kFwdThreads];
+    __shared__ uint32_t s_gid[BWD ? kFwdThreads : 1];
+    __shared__ int s_used[BWD ? kFwdThreads : 1];
     __shared__ uint32_t s_max_useful;
 
     const uint32_t tile = blockIdx.x;
     const uint32_t tx = tile % a.tbw, ty = tile / a.tbw;
-    const uint32_t lxp = compact_bits_16(threadIdx.x), lyp = compact_bits_16(threadIdx.x >> 1);
-    // the warp's 8x4 Morton patch as column / row masks (for warp-uniform skips)
+    const uint32_t lx = compact_bits_16(threadIdx.x), ly = compact_bits_16(threadIdx.x >> 1);
     const uint32_t wid = threadIdx.x >> 5;
     const uint32_t wcols = 0xffu << (8 * ((wid >> 1) & 1));
-    const uint32_t wrows = 0xfu << (4 * (wid & 1) + 8 * ((wid >> 2) & 1));
-    const uint32_t px = tx * kTile + lxp;
-    const uint32_t py = ty * kTile + lyp;
-    const bool inside = px < a.w && py < a.h;
-    const float pcx = (float)px + 0.5f, pcy = (float)py + 0.5f;
+    const uint32_t wrows = 0x0f0fu << (4 * (wid & 1));  // rows r..r+3 and r+8..r+11
+    const uint32_t px = tx * kTile + lx, pyA = ty * kTile + ly, pyB = pyA + 8;
+    const bool inA = px < a.w && pyA < a.h, inB = px < a.w && pyB < a.h;
+    const float pcx = (float)px + 0.5f, pcyA = (float)pyA + 0.5f, pcyB = (float)pyB + 0.5f;
     const uint32_t lo = a.tile_offsets[tile * 2], hi = a.tile_offsets[tile * 2 + 1];
     if (BWD) {
         if (threadIdx.x == 0) s_max_useful = lo;
         __syncthreads();
     }
-
-    float T = 1.0f, cr = 0.0f, cg = 0.0f, cb = 0.0f;
-    bool done = !inside;
+    float TA = 1.0f, rA = 0.0f, gA = 0.0f, bA = 0.0f;
+    float TB = 1.0f, rB = 0.0f, gB = 0.0f, bB = 0.0f;
+    bool doneA = !inA, doneB = !inB;
     uint32_t last = lo;
     const float margin = SMOOTH ? kMarginSmooth : kMarginHard;
 
-    for (uint32_t batch = lo; batch < hi; batch += kRasterThreads) {
-        if (__syncthreads_count(done) == kRasterThreads) break;
-        const uint32_t n = min((uint32_t)kRasterThreads, hi - batch);
+    for (uint32_t batch = lo; batch < hi; batch += kFwdThreads) {
+        if (__syncthreads_count(doneA && doneB) == kFwdThreads) break;
+        const uint32_t n = min((uint32_t)kFwdThreads, hi - batch);
         if (threadIdx.x < n) {
             const uint32_t g = __ldg(a.isect_gid + batch + threadIdx.x);
             const float4* row = reinterpret_cast<const float4*>(a.projected + (size_t)g * BSX_PROJECTED_LANES);
             const float4 ra = __ldg(row), rb = __ldg(row + 1), rc = __ldg(row + 2);
             s_a[threadIdx.x] = ra;
             s_b[threadIdx.x] = rb;
-            s_c[threadIdx.x] = rc;
-            s_mask[threadIdx.x] = splat_pixel_mask(ra.x, ra.y, ra.z, ra.w, rb.x, rc.z + margin, tx * kTile, ty * kTile);
+            s_c[threadIdx.x] = make_float2(rc.x, rc.z + margin);
+            s_mask[threadIdx.x] =
+                splat_pixel_mask(ra.x, ra.y, ra.z, ra.w, rb.x, rc.z + margin, tx * kTile, ty * kTile);
             if (BWD) {
                 s_gid[threadIdx.x] = g;
                 s_used[threadIdx.x] = 0;
             }
         }
         __syncthreads();
-        if (!done) {
-            for (uint32_t t = 0; t < n; ++t) {
-                const uint32_t m = s_mask[t];
-                if (!(m & wcols) || !((m >> 16) & wrows)) continue;
-                if (!((m >> lxp) & (m >> (16 + lyp)) & 1u)) continue;
-                const float4 A = s_a[t];
-                const float c11 = s_b[t].x;
-                const float sigma = calc_sigma(pcx, pcy, A.z, A.w, c11, A.x, A.y);
-                if (sigma > s_c[t].z + margin) continue;
+        for (uint32_t t = 0; t < n && !(doneA && doneB); ++t) {
+            const uint32_t m = s_mask[t];
+            if (!(m & wcols) || !((m >> 16) & wrows)) continue;
+            const float4 A = s_a[t];
+            const float c11 = s_b[t].x;
+            const float thr = s_c[t].y;
+            // calc_sigma(px, py, conic, x, y) with dx shared by both pixels
+            const float dx = pcx - A.x;
+            const float xx = A.z * dx * dx;
+            const float xy = A.w * dx;
+            bool used = false;
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                bool& done = q ? doneB : doneA;
+                if (done) continue;
+                const float dy = (q ? pcyB : pcyA) - A.y;
+                const float sigma = 0.5f * (xx + c11 * dy * dy) + xy * dy;
+                if (!(sigma >= 0.0f) || sigma > thr) continue;
                 const float4 B = s_b[t];
-                const float alpha = bsx_min(0.999f, B.y * bsx_expf(-sigma));
+                const float alpha = bsx_min(0.999f, B.y * bsx_expf_neg(-sigma));
                 const float wc = SMOOTH ? cutoff_weight(alpha) : (alpha >= 1.0f / 255.0f ? 1.0f : 0.0f);
-                if (sigma >= 0.0f && wc > 0.0f) {
-                    const float ae = alpha * wc;
-                    const float next_t = T * (1.0f - ae);
-                    if (next_t <= 1.0e-4f) {
-                        done = true;
-                        break;
-                    }
-                    if (BWD) s_used[t] = 1;
-                    const float vis = ae * T;
-                    cr += bsx_max(B.z, 0.0f) * vis;
-                    cg += bsx_max(B.w, 0.0f) * vis;
-                    cb += bsx_max(s_c[t].x, 0.0f) * vis;
-                    T = next_t;
-                    last = batch + t + 1;
+                if (!(wc > 0.0f)) continue;
+                float& T = q ? TB : TA;
+                const float ae = alpha * wc;
+                const float next_t = T * (1.0f - ae);
+                if (next_t <= 1.0e-4f) {
+                    done = true;
+                    continue;
                 }
+                const float vis = ae * T;
+                const float cb = s_c[t].x;
+                if (q) {
+                    rB += bsx_max(B.z, 0.0f) * vis;
+                    gB += bsx_max(B.w, 0.0f) * vis;
+                    bB += bsx_max(cb, 0.0f) * vis;
+                } else {
+                    rA += bsx_max(B.z, 0.0f) * vis;
+                    gA += bsx_max(B.w, 0.0f) * vis;
+                    bA += bsx_max(cb, 0.0f) * vis;
+                }
+                T = next_t;
+                used = true;
+            }
+            if (used) {
+                last = batch + t + 1;
+                if (BWD) s_used[t] = 1;
             }
         }
         if (BWD) {
@@ -158,10 +179,13 @@ __global__ void __launch_bounds__(kRasterThreads) raster_fwd_kernel(const FwdArg
         }
     }
 
-    if (inside) {
-        const float fr = cr + T * a.bg_r, fg = cg + T * a.bg_g, fb = cb + T * a.bg_b;
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+        if (!(q ? inB : inA)) continue;
+        const float T = q ? TB : TA;
+        const float fr = (q ? rB : rA) + T * a.bg_r, fg = (q ? gB : gA) + T * a.bg_g, fb = (q ? bB : bA) + T * a.bg_b;
         const float fa = 1.0f - T;
-        const size_t pid = (size_t)py * a.w + px;
+        const size_t pid = (size_t)(q ? pyB : pyA) * a.w + px;
         if (BWD) {
             reinterpret_cast<float4*>(a.image)[pid] = make_float4(fr, fg, fb, fa);
         } else {
@@ -199,9 +223,9 @@ bsx_status launch_raster_fwd(bsx_ctx* ctx, const uint32_t* isect_gid, uint32_t* 
     a.bg_b = bg[2];
     const uint32_t tiles = u.tile_bw * u.tile_bh;
     prof_begin(ctx);
-    if (!bwd_info) raster_fwd_kernel<false, false><<<tiles, kRasterThreads, 0, ctx->stream>>>(a);
-    else if (!smooth) raster_fwd_kernel<true, false><<<tiles, kRasterThreads, 0, ctx->stream>>>(a);
-    else raster_fwd_kernel<true, true><<<tiles, kRasterThreads, 0, ctx->stream>>>(a);
+    if (!bwd_info) raster_fwd_kernel<false, false><<<tiles, kFwdThreads, 0, ctx->stream>>>(a);
+    else if (!smooth) raster_fwd_kernel<true, false><<<tiles, kFwdThreads, 0, ctx->stream>>>(a);
+    else raster_fwd_kernel<true, true><<<tiles, kFwdThreads, 0, ctx->stream>>>(a);
     return post_launch(ctx, "raster_fwd_kernel");
 }
 

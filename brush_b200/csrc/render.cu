@@ -64,8 +64,8 @@ bsx_status bsx_render_fwd(bsx_ctx* ctx, const bsx_camera* cam, uint32_t w, uint3
     if (raster_pass < 0 || raster_pass > 2) return fail(ctx, BSX_ERR_INVALID_ARG, "raster_pass");
     const int degree = degree_from_coeffs(coeffs);
     if (degree < 0) return fail(ctx, BSX_ERR_SHAPE, "sh_coeffs must be [N, (degree+1)^2, 3] with degree <= 4");
-    if (((uintptr_t)d_transforms | (uintptr_t)d_sh | (uintptr_t)d_raw_opac) % 4)
-        return fail(ctx, BSX_ERR_INVALID_ARG, "splat tensors must be 4-byte aligned");
+    if (((uintptr_t)d_sh | (uintptr_t)d_raw_opac) % 4 || (uintptr_t)d_transforms % 8)
+        return fail(ctx, BSX_ERR_INVALID_ARG, "transforms must be 8-byte aligned, sh / opacities 4-byte aligned");
     cudaSetDevice(ctx->device);
     bsx_project_uniforms uni;
     BSX_TRY(bsx_make_project_uniforms(cam, w, h, (uint32_t)degree, n, &uni));

@@ -9,8 +9,8 @@
 namespace bsx {
 
 template <int DEG>
-__device__ __forceinline__ V3 sh_to_color(const float* __restrict__ c, V3 v) {
-    auto rc = [&](int k) { return v3(__ldg(c + 3 * k), __ldg(c + 3 * k + 1), __ldg(c + 3 * k + 2)); };
+__device__ __forceinline__ V3 sh_to_color(const float* c, V3 v) {
+    auto rc = [&](int k) { return v3(c[3 * k], c[3 * k + 1], c[3 * k + 2]); };
     V3 color = vscale(rc(0), 0.2820948f);
     if (DEG >= 1) {
         const float f0a = 0.4886025f;
@@ -132,8 +132,8 @@ __device__ __forceinline__ void sh_coeffs_vjp(float* __restrict__ out, V3 v, V3 
 
 // d loss / d view direction through the SH basis (sh.rs:342-470).
 template <int DEG>
-__device__ __forceinline__ V3 sh_viewdir_vjp(const float* __restrict__ c, V3 v, V3 vc) {
-    auto sd = [&](int k) { return vdot(v3(__ldg(c + 3 * k), __ldg(c + 3 * k + 1), __ldg(c + 3 * k + 2)), vc); };
+__device__ __forceinline__ V3 sh_viewdir_vjp(const float* c, V3 v, V3 vc) {
+    auto sd = [&](int k) { return vdot(v3(c[3 * k], c[3 * k + 1], c[3 * k + 2]), vc); };
     float gx = 0.0f, gy = 0.0f, gz = 0.0f;
     if (DEG >= 1) {
         const float f0a = 0.4886025f;

@@ -137,7 +137,7 @@ typedef struct bsx_adam_group {
     float* d_v;            /* [rows, cols] or [rows] when reduce_moment_2 */
     uint32_t rows, cols;
     float lr;
-    const float* h_col_scale;  /* may be NULL (all ones); at most 64 entries */
+    const float* h_col_scale;  /* may be NULL (all ones); at most 80 entries */
     int32_t reduce_moment_2;
 } bsx_adam_group;
 

@@ -116,6 +116,27 @@ BSX_HD float bsx_expf(float x) {
     return (p * bsx_pow2i(ki + 64)) * 5.421010862427522e-20f; /* 2^-64 */
 }
 
+/* bsx_expf for arguments known to lie in [-87, 0] (no NaN, overflow or
+ * subnormal handling needed): the same operation sequence as bsx_expf, so the
+ * result is bit-identical there. */
+BSX_HD float bsx_expf_neg(float x) {
+    const float kLog2e = 1.4426950216293335f;
+    const float kLn2Hi = 0.693145751953125f;
+    const float kLn2Lo = 1.428606765330187e-06f;
+    float k = bsx_rint(x * kLog2e);
+    float r = bsx_fma(-k, kLn2Hi, x);
+    r = bsx_fma(-k, kLn2Lo, r);
+    float p = 0.00019841270113829523f;
+    p = bsx_fma(p, r, 0.0013888889225199819f);
+    p = bsx_fma(p, r, 0.008333333767950535f);
+    p = bsx_fma(p, r, 0.0416666679084301f);
+    p = bsx_fma(p, r, 0.1666666716337204f);
+    p = bsx_fma(p, r, 0.5f);
+    p = bsx_fma(p, r, 1.0f);
+    p = bsx_fma(p, r, 1.0f);
+    return p * bsx_pow2i((int)k);
+}
+
 /* Natural logarithm in float32. */
 BSX_HD float bsx_logf(float x) {
     if (x != x) return x;
