@@ -50,12 +50,15 @@ __device__ __forceinline__ uint32_t row_of(uint32_t e, float inv_cols) {
 }
 
 // One block = one contiguous tile of whole rows of one group. The gradient
-// tile is staged in shared memory with coalesced float4 loads (accumulating
-// per-row sums of squares for reduce_moment_2 groups on the way), then p, m, v
-// stream through once with coalesced float4 loads and stores.
+// tile is staged in shared memory with coalesced float4 loads (keeping the sum
+// of squares of each float4 for reduce_moment_2 groups on the way), then p, m,
+// v stream through once with coalesced float4 loads and stores. Every sum is
+// taken in a fixed order, so equal inputs give bit-equal outputs on every run
+// and every data-parallel replica.
 __global__ void __launch_bounds__(kAdamThreads) adam_kernel(const __grid_constant__ AdamArgs a) {
     __shared__ __align__(16) float s_g[kTileFloats];
     __shared__ float s_v[kTileFloats];
+    __shared__ float s_q[kTileFloats / 4];
     int k = 0;
     for (int i = 1; i < a.ngroups; ++i)
         if (blockIdx.x >= a.g[i].block_begin) k = i;
@@ -68,27 +71,26 @@ __global__ void __launch_bounds__(kAdamThreads) adam_kernel(const __grid_constan
     const float one_m_b1 = 1.0f - a.b1, one_m_b2 = 1.0f - a.b2;
     const bool vec = G.vec;
     const uint32_t nvec = vec ? count / 4 : 0;
-    if (G.reduce)
-        for (uint32_t r = threadIdx.x; r < nrows; r += kAdamThreads) s_v[r] = 0.0f;
-    __syncthreads();
     const bool row_quads = G.reduce && (cols % 4) == 0;  // a float4 never straddles two rows
     for (uint32_t j = threadIdx.x; j < nvec; j += kAdamThreads) {
         float4 v = __ldg(reinterpret_cast<const float4*>(G.grad + base) + j);
         v = make_float4(v.x * a.gscale, v.y * a.gscale, v.z * a.gscale, v.w * a.gscale);
         reinterpret_cast<float4*>(s_g)[j] = v;
-        if (row_quads) atomicAdd(&s_v[row_of(4 * j, G.inv_cols)], v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w);
+        if (row_quads) s_q[j] = v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
     }
     for (uint32_t j = nvec * 4 + threadIdx.x; j < count; j += kAdamThreads) {
         const float g = __ldg(G.grad + base + j) * a.gscale;
         s_g[j] = g;
-        if (row_quads) atomicAdd(&s_v[row_of(j, G.inv_cols)], g * g);
     }
     __syncthreads();
     if (G.reduce) {
         for (uint32_t r = threadIdx.x; r < nrows; r += kAdamThreads) {
             float s2;
-            if (row_quads) {
-                s2 = s_v[r];
+            if (row_quads && vec) {
+                // fixed summation order: quads of the row in column order
+                const uint32_t q = cols / 4;
+                s2 = 0.0f;
+                for (uint32_t i = 0; i < q; ++i) s2 += s_q[r * q + i];
             } else {
                 s2 = 0.0f;
                 for (uint32_t c = 0; c < cols; ++c) {

@@ -47,3 +47,36 @@ def replicas_agree(group, *tensors: torch.Tensor, tol: float = 0.0) -> bool:
     torch.distributed.all_reduce(lo, op=torch.distributed.ReduceOp.MIN, group=group)
     torch.distributed.all_reduce(hi, op=torch.distributed.ReduceOp.MAX, group=group)
     return float(hi - lo) <= tol
+
+
+def row_shard(n: int, world: int, rank: int) -> tuple[int, int]:
+    """Rows [start, end) of every parameter owned by ``rank`` (requires n % world == 0)."""
+    rows = n // world
+    return rank * rows, (rank + 1) * rows
+
+
+def _coalesced(group, fn):
+    """Issue the collectives ``fn`` enqueues as one NCCL group where supported."""
+    backend = torch.distributed.get_backend(group)
+    if backend == "nccl":
+        with torch.distributed._coalescing_manager(group=group):
+            fn()
+    else:
+        fn()
+
+
+def reduce_scatter_rows(fulls, shards, group) -> None:
+    """SUM-reduce row-sharded tensors: shards[i] <- rows of this rank of sum over ranks of fulls[i]."""
+    def run():
+        for f, s in zip(fulls, shards):
+            torch.distributed.reduce_scatter_tensor(s, f, op=torch.distributed.ReduceOp.SUM, group=group)
+    _coalesced(group, run)
+
+
+def all_gather_rows(fulls, group, rank: int, world: int) -> None:
+    """In-place all-gather: every rank's row shard of each tensor is copied to all ranks."""
+    def run():
+        for f in fulls:
+            rows = f.shape[0] // world
+            torch.distributed.all_gather_into_tensor(f, f[rank * rows:(rank + 1) * rows], group=group)
+    _coalesced(group, run)

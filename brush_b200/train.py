@@ -20,7 +20,7 @@ import torch
 from . import _lib
 from .adam import AdamGroup, AdamScaled
 from .camera import Camera
-from .dist import reduce_gradients
+from .dist import all_gather_rows, reduce_gradients, reduce_scatter_rows, row_shard
 from .loss import ImageLossConfig, image_loss_fused
 from .render import render
 from .render_bwd import SplatGrads, project_bwd, rasterize_bwd
@@ -74,8 +74,13 @@ class RefineRecord:
 
 
 class SplatTrainer:
-    def __init__(self, config: TrainConfig, splats: Splats, process_group=None, gather_stats: bool = True):
+    def __init__(self, config: TrainConfig, splats: Splats, process_group=None, gather_stats: bool = True,
+                 shard_optimizer: bool = True):
         self.config = config
+        # With several ranks and N divisible by the world size, each rank keeps
+        # Adam state for, and updates, only its row shard of the splats:
+        # reduce-scatter gradients -> fused Adam on the shard -> all-gather.
+        self.shard_optimizer = shard_optimizer
         self.adam = AdamScaled(epsilon=1e-15)
         self.step_count = 0
         self.pg = process_group
@@ -106,6 +111,13 @@ class SplatTrainer:
         self.v_output = None
         self.record = RefineRecord.new(n, dev) if self.gather_stats else None
         self.groups = None
+        self.sharded = self.shard_optimizer and self.world > 1 and n % self.world == 0
+        if self.sharded:
+            self.rank = torch.distributed.get_rank(self.pg)
+            self.row0, self.row1 = row_shard(n, self.world, self.rank)
+            r = self.row1 - self.row0
+            self.shard_grads = (torch.empty((r, 10), device=dev), torch.empty((r, 3 * c), device=dev),
+                                torch.empty((r, 1), device=dev))
 
     def _lr_table(self):
         cfg = self.config
@@ -135,23 +147,35 @@ class SplatTrainer:
         image_loss_fused(out.out_img, gt_packed, lcfg, self.loss, self.v_output)
         rasterize_bwd(self.v_output, compute_refine_weight, self.v_combined)
         project_bwd(self.v_combined, self.n, self.c, self.grads)
-        grad_scale = reduce_gradients(self.flat_grad, self.grads.v_refine_weight if self.record is not None else None,
-                                      self.pg)
-        lr_t, tscale, lr_sh, sh_cols, lr_op, lr_mean = self._lr_table()
         n, c = self.n, self.c
+        full_params = (splats.transforms, splats.sh_coeffs.view(n, 3 * c), splats.raw_opacities.view(n, 1))
+        full_grads = (self.grads.v_transforms, self.grads.v_coeffs.view(n, 3 * c), self.grads.v_raw_opac.view(n, 1))
+        if self.sharded:
+            reduce_scatter_rows(full_grads, self.shard_grads, self.pg)
+            if self.record is not None:
+                torch.distributed.all_reduce(self.grads.v_refine_weight, op=torch.distributed.ReduceOp.MAX,
+                                             group=self.pg)
+            grad_scale = 1.0 / self.world
+            params = tuple(p[self.row0:self.row1] for p in full_params)
+            grads = self.shard_grads
+        else:
+            grad_scale = reduce_gradients(self.flat_grad,
+                                          self.grads.v_refine_weight if self.record is not None else None, self.pg)
+            params, grads = full_params, full_grads
+        lr_t, tscale, lr_sh, sh_cols, lr_op, lr_mean = self._lr_table()
         if self.groups is None:
-            self.groups = [
-                AdamGroup(splats.transforms, self.grads.v_transforms, lr_t),
-                AdamGroup(splats.sh_coeffs.view(n, 3 * c), self.grads.v_coeffs.view(n, 3 * c), lr_sh,
-                          reduce_moment_2=True),
-                AdamGroup(splats.raw_opacities.view(n, 1), self.grads.v_raw_opac.view(n, 1), lr_op),
-            ]
+            self.groups = [AdamGroup(params[0], grads[0], lr_t),
+                           AdamGroup(params[1], grads[1], lr_sh, reduce_moment_2=True),
+                           AdamGroup(params[2], grads[2], lr_op)]
         g0, g1, g2 = self.groups
-        g0.param, g1.param, g2.param = splats.transforms, splats.sh_coeffs.view(n, 3 * c), splats.raw_opacities.view(n, 1)
+        g0.param, g1.param, g2.param = params
+        g0.grad, g1.grad, g2.grad = grads
         g0.lr, g0.col_scale = lr_t, tscale
         g1.lr, g1.col_scale = lr_sh, sh_cols
         g2.lr = lr_op
         self.adam.step(self.groups, grad_scale=grad_scale)
+        if self.sharded:
+            all_gather_rows(full_params, self.pg, self.rank, self.world)
         if self.record is not None:
             if compute_refine_weight:
                 self.record.gather_stats(self.grads.v_refine_weight, out.aux.visible, out.aux.max_radius)

@@ -61,7 +61,32 @@ def _apply(orc, splats, flat, scale):
     return t, sh, op
 
 
-def _worker(rank, world, port, q, die_rank):
+def _apply_sharded(orc, splats, flat, rank, world, group):
+    """reduce-scatter rows -> Adam on this rank's rows -> in-place all-gather."""
+    import torch
+
+    from brush_b200.dist import all_gather_rows, reduce_scatter_rows, row_shard
+
+    n, c = splats.num_splats, splats.sh_coeffs_per_splat
+    ft = torch.from_numpy(flat)
+    fulls_g = (ft[: n * 10].view(n, 10), ft[n * 10: n * (10 + 3 * c)].view(n, 3 * c), ft[n * (10 + 3 * c):].view(n, 1))
+    r0, r1 = row_shard(n, world, rank)
+    shards = tuple(torch.empty((r1 - r0, f.shape[1])) for f in fulls_g)
+    reduce_scatter_rows(fulls_g, shards, group)
+    t = splats.transforms.numpy().copy()
+    sh = splats.sh_coeffs.numpy().reshape(n, 3 * c).copy()
+    op = splats.raw_opacities.numpy().reshape(n, 1).copy()
+    for p, g, red in [(t, shards[0], False), (sh, shards[1], True), (op, shards[2], False)]:
+        pv = np.ascontiguousarray(p[r0:r1])
+        orc.adam(pv, g.numpy(), np.zeros_like(pv), np.zeros(r1 - r0, np.float32) if red else np.zeros_like(pv), 1e-3,
+                 None, red, grad_scale=1.0 / world)
+        p[r0:r1] = pv
+    fulls_p = (torch.from_numpy(t), torch.from_numpy(sh), torch.from_numpy(op))
+    all_gather_rows(fulls_p, group, rank, world)
+    return fulls_p[0].numpy(), fulls_p[1].numpy(), fulls_p[2].numpy()
+
+
+def _worker(rank, world, port, q, die_rank, sharded=False):
     sys.path.insert(0, str(ROOT))
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -78,9 +103,14 @@ def _worker(rank, world, port, q, die_rank):
         flat, vr = _view_grad(orc, splats, cams[v], size, gts[v])
         if rank == die_rank:
             os._exit(3)  # leaves between steps, before the collective
-        ft, rt = torch.from_numpy(flat), torch.from_numpy(vr)
-        scale = reduce_gradients(ft, rt, torch.distributed.group.WORLD)
-        t, sh, op = _apply(orc, splats, ft.numpy(), scale)
+        if sharded:
+            t, sh, op = _apply_sharded(orc, splats, flat, rank, world, torch.distributed.group.WORLD)
+            rt, scale = torch.from_numpy(vr), 1.0 / world
+            torch.distributed.all_reduce(rt, op=torch.distributed.ReduceOp.MAX)
+        else:
+            ft, rt = torch.from_numpy(flat), torch.from_numpy(vr)
+            scale = reduce_gradients(ft, rt, torch.distributed.group.WORLD)
+            t, sh, op = _apply(orc, splats, ft.numpy(), scale)
         agree = replicas_agree(torch.distributed.group.WORLD, torch.from_numpy(t), torch.from_numpy(sh),
                                torch.from_numpy(op))
         q.put((rank, "ok", t, sh, op, scale, agree, rt.numpy()))
@@ -93,11 +123,11 @@ def _worker(rank, world, port, q, die_rank):
             pass
 
 
-def _run(world, die_rank=-1, timeout=120):
+def _run(world, die_rank=-1, timeout=120, sharded=False):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q, die_rank)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, die_rank, sharded)) for r in range(world)]
     for p in procs:
         p.start()
     out = []
@@ -111,8 +141,9 @@ def _run(world, die_rank=-1, timeout=120):
     return sorted(out, key=lambda r: r[0])
 
 
-def test_two_ranks_match_mean_of_views_step(orc):
-    res = _run(2)
+@pytest.mark.parametrize("sharded", [False, True], ids=["allreduce", "reduce_scatter"])
+def test_two_ranks_match_mean_of_views_step(orc, sharded):
+    res = _run(2, sharded=sharded)
     assert all(r[1] == "ok" for r in res), res
     (_, _, t0, s0, o0, sc0, ag0, r0), (_, _, t1, s1, o1, sc1, ag1, r1) = res
     assert sc0 == sc1 == 0.5 and ag0 and ag1

@@ -175,3 +175,24 @@ def test_train_step_matches_oracle_chain(cuda, orc):
         # where the reference gradient is not vanishingly small.
         big = np.abs(grad) > 1e-3 * np.abs(grad).max()
         assert np.abs(got - param)[big].max() <= 1e-3 * moved + 1e-7
+
+
+@pytest.mark.parametrize("cols", [48, 12, 75])
+def test_adam_bit_reproducible(cuda, cols):
+    """Equal inputs give bit-equal parameters and moments on every run (data-parallel replicas rely on it)."""
+    from brush_b200.adam import AdamGroup, AdamScaled
+
+    p0 = np.random.default_rng(cols).normal(0, 1, (50000, cols)).astype(np.float32)
+    grads = [torch.from_numpy(np.random.default_rng(100 + s).normal(0, 1, p0.shape).astype(np.float32)).cuda()
+             for s in range(2)]
+    outs = []
+    for _ in range(3):
+        g = AdamGroup(torch.from_numpy(p0.copy()).cuda(), None, 1e-3, reduce_moment_2=True)
+        opt = AdamScaled()
+        for gr in grads:
+            g.grad = gr
+            opt.step([g])
+        outs.append([t.cpu().numpy() for t in (g.param, g.m, g.v)])
+    for o in outs[1:]:
+        for a, b in zip(o, outs[0]):
+            np.testing.assert_array_equal(a, b)
