@@ -233,9 +233,12 @@ def run_ours(args, rank, world, local_rank):
                          "alg_bytes": int(b), "gbs": round(b / (avg_ms * 1e-3) / 1e9, 1) if avg_ms > 0 else None}
     dom = max(prof.items(), key=lambda kv: kv[1][0])[0] if prof else None
     traffic = None
-    tfile = ROOT / "profiles" / "traffic.json"
+    tfile = ROOT / "profiles" / "dram_traffic_cfg2.txt"
     if tfile.exists() and dom:
-        traffic = json.loads(tfile.read_text()).get(dom)
+        for ln in tfile.read_text().splitlines():
+            parts = ln.split()
+            if len(parts) == 2 and not ln.startswith("#") and parts[0] == dom:
+                traffic = int(parts[1])
     roof = None
     if dom:
         kd = kernels[dom]
