@@ -136,7 +136,7 @@ def run_ours(args, rank, world, local_rank):
     cams = [orbit_camera(i, ncam, 8.0, w, h) for i in range(ncam)]
     gts_host = [random_gt(h, w, 1000 + i, "cpu").pin_memory() for i in range(ncam)]
     gts_dev = [g.to(dev) for g in gts_host]
-    trainer = bsx.SplatTrainer(bsx.TrainConfig(), splats, process_group=pg)
+    trainer = bsx.SplatTrainer(bsx.TrainConfig(), splats, process_group=pg, exchange=args.exchange)
     ctx = context(dev)
 
     def view(step):
@@ -254,6 +254,9 @@ def run_ours(args, rank, world, local_rank):
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded; no dataset)",
         "config": {"workload": WORKLOAD, "splats": N, "sh_degree": 3, "width": w, "height": h,
                    "views_per_step_per_gpu": 1, "parallelism": f"dp{world}", "l2": "inputs larger than L2",
+                   "exchange": (None if world == 1 else
+                                "peer-memory fused reduce+Adam+broadcast kernel" if args.exchange == "peer" else
+                                "NCCL reduce-scatter + sharded Adam + all-gather"),
                    "num_visible": V, "num_intersections": M, "intersections_after_early_out": Mp},
         "fwd_bwd_ms": round(fwdbwd_ms, 4),
         "e2e": {"value": round(e2e_value, 3), "unit": "train steps/s",
@@ -263,6 +266,7 @@ def run_ours(args, rank, world, local_rank):
         "kernels": kernels,
         "clocks": clocks,
     }
+    trainer.close()
     return line
 
 
@@ -332,6 +336,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                    help="data-parallel gradient exchange with --gpus > 1")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -16,6 +16,9 @@ BSX_COMPACT_GRAD_LANES = 11
 BSX_GRAD_STRIDE = 12
 BSX_PROJECTED_LANES = 12
 BSX_TILE_WIDTH = 16
+BSX_MAX_RANKS = 8
+BSX_PEER_HANDLE_BYTES = 64
+BSX_DP_FLAG_WORDS = 64
 
 STATUS_NAMES = {
     0: "BSX_OK",
@@ -129,6 +132,32 @@ class AdamCfg(C.Structure):
     ]
 
 
+class DpGroup(C.Structure):
+    _fields_ = [
+        ("d_param", C.c_void_p * BSX_MAX_RANKS),
+        ("d_grad", C.c_void_p * BSX_MAX_RANKS),
+        ("d_m", C.c_void_p),
+        ("d_v", C.c_void_p),
+        ("rows", C.c_uint32),
+        ("cols", C.c_uint32),
+        ("lr", C.c_float),
+        ("h_col_scale", C.POINTER(C.c_float)),
+        ("reduce_moment_2", C.c_int32),
+    ]
+
+
+class DpExchange(C.Structure):
+    _fields_ = [
+        ("rank", C.c_int32),
+        ("world", C.c_int32),
+        ("d_flags", C.c_void_p * BSX_MAX_RANKS),
+        ("d_refine", C.c_void_p * BSX_MAX_RANKS),
+        ("refine_rows", C.c_uint32),
+        ("epoch", C.c_uint32),
+        ("timeout_ns", C.c_uint64),
+    ]
+
+
 # name -> (restype, argtypes); exactly the functions include/bsx.h declares.
 SIGNATURES = {
     "bsx_create": (C.c_int, [C.c_int, C.POINTER(C.c_void_p)]),
@@ -171,6 +200,13 @@ SIGNATURES = {
         [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.POINTER(LossCfg), C.c_void_p, C.c_void_p],
     ),
     "bsx_adam_step": (C.c_int, [C.c_void_p, C.POINTER(AdamGroup), C.c_int32, C.POINTER(AdamCfg)]),
+    "bsx_peer_alloc": (C.c_int, [C.c_void_p, C.c_uint64, C.POINTER(C.c_void_p), C.c_char_p]),
+    "bsx_peer_free": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "bsx_peer_open": (C.c_int, [C.c_void_p, C.c_char_p, C.POINTER(C.c_void_p)]),
+    "bsx_peer_close": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "bsx_dp_adam_step": (
+        C.c_int, [C.c_void_p, C.POINTER(DpExchange), C.POINTER(DpGroup), C.c_int32, C.POINTER(AdamCfg)]
+    ),
     "bsx_radix_argsort_u32": (
         C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p]
     ),

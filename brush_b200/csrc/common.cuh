@@ -24,6 +24,7 @@ enum DeviceError : int {
     kDevOk = 0,
     kDevLookbackTimeout = 1,
     kDevOutOfRange = 2,
+    kDevPeerTimeout = 3,
 };
 
 // Bounded spin for device-side waits on another block's published state.
@@ -33,6 +34,21 @@ constexpr uint32_t kSpinLimit = 1u << 22;
 
 __device__ __forceinline__ void set_error(int* err, int code) {
     if (err) atomicCAS(err, 0, code);
+}
+
+// System-scope flag accesses for waits on other GPUs (peer memory over NVLink).
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys_u32(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t global_timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
 }
 
 __device__ __forceinline__ uint64_t ld_relaxed_u64(const uint64_t* p) {

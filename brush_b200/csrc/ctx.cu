@@ -81,6 +81,8 @@ bsx_status check_device_error(bsx_ctx* ctx) {
     cudaMemsetAsync(ctx->d_err, 0, sizeof(int), ctx->stream);
     if (code == kDevLookbackTimeout)
         return fail(ctx, BSX_ERR_DEVICE_TIMEOUT, "a bounded device-side lookback wait expired");
+    if (code == kDevPeerTimeout)
+        return fail(ctx, BSX_ERR_DEVICE_TIMEOUT, "a data-parallel peer did not reach the exchange within the timeout");
     return fail(ctx, BSX_ERR_CAPACITY, "device-side range check failed (code " + std::to_string(code) + ")");
 }
 

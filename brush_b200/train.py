@@ -2,10 +2,11 @@
 (crates/brush-train/src/train.rs:619-1182).
 
 One step: backward-pass render -> fused SSIM+L1 loss and its gradient ->
-raster backward -> projection backward -> (data parallel: NCCL all-reduce of
-the flat gradient buffer) -> fused AdamScaled over transforms / SH / opacity
-with the reference's learning-rate table (train.rs:964-1051) -> refine
-statistics (stats.rs:111-121).
+raster backward -> projection backward -> fused AdamScaled over transforms /
+SH / opacity with the reference's learning-rate table (train.rs:964-1051) ->
+refine statistics (stats.rs:111-121). With several ranks (one view each) the
+gradient exchange and Adam are one peer-memory kernel (brush_b200.peer), or
+NCCL collectives around the fused Adam (brush_b200.dist).
 
 Not applied: the reference's random mean-noise injection after Adam
 (train.rs:1095-1169); it draws from a non-reproducible RNG stream and is
@@ -75,11 +76,19 @@ class RefineRecord:
 
 class SplatTrainer:
     def __init__(self, config: TrainConfig, splats: Splats, process_group=None, gather_stats: bool = True,
-                 shard_optimizer: bool = True):
+                 shard_optimizer: bool = True, exchange: str = "peer"):
         self.config = config
-        # With several ranks and N divisible by the world size, each rank keeps
-        # Adam state for, and updates, only its row shard of the splats:
-        # reduce-scatter gradients -> fused Adam on the shard -> all-gather.
+        # Data-parallel exchange with several ranks:
+        #   "peer": one fused kernel over peer memory (brush_b200.peer); the
+        #           splat parameters then live in the exchange region and the
+        #           tensors of ``splats`` are rebound to it.
+        #   "nccl": with shard_optimizer and N divisible by the world size,
+        #           reduce-scatter gradients -> fused Adam on this rank's row
+        #           shard -> all-gather; otherwise all-reduce -> full Adam.
+        if exchange not in ("peer", "nccl"):
+            raise ValueError("exchange must be 'peer' or 'nccl'")
+        self.exchange = exchange
+        self.peer = None
         self.shard_optimizer = shard_optimizer
         self.adam = AdamScaled(epsilon=1e-15)
         self.step_count = 0
@@ -97,21 +106,34 @@ class SplatTrainer:
         n, c = splats.num_splats, splats.sh_coeffs_per_splat
         dev = splats.transforms.device
         self.n, self.c = n, c
-        # One flat gradient buffer so data-parallel ranks all-reduce once per step.
-        self.flat_grad = torch.empty(n * (10 + 3 * c + 1), device=dev)
-        g = self.flat_grad
-        self.grads = SplatGrads(
-            v_transforms=g[: n * 10].view(n, 10),
-            v_coeffs=g[n * 10: n * (10 + 3 * c)].view(n, c, 3),
-            v_raw_opac=g[n * (10 + 3 * c):].view(n),
-            v_refine_weight=torch.empty(n, device=dev),
-        )
+        use_peer = self.world > 1 and self.exchange == "peer"
+        if not use_peer:
+            # One flat gradient buffer so data-parallel ranks all-reduce once per step.
+            self.flat_grad = torch.empty(n * (10 + 3 * c + 1), device=dev)
+            g = self.flat_grad
+            self.grads = SplatGrads(
+                v_transforms=g[: n * 10].view(n, 10),
+                v_coeffs=g[n * 10: n * (10 + 3 * c)].view(n, c, 3),
+                v_raw_opac=g[n * (10 + 3 * c):].view(n),
+                v_refine_weight=torch.empty(n, device=dev),
+            )
         self.v_combined = torch.empty((max(n, 1), _lib.BSX_GRAD_STRIDE), device=dev)
         self.loss = torch.empty(1, device=dev)
         self.v_output = None
         self.record = RefineRecord.new(n, dev) if self.gather_stats else None
         self.groups = None
-        self.sharded = self.shard_optimizer and self.world > 1 and n % self.world == 0
+        old, self.peer = self.peer, None
+        if use_peer:
+            from .peer import PeerExchange
+
+            self.peer = PeerExchange(n, c, dev.index, self.pg)
+            self.peer.load(splats.transforms, splats.sh_coeffs, splats.raw_opacities)
+            splats.transforms, splats.sh_coeffs, splats.raw_opacities = self.peer.params
+            self.grads = SplatGrads(*self.peer.grads, v_refine_weight=self.peer.refine)
+            self.flat_grad = None
+        if old is not None:
+            old.close()
+        self.sharded = (self.peer is None and self.shard_optimizer and self.world > 1 and n % self.world == 0)
         if self.sharded:
             self.rank = torch.distributed.get_rank(self.pg)
             self.row0, self.row1 = row_shard(n, self.world, self.rank)
@@ -148,6 +170,14 @@ class SplatTrainer:
         rasterize_bwd(self.v_output, compute_refine_weight, self.v_combined)
         project_bwd(self.v_combined, self.n, self.c, self.grads)
         n, c = self.n, self.c
+        if self.peer is not None:
+            lr_t, tscale, lr_sh, sh_cols, lr_op, lr_mean = self._lr_table()
+            with_refine = self.record is not None and compute_refine_weight
+            self.peer.adam_step(self.adam, [(lr_t, tscale, False), (lr_sh, sh_cols, True), (lr_op, None, False)],
+                                1.0 / self.world, with_refine)
+            if with_refine:
+                self.record.gather_stats(self.grads.v_refine_weight, out.aux.visible, out.aux.max_radius)
+            return TrainStepStats(out.aux.num_visible, out.aux.num_intersections, self.loss, lr_mean)
         full_params = (splats.transforms, splats.sh_coeffs.view(n, 3 * c), splats.raw_opacities.view(n, 1))
         full_grads = (self.grads.v_transforms, self.grads.v_coeffs.view(n, 3 * c), self.grads.v_raw_opac.view(n, 1))
         if self.sharded:
@@ -180,3 +210,9 @@ class SplatTrainer:
             if compute_refine_weight:
                 self.record.gather_stats(self.grads.v_refine_weight, out.aux.visible, out.aux.max_radius)
         return TrainStepStats(out.aux.num_visible, out.aux.num_intersections, self.loss, lr_mean)
+
+    def close(self) -> None:
+        """Release the data-parallel exchange region (collective over the process group)."""
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None

@@ -215,6 +215,58 @@ BSX_API bsx_status bsx_loss_fused(bsx_ctx* ctx, const float* d_image_hwc4, const
 BSX_API bsx_status bsx_adam_step(bsx_ctx* ctx, const bsx_adam_group* groups, int32_t num_groups,
                          const bsx_adam_cfg* cfg);
 
+/* ---- data-parallel exchange over peer memory (one process per GPU) ------
+ * The reference trains on one device (crates/brush-process/src/train_stream.rs:449-465,
+ * crates/brush-train/src/train.rs:619-1182); these entry points are this
+ * library's addition for N GPUs of one node, where each rank trains its own
+ * view and the update uses the mean of the ranks' gradients.
+ *
+ * bsx_peer_alloc exports device memory that the other ranks' processes map
+ * with bsx_peer_open (CUDA IPC; loads and stores then cross NVLink). The
+ * handle is an opaque blob of BSX_PEER_HANDLE_BYTES to pass between processes.
+ * An exporter frees its buffer only after every importer has closed it. */
+#define BSX_MAX_RANKS 8
+#define BSX_PEER_HANDLE_BYTES 64
+#define BSX_DP_FLAG_WORDS 64
+BSX_API bsx_status bsx_peer_alloc(bsx_ctx* ctx, uint64_t bytes, void** d_ptr, uint8_t* handle_out);
+BSX_API bsx_status bsx_peer_free(bsx_ctx* ctx, void* d_ptr);
+BSX_API bsx_status bsx_peer_open(bsx_ctx* ctx, const uint8_t* handle, void** d_ptr);
+BSX_API bsx_status bsx_peer_close(bsx_ctx* ctx, void* d_ptr);
+
+typedef struct bsx_dp_group {
+    float* d_param[BSX_MAX_RANKS];       /* every rank's copy of the parameter [rows, cols] (own + mapped) */
+    const float* d_grad[BSX_MAX_RANKS];  /* every rank's gradient [rows, cols] (own + mapped) */
+    float* d_m;                          /* this rank's first moment for its shard rows [shard_rows, cols] */
+    float* d_v;                          /* [shard_rows, cols], or [shard_rows] when reduce_moment_2 */
+    uint32_t rows, cols;                 /* full parameter shape; cols <= 80 */
+    float lr;
+    const float* h_col_scale;            /* may be NULL (all ones); at most 80 entries */
+    int32_t reduce_moment_2;
+} bsx_dp_group;
+
+typedef struct bsx_dp_exchange {
+    int32_t rank, world;                 /* 1 <= world <= BSX_MAX_RANKS */
+    uint32_t* d_flags[BSX_MAX_RANKS];    /* every rank's BSX_DP_FLAG_WORDS words, zeroed before the first call */
+    float* d_refine[BSX_MAX_RANKS];      /* optional [refine_rows] per rank, MAX-combined in place (NULL: none) */
+    uint32_t refine_rows;
+    uint32_t epoch;                      /* 1, 2, 3, ... one per call, equal on every rank */
+    uint64_t timeout_ns;                 /* bound on each wait for the other ranks (0: 5 s) */
+} bsx_dp_exchange;
+
+/* One kernel in place of "all-reduce the gradients, then bsx_adam_step": rank
+ * r owns rows [rows*r/world, rows*(r+1)/world) of every group. After every
+ * rank has arrived (a flag barrier), it sums its rows' gradients over all
+ * ranks in rank order (peer loads), scales by cfg->grad_scale, applies
+ * AdamScaled with its shard's moments, and stores the new rows into every
+ * rank's parameters (peer stores); refine rows take the MAX over ranks the
+ * same way. The launch completes only after every rank has finished reading
+ * and writing, so the next step may overwrite gradients and read parameters.
+ * Every rank calls it with the same epoch, groups and cfg; the result is
+ * bit-identical on every rank. A wait that exceeds timeout_ns ends the launch
+ * and the next bsx_sync / render readback returns BSX_ERR_DEVICE_TIMEOUT. */
+BSX_API bsx_status bsx_dp_adam_step(bsx_ctx* ctx, const bsx_dp_exchange* ex, const bsx_dp_group* groups,
+                                    int32_t num_groups, const bsx_adam_cfg* cfg);
+
 /* ---- primitives: brush-sort / brush-prefix-sum / get_tile_offsets ---- */
 /* Stable argsort by key & mask(bits rounded up to a multiple of 4), as
  * crates/brush-sort/src/lib.rs:16-129. Inputs are left untouched. */

@@ -1,9 +1,10 @@
-"""Data-parallel training step on 2 GPUs over NCCL (skipped with fewer GPUs).
+"""Data-parallel training step on 2 GPUs (skipped with fewer GPUs), and the
+peer-exchange kernel's single-GPU forms.
 
-Each rank trains its own view; after one step (reduce-scatter -> sharded fused
-Adam -> all-gather, and the all-reduce variant) every rank holds identical
-splats, equal to one single-GPU Adam step on the mean of the two views'
-gradients computed with the same library.
+Each rank trains its own view; after one step (the fused peer-memory exchange,
+NCCL reduce-scatter -> sharded fused Adam -> all-gather, or NCCL all-reduce ->
+fused Adam) every rank holds identical splats, equal to one single-GPU Adam
+step on the mean of the two views' gradients computed with the same library.
 """
 import datetime
 import multiprocessing as mp
@@ -36,7 +37,7 @@ def _scene(dev):
     return splats, cams, (w, h), gts
 
 
-def _worker(rank, world, port, q, shard):
+def _worker(rank, world, port, q, mode):
     sys.path.insert(0, str(ROOT))
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     import brush_b200 as bsx
@@ -49,12 +50,15 @@ def _worker(rank, world, port, q, shard):
     try:
         splats, cams, size, gts = _scene(dev)
         tr = bsx.SplatTrainer(bsx.TrainConfig(uniform_lr=1e-3), splats, process_group=torch.distributed.group.WORLD,
-                              gather_stats=False, shard_optimizer=shard)
+                              gather_stats=False, shard_optimizer=mode == "sharded_adam",
+                              exchange="peer" if mode == "peer" else "nccl")
         v = view_for(0, rank, world, len(cams))
         tr.step(cams[v], size, gts[v], splats)
         torch.cuda.synchronize()
+        tr.peer and tr.peer.ctx.sync()
         q.put((rank, "ok", splats.transforms.cpu().numpy(), splats.sh_coeffs.cpu().numpy(),
-               splats.raw_opacities.cpu().numpy(), tr.sharded))
+               splats.raw_opacities.cpu().numpy(), (tr.peer is not None, tr.sharded)))
+        tr.close()
     except Exception as e:  # noqa: BLE001
         q.put((rank, "error", repr(e)))
     finally:
@@ -86,21 +90,21 @@ def _single_gpu_mean_of_views():
     return splats.transforms.cpu().numpy(), splats.sh_coeffs.cpu().numpy(), splats.raw_opacities.cpu().numpy()
 
 
-@pytest.mark.parametrize("shard", [True, False], ids=["sharded_adam", "allreduce"])
-def test_two_gpu_step_matches_mean_of_views(cuda, shard):
+@pytest.mark.parametrize("mode", ["peer", "sharded_adam", "allreduce"])
+def test_two_gpu_step_matches_mean_of_views(cuda, mode):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, shard)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, mode)) for r in range(2)]
     for p in procs:
         p.start()
     res = sorted([q.get(timeout=300) for _ in range(2)], key=lambda r: r[0])
     for p in procs:
         p.join(timeout=60)
     assert all(r[1] == "ok" for r in res), res
-    assert res[0][5] == shard
+    assert res[0][5] == (mode == "peer", mode == "sharded_adam")
     for k in (2, 3, 4):
         np.testing.assert_array_equal(res[0][k], res[1][k])
     ref = _single_gpu_mean_of_views()
@@ -108,3 +112,95 @@ def test_two_gpu_step_matches_mean_of_views(cuda, shard):
         # Adam's first step moves each element by ~lr; differences come only from
         # the order of float atomics in the raster backward.
         assert np.abs(res[0][k] - r).max() <= 1e-4
+
+
+def _dp_call(lib, ctx, groups, world, rank, flags, epoch, timeout_ns, step=1, grad_scale=1.0):
+    import ctypes as C
+
+    from brush_b200 import _lib
+
+    ex = _lib.DpExchange()
+    ex.rank, ex.world = rank, world
+    for q in range(world):
+        ex.d_flags[q] = flags[q].data_ptr()
+    ex.refine_rows = 0
+    ex.epoch = epoch
+    ex.timeout_ns = timeout_ns
+    arr = (_lib.DpGroup * len(groups))()
+    for i, g in enumerate(groups):
+        for q in range(world):
+            arr[i].d_param[q] = g["param"][q].data_ptr()
+            arr[i].d_grad[q] = g["grad"][q].data_ptr()
+        arr[i].d_m = g["m"].data_ptr()
+        arr[i].d_v = g["v"].data_ptr()
+        arr[i].rows, arr[i].cols = g["param"][0].shape
+        arr[i].lr = g["lr"]
+        arr[i].h_col_scale = None
+        arr[i].reduce_moment_2 = int(g["reduce"])
+    cfg = _lib.AdamCfg(beta_1=0.9, beta_2=0.999, epsilon=1e-15, step=step, grad_scale=grad_scale)
+    return lib.bsx_dp_adam_step(ctx.handle, C.byref(ex), arr, len(groups), C.byref(cfg))
+
+
+def test_dp_kernel_world_one_equals_adam(cuda):
+    """With one rank the exchange kernel is the fused Adam: bit-equal parameters and moments."""
+    from brush_b200 import _lib
+    from brush_b200._context import context
+    from brush_b200.adam import AdamGroup, AdamScaled
+
+    rng = np.random.default_rng(5)
+    n = 30011
+    shapes = [(n, 10, False), (n, 48, True), (n, 1, False)]
+    ctx = context(0)
+    lib = _lib.lib()
+    flags = [torch.zeros(_lib.BSX_DP_FLAG_WORDS, dtype=torch.int32, device="cuda")]
+    p0 = [rng.normal(0, 1, (r, c)).astype(np.float32) for r, c, _ in shapes]
+    ref = [AdamGroup(torch.from_numpy(p.copy()).cuda(), None, 1e-3, reduce_moment_2=red)
+           for p, (_, _, red) in zip(p0, shapes)]
+    dp = [dict(param=[torch.from_numpy(p.copy()).cuda()], grad=[None], m=torch.zeros(r, c, device="cuda"),
+               v=torch.zeros((r,) if red else (r, c), device="cuda"), lr=1e-3, reduce=red)
+          for p, (r, c, red) in zip(p0, shapes)]
+    opt = AdamScaled()
+    for step in (1, 2, 3):
+        grads = [torch.from_numpy(rng.normal(0, 1, p.shape).astype(np.float32)).cuda() for p in p0]
+        for g, gr in zip(ref, grads):
+            g.grad = gr
+        opt.step(ref, grad_scale=0.5)
+        for d, gr in zip(dp, grads):
+            d["grad"] = [gr]
+        ctx.check(_dp_call(lib, ctx, dp, 1, 0, flags, step, int(1e9), step=step, grad_scale=0.5))
+    ctx.sync()
+    for g, d in zip(ref, dp):
+        np.testing.assert_array_equal(g.param.cpu().numpy(), d["param"][0].cpu().numpy())
+        np.testing.assert_array_equal(g.m.cpu().numpy(), d["m"].cpu().numpy())
+        np.testing.assert_array_equal(g.v.cpu().numpy(), d["v"].cpu().numpy())
+
+
+def test_dp_kernel_times_out_when_a_rank_never_arrives(cuda):
+    """Rank 0 of a 2-rank exchange whose partner never launches: the bounded wait
+    expires, the launch ends, and the host reads BSX_ERR_DEVICE_TIMEOUT."""
+    import time
+
+    from brush_b200 import _lib
+    from brush_b200._context import context
+
+    ctx = context(0)
+    lib = _lib.lib()
+    n, c = 4096, 10
+    # the absent rank's buffers are ordinary local memory that nothing signals
+    flags = [torch.zeros(_lib.BSX_DP_FLAG_WORDS, dtype=torch.int32, device="cuda") for _ in range(2)]
+    g = dict(param=[torch.zeros(n, c, device="cuda") for _ in range(2)],
+             grad=[torch.ones(n, c, device="cuda") for _ in range(2)],
+             m=torch.zeros(n // 2, c, device="cuda"), v=torch.zeros(n // 2, c, device="cuda"), lr=1e-3, reduce=False)
+    t0 = time.perf_counter()
+    ctx.check(_dp_call(lib, ctx, [g], 2, 0, flags, 1, int(2e8)))
+    with pytest.raises(_lib.BsxError) as ei:
+        ctx.sync()
+    dt = time.perf_counter() - t0
+    assert ei.value.status == 4  # BSX_ERR_DEVICE_TIMEOUT
+    assert dt < 30.0
+    # the context stays usable: the error word was cleared and a world-1 call succeeds
+    g1 = dict(param=[g["param"][0]], grad=[g["grad"][0]], m=torch.zeros(n, c, device="cuda"),
+              v=torch.zeros(n, c, device="cuda"), lr=1e-3, reduce=False)
+    ctx.check(_dp_call(lib, ctx, [g1], 1, 0, [torch.zeros(64, dtype=torch.int32, device="cuda")], 1, int(1e9)))
+    ctx.sync()
+    assert torch.isfinite(g["param"][0]).all()
