@@ -90,15 +90,22 @@ def test_loss_alpha_channel(cuda, orc):
     assert _rel(d, orc.loss_bwd(pred, gt, oc, dl)) <= 1e-5
 
 
-def test_fused_loss_matches_mean_and_gradient(cuda, orc):
+@pytest.mark.parametrize("h,w,cfg", [
+    (96, 160, {}),
+    (75, 131, {}),
+    (33, 70, {"composite_bg": (0.2, 0.5, 0.9), "mask": True}),
+    (40, 47, {"l1_weight": 1.0, "ssim_weight": 0.0}),
+    (1, 1, {}),
+], ids=["aligned", "ragged", "composite_mask", "l1_only", "single_pixel"])
+def test_fused_loss_matches_mean_and_gradient(cuda, orc, h, w, cfg):
     from brush_b200.loss import ImageLossConfig, image_loss_fused
 
     rng = np.random.default_rng(3)
-    h, w = 96, 160
     img = rng.uniform(0, 1, (h, w, 4)).astype(np.float32)
     gt = rng.integers(0, 2**32, (h, w), dtype=np.uint64).astype(np.uint32).view(np.int32)
-    loss, vout = image_loss_fused(torch.from_numpy(img).cuda(), torch.from_numpy(gt).cuda(), ImageLossConfig())
-    oc = orc.loss_cfg(0.8, -0.2)
+    c = ImageLossConfig(**cfg)
+    loss, vout = image_loss_fused(torch.from_numpy(img).cuda(), torch.from_numpy(gt).cuda(), c)
+    oc = orc.loss_cfg(c.l1_weight, c.ssim_weight, c.composite_bg, c.mask)
     chw = np.ascontiguousarray(img[..., :3].transpose(2, 0, 1))
     ref_map = orc.loss_fwd(chw, gt, oc)
     assert abs(float(loss.item()) - float(ref_map.astype(np.float64).mean())) <= 1e-5 * abs(ref_map.mean()) + 1e-7
