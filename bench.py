@@ -100,9 +100,11 @@ class ClockSampler:
 # Algorithmic bytes moved by each kernel per launch (fp32 = 4 B). N splats,
 # V visible, M intersections, Mp intersections surviving the forward early-out,
 # P pixels, T tiles, C SH coefficients per splat.
-def kernel_bytes(name, N, V, M, Mp, P, T, C):
+def kernel_bytes(name, N, V, M, Mp, P, T, C, W=1):
+    row = 4 * (11 + 3 * C)  # bytes of one splat's parameters (or gradients)
     table = {
-        "project_fwd_kernel": 44 * N + 8 * N + V * (12 * C + 48 + 8),
+        "project_fwd_kernel": 44 * N + 8 * N + N // 8 + V * (12 * C + 48 + 4),
+        "compact_visible_kernel": 4 * N + N // 8 + 12 * V,
         "sort_hist_kernel": 4 * V,  # depth sort; the tile sort adds 4 M (below)
         "sort_pass_kernel": 16 * V,
         "scan_kernel": 12 * V,
@@ -114,6 +116,8 @@ def kernel_bytes(name, N, V, M, Mp, P, T, C):
         "raster_bwd_kernel": 32 * P + 52 * Mp + 48 * V,
         "project_bwd_kernel": 48 * N + V * (44 + 12 * C) + N * (48 + 12 * C),
         "adam_kernel": (316 + 60 * C) * N,
+        # NVLink bytes per rank: peer gradient rows in + parameter rows out
+        "dp_adam_kernel": 2 * (W - 1) * (N // W) * row if W > 1 else 0,
     }
     return table.get(name, 0)
 
@@ -224,7 +228,7 @@ def run_ours(args, rank, world, local_rank):
     kernels = {}
     for name, (tot, cnt) in prof.items():
         avg_ms = tot / max(cnt, 1)
-        b = kernel_bytes(name, N, V, M, Mp, P, T, C)
+        b = kernel_bytes(name, N, V, M, Mp, P, T, C, world)
         if name in ("sort_pass_kernel", "sort_hist_kernel"):
             # two sorts per step: V depth keys (4 passes) and M tile keys (2 passes at 1080p)
             per_step = 4 * 16 * V + 2 * 16 * M if name == "sort_pass_kernel" else 4 * V + 4 * M

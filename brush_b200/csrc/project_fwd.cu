@@ -1,13 +1,17 @@
-// project_fwd.cu - fused cull / project / SH colour / visible compaction.
+// project_fwd.cu - fused cull / project / SH colour, then visible compaction.
 //
-// One thread per splat, 256 splats per block. Restates, in one pass,
-// project_forward_kernel (crates/brush-render/src/kernels/project_forward.rs:20-144)
+// project_fwd_kernel: one thread per splat, 256 splats per block. Restates, in
+// one pass, project_forward_kernel (crates/brush-render/src/kernels/project_forward.rs:20-144)
 // and project_visible_kernel (kernels/project_visible.rs:22-89): the cull
 // predicates, the EWA covariance, the StopThePop per-tile count, and the SH
-// colour of every surviving splat. Where the reference appends visible ids
-// with an atomic counter (order depends on scheduling), blocks here take
-// tickets and compact with a decoupled look-back, so the visible list is in
-// global-id order on every run.
+// colour of every surviving splat. No block-wide barrier: every block streams
+// independently.
+//
+// compact_visible_kernel: where the reference appends visible ids with an
+// atomic counter (order depends on scheduling), blocks of 1024 splats here
+// take tickets and compact with a decoupled look-back over the projection's
+// per-warp visibility masks, so the visible list is in global-id order on
+// every run; the same pass sums the intersection counts.
 //
 // Outputs (global-id indexed unless noted):
 //   projected[N,12]  rows {x, y, conic00, conic01, conic11, opacity, r, g, b,
@@ -16,6 +20,7 @@
 //   max_radius[N]    max(ex/W, ey/H) (0 when culled)
 //   vis_gid[V], depth_key[V]  compacted visible ids and depth bits, id order
 //   scalars[0] = V, scalars[1] = total intersections (u32, wraps as the reference)
+// Scratch: vis_mask[ceil(N/32)] (bit per splat), depth_dense[N] (visible only).
 #include "lookback.cuh"
 #include "sh.cuh"
 
@@ -37,6 +42,15 @@ struct ProjArgs {
     float* projected;
     uint32_t* counts;
     float* max_radius;
+    uint32_t* vis_mask;
+    uint32_t* depth_dense;
+};
+
+struct CompactArgs {
+    const uint32_t* vis_mask;
+    const uint32_t* depth_dense;
+    const uint32_t* counts;
+    uint32_t n;
     uint32_t* vis_gid;
     uint32_t* depth_key;
     uint32_t* scalars;
@@ -46,15 +60,8 @@ struct ProjArgs {
 };
 
 template <int DEG>
-__global__ void __launch_bounds__(kProjThreads) project_fwd_kernel(const ProjArgs a) {
-    __shared__ uint32_t s_tile;
-    __shared__ uint32_t s_warp_vis[kProjThreads / 32];
-    __shared__ uint32_t s_warp_hits[kProjThreads / 32];
-    __shared__ uint32_t s_base;
-    if (threadIdx.x == 0) s_tile = atomicAdd(a.ticket, 1u);
-    __syncthreads();
-    const uint32_t tile = s_tile;
-    const uint32_t g = tile * kProjThreads + threadIdx.x;
+__global__ void __launch_bounds__(kProjThreads) project_fwd_kernel(const __grid_constant__ ProjArgs a) {
+    const uint32_t g = blockIdx.x * kProjThreads + threadIdx.x;
     const Uni& u = a.u;
 
     bool visible = false;
@@ -136,45 +143,80 @@ __global__ void __launch_bounds__(kProjThreads) project_fwd_kernel(const ProjArg
         a.max_radius[g] = radius;
     }
 
-    // Block-level compaction of visible ids + intersection total.
+    const uint32_t vmask = __ballot_sync(0xffffffffu, visible);
+    if ((threadIdx.x & 31) == 0 && g < a.n) a.vis_mask[g >> 5] = vmask;
+    if (visible) a.depth_dense[g] = bsx_f32_to_bits(depth);
+}
+
+constexpr int kCompactThreads = 256;
+constexpr int kCompactPer = 4;  // splats per thread
+constexpr uint32_t kCompactTile = kCompactThreads * kCompactPer;
+
+// Ordered compaction of the visible ids + intersection total.
+__global__ void __launch_bounds__(kCompactThreads) compact_visible_kernel(const __grid_constant__ CompactArgs a) {
+    __shared__ uint32_t s_tile;
+    __shared__ uint32_t s_warp_vis[kCompactThreads / 32];
+    __shared__ uint32_t s_warp_hits[kCompactThreads / 32];
+    __shared__ uint32_t s_base;
+    if (threadIdx.x == 0) s_tile = atomicAdd(a.ticket, 1u);
+    __syncthreads();
+    const uint32_t tile = s_tile;
+    const uint32_t g0 = tile * kCompactTile + threadIdx.x * kCompactPer;
+    // 4 consecutive splats never straddle a 32-bit mask word
+    const uint32_t word = g0 < a.n ? __ldg(a.vis_mask + (g0 >> 5)) : 0u;
+    uint32_t bits = (word >> (g0 & 31)) & 0xfu;
+    uint32_t hits = 0;
+#pragma unroll
+    for (int k = 0; k < kCompactPer; ++k) {
+        if (g0 + k < a.n) hits += __ldg(a.counts + g0 + k);
+        else bits &= ~(1u << k);
+    }
+    const uint32_t nvis = __popc(bits);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    uint32_t vmask = __ballot_sync(0xffffffffu, visible);
+    uint32_t inc = nvis;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t t = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += t;
+    }
     uint32_t whits = hits;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) whits += __shfl_xor_sync(0xffffffffu, whits, o);
-    if (lane == 0) {
-        s_warp_vis[warp] = __popc(vmask);
-        s_warp_hits[warp] = whits;
-    }
+    if (lane == 31) s_warp_vis[warp] = inc;
+    if (lane == 0) s_warp_hits[warp] = whits;
     __syncthreads();
     if (warp == 0) {
-        uint32_t wv = lane < kProjThreads / 32 ? s_warp_vis[lane] : 0u;
-        uint32_t wh = lane < kProjThreads / 32 ? s_warp_hits[lane] : 0u;
-        uint32_t inc = wv;
+        const uint32_t wv = lane < kCompactThreads / 32 ? s_warp_vis[lane] : 0u;
+        uint32_t wh = lane < kCompactThreads / 32 ? s_warp_hits[lane] : 0u;
+        uint32_t winc = wv;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
-            uint32_t tv = __shfl_up_sync(0xffffffffu, inc, o);
-            if (lane >= o) inc += tv;
+            const uint32_t t = __shfl_up_sync(0xffffffffu, winc, o);
+            if (lane >= o) winc += t;
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) wh += __shfl_xor_sync(0xffffffffu, wh, o);
-        uint32_t block_vis = __shfl_sync(0xffffffffu, inc, 31);
-        if (lane < kProjThreads / 32) s_warp_vis[lane] = inc - wv;
-        uint32_t prefix = lookback_publish(a.status, tile, block_vis, a.err);
+        const uint32_t block_vis = __shfl_sync(0xffffffffu, winc, 31);
+        if (lane < kCompactThreads / 32) s_warp_vis[lane] = winc - wv;
+        const uint32_t prefix = lookback_publish(a.status, tile, block_vis, a.err);
         if (lane == 0) {
             s_base = prefix;
             if (wh) atomicAdd(a.scalars + 1, wh);
-            if ((uint64_t)(tile + 1) * kProjThreads >= a.n) a.scalars[0] = prefix + block_vis;
+            if ((uint64_t)(tile + 1) * kCompactTile >= a.n) a.scalars[0] = prefix + block_vis;
         }
     }
     __syncthreads();
-    if (visible) {
-        uint32_t pos = s_base + s_warp_vis[warp] + __popc(vmask & ((1u << lane) - 1u));
-        if (pos < a.n) {
-            a.vis_gid[pos] = g;
-            a.depth_key[pos] = bsx_f32_to_bits(depth);
-        } else {
-            set_error(a.err, kDevOutOfRange);
+    uint32_t pos = s_base + s_warp_vis[warp] + inc - nvis;
+#pragma unroll
+    for (int k = 0; k < kCompactPer; ++k) {
+        if (bits & (1u << k)) {
+            if (pos < a.n) {
+                a.vis_gid[pos] = g0 + k;
+                a.depth_key[pos] = __ldg(a.depth_dense + g0 + k);
+            } else {
+                set_error(a.err, kDevOutOfRange);
+            }
+            ++pos;
         }
     }
 }
@@ -184,16 +226,19 @@ __global__ void __launch_bounds__(kProjThreads) project_fwd_kernel(const ProjArg
 bsx_status launch_project_fwd(bsx_ctx* ctx, const bsx_project_uniforms& uni, const float* transforms,
                               const float* sh, const float* raw_opac, uint32_t n, uint32_t coeffs, int degree,
                               int mip, float* projected, uint32_t* counts, float* max_radius, uint32_t* vis_gid,
-                              uint32_t* depth_key, uint32_t* scalars) {
-    const uint32_t tiles = (n + kProjThreads - 1) / kProjThreads;
+                              uint32_t* depth_key, uint32_t* scalars, uint32_t* vis_mask, uint32_t* depth_dense) {
+    if (degree < 0 || degree > 4) return fail(ctx, BSX_ERR_SHAPE, "sh coefficient count must be (degree+1)^2 with degree <= 4");
+    const uint32_t blocks = (n + kProjThreads - 1) / kProjThreads;
+    const uint32_t tiles = (n + kCompactTile - 1) / kCompactTile;
     bsx_status s = ensure(ctx, ctx->scan_status, scan_status_words(tiles) * sizeof(uint64_t));
     if (s != BSX_OK) return s;
     uint64_t* status = ctx->scan_status.as<uint64_t>();
     s = check_cuda(ctx, cudaMemsetAsync(status, 0, scan_status_words(tiles) * sizeof(uint64_t), ctx->stream),
-                   "memset projection status");
+                   "memset compaction status");
     if (s != BSX_OK) return s;
     s = check_cuda(ctx, cudaMemsetAsync(scalars, 0, 2 * sizeof(uint32_t), ctx->stream), "memset scalars");
     if (s != BSX_OK) return s;
+    if (n == 0) return BSX_OK;
     ProjArgs a;
     a.transforms = transforms;
     a.sh = sh;
@@ -206,23 +251,32 @@ bsx_status launch_project_fwd(bsx_ctx* ctx, const bsx_project_uniforms& uni, con
     a.projected = projected;
     a.counts = counts;
     a.max_radius = max_radius;
-    a.vis_gid = vis_gid;
-    a.depth_key = depth_key;
-    a.scalars = scalars;
-    a.status = status;
-    a.ticket = reinterpret_cast<uint32_t*>(status + tiles);
-    a.err = ctx->d_err;
-    if (degree < 0 || degree > 4) return fail(ctx, BSX_ERR_SHAPE, "sh coefficient count must be (degree+1)^2 with degree <= 4");
+    a.vis_mask = vis_mask;
+    a.depth_dense = depth_dense;
     prof_begin(ctx);
     switch (degree) {
-        case 0: project_fwd_kernel<0><<<tiles, kProjThreads, 0, ctx->stream>>>(a); break;
-        case 1: project_fwd_kernel<1><<<tiles, kProjThreads, 0, ctx->stream>>>(a); break;
-        case 2: project_fwd_kernel<2><<<tiles, kProjThreads, 0, ctx->stream>>>(a); break;
-        case 3: project_fwd_kernel<3><<<tiles, kProjThreads, 0, ctx->stream>>>(a); break;
-        case 4: project_fwd_kernel<4><<<tiles, kProjThreads, 0, ctx->stream>>>(a); break;
-        default: return fail(ctx, BSX_ERR_SHAPE, "sh coefficient count must be (degree+1)^2 with degree <= 4");
+        case 0: project_fwd_kernel<0><<<blocks, kProjThreads, 0, ctx->stream>>>(a); break;
+        case 1: project_fwd_kernel<1><<<blocks, kProjThreads, 0, ctx->stream>>>(a); break;
+        case 2: project_fwd_kernel<2><<<blocks, kProjThreads, 0, ctx->stream>>>(a); break;
+        case 3: project_fwd_kernel<3><<<blocks, kProjThreads, 0, ctx->stream>>>(a); break;
+        default: project_fwd_kernel<4><<<blocks, kProjThreads, 0, ctx->stream>>>(a); break;
     }
-    return post_launch(ctx, "project_fwd_kernel");
+    s = post_launch(ctx, "project_fwd_kernel");
+    if (s != BSX_OK) return s;
+    CompactArgs c;
+    c.vis_mask = vis_mask;
+    c.depth_dense = depth_dense;
+    c.counts = counts;
+    c.n = n;
+    c.vis_gid = vis_gid;
+    c.depth_key = depth_key;
+    c.scalars = scalars;
+    c.status = status;
+    c.ticket = reinterpret_cast<uint32_t*>(status + tiles);
+    c.err = ctx->d_err;
+    prof_begin(ctx);
+    compact_visible_kernel<<<tiles, kCompactThreads, 0, ctx->stream>>>(c);
+    return post_launch(ctx, "compact_visible_kernel");
 }
 
 }  // namespace bsx

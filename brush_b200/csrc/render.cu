@@ -17,7 +17,7 @@ namespace bsx {
 bsx_status launch_project_fwd(bsx_ctx* ctx, const bsx_project_uniforms& uni, const float* transforms,
                               const float* sh, const float* raw_opac, uint32_t n, uint32_t coeffs, int degree,
                               int mip, float* projected, uint32_t* counts, float* max_radius, uint32_t* vis_gid,
-                              uint32_t* depth_key, uint32_t* scalars);
+                              uint32_t* depth_key, uint32_t* scalars, uint32_t* vis_mask, uint32_t* depth_dense);
 bsx_status launch_emit(bsx_ctx* ctx, const float* projected, const uint32_t* depth_order, const uint32_t* cum,
                        uint32_t num_visible, uint32_t tbw, uint32_t tbh, uint32_t* tile_out, uint32_t* gid_out,
                        uint32_t num_isect);
@@ -96,7 +96,9 @@ bsx_status bsx_render_fwd(bsx_ctx* ctx, const bsx_camera* cam, uint32_t w, uint3
     if (n) {
         BSX_TRY(launch_project_fwd(ctx, uni, d_transforms, d_sh, d_raw_opac, n, coeffs, degree, mip,
                                    ctx->projected.as<float>(), ctx->counts.as<uint32_t>(), ctx->max_radius.as<float>(),
-                                   ctx->vis_gid.as<uint32_t>(), ctx->depth_keys.as<uint32_t>(), scalars));
+                                   ctx->vis_gid.as<uint32_t>(), ctx->depth_keys.as<uint32_t>(), scalars,
+                                   // scratch: both are rewritten later in the render (depth sort, count scan)
+                                   ctx->depth_order.as<uint32_t>(), ctx->cum.as<uint32_t>()));
         // The one host synchronisation of the render (render.rs:308-330).
         BSX_TRY(check_cuda(ctx, cudaMemcpyAsync(ctx->h_pinned, scalars, 8, cudaMemcpyDeviceToHost, ctx->stream),
                            "count readback"));
