@@ -2,17 +2,18 @@
 //
 // Restates rasterize_backwards_kernel
 // (crates/brush-render-bwd/src/kernels/rasterize_backwards.rs:79-443) with a
-// pixel-parallel schedule: one 256-thread block per 16x16 tile, one pixel per
-// thread in the forward's Morton order. Each thread replays its pixel front to
-// back exactly as the forward did (same float operations, so T and every
-// accept / early-out decision match the forward bit-for-bit), carrying the
-// residual colour C - T_final*bg - (front contributions) in registers as the
-// reference does. Per splat, a warp whose 8x4 pixel patch misses the splat's
-// pixel box skips it uniformly; otherwise each lane forms its pixel's
-// contribution to the splat's 10 gradient lanes, the warp sums them with a
-// 16-value butterfly (16 shuffles), the sums are accumulated per splat in
-// shared memory across the tile's 8 warps, and each (splat, tile) leaves with
-// three 16-byte vector atomics (red.global.add.v4.f32) into a 12-lane row.
+// pixel-parallel schedule: one 128-thread block per 16x16 tile, two pixels per
+// thread (Morton position (x, y) in the top half of the tile and (x, y + 8)).
+// Each thread replays its pixels front to back exactly as the forward did
+// (same float operations, so T and every accept / early-out decision match the
+// forward bit-for-bit), carrying the residual colour C - T_final*bg - (front
+// contributions) in registers as the reference does. Per splat, a warp whose
+// pixels all lie outside the splat's padded pixel box skips it uniformly;
+// otherwise each lane forms its pixels' contribution to the splat's 10
+// gradient lanes, the warp sums them with a 10-value butterfly (12 shuffles),
+// the sums are accumulated per splat in shared memory across the tile's 4
+// warps, and each (splat, tile) leaves with three 16-byte vector atomics
+// (red.global.add.v4.f32) into a 12-lane row.
 // The alpha / T chain uses exact IEEE operations; the gradient arithmetic,
 // which is tolerance-checked, uses fused multiply-adds and fast reciprocals.
 #include "splat_math.cuh"
@@ -79,38 +80,37 @@ __device__ __forceinline__ uint32_t splat_pixel_mask(float sx, float sy, float c
     return xm | (ym << 16);
 }
 
-// Sum 16 per-lane values over the warp. Returns, on lane l, the total of
-// value (l >> 1). Butterfly that halves the live values at each level:
-// 8 + 4 + 2 + 1 + 1 shuffles.
-__device__ __forceinline__ float warp_sum16(float (&v)[16], int lane) {
+// Pairwise butterfly step: lanes with `bit` clear keep value k and send k+h,
+// lanes with it set keep k+h and send k; each keeps the pair sum.
+template <int H, int N>
+__device__ __forceinline__ void butterfly_step(float (&v)[N], bool up, int lane_xor) {
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-        const bool up = lane & 16;
-        const float send = up ? v[k] : v[k + 8];
-        const float keep = up ? v[k + 8] : v[k];
-        v[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    for (int k = 0; k < H; ++k) {
+        const float hi = k + H < N ? v[k + H] : 0.0f;
+        const float send = up ? v[k] : hi;
+        const float keep = up ? hi : v[k];
+        v[k] = keep + __shfl_xor_sync(0xffffffffu, send, lane_xor);
     }
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const bool up = lane & 8;
-        const float send = up ? v[k] : v[k + 4];
-        const float keep = up ? v[k + 4] : v[k];
-        v[k] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-    }
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-        const bool up = lane & 4;
-        const float send = up ? v[k] : v[k + 2];
-        const float keep = up ? v[k + 2] : v[k];
-        v[k] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-    }
-    {
-        const bool up = lane & 2;
-        const float send = up ? v[0] : v[1];
-        const float keep = up ? v[1] : v[0];
-        v[0] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
-    }
-    return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
+}
+
+// Sum 10 per-lane values over the warp with 12 shuffles (5 + 3 + 2 + 1 + 1).
+// Returns on lane l the total of value warp_sum10_index(l) (both lanes of an
+// even/odd pair hold it); lanes whose index is >= 10 hold padding.
+__device__ __forceinline__ int warp_sum10_index(int lane) {
+    const int b4 = (lane >> 4) & 1, b3 = (lane >> 3) & 1, b2 = (lane >> 2) & 1, b1 = (lane >> 1) & 1;
+    const int w = 2 * b2 + b1;            // index within the 3 values of level 3
+    const int u = 3 * b3 + w;             // index within the 5 values of level 2
+    return (w < 3 && u < 5) ? 5 * b4 + u : 16;
+}
+__device__ __forceinline__ float warp_sum10(float (&v)[10], int lane) {
+    butterfly_step<5, 10>(v, lane & 16, 16);
+    float u[5] = {v[0], v[1], v[2], v[3], v[4]};
+    butterfly_step<3, 5>(u, lane & 8, 8);
+    float w[3] = {u[0], u[1], u[2]};
+    butterfly_step<2, 3>(w, lane & 4, 4);
+    float x[2] = {w[0], w[1]};
+    butterfly_step<1, 2>(x, lane & 2, 2);
+    return x[0] + __shfl_xor_sync(0xffffffffu, x[0], 1);
 }
 
 // Per-pixel replay state and constants.
@@ -150,7 +150,7 @@ __device__ __forceinline__ void pixel_init(PixelBwd& P, const BwdArgs& a, uint32
 template <bool SMOOTH, bool REFINE>
 __device__ __forceinline__ bool pixel_step(PixelBwd& P, float pcx, float dx0, float xx, float xy, float sx, float sy,
                                            float c00, float c01, float c11, float ca, float thr, float craw,
-                                           float cgraw, float cbraw, float wf, float hf, float (&gv)[16]) {
+                                           float cgraw, float cbraw, float wf, float hf, float (&gv)[10]) {
     if (P.done) return false;
     const float dyp = P.pcy - sy;
     const float sigma = 0.5f * (xx + c11 * dyp * dyp) + xy * dyp;
@@ -217,6 +217,7 @@ __global__ void __launch_bounds__(kBwdPixThreads) raster_bwd_kernel(const BwdArg
     __shared__ float s_grad[kBwdPixThreads][kGradLanes + 1];
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int sum_idx = warp_sum10_index(lane);
     const uint32_t tile = blockIdx.x;
     const uint32_t lo = __ldg(a.tile_offsets + tile * 2), hi = __ldg(a.tile_offsets + tile * 2 + 1);
     if (hi <= lo) return;
@@ -258,17 +259,16 @@ __global__ void __launch_bounds__(kBwdPixThreads) raster_bwd_kernel(const BwdArg
             const float dx0 = pcx - A.x;
             const float xx = A.z * dx0 * dx0;
             const float xy = A.w * dx0;
-            float gv[16];
+            float gv[kGradLanes];
 #pragma unroll
-            for (int k = 0; k < 16; ++k) gv[k] = 0.0f;
+            for (int k = 0; k < kGradLanes; ++k) gv[k] = 0.0f;
             bool contrib = pixel_step<SMOOTH, REFINE>(PA, pcx, dx0, xx, xy, A.x, A.y, A.z, A.w, B.x, B.y, Cc.y, B.z,
                                                       B.w, Cc.x, wf, hf, gv);
             contrib |= pixel_step<SMOOTH, REFINE>(PB, pcx, dx0, xx, xy, A.x, A.y, A.z, A.w, B.x, B.y, Cc.y, B.z, B.w,
                                                   Cc.x, wf, hf, gv);
             if (__any_sync(0xffffffffu, contrib)) {
-                const float tot = warp_sum16(gv, lane);
-                const int k = lane >> 1;
-                if (!(lane & 1) && k < kGradLanes) atomicAdd(&s_grad[t][k], tot);
+                const float tot = warp_sum10(gv, lane);
+                if (!(lane & 1) && sum_idx < kGradLanes) atomicAdd(&s_grad[t][sum_idx], tot);
             }
         }
         __syncthreads();
