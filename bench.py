@@ -116,6 +116,7 @@ def kernel_bytes(name, N, V, M, Mp, P, T, C, W=1):
         "raster_bwd_kernel": 32 * P + 52 * Mp + 48 * V,
         "project_bwd_kernel": 48 * N + V * (44 + 12 * C) + N * (48 + 12 * C),
         "adam_kernel": (316 + 60 * C) * N,
+        "gather_stats_kernel": 36 * N,
         # NVLink bytes per rank: peer gradient rows in + parameter rows out
         "dp_adam_kernel": 2 * (W - 1) * (N // W) * row if W > 1 else 0,
     }

@@ -158,6 +158,40 @@ class DpExchange(C.Structure):
     ]
 
 
+class TrainConfig(C.Structure):
+    _fields_ = [
+        ("total_train_iters", C.c_uint32),
+        ("lr_mean", C.c_double),
+        ("lr_mean_end", C.c_double),
+        ("lr_coeffs_dc", C.c_double),
+        ("lr_coeffs_sh_scale", C.c_float),
+        ("lr_opac", C.c_double),
+        ("lr_scale", C.c_double),
+        ("lr_scale_end", C.c_double),
+        ("lr_rotation", C.c_double),
+        ("ssim_weight", C.c_float),
+        ("background", C.c_float * 3),
+        ("median_scale", C.c_float),
+        ("uniform_lr", C.c_float),
+        ("render_mode", C.c_int32),
+        ("gather_stats", C.c_int32),
+    ]
+
+
+class TrainStats(C.Structure):
+    _fields_ = [
+        ("num_visible", C.c_uint32),
+        ("num_intersections", C.c_uint32),
+        ("lr_mean", C.c_float),
+        ("step", C.c_uint32),
+    ]
+
+
+class DpSplats(C.Structure):
+    _fields_ = [(name, C.c_void_p * BSX_MAX_RANKS) for name in
+                ("d_transforms", "d_sh_coeffs", "d_raw_opac", "d_v_transforms", "d_v_sh_coeffs", "d_v_raw_opac")]
+
+
 # name -> (restype, argtypes); exactly the functions include/bsx.h declares.
 SIGNATURES = {
     "bsx_create": (C.c_int, [C.c_int, C.POINTER(C.c_void_p)]),
@@ -206,6 +240,27 @@ SIGNATURES = {
     "bsx_peer_close": (C.c_int, [C.c_void_p, C.c_void_p]),
     "bsx_dp_adam_step": (
         C.c_int, [C.c_void_p, C.POINTER(DpExchange), C.POINTER(DpGroup), C.c_int32, C.POINTER(AdamCfg)]
+    ),
+    "bsx_trainer_create": (
+        C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.POINTER(TrainConfig), C.POINTER(C.c_void_p)]
+    ),
+    "bsx_trainer_destroy": (C.c_int, [C.c_void_p]),
+    "bsx_trainer_stats_buffers": (
+        C.c_int, [C.c_void_p, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), C.POINTER(C.c_void_p)]
+    ),
+    "bsx_trainer_grad_buffers": (
+        C.c_int,
+        [C.c_void_p, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), C.POINTER(C.c_void_p)],
+    ),
+    "bsx_train_step": (
+        C.c_int,
+        [C.c_void_p, C.POINTER(Camera), C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+         C.c_int32, C.c_void_p, C.POINTER(TrainStats)],
+    ),
+    "bsx_train_step_dp": (
+        C.c_int,
+        [C.c_void_p, C.POINTER(Camera), C.c_uint32, C.c_uint32, C.c_void_p, C.POINTER(DpExchange),
+         C.POINTER(DpSplats), C.c_int32, C.c_void_p, C.POINTER(TrainStats)],
     ),
     "bsx_radix_argsort_u32": (
         C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p]

@@ -1,0 +1,347 @@
+// train.cu - the whole training step behind one C entry point.
+//
+// Restates SplatTrainer::step_with_refine_weight
+// (crates/brush-train/src/train.rs:619-1182) for the hot path: backward-pass
+// render -> fused SSIM+L1 loss and its gradient (train.rs:729-761) -> raster
+// backward -> projection backward -> AdamScaled over transforms / SH /
+// opacity with the per-step rate table (train.rs:964-1051) -> RefineRecord
+// statistics (stats.rs:111-121). Every stage is a launch of this library on
+// the context's stream; the only host synchronisation is the render's count
+// readback.
+//
+// Learning-rate schedules: the reference steps two burn ExponentialLrScheduler
+// instances once per optimizer step (train.rs:991-994; burn git main, pinned
+// da67c939 in the reference's Cargo.lock). Restated here from burn's published
+// definition: the scheduler starts at initial / gamma and each step multiplies
+// by gamma (f64) and returns the new rate, so the first step uses the initial
+// rate; gamma = (end / start)^(1 / total_train_iters) (train.rs:243-258).
+#include <math.h>
+
+#include <vector>
+
+#include "common.cuh"
+
+struct bsx_trainer {
+    bsx_ctx* ctx = nullptr;
+    uint32_t n = 0, coeffs = 0;
+    bsx_train_config cfg{};
+    bsx::DevBuf grads, v_combined, v_output, stats, moments;
+    uint32_t moment_rows = 0;  // rows the moments cover (all, or this rank's shard)
+    int moment_world = 0, moment_rank = -1;
+    uint32_t step = 0;
+    double mean_prev = 0.0, mean_gamma = 1.0, scale_prev = 0.0, scale_gamma = 1.0;
+    uint32_t dp_epoch = 0;
+};
+
+namespace bsx {
+
+namespace {
+
+constexpr int kStatsThreads = 256;
+
+// RefineRecord::gather_stats (stats.rs:111-121): running MAX of the refine
+// weight, SUM of visibility, MAX of the screen-space radius.
+__global__ void __launch_bounds__(kStatsThreads)
+    gather_stats_kernel(const float* __restrict__ refine, const float* __restrict__ visible,
+                        const float* __restrict__ radius, uint32_t n, float* __restrict__ rmax,
+                        float* __restrict__ vsum, float* __restrict__ smax) {
+    for (uint32_t i = blockIdx.x * kStatsThreads + threadIdx.x; i < n; i += gridDim.x * kStatsThreads) {
+        rmax[i] = bsx_max(rmax[i], refine[i]);
+        vsum[i] = vsum[i] + visible[i];
+        smax[i] = bsx_max(smax[i], radius[i]);
+    }
+}
+
+size_t grad_floats(uint32_t n, uint32_t c) { return (size_t)n * (11 + 3 * (size_t)c); }
+
+// Per-step rates: (transform base lr, transform column scales, SH lr, SH
+// column scales, opacity lr, lr_mean).
+struct Rates {
+    float lr_t;
+    float t_scale[10];
+    float lr_sh;
+    std::vector<float> sh_scale;
+    float lr_op;
+    float lr_mean;
+    bool scaled;
+};
+
+Rates next_rates(bsx_trainer* tr) {
+    Rates r;
+    const bsx_train_config& c = tr->cfg;
+    if (c.uniform_lr > 0.0f) {
+        r.lr_t = r.lr_sh = r.lr_op = r.lr_mean = c.uniform_lr;
+        r.scaled = false;
+        return r;
+    }
+    tr->mean_prev *= tr->mean_gamma;
+    tr->scale_prev *= tr->scale_gamma;
+    const double lr_mean = tr->mean_prev * (double)c.median_scale;
+    const double lr_scale = tr->scale_prev;
+    r.scaled = true;
+    r.lr_t = 1.0f;
+    for (int k = 0; k < 3; ++k) r.t_scale[k] = (float)lr_mean;
+    for (int k = 3; k < 7; ++k) r.t_scale[k] = (float)c.lr_rotation;
+    for (int k = 7; k < 10; ++k) r.t_scale[k] = (float)lr_scale;
+    r.lr_sh = (float)c.lr_coeffs_dc;
+    r.sh_scale.assign(3 * (size_t)tr->coeffs, 1.0f / c.lr_coeffs_sh_scale);
+    for (int k = 0; k < 3; ++k) r.sh_scale[k] = 1.0f;
+    r.lr_op = (float)c.lr_opac;
+    r.lr_mean = (float)lr_mean;
+    return r;
+}
+
+// Moments for `rows` rows (zeroed when the layout changes).
+bsx_status ensure_moments(bsx_trainer* tr, uint32_t rows, int world, int rank, float** m, float** v) {
+    const size_t c3 = 3 * (size_t)tr->coeffs;
+    const size_t mf = (size_t)rows * (10 + c3 + 1), vf = (size_t)rows * (10 + 1 + 1);
+    if (tr->moment_rows != rows || tr->moment_world != world || tr->moment_rank != rank) {
+        bsx_status s = ensure(tr->ctx, tr->moments, (mf + vf) * 4 + 64);
+        if (s != BSX_OK) return s;
+        s = check_cuda(tr->ctx, cudaMemsetAsync(tr->moments.p, 0, (mf + vf) * 4, tr->ctx->stream), "memset moments");
+        if (s != BSX_OK) return s;
+        tr->moment_rows = rows;
+        tr->moment_world = world;
+        tr->moment_rank = rank;
+        tr->step = 0;
+    }
+    float* base = tr->moments.as<float>();
+    // m: [rows,10] | [rows,3C] | [rows,1]; v: [rows,10] | [rows] | [rows,1]
+    m[0] = base;
+    m[1] = m[0] + (size_t)rows * 10;
+    m[2] = m[1] + (size_t)rows * c3;
+    v[0] = m[2] + rows;
+    v[1] = v[0] + (size_t)rows * 10;
+    v[2] = v[1] + rows;
+    return BSX_OK;
+}
+
+bsx_loss_cfg loss_cfg_of(const bsx_train_config& c) {
+    bsx_loss_cfg l{};
+    if (c.ssim_weight > 0.0f) {
+        l.l1_weight = 1.0f - c.ssim_weight;
+        l.ssim_weight = -c.ssim_weight;
+    } else {
+        l.l1_weight = 1.0f;
+        l.ssim_weight = 0.0f;
+    }
+    l.composite_bg = 0;
+    l.mask = 0;
+    return l;
+}
+
+// Render -> loss -> raster backward -> projection backward, into the given gradient buffers.
+bsx_status forward_backward(bsx_trainer* tr, const bsx_camera* cam, uint32_t w, uint32_t h, const uint32_t* gt,
+                            const float* transforms, const float* sh, const float* opac, float* vt, float* vs,
+                            float* vo, float* vr, int refine, float* d_loss, bsx_render_out* out) {
+    bsx_ctx* ctx = tr->ctx;
+    bsx_status s = bsx_render_fwd(ctx, cam, w, h, transforms, sh, opac, tr->n, tr->coeffs, tr->cfg.render_mode,
+                                  BSX_PASS_BACKWARD, tr->cfg.background, out);
+    if (s != BSX_OK) return s;
+    s = ensure(ctx, tr->v_output, (size_t)w * h * 16);
+    if (s != BSX_OK) return s;
+    const bsx_loss_cfg lc = loss_cfg_of(tr->cfg);
+    s = bsx_loss_fused(ctx, out->d_image, gt, w, h, &lc, d_loss, tr->v_output.as<float>());
+    if (s != BSX_OK) return s;
+    s = bsx_rasterize_bwd(ctx, tr->v_output.as<float>(), refine, tr->v_combined.as<float>());
+    if (s != BSX_OK) return s;
+    return bsx_project_bwd(ctx, tr->v_combined.as<float>(), vt, vs, vo, vr);
+}
+
+bsx_status gather_stats(bsx_trainer* tr, const float* refine, const bsx_render_out& out) {
+    if (!tr->cfg.gather_stats || tr->n == 0) return BSX_OK;
+    float* st = tr->stats.as<float>();
+    const uint32_t blocks = std::min<uint32_t>((tr->n + kStatsThreads - 1) / kStatsThreads, 148 * 8);
+    prof_begin(tr->ctx);
+    gather_stats_kernel<<<blocks, kStatsThreads, 0, tr->ctx->stream>>>(refine, out.d_visible, out.d_max_radius, tr->n,
+                                                                       st, st + tr->n, st + 2 * (size_t)tr->n);
+    return post_launch(tr->ctx, "gather_stats_kernel");
+}
+
+bsx_status check_cfg(const bsx_train_config* c) {
+    if (!c) return BSX_ERR_INVALID_ARG;
+    if (c->uniform_lr > 0.0f) return BSX_OK;
+    if (!(c->lr_mean > 0.0) || !(c->lr_mean_end > 0.0) || !(c->lr_coeffs_sh_scale > 0.0f) ||
+        c->total_train_iters == 0)
+        return BSX_ERR_INVALID_ARG;
+    return BSX_OK;
+}
+
+}  // namespace
+
+}  // namespace bsx
+
+using namespace bsx;
+
+extern "C" {
+
+bsx_status bsx_trainer_create(bsx_ctx* ctx, uint32_t n, uint32_t coeffs, const bsx_train_config* cfg,
+                              bsx_trainer** out) {
+    if (!ctx || !out || coeffs == 0) return BSX_ERR_INVALID_ARG;
+    *out = nullptr;
+    if (check_cfg(cfg) != BSX_OK) return fail(ctx, BSX_ERR_INVALID_ARG, "invalid train config");
+    bsx_trainer* tr = new (std::nothrow) bsx_trainer();
+    if (!tr) return BSX_ERR_CAPACITY;
+    tr->ctx = ctx;
+    tr->n = n;
+    tr->coeffs = coeffs;
+    tr->cfg = *cfg;
+    if (cfg->uniform_lr <= 0.0f) {
+        const double t = (double)cfg->total_train_iters;
+        tr->mean_gamma = pow(cfg->lr_mean_end / cfg->lr_mean, 1.0 / t);
+        tr->scale_gamma =
+            (cfg->lr_scale > 0.0 && cfg->lr_scale_end > 0.0) ? pow(cfg->lr_scale_end / cfg->lr_scale, 1.0 / t) : 1.0;
+        tr->mean_prev = cfg->lr_mean / tr->mean_gamma;
+        tr->scale_prev = cfg->lr_scale / tr->scale_gamma;
+    }
+    cudaSetDevice(ctx->device);
+    const size_t nn = n ? n : 1;
+    bsx_status s = ensure(ctx, tr->v_combined, nn * BSX_GRAD_STRIDE * 4);
+    if (s == BSX_OK && cfg->gather_stats) {
+        s = ensure(ctx, tr->stats, 3 * nn * 4);
+        if (s == BSX_OK)
+            s = check_cuda(ctx, cudaMemsetAsync(tr->stats.p, 0, 3 * nn * 4, ctx->stream), "memset refine record");
+    }
+    if (s != BSX_OK) {
+        bsx_trainer_destroy(tr);
+        return s;
+    }
+    *out = tr;
+    return BSX_OK;
+}
+
+bsx_status bsx_trainer_destroy(bsx_trainer* tr) {
+    if (!tr) return BSX_ERR_INVALID_ARG;
+    cudaSetDevice(tr->ctx->device);
+    if (tr->ctx->stream) cudaStreamSynchronize(tr->ctx->stream);
+    DevBuf* bufs[] = {&tr->grads, &tr->v_combined, &tr->v_output, &tr->stats, &tr->moments};
+    for (DevBuf* b : bufs)
+        if (b->p) cudaFree(b->p);
+    delete tr;
+    return BSX_OK;
+}
+
+bsx_status bsx_trainer_stats_buffers(bsx_trainer* tr, float** rmax, float** vsum, float** smax) {
+    if (!tr || !rmax || !vsum || !smax) return BSX_ERR_INVALID_ARG;
+    if (!tr->cfg.gather_stats) return fail(tr->ctx, BSX_ERR_STATE, "trainer created without gather_stats");
+    float* st = tr->stats.as<float>();
+    *rmax = st;
+    *vsum = st + tr->n;
+    *smax = st + 2 * (size_t)tr->n;
+    return BSX_OK;
+}
+
+bsx_status bsx_trainer_grad_buffers(bsx_trainer* tr, float** vt, float** vs, float** vo, float** vr) {
+    if (!tr || !vt || !vs || !vo || !vr) return BSX_ERR_INVALID_ARG;
+    // allocated on first use: the data-parallel step writes into the exchange buffers instead
+    bsx_status s = ensure(tr->ctx, tr->grads, (grad_floats(tr->n, tr->coeffs) + tr->n) * 4 + 64);
+    if (s != BSX_OK) return s;
+    float* g = tr->grads.as<float>();
+    *vt = g;
+    *vs = g + (size_t)tr->n * 10;
+    *vo = *vs + (size_t)tr->n * 3 * tr->coeffs;
+    *vr = *vo + tr->n;
+    return BSX_OK;
+}
+
+bsx_status bsx_train_step(bsx_trainer* tr, const bsx_camera* cam, uint32_t w, uint32_t h, const uint32_t* gt,
+                          float* transforms, float* sh, float* opac, int32_t refine, float* d_loss,
+                          bsx_train_stats* stats) {
+    if (!tr || !cam || !gt || !d_loss || (tr->n && (!transforms || !sh || !opac))) return BSX_ERR_INVALID_ARG;
+    bsx_ctx* ctx = tr->ctx;
+    cudaSetDevice(ctx->device);
+    float *vt, *vs, *vo, *vr;
+    bsx_status s0 = bsx_trainer_grad_buffers(tr, &vt, &vs, &vo, &vr);
+    if (s0 != BSX_OK) return s0;
+    bsx_render_out out{};
+    bsx_status s = forward_backward(tr, cam, w, h, gt, transforms, sh, opac, vt, vs, vo, vr, refine, d_loss, &out);
+    if (s != BSX_OK) return s;
+    float* m[3];
+    float* v[3];
+    s = ensure_moments(tr, tr->n, 1, 0, m, v);
+    if (s != BSX_OK) return s;
+    const Rates r = next_rates(tr);
+    tr->step++;
+    const uint32_t c3 = 3 * tr->coeffs;
+    bsx_adam_group g[3];
+    g[0] = {transforms, vt, m[0], v[0], tr->n, 10, r.lr_t, r.scaled ? r.t_scale : nullptr, 0};
+    g[1] = {sh, vs, m[1], v[1], tr->n, c3, r.lr_sh, r.scaled ? r.sh_scale.data() : nullptr, 1};
+    g[2] = {opac, vo, m[2], v[2], tr->n, 1, r.lr_op, nullptr, 0};
+    const bsx_adam_cfg ac{0.9f, 0.999f, 1e-15f, tr->step, 1.0f};
+    if (tr->n) {
+        s = bsx_adam_step(ctx, g, 3, &ac);
+        if (s != BSX_OK) return s;
+    }
+    if (refine) {
+        s = gather_stats(tr, vr, out);
+        if (s != BSX_OK) return s;
+    }
+    if (stats) {
+        stats->num_visible = out.num_visible;
+        stats->num_intersections = out.num_intersections;
+        stats->lr_mean = r.lr_mean;
+        stats->step = tr->step;
+    }
+    return BSX_OK;
+}
+
+bsx_status bsx_train_step_dp(bsx_trainer* tr, const bsx_camera* cam, uint32_t w, uint32_t h, const uint32_t* gt,
+                             const bsx_dp_exchange* ex, const bsx_dp_splats* sp, int32_t refine, float* d_loss,
+                             bsx_train_stats* stats) {
+    if (!tr || !cam || !gt || !ex || !sp || !d_loss) return BSX_ERR_INVALID_ARG;
+    bsx_ctx* ctx = tr->ctx;
+    const int rank = ex->rank, world = ex->world;
+    if (world < 1 || world > BSX_MAX_RANKS || rank < 0 || rank >= world)
+        return fail(ctx, BSX_ERR_INVALID_ARG, "rank / world out of range (world <= 8)");
+    if (!ex->d_refine[rank]) return fail(ctx, BSX_ERR_INVALID_ARG, "the exchange needs refine-weight buffers");
+    cudaSetDevice(ctx->device);
+    bsx_render_out out{};
+    bsx_status s = forward_backward(tr, cam, w, h, gt, sp->d_transforms[rank], sp->d_sh_coeffs[rank],
+                                    sp->d_raw_opac[rank], sp->d_v_transforms[rank], sp->d_v_sh_coeffs[rank],
+                                    sp->d_v_raw_opac[rank], ex->d_refine[rank], refine, d_loss, &out);
+    if (s != BSX_OK) return s;
+    const uint32_t rb = (uint32_t)((uint64_t)tr->n * rank / world), re = (uint32_t)((uint64_t)tr->n * (rank + 1) / world);
+    float* m[3];
+    float* v[3];
+    s = ensure_moments(tr, re - rb, world, rank, m, v);
+    if (s != BSX_OK) return s;
+    const Rates r = next_rates(tr);
+    tr->step++;
+    bsx_dp_group g[3];
+    const float* lrs[3] = {&r.lr_t, &r.lr_sh, &r.lr_op};
+    const float* scales[3] = {r.scaled ? r.t_scale : nullptr, r.scaled ? r.sh_scale.data() : nullptr, nullptr};
+    const uint32_t cols[3] = {10, 3 * tr->coeffs, 1};
+    for (int i = 0; i < 3; ++i) {
+        for (int q = 0; q < BSX_MAX_RANKS; ++q) {
+            const bool in = q < world;
+            g[i].d_param[q] = !in ? nullptr : i == 0 ? sp->d_transforms[q] : i == 1 ? sp->d_sh_coeffs[q] : sp->d_raw_opac[q];
+            g[i].d_grad[q] = !in ? nullptr : i == 0 ? sp->d_v_transforms[q] : i == 1 ? sp->d_v_sh_coeffs[q] : sp->d_v_raw_opac[q];
+        }
+        g[i].d_m = m[i];
+        g[i].d_v = v[i];
+        g[i].rows = tr->n;
+        g[i].cols = cols[i];
+        g[i].lr = *lrs[i];
+        g[i].h_col_scale = scales[i];
+        g[i].reduce_moment_2 = i == 1;
+    }
+    bsx_dp_exchange e = *ex;
+    e.refine_rows = refine ? tr->n : 0;
+    e.epoch = ++tr->dp_epoch;
+    const bsx_adam_cfg ac{0.9f, 0.999f, 1e-15f, tr->step, 1.0f / (float)world};
+    s = bsx_dp_adam_step(ctx, &e, g, 3, &ac);
+    if (s != BSX_OK) return s;
+    if (refine) {
+        s = gather_stats(tr, ex->d_refine[rank], out);
+        if (s != BSX_OK) return s;
+    }
+    if (stats) {
+        stats->num_visible = out.num_visible;
+        stats->num_intersections = out.num_intersections;
+        stats->lr_mean = r.lr_mean;
+        stats->step = tr->step;
+    }
+    return BSX_OK;
+}
+
+}  // extern "C"

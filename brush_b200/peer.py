@@ -89,18 +89,13 @@ class PeerExchange:
             self.ctx.check(L.bsx_peer_open(self.ctx.handle, C.create_string_buffer(h, len(h)), C.byref(p)))
             self.bases.append(p.value)
             self._opened.append(p.value)
-        lay = self.layout
         self.params = (self._view(("param", "transforms"), (n, 10)), self._view(("param", "sh"), (n, c, 3)),
                        self._view(("param", "opac"), (n,)))
         self.grads = (self._view(("grad", "transforms"), (n, 10)), self._view(("grad", "sh"), (n, c, 3)),
                       self._view(("grad", "opac"), (n,)))
         self.refine = self._view("refine", (n,))
         self.row0, self.row1 = shard_rows(n, self.rank, self.world)
-        rows = self.row1 - self.row0
-        dev = torch.device("cuda", device)
-        self.m = [torch.zeros((rows, w), device=dev) for w in lay.widths.values()]
-        self.v = [torch.zeros((rows, 10), device=dev), torch.zeros((rows,), device=dev),
-                  torch.zeros((rows, 1), device=dev)]
+        self.m = self.v = None  # shard moments of adam_step (the native trainer keeps its own)
         self._closed = False
 
     def _view(self, key, shape) -> torch.Tensor:
@@ -118,6 +113,11 @@ class PeerExchange:
         """One fused exchange + AdamScaled step. ``specs``: (lr, col_scale, reduce_moment_2) for
         transforms, SH rows and opacities."""
         L = _lib.lib()
+        if self.m is None:
+            rows, dev = self.row1 - self.row0, torch.device("cuda", self.device)
+            self.m = [torch.zeros((rows, w), device=dev) for w in self.layout.widths.values()]
+            self.v = [torch.zeros((rows, 10), device=dev), torch.zeros((rows,), device=dev),
+                      torch.zeros((rows, 1), device=dev)]
         adam.step_count += 1
         self.epoch += 1
         ex = _lib.DpExchange()
@@ -152,6 +152,24 @@ class PeerExchange:
         cfg = _lib.AdamCfg(beta_1=adam.beta_1, beta_2=adam.beta_2, epsilon=adam.epsilon, step=adam.step_count,
                            grad_scale=float(grad_scale))
         self.ctx.check(L.bsx_dp_adam_step(self.ctx.handle, C.byref(ex), arr, 3, C.byref(cfg)))
+
+    def train_structs(self):
+        """(bsx_dp_exchange, bsx_dp_splats) describing every rank's region, for bsx_train_step_dp."""
+        ex = _lib.DpExchange()
+        ex.rank, ex.world = self.rank, self.world
+        sp = _lib.DpSplats()
+        for q in range(self.world):
+            ex.d_flags[q] = self._ptr(q, "flags")
+            ex.d_refine[q] = self._ptr(q, "refine")
+            sp.d_transforms[q] = self._ptr(q, ("param", "transforms"))
+            sp.d_sh_coeffs[q] = self._ptr(q, ("param", "sh"))
+            sp.d_raw_opac[q] = self._ptr(q, ("param", "opac"))
+            sp.d_v_transforms[q] = self._ptr(q, ("grad", "transforms"))
+            sp.d_v_sh_coeffs[q] = self._ptr(q, ("grad", "sh"))
+            sp.d_v_raw_opac[q] = self._ptr(q, ("grad", "opac"))
+        ex.refine_rows = self.layout.n
+        ex.timeout_ns = self.timeout_ns
+        return ex, sp
 
     def close(self) -> None:
         """Unmap the other ranks' regions, then free this rank's (collective)."""

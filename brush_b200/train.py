@@ -4,9 +4,13 @@
 One step: backward-pass render -> fused SSIM+L1 loss and its gradient ->
 raster backward -> projection backward -> fused AdamScaled over transforms /
 SH / opacity with the reference's learning-rate table (train.rs:964-1051) ->
-refine statistics (stats.rs:111-121). With several ranks (one view each) the
-gradient exchange and Adam are one peer-memory kernel (brush_b200.peer), or
-NCCL collectives around the fused Adam (brush_b200.dist).
+refine statistics (stats.rs:111-121).
+
+On one GPU, and with several ranks using the peer-memory exchange, the whole
+step is one call into the library (``bsx_train_step`` / ``bsx_train_step_dp``,
+a native trainer owning gradients, moments, schedules and statistics). The
+NCCL alternative (``exchange="nccl"``) orchestrates the same kernels from
+here around reduce-scatter / all-gather (brush_b200.dist).
 
 Not applied: the reference's random mean-noise injection after Adam
 (train.rs:1095-1169); it draws from a non-reproducible RNG stream and is
@@ -14,11 +18,14 @@ outside the parity contract.
 """
 from __future__ import annotations
 
-from dataclasses import dataclass, field
+import ctypes as C
+from dataclasses import dataclass
 
+import numpy as np
 import torch
 
 from . import _lib
+from ._context import context, device_view, ptr
 from .adam import AdamGroup, AdamScaled
 from .camera import Camera
 from .dist import all_gather_rows, reduce_gradients, reduce_scatter_rows, row_shard
@@ -47,6 +54,22 @@ class TrainConfig:
     # "one Adam step, lr 1e-3"); None selects the reference table above.
     uniform_lr: float | None = None
 
+    def to_c(self, median_scale: float, render_mode: int, gather_stats: bool) -> _lib.TrainConfig:
+        c = _lib.TrainConfig()
+        c.total_train_iters = int(self.total_train_iters)
+        c.lr_mean, c.lr_mean_end = float(self.lr_mean), float(self.lr_mean_end)
+        c.lr_coeffs_dc, c.lr_coeffs_sh_scale = float(self.lr_coeffs_dc), float(self.lr_coeffs_sh_scale)
+        c.lr_opac = float(self.lr_opac)
+        c.lr_scale, c.lr_scale_end = float(self.lr_scale), float(self.lr_scale_end)
+        c.lr_rotation = float(self.lr_rotation)
+        c.ssim_weight = float(self.ssim_weight)
+        c.background[:] = [float(v) for v in self.background_color]
+        c.median_scale = float(median_scale)
+        c.uniform_lr = float(self.uniform_lr) if self.uniform_lr is not None else 0.0
+        c.render_mode = int(render_mode)
+        c.gather_stats = int(gather_stats)
+        return c
+
 
 @dataclass
 class TrainStepStats:
@@ -74,6 +97,40 @@ class RefineRecord:
         torch.maximum(self.max_screen_size, screen_radius, out=self.max_screen_size)
 
 
+class _NativeTrainer:
+    """Owner of one ``bsx_trainer`` (gradients, moments, schedules, statistics)."""
+
+    def __init__(self, device: int, n: int, c: int, cfg: _lib.TrainConfig):
+        self.ctx = context(device)
+        self.device = device
+        self.n, self.c = n, c
+        h = C.c_void_p()
+        self.ctx.check(_lib.lib().bsx_trainer_create(self.ctx.handle, n, c, C.byref(cfg), C.byref(h)))
+        self.handle = h
+        self.gather = bool(cfg.gather_stats)
+
+    def grads(self) -> SplatGrads:
+        p = [C.c_void_p() for _ in range(4)]
+        self.ctx.check(_lib.lib().bsx_trainer_grad_buffers(self.handle, *[C.byref(x) for x in p]))
+        n, c, d = self.n, self.c, self.device
+        return SplatGrads(device_view(p[0].value, (n, 10), torch.float32, d),
+                          device_view(p[1].value, (n, c, 3), torch.float32, d),
+                          device_view(p[2].value, (n,), torch.float32, d),
+                          device_view(p[3].value, (n,), torch.float32, d))
+
+    def record(self) -> RefineRecord | None:
+        if not self.gather:
+            return None
+        p = [C.c_void_p() for _ in range(3)]
+        self.ctx.check(_lib.lib().bsx_trainer_stats_buffers(self.handle, *[C.byref(x) for x in p]))
+        return RefineRecord(*[device_view(x.value, (self.n,), torch.float32, self.device) for x in p])
+
+    def close(self) -> None:
+        if self.handle:
+            self.ctx.check(_lib.lib().bsx_trainer_destroy(self.handle))
+            self.handle = None
+
+
 class SplatTrainer:
     def __init__(self, config: TrainConfig, splats: Splats, process_group=None, gather_stats: bool = True,
                  shard_optimizer: bool = True, exchange: str = "peer"):
@@ -89,25 +146,50 @@ class SplatTrainer:
             raise ValueError("exchange must be 'peer' or 'nccl'")
         self.exchange = exchange
         self.peer = None
+        self.native = None
         self.shard_optimizer = shard_optimizer
         self.adam = AdamScaled(epsilon=1e-15)
         self.step_count = 0
         self.pg = process_group
         self.world = 1 if process_group is None else torch.distributed.get_world_size(process_group)
         self.gather_stats = gather_stats
-        self.median_scale = median_size(splats.means(), config.bounds_percentile)
+        # f32, as BoundingBox::median_size returns it (the rate is lr * median_scale as f64, train.rs:991)
+        self.median_scale = float(np.float32(median_size(splats.means(), config.bounds_percentile)))
         t = max(config.total_train_iters, 1)
         self.mean_decay = (config.lr_mean_end / config.lr_mean) ** (1.0 / t)
         self.scale_decay = ((config.lr_scale_end / config.lr_scale) ** (1.0 / t)
                             if config.lr_scale > 0 and config.lr_scale_end > 0 else 1.0)
+        # burn ExponentialLrScheduler state: starts at initial / gamma (first step uses the initial rate)
+        self._mean_prev = config.lr_mean / self.mean_decay
+        self._scale_prev = config.lr_scale / self.scale_decay
         self._alloc(splats)
 
     def _alloc(self, splats: Splats) -> None:
         n, c = splats.num_splats, splats.sh_coeffs_per_splat
         dev = splats.transforms.device
         self.n, self.c = n, c
-        use_peer = self.world > 1 and self.exchange == "peer"
-        if not use_peer:
+        self.loss = torch.empty(1, device=dev)
+        self.v_output = None
+        self.groups = None
+        old_peer, self.peer = self.peer, None
+        old_native, self.native = self.native, None
+        if self.world == 1 or self.exchange == "peer":
+            self.native = _NativeTrainer(dev.index, n, c, self.config.to_c(self.median_scale, splats.render_mode,
+                                                                          self.gather_stats))
+            self.record = self.native.record()
+            if self.world > 1:
+                from .peer import PeerExchange
+
+                self.peer = PeerExchange(n, c, dev.index, self.pg)
+                self.peer.load(splats.transforms, splats.sh_coeffs, splats.raw_opacities)
+                splats.transforms, splats.sh_coeffs, splats.raw_opacities = self.peer.params
+                self.grads = SplatGrads(*self.peer.grads, v_refine_weight=self.peer.refine)
+                self._dp = self.peer.train_structs()
+            else:
+                self.grads = self.native.grads()
+            self.flat_grad = None
+            self.sharded = False
+        else:
             # One flat gradient buffer so data-parallel ranks all-reduce once per step.
             self.flat_grad = torch.empty(n * (10 + 3 * c + 1), device=dev)
             g = self.flat_grad
@@ -117,37 +199,29 @@ class SplatTrainer:
                 v_raw_opac=g[n * (10 + 3 * c):].view(n),
                 v_refine_weight=torch.empty(n, device=dev),
             )
-        self.v_combined = torch.empty((max(n, 1), _lib.BSX_GRAD_STRIDE), device=dev)
-        self.loss = torch.empty(1, device=dev)
-        self.v_output = None
-        self.record = RefineRecord.new(n, dev) if self.gather_stats else None
-        self.groups = None
-        old, self.peer = self.peer, None
-        if use_peer:
-            from .peer import PeerExchange
-
-            self.peer = PeerExchange(n, c, dev.index, self.pg)
-            self.peer.load(splats.transforms, splats.sh_coeffs, splats.raw_opacities)
-            splats.transforms, splats.sh_coeffs, splats.raw_opacities = self.peer.params
-            self.grads = SplatGrads(*self.peer.grads, v_refine_weight=self.peer.refine)
-            self.flat_grad = None
-        if old is not None:
-            old.close()
-        self.sharded = (self.peer is None and self.shard_optimizer and self.world > 1 and n % self.world == 0)
-        if self.sharded:
-            self.rank = torch.distributed.get_rank(self.pg)
-            self.row0, self.row1 = row_shard(n, self.world, self.rank)
-            r = self.row1 - self.row0
-            self.shard_grads = (torch.empty((r, 10), device=dev), torch.empty((r, 3 * c), device=dev),
-                                torch.empty((r, 1), device=dev))
+            self.v_combined = torch.empty((max(n, 1), _lib.BSX_GRAD_STRIDE), device=dev)
+            self.record = RefineRecord.new(n, dev) if self.gather_stats else None
+            self.sharded = self.shard_optimizer and n % self.world == 0
+            if self.sharded:
+                self.rank = torch.distributed.get_rank(self.pg)
+                self.row0, self.row1 = row_shard(n, self.world, self.rank)
+                r = self.row1 - self.row0
+                self.shard_grads = (torch.empty((r, 10), device=dev), torch.empty((r, 3 * c), device=dev),
+                                    torch.empty((r, 1), device=dev))
+        if old_peer is not None:
+            old_peer.close()
+        if old_native is not None:
+            old_native.close()
 
     def _lr_table(self):
+        """Rates of this step: burn ExponentialLrScheduler, stepped once per optimizer step."""
         cfg = self.config
-        k = self.step_count
         if cfg.uniform_lr is not None:
             return cfg.uniform_lr, None, cfg.uniform_lr, None, cfg.uniform_lr, cfg.uniform_lr
-        lr_mean = cfg.lr_mean * self.mean_decay ** k * self.median_scale
-        lr_scale = cfg.lr_scale * self.scale_decay ** k
+        self._mean_prev *= self.mean_decay
+        self._scale_prev *= self.scale_decay
+        lr_mean = self._mean_prev * self.median_scale
+        lr_scale = self._scale_prev
         tscale = [lr_mean] * 3 + [cfg.lr_rotation] * 4 + [lr_scale] * 3
         sh_scale = [1.0] + [1.0 / cfg.lr_coeffs_sh_scale] * (self.c - 1)
         sh_cols = [s for s in sh_scale for _ in range(3)]
@@ -158,6 +232,30 @@ class SplatTrainer:
         """One optimisation step in place on ``splats`` (device tensors)."""
         if splats.num_splats != self.n or splats.sh_coeffs_per_splat != self.c:
             self._alloc(splats)
+        if self.native is not None:
+            return self._native_step(camera, img_size, gt_packed, splats, compute_refine_weight)
+        return self._nccl_step(camera, img_size, gt_packed, splats, compute_refine_weight)
+
+    def _native_step(self, camera, img_size, gt_packed, splats, compute_refine_weight) -> TrainStepStats:
+        L = _lib.lib()
+        ctx = context(splats.transforms.device)
+        w, h = img_size
+        cam = camera.to_c()
+        st = _lib.TrainStats()
+        if gt_packed.shape != (h, w) or gt_packed.dtype not in (torch.int32, torch.uint32):
+            raise ValueError("gt_packed must be [H,W] packed RGBA8 (int32/uint32)")
+        if self.peer is None:
+            ctx.check(L.bsx_train_step(self.native.handle, C.byref(cam), w, h, ptr(gt_packed), ptr(splats.transforms),
+                                       ptr(splats.sh_coeffs), ptr(splats.raw_opacities), int(compute_refine_weight),
+                                       ptr(self.loss), C.byref(st)))
+        else:
+            ex, sp = self._dp
+            ctx.check(L.bsx_train_step_dp(self.native.handle, C.byref(cam), w, h, ptr(gt_packed), C.byref(ex),
+                                          C.byref(sp), int(compute_refine_weight), ptr(self.loss), C.byref(st)))
+        self.step_count = int(st.step)
+        return TrainStepStats(int(st.num_visible), int(st.num_intersections), self.loss, float(st.lr_mean))
+
+    def _nccl_step(self, camera, img_size, gt_packed, splats, compute_refine_weight) -> TrainStepStats:
         self.step_count += 1
         cfg = self.config
         out = render(camera, img_size, splats.transforms, splats.sh_coeffs, splats.raw_opacities,
@@ -170,14 +268,6 @@ class SplatTrainer:
         rasterize_bwd(self.v_output, compute_refine_weight, self.v_combined)
         project_bwd(self.v_combined, self.n, self.c, self.grads)
         n, c = self.n, self.c
-        if self.peer is not None:
-            lr_t, tscale, lr_sh, sh_cols, lr_op, lr_mean = self._lr_table()
-            with_refine = self.record is not None and compute_refine_weight
-            self.peer.adam_step(self.adam, [(lr_t, tscale, False), (lr_sh, sh_cols, True), (lr_op, None, False)],
-                                1.0 / self.world, with_refine)
-            if with_refine:
-                self.record.gather_stats(self.grads.v_refine_weight, out.aux.visible, out.aux.max_radius)
-            return TrainStepStats(out.aux.num_visible, out.aux.num_intersections, self.loss, lr_mean)
         full_params = (splats.transforms, splats.sh_coeffs.view(n, 3 * c), splats.raw_opacities.view(n, 1))
         full_grads = (self.grads.v_transforms, self.grads.v_coeffs.view(n, 3 * c), self.grads.v_raw_opac.view(n, 1))
         if self.sharded:
@@ -206,13 +296,15 @@ class SplatTrainer:
         self.adam.step(self.groups, grad_scale=grad_scale)
         if self.sharded:
             all_gather_rows(full_params, self.pg, self.rank, self.world)
-        if self.record is not None:
-            if compute_refine_weight:
-                self.record.gather_stats(self.grads.v_refine_weight, out.aux.visible, out.aux.max_radius)
+        if self.record is not None and compute_refine_weight:
+            self.record.gather_stats(self.grads.v_refine_weight, out.aux.visible, out.aux.max_radius)
         return TrainStepStats(out.aux.num_visible, out.aux.num_intersections, self.loss, lr_mean)
 
     def close(self) -> None:
-        """Release the data-parallel exchange region (collective over the process group)."""
+        """Release the exchange region (collective over the process group) and the native trainer."""
         if self.peer is not None:
             self.peer.close()
             self.peer = None
+        if self.native is not None:
+            self.native.close()
+            self.native = None

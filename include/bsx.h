@@ -267,6 +267,75 @@ typedef struct bsx_dp_exchange {
 BSX_API bsx_status bsx_dp_adam_step(bsx_ctx* ctx, const bsx_dp_exchange* ex, const bsx_dp_group* groups,
                                     int32_t num_groups, const bsx_adam_cfg* cfg);
 
+/* ---- whole training step: SplatTrainer::step (crates/brush-train/src/train.rs:619-1182) ----
+ * A trainer owns what one step needs besides the splats: the loss gradient
+ * image, the raster-backward rows, the dense gradients (or caller-supplied
+ * buffers), the AdamScaled moments, the learning-rate schedules and the
+ * refine statistics. One bsx_train_step = backward-pass render -> fused
+ * SSIM+L1 loss and its gradient -> raster backward -> projection backward ->
+ * fused AdamScaled over transforms / SH / opacity with the reference's rate
+ * table (train.rs:964-1051) -> refine statistics (stats.rs:111-121), all on
+ * the context's stream. The random mean-noise injection after Adam
+ * (train.rs:1095-1169) is not applied. */
+typedef struct bsx_train_config {        /* TrainConfig subset (crates/brush-train/src/config.rs:15-136) */
+    uint32_t total_train_iters;          /* 30000 */
+    double lr_mean, lr_mean_end;         /* 2e-5, 2e-7 (scaled by median_scale) */
+    double lr_coeffs_dc;                 /* 2e-3 */
+    float lr_coeffs_sh_scale;            /* 10: higher SH bands use lr_coeffs_dc / this */
+    double lr_opac;                      /* 0.012 */
+    double lr_scale, lr_scale_end;       /* 7e-3, 5e-3 */
+    double lr_rotation;                  /* 2e-3 */
+    float ssim_weight;                   /* 0.2: loss = (1-w) L1 + w (1 - SSIM) */
+    float background[3];
+    float median_scale;                  /* BoundingBox::median_size of the initial means */
+    float uniform_lr;                    /* > 0: this rate for every parameter, no schedule */
+    int32_t render_mode;                 /* bsx_render_mode */
+    int32_t gather_stats;                /* 1: keep the RefineRecord statistics */
+} bsx_train_config;
+
+typedef struct bsx_train_stats {
+    uint32_t num_visible, num_intersections;
+    float lr_mean;                       /* mean learning rate used by this step */
+    uint32_t step;                       /* optimizer steps taken, this one included */
+} bsx_train_stats;
+
+/* Every rank's splats and gradients for bsx_train_step_dp (own + mapped). */
+typedef struct bsx_dp_splats {
+    float* d_transforms[BSX_MAX_RANKS];
+    float* d_sh_coeffs[BSX_MAX_RANKS];
+    float* d_raw_opac[BSX_MAX_RANKS];
+    float* d_v_transforms[BSX_MAX_RANKS];
+    float* d_v_sh_coeffs[BSX_MAX_RANKS];
+    float* d_v_raw_opac[BSX_MAX_RANKS];
+} bsx_dp_splats;
+
+typedef struct bsx_trainer bsx_trainer;
+BSX_API bsx_status bsx_trainer_create(bsx_ctx* ctx, uint32_t num_splats, uint32_t sh_coeffs_per_splat,
+                                      const bsx_train_config* cfg, bsx_trainer** out);
+BSX_API bsx_status bsx_trainer_destroy(bsx_trainer* tr);
+/* RefineRecord arrays [N] (refine_weight_norm MAX, vis_weight SUM, max_screen_size MAX),
+ * zeroed at creation; valid while the trainer lives. */
+BSX_API bsx_status bsx_trainer_stats_buffers(bsx_trainer* tr, float** d_refine_weight_norm, float** d_vis_weight,
+                                             float** d_max_screen_size);
+/* Dense gradients of the last step ([N,10], [N,C,3], [N], refine weight [N]). */
+BSX_API bsx_status bsx_trainer_grad_buffers(bsx_trainer* tr, float** d_v_transforms, float** d_v_sh_coeffs,
+                                            float** d_v_raw_opac, float** d_v_refine_weight);
+/* One step in place on the splats. d_loss receives the step's mean loss (one float, device). */
+BSX_API bsx_status bsx_train_step(bsx_trainer* tr, const bsx_camera* cam, uint32_t img_w, uint32_t img_h,
+                                  const uint32_t* d_gt_packed, float* d_transforms, float* d_sh_coeffs,
+                                  float* d_raw_opac, int32_t compute_refine_weight, float* d_loss,
+                                  bsx_train_stats* stats);
+/* Data-parallel step: this rank renders its view from its own copy of the
+ * splats, writes its gradients into sp->d_v_*[rank] and ex->d_refine[rank],
+ * then bsx_dp_adam_step (gradient scale 1/world) updates every rank's copy.
+ * The trainer numbers the exchange epochs itself (ex->epoch is ignored), so
+ * every rank's trainer must take the same data-parallel steps on flag words
+ * that no other exchange uses. */
+BSX_API bsx_status bsx_train_step_dp(bsx_trainer* tr, const bsx_camera* cam, uint32_t img_w, uint32_t img_h,
+                                     const uint32_t* d_gt_packed, const bsx_dp_exchange* ex,
+                                     const bsx_dp_splats* sp, int32_t compute_refine_weight, float* d_loss,
+                                     bsx_train_stats* stats);
+
 /* ---- primitives: brush-sort / brush-prefix-sum / get_tile_offsets ---- */
 /* Stable argsort by key & mask(bits rounded up to a multiple of 4), as
  * crates/brush-sort/src/lib.rs:16-129. Inputs are left untouched. */
