@@ -1,13 +1,16 @@
 #!/usr/bin/env python3
 """Benchmark: Brush's differentiable Gaussian-splat training step on B200.
 
-Workload: 1,000,000 splats, SH degree 3, 1920x1080,
-seeded synthetic scene (64 isotropic clusters, sigma 0.3, inside a radius-5
-ball; log-scales N(-4.5,0.7); opacity logits N(0,1.5)), cameras on a radius-8
-orbit, uniform random targets. One step = render forward (backward-pass
-bookkeeping) -> 0.8 L1 + 0.2 (1-SSIM) loss and gradient -> raster backward ->
-projection backward -> [N>1: NCCL all-reduce of the flat gradient] -> fused
-Adam with the reference's learning-rate table -> refine statistics.
+Default workload (the headline metric): 1,000,000 splats,
+SH degree 3, 1920x1080, seeded synthetic scene (64 isotropic clusters, sigma
+0.3, inside a radius-5 ball; log-scales N(-4.5,0.7); opacity logits
+N(0,1.5)), 16 cameras on a radius-8 orbit, uniform random targets. One step =
+render forward (backward-pass bookkeeping) -> 0.8 L1 + 0.2 (1-SSIM) loss and
+gradient -> raster backward -> projection backward -> [N>1: the peer-memory
+gradient exchange fused with Adam] -> fused Adam with the reference's
+learning-rate table -> refine statistics, one bsx_train_step call.
+``--workload`` selects the other BASELINE configurations (cfg1, cfg3 and the
+render-only cfg5) as additional measurements.
 
 With N GPUs (one process per GPU, torchrun) every rank trains on its own view
 against replicated splats each step (weak scaling); value = views/s over all
@@ -45,7 +48,8 @@ def _peaks():
 
 
 class ClockSampler:
-    """Samples nvidia-smi clocks / throttle reasons while the timed region runs."""
+    """Samples nvidia-smi clocks / throttle reasons every 20 ms; keeps the samples that fall
+    inside the timed region (host monotonic clock, bracketed by device synchronisation)."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -55,33 +59,46 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.lines = []
+        self.region = None
 
     def start(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
         except (FileNotFoundError, OSError):
             self.proc = None
+            return
+        deadline = time.monotonic() + 5.0  # nvidia-smi is sampling before the timed region starts
+        while not self.lines and time.monotonic() < deadline and self.proc.poll() is None:
+            time.sleep(0.01)
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.monotonic(), line.strip()))
+
+    def mark(self, t0: float, t1: float) -> None:
+        self.region = (t0, t1)
 
     def stop(self) -> dict:
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        time.sleep(0.25)
+        time.sleep(0.05)
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
+        t0, t1 = self.region if self.region else (float("-inf"), float("inf"))
+        inside = [ln for ts, ln in self.lines if t0 <= ts <= t1]
+        chosen = inside
+        if not chosen and self.lines:  # region shorter than one sample: the nearest sample
+            chosen = [min(self.lines, key=lambda x: abs(x[0] - 0.5 * (t0 + t1)))[1]]
         sm, smax, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in chosen:
             parts = [x.strip() for x in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -94,7 +111,7 @@ class ClockSampler:
                 if v.lower() == "active":
                     reasons.add(nm)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "samples_in_region": len(inside)}
 
 
 # Algorithmic bytes moved by each kernel per launch (fp32 = 4 B). N splats,
@@ -123,6 +140,61 @@ def kernel_bytes(name, N, V, M, Mp, P, T, C, W=1):
     return table.get(name, 0)
 
 
+# ---- workloads (synthetic, seeded) -------------------------
+WORKLOADS = {
+    "cfg1": "cfg1: 16,384 splats SH0 256x256 full train step (fwd+SSIM/L1+bwd+Adam lr 1e-3)",
+    "cfg2": WORKLOAD,
+    "cfg3": "cfg3: 3M splats SH3 1297x840, 200 hemisphere views, full train step (fwd+SSIM/L1+bwd+Adam)",
+    "cfg5": "cfg5: 6M splats SH3 3840x2160 render-only forward (viewer path, packed RGBA8), 120-frame circle",
+}
+
+
+def build_workload(name, dev, world):
+    """(splats, cameras, (w, h), host targets, TrainConfig or None for render-only)."""
+    import torch
+
+    import brush_b200 as bsx
+    from brush_b200 import splats as S
+
+    if name == "cfg1":
+        splats, cam, size, gt = S.config1_scene(dev, seed=1)
+        return splats, [cam], size, [gt.cpu()], bsx.TrainConfig(uniform_lr=1e-3)
+    if name == "cfg2":
+        splats, _, size, _ = S.config2_scene(dev, seed=2)
+        w, h = size
+        cams = [S.orbit_camera(i, 16, 8.0, w, h) for i in range(16)]
+        return splats, cams, size, [S.random_gt(h, w, 1000 + i, "cpu") for i in range(16)], bsx.TrainConfig()
+    if name == "cfg3":
+        splats, cams, size, gts = S.config3_scene(dev, seed=3)
+        return splats, cams, size, [g.cpu() for g in gts], bsx.TrainConfig()
+    if name == "cfg5":
+        splats, size = S.config5_scene(dev, seed=5)
+        cams = S.circle_cameras(120, 8.0, size[0], size[1])
+        return splats, cams, size, None, None
+    raise ValueError(name)
+
+
+def _time_region(args, world, body):
+    """Barrier + sync, CUDA events around body(), sync + barrier; returns the max over ranks (ms)."""
+    import torch
+
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    body()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        torch.distributed.barrier()
+        t = torch.tensor([ms], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
 
@@ -130,116 +202,166 @@ def run_ours(args, rank, world, local_rank):
     dev = torch.device("cuda", local_rank)
     import brush_b200 as bsx
     from brush_b200._context import context
-    from brush_b200.splats import config2_scene, orbit_camera, random_gt
+    from brush_b200.render import render
 
-    pg = None
-    if world > 1:
-        pg = torch.distributed.group.WORLD
-    splats, _, size, _ = config2_scene(dev, seed=2)
+    pg = torch.distributed.group.WORLD if world > 1 else None
+    splats, cams, size, gts_cpu, tcfg = build_workload(args.workload, dev, world)
     w, h = size
-    ncam = 16
-    cams = [orbit_camera(i, ncam, 8.0, w, h) for i in range(ncam)]
-    gts_host = [random_gt(h, w, 1000 + i, "cpu").pin_memory() for i in range(ncam)]
-    gts_dev = [g.to(dev) for g in gts_host]
-    trainer = bsx.SplatTrainer(bsx.TrainConfig(), splats, process_group=pg, exchange=args.exchange)
+    ncam = len(cams)
+    train = tcfg is not None
     ctx = context(dev)
 
     def view(step):
         return (step * world + rank) % ncam
 
-    def step(i, gt=None):
-        k = view(i)
-        return trainer.step(cams[k], size, gts_dev[k] if gt is None else gt, splats)
+    # Training changes the splats and with them the work per step (scales and
+    # opacities grow, and so do the intersections), so every measured region
+    # below restarts from the same snapshot with a fresh trainer and the same
+    # warm-up: the timed region, the per-kernel pass and the end-to-end run
+    # all measure the same steps.
+    snapshot = splats.clone()
+    live = {"splats": splats, "trainer": None}
 
-    for i in range(args.warmup):
-        step(i)
-    torch.cuda.synchronize()
-    if world > 1:
-        torch.distributed.barrier()
+    def restart():
+        if not train:
+            for i in range(args.warmup):
+                step(i)
+            return
+        if live["trainer"] is not None:
+            live["trainer"].close()
+        live["splats"] = snapshot.clone()
+        live["trainer"] = bsx.SplatTrainer(tcfg, live["splats"], process_group=pg, exchange=args.exchange)
+        for i in range(args.warmup):
+            step(i)
 
-    # ---- timed region: device-resident inputs -------------------------------
+    if train:
+        gts_host = [g.pin_memory() for g in gts_cpu]
+        gts_dev = [g.to(dev) for g in gts_host]
+
+        def step(i, gt=None):
+            k = view(i)
+            return live["trainer"].step(cams[k], size, gts_dev[k] if gt is None else gt, live["splats"])
+    else:
+        def step(i, gt=None):
+            k = view(i)
+            return render(cams[k], size, splats.transforms, splats.sh_coeffs, splats.raw_opacities,
+                          raster_pass=bsx._lib.PASS_FORWARD)
+
+    restart()
+
+    # ---- timed region: device-resident inputs, no instrumentation ------------
     sampler = ClockSampler(local_rank)
     sampler.start()
+    l0 = ctx.launches()
+    stats = []
+
+    def timed():
+        for i in range(args.steps):
+            stats.append(step(args.warmup + i))
+
+    h0 = time.monotonic()
+    ms = _time_region(args, world, timed)
+    sampler.mark(h0, time.monotonic())
+    launches = ctx.launches() - l0
+    clocks = sampler.stop()
+
+    # ---- per-kernel table: a separate pass over the same steps with CUDA
+    # events around every launch (kept out of the timed region above) --------
+    restart()
     ctx.profile_reset()
     ctx.profile(True)
-    l0 = ctx.launches()
-    torch.cuda.synchronize()
-    if world > 1:
-        torch.distributed.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    stats = []
-    e0.record()
-    for i in range(args.steps):
-        stats.append(step(args.warmup + i))
-    e1.record()
-    torch.cuda.synchronize()
-    if world > 1:
-        torch.distributed.barrier()
-    ms = e0.elapsed_time(e1)
-    launches = ctx.launches() - l0
+    _time_region(args, world, lambda: [step(args.warmup + i) for i in range(args.steps)])
     ctx.profile(False)
     prof = ctx.profile_read()
-    clocks = sampler.stop()
-    t = torch.tensor([ms], device=dev)
-    if world > 1:
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    ms = float(t.item())
 
-    # ---- e2e: public API with host buffers (GT upload + loss readback) -------
-    torch.cuda.synchronize()
-    if world > 1:
-        torch.distributed.barrier()
-    x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    x0.record()
-    for i in range(args.steps):
-        k = view(args.warmup + args.steps + i)
-        gt = gts_host[k].to(dev, non_blocking=True)
-        st = step(args.warmup + args.steps + i, gt)
-        float(st.loss.item())
-    x1.record()
-    torch.cuda.synchronize()
-    if world > 1:
-        torch.distributed.barrier()
-    e2e_ms = x0.elapsed_time(x1)
-    t = torch.tensor([e2e_ms], device=dev)
-    if world > 1:
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    e2e_ms = float(t.item())
+    # ---- e2e: public API with host buffers ----------------------------------
+    # Training: every step uploads its ground truth from pinned host memory and
+    # reads its loss back into pinned host memory, inside the timed region; the
+    # upload of step i+1 runs on a copy stream while step i computes (double
+    # buffer), as a data loader would. Render-only: every frame's packed image
+    # is copied back to pinned host memory (no tensor input per frame: the
+    # camera travels in the launch parameters).
+    restart()
+    compute = torch.cuda.current_stream()
+    copy = torch.cuda.Stream()
+    base = args.warmup
+    if train:
+        gt_buf = [torch.empty_like(gts_dev[0]) for _ in range(2)]
+        loaded = [torch.cuda.Event() for _ in range(2)]
+        consumed = [torch.cuda.Event() for _ in range(2)]
+        loss_host = torch.empty(args.steps, dtype=torch.float32).pin_memory()
 
-    # fwd+bwd time (render + loss + raster bwd + project bwd) from the profile
-    fwdbwd_names = [n for n in prof if n not in ("adam_kernel",)]
-    fwdbwd_ms = sum(prof[n][0] for n in fwdbwd_names) / args.steps
+        def upload(i):
+            b = i % 2
+            with torch.cuda.stream(copy):
+                if i >= 2:
+                    copy.wait_event(consumed[b])
+                gt_buf[b].copy_(gts_host[view(base + i)], non_blocking=True)
+                loaded[b].record(copy)
 
-    V = int(statistics.mean(s.num_visible for s in stats))
-    M = int(statistics.mean(s.num_intersections for s in stats))
-    out = trainer  # noqa: F841
-    # surviving intersections after the forward early-out
-    Mp = M
-    try:
-        from brush_b200.render import render
+        def e2e():
+            upload(0)
+            for i in range(args.steps):
+                b = i % 2
+                compute.wait_event(loaded[b])
+                if i + 1 < args.steps:
+                    upload(i + 1)
+                st = step(base + i, gt_buf[b])
+                consumed[b].record(compute)
+                loss_host[i:i + 1].copy_(st.loss, non_blocking=True)
 
-        r = render(cams[view(0)], size, splats.transforms, splats.sh_coeffs, splats.raw_opacities)
-        off = r.aux.tile_offsets.reshape(-1, 2).to(torch.int64)
-        Mp = int((off[:, 1] - off[:, 0]).clamp_min(0).sum())
-    except Exception:  # noqa: BLE001
-        pass
+        e2e_sampler = ClockSampler(local_rank)
+        e2e_sampler.start()
+        h1 = time.monotonic()
+        e2e_ms = _time_region(args, world, e2e)
+        e2e_sampler.mark(h1, time.monotonic())
+        clocks_e2e = e2e_sampler.stop()
+        assert torch.isfinite(loss_host).all(), "non-finite loss in the end-to-end run"
+        h2d, d2h = int(w * h * 4), 4
+    else:
+        frames_host = [torch.empty((h, w), dtype=torch.int32).pin_memory() for _ in range(2)]
+
+        def e2e():
+            for i in range(args.steps):
+                out = step(base + i)
+                frames_host[i % 2].copy_(out.out_img, non_blocking=True)
+
+        e2e_sampler = ClockSampler(local_rank)
+        e2e_sampler.start()
+        h1 = time.monotonic()
+        e2e_ms = _time_region(args, world, e2e)
+        e2e_sampler.mark(h1, time.monotonic())
+        clocks_e2e = e2e_sampler.stop()
+        h2d, d2h = 0, int(w * h * 4)
+
+    V = int(statistics.mean(s.num_visible if train else s.aux.num_visible for s in stats))
+    M = int(statistics.mean(s.num_intersections if train else s.aux.num_intersections for s in stats))
+    # surviving intersections after the forward early-out (backward-pass render of one view)
+    sp = live["splats"]
+    r = render(cams[view(args.warmup)], size, sp.transforms, sp.sh_coeffs, sp.raw_opacities)
+    off = r.aux.tile_offsets.reshape(-1, 2).to(torch.int64)
+    Mp = int((off[:, 1] - off[:, 0]).clamp_min(0).sum()) if train else M
     N, C = splats.num_splats, splats.sh_coeffs_per_splat
     P, T = w * h, ((w + 15) // 16) * ((h + 15) // 16)
+    tile_passes = (max(1, T.bit_length()) + 7) // 8
     peak, peak_kind = _peaks()
     kernels = {}
+    total_prof = max(sum(v[0] for v in prof.values()), 1e-9)
     for name, (tot, cnt) in prof.items():
         avg_ms = tot / max(cnt, 1)
         b = kernel_bytes(name, N, V, M, Mp, P, T, C, world)
         if name in ("sort_pass_kernel", "sort_hist_kernel"):
-            # two sorts per step: V depth keys (4 passes) and M tile keys (2 passes at 1080p)
-            per_step = 4 * 16 * V + 2 * 16 * M if name == "sort_pass_kernel" else 4 * V + 4 * M
+            # two sorts per step: V depth keys (4 passes) and M tile keys
+            per_step = (4 * 16 * V + tile_passes * 16 * M) if name == "sort_pass_kernel" else 4 * V + 4 * M
             b = per_step / max(cnt / args.steps, 1)
-        kernels[name] = {"launches": cnt, "avg_ms": round(avg_ms, 4), "share": round(tot / max(sum(v[0] for v in prof.values()), 1e-9), 4),
+        if name == "raster_fwd_kernel" and not train:
+            b = 52 * M + 4 * P + 8 * T
+        kernels[name] = {"launches": cnt, "avg_ms": round(avg_ms, 4), "share": round(tot / total_prof, 4),
                          "alg_bytes": int(b), "gbs": round(b / (avg_ms * 1e-3) / 1e9, 1) if avg_ms > 0 else None}
     dom = max(prof.items(), key=lambda kv: kv[1][0])[0] if prof else None
     traffic = None
     tfile = ROOT / "profiles" / "dram_traffic_cfg2.txt"
-    if tfile.exists() and dom:
+    if args.workload == "cfg2" and tfile.exists() and dom:
         for ln in tfile.read_text().splitlines():
             parts = ln.split()
             if len(parts) == 2 and not ln.startswith("#") and parts[0] == dom:
@@ -253,36 +375,60 @@ def run_ours(args, rank, world, local_rank):
                 "note": "raster kernels are FP32/MUFU issue-bound; HBM fraction is reported as the spec asks"}
     value = args.steps * world / (ms * 1e-3)
     e2e_value = args.steps * world / (e2e_ms * 1e-3)
+    unit = "train steps/s" if train else "frames/s"
     line = {
-        "metric": METRIC, "value": round(value, 3), "unit": "train steps/s", "n_gpus": world, "steps": args.steps,
+        "metric": METRIC if train else "render frames/s @6M splats SH3 2160p; ms per stage",
+        "value": round(value, 3), "unit": unit, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded; no dataset)",
-        "config": {"workload": WORKLOAD, "splats": N, "sh_degree": 3, "width": w, "height": h,
-                   "views_per_step_per_gpu": 1, "parallelism": f"dp{world}", "l2": "inputs larger than L2",
-                   "exchange": (None if world == 1 else
+        "config": {"workload": WORKLOADS[args.workload], "splats": N, "sh_degree": int(round(C ** 0.5)) - 1,
+                   "width": w, "height": h, "views": ncam,
+                   "views_per_step_per_gpu": 1, "parallelism": f"dp{world}",
+                   "l2": "inputs larger than L2" if N * (44 + 12 * C) > 126e6 else "inputs smaller than L2",
+                   "exchange": (None if world == 1 or not train else
                                 "peer-memory fused reduce+Adam+broadcast kernel" if args.exchange == "peer" else
                                 "NCCL reduce-scatter + sharded Adam + all-gather"),
                    "num_visible": V, "num_intersections": M, "intersections_after_early_out": Mp},
-        "fwd_bwd_ms": round(fwdbwd_ms, 4),
-        "e2e": {"value": round(e2e_value, 3), "unit": "train steps/s",
-                "h2d_bytes_per_step": int(w * h * 4), "d2h_bytes_per_step": 4},
+        "e2e": {"value": round(e2e_value, 3), "unit": unit, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": int(launches),
         "roofline": roof,
         "kernels": kernels,
         "clocks": clocks,
+        "clocks_e2e": clocks_e2e,
     }
-    trainer.close()
+    not_fwdbwd = ("adam_kernel", "dp_adam_kernel", "gather_stats_kernel")
+    if train:
+        line["fwd_bwd_ms"] = round(sum(v[0] for n, v in prof.items() if n not in not_fwdbwd) / args.steps, 4)
+        live["trainer"].close()
+    else:
+        stage = {"project": ("project_fwd_kernel", "compact_visible_kernel"), "scan": ("scan_kernel",),
+                 "sort": ("sort_hist_kernel", "sort_pass_kernel"), "emit": ("emit_kernel", "tile_offsets_kernel"),
+                 "rasterize": ("raster_fwd_kernel",)}
+        line["stages_ms"] = {k: round(sum(prof[n][0] for n in v if n in prof) / args.steps, 4) for k, v in stage.items()}
     return line
 
 
-def cpu_baseline_sample(dev_scene=None):
-    """One oracle training step (all host threads) on the same config-2 workload."""
+def cpu_baseline_sample(workload="cfg2"):
+    """One oracle step (all host threads) on the same workload: a full training step, or a
+    forward render for the render-only workload. Returns (seconds, threads)."""
     import numpy as np
 
-    from brush_b200.splats import config2_scene
+    from brush_b200 import splats as S
     from oracle import oracle as orc
 
-    splats, cam, size, gt = config2_scene("cpu", seed=2)
+    if workload == "cfg1":
+        splats, cam, size, gt = S.config1_scene("cpu", seed=1)
+    elif workload == "cfg3":
+        raise ValueError("cfg3 has no CPU sample (its targets are rendered by the GPU library)")
+    elif workload == "cfg5":
+        splats, size = S.config5_scene("cpu", seed=5)
+        cam = S.circle_cameras(120, 8.0, size[0], size[1])[0]
+        t0 = time.perf_counter()
+        orc.RenderResult(cam, size, splats.transforms.numpy(), splats.sh_coeffs.numpy(),
+                         splats.raw_opacities.numpy())
+        return time.perf_counter() - t0, orc.threads()
+    else:
+        splats, cam, size, gt = S.config2_scene("cpu", seed=2)
     t = splats.transforms.numpy()
     sh = splats.sh_coeffs.numpy()
     op = splats.raw_opacities.numpy()
@@ -314,35 +460,42 @@ def run_reference(args, rank, world):
     from oracle import oracle as orc
 
     orc.set_threads(os.cpu_count() or 1)
+    if args.workload == "cfg3":
+        return {"impl": "reference", "unavailable": "cfg3 targets are rendered by the GPU library; no CPU sample"}
     times = []
     for i in range(args.warmup + args.steps):
-        dt, cores = cpu_baseline_sample()
+        dt, cores = cpu_baseline_sample(args.workload)
         if i >= args.warmup:
             times.append(dt)
     total = sum(times)
     value = args.steps / total
+    unit = "frames/s" if args.workload == "cfg5" else "train steps/s"
+    what = "forward render" if args.workload == "cfg5" else "train step"
     return {
-        "impl": "reference", "metric": METRIC, "value": round(value, 5), "unit": "train steps/s", "n_gpus": world,
+        "impl": "reference", "metric": METRIC if args.workload != "cfg5" else "render frames/s @6M splats SH3 2160p",
+        "value": round(value, 5), "unit": unit, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * total / args.steps, 2),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded; no dataset)",
-        "config": {"workload": WORKLOAD, "splats": 1_000_000, "sh_degree": 3, "width": 1920, "height": 1080},
-        "cpu_baseline": {"value": round(value, 5), "unit": "train steps/s", "cores": cores, "kind": "port",
-                         "sample": "full config-2 train step per timed step (CPU restatement of the reference "
-                                   "algorithm; the Rust/wgpu reference cannot be built or run on this box)"},
-        "e2e": {"value": round(value, 5), "unit": "train steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "config": {"workload": WORKLOADS[args.workload]},
+        "cpu_baseline": {"value": round(value, 5), "unit": unit, "cores": cores, "kind": "port",
+                         "sample": f"one full {args.workload} {what} per timed step (CPU restatement of the "
+                                   "reference algorithm; the Rust/wgpu reference cannot be built or run on this box)"},
+        "e2e": {"value": round(value, 5), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                     help="data-parallel gradient exchange with --gpus > 1")
+    ap.add_argument("--workload", default="cfg2", choices=sorted(WORKLOADS),
+                    help="BASELINE configuration (cfg2 is the headline metric)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -369,16 +522,17 @@ def main():
     if world > 1:
         torch.distributed.barrier()
     line = run_ours(args, rank, world, local_rank)
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload != "cfg3":
         from oracle import build as obuild
 
         obuild.build()
         from oracle import oracle as orc
 
         orc.set_threads(os.cpu_count() or 1)
-        dt, cores = cpu_baseline_sample()
-        line["cpu_baseline"] = {"value": round(1.0 / dt, 5), "unit": "train steps/s", "cores": cores, "kind": "port",
-                                "sample": "one full config-2 train step on the CPU restatement, all host threads"}
+        dt, cores = cpu_baseline_sample(args.workload)
+        what = "forward render" if args.workload == "cfg5" else "train step"
+        line["cpu_baseline"] = {"value": round(1.0 / dt, 5), "unit": line["unit"], "cores": cores, "kind": "port",
+                                "sample": f"one full {args.workload} {what} on the CPU restatement, all host threads"}
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()

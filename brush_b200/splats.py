@@ -160,3 +160,32 @@ def config5_scene(device="cuda", seed: int = 5, n: int = 6_000_000):
     """6M splats, SH degree 3, log-scales N(-5,0.8), 3840x2160 (viewer path)."""
     splats = clustered_scene(n, 3, device, seed, log_scale_mean=-5.0, log_scale_std=0.8)
     return splats, (3840, 2160)
+
+
+def perturbed(splats: Splats, seed: int, mean_std: float = 0.02, dc_std: float = 0.05) -> Splats:
+    """A seed-perturbed copy: means + N(0, mean_std), SH DC + N(0, dc_std)."""
+    dev = splats.transforms.device
+    g = _gen(dev, seed)
+    p = splats.clone()
+    p.transforms[:, 0:3] += _normal((p.num_splats, 3), 0.0, mean_std, g, dev)
+    p.sh_coeffs[:, 0, :] += _normal((p.num_splats, 3), 0.0, dc_std, g, dev)
+    return p
+
+
+def config3_scene(device="cuda", seed: int = 3, n: int = 3_000_000, views: int = 200):
+    """3M splats, SH degree 3, config-2 distributions; ``views`` cameras on a radius-8
+    hemisphere at 1297x840. Targets are rendered (by this library's forward pass)
+    from a seed-perturbed copy of the splats, one per view."""
+    from .render import render_splats
+
+    splats = clustered_scene(n, 3, device, seed)
+    w, h = 1297, 840
+    cams = hemisphere_cameras(views, 8.0, w, h, seed=seed)
+    src = perturbed(splats, seed + 7)
+    gts = [render_splats(src, c, (w, h), packed=True)[0].clone() for c in cams]
+    return splats, cams, (w, h), gts
+
+
+def circle_cameras(count: int, radius: float, w: int, h: int, fov_deg: float = 60.0, elevation: float = 0.3):
+    """``count`` cameras on a horizontal circle looking at the origin (viewer path)."""
+    return [orbit_camera(i, count, radius, w, h, fov_deg, elevation) for i in range(count)]
