@@ -12,4 +12,4 @@ from .primitives import get_tile_offsets, prefix_sum, radix_argsort  # noqa: F40
 from .render import RasterPass, RenderOutput, SplatRenderMode, render, render_splats  # noqa: F401
 from .render_bwd import SplatGrads, project_bwd, rasterize_bwd  # noqa: F401
 from .splats import Splats  # noqa: F401
-from .train import SplatTrainer, TrainConfig  # noqa: F401
+from .train import RefineConfig, SplatTrainer, TrainConfig  # noqa: F401

@@ -192,6 +192,33 @@ class DpSplats(C.Structure):
                 ("d_transforms", "d_sh_coeffs", "d_raw_opac", "d_v_transforms", "d_v_sh_coeffs", "d_v_raw_opac")]
 
 
+class RefineConfig(C.Structure):
+    _fields_ = [
+        ("max_splats", C.c_uint32),
+        ("growth_grad_threshold", C.c_float),
+        ("growth_select_fraction", C.c_float),
+        ("growth_stop_iter", C.c_uint32),
+        ("split_at_screen_size", C.c_float),
+        ("opac_decay", C.c_float),
+        ("scale_decay", C.c_float),
+        ("min_scale_prune", C.c_int32),
+        ("min_scale_prune_threshold", C.c_float),
+        ("near_zero_rotation_prune", C.c_int32),
+        ("radial_bounds_prune", C.c_int32),
+        ("min_opacity", C.c_float),
+        ("prune_extent_factor", C.c_float),
+        ("split_long_axis_scale", C.c_float),
+        ("split_other_axis_scale", C.c_float),
+        ("split_opacity_scale", C.c_float),
+        ("seed", C.c_uint64),
+    ]
+
+
+class RefineStats(C.Structure):
+    _fields_ = [(name, C.c_uint32) for name in ("num_added", "num_split_oversized", "num_split_high_grad",
+                                                 "num_pruned", "num_pruned_non_finite", "total_splats")]
+
+
 # name -> (restype, argtypes); exactly the functions include/bsx.h declares.
 SIGNATURES = {
     "bsx_create": (C.c_int, [C.c_int, C.POINTER(C.c_void_p)]),
@@ -262,6 +289,18 @@ SIGNATURES = {
         [C.c_void_p, C.POINTER(Camera), C.c_uint32, C.c_uint32, C.c_void_p, C.POINTER(DpExchange),
          C.POINTER(DpSplats), C.c_int32, C.c_void_p, C.POINTER(TrainStats)],
     ),
+    "bsx_trainer_refine_plan": (
+        C.c_int,
+        [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.POINTER(RefineConfig), C.POINTER(C.c_float),
+         C.POINTER(C.c_float), C.c_uint32, C.POINTER(RefineStats)],
+    ),
+    "bsx_trainer_refine_apply": (
+        C.c_int,
+        [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32,
+         C.c_uint32],
+    ),
+    "bsx_trainer_set_median_scale": (C.c_int, [C.c_void_p, C.c_float]),
+    "bsx_trainer_optimizer_state": (C.c_int, [C.c_void_p] + [C.POINTER(C.c_void_p)] * 6 + [C.POINTER(C.c_uint32)]),
     "bsx_radix_argsort_u32": (
         C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p]
     ),

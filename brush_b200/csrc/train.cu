@@ -19,19 +19,7 @@
 
 #include <vector>
 
-#include "common.cuh"
-
-struct bsx_trainer {
-    bsx_ctx* ctx = nullptr;
-    uint32_t n = 0, coeffs = 0;
-    bsx_train_config cfg{};
-    bsx::DevBuf grads, v_combined, v_output, stats, moments;
-    uint32_t moment_rows = 0;  // rows the moments cover (all, or this rank's shard)
-    int moment_world = 0, moment_rank = -1;
-    uint32_t step = 0;
-    double mean_prev = 0.0, mean_gamma = 1.0, scale_prev = 0.0, scale_gamma = 1.0;
-    uint32_t dp_epoch = 0;
-};
+#include "trainer.cuh"
 
 namespace bsx {
 
@@ -40,13 +28,14 @@ namespace {
 constexpr int kStatsThreads = 256;
 
 // RefineRecord::gather_stats (stats.rs:111-121): running MAX of the refine
-// weight, SUM of visibility, MAX of the screen-space radius.
+// weight, SUM of visibility, MAX of the screen-space radius; without a refine
+// weight (refine == null) gather_aux_stats (stats.rs:123-127).
 __global__ void __launch_bounds__(kStatsThreads)
     gather_stats_kernel(const float* __restrict__ refine, const float* __restrict__ visible,
                         const float* __restrict__ radius, uint32_t n, float* __restrict__ rmax,
                         float* __restrict__ vsum, float* __restrict__ smax) {
     for (uint32_t i = blockIdx.x * kStatsThreads + threadIdx.x; i < n; i += gridDim.x * kStatsThreads) {
-        rmax[i] = bsx_max(rmax[i], refine[i]);
+        if (refine) rmax[i] = bsx_max(rmax[i], refine[i]);
         vsum[i] = vsum[i] + visible[i];
         smax[i] = bsx_max(smax[i], radius[i]);
     }
@@ -105,14 +94,7 @@ bsx_status ensure_moments(bsx_trainer* tr, uint32_t rows, int world, int rank, f
         tr->moment_rank = rank;
         tr->step = 0;
     }
-    float* base = tr->moments.as<float>();
-    // m: [rows,10] | [rows,3C] | [rows,1]; v: [rows,10] | [rows] | [rows,1]
-    m[0] = base;
-    m[1] = m[0] + (size_t)rows * 10;
-    m[2] = m[1] + (size_t)rows * c3;
-    v[0] = m[2] + rows;
-    v[1] = v[0] + (size_t)rows * 10;
-    v[2] = v[1] + rows;
+    moment_views(tr->moments.as<float>(), rows, tr->coeffs, m, v);
     return BSX_OK;
 }
 
@@ -214,10 +196,33 @@ bsx_status bsx_trainer_destroy(bsx_trainer* tr) {
     if (!tr) return BSX_ERR_INVALID_ARG;
     cudaSetDevice(tr->ctx->device);
     if (tr->ctx->stream) cudaStreamSynchronize(tr->ctx->stream);
-    DevBuf* bufs[] = {&tr->grads, &tr->v_combined, &tr->v_output, &tr->stats, &tr->moments};
+    DevBuf* bufs[] = {&tr->grads, &tr->v_combined, &tr->v_output, &tr->stats, &tr->moments, &tr->moments_next,
+                      &tr->plan_keep, &tr->plan_split, &tr->plan_scratch};
     for (DevBuf* b : bufs)
         if (b->p) cudaFree(b->p);
     delete tr;
+    return BSX_OK;
+}
+
+bsx_status bsx_trainer_optimizer_state(bsx_trainer* tr, float** mt, float** ms, float** mo, float** vt, float** vs,
+                                       float** vo, uint32_t* rows) {
+    if (!tr || !mt || !ms || !mo || !vt || !vs || !vo || !rows) return BSX_ERR_INVALID_ARG;
+    float* m[3] = {nullptr, nullptr, nullptr};
+    float* v[3] = {nullptr, nullptr, nullptr};
+    if (tr->moment_rows && tr->moments.p) moment_views(tr->moments.as<float>(), tr->moment_rows, tr->coeffs, m, v);
+    *mt = m[0];
+    *ms = m[1];
+    *mo = m[2];
+    *vt = v[0];
+    *vs = v[1];
+    *vo = v[2];
+    *rows = tr->moment_rows;
+    return BSX_OK;
+}
+
+bsx_status bsx_trainer_set_median_scale(bsx_trainer* tr, float median_scale) {
+    if (!tr || !(median_scale > 0.0f)) return BSX_ERR_INVALID_ARG;
+    tr->cfg.median_scale = median_scale;
     return BSX_OK;
 }
 
@@ -249,6 +254,7 @@ bsx_status bsx_train_step(bsx_trainer* tr, const bsx_camera* cam, uint32_t w, ui
                           bsx_train_stats* stats) {
     if (!tr || !cam || !gt || !d_loss || (tr->n && (!transforms || !sh || !opac))) return BSX_ERR_INVALID_ARG;
     bsx_ctx* ctx = tr->ctx;
+    tr->planned = false;
     cudaSetDevice(ctx->device);
     float *vt, *vs, *vo, *vr;
     bsx_status s0 = bsx_trainer_grad_buffers(tr, &vt, &vs, &vo, &vr);
@@ -272,10 +278,8 @@ bsx_status bsx_train_step(bsx_trainer* tr, const bsx_camera* cam, uint32_t w, ui
         s = bsx_adam_step(ctx, g, 3, &ac);
         if (s != BSX_OK) return s;
     }
-    if (refine) {
-        s = gather_stats(tr, vr, out);
-        if (s != BSX_OK) return s;
-    }
+    s = gather_stats(tr, refine ? vr : nullptr, out);
+    if (s != BSX_OK) return s;
     if (stats) {
         stats->num_visible = out.num_visible;
         stats->num_intersections = out.num_intersections;
@@ -290,6 +294,7 @@ bsx_status bsx_train_step_dp(bsx_trainer* tr, const bsx_camera* cam, uint32_t w,
                              bsx_train_stats* stats) {
     if (!tr || !cam || !gt || !ex || !sp || !d_loss) return BSX_ERR_INVALID_ARG;
     bsx_ctx* ctx = tr->ctx;
+    tr->planned = false;
     const int rank = ex->rank, world = ex->world;
     if (world < 1 || world > BSX_MAX_RANKS || rank < 0 || rank >= world)
         return fail(ctx, BSX_ERR_INVALID_ARG, "rank / world out of range (world <= 8)");
@@ -331,10 +336,8 @@ bsx_status bsx_train_step_dp(bsx_trainer* tr, const bsx_camera* cam, uint32_t w,
     const bsx_adam_cfg ac{0.9f, 0.999f, 1e-15f, tr->step, 1.0f / (float)world};
     s = bsx_dp_adam_step(ctx, &e, g, 3, &ac);
     if (s != BSX_OK) return s;
-    if (refine) {
-        s = gather_stats(tr, ex->d_refine[rank], out);
-        if (s != BSX_OK) return s;
-    }
+    s = gather_stats(tr, refine ? ex->d_refine[rank] : nullptr, out);
+    if (s != BSX_OK) return s;
     if (stats) {
         stats->num_visible = out.num_visible;
         stats->num_intersections = out.num_intersections;

@@ -50,20 +50,31 @@ class Splats:
         return Splats(t, sh_coeffs.contiguous(), raw_opacities.contiguous(), render_mode)
 
 
-def median_size(means: torch.Tensor, percentile: float = 0.8) -> float:
-    """``BoundingBox::median_size`` of the robust percentile AABB (splat_init.rs:130-158,
-    bounding_box.rs:23-29)."""
+def splat_bounds(means: torch.Tensor, percentile: float = 0.8):
+    """Robust percentile AABB of the means as (center, extent), f32 as ``bounds_from_pos``
+    computes it (crates/brush-train/src/splat_init.rs:130-158, bounding_box.rs:8-13)."""
     m = means.detach().float().cpu().numpy()
-    ext = []
+    p = np.float32(percentile)
+    lo_v, hi_v = [], []
     for k in range(3):
-        v = np.sort(m[np.isfinite(m[:, k]), k])
-        if v.size == 0:
-            return 2.0
+        v = m[np.isfinite(m[:, k]), k]
+        if v.size == 0:  # an axis with no finite value: the unit box
+            one = np.ones(3, np.float32)
+            return np.zeros(3, np.float32), one
         n = v.size
-        lo = int((1.0 - percentile) / 2.0 * n)
-        hi = min(n - 1, int((1.0 + percentile) / 2.0 * n))
-        ext.append((v[hi] - v[lo]) / 2.0)
-    return float(sorted(ext)[1] * 2.0)
+        lo = int(np.float32((np.float32(1.0) - p) / np.float32(2.0)) * np.float32(n))
+        hi = min(n - 1, int(np.float32((np.float32(1.0) + p) / np.float32(2.0)) * np.float32(n)))
+        part = np.partition(v, (lo, hi))
+        lo_v.append(part[lo])
+        hi_v.append(part[hi])
+    mn, mx = np.array(lo_v, np.float32), np.array(hi_v, np.float32)
+    return (mx + mn) / np.float32(2.0), (mx - mn) / np.float32(2.0)
+
+
+def median_size(means: torch.Tensor, percentile: float = 0.8) -> float:
+    """``BoundingBox::median_size`` of the robust percentile AABB (bounding_box.rs:23-29)."""
+    _, ext = splat_bounds(means, percentile)
+    return float(np.sort(ext)[1] * np.float32(2.0))
 
 
 def _gen(device, seed):

@@ -32,7 +32,7 @@ from .dist import all_gather_rows, reduce_gradients, reduce_scatter_rows, row_sh
 from .loss import ImageLossConfig, image_loss_fused
 from .render import render
 from .render_bwd import SplatGrads, project_bwd, rasterize_bwd
-from .splats import Splats, median_size
+from .splats import Splats, splat_bounds
 
 
 @dataclass
@@ -69,6 +69,40 @@ class TrainConfig:
         c.render_mode = int(render_mode)
         c.gather_stats = int(gather_stats)
         return c
+
+
+@dataclass
+class RefineConfig:
+    """Refine options of ``TrainConfig`` (crates/brush-train/src/config.rs:100-330) with their defaults."""
+    refine_every: int = 200
+    max_splats: int = 10_000_000
+    growth_grad_threshold: float = 0.0025
+    growth_select_fraction: float = 0.07
+    growth_stop_iter: int = 15000
+    split_at_screen_size: float = 0.5
+    opac_decay: float = 0.004
+    scale_decay: float = 0.002
+    min_scale_prune: bool = True
+    min_scale_prune_threshold: float = 1e-10
+    near_zero_rotation_prune: bool = True
+    radial_bounds_prune: bool = False
+    min_opacity: float = 1.0 / 255.0
+    prune_extent_factor: float = 100.0
+    split_long_axis_scale: float = 0.5
+    split_other_axis_scale: float = 0.85
+    split_opacity_scale: float = 0.6
+    seed: int = 42
+
+    def to_c(self) -> _lib.RefineConfig:
+        c = _lib.RefineConfig()
+        for name, _ in _lib.RefineConfig._fields_:
+            setattr(c, name, type(getattr(c, name))(getattr(self, name)))
+        return c
+
+    def due(self, phase_iter: int, phase_total: int) -> bool:
+        """The training loop's gate (crates/brush-process/src/train_stream.rs:481-483)."""
+        progress = min(max(np.float32(phase_iter) / np.float32(max(phase_total, 1)), 0.0), 1.0)
+        return phase_iter > 0 and phase_iter % self.refine_every == 0 and progress <= 0.95
 
 
 @dataclass
@@ -125,6 +159,18 @@ class _NativeTrainer:
         self.ctx.check(_lib.lib().bsx_trainer_stats_buffers(self.handle, *[C.byref(x) for x in p]))
         return RefineRecord(*[device_view(x.value, (self.n,), torch.float32, self.device) for x in p])
 
+    def optimizer_state(self):
+        """((m_transforms, m_sh, m_opac), (v_transforms, v_sh, v_opac)) views, or None before the first step."""
+        p = [C.c_void_p() for _ in range(6)]
+        rows = C.c_uint32()
+        self.ctx.check(_lib.lib().bsx_trainer_optimizer_state(self.handle, *[C.byref(x) for x in p], C.byref(rows)))
+        r, d = rows.value, self.device
+        if r == 0 or not p[0].value:
+            return None
+        shapes = [(r, 10), (r, self.c, 3), (r,), (r, 10), (r,), (r,)]
+        views = [device_view(x.value, sh, torch.float32, d) for x, sh in zip(p, shapes)]
+        return tuple(views[:3]), tuple(views[3:])
+
     def close(self) -> None:
         if self.handle:
             self.ctx.check(_lib.lib().bsx_trainer_destroy(self.handle))
@@ -153,8 +199,10 @@ class SplatTrainer:
         self.pg = process_group
         self.world = 1 if process_group is None else torch.distributed.get_world_size(process_group)
         self.gather_stats = gather_stats
-        # f32, as BoundingBox::median_size returns it (the rate is lr * median_scale as f64, train.rs:991)
-        self.median_scale = float(np.float32(median_size(splats.means(), config.bounds_percentile)))
+        # trainer bounds (percentile AABB of the means); the rate uses their median size
+        # as f32 (lr * median_scale as f64, train.rs:656,991); refine updates both
+        self.bounds = splat_bounds(splats.means(), config.bounds_percentile)
+        self.median_scale = float(np.float32(np.sort(self.bounds[1])[1] * np.float32(2.0)))
         t = max(config.total_train_iters, 1)
         self.mean_decay = (config.lr_mean_end / config.lr_mean) ** (1.0 / t)
         self.scale_decay = ((config.lr_scale_end / config.lr_scale) ** (1.0 / t)
@@ -299,6 +347,44 @@ class SplatTrainer:
         if self.record is not None and compute_refine_weight:
             self.record.gather_stats(self.grads.v_refine_weight, out.aux.visible, out.aux.max_radius)
         return TrainStepStats(out.aux.num_visible, out.aux.num_intersections, self.loss, lr_mean)
+
+    def refine(self, splats: Splats, global_iter: int, phase_iter: int | None = None, phase_total: int | None = None,
+               refine_config: RefineConfig | None = None) -> _lib.RefineStats:
+        """``SplatTrainer::refine_for_phase`` (crates/brush-train/src/train.rs:1191-1534) in place on
+        ``splats``: prune, replace, split oversized, grow by gradient; the splat tensors are
+        replaced by tensors of the new count and the optimizer state follows the rows."""
+        if self.native is None or self.world > 1:
+            raise NotImplementedError("refine runs on the single-GPU native trainer")
+        cfg = refine_config or RefineConfig()
+        phase_iter = global_iter if phase_iter is None else phase_iter
+        phase_total = self.config.total_train_iters if phase_total is None else phase_total
+        L = _lib.lib()
+        ctx = context(splats.transforms.device)
+        center = (C.c_float * 3)(*[float(v) for v in self.bounds[0]])
+        extent = (C.c_float * 3)(*[float(v) for v in self.bounds[1]])
+        st = _lib.RefineStats()
+        c = cfg.to_c()
+        ctx.check(L.bsx_trainer_refine_plan(self.native.handle, ptr(splats.transforms), ptr(splats.sh_coeffs),
+                                            ptr(splats.raw_opacities), C.byref(c), center, extent, int(global_iter),
+                                            C.byref(st)))
+        n2 = int(st.total_splats)
+        dev = splats.transforms.device
+        nt = torch.empty((n2, 10), device=dev)
+        nsh = torch.empty((n2, self.c, 3), device=dev)
+        nop = torch.empty((n2,), device=dev)
+        ctx.check(L.bsx_trainer_refine_apply(self.native.handle, ptr(splats.transforms), ptr(splats.sh_coeffs),
+                                             ptr(splats.raw_opacities), ptr(nt), ptr(nsh), ptr(nop),
+                                             int(phase_iter), int(phase_total)))
+        splats.transforms, splats.sh_coeffs, splats.raw_opacities = nt, nsh, nop
+        self.n = n2
+        self.native.n = n2
+        self.grads = self.native.grads()
+        self.record = self.native.record()
+        # new bounds and rate scale (train.rs:1506, :656)
+        self.bounds = splat_bounds(splats.means(), self.config.bounds_percentile)
+        self.median_scale = float(np.float32(np.sort(self.bounds[1])[1] * np.float32(2.0)))
+        ctx.check(L.bsx_trainer_set_median_scale(self.native.handle, self.median_scale))
+        return st
 
     def close(self) -> None:
         """Release the exchange region (collective over the process group) and the native trainer."""

@@ -336,6 +336,68 @@ BSX_API bsx_status bsx_train_step_dp(bsx_trainer* tr, const bsx_camera* cam, uin
                                      const bsx_dp_splats* sp, int32_t compute_refine_weight, float* d_loss,
                                      bsx_train_stats* stats);
 
+/* ---- densification: SplatTrainer::refine_for_phase (crates/brush-train/src/train.rs:1191-1534) ----
+ * Two calls, because the splat count changes:
+ *   bsx_trainer_refine_plan decides, from the splats and the trainer's
+ *   RefineRecord: the prune mask (opacity, oversize, out-of-bounds, non-finite,
+ *   tiny scale, degenerate rotation; train.rs:1268-1350), the replacement of
+ *   pruned splats (weighted by opacity x visibility), the forced split of
+ *   splats too large on screen, and gradient-threshold growth; it returns the
+ *   new count in stats->total_splats.
+ *   bsx_trainer_refine_apply writes the refined splats into caller buffers of
+ *   that count (kept rows in order, then one child per split splat), applies
+ *   the long-axis split (train.rs:1547-1700) and the opacity / scale decay
+ *   (train.rs:1700-1740), compacts and zeroes the Adam moments as the
+ *   reference does, resets the RefineRecord and resizes the trainer.
+ * Sampling: weighted sampling without replacement (the reference's
+ * rand::seq::index::sample_weighted, crates/brush-train/src/multinomial.rs),
+ * realised with Efraimidis-Spirakis keys log(u)/w from a counter-based
+ * generator (SplitMix64 of seed, refine count and index): deterministic, and
+ * the same distribution as the reference's, not the same draws. The growth
+ * signal is the gradient norm (error-map / edge-map growth are not built). */
+typedef struct bsx_refine_config {       /* refine options (crates/brush-train/src/config.rs:100-330) */
+    uint32_t max_splats;                 /* 10,000,000 */
+    float growth_grad_threshold;         /* 0.0025 */
+    float growth_select_fraction;        /* 0.07 */
+    uint32_t growth_stop_iter;           /* 15000 */
+    float split_at_screen_size;          /* 0.5 (0 disables) */
+    float opac_decay;                    /* 0.004 */
+    float scale_decay;                   /* 0.002 */
+    int32_t min_scale_prune;             /* 1 */
+    float min_scale_prune_threshold;     /* 1e-10 */
+    int32_t near_zero_rotation_prune;    /* 1 */
+    int32_t radial_bounds_prune;         /* 0: per-axis (L-inf) bounds test */
+    float min_opacity;                   /* 1/255 */
+    float prune_extent_factor;           /* 100 */
+    float split_long_axis_scale;         /* 0.5 */
+    float split_other_axis_scale;        /* 0.85 */
+    float split_opacity_scale;           /* 0.6 */
+    uint64_t seed;
+} bsx_refine_config;
+
+typedef struct bsx_refine_stats {        /* RefineStats (train.rs:1520-1530) */
+    uint32_t num_added, num_split_oversized, num_split_high_grad;
+    uint32_t num_pruned, num_pruned_non_finite, total_splats;
+} bsx_refine_stats;
+
+/* bounds_center / bounds_extent: the trainer's current BoundingBox (percentile
+ * bounds of the means, splat_init.rs:130-158); max_allowed = max extent *
+ * prune_extent_factor. */
+BSX_API bsx_status bsx_trainer_refine_plan(bsx_trainer* tr, const float* d_transforms, const float* d_sh_coeffs,
+                                           const float* d_raw_opac, const bsx_refine_config* cfg,
+                                           const float bounds_center[3], const float bounds_extent[3],
+                                           uint32_t global_iter, bsx_refine_stats* stats);
+BSX_API bsx_status bsx_trainer_refine_apply(bsx_trainer* tr, const float* d_transforms, const float* d_sh_coeffs,
+                                            const float* d_raw_opac, float* d_new_transforms, float* d_new_sh_coeffs,
+                                            float* d_new_raw_opac, uint32_t phase_iter, uint32_t phase_total);
+/* The AdamScaled moments (first m, second v) per group and the rows they cover;
+ * NULL pointers before the first optimizer step. v of the SH group is per row. */
+BSX_API bsx_status bsx_trainer_optimizer_state(bsx_trainer* tr, float** d_m_transforms, float** d_m_sh_coeffs,
+                                               float** d_m_raw_opac, float** d_v_transforms, float** d_v_sh_coeffs,
+                                               float** d_v_raw_opac, uint32_t* rows);
+/* Rate schedule input after the bounds change (train.rs:656: lr_mean uses bounds.median_size()). */
+BSX_API bsx_status bsx_trainer_set_median_scale(bsx_trainer* tr, float median_scale);
+
 /* ---- primitives: brush-sort / brush-prefix-sum / get_tile_offsets ---- */
 /* Stable argsort by key & mask(bits rounded up to a multiple of 4), as
  * crates/brush-sort/src/lib.rs:16-129. Inputs are left untouched. */

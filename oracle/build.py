@@ -13,8 +13,8 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 OUT = HERE / "_build" / "liboracle.so"
-SRC = HERE / "oracle.cpp"
-DEPS = [SRC, HERE.parent / "include" / "bsx.h", HERE.parent / "include" / "bsx_fmath.h"]
+SRCS = [HERE / "oracle.cpp", HERE / "refine.cpp"]
+DEPS = SRCS + [HERE.parent / "include" / "bsx.h", HERE.parent / "include" / "bsx_fmath.h"]
 
 
 def build(force: bool = False) -> Path:
@@ -23,7 +23,7 @@ def build(force: bool = False) -> Path:
         return OUT
     tmp = OUT.with_suffix(".so.tmp")
     cmd = ["g++", "-O3", "-std=c++17", "-fopenmp", "-ffp-contract=off", "-fno-fast-math", "-fPIC", "-shared",
-           str(SRC), "-o", str(tmp)]
+           *[str(x) for x in SRCS], "-o", str(tmp)]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"oracle build failed:\n{res.stderr}")

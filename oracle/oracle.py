@@ -36,6 +36,23 @@ class LossCfg(C.Structure):
                 ("bg", C.c_float * 3), ("mask", C.c_int32)]
 
 
+class RefineCfg(C.Structure):
+    """bsx_refine_config (include/bsx.h)."""
+    _fields_ = [("max_splats", C.c_uint32), ("growth_grad_threshold", C.c_float),
+                ("growth_select_fraction", C.c_float), ("growth_stop_iter", C.c_uint32),
+                ("split_at_screen_size", C.c_float), ("opac_decay", C.c_float), ("scale_decay", C.c_float),
+                ("min_scale_prune", C.c_int32), ("min_scale_prune_threshold", C.c_float),
+                ("near_zero_rotation_prune", C.c_int32), ("radial_bounds_prune", C.c_int32),
+                ("min_opacity", C.c_float), ("prune_extent_factor", C.c_float),
+                ("split_long_axis_scale", C.c_float), ("split_other_axis_scale", C.c_float),
+                ("split_opacity_scale", C.c_float), ("seed", C.c_uint64)]
+
+
+class RefineStats(C.Structure):
+    _fields_ = [(name, C.c_uint32) for name in ("num_added", "num_split_oversized", "num_split_high_grad",
+                                                 "num_pruned", "num_pruned_non_finite", "total_splats")]
+
+
 def lib() -> C.CDLL:
     global _lib
     if _lib is None:
@@ -68,6 +85,20 @@ def lib() -> C.CDLL:
         _lib.orc_tile_offsets.argtypes = [u32p, C.c_uint32, C.c_uint32, u32p]
         _lib.orc_rasterize_rows.argtypes = [f32p, C.c_uint32, C.c_uint32, C.c_uint32, f32p, C.c_int, f32p]
         _lib.orc_gauss_taps.argtypes = [f32p]
+        u8p = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
+        _lib.orc_refine_prune_mask.argtypes = [f32p, f32p, f32p, C.c_uint32, C.c_uint32, C.POINTER(RefineCfg), f32p,
+                                               C.c_float, u8p]
+        _lib.orc_refine_plan.restype = C.c_void_p
+        _lib.orc_refine_plan.argtypes = [f32p, f32p, f32p, f32p, f32p, f32p, C.c_uint32, C.c_uint32,
+                                         C.POINTER(RefineCfg), f32p, f32p, C.c_uint32, C.c_uint32,
+                                         C.POINTER(RefineStats)]
+        _lib.orc_refine_plan_rows.argtypes = [C.c_void_p, u32p, u32p]
+        _lib.orc_refine_apply.argtypes = [C.c_void_p] + [f32p] * 18 + [C.c_uint32, C.c_uint32]
+        _lib.orc_refine_free.argtypes = [C.c_void_p]
+        _lib.orc_weighted_sample.restype = C.c_uint32
+        _lib.orc_weighted_sample.argtypes = [f32p, C.c_uint32, C.c_uint32, C.c_uint64, C.c_uint32, u32p]
+        _lib.orc_refine_uniform.restype = C.c_float
+        _lib.orc_refine_uniform.argtypes = [C.c_uint64, C.c_uint32, C.c_uint32]
         _lib.orc_expf.restype = C.c_float
         _lib.orc_expf.argtypes = [C.c_float]
         _lib.orc_logf.restype = C.c_float
@@ -252,3 +283,66 @@ def expf(x: float) -> float:
 
 def logf(x: float) -> float:
     return float(lib().orc_logf(float(x)))
+
+
+def refine_cfg(**kw) -> RefineCfg:
+    """bsx_refine_config with the reference defaults (config.rs:100-330), overridden by kw."""
+    d = dict(max_splats=10_000_000, growth_grad_threshold=0.0025, growth_select_fraction=0.07,
+             growth_stop_iter=15000, split_at_screen_size=0.5, opac_decay=0.004, scale_decay=0.002,
+             min_scale_prune=1, min_scale_prune_threshold=1e-10, near_zero_rotation_prune=1,
+             radial_bounds_prune=0, min_opacity=1.0 / 255.0, prune_extent_factor=100.0,
+             split_long_axis_scale=0.5, split_other_axis_scale=0.85, split_opacity_scale=0.6, seed=42)
+    d.update(kw)
+    c = RefineCfg()
+    for k, v in d.items():
+        setattr(c, k, v)
+    return c
+
+
+def refine_prune_mask(t, sh, op, cfg, center, max_allowed):
+    n = t.shape[0]
+    out = np.empty(n, np.uint8)
+    lib().orc_refine_prune_mask(_f32(t).reshape(-1), _f32(sh).reshape(-1), _f32(op).reshape(-1), n,
+                                _f32(sh).reshape(n, -1).shape[1] // 3 if n else 1, C.byref(cfg),
+                                _f32(center), float(max_allowed), out)
+    return out
+
+
+def refine(t, sh, op, record, moments, cfg, center, extent, global_iter, refine_count, phase_iter, phase_total):
+    """Prune / replace / split / grow (train.rs:1191-1860). record = (refine_norm, vis, screen);
+    moments = ((m_t [n,10], m_s [n,3C], m_o [n]), (v_t [n,10], v_s [n], v_o [n])). Returns
+    dict(stats, keep, split, transforms, sh, opac, m, v)."""
+    n, c = t.shape[0], sh.shape[1]
+    st = RefineStats()
+    h = lib().orc_refine_plan(_f32(t).reshape(-1), _f32(sh).reshape(-1), _f32(op).reshape(-1),
+                              *[_f32(x).reshape(-1) for x in record], n, c, C.byref(cfg), _f32(center),
+                              _f32(extent), int(global_iter), int(refine_count), C.byref(st))
+    try:
+        K = st.total_splats - st.num_added
+        keep = np.empty(max(K, 1), np.uint32)
+        split = np.empty(max(st.num_added, 1), np.uint32)
+        lib().orc_refine_plan_rows(h, keep, split)
+        n2 = st.total_splats
+        nt, nsh, nop = np.empty((n2, 10), np.float32), np.empty((n2, c, 3), np.float32), np.empty(n2, np.float32)
+        nm = (np.empty((n2, 10), np.float32), np.empty((n2, 3 * c), np.float32), np.empty(n2, np.float32))
+        nv = (np.empty((n2, 10), np.float32), np.empty(n2, np.float32), np.empty(n2, np.float32))
+        (m_t, m_s, m_o), (v_t, v_s, v_o) = moments
+        lib().orc_refine_apply(h, _f32(t).reshape(-1), _f32(sh).reshape(-1), _f32(op).reshape(-1),
+                               *[_f32(x).reshape(-1) for x in (m_t, m_s, m_o, v_t, v_s, v_o)],
+                               nt.reshape(-1), nsh.reshape(-1), nop, *[x.reshape(-1) for x in nm + nv],
+                               int(phase_iter), int(phase_total))
+    finally:
+        lib().orc_refine_free(h)
+    return dict(stats=st, keep=keep[:K], split=split[:st.num_added], transforms=nt, sh=nsh, opac=nop, m=nm, v=nv)
+
+
+def refine_uniform(seed, stream, index) -> float:
+    return float(lib().orc_refine_uniform(int(seed), int(stream), int(index)))
+
+
+def weighted_sample(w, k, seed=42, stream=0):
+    """Up to k distinct indices drawn without replacement with probability proportional to w."""
+    w = _f32(w)
+    out = np.empty(max(k, 1), np.uint32)
+    m = lib().orc_weighted_sample(w, w.size, int(k), int(seed), int(stream), out)
+    return out[:m].astype(np.int64)

@@ -1,0 +1,95 @@
+"""Densification on the GPU (bsx_trainer_refine_plan / _apply) against the
+oracle restatement of refine_for_phase (crates/brush-train/src/train.rs:1191-1860):
+same prune decisions, same draws, same split arithmetic, same optimizer-state
+remap, bit for bit; then training continues at the new count."""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _snapshot(tr, splats):
+    n = splats.num_splats
+    rec = tr.record
+    state = tr.native.optimizer_state()
+    (m_t, m_s, m_o), (v_t, v_s, v_o) = state
+    c = splats.sh_coeffs_per_splat
+    return dict(
+        t=splats.transforms.cpu().numpy().copy(), sh=splats.sh_coeffs.cpu().numpy().copy(),
+        op=splats.raw_opacities.cpu().numpy().copy(),
+        record=tuple(x.cpu().numpy().copy() for x in (rec.refine_weight_norm, rec.vis_weight, rec.max_screen_size)),
+        moments=((m_t.cpu().numpy().copy(), m_s.reshape(n, 3 * c).cpu().numpy().copy(), m_o.cpu().numpy().copy()),
+                 (v_t.cpu().numpy().copy(), v_s.cpu().numpy().copy(), v_o.cpu().numpy().copy())),
+        bounds=(tr.bounds[0].copy(), tr.bounds[1].copy()))
+
+
+def _check(tr, splats, snap, ref, st):
+    for f in ("num_added", "num_split_oversized", "num_split_high_grad", "num_pruned", "num_pruned_non_finite",
+              "total_splats"):
+        assert getattr(st, f) == getattr(ref["stats"], f), f
+    np.testing.assert_array_equal(splats.transforms.cpu().numpy(), ref["transforms"])
+    np.testing.assert_array_equal(splats.sh_coeffs.cpu().numpy(), ref["sh"])
+    np.testing.assert_array_equal(splats.raw_opacities.cpu().numpy(), ref["opac"])
+    n2 = st.total_splats
+    (m_t, m_s, m_o), (v_t, v_s, v_o) = tr.native.optimizer_state()
+    got_m = (m_t.cpu().numpy(), m_s.reshape(n2, -1).cpu().numpy(), m_o.cpu().numpy())
+    got_v = (v_t.cpu().numpy(), v_s.cpu().numpy(), v_o.cpu().numpy())
+    for a, b in zip(got_m + got_v, ref["m"] + ref["v"]):
+        np.testing.assert_array_equal(a, b)
+    rec = tr.record
+    assert rec.vis_weight.shape[0] == n2 and not rec.vis_weight.any() and not rec.refine_weight_norm.any()
+    assert tr.n == n2 and splats.num_splats == n2
+
+
+def test_refine_matches_oracle_and_training_continues(cuda, orc):
+    import brush_b200 as bsx
+    from brush_b200.splats import clustered_scene, orbit_camera, random_gt
+
+    splats = clustered_scene(30000, 1, "cpu", seed=21, log_scale_mean=-2.5).to("cuda")
+    w, h = 256, 192
+    cams = [orbit_camera(i, 4, 8.0, w, h) for i in range(4)]
+    gts = [random_gt(h, w, 70 + i, "cpu").cuda() for i in range(4)]
+    tr = bsx.SplatTrainer(bsx.TrainConfig(), splats)
+    for k in range(6):
+        tr.step(cams[k % 4], (w, h), gts[k % 4], splats)
+    # prune cases the training alone would not produce
+    with torch.no_grad():
+        splats.raw_opacities[:50] = -12.0
+        splats.transforms[50:55, 0] = 1e4
+        splats.transforms[55, 8] = float("nan")
+        splats.transforms[56, 3:7] = 1e-6
+        splats.transforms[57, 7] = -40.0
+    cfg = bsx.RefineConfig(growth_grad_threshold=2e-5, growth_select_fraction=0.3, split_at_screen_size=0.05,
+                           seed=1234)
+    for r in range(2):
+        torch.cuda.synchronize()
+        snap = _snapshot(tr, splats)
+        n = snap["t"].shape[0]
+        st = tr.refine(splats, global_iter=200 * (r + 1), phase_iter=200 * (r + 1), phase_total=3000,
+                       refine_config=cfg)
+        ref = orc.refine(snap["t"], snap["sh"], snap["op"], snap["record"], snap["moments"],
+                         orc.refine_cfg(growth_grad_threshold=2e-5, growth_select_fraction=0.3,
+                                        split_at_screen_size=0.05, seed=1234),
+                         snap["bounds"][0], snap["bounds"][1], 200 * (r + 1), r, 200 * (r + 1), 3000)
+        torch.cuda.synchronize()
+        _check(tr, splats, snap, ref, st)
+        if r == 0:
+            assert st.num_pruned >= 58 and st.num_pruned_non_finite >= 1
+            assert st.num_added > 0 and st.num_split_high_grad > 0
+        for k in range(4):
+            s2 = tr.step(cams[k], (w, h), gts[k], splats)
+            assert np.isfinite(float(s2.loss.item()))
+    tr.close()
+
+
+def test_refine_refuses_without_statistics(cuda):
+    import brush_b200 as bsx
+    from brush_b200.splats import config1_scene
+
+    splats, cam, size, gt = config1_scene("cuda", seed=3)
+    tr = bsx.SplatTrainer(bsx.TrainConfig(uniform_lr=1e-3), splats, gather_stats=False)
+    tr.step(cam, size, gt.cuda(), splats)
+    with pytest.raises(bsx.BsxError):
+        tr.refine(splats, 100)
+    tr.close()
