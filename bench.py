@@ -145,6 +145,8 @@ WORKLOADS = {
     "cfg1": "cfg1: 16,384 splats SH0 256x256 full train step (fwd+SSIM/L1+bwd+Adam lr 1e-3)",
     "cfg2": WORKLOAD,
     "cfg3": "cfg3: 3M splats SH3 1297x840, 200 hemisphere views, full train step (fwd+SSIM/L1+bwd+Adam)",
+    "cfg4": ("cfg4: densification run from 100k splats SH3 1280x720, 100 hemisphere views, refine every 100 "
+             "steps (growth threshold 2e-4, prune opacity < 0.005, growth fraction 0.1, cap 1.5M)"),
     "cfg5": "cfg5: 6M splats SH3 3840x2160 render-only forward (viewer path, packed RGBA8), 120-frame circle",
 }
 
@@ -167,6 +169,12 @@ def build_workload(name, dev, world):
     if name == "cfg3":
         splats, cams, size, gts = S.config3_scene(dev, seed=3)
         return splats, cams, size, [g.cpu() for g in gts], bsx.TrainConfig()
+    if name == "cfg4":
+        splats = S.clustered_scene(100_000, 3, dev, seed=4)
+        w, h = 1280, 720
+        cams = S.hemisphere_cameras(100, 8.0, w, h, seed=4)
+        return splats, cams, (w, h), [S.random_gt(h, w, 4000 + i, "cpu") for i in range(100)], \
+            bsx.TrainConfig(total_train_iters=3000)
     if name == "cfg5":
         splats, size = S.config5_scene(dev, seed=5)
         cams = S.circle_cameras(120, 8.0, size[0], size[1])
@@ -210,6 +218,13 @@ def run_ours(args, rank, world, local_rank):
     ncam = len(cams)
     train = tcfg is not None
     ctx = context(dev)
+    refine_cfg = None
+    if args.workload == "cfg4":
+        if world > 1:
+            raise SystemExit("cfg4 (densification) runs on one GPU")
+        refine_cfg = bsx.RefineConfig(refine_every=100, growth_grad_threshold=2e-4, min_opacity=0.005,
+                                      growth_select_fraction=0.1, max_splats=1_500_000)
+    refines = []
 
     def view(step):
         return (step * world + rank) % ncam
@@ -223,6 +238,11 @@ def run_ours(args, rank, world, local_rank):
     live = {"splats": splats, "trainer": None}
 
     def restart():
+        # every region starts from an empty workspace, so buffer growth (a
+        # densification run grows it repeatedly) costs every region the same
+        refines.clear()
+        torch.cuda.synchronize()
+        ctx.trim()
         if not train:
             for i in range(args.warmup):
                 step(i)
@@ -231,6 +251,8 @@ def run_ours(args, rank, world, local_rank):
             live["trainer"].close()
         live["splats"] = snapshot.clone()
         live["trainer"] = bsx.SplatTrainer(tcfg, live["splats"], process_group=pg, exchange=args.exchange)
+        if refine_cfg is not None:  # the run's splat budget is allocated once, before timing
+            live["trainer"].reserve(refine_cfg.max_splats, live["splats"])
         for i in range(args.warmup):
             step(i)
 
@@ -240,7 +262,12 @@ def run_ours(args, rank, world, local_rank):
 
         def step(i, gt=None):
             k = view(i)
-            return live["trainer"].step(cams[k], size, gts_dev[k] if gt is None else gt, live["splats"])
+            st = live["trainer"].step(cams[k], size, gts_dev[k] if gt is None else gt, live["splats"])
+            it = i + 1
+            if refine_cfg is not None and refine_cfg.due(it, tcfg.total_train_iters):
+                rs = live["trainer"].refine(live["splats"], it, it, tcfg.total_train_iters, refine_cfg)
+                refines.append((it, rs.total_splats, rs.num_added, rs.num_pruned))
+            return st
     else:
         def step(i, gt=None):
             k = view(i)
@@ -259,9 +286,12 @@ def run_ours(args, rank, world, local_rank):
         for i in range(args.steps):
             stats.append(step(args.warmup + i))
 
+    refines.clear()
     h0 = time.monotonic()
     ms = _time_region(args, world, timed)
     sampler.mark(h0, time.monotonic())
+    timed_refines = list(refines)
+    timed_n = live["splats"].num_splats
     launches = ctx.launches() - l0
     clocks = sampler.stop()
 
@@ -397,6 +427,11 @@ def run_ours(args, rank, world, local_rank):
         "clocks_e2e": clocks_e2e,
     }
     not_fwdbwd = ("adam_kernel", "dp_adam_kernel", "gather_stats_kernel")
+    if refine_cfg is not None:
+        line["refine"] = {"every": refine_cfg.refine_every, "refines_in_timed_region": len(timed_refines),
+                          "start_splats": N, "end_splats": timed_n,
+                          "log": [{"iter": r[0], "splats": r[1], "added": r[2], "pruned": r[3]}
+                                  for r in timed_refines]}
     if train:
         line["fwd_bwd_ms"] = round(sum(v[0] for n, v in prof.items() if n not in not_fwdbwd) / args.steps, 4)
         live["trainer"].close()

@@ -52,6 +52,10 @@ class Context:
             out[name.value.decode()] = (ms.value, int(cnt.value))
         return out
 
+    def trim(self) -> None:
+        """Release the grow-only workspace (reallocated on demand)."""
+        self.check(_lib.lib().bsx_trim(self.handle))
+
     def sync(self) -> None:
         self.check(_lib.lib().bsx_sync(self.handle))
 

@@ -224,6 +224,7 @@ SIGNATURES = {
     "bsx_create": (C.c_int, [C.c_int, C.POINTER(C.c_void_p)]),
     "bsx_destroy": (C.c_int, [C.c_void_p]),
     "bsx_set_stream": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "bsx_trim": (C.c_int, [C.c_void_p]),
     "bsx_sync": (C.c_int, [C.c_void_p]),
     "bsx_last_error": (C.c_char_p, [C.c_void_p]),
     "bsx_status_string": (C.c_char_p, [C.c_int]),
@@ -300,6 +301,7 @@ SIGNATURES = {
          C.c_uint32],
     ),
     "bsx_trainer_set_median_scale": (C.c_int, [C.c_void_p, C.c_float]),
+    "bsx_trainer_reserve": (C.c_int, [C.c_void_p, C.c_uint32]),
     "bsx_trainer_optimizer_state": (C.c_int, [C.c_void_p] + [C.POINTER(C.c_void_p)] * 6 + [C.POINTER(C.c_uint32)]),
     "bsx_radix_argsort_u32": (
         C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p]

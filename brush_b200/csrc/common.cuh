@@ -125,6 +125,8 @@ namespace bsx {
 bsx_status fail(bsx_ctx* ctx, bsx_status s, const std::string& msg);
 bsx_status check_cuda(bsx_ctx* ctx, cudaError_t e, const char* what);
 bsx_status ensure(bsx_ctx* ctx, DevBuf& b, size_t bytes);
+// Stream-ordered release of a workspace buffer.
+void release(bsx_ctx* ctx, DevBuf& b);
 // Records a start event before a kernel launch when profiling is on.
 void prof_begin(bsx_ctx* ctx);
 // Checks the launch that was just enqueued and counts it.

@@ -18,20 +18,23 @@ bsx_status check_cuda(bsx_ctx* ctx, cudaError_t e, const char* what) {
     return fail(ctx, BSX_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
 }
 
+// Workspace memory is stream-ordered (cudaMallocAsync / cudaFreeAsync on the
+// context's stream, from the device's default pool, which keeps what it
+// frees): growing a buffer neither synchronises the device nor waits for the
+// stream, and the old buffer is released only after the work queued before it.
+void release(bsx_ctx* ctx, DevBuf& b) {
+    if (b.p) cudaFreeAsync(b.p, ctx->stream);
+    b.p = nullptr;
+    b.cap = 0;
+}
+
 bsx_status ensure(bsx_ctx* ctx, DevBuf& b, size_t bytes) {
     if (bytes == 0) bytes = 16;
     if (bytes <= b.cap) return BSX_OK;
-    size_t nb = bytes + bytes / 4;
+    size_t nb = bytes + bytes / 2;  // headroom: a growing splat count reallocates rarely
     nb = (nb + 255) & ~size_t(255);
-    if (b.p) {
-        // The stream may still be reading the old buffer.
-        cudaError_t e = cudaStreamSynchronize(ctx->stream);
-        if (e != cudaSuccess) return check_cuda(ctx, e, "cudaStreamSynchronize");
-        cudaFree(b.p);
-        b.p = nullptr;
-        b.cap = 0;
-    }
-    cudaError_t e = cudaMalloc(&b.p, nb);
+    release(ctx, b);
+    cudaError_t e = cudaMallocAsync(&b.p, nb, ctx->stream);
     if (e != cudaSuccess) {
         b.p = nullptr;
         return fail(ctx, BSX_ERR_CUDA, std::string("workspace allocation of ") + std::to_string(nb) +
@@ -118,6 +121,13 @@ bsx_status bsx_create(int device, bsx_ctx** out) {
     if (e == cudaSuccess) e = cudaMalloc(&ctx->d_err, 256);
     if (e == cudaSuccess) e = cudaMemset(ctx->d_err, 0, 256);
     if (e == cudaSuccess) e = cudaMallocHost(&ctx->h_pinned, 64 * sizeof(uint32_t));
+    if (e == cudaSuccess) {
+        // workspace growth reuses freed blocks instead of returning them to the device
+        cudaMemPool_t pool;
+        e = cudaDeviceGetDefaultMemPool(&pool, device);
+        uint64_t keep = UINT64_MAX;
+        if (e == cudaSuccess) e = cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+    }
     if (e != cudaSuccess) {
         if (ctx->d_err) cudaFree(ctx->d_err);
         delete ctx;
@@ -137,8 +147,9 @@ bsx_status bsx_destroy(bsx_ctx* ctx) {
                       &ctx->image_packed, &ctx->visible, &ctx->max_radius, &ctx->sort_tmp_k, &ctx->sort_tmp_v,
                       &ctx->sort_hist, &ctx->sort_lookback, &ctx->scan_status, &ctx->scalars, &ctx->grad,
                       &ctx->loss_partials, &ctx->sort_keys_b, &ctx->sort_vals_b};
-    for (DevBuf* b : bufs)
-        if (b->p) cudaFree(b->p);
+    for (DevBuf* b : bufs) release(ctx, *b);
+    if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    else cudaDeviceSynchronize();
     if (ctx->d_err) cudaFree(ctx->d_err);
     if (ctx->h_pinned) cudaFreeHost(ctx->h_pinned);
     for (auto& r : ctx->prof_pending) {
@@ -147,6 +158,26 @@ bsx_status bsx_destroy(bsx_ctx* ctx) {
     }
     for (cudaEvent_t e : ctx->prof_pool) cudaEventDestroy(e);
     delete ctx;
+    return BSX_OK;
+}
+
+bsx_status bsx_trim(bsx_ctx* ctx) {
+    if (!ctx) return BSX_ERR_INVALID_ARG;
+    cudaSetDevice(ctx->device);
+    cudaError_t e = ctx->stream ? cudaStreamSynchronize(ctx->stream) : cudaDeviceSynchronize();
+    if (e != cudaSuccess) return check_cuda(ctx, e, "synchronise before trim");
+    DevBuf* bufs[] = {&ctx->projected, &ctx->counts, &ctx->depth_keys, &ctx->vis_gid, &ctx->depth_order,
+                      &ctx->cum, &ctx->isect_tile, &ctx->isect_gid, &ctx->tile_offsets, &ctx->image,
+                      &ctx->image_packed, &ctx->visible, &ctx->max_radius, &ctx->sort_tmp_k, &ctx->sort_tmp_v,
+                      &ctx->sort_hist, &ctx->sort_lookback, &ctx->scan_status, &ctx->scalars, &ctx->grad,
+                      &ctx->loss_partials, &ctx->sort_keys_b, &ctx->sort_vals_b};
+    for (DevBuf* b : bufs) release(ctx, *b);
+    ctx->fwd.valid = 0;
+    e = ctx->stream ? cudaStreamSynchronize(ctx->stream) : cudaDeviceSynchronize();
+    if (e != cudaSuccess) return check_cuda(ctx, e, "synchronise after trim");
+    // hand the pool's unused memory back to the device
+    cudaMemPool_t pool;
+    if (cudaDeviceGetDefaultMemPool(&pool, ctx->device) == cudaSuccess) cudaMemPoolTrimTo(pool, 0);
     return BSX_OK;
 }
 

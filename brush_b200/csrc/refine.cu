@@ -3,15 +3,16 @@
 // Restates SplatTrainer::refine_for_phase, refine_splats and prune_points
 // (crates/brush-train/src/train.rs:1191-1860) with the gradient-norm growth
 // signal. Decisions and parameter arithmetic run on the device; only counts
-// and the (small) sampled index lists come back to the host, where the split
-// set is merged in the reference's order (replacement, oversized, growth).
+// come back to the host. The split set is merged in the reference's order
+// (replacement, oversized, growth) as flags over the kept rows.
 //
 //   plan:  refine_mask_kernel (prune predicates, train.rs:1258-1350) ->
 //          ordered compaction of the kept ids (scan + scatter) ->
 //          sample_keys_kernel + radix sort: weighted sampling without
 //          replacement as the k largest Efraimidis-Spirakis keys log(u)/w
 //          (u from SplitMix64 of seed, refine count, stream, index) ->
-//          oversized candidates (compaction) -> host merge.
+//          oversized candidates -> the split set as device flags (the
+//          host sees only counts) -> ordered compaction of the split rows.
 //   apply: gather_rows_kernel (kept rows of splats and Adam moments) ->
 //          split_kernel (long-axis split of every selected splat, child
 //          appended, both halves' moments zeroed, train.rs:1547-1700) ->
@@ -19,8 +20,6 @@
 // Every per-element expression is evaluated in the reference's order, so the
 // host restatement in the oracle matches bit for bit.
 #include <algorithm>
-#include <set>
-#include <vector>
 
 #include "trainer.cuh"
 
@@ -146,15 +145,41 @@ __global__ void __launch_bounds__(kRefThreads) sample_keys_kernel(const __grid_c
     }
 }
 
-__global__ void __launch_bounds__(kRefThreads) oversized_kernel(const uint32_t* __restrict__ keep, uint32_t K,
-                                                                const float* __restrict__ screen,
-                                                                const float* __restrict__ vis, float thr,
-                                                                uint32_t* __restrict__ flag) {
+// Marks the first `take` sampled rows as split (no duplicates within one draw);
+// counts the rows that were not marked before.
+__global__ void __launch_bounds__(kRefThreads) mark_sampled_kernel(const uint32_t* __restrict__ vals, uint32_t take,
+                                                                   uint32_t* __restrict__ mark,
+                                                                   uint32_t* __restrict__ fresh) {
+    const uint32_t i = blockIdx.x * kRefThreads + threadIdx.x;
+    bool is_new = false;
+    if (i < take) {
+        const uint32_t j = vals[i];
+        is_new = mark[j] == 0u;
+        mark[j] = 1u;
+    }
+    const uint32_t c = __popc(__ballot_sync(0xffffffffu, is_new));
+    if ((threadIdx.x & 31) == 0 && c) atomicAdd(fresh, c);
+}
+
+// Oversized candidates not yet in the split set, in row order.
+__global__ void __launch_bounds__(kRefThreads) oversized_new_kernel(const uint32_t* __restrict__ keep, uint32_t K,
+                                                                    const float* __restrict__ screen,
+                                                                    const float* __restrict__ vis, float thr,
+                                                                    const uint32_t* __restrict__ mark,
+                                                                    uint32_t* __restrict__ flag) {
     const uint32_t j = blockIdx.x * kRefThreads + threadIdx.x;
     if (j < K) {
         const uint32_t i = keep[j];
-        flag[j] = (screen[i] > thr && vis[i] > 0.0f) ? 1u : 0u;
+        flag[j] = (screen[i] > thr && vis[i] > 0.0f && mark[j] == 0u) ? 1u : 0u;
     }
+}
+
+// The first `budget` new candidates join the split set (train.rs:1410-1421).
+__global__ void __launch_bounds__(kRefThreads) mark_budget_kernel(const uint32_t* __restrict__ flag,
+                                                                  const uint32_t* __restrict__ pos, uint32_t K,
+                                                                  uint32_t budget, uint32_t* __restrict__ mark) {
+    const uint32_t j = blockIdx.x * kRefThreads + threadIdx.x;
+    if (j < K && flag[j] && pos[j] <= budget) mark[j] = 1u;
 }
 
 // dst[j, :] = src[idx[j], :] for j < rows (cols floats per row).
@@ -275,9 +300,12 @@ bsx_status read_u32(bsx_ctx* ctx, const uint32_t* d, uint32_t count, uint32_t* h
     return check_device_error(ctx);
 }
 
-// Weighted sample without replacement of up to k kept rows; stream picks the draw.
+// Weighted sample without replacement of up to k kept rows (stream picks the
+// draw); the drawn rows are marked in `mark`. Returns through `drawn_new` how
+// many of them were not marked before, and through `above_count` the rows
+// above the growth threshold.
 bsx_status weighted_sample(bsx_trainer* tr, const float* op, int growth, uint32_t k, uint32_t stream,
-                           uint32_t* scratch, uint32_t* above_count, std::vector<uint32_t>* out) {
+                           uint32_t* scratch, uint32_t* mark, uint32_t* above_count, uint32_t* drawn_new) {
     bsx_ctx* ctx = tr->ctx;
     const uint32_t K = tr->plan_kept, n = tr->plan_n;
     float* st = tr->stats.as<float>();
@@ -286,7 +314,7 @@ bsx_status weighted_sample(bsx_trainer* tr, const float* op, int growth, uint32_
     uint32_t* keys_out = vals + n;
     uint32_t* vals_out = keys_out + n;
     uint32_t* counters = scratch + (size_t)n * 5 + 8;
-    bsx_status s = check_cuda(ctx, cudaMemsetAsync(counters, 0, 8, ctx->stream), "memset sample counters");
+    bsx_status s = check_cuda(ctx, cudaMemsetAsync(counters, 0, 12, ctx->stream), "memset sample counters");
     if (s != BSX_OK) return s;
     KeyArgs a;
     a.keep = tr->plan_keep.as<uint32_t>();
@@ -311,13 +339,16 @@ bsx_status weighted_sample(bsx_trainer* tr, const float* op, int growth, uint32_
     s = read_u32(ctx, counters, 2, c);
     if (s != BSX_OK) return s;
     if (above_count) *above_count = c[1];
-    out->clear();
+    if (drawn_new) *drawn_new = 0;
     const uint32_t take = std::min(k, c[0]);
     if (take == 0) return BSX_OK;
     s = radix_sort_pairs(ctx, keys, vals, K, 32, keys_out, vals_out);
     if (s != BSX_OK) return s;
-    out->resize(take);
-    return read_u32(ctx, vals_out, take, out->data());
+    prof_begin(ctx);
+    mark_sampled_kernel<<<blocks_for(take), kRefThreads, 0, ctx->stream>>>(vals_out, take, mark, counters + 2);
+    s = post_launch(ctx, "mark_sampled_kernel");
+    if (s == BSX_OK && drawn_new) s = read_u32(ctx, counters + 2, 1, drawn_new);
+    return s;
 }
 
 uint32_t sat_sub(uint32_t a, uint32_t b) { return a > b ? a - b : 0u; }
@@ -342,8 +373,9 @@ extern "C" bsx_status bsx_trainer_refine_plan(bsx_trainer* tr, const float* t, c
     tr->plan_n = n;
     tr->plan_cfg = *cfg;
     bsx_status s = ensure(ctx, tr->plan_keep, ((size_t)n + 1) * 4);
-    // scratch (u32): four arrays of n (mask / positions / sort keys and values), then counters
-    if (s == BSX_OK) s = ensure(ctx, tr->plan_scratch, ((size_t)n * 5 + 32) * 4);
+    // scratch (u32): four arrays of n (mask / positions / sort keys and values), counters at 5n,
+    // then the split membership of the kept rows at 5n + 32
+    if (s == BSX_OK) s = ensure(ctx, tr->plan_scratch, ((size_t)n * 6 + 32) * 4);
     if (s != BSX_OK) return s;
     uint32_t* scratch = tr->plan_scratch.as<uint32_t>();
     uint32_t* flag = scratch;
@@ -395,71 +427,80 @@ extern "C" bsx_status bsx_trainer_refine_plan(bsx_trainer* tr, const float* t, c
     tr->plan_kept = K;
     const uint32_t pruned = n - K;
     const uint32_t stream0 = 2 * tr->refines;
-    std::set<uint32_t> split;
-    std::vector<uint32_t> picked;
+    // split membership of the kept rows; the reference's HashSet (train.rs:1366)
+    uint32_t* mark = scratch + (size_t)n * 5 + 32;
     uint32_t* sample_scratch = scratch;  // the mask and positions are no longer needed
-    if (pruned > 0) {  // replacement weighted by opacity x visibility (train.rs:1368-1392)
-        s = weighted_sample(tr, op, 0, pruned, stream0, sample_scratch, nullptr, &picked);
+    if (K) {
+        s = check_cuda(ctx, cudaMemsetAsync(mark, 0, (size_t)K * 4, ctx->stream), "memset split set");
         if (s != BSX_OK) return s;
-        split.insert(picked.begin(), picked.end());
     }
-    const uint32_t pre_oversized = (uint32_t)split.size();
+    uint32_t in_set = 0;
+    if (pruned > 0) {  // replacement weighted by opacity x visibility (train.rs:1368-1392)
+        uint32_t fresh = 0;
+        s = weighted_sample(tr, op, 0, pruned, stream0, sample_scratch, mark, nullptr, &fresh);
+        if (s != BSX_OK) return s;
+        in_set += fresh;
+    }
+    uint32_t num_oversized = 0;
     if (cfg->split_at_screen_size > 0.0f && K) {  // train.rs:1398-1424
         float* st = tr->stats.as<float>();
         uint32_t* oflag = scratch;
         uint32_t* opos = oflag + n;
-        uint32_t* olist = opos + n;
-        uint32_t* ocount = scratch + (size_t)n * 5 + 2;
+        uint32_t* ocount = scratch + (size_t)n * 5 + 4;
         prof_begin(ctx);
-        oversized_kernel<<<blocks_for(K), kRefThreads, 0, ctx->stream>>>(keep, K, st + 2 * (size_t)tr->n,
-                                                                         st + tr->n, cfg->split_at_screen_size, oflag);
-        s = post_launch(ctx, "oversized_kernel");
+        oversized_new_kernel<<<blocks_for(K), kRefThreads, 0, ctx->stream>>>(
+            keep, K, st + 2 * (size_t)tr->n, st + tr->n, cfg->split_at_screen_size, mark, oflag);
+        s = post_launch(ctx, "oversized_new_kernel");
         if (s == BSX_OK) s = scan_inclusive_u32(ctx, oflag, nullptr, K, opos, ocount);
+        uint32_t fresh_candidates = 0;
+        if (s == BSX_OK) s = read_u32(ctx, ocount, 1, &fresh_candidates);
         if (s != BSX_OK) return s;
-        prof_begin(ctx);
-        scatter_flagged_kernel<<<blocks_for(K), kRefThreads, 0, ctx->stream>>>(oflag, opos, K, olist);
-        s = post_launch(ctx, "scatter_flagged_kernel");
-        uint32_t O = 0;
-        if (s == BSX_OK) s = read_u32(ctx, ocount, 1, &O);
-        std::vector<uint32_t> cand(O);
-        if (s == BSX_OK) s = read_u32(ctx, olist, O, cand.data());
-        if (s != BSX_OK) return s;
-        uint32_t budget = sat_sub(cfg->max_splats, K + (uint32_t)split.size());
-        for (uint32_t j : cand) {
-            if (budget == 0) break;
-            if (split.insert(j).second) --budget;
+        const uint32_t budget = sat_sub(cfg->max_splats, K + in_set);
+        num_oversized = std::min(budget, fresh_candidates);
+        if (num_oversized) {
+            prof_begin(ctx);
+            mark_budget_kernel<<<blocks_for(K), kRefThreads, 0, ctx->stream>>>(oflag, opos, K, budget, mark);
+            s = post_launch(ctx, "mark_budget_kernel");
+            if (s != BSX_OK) return s;
         }
+        in_set += num_oversized;
     }
-    const uint32_t num_oversized = (uint32_t)split.size() - pre_oversized;
-    const uint32_t pre_grow = (uint32_t)split.size();
+    uint32_t num_high_grad = 0;
     if (global_iter < cfg->growth_stop_iter && K) {  // train.rs:1428-1495, gradient signal
         // count the candidates first (k = 0 draws nothing), then draw
         uint32_t count = 0;
-        s = weighted_sample(tr, op, 1, 0, stream0 + 1, sample_scratch, &count, &picked);
+        s = weighted_sample(tr, op, 1, 0, stream0 + 1, sample_scratch, mark, &count, nullptr);
         if (s != BSX_OK) return s;
         const uint32_t grow_count = (uint32_t)roundf((float)count * cfg->growth_select_fraction);
         const uint32_t sample_high = sat_sub(grow_count, pruned);
-        const uint32_t headroom = sat_sub(cfg->max_splats, K + (uint32_t)split.size());
+        const uint32_t headroom = sat_sub(cfg->max_splats, K + in_set);
         const uint32_t grow = std::min(sample_high, headroom);
         if (grow > 0) {
-            s = weighted_sample(tr, op, 1, grow, stream0 + 1, sample_scratch, nullptr, &picked);
+            s = weighted_sample(tr, op, 1, grow, stream0 + 1, sample_scratch, mark, nullptr, &num_high_grad);
             if (s != BSX_OK) return s;
-            split.insert(picked.begin(), picked.end());
+            in_set += num_high_grad;
         }
     }
-    const std::vector<uint32_t> list(split.begin(), split.end());
-    const uint32_t S = (uint32_t)list.size();
-    s = ensure(ctx, tr->plan_split, ((size_t)S + 1) * 4);
-    if (s == BSX_OK && S)
-        s = check_cuda(ctx, cudaMemcpy(tr->plan_split.p, list.data(), (size_t)S * 4, cudaMemcpyHostToDevice),
-                       "upload split list");
+    // the split rows in ascending order
+    const uint32_t S = in_set;
+    s = ensure(ctx, tr->plan_split, ((size_t)K + 1) * 4);
     if (s != BSX_OK) return s;
+    if (S) {
+        uint32_t* mpos = scratch;
+        s = scan_inclusive_u32(ctx, mark, nullptr, K, mpos, nullptr);
+        if (s != BSX_OK) return s;
+        prof_begin(ctx);
+        scatter_flagged_kernel<<<blocks_for(K), kRefThreads, 0, ctx->stream>>>(mark, mpos, K,
+                                                                               tr->plan_split.as<uint32_t>());
+        s = post_launch(ctx, "scatter_flagged_kernel");
+        if (s != BSX_OK) return s;
+    }
     tr->plan_split_count = S;
     tr->planned = true;
     if (stats) {
         stats->num_added = S;
         stats->num_split_oversized = num_oversized;
-        stats->num_split_high_grad = (uint32_t)split.size() - pre_grow;
+        stats->num_split_high_grad = num_high_grad;
         stats->num_pruned = pruned;
         stats->num_pruned_non_finite = non_finite;
         stats->total_splats = K + S;

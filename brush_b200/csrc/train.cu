@@ -17,6 +17,8 @@
 // rate; gamma = (end / start)^(1 / total_train_iters) (train.rs:243-258).
 #include <math.h>
 
+#include <algorithm>
+
 #include <vector>
 
 #include "trainer.cuh"
@@ -198,8 +200,8 @@ bsx_status bsx_trainer_destroy(bsx_trainer* tr) {
     if (tr->ctx->stream) cudaStreamSynchronize(tr->ctx->stream);
     DevBuf* bufs[] = {&tr->grads, &tr->v_combined, &tr->v_output, &tr->stats, &tr->moments, &tr->moments_next,
                       &tr->plan_keep, &tr->plan_split, &tr->plan_scratch};
-    for (DevBuf* b : bufs)
-        if (b->p) cudaFree(b->p);
+    for (DevBuf* b : bufs) release(tr->ctx, *b);
+    if (tr->ctx->stream) cudaStreamSynchronize(tr->ctx->stream);
     delete tr;
     return BSX_OK;
 }
@@ -217,6 +219,48 @@ bsx_status bsx_trainer_optimizer_state(bsx_trainer* tr, float** mt, float** ms, 
     *vs = v[1];
     *vo = v[2];
     *rows = tr->moment_rows;
+    return BSX_OK;
+}
+
+bsx_status bsx_trainer_reserve(bsx_trainer* tr, uint32_t max_splats) {
+    if (!tr) return BSX_ERR_INVALID_ARG;
+    bsx_ctx* ctx = tr->ctx;
+    cudaSetDevice(ctx->device);
+    const size_t m = std::max<uint32_t>(max_splats, 1), c3 = 3 * (size_t)tr->coeffs;
+    // Sizes each ensure() caller asks for at m splats (render, raster backward,
+    // trainer, refine), so none of them reallocates below max_splats.
+    struct R {
+        DevBuf* b;
+        size_t bytes;
+    } rs[] = {{&ctx->projected, m * BSX_PROJECTED_LANES * 4},
+              {&ctx->counts, m * 4},
+              {&ctx->max_radius, m * 4},
+              {&ctx->vis_gid, m * 4},
+              {&ctx->depth_keys, m * 4},
+              {&ctx->depth_order, m * 4},
+              {&ctx->cum, m * 4},
+              {&ctx->visible, m * 4},
+              {&tr->grads, (m * (11 + c3) + m) * 4 + 64},
+              {&tr->v_combined, m * BSX_GRAD_STRIDE * 4},
+              {&tr->stats, 3 * m * 4},
+              {&tr->moments, moment_floats((uint32_t)m, tr->coeffs) * 4 + 64},
+              {&tr->moments_next, moment_floats((uint32_t)m, tr->coeffs) * 4 + 64},
+              {&tr->plan_keep, (m + 1) * 4},
+              {&tr->plan_split, (m + 1) * 4},
+              {&tr->plan_scratch, (m * 6 + 32) * 4}};
+    for (const R& r : rs) {
+        if (r.bytes <= r.b->cap) continue;
+        // keep the contents of live buffers (moments, statistics) across the growth
+        DevBuf grown;
+        bsx_status s = ensure(ctx, grown, r.bytes);
+        if (s != BSX_OK) return s;
+        if (r.b->p)
+            s = check_cuda(ctx, cudaMemcpyAsync(grown.p, r.b->p, r.b->cap, cudaMemcpyDeviceToDevice, ctx->stream),
+                           "copy on reserve");
+        if (s != BSX_OK) return s;
+        release(ctx, *r.b);
+        *r.b = grown;
+    }
     return BSX_OK;
 }
 

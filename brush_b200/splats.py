@@ -53,20 +53,23 @@ class Splats:
 def splat_bounds(means: torch.Tensor, percentile: float = 0.8):
     """Robust percentile AABB of the means as (center, extent), f32 as ``bounds_from_pos``
     computes it (crates/brush-train/src/splat_init.rs:130-158, bounding_box.rs:8-13)."""
-    m = means.detach().float().cpu().numpy()
+    m = means.detach().float()
     p = np.float32(percentile)
     lo_v, hi_v = [], []
     for k in range(3):
-        v = m[np.isfinite(m[:, k]), k]
-        if v.size == 0:  # an axis with no finite value: the unit box
+        v = m[:, k]
+        v = v[torch.isfinite(v)]
+        if v.numel() == 0:  # an axis with no finite value: the unit box
             one = np.ones(3, np.float32)
             return np.zeros(3, np.float32), one
-        n = v.size
+        n = v.numel()
         lo = int(np.float32((np.float32(1.0) - p) / np.float32(2.0)) * np.float32(n))
         hi = min(n - 1, int(np.float32((np.float32(1.0) + p) / np.float32(2.0)) * np.float32(n)))
-        part = np.partition(v, (lo, hi))
-        lo_v.append(part[lo])
-        hi_v.append(part[hi])
+        # order statistics by a full sort (on the tensor's device): the same values as select_nth
+        vs = torch.sort(v).values
+        pair = torch.stack([vs[lo], vs[hi]]).cpu().numpy()
+        lo_v.append(pair[0])
+        hi_v.append(pair[1])
     mn, mx = np.array(lo_v, np.float32), np.array(hi_v, np.float32)
     return (mx + mn) / np.float32(2.0), (mx - mn) / np.float32(2.0)
 

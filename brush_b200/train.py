@@ -348,6 +348,38 @@ class SplatTrainer:
             self.record.gather_stats(self.grads.v_refine_weight, out.aux.visible, out.aux.max_radius)
         return TrainStepStats(out.aux.num_visible, out.aux.num_intersections, self.loss, lr_mean)
 
+    def reserve(self, max_splats: int, splats: Splats) -> None:
+        """Allocate up front for a run that grows to ``max_splats`` (single-GPU native trainer):
+        the trainer's and context's per-splat buffers and the refine output storages."""
+        if self.native is None or self.world > 1:
+            raise NotImplementedError("reserve applies to the single-GPU native trainer")
+        ctx = context(splats.transforms.device)
+        ctx.check(_lib.lib().bsx_trainer_reserve(self.native.handle, int(max_splats)))
+        dev = splats.transforms.device
+        self._store = [tuple(torch.empty(shape, device=dev) for shape in
+                             ((max_splats, 10), (max_splats, self.c, 3), (max_splats,))) for _ in range(2)]
+        self._store_next = 0
+
+    def _refine_storage(self, n2: int, splats: Splats):
+        """Output splat tensors for a refine: views of one of two storages used in turn (the
+        other holds the splats being refined), each grown with headroom, so a growing run
+        does not allocate at every refine. The splat tensors from before a refine are
+        overwritten by the refine after next."""
+        dev = splats.transforms.device
+        if not hasattr(self, "_store"):
+            self._store, self._store_next = [None, None], 0
+        k = self._store_next
+        if self._store[k] is not None and splats.transforms.data_ptr() == self._store[k][0].data_ptr():
+            k ^= 1  # never write into the storage being read
+        buf = self._store[k]
+        if buf is None or buf[0].shape[0] < n2:
+            cap = max(n2, int(n2 * 1.5))
+            buf = (torch.empty((cap, 10), device=dev), torch.empty((cap, self.c, 3), device=dev),
+                   torch.empty((cap,), device=dev))
+            self._store[k] = buf
+        self._store_next = k ^ 1
+        return buf[0][:n2], buf[1][:n2], buf[2][:n2]
+
     def refine(self, splats: Splats, global_iter: int, phase_iter: int | None = None, phase_total: int | None = None,
                refine_config: RefineConfig | None = None) -> _lib.RefineStats:
         """``SplatTrainer::refine_for_phase`` (crates/brush-train/src/train.rs:1191-1534) in place on
@@ -368,10 +400,7 @@ class SplatTrainer:
                                             ptr(splats.raw_opacities), C.byref(c), center, extent, int(global_iter),
                                             C.byref(st)))
         n2 = int(st.total_splats)
-        dev = splats.transforms.device
-        nt = torch.empty((n2, 10), device=dev)
-        nsh = torch.empty((n2, self.c, 3), device=dev)
-        nop = torch.empty((n2,), device=dev)
+        nt, nsh, nop = self._refine_storage(n2, splats)
         ctx.check(L.bsx_trainer_refine_apply(self.native.handle, ptr(splats.transforms), ptr(splats.sh_coeffs),
                                              ptr(splats.raw_opacities), ptr(nt), ptr(nsh), ptr(nop),
                                              int(phase_iter), int(phase_total)))

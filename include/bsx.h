@@ -155,6 +155,10 @@ typedef struct bsx_ctx bsx_ctx;
 BSX_API bsx_status bsx_create(int device, bsx_ctx** out);
 BSX_API bsx_status bsx_destroy(bsx_ctx* ctx);
 BSX_API bsx_status bsx_set_stream(bsx_ctx* ctx, void* cuda_stream);
+/* Free the context's grow-only workspace (synchronises its stream); it is
+ * reallocated on demand. Invalidates the last forward's state and every
+ * bsx_render_out pointer. */
+BSX_API bsx_status bsx_trim(bsx_ctx* ctx);
 BSX_API bsx_status bsx_sync(bsx_ctx* ctx);
 BSX_API const char* bsx_last_error(const bsx_ctx* ctx);
 BSX_API const char* bsx_status_string(bsx_status s);
@@ -395,6 +399,11 @@ BSX_API bsx_status bsx_trainer_refine_apply(bsx_trainer* tr, const float* d_tran
 BSX_API bsx_status bsx_trainer_optimizer_state(bsx_trainer* tr, float** d_m_transforms, float** d_m_sh_coeffs,
                                                float** d_m_raw_opac, float** d_v_transforms, float** d_v_sh_coeffs,
                                                float** d_v_raw_opac, uint32_t* rows);
+/* Allocate now every buffer the trainer and its context index by splat, for
+ * up to max_splats splats (gradients, moments, statistics, refine scratch,
+ * projected rows, counts and ids), so a growing run does not allocate at its
+ * refines. Buffers sized by intersections still grow on demand. */
+BSX_API bsx_status bsx_trainer_reserve(bsx_trainer* tr, uint32_t max_splats);
 /* Rate schedule input after the bounds change (train.rs:656: lr_mean uses bounds.median_size()). */
 BSX_API bsx_status bsx_trainer_set_median_scale(bsx_trainer* tr, float median_scale);
 
