@@ -222,6 +222,35 @@ bsx_status bsx_trainer_optimizer_state(bsx_trainer* tr, float** mt, float** ms, 
     return BSX_OK;
 }
 
+bsx_status bsx_trainer_load_optimizer_state(bsx_trainer* tr, const float* mt, const float* ms, const float* mo,
+                                            const float* vt, const float* vs, const float* vo, uint32_t rows,
+                                            int32_t world, int32_t rank) {
+    if (!tr || world < 1 || world > BSX_MAX_RANKS || rank < 0 || rank >= world) return BSX_ERR_INVALID_ARG;
+    if (rows && (!mt || !ms || !mo || !vt || !vs || !vo)) return BSX_ERR_INVALID_ARG;
+    bsx_ctx* ctx = tr->ctx;
+    const uint32_t rb = (uint32_t)((uint64_t)tr->n * rank / world), re = (uint32_t)((uint64_t)tr->n * (rank + 1) / world);
+    if (rows != re - rb) return fail(ctx, BSX_ERR_SHAPE, "optimizer state rows do not match the shard of this rank");
+    cudaSetDevice(ctx->device);
+    bsx_status s = ensure(ctx, tr->moments, moment_floats(rows, tr->coeffs) * 4 + 64);
+    if (s != BSX_OK) return s;
+    float* m[3];
+    float* v[3];
+    moment_views(tr->moments.as<float>(), rows, tr->coeffs, m, v);
+    const float* src[6] = {mt, ms, mo, vt, vs, vo};
+    float* dst[6] = {m[0], m[1], m[2], v[0], v[1], v[2]};
+    const size_t cols[6] = {10, 3 * (size_t)tr->coeffs, 1, 10, 1, 1};
+    for (int k = 0; k < 6 && rows; ++k) {
+        s = check_cuda(ctx, cudaMemcpyAsync(dst[k], src[k], (size_t)rows * cols[k] * 4, cudaMemcpyDeviceToDevice,
+                                            ctx->stream),
+                       "load optimizer state");
+        if (s != BSX_OK) return s;
+    }
+    tr->moment_rows = rows;
+    tr->moment_world = world;
+    tr->moment_rank = rank;
+    return BSX_OK;
+}
+
 bsx_status bsx_trainer_reserve(bsx_trainer* tr, uint32_t max_splats) {
     if (!tr) return BSX_ERR_INVALID_ARG;
     bsx_ctx* ctx = tr->ctx;

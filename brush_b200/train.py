@@ -171,6 +171,13 @@ class _NativeTrainer:
         views = [device_view(x.value, sh, torch.float32, d) for x, sh in zip(p, shapes)]
         return tuple(views[:3]), tuple(views[3:])
 
+    def load_optimizer_state(self, m, v, rows: int, world: int = 1, rank: int = 0) -> None:
+        """Replace the moments with device tensors laid out as optimizer_state() returns them."""
+        arrs = [t.contiguous() for t in (*m, *v)]
+        self.ctx.check(_lib.lib().bsx_trainer_load_optimizer_state(self.handle, *[t.data_ptr() for t in arrs],
+                                                                    int(rows), int(world), int(rank)))
+        torch.cuda.current_stream(self.device).synchronize()
+
     def close(self) -> None:
         if self.handle:
             self.ctx.check(_lib.lib().bsx_trainer_destroy(self.handle))
@@ -385,9 +392,11 @@ class SplatTrainer:
         """``SplatTrainer::refine_for_phase`` (crates/brush-train/src/train.rs:1191-1534) in place on
         ``splats``: prune, replace, split oversized, grow by gradient; the splat tensors are
         replaced by tensors of the new count and the optimizer state follows the rows."""
-        if self.native is None or self.world > 1:
-            raise NotImplementedError("refine runs on the single-GPU native trainer")
+        if self.native is None:
+            raise NotImplementedError("refine runs on the native trainer (one GPU, or the peer exchange)")
         cfg = refine_config or RefineConfig()
+        if self.world > 1:
+            self._gather_for_refine()
         phase_iter = global_iter if phase_iter is None else phase_iter
         phase_total = self.config.total_train_iters if phase_total is None else phase_total
         L = _lib.lib()
@@ -407,13 +416,59 @@ class SplatTrainer:
         splats.transforms, splats.sh_coeffs, splats.raw_opacities = nt, nsh, nop
         self.n = n2
         self.native.n = n2
-        self.grads = self.native.grads()
         self.record = self.native.record()
+        if self.world > 1:
+            self._reshard_after_refine(splats)
+        else:
+            self.grads = self.native.grads()
         # new bounds and rate scale (train.rs:1506, :656)
         self.bounds = splat_bounds(splats.means(), self.config.bounds_percentile)
         self.median_scale = float(np.float32(np.sort(self.bounds[1])[1] * np.float32(2.0)))
         ctx.check(L.bsx_trainer_set_median_scale(self.native.handle, self.median_scale))
         return st
+
+    def _gather_for_refine(self) -> None:
+        """Every rank refines the same model identically: combine the ranks' statistics
+        (visibility SUM, screen size MAX; the refine weights are already MAX-combined by the
+        exchange) and give every rank the full optimizer state (all-gather of the row shards)."""
+        rec = self.record
+        torch.distributed.all_reduce(rec.vis_weight, op=torch.distributed.ReduceOp.SUM, group=self.pg)
+        torch.distributed.all_reduce(rec.max_screen_size, op=torch.distributed.ReduceOp.MAX, group=self.pg)
+        state = self.native.optimizer_state()
+        n, w = self.n, self.world
+        if state is None:
+            return
+        bounds = [n * r // w for r in range(w + 1)]
+        pad = max(bounds[r + 1] - bounds[r] for r in range(w))
+        full = []
+        for t in (*state[0], *state[1]):
+            flat = t.reshape(t.shape[0], -1)
+            mine = torch.zeros((pad, flat.shape[1]), device=flat.device)
+            mine[:flat.shape[0]] = flat
+            gathered = torch.empty((w * pad, flat.shape[1]), device=flat.device)
+            torch.distributed.all_gather_into_tensor(gathered, mine, group=self.pg)
+            rows = [gathered[r * pad: r * pad + bounds[r + 1] - bounds[r]] for r in range(w)]
+            full.append(torch.cat(rows, 0).reshape((n,) + tuple(t.shape[1:])))
+        self.native.load_optimizer_state(full[:3], full[3:], n, 1, 0)
+
+    def _reshard_after_refine(self, splats: Splats) -> None:
+        """After a data-parallel refine: a new exchange region for the new count, the splats
+        copied into it, and this rank's row shard of the (full, refined) optimizer state."""
+        from .peer import PeerExchange
+
+        old = self.peer
+        self.peer = PeerExchange(self.n, self.c, splats.transforms.device.index, self.pg)
+        self.peer.load(splats.transforms, splats.sh_coeffs, splats.raw_opacities)
+        splats.transforms, splats.sh_coeffs, splats.raw_opacities = self.peer.params
+        self.grads = SplatGrads(*self.peer.grads, v_refine_weight=self.peer.refine)
+        self._dp = self.peer.train_structs()
+        old.close()
+        state = self.native.optimizer_state()
+        if state is not None:
+            rank = torch.distributed.get_rank(self.pg)
+            r0, r1 = self.n * rank // self.world, self.n * (rank + 1) // self.world
+            shard = [t[r0:r1].clone() for t in (*state[0], *state[1])]
+            self.native.load_optimizer_state(shard[:3], shard[3:], r1 - r0, self.world, rank)
 
     def close(self) -> None:
         """Release the exchange region (collective over the process group) and the native trainer."""

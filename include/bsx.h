@@ -404,6 +404,16 @@ BSX_API bsx_status bsx_trainer_optimizer_state(bsx_trainer* tr, float** d_m_tran
  * projected rows, counts and ids), so a growing run does not allocate at its
  * refines. Buffers sized by intersections still grow on demand. */
 BSX_API bsx_status bsx_trainer_reserve(bsx_trainer* tr, uint32_t max_splats);
+/* Replace the moments with the given rows: the whole model (world 1), or the
+ * shard rows [rows_total*rank/world, rows_total*(rank+1)/world) the
+ * data-parallel step of `rank` of `world` uses, where rows_total is the
+ * trainer's splat count. Device arrays laid out as bsx_trainer_optimizer_state
+ * returns them; the Adam time step is kept. */
+BSX_API bsx_status bsx_trainer_load_optimizer_state(bsx_trainer* tr, const float* d_m_transforms,
+                                                    const float* d_m_sh_coeffs, const float* d_m_raw_opac,
+                                                    const float* d_v_transforms, const float* d_v_sh_coeffs,
+                                                    const float* d_v_raw_opac, uint32_t rows, int32_t world,
+                                                    int32_t rank);
 /* Rate schedule input after the bounds change (train.rs:656: lr_mean uses bounds.median_size()). */
 BSX_API bsx_status bsx_trainer_set_median_scale(bsx_trainer* tr, float median_scale);
 

@@ -204,3 +204,80 @@ def test_dp_kernel_times_out_when_a_rank_never_arrives(cuda):
     ctx.check(_dp_call(lib, ctx, [g1], 1, 0, [torch.zeros(64, dtype=torch.int32, device="cuda")], 1, int(1e9)))
     ctx.sync()
     assert torch.isfinite(g["param"][0]).all()
+
+
+def _refine_worker(rank, world, port, q):
+    sys.path.insert(0, str(ROOT))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import brush_b200 as bsx
+    from brush_b200.dist import view_for
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    torch.distributed.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                                         timeout=datetime.timedelta(seconds=60))
+    try:
+        splats, cams, size, gts = _scene(dev)
+        tr = bsx.SplatTrainer(bsx.TrainConfig(), splats, process_group=torch.distributed.group.WORLD)
+        for k in range(4):
+            v = view_for(k, rank, world, len(cams))
+            tr.step(cams[v], size, gts[v], splats)
+        torch.cuda.synchronize()
+        n = splats.num_splats
+        rec = [x.cpu().numpy().copy() for x in (tr.record.refine_weight_norm, tr.record.vis_weight,
+                                                tr.record.max_screen_size)]
+        (m_t, m_s, m_o), (v_t, v_s, v_o) = tr.native.optimizer_state()
+        shard = [x.reshape(x.shape[0], -1).cpu().numpy().copy() for x in (m_t, m_s, m_o, v_t, v_s, v_o)]
+        pre = [x.cpu().numpy().copy() for x in (splats.transforms, splats.sh_coeffs, splats.raw_opacities)]
+        bounds = (tr.bounds[0].copy(), tr.bounds[1].copy())
+        cfg = bsx.RefineConfig(growth_grad_threshold=2e-5, growth_select_fraction=0.3, split_at_screen_size=0.05,
+                               seed=99)
+        st = tr.refine(splats, 200, 200, 3000, cfg)
+        torch.cuda.synchronize()
+        post = [x.cpu().numpy().copy() for x in (splats.transforms, splats.sh_coeffs, splats.raw_opacities)]
+        for k in range(4, 7):
+            v = view_for(k, rank, world, len(cams))
+            tr.step(cams[v], size, gts[v], splats)
+        torch.cuda.synchronize()
+        tr.peer.ctx.sync()
+        later = [x.cpu().numpy().copy() for x in (splats.transforms, splats.sh_coeffs, splats.raw_opacities)]
+        q.put((rank, "ok", dict(rec=rec, shard=shard, pre=pre, bounds=bounds, post=post, later=later,
+                                total=st.total_splats, added=st.num_added)))
+        tr.close()
+    except Exception as e:  # noqa: BLE001
+        import traceback
+
+        q.put((rank, "error", traceback.format_exc()))
+    finally:
+        torch.distributed.destroy_process_group()
+
+
+def test_two_gpu_refine_identical_on_both_ranks_and_matches_oracle(cuda, orc):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_refine_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=300) for _ in range(2)], key=lambda r: r[0])
+    for p in procs:
+        p.join(timeout=60)
+    assert all(r[1] == "ok" for r in res), res
+    a, b = res[0][2], res[1][2]
+    assert a["total"] == b["total"] and a["added"] > 0
+    for x, y in zip(a["post"] + a["later"], b["post"] + b["later"]):
+        np.testing.assert_array_equal(x, y)
+    # the oracle refines the combined state: statistics combined over ranks, full moments
+    rec = (np.maximum(a["rec"][0], b["rec"][0]), a["rec"][1] + b["rec"][1], np.maximum(a["rec"][2], b["rec"][2]))
+    full = [np.concatenate([sa, sb], 0) for sa, sb in zip(a["shard"], b["shard"])]
+    n = a["pre"][0].shape[0]
+    moments = ((full[0], full[1], full[2].reshape(n)), (full[3], full[4].reshape(n), full[5].reshape(n)))
+    ref = orc.refine(*a["pre"], rec, moments, orc.refine_cfg(growth_grad_threshold=2e-5, growth_select_fraction=0.3,
+                                                              split_at_screen_size=0.05, seed=99),
+                     a["bounds"][0], a["bounds"][1], 200, 0, 200, 3000)
+    assert ref["stats"].total_splats == a["total"]
+    np.testing.assert_array_equal(a["post"][0], ref["transforms"])
+    np.testing.assert_array_equal(a["post"][1], ref["sh"])
+    np.testing.assert_array_equal(a["post"][2], ref["opac"])
