@@ -22,6 +22,7 @@ class Context:
             _lib.check(_lib.lib().bsx_create(device, C.byref(h)))
         self.handle = h
         self.last_n = 0  # splat count of the last forward render
+        self.fwd_inputs = ()  # splat tensors of the last forward render (read by the backward)
 
     def bind_stream(self) -> None:
         """Enqueue subsequent library work on torch's current stream of this device."""

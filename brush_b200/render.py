@@ -88,6 +88,9 @@ def render(camera: Camera, img_size: tuple, transforms: torch.Tensor, sh_coeffs:
                                         ptr(raw_opacities), n, coeffs, int(render_mode), int(raster_pass), bg,
                                         C.byref(out)))
     ctx.last_n = n
+    # rasterize_bwd / project_bwd read these device buffers later (the forward
+    # state of the context): keep them alive until the next render
+    ctx.fwd_inputs = (transforms, sh_coeffs, raw_opacities)
     V, M = out.num_visible, out.num_intersections
     bwd = raster_pass != _lib.PASS_FORWARD
     f32, i32 = torch.float32, torch.int32

@@ -191,7 +191,9 @@ BSX_API bsx_status bsx_render_fwd(bsx_ctx* ctx, const bsx_camera* cam, uint32_t 
                           bsx_render_out* out);
 
 /* ---- backward: SplatBwdOps (crates/brush-render-bwd/src/burn_glue.rs:80-172) ----
- * Both consume the state of the last backward-pass forward render on ctx. */
+ * Both consume the state of the last backward-pass forward render on ctx,
+ * including its splat buffers (transforms, SH, opacities), which must stay
+ * valid and unchanged until the backward has run. */
 /* rasterize_bwd: v_output [H,W,4] -> d_v_combined [N, BSX_GRAD_STRIDE]
  * (zeroed, then accumulated). Both buffers 16-byte aligned. */
 BSX_API bsx_status bsx_rasterize_bwd(bsx_ctx* ctx, const float* d_v_output, int32_t compute_refine_weight,
