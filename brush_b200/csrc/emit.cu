@@ -1,16 +1,17 @@
 // emit.cu - intersection emission and per-tile ranges.
 //
 // emit_kernel restates map_gaussians_to_intersect_kernel
-// (crates/brush-render/src/kernels/map_gaussians.rs:14-92): one thread per
-// visible splat in depth order walks its tile bbox row-major, writes
-// (tile id, splat id) for every tile passing the StopThePop test into the
-// slots reserved by the inclusive count scan, and pads any shortfall with the
-// sentinel tile id T (sorted after every real tile). The splat id written is
-// the global id (projected rows are global-id indexed here).
+// (crates/brush-render/src/kernels/map_gaussians.rs:14-92): for every visible
+// splat in depth order, the tiles of its bbox in row-major order that pass
+// the StopThePop test are written as (tile id, splat id) into the slots
+// reserved by the inclusive count scan, and any shortfall is padded with the
+// sentinel tile id T (sorted after every real tile). A warp walks its 32
+// splats' boxes together (tile_walk.cuh). The splat id written is the global
+// id (projected rows are global-id indexed here).
 //
 // tile_offsets_kernel restates get_tile_offsets
 // (crates/brush-render/src/get_tile_offset.rs:10-62).
-#include "splat_math.cuh"
+#include "tile_walk.cuh"
 
 namespace bsx {
 
@@ -22,33 +23,47 @@ __global__ void __launch_bounds__(256) emit_kernel(const float* __restrict__ pro
                                                    uint32_t tbw, uint32_t tbh, uint32_t* __restrict__ tile_out,
                                                    uint32_t* __restrict__ gid_out, uint32_t num_isect, int* err) {
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= num_visible) return;
-    const uint32_t g = __ldg(depth_order + i);
-    const float4* row = reinterpret_cast<const float4*>(projected + (size_t)g * BSX_PROJECTED_LANES);
-    const float4 r0 = __ldg(row), r1 = __ldg(row + 1), r2 = __ldg(row + 2);
-    const float x = r0.x, y = r0.y;
-    const S2 conic{r0.z, r0.w, r1.x};
-    // ln(255 * opacity): the projection pass stored it from the same opacity.
-    const float pt = r2.z;
-    float ex, ey;
-    bbox_extent(conic, pt, &ex, &ey);
-    const TileBox bb = tile_bbox(x, y, ex, ey, tbw, tbh);
-    const uint32_t base = i == 0 ? 0u : __ldg(cum + i - 1);
-    const uint32_t budget = __ldg(cum + i) - base;
-    if (base > num_isect || budget > num_isect - base) {
-        set_error(err, kDevOutOfRange);
-        return;
+    WalkSplat ws{0u, 0u, 0u, 0u, 0.0f, 0.0f, S2{0.0f, 0.0f, 0.0f}, 0.0f};
+    uint32_t g = 0, base = 0, budget = 0;
+    if (i < num_visible) {
+        g = __ldg(depth_order + i);
+        const float4* row = reinterpret_cast<const float4*>(projected + (size_t)g * BSX_PROJECTED_LANES);
+        const float4 r0 = __ldg(row), r1 = __ldg(row + 1), r2 = __ldg(row + 2);
+        const S2 conic{r0.z, r0.w, r1.x};
+        // ln(255 * opacity): the projection pass stored it from the same opacity.
+        const float pt = r2.z;
+        float ex, ey;
+        bbox_extent(conic, pt, &ex, &ey);
+        const TileBox bb = tile_bbox(r0.x, r0.y, ex, ey, tbw, tbh);
+        base = i == 0 ? 0u : __ldg(cum + i - 1);
+        budget = __ldg(cum + i) - base;
+        if (base > num_isect || budget > num_isect - base) {
+            set_error(err, kDevOutOfRange);
+            budget = 0;
+        } else {
+            const uint32_t bw = bb.max_x > bb.min_x ? bb.max_x - bb.min_x : 0u;
+            const uint32_t bh = bb.max_y > bb.min_y ? bb.max_y - bb.min_y : 0u;
+            ws = WalkSplat{bb.min_x, bb.min_y, bw, bw * bh, r0.x, r0.y, conic, pt};
+        }
     }
-    uint32_t hit = 0;
-    for (uint32_t ty = bb.min_y; ty < bb.max_y && hit < budget; ++ty)
-        for (uint32_t tx = bb.min_x; tx < bb.max_x && hit < budget; ++tx)
-            if (tile_contrib(tx, ty, x, y, conic, pt)) {
-                tile_out[base + hit] = tx + ty * tbw;
-                gid_out[base + hit] = g;
-                ++hit;
-            }
+    // Hits of one splat land at consecutive slots from its scan offset, in
+    // row-major box order; a warp iteration writes one contiguous run.
+    uint32_t written = 0;
+    warp_tile_walk(ws, [&](const WalkStep& s) {
+        const uint32_t o_written = __shfl_sync(kFullMask, written, s.owner);
+        const uint32_t o_base = __shfl_sync(kFullMask, base, s.owner);
+        const uint32_t o_budget = __shfl_sync(kFullMask, budget, s.owner);
+        const uint32_t o_gid = __shfl_sync(kFullMask, g, s.owner);
+        const uint32_t slot = o_written + s.before;
+        if (s.hit && slot < o_budget) {
+            tile_out[o_base + slot] = s.tx + s.ty * tbw;
+            gid_out[o_base + slot] = o_gid;
+        }
+        written += s.own;
+    });
+    // pad any shortfall with the sentinel tile id (sorted after every real tile)
     const uint32_t sentinel = tbw * tbh;
-    for (uint32_t k = hit; k < budget; ++k) {
+    for (uint32_t k = written; k < budget; ++k) {
         tile_out[base + k] = sentinel;
         gid_out[base + k] = g;
     }

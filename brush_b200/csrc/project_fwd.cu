@@ -4,8 +4,9 @@
 // one pass, project_forward_kernel (crates/brush-render/src/kernels/project_forward.rs:20-144)
 // and project_visible_kernel (kernels/project_visible.rs:22-89): the cull
 // predicates, the EWA covariance, the StopThePop per-tile count, and the SH
-// colour of every surviving splat. No block-wide barrier: every block streams
-// independently.
+// colour of every surviving splat. The per-tile count is taken by the warp
+// together (tile_walk.cuh) instead of one lane per box. No block-wide
+// barrier: every block streams independently.
 //
 // compact_visible_kernel: where the reference appends visible ids with an
 // atomic counter (order depends on scheduling), blocks of 1024 splats here
@@ -23,6 +24,7 @@
 // Scratch: vis_mask[ceil(N/32)] (bit per splat), depth_dense[N] (visible only).
 #include "lookback.cuh"
 #include "sh.cuh"
+#include "tile_walk.cuh"
 
 namespace bsx {
 
@@ -64,17 +66,18 @@ __global__ void __launch_bounds__(kProjThreads) project_fwd_kernel(const __grid_
     const uint32_t g = blockIdx.x * kProjThreads + threadIdx.x;
     const Uni& u = a.u;
 
+    // Cull and project; a surviving splat leaves its tile box for the walk.
     bool visible = false;
-    uint32_t hits = 0;
-    float depth = 0.0f;
-    float radius = 0.0f;
+    WalkSplat ws{0u, 0u, 0u, 0u, 0.0f, 0.0f, S2{0.0f, 0.0f, 0.0f}, 0.0f};
+    V3 mean = v3(0.0f, 0.0f, 0.0f);
+    float depth = 0.0f, radius = 0.0f, opac = 0.0f;
     if (g < a.n) {
         do {
             // one transform row = five 8-byte words
             const float2* t2 = reinterpret_cast<const float2*>(a.transforms + (size_t)g * 10);
             const float2 w0 = __ldg(t2), w1 = __ldg(t2 + 1), w2 = __ldg(t2 + 2), w3 = __ldg(t2 + 3), w4 = __ldg(t2 + 4);
             const float t[10] = {w0.x, w0.y, w1.x, w1.y, w2.x, w2.y, w3.x, w3.y, w4.x, w4.y};
-            V3 mean = v3(t[0], t[1], t[2]);
+            mean = v3(t[0], t[1], t[2]);
             V3 mean_c = vadd(mmul(u.rot, mean), u.trans);
             if (!(vfinite(mean_c) && mean_c.z <= 1.0e10f)) break;
             if (mean_c.z < 0.01f) break;
@@ -89,7 +92,7 @@ __global__ void __launch_bounds__(kProjThreads) project_fwd_kernel(const __grid_
             S2 raw = calc_cov2d(scl, q, mean_c, u);
             float fc;
             S2 cov = compensate_cov2d(raw, a.mip != 0, &fc);
-            float opac = bsx_sigmoid(ro) * fc;
+            opac = bsx_sigmoid(ro) * fc;
             if (!s2finite(cov)) break;
             float inv_z = 1.0f / mean_c.z;
             float m2x = u.fx * mean_c.x * inv_z + u.cx;
@@ -104,41 +107,50 @@ __global__ void __launch_bounds__(kProjThreads) project_fwd_kernel(const __grid_
             bool on_screen = m2x + ex > 0.0f && m2x - ex < wf && m2y + ey > 0.0f && m2y - ey < hf;
             if (!on_screen) break;
             TileBox bb = tile_bbox(m2x, m2y, ex, ey, u.tbw, u.tbh);
-            for (uint32_t ty = bb.min_y; ty < bb.max_y; ++ty)
-                for (uint32_t tx = bb.min_x; tx < bb.max_x; ++tx)
-                    if (tile_contrib(tx, ty, m2x, m2y, conic, pt)) ++hits;
+            const uint32_t bw = bb.max_x > bb.min_x ? bb.max_x - bb.min_x : 0u;
+            const uint32_t bh = bb.max_y > bb.min_y ? bb.max_y - bb.min_y : 0u;
+            ws = WalkSplat{bb.min_x, bb.min_y, bw, bw * bh, m2x, m2y, conic, pt};
             visible = true;
             depth = mean_c.z;
             radius = bsx_max(ex / wf, ey / hf);
-            // SH colour at the normalised view direction (project_visible.rs:56-71).
-            V3 dv = vsub(mean, u.cam);
-            V3 vdir = vscale(dv, 1.0f / sqrtf(vdot(dv, dv)));
-            constexpr int C3 = (DEG + 1) * (DEG + 1) * 3;
-            float shc[C3];
-            const float* srow = a.sh + (size_t)g * C3;
-            if (C3 % 4 == 0 && a.sh_vec) {
-#pragma unroll
-                for (int k = 0; k < C3 / 4; ++k) {
-                    const float4 q4 = __ldg(reinterpret_cast<const float4*>(srow) + k);
-                    shc[4 * k] = q4.x;
-                    shc[4 * k + 1] = q4.y;
-                    shc[4 * k + 2] = q4.z;
-                    shc[4 * k + 3] = q4.w;
-                }
-            } else {
-#pragma unroll
-                for (int k = 0; k < C3; ++k) shc[k] = __ldg(srow + k);
-            }
-            V3 col = sh_to_color<DEG>(shc, vdir);
-            float cr = col.x + 0.5f, cg = col.y + 0.5f, cb = col.z + 0.5f;
-            cr = bsx_clamp(bsx_is_finite(cr) ? cr : 0.0f, -100.0f, 100.0f);
-            cg = bsx_clamp(bsx_is_finite(cg) ? cg : 0.0f, -100.0f, 100.0f);
-            cb = bsx_clamp(bsx_is_finite(cb) ? cb : 0.0f, -100.0f, 100.0f);
-            float4* row = reinterpret_cast<float4*>(a.projected + (size_t)g * BSX_PROJECTED_LANES);
-            row[0] = make_float4(m2x, m2y, conic.c00, conic.c01);
-            row[1] = make_float4(conic.c11, opac, cr, cg);
-            row[2] = make_float4(cb, mean_c.z, pt, 0.0f);
         } while (false);
+    }
+
+    // Contributing-tile count: the warp walks its splats' boxes together.
+    uint32_t hits = 0;
+    warp_tile_walk(ws, [&](const WalkStep& s) { hits += s.own; });
+
+    if (visible) {
+        // SH colour at the normalised view direction (project_visible.rs:56-71).
+        V3 dv = vsub(mean, u.cam);
+        V3 vdir = vscale(dv, 1.0f / sqrtf(vdot(dv, dv)));
+        constexpr int C3 = (DEG + 1) * (DEG + 1) * 3;
+        float shc[C3];
+        const float* srow = a.sh + (size_t)g * C3;
+        if (C3 % 4 == 0 && a.sh_vec) {
+#pragma unroll
+            for (int k = 0; k < C3 / 4; ++k) {
+                const float4 q4 = __ldg(reinterpret_cast<const float4*>(srow) + k);
+                shc[4 * k] = q4.x;
+                shc[4 * k + 1] = q4.y;
+                shc[4 * k + 2] = q4.z;
+                shc[4 * k + 3] = q4.w;
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < C3; ++k) shc[k] = __ldg(srow + k);
+        }
+        V3 col = sh_to_color<DEG>(shc, vdir);
+        float cr = col.x + 0.5f, cg = col.y + 0.5f, cb = col.z + 0.5f;
+        cr = bsx_clamp(bsx_is_finite(cr) ? cr : 0.0f, -100.0f, 100.0f);
+        cg = bsx_clamp(bsx_is_finite(cg) ? cg : 0.0f, -100.0f, 100.0f);
+        cb = bsx_clamp(bsx_is_finite(cb) ? cb : 0.0f, -100.0f, 100.0f);
+        float4* row = reinterpret_cast<float4*>(a.projected + (size_t)g * BSX_PROJECTED_LANES);
+        row[0] = make_float4(ws.mx, ws.my, ws.conic.c00, ws.conic.c01);
+        row[1] = make_float4(ws.conic.c11, opac, cr, cg);
+        row[2] = make_float4(cb, depth, ws.pt, 0.0f);
+    }
+    if (g < a.n) {
         a.counts[g] = hits;
         a.max_radius[g] = radius;
     }

@@ -7,23 +7,24 @@
 // Each thread replays its pixels front to back exactly as the forward did
 // (same float operations, so T and every accept / early-out decision match the
 // forward bit-for-bit), carrying the residual colour C - T_final*bg - (front
-// contributions) in registers as the reference does. Per splat, a warp whose
-// pixels all lie outside the splat's padded pixel box skips it uniformly;
-// otherwise each lane forms its pixels' contribution to the splat's 10
+// contributions) in registers as the reference does. Per splat, a warp that
+// none of the splat's acceptable pixels reach (the forward's exact footprint
+// test, raster_common.cuh) skips it uniformly; otherwise each lane forms its
+// pixels' contribution to the splat's 10
 // gradient lanes, the warp sums them with a 10-value butterfly (12 shuffles),
 // the sums are accumulated per splat in shared memory across the tile's 4
 // warps, and each (splat, tile) leaves with three 16-byte vector atomics
 // (red.global.add.v4.f32) into a 12-lane row.
 // The alpha / T chain uses exact IEEE operations; the gradient arithmetic,
 // which is tolerance-checked, uses fused multiply-adds and fast reciprocals.
-#include "splat_math.cuh"
+// Colours are clamped once per splat while staging; the colour-gradient
+// gates (raw colour >= 0) are per-splat constants applied once at the flush.
+#include "raster_common.cuh"
 
 namespace bsx {
 
 namespace {
 
-constexpr float kMarginHard = 1.0e-3f;
-constexpr float kMarginSmooth = 0.25f;
 constexpr int kGradLanes = 10;  // xy(2) conic(3) rgb(3) alpha refine
 
 struct BwdArgs {
@@ -36,49 +37,6 @@ struct BwdArgs {
     uint32_t tbw, num_tiles, w, h;
     float bg_r, bg_g, bg_b;
 };
-
-__device__ __forceinline__ float cutoff_weight(float a) {
-    const float mid = 1.0f / 255.0f, band = 1.0e-3f;
-    float t = bsx_clamp((a - (mid - 0.5f * band)) / band, 0.0f, 1.0f);
-    return t * t * (3.0f - 2.0f * t);
-}
-__device__ __forceinline__ float cutoff_weight_deriv(float a) {
-    const float mid = 1.0f / 255.0f, band = 1.0e-3f;
-    const float lo = mid - 0.5f * band, hi = mid + 0.5f * band;
-    const bool inside = a > lo && a < hi;
-    const float t = (a - lo) / band;
-    return inside ? (6.0f * t - 6.0f * t * t) / band : 0.0f;
-}
-
-__device__ __forceinline__ uint32_t compact_bits_16(uint32_t v) {
-    uint32_t x = v & 0x55555555u;
-    x = (x | (x >> 1)) & 0x33333333u;
-    x = (x | (x >> 2)) & 0x0F0F0F0Fu;
-    x = (x | (x >> 4)) & 0x00FF00FFu;
-    x = (x | (x >> 8)) & 0x0000FFFFu;
-    return x;
-}
-
-// Tile-local pixel masks of a splat (bit x: column x, bit 16+y: row y) that
-// can hold a pixel with sigma <= thr: exact ellipse half-extents padded by one
-// pixel. Zero when nothing can pass.
-__device__ __forceinline__ uint32_t splat_pixel_mask(float sx, float sy, float c00, float c01, float c11, float thr,
-                                                     uint32_t ox, uint32_t oy) {
-    const float det = c00 * c11 - c01 * c01;
-    if (!(det > 0.0f) || !(thr >= 0.0f)) return 0u;
-    const float inv = 1.0f / det;
-    const float ex = sqrtf(2.0f * thr * c11 * inv) + 1.0f;
-    const float ey = sqrtf(2.0f * thr * c00 * inv) + 1.0f;
-    const float lx = sx - 0.5f - (float)ox, ly = sy - 0.5f - (float)oy;
-    const int x0 = max(0, (int)floorf(fmaxf(lx - ex, -1.0f)));
-    const int x1 = min(15, (int)ceilf(fminf(lx + ex, 16.0f)));
-    const int y0 = max(0, (int)floorf(fmaxf(ly - ey, -1.0f)));
-    const int y1 = min(15, (int)ceilf(fminf(ly + ey, 16.0f)));
-    if (x0 > x1 || y0 > y1) return 0u;
-    const uint32_t xm = ((0xffffu >> (15 - x1)) >> x0) << x0;
-    const uint32_t ym = ((0xffffu >> (15 - y1)) >> y0) << y0;
-    return xm | (ym << 16);
-}
 
 // Pairwise butterfly step: lanes with `bit` clear keep value k and send k+h,
 // lanes with it set keep k+h and send k; each keeps the pair sum.
@@ -149,8 +107,8 @@ __device__ __forceinline__ void pixel_init(PixelBwd& P, const BwdArgs& a, uint32
 // sigma / alpha / T, then the pixel's gradient contribution added into gv.
 template <bool SMOOTH, bool REFINE>
 __device__ __forceinline__ bool pixel_step(PixelBwd& P, float pcx, float dx0, float xx, float xy, float sx, float sy,
-                                           float c00, float c01, float c11, float ca, float thr, float craw,
-                                           float cgraw, float cbraw, float wf, float hf, float (&gv)[10]) {
+                                           float c00, float c01, float c11, float ca, float thr, float clr,
+                                           float clg, float clb, float wf, float hf, float (&gv)[10]) {
     if (P.done) return false;
     const float dyp = P.pcy - sy;
     const float sigma = 0.5f * (xx + c11 * dyp * dyp) + xy * dyp;
@@ -167,11 +125,11 @@ __device__ __forceinline__ bool pixel_step(PixelBwd& P, float pcx, float dx0, fl
     }
     // gradient arithmetic (tolerance-checked): fused operations allowed
     const float T = P.T;
-    const float clr = bsx_max(craw, 0.0f), clg = bsx_max(cgraw, 0.0f), clb = bsx_max(cbraw, 0.0f);
     const float vis = ae * T;
-    if (craw >= 0.0f) gv[5] = __fmaf_rn(vis, P.vor, gv[5]);
-    if (cgraw >= 0.0f) gv[6] = __fmaf_rn(vis, P.vog, gv[6]);
-    if (cbraw >= 0.0f) gv[7] = __fmaf_rn(vis, P.vob, gv[7]);
+    // colour lanes: gated on raw colour >= 0 at the flush
+    gv[5] = __fmaf_rn(vis, P.vor, gv[5]);
+    gv[6] = __fmaf_rn(vis, P.vog, gv[6]);
+    gv[7] = __fmaf_rn(vis, P.vob, gv[7]);
     const float ra = __fdividef(1.0f, 1.0f - ae);
     float dot_rgb = __fmaf_rn(T, clr, -P.sr) * P.vor;
     dot_rgb = __fmaf_rn(__fmaf_rn(T, clg, -P.sg), P.vog, dot_rgb);
@@ -210,9 +168,9 @@ constexpr int kBwdPixThreads = 128;
 template <bool SMOOTH, bool REFINE>
 __global__ void __launch_bounds__(kBwdPixThreads) raster_bwd_kernel(const BwdArgs a) {
     __shared__ float4 s_a[kBwdPixThreads];  // x, y, c00, c01
-    __shared__ float4 s_b[kBwdPixThreads];  // c11, opacity, r, g
-    __shared__ float2 s_c[kBwdPixThreads];  // b, ln(255 o) + margin
-    __shared__ uint32_t s_mask[kBwdPixThreads];
+    __shared__ float4 s_b[kBwdPixThreads];  // c11, opacity, max(r,0), max(g,0)
+    __shared__ float2 s_c[kBwdPixThreads];  // max(b,0), ln(255 o) + margin
+    __shared__ uint32_t s_mask[kBwdPixThreads];  // bits 0-3 warps, 4-6 colour gates
     __shared__ uint32_t s_gid[kBwdPixThreads];
     __shared__ float s_grad[kBwdPixThreads][kGradLanes + 1];
 
@@ -223,8 +181,7 @@ __global__ void __launch_bounds__(kBwdPixThreads) raster_bwd_kernel(const BwdArg
     if (hi <= lo) return;
     const uint32_t ox = (tile % a.tbw) * kTile, oy = (tile / a.tbw) * kTile;
     const uint32_t lx = compact_bits_16(threadIdx.x), ly = compact_bits_16(threadIdx.x >> 1);
-    const uint32_t wcols = 0xffu << (8 * ((warp >> 1) & 1));
-    const uint32_t wrows = 0x0f0fu << (4 * (warp & 1));
+    const uint32_t wbit = 1u << warp;
     const uint32_t px = ox + lx;
     const float pcx = (float)px + 0.5f;
     const float margin = SMOOTH ? kMarginSmooth : kMarginHard;
@@ -241,17 +198,17 @@ __global__ void __launch_bounds__(kBwdPixThreads) raster_bwd_kernel(const BwdArg
             const float4* row = reinterpret_cast<const float4*>(a.projected + (size_t)g * BSX_PROJECTED_LANES);
             const float4 ra = __ldg(row), rb = __ldg(row + 1), rc = __ldg(row + 2);
             s_a[threadIdx.x] = ra;
-            s_b[threadIdx.x] = rb;
-            s_c[threadIdx.x] = make_float2(rc.x, rc.z + margin);
-            s_mask[threadIdx.x] = splat_pixel_mask(ra.x, ra.y, ra.z, ra.w, rb.x, rc.z + margin, ox, oy);
+            s_b[threadIdx.x] = make_float4(rb.x, rb.y, bsx_max(rb.z, 0.0f), bsx_max(rb.w, 0.0f));
+            s_c[threadIdx.x] = make_float2(bsx_max(rc.x, 0.0f), rc.z + margin);
+            const uint32_t gates = (rb.z >= 0.0f ? 16u : 0u) | (rb.w >= 0.0f ? 32u : 0u) | (rc.x >= 0.0f ? 64u : 0u);
+            s_mask[threadIdx.x] = warp_visit_mask(ra.x, ra.y, ra.z, ra.w, rb.x, rc.z + margin, ox, oy) | gates;
             s_gid[threadIdx.x] = g;
 #pragma unroll
             for (int k = 0; k <= kGradLanes; ++k) s_grad[threadIdx.x][k] = 0.0f;
         }
         __syncthreads();
         for (uint32_t t = 0; t < n; ++t) {
-            const uint32_t m = s_mask[t];
-            if (!(m & wcols) || !((m >> 16) & wrows)) continue;    // warp-uniform
+            if (!(s_mask[t] & wbit)) continue;                      // warp-uniform
             if (__all_sync(0xffffffffu, PA.done && PB.done)) break;  // warp-uniform
             const float4 A = s_a[t];
             const float4 B = s_b[t];
@@ -274,13 +231,16 @@ __global__ void __launch_bounds__(kBwdPixThreads) raster_bwd_kernel(const BwdArg
         __syncthreads();
         if (threadIdx.x < n) {
             const float* sgr = s_grad[threadIdx.x];
+            const uint32_t gates = s_mask[threadIdx.x];
+            const float vr = (gates & 16u) ? sgr[5] : 0.0f, vg = (gates & 32u) ? sgr[6] : 0.0f,
+                        vb = (gates & 64u) ? sgr[7] : 0.0f;
             bool any = false;
 #pragma unroll
             for (int k = 0; k < kGradLanes; ++k) any = any || sgr[k] != 0.0f;
             if (any) {
                 float4* dst = reinterpret_cast<float4*>(a.v_grad + (size_t)s_gid[threadIdx.x] * kGradStride);
                 atomicAdd(dst, make_float4(sgr[0], sgr[1], sgr[2], sgr[3]));
-                atomicAdd(dst + 1, make_float4(sgr[4], sgr[5], sgr[6], sgr[7]));
+                atomicAdd(dst + 1, make_float4(sgr[4], vr, vg, vb));
                 atomicAdd(dst + 2, make_float4(sgr[8], sgr[9], 0.0f, 0.0f));
             }
         }

@@ -1,66 +1,26 @@
 // raster_fwd.cu - tile rasterizer, forward.
 //
 // Restates rasterize_kernel (crates/brush-render/src/kernels/rasterize.rs:24-200):
-// one 256-thread block per 16x16 tile, one pixel per thread in the
-// reference's Morton order (helpers.rs:54-81, so each warp covers an 8x4
-// patch), front-to-back compositing over the tile's depth-sorted splats in
-// batches of 256 staged in shared memory. Per pair:
+// one 128-thread block per 16x16 tile, two pixels per thread (the layout in
+// raster_common.cuh), front-to-back compositing over the tile's depth-sorted
+// splats in batches of 128 staged in shared memory. Per pair:
 //   sigma = 0.5*(c00 dx^2 + c11 dy^2) + c01 dx dy,  alpha = min(0.999, o e^-sigma)
 //   accept iff sigma >= 0 and alpha >= 1/255; stop before accumulating once
 //   T*(1-alpha) <= 1e-4.
 // B200 specifics: the block-wide early-out is a __syncthreads_count vote;
-// pairs whose sigma exceeds ln(255*o) + margin (where alpha < 1/255 is
-// certain) skip the exponential, which leaves every decision and every
-// accumulated value bit-identical; visibility marks are collected per batch
-// in shared memory and written once per splat instead of once per pixel.
-#include "splat_math.cuh"
+// while a batch is staged, each splat gets a 4-bit mask of the warps whose
+// pixels it can reach (exact minimum of sigma over each warp's footprint), so
+// a warp skips splats none of its pixels can accept; pairs whose sigma
+// exceeds ln(255*o) + margin (where alpha < 1/255 is certain) skip the
+// exponential; colours are clamped once per splat while staging. Every
+// decision and every accumulated value stays bit-identical. Visibility marks
+// are collected per batch in shared memory and written once per splat instead
+// of once per pixel.
+#include "raster_common.cuh"
 
 namespace bsx {
 
 namespace {
-
-// Rejection margin on sigma for the exponential-free pre-filter. With the
-// hard cutoff the exact test is sigma <= ln(255 o) up to a few ulp of the
-// shared exp/ln; the smooth ramp starts at alpha = 1/255 - 5e-4, i.e.
-// ln(255 o) + 0.137.
-constexpr float kMarginHard = 1.0e-3f;
-constexpr float kMarginSmooth = 0.25f;
-
-__device__ __forceinline__ uint32_t compact_bits_16(uint32_t v) {
-    uint32_t x = v & 0x55555555u;
-    x = (x | (x >> 1)) & 0x33333333u;
-    x = (x | (x >> 2)) & 0x0F0F0F0Fu;
-    x = (x | (x >> 4)) & 0x00FF00FFu;
-    x = (x | (x >> 8)) & 0x0000FFFFu;
-    return x;
-}
-
-__device__ __forceinline__ float cutoff_weight(float a) {
-    const float mid = 1.0f / 255.0f, band = 1.0e-3f;
-    float t = bsx_clamp((a - (mid - 0.5f * band)) / band, 0.0f, 1.0f);
-    return t * t * (3.0f - 2.0f * t);
-}
-
-// Tile-local pixel masks of a splat: bit x of the low half / bit y of the high
-// half is set when column x / row y of the tile can hold a pixel with
-// sigma <= thr (exact ellipse half-extents, padded by one pixel).
-__device__ __forceinline__ uint32_t splat_pixel_mask(float sx, float sy, float c00, float c01, float c11, float thr,
-                                                     uint32_t ox, uint32_t oy) {
-    const float det = c00 * c11 - c01 * c01;
-    if (!(det > 0.0f) || !(thr >= 0.0f)) return 0u;
-    const float inv = 1.0f / det;
-    const float ex = sqrtf(2.0f * thr * c11 * inv) + 1.0f;
-    const float ey = sqrtf(2.0f * thr * c00 * inv) + 1.0f;
-    const float lx = sx - 0.5f - (float)ox, ly = sy - 0.5f - (float)oy;
-    const int x0 = max(0, (int)floorf(fmaxf(lx - ex, -1.0f)));
-    const int x1 = min(15, (int)ceilf(fminf(lx + ex, 16.0f)));
-    const int y0 = max(0, (int)floorf(fmaxf(ly - ey, -1.0f)));
-    const int y1 = min(15, (int)ceilf(fminf(ly + ey, 16.0f)));
-    if (x0 > x1 || y0 > y1) return 0u;
-    const uint32_t xm = ((0xffffu >> (15 - x1)) >> x0) << x0;
-    const uint32_t ym = ((0xffffu >> (15 - y1)) >> y0) << y0;
-    return xm | (ym << 16);
-}
 
 struct FwdArgs {
     const uint32_t* isect_gid;
@@ -80,8 +40,8 @@ constexpr int kFwdThreads = 128;
 template <bool BWD, bool SMOOTH>
 __global__ void __launch_bounds__(kFwdThreads) raster_fwd_kernel(const FwdArgs a) {
     __shared__ float4 s_a[kFwdThreads];  // x, y, c00, c01
-    __shared__ float4 s_b[kFwdThreads];  // c11, opacity, r, g
-    __shared__ float2 s_c[kFwdThreads];  // b, ln(255 o) + margin
+    __shared__ float4 s_b[kFwdThreads];  // c11, opacity, max(r,0), max(g,0)
+    __shared__ float2 s_c[kFwdThreads];  // max(b,0), ln(255 o) + margin
     __shared__ uint32_t s_mask[kFwdThreads];
     __shared__ uint32_t s_gid[BWD ? kFwdThreads : 1];
     __shared__ int s_used[BWD ? kFwdThreads : 1];
@@ -90,9 +50,7 @@ __global__ void __launch_bounds__(kFwdThreads) raster_fwd_kernel(const FwdArgs a
     const uint32_t tile = blockIdx.x;
     const uint32_t tx = tile % a.tbw, ty = tile / a.tbw;
     const uint32_t lx = compact_bits_16(threadIdx.x), ly = compact_bits_16(threadIdx.x >> 1);
-    const uint32_t wid = threadIdx.x >> 5;
-    const uint32_t wcols = 0xffu << (8 * ((wid >> 1) & 1));
-    const uint32_t wrows = 0x0f0fu << (4 * (wid & 1));  // rows r..r+3 and r+8..r+11
+    const uint32_t wbit = 1u << (threadIdx.x >> 5);
     const uint32_t px = tx * kTile + lx, pyA = ty * kTile + ly, pyB = pyA + 8;
     const bool inA = px < a.w && pyA < a.h, inB = px < a.w && pyB < a.h;
     const float pcx = (float)px + 0.5f, pcyA = (float)pyA + 0.5f, pcyB = (float)pyB + 0.5f;
@@ -115,10 +73,10 @@ __global__ void __launch_bounds__(kFwdThreads) raster_fwd_kernel(const FwdArgs a
             const float4* row = reinterpret_cast<const float4*>(a.projected + (size_t)g * BSX_PROJECTED_LANES);
             const float4 ra = __ldg(row), rb = __ldg(row + 1), rc = __ldg(row + 2);
             s_a[threadIdx.x] = ra;
-            s_b[threadIdx.x] = rb;
-            s_c[threadIdx.x] = make_float2(rc.x, rc.z + margin);
+            s_b[threadIdx.x] = make_float4(rb.x, rb.y, bsx_max(rb.z, 0.0f), bsx_max(rb.w, 0.0f));
+            s_c[threadIdx.x] = make_float2(bsx_max(rc.x, 0.0f), rc.z + margin);
             s_mask[threadIdx.x] =
-                splat_pixel_mask(ra.x, ra.y, ra.z, ra.w, rb.x, rc.z + margin, tx * kTile, ty * kTile);
+                warp_visit_mask(ra.x, ra.y, ra.z, ra.w, rb.x, rc.z + margin, tx * kTile, ty * kTile);
             if (BWD) {
                 s_gid[threadIdx.x] = g;
                 s_used[threadIdx.x] = 0;
@@ -126,8 +84,7 @@ __global__ void __launch_bounds__(kFwdThreads) raster_fwd_kernel(const FwdArgs a
         }
         __syncthreads();
         for (uint32_t t = 0; t < n && !(doneA && doneB); ++t) {
-            const uint32_t m = s_mask[t];
-            if (!(m & wcols) || !((m >> 16) & wrows)) continue;
+            if (!(s_mask[t] & wbit)) continue;
             const float4 A = s_a[t];
             const float c11 = s_b[t].x;
             const float thr = s_c[t].y;
@@ -157,13 +114,13 @@ __global__ void __launch_bounds__(kFwdThreads) raster_fwd_kernel(const FwdArgs a
                 const float vis = ae * T;
                 const float cb = s_c[t].x;
                 if (q) {
-                    rB += bsx_max(B.z, 0.0f) * vis;
-                    gB += bsx_max(B.w, 0.0f) * vis;
-                    bB += bsx_max(cb, 0.0f) * vis;
+                    rB += B.z * vis;
+                    gB += B.w * vis;
+                    bB += cb * vis;
                 } else {
-                    rA += bsx_max(B.z, 0.0f) * vis;
-                    gA += bsx_max(B.w, 0.0f) * vis;
-                    bA += bsx_max(cb, 0.0f) * vis;
+                    rA += B.z * vis;
+                    gA += B.w * vis;
+                    bA += cb * vis;
                 }
                 T = next_t;
                 used = true;

@@ -1387,4 +1387,17 @@ void orc_rasterize_rows(const float* rows10, uint32_t count, uint32_t w, uint32_
 float orc_expf(float x) { return bsx_expf(x); }
 float orc_logf(float x) { return bsx_logf(x); }
 
+// Number of floats in [-|lo|, 0] (every bit pattern from -0 to lo) where the
+// rasterizers' bsx_expf_neg differs in any bit from bsx_expf.
+uint64_t orc_expf_neg_mismatches(float lo) {
+    const uint32_t last = bsx_f32_to_bits(-fabsf(lo));
+    uint64_t bad = 0;
+#pragma omp parallel for reduction(+ : bad) schedule(static)
+    for (int64_t b = 0x80000000ll; b <= (int64_t)last; ++b) {
+        const float x = bsx_bits_to_f32((uint32_t)b);
+        bad += bsx_f32_to_bits(bsx_expf_neg(x)) != bsx_f32_to_bits(bsx_expf(x));
+    }
+    return bad;
+}
+
 }  // extern "C"

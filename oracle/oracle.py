@@ -102,6 +102,8 @@ def lib() -> C.CDLL:
         _lib.orc_expf.restype = C.c_float
         _lib.orc_expf.argtypes = [C.c_float]
         _lib.orc_logf.restype = C.c_float
+        _lib.orc_expf_neg_mismatches.restype = C.c_uint64
+        _lib.orc_expf_neg_mismatches.argtypes = [C.c_float]
         _lib.orc_logf.argtypes = [C.c_float]
         _lib.orc_set_threads.argtypes = [C.c_int]
         _lib.orc_get_threads.restype = C.c_int
@@ -283,6 +285,11 @@ def expf(x: float) -> float:
 
 def logf(x: float) -> float:
     return float(lib().orc_logf(float(x)))
+
+
+def expf_neg_mismatches(lo: float) -> int:
+    """Floats in [lo, 0] where the rasterizers' exp differs from bsx_expf (full sweep)."""
+    return int(lib().orc_expf_neg_mismatches(float(lo)))
 
 
 def refine_cfg(**kw) -> RefineCfg:

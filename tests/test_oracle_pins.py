@@ -105,6 +105,11 @@ def test_shared_exp_log_accuracy(orc):
         assert abs(np.int64(np.float32(lg).view(np.int32)) - np.int64(ref.view(np.int32))) <= 2
 
 
+def test_raster_exp_bit_identical_on_its_domain(orc):
+    """bsx_expf_neg (the rasterizers' exp) equals bsx_expf on every float in [-80, 0]."""
+    assert orc.expf_neg_mismatches(-80.0) == 0
+
+
 def test_gauss_taps_normalised(orc):
     w = orc.gauss_taps()
     assert abs(float(w.sum()) - 1.0) < 1e-6 and np.allclose(w, w[::-1])
