@@ -4,10 +4,13 @@
 // 4-bit digits, five kernels per pass). Here: one histogram kernel reads the
 // keys once for every pass, then one kernel per 8-bit digit pass ("onesweep",
 // Adinets & Merrill 2022): each 4096-key tile takes a ticket, ranks its keys
-// stably with warp-level match/ballot multi-split, publishes its per-digit
-// counts, looks back over predecessors' per-digit prefixes (bounded waits),
-// and scatters through shared memory so that global writes are runs of
-// consecutive addresses.
+// stably with a warp-level ballot multi-split (the lanes holding the same
+// digit are found by one ballot per digit bit, cheaper here than a match
+// instruction), publishes its per-digit counts, looks back over
+// predecessors' per-digit prefixes (bounded waits), and scatters through
+// shared memory so that global writes are runs of consecutive addresses. The
+// pass is register-bounded to four resident blocks per SM (64 registers):
+// occupancy, not arithmetic, sets its speed.
 //
 // Semantics match the reference: the order is by (key & mask) where mask
 // keeps ceil(bits/4)*4 low bits; equal keys keep their input order; the
@@ -60,7 +63,7 @@ struct PassArgs {
     int* err;
 };
 
-__global__ void __launch_bounds__(kSortThreads) sort_pass_kernel(const PassArgs a) {
+__global__ void __launch_bounds__(kSortThreads, 4) sort_pass_kernel(const PassArgs a) {
     __shared__ uint32_t s_tile;
     __shared__ uint32_t s_warp_hist[kSortWarps][kRadix + 1];
     __shared__ uint32_t s_block_start[kRadix];
@@ -92,7 +95,15 @@ __global__ void __launch_bounds__(kSortThreads) sort_pass_kernel(const PassArgs 
     // Stable per-warp multi-split: items in order, lanes in order.
 #pragma unroll
     for (int i = 0; i < kSortItems; ++i) {
-        uint32_t peers = __match_any_sync(0xffffffffu, dig[i]);
+        // lanes with the same digit: agree on validity and on each of the 8 bits
+        uint32_t peers = __ballot_sync(0xffffffffu, dig[i] < kRadix);
+        if (dig[i] >= kRadix) peers = ~peers;
+#pragma unroll
+        for (int b = 0; b < 8; ++b) {
+            const bool bit = (dig[i] >> b) & 1;
+            const uint32_t bal = __ballot_sync(0xffffffffu, bit);
+            peers &= bit ? bal : ~bal;
+        }
         uint32_t before = peers & lt_mask;
         uint32_t base = s_warp_hist[warp][dig[i]];
         __syncwarp();
