@@ -29,6 +29,7 @@ STATUS_NAMES = {
     5: "BSX_ERR_CUDA",
     6: "BSX_ERR_STATE",
     7: "BSX_ERR_UNSUPPORTED",
+    8: "BSX_ERR_FORMAT",
 }
 
 RENDER_DEFAULT, RENDER_MIP = 0, 1
@@ -219,6 +220,19 @@ class RefineStats(C.Structure):
                                                  "num_pruned", "num_pruned_non_finite", "total_splats")]
 
 
+class PlyInfo(C.Structure):
+    _fields_ = [
+        ("num_splats", C.c_uint32),
+        ("total_rows", C.c_uint32),
+        ("sh_coeffs", C.c_uint32),
+        ("subsample", C.c_uint32),
+        ("compressed", C.c_int32),
+        ("render_mode", C.c_int32),
+        ("has_up_axis", C.c_int32),
+        ("up_axis", C.c_float * 3),
+    ]
+
+
 # name -> (restype, argtypes); exactly the functions include/bsx.h declares.
 SIGNATURES = {
     "bsx_create": (C.c_int, [C.c_int, C.POINTER(C.c_void_p)]),
@@ -312,6 +326,18 @@ SIGNATURES = {
     "bsx_prefix_sum_u32": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32, C.c_void_p]),
     "bsx_prefix_sum_u32_noalloc": (C.c_int, [C.c_void_p, C.c_uint32, C.c_void_p, C.c_void_p]),
     "bsx_get_tile_offsets": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p]),
+    "bsx_ply_parse": (
+        C.c_int, [C.c_void_p, C.c_size_t, C.c_uint32, C.POINTER(C.c_void_p), C.POINTER(PlyInfo), C.c_char_p,
+                  C.c_size_t]
+    ),
+    "bsx_ply_free": (None, [C.c_void_p]),
+    "bsx_ply_load": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "bsx_ply_export_size": (C.c_int, [C.c_uint32, C.c_uint32, C.c_int32, C.POINTER(C.c_float),
+                                      C.POINTER(C.c_uint64)]),
+    "bsx_ply_export": (
+        C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_int32,
+                  C.POINTER(C.c_float), C.c_void_p, C.c_uint64, C.POINTER(C.c_uint64)]
+    ),
 }
 
 _LIB = None

@@ -107,6 +107,7 @@ const char* bsx_status_string(bsx_status s) {
         case BSX_ERR_CUDA: return "CUDA error";
         case BSX_ERR_STATE: return "invalid call order";
         case BSX_ERR_UNSUPPORTED: return "unsupported";
+        case BSX_ERR_FORMAT: return "malformed file";
     }
     return "unknown status";
 }

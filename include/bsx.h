@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define BSX_ABI_VERSION 1
+#define BSX_ABI_VERSION 2
 /* Gradient lanes per splat written by the raster backward:
  * xy(2) conic(3) rgb(3) alpha refine depth. Reference:
  * crates/brush-render-bwd/src/kernels/rasterize_backwards.rs:40 */
@@ -55,7 +55,8 @@ typedef enum bsx_status {
     BSX_ERR_DEVICE_TIMEOUT = 4,/* a bounded device-side wait gave up */
     BSX_ERR_CUDA = 5,          /* a CUDA runtime call failed */
     BSX_ERR_STATE = 6,         /* call order violated (e.g. backward without forward) */
-    BSX_ERR_UNSUPPORTED = 7    /* valid request this build does not implement */
+    BSX_ERR_UNSUPPORTED = 7,   /* valid request this build does not implement */
+    BSX_ERR_FORMAT = 8         /* malformed or unsupported file contents (PLY import) */
 } bsx_status;
 
 typedef enum bsx_render_mode { BSX_RENDER_DEFAULT = 0, BSX_RENDER_MIP = 1 } bsx_render_mode;
@@ -442,6 +443,45 @@ BSX_API bsx_status bsx_prefix_sum_u32_noalloc(const uint32_t* d_in, uint32_t n, 
  * (crates/brush-render/src/get_tile_offset.rs:10-62). d_offsets is zeroed first. */
 BSX_API bsx_status bsx_get_tile_offsets(bsx_ctx* ctx, const uint32_t* d_tile_ids, uint32_t n, uint32_t num_tiles,
                                 uint32_t* d_offsets);
+
+/* ---- splat PLY import / export (crates/brush-serde) ----
+ * bsx_ply_parse reads the header and the row layout of a PLY byte buffer
+ * (ascii, binary_little_endian or binary_big_endian; the standard 3DGS vertex
+ * properties, or the SuperSplat compressed chunk/vertex/sh layout), validates
+ * it as stream_splat_from_ply does (crates/brush-serde/src/import.rs:180-333)
+ * and keeps every subsample-th row. It needs no GPU. On BSX_ERR_FORMAT, err
+ * receives the reason (the reference's messages). For little-endian binary
+ * input the parsed file refers to `bytes`, which must stay valid and unchanged
+ * until the stream has executed bsx_ply_load.
+ * bsx_ply_load decodes on the device into the splat layout: transforms
+ * [N,10] (mean, quaternion w x y z, log-scale), sh [N, sh_coeffs, 3]
+ * (coefficient-major) and raw opacities [N], N = info.num_splats. Absent
+ * fields take the reference's defaults (import.rs:77-95).
+ * bsx_ply_export writes splat_to_ply's file (crates/brush-serde/src/export.rs:
+ * 84-191: binary little-endian, quaternion normalised, SH rest in the
+ * channel-major order of the 3DGS format) into host memory; up_axis may be
+ * NULL ("Vertical axis: y"). It synchronises the context's stream. */
+typedef struct bsx_ply_info {
+    uint32_t num_splats;   /* rows kept after subsampling */
+    uint32_t total_rows;   /* vertex rows in the file */
+    uint32_t sh_coeffs;    /* SH coefficients per channel of the decoded splats */
+    uint32_t subsample;
+    int32_t compressed;    /* SuperSplat compressed layout */
+    int32_t render_mode;   /* -1 none, 0 default, 1 mip ("SplatRenderMode:" comment) */
+    int32_t has_up_axis;   /* "Vertical axis:" comment */
+    float up_axis[3];
+} bsx_ply_info;
+typedef struct bsx_ply_file bsx_ply_file;
+BSX_API bsx_status bsx_ply_parse(const uint8_t* bytes, size_t len, uint32_t subsample, bsx_ply_file** out,
+                                 bsx_ply_info* info, char* err, size_t err_len);
+BSX_API void bsx_ply_free(bsx_ply_file* f);
+BSX_API bsx_status bsx_ply_load(bsx_ctx* ctx, const bsx_ply_file* f, float* d_transforms, float* d_sh,
+                                float* d_raw_opac);
+BSX_API bsx_status bsx_ply_export_size(uint32_t n, uint32_t sh_coeffs, int32_t mip, const float* up_axis,
+                                       uint64_t* bytes);
+BSX_API bsx_status bsx_ply_export(bsx_ctx* ctx, const float* d_transforms, const float* d_sh,
+                                  const float* d_raw_opac, uint32_t n, uint32_t sh_coeffs, int32_t mip,
+                                  const float* up_axis, uint8_t* host_out, uint64_t capacity, uint64_t* written);
 
 #ifdef __cplusplus
 }

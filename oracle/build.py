@@ -13,7 +13,7 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 OUT = HERE / "_build" / "liboracle.so"
-SRCS = [HERE / "oracle.cpp", HERE / "refine.cpp"]
+SRCS = [HERE / "oracle.cpp", HERE / "refine.cpp", HERE / "ply.cpp"]
 DEPS = SRCS + [HERE.parent / "include" / "bsx.h", HERE.parent / "include" / "bsx_fmath.h"]
 
 

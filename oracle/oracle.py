@@ -102,6 +102,12 @@ def lib() -> C.CDLL:
         _lib.orc_expf.restype = C.c_float
         _lib.orc_expf.argtypes = [C.c_float]
         _lib.orc_logf.restype = C.c_float
+        _lib.orc_ply_decode.restype = C.c_int
+        _lib.orc_ply_decode.argtypes = [C.c_char_p, C.c_size_t, C.c_uint32, C.POINTER(C.c_uint32),
+                                        C.POINTER(C.c_uint32), C.c_void_p, C.c_void_p, C.c_void_p, C.c_char_p,
+                                        C.c_size_t]
+        _lib.orc_ply_encode_rows.restype = C.c_uint64
+        _lib.orc_ply_encode_rows.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p]
         _lib.orc_expf_neg_mismatches.restype = C.c_uint64
         _lib.orc_expf_neg_mismatches.argtypes = [C.c_float]
         _lib.orc_logf.argtypes = [C.c_float]
@@ -285,6 +291,33 @@ def expf(x: float) -> float:
 
 def logf(x: float) -> float:
     return float(lib().orc_logf(float(x)))
+
+
+def ply_decode(data: bytes, subsample: int = 1):
+    """CPU restatement of load_splat_from_ply: (transforms [N,10], sh [N,C,3], opacities [N])."""
+    n, c = C.c_uint32(), C.c_uint32()
+    err = C.create_string_buffer(512)
+    if lib().orc_ply_decode(data, len(data), subsample, C.byref(n), C.byref(c), None, None, None, err, 512):
+        raise ValueError(err.value.decode())
+    t = np.zeros((n.value, 10), np.float32)
+    sh = np.zeros((n.value, c.value, 3), np.float32)
+    op = np.zeros(n.value, np.float32)
+    if lib().orc_ply_decode(data, len(data), subsample, C.byref(n), C.byref(c), t.ctypes.data, sh.ctypes.data,
+                            op.ctypes.data, err, 512):
+        raise ValueError(err.value.decode())
+    return t, sh, op
+
+
+def ply_encode_rows(t, sh, op) -> bytes:
+    """The vertex rows splat_to_ply writes (without the header)."""
+    t, sh, op = _f32(t).reshape(-1, 10), _f32(sh), _f32(op).reshape(-1)
+    n = t.shape[0]
+    c = sh.reshape(n, -1, 3).shape[1]
+    sh = sh.reshape(n, c, 3)
+    size = lib().orc_ply_encode_rows(t.ctypes.data, sh.ctypes.data, op.ctypes.data, n, c, None)
+    out = np.zeros(size, np.uint8)
+    lib().orc_ply_encode_rows(t.ctypes.data, sh.ctypes.data, op.ctypes.data, n, c, out.ctypes.data)
+    return out.tobytes()
 
 
 def expf_neg_mismatches(lo: float) -> int:
