@@ -148,6 +148,8 @@ WORKLOADS = {
     "cfg4": ("cfg4: densification run from 100k splats SH3 1280x720, 100 hemisphere views, refine every 100 "
              "steps (growth threshold 2e-4, prune opacity < 0.005, growth fraction 0.1, cap 1.5M)"),
     "cfg5": "cfg5: 6M splats SH3 3840x2160 render-only forward (viewer path, packed RGBA8), 120-frame circle",
+    "ply": "ply: 1M splats SH3 (cfg2 scene) as a binary little-endian 3DGS PLY in pinned host memory -> device "
+           "splats (import), and back (export)",
 }
 
 
@@ -443,6 +445,103 @@ def run_ours(args, rank, world, local_rank):
     return line
 
 
+def run_ply(args, rank, world, local_rank):
+    """PLY import / export throughput (splats/s) through the public API's C entry points:
+    each import step parses the header and uploads + decodes every row; each export
+    step encodes and reads the file back into pinned host memory."""
+    import ctypes as C
+
+    import torch
+
+    from brush_b200 import _lib
+    from brush_b200 import splats as S
+    from brush_b200._context import context, ptr
+    from brush_b200.ply import export_into, export_size, load_splat_from_ply
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    splats, _, _, _ = S.config2_scene(dev, seed=2)
+    size = export_size(splats)
+    host = torch.empty(size, dtype=torch.uint8).pin_memory()
+    n_file = export_into(splats, host)
+    L = _lib.lib()
+    ctx = context(dev)
+    ctx.bind_stream()
+    n, c = splats.num_splats, splats.sh_coeffs_per_splat
+    t = torch.empty((n, 10), device=dev)
+    sh = torch.empty((n, c, 3), device=dev)
+    op = torch.empty((n,), device=dev)
+    err = C.create_string_buffer(256)
+
+    def import_step():
+        h = C.c_void_p()
+        info = _lib.PlyInfo()
+        if L.bsx_ply_parse(host.data_ptr(), n_file, 1, C.byref(h), C.byref(info), err, 256):
+            raise RuntimeError(err.value.decode())
+        try:
+            ctx.check(L.bsx_ply_load(ctx.handle, h, ptr(t), ptr(sh), ptr(op)))
+        finally:
+            L.bsx_ply_free(h)
+
+    out = torch.empty(size, dtype=torch.uint8).pin_memory()
+
+    def export_step():
+        export_into(splats, out)
+
+    for _ in range(args.warmup):
+        import_step()
+        export_step()
+    torch.cuda.synchronize()
+    assert torch.equal(sh, splats.sh_coeffs) and torch.equal(out[:n_file], host[:n_file])
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    h0 = time.monotonic()
+    l0 = ctx.launches()
+    ms_imp = _time_region(args, world, lambda: [import_step() for _ in range(args.steps)])
+    launches = ctx.launches() - l0
+    ms_exp = _time_region(args, world, lambda: [export_step() for _ in range(args.steps)])
+    sampler.mark(h0, time.monotonic())
+    clocks = sampler.stop()
+    ctx.profile_reset()
+    ctx.profile(True)
+    for _ in range(args.steps):
+        import_step()
+        export_step()
+    torch.cuda.synchronize()
+    ctx.profile(False)
+    prof = ctx.profile_read()
+    peak, peak_kind = _peaks()
+    row_bytes = (14 + 3 * (c - 1)) * 4
+    splat_bytes = 4 * (10 + 3 * c + 1)
+    kernels = {}
+    for name, (tot, cnt) in prof.items():
+        alg = n * (row_bytes + splat_bytes)
+        kernels[name] = {"launches": cnt, "avg_ms": round(tot / cnt, 4), "alg_bytes": alg,
+                         "gbs": round(alg / (tot / cnt * 1e-3) / 1e9, 1)}
+    dec = kernels.get("ply_decode_kernel", {"gbs": 0.0, "avg_ms": 0.0})
+    value = world * n * args.steps / (ms_imp * 1e-3)
+    line = {
+        "metric": "PLY import splats/s (1M splats SH3, pinned host file bytes -> device splats)",
+        "value": round(value, 1), "unit": "splats/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_imp / args.steps, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded cfg2 scene written as PLY)",
+        "config": {"workload": WORKLOADS["ply"], "splats": n, "sh_degree": splats.sh_degree,
+                   "file_bytes": n_file, "l2": "inputs larger than L2"},
+        "e2e": {"value": round(value, 1), "unit": "splats/s", "h2d_bytes_per_step": n_file,
+                "d2h_bytes_per_step": 0},
+        "export": {"value": round(world * n * args.steps / (ms_exp * 1e-3), 1), "unit": "splats/s",
+                   "ms_per_step": round(ms_exp / args.steps, 4), "d2h_bytes_per_step": n_file},
+        "gpu_launches": launches,
+        "roofline": {"bound": "hbm", "kernel": "ply_decode_kernel", "achieved": dec["gbs"], "peak": peak,
+                     "unit": "GB/s", "frac": round(dec["gbs"] / peak, 4), "traffic": None, "peak_source": peak_kind,
+                     "note": "the import is bound by the host-to-device copy of the file; the decode kernel "
+                             "is the device part"},
+        "h2d_gbs": round(n_file / (ms_imp / args.steps * 1e-3) / 1e9, 1),
+        "kernels": kernels, "clocks": clocks,
+    }
+    return line
+
+
 def cpu_baseline_sample(workload="cfg2"):
     """One oracle step (all host threads) on the same workload: a full training step, or a
     forward render for the render-only workload. Returns (seconds, threads)."""
@@ -455,6 +554,15 @@ def cpu_baseline_sample(workload="cfg2"):
         splats, cam, size, gt = S.config1_scene("cpu", seed=1)
     elif workload == "cfg3":
         raise ValueError("cfg3 has no CPU sample (its targets are rendered by the GPU library)")
+    elif workload == "ply":
+        # the CPU restatement's decode of a 20 000-row sample of the same file, scaled per splat
+        import torch
+
+        sp, _, _, _ = S.config2_scene("cpu", seed=2, n=20000)
+        data = _ply_host_bytes(sp)
+        t0 = time.perf_counter()
+        orc.ply_decode(data)
+        return (time.perf_counter() - t0) * (1_000_000 / 20000), 1
     elif workload == "cfg5":
         splats, size = S.config5_scene("cpu", seed=5)
         cam = S.circle_cameras(120, 8.0, size[0], size[1])[0]
@@ -486,6 +594,27 @@ def cpu_baseline_sample(workload="cfg2"):
     return time.perf_counter() - t0, orc.threads()
 
 
+def _ply_host_bytes(sp) -> bytes:
+    """The 3DGS binary PLY of CPU splats, written with numpy (same layout as splat_to_ply)."""
+    import numpy as np
+
+    t = sp.transforms.numpy()
+    sh = sp.sh_coeffs.numpy()
+    op = sp.raw_opacities.numpy()
+    n, c = t.shape[0], sh.shape[1]
+    q = t[:, 3:7]
+    rn = np.maximum(np.sqrt(((q[:, 0] * q[:, 0] + q[:, 1] * q[:, 1]) + q[:, 2] * q[:, 2]) + q[:, 3] * q[:, 3]),
+                    np.float32(1e-12))
+    cols = [t[:, 0], t[:, 1], t[:, 2], t[:, 7], t[:, 8], t[:, 9], op] + [q[:, k] / rn for k in range(4)]
+    cols += [sh[:, 0, k] for k in range(3)] + [sh[:, k, ch] for ch in range(3) for k in range(1, c)]
+    rows = np.stack(cols, 1).astype("<f4")
+    names = ["x", "y", "z", "scale_0", "scale_1", "scale_2", "opacity", "rot_0", "rot_1", "rot_2", "rot_3",
+             "f_dc_0", "f_dc_1", "f_dc_2"] + [f"f_rest_{k}" for k in range(3 * (c - 1))]
+    head = "ply\nformat binary_little_endian 1.0\nelement vertex %d\n" % n
+    head += "".join(f"property float {nm}\n" for nm in names) + "end_header\n"
+    return head.encode() + rows.tobytes()
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return None
@@ -497,6 +626,23 @@ def run_reference(args, rank, world):
     orc.set_threads(os.cpu_count() or 1)
     if args.workload == "cfg3":
         return {"impl": "reference", "unavailable": "cfg3 targets are rendered by the GPU library; no CPU sample"}
+    if args.workload == "ply":
+        times = []
+        for i in range(args.warmup + args.steps):
+            dt, cores = cpu_baseline_sample("ply")
+            if i >= args.warmup:
+                times.append(dt)
+        value = 1_000_000 * args.steps / sum(times)
+        return {"impl": "reference", "metric": "PLY import splats/s (1M splats SH3, pinned host file bytes -> "
+                "device splats)", "value": round(value, 1), "unit": "splats/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * sum(times) / args.steps, 2),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (seeded cfg2 scene written as PLY)", "config": {"workload": WORKLOADS["ply"]},
+                "cpu_baseline": {"value": round(value, 1), "unit": "splats/s", "cores": 1, "kind": "port",
+                                 "sample": "the CPU restatement's decode of a 20 000-row sample of the same file, "
+                                           "scaled to 1M splats"},
+                "e2e": {"value": round(value, 1), "unit": "splats/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
     times = []
     for i in range(args.warmup + args.steps):
         dt, cores = cpu_baseline_sample(args.workload)
@@ -556,7 +702,10 @@ def main():
         bbuild.build()
     if world > 1:
         torch.distributed.barrier()
-    line = run_ours(args, rank, world, local_rank)
+    if args.workload == "ply":
+        line = run_ply(args, rank, world, local_rank)
+    else:
+        line = run_ours(args, rank, world, local_rank)
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload != "cfg3":
         from oracle import build as obuild
 
@@ -565,9 +714,15 @@ def main():
 
         orc.set_threads(os.cpu_count() or 1)
         dt, cores = cpu_baseline_sample(args.workload)
-        what = "forward render" if args.workload == "cfg5" else "train step"
-        line["cpu_baseline"] = {"value": round(1.0 / dt, 5), "unit": line["unit"], "cores": cores, "kind": "port",
-                                "sample": f"one full {args.workload} {what} on the CPU restatement, all host threads"}
+        if args.workload == "ply":
+            line["cpu_baseline"] = {"value": round(1_000_000 / dt, 1), "unit": "splats/s", "cores": cores,
+                                    "kind": "port", "sample": "the CPU restatement's decode of a 20 000-row sample "
+                                                              "of the same file, scaled to 1M splats"}
+        else:
+            what = "forward render" if args.workload == "cfg5" else "train step"
+            line["cpu_baseline"] = {"value": round(1.0 / dt, 5), "unit": line["unit"], "cores": cores,
+                                    "kind": "port",
+                                    "sample": f"one full {args.workload} {what} on the CPU restatement, all host threads"}
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()

@@ -52,7 +52,11 @@ class Camera(C.Structure):
         ("position", C.c_float * 3),
         ("rotation", C.c_float * 4),
         ("camera_model", C.c_int32),
+        ("model_params", C.c_float * 8),
     ]
+
+
+CAMERA_PINHOLE, CAMERA_KANNALA_BRANDT_4, CAMERA_RADIAL_TANGENTIAL_8, CAMERA_THIN_PRISM_FISHEYE = 0, 1, 2, 3
 
 
 class ProjectUniforms(C.Structure):
@@ -75,6 +79,8 @@ class ProjectUniforms(C.Structure):
         ("sh_degree", C.c_uint32),
         ("total_splats", C.c_uint32),
         ("num_visible", C.c_uint32),
+        ("camera_model", C.c_int32),
+        ("model_params", C.c_float * 8),
     ]
 
 

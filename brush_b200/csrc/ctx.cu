@@ -250,10 +250,51 @@ bsx_status bsx_profile_reset(bsx_ctx* ctx) {
 // camera.rs:49-101 (focal, centre, world_to_local via glam's Affine3A
 // inverse), camera.rs:200-254 (pinhole Jacobian clamp limits) and
 // render.rs:116-136 (uniform assembly).
+// Per-model focal length and Jacobian clamp (crates/brush-render/src/camera.rs:85-254), in f64 like
+// the reference. p holds the model's f32 coefficients (bsx_camera_model).
+static double kb4_d(double theta, const float* p) {
+    const double t2 = theta * theta, t3 = t2 * theta, t5 = t3 * t2, t7 = t5 * t2, t9 = t7 * t2;
+    return theta + (double)p[0] * t3 + (double)p[1] * t5 + (double)p[2] * t7 + (double)p[3] * t9;
+}
+static double rt8_radial(double r, const float* p) {
+    const double r2 = r * r, r4 = r2 * r2, r6 = r4 * r2;
+    const double num = 1.0 + (double)p[0] * r2 + (double)p[1] * r4 + (double)p[2] * r6;
+    const double den = 1.0 + (double)p[3] * r2 + (double)p[4] * r4 + (double)p[5] * r6;
+    return num / den;
+}
+static double rt8_undistort_radius(double r_d, const float* p) {
+    double r = r_d;
+    for (int i = 0; i < 30; ++i) {
+        const double factor = rt8_radial(r, p);
+        if (std::fabs(factor) < 1e-12) break;
+        const double r_new = r_d / factor;
+        if (std::fabs(r_new - r) < 1e-12) {
+            r = r_new;
+            break;
+        }
+        r = r_new;
+    }
+    return r;
+}
+static double model_fov_to_focal(double fov, uint32_t pixels, int model, const float* p) {
+    const double half = fov / 2.0;
+    double proj = std::tan(half);
+    if (model == BSX_CAMERA_KANNALA_BRANDT_4 || model == BSX_CAMERA_THIN_PRISM_FISHEYE) proj = kb4_d(half, p);
+    else if (model == BSX_CAMERA_RADIAL_TANGENTIAL_8) proj = proj * rt8_radial(proj, p);
+    return ((double)pixels / 2.0) / proj;
+}
+static float rt8_undistort_edge(float edge, const float* p) {
+    const float mag = (float)rt8_undistort_radius((double)std::fabs(edge), p);
+    return mag * (std::signbit(edge) ? -1.0f : 1.0f);
+}
+
 bsx_status bsx_make_project_uniforms(const bsx_camera* cam, uint32_t w, uint32_t h, uint32_t sh_degree,
                                      uint32_t total, bsx_project_uniforms* out) {
     if (!cam || !out || w == 0 || h == 0) return BSX_ERR_INVALID_ARG;
-    if (cam->camera_model != BSX_CAMERA_PINHOLE) return BSX_ERR_UNSUPPORTED;
+    if (cam->camera_model < BSX_CAMERA_PINHOLE || cam->camera_model > BSX_CAMERA_THIN_PRISM_FISHEYE)
+        return BSX_ERR_INVALID_ARG;
+    const int model = cam->camera_model;
+    const float* kp = cam->model_params;
     // Rotation matrix columns from the (x, y, z, w) quaternion.
     const float qx = cam->rotation[0], qy = cam->rotation[1], qz = cam->rotation[2], qw = cam->rotation[3];
     const float x2 = qx + qx, y2 = qy + qy, z2 = qz + qz;
@@ -296,8 +337,8 @@ bsx_status bsx_make_project_uniforms(const bsx_camera* cam, uint32_t w, uint32_t
     out->viewmat[9] = -mp[0];
     out->viewmat[10] = -mp[1];
     out->viewmat[11] = -mp[2];
-    const double fx = ((double)w / 2.0) / std::tan(cam->fov_x / 2.0);
-    const double fy = ((double)h / 2.0) / std::tan(cam->fov_y / 2.0);
+    const double fx = model_fov_to_focal(cam->fov_x, w, model, kp);
+    const double fy = model_fov_to_focal(cam->fov_y, h, model, kp);
     out->fx = (float)fx;
     out->fy = (float)fy;
     out->cx = cam->center_uv[0] * (float)w;
@@ -308,10 +349,20 @@ bsx_status bsx_make_project_uniforms(const bsx_camera* cam, uint32_t w, uint32_t
     const float hyp = std::hypot((float)cam->fov_x, (float)cam->fov_y);
     out->half_max_render_fov = fminf(hyp * 1.05f, 2.0f * 3.14159265358979323846f - 1e-6f) * 0.5f;
     const float wf = (float)w, hf = (float)h;
-    out->lim_pos_x = (1.15f * wf - out->cx) / out->fx;
-    out->lim_pos_y = (1.15f * hf - out->cy) / out->fy;
-    out->lim_neg_x = (-0.15f * wf - out->cx) / out->fx;
-    out->lim_neg_y = (-0.15f * hf - out->cy) / out->fy;
+    if (model == BSX_CAMERA_PINHOLE || model == BSX_CAMERA_RADIAL_TANGENTIAL_8) {
+        out->lim_pos_x = (1.15f * wf - out->cx) / out->fx;
+        out->lim_pos_y = (1.15f * hf - out->cy) / out->fy;
+        out->lim_neg_x = (-0.15f * wf - out->cx) / out->fx;
+        out->lim_neg_y = (-0.15f * hf - out->cy) / out->fy;
+        if (model == BSX_CAMERA_RADIAL_TANGENTIAL_8) {  // undistorted bounds (camera.rs:227-240)
+            out->lim_pos_x = rt8_undistort_edge(out->lim_pos_x, kp);
+            out->lim_pos_y = rt8_undistort_edge(out->lim_pos_y, kp);
+            out->lim_neg_x = rt8_undistort_edge(out->lim_neg_x, kp);
+            out->lim_neg_y = rt8_undistort_edge(out->lim_neg_y, kp);
+        }
+    }  // fisheye models: no clamp, limits stay 0 (camera.rs:241-244)
+    out->camera_model = model;
+    for (int k = 0; k < BSX_CAMERA_PARAMS; ++k) out->model_params[k] = kp[k];
     out->img_w = w;
     out->img_h = h;
     out->tile_bw = (w + kTile - 1) / kTile;

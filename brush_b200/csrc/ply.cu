@@ -107,9 +107,12 @@ __device__ __forceinline__ uint32_t load_bytes(const uint8_t* p, uint32_t n) {
     return v;
 }
 
-// Numeric field as f32, serde's primitive conversion ("as" casts).
+// Numeric field as f32, serde's primitive conversion ("as" casts). 4-byte
+// fields at 4-byte aligned offsets of 4-byte aligned rows (the usual all-float
+// file) take one word load.
 __device__ __forceinline__ float read_num(const uint8_t* row, Field f) {
     const uint8_t* p = row + f.offset;
+    if (f.type == kF32 && !(reinterpret_cast<uintptr_t>(p) & 3u)) return __ldg(reinterpret_cast<const float*>(p));
     switch (f.type) {
         case kI8: return (float)(int8_t)p[0];
         case kU8: return (float)p[0];
@@ -273,13 +276,9 @@ struct EncArgs {
     uint8_t* out;  // rows of (14 + 3 (coeffs - 1)) little-endian f32
 };
 
-__device__ __forceinline__ void put_f32(uint8_t* p, float v) {
-    const uint32_t b = __float_as_uint(v);
-    p[0] = (uint8_t)b;
-    p[1] = (uint8_t)(b >> 8);
-    p[2] = (uint8_t)(b >> 16);
-    p[3] = (uint8_t)(b >> 24);
-}
+// Rows are whole 4-byte words and the staging buffer is aligned: word stores
+// (the device is little-endian like the file).
+__device__ __forceinline__ void put_f32(uint8_t* p, float v) { *reinterpret_cast<float*>(p) = v; }
 
 // read_splat_data (export.rs:84-167): x y z, scale_0..2, opacity, rot_0..3
 // normalised by max(|q|, 1e-12), f_dc_0..2, f_rest_{channel * rest + k}.

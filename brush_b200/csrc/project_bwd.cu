@@ -2,8 +2,8 @@
 //
 // Restates project_backwards_kernel
 // (crates/brush-render-bwd/src/kernels/project_backwards.rs:19-263): conic
-// VJP -> 2D covariance VJP -> EWA/pinhole Jacobian VJP
-// (kernels/camera_model/pinhole.rs:58-123) -> rotation/scale VJP, plus the SH
+// VJP -> 2D covariance VJP -> projection Jacobian VJP of the camera model
+// (kernels/camera_model/, camera_models.cuh) -> rotation/scale VJP, plus the SH
 // coefficient VJP and the view-direction VJP into the mean (kernels/sh.rs).
 // One thread per splat over all N rows; rows without gradient are written as
 // zeros, so no separate zero-fill of the dense outputs is needed.
@@ -36,6 +36,41 @@ struct PbArgs {
 __device__ __forceinline__ V3 s3mul(const S3& s, V3 v) {
     return vadd(vadd(vscale(v3(s.c00, s.c01, s.c02), v.x), vscale(v3(s.c01, s.c11, s.c12), v.y)),
                 vscale(v3(s.c02, s.c12, s.c22), v.z));
+}
+
+// Pinhole projection VJP (pinhole.rs:58-123).
+__device__ __forceinline__ V3 vjp_pinhole(const M23& J, V3 mean_c, const S3& cov_c, const Uni& u, S2 vcov,
+                                          float vmx, float vmy) {
+    const float mx = mean_c.x, my = mean_c.y, mz = mean_c.z;
+    const float inv_z = 1.0f / mz;
+    const float mxr = mx * inv_z, myr = my * inv_z;
+    const float mxc = bsx_clamp(mxr, u.lnx, u.lpx), myc = bsx_clamp(myr, u.lny, u.lpy);
+    const bool in_x = mxr <= u.lpx && mxr >= u.lnx;
+    const bool in_y = myr <= u.lpy && myr >= u.lny;
+    const float iz2 = inv_z * inv_z, iz3 = iz2 * inv_z;
+    float v_mx = u.fx * inv_z * vmx;
+    float v_my = u.fy * inv_z * vmy;
+    float v_mz = -(u.fx * mx * vmx + u.fy * my * vmy) * iz2;
+    const VJRows vj = vj_rows(J, vcov, cov_c);
+    const float vj00 = vj.u0, vj11 = vj.v1, vj20 = vj.u2, vj21 = vj.v2;
+    const float txv = mz * mxc, tyv = mz * myc;
+    if (in_x) v_mx += -u.fx * iz2 * vj20;
+    else v_mz += -u.fx * iz3 * vj20 * txv;
+    if (in_y) v_my += -u.fy * iz2 * vj21;
+    else v_mz += -u.fy * iz3 * vj21 * tyv;
+    v_mz += -u.fx * iz2 * vj00 - u.fy * iz2 * vj11 + 2.0f * u.fx * txv * iz3 * vj20 + 2.0f * u.fy * tyv * iz3 * vj21;
+    return v3(v_mx, v_my, v_mz);
+}
+
+// calculate_projection_vjp (camera_model/mod.rs:88-136)
+__device__ __forceinline__ V3 projection_vjp(const M23& J, V3 mean_c, const S3& cov_c, const Uni& u, S2 vcov,
+                                             float vmx, float vmy) {
+    switch (u.model) {
+        case BSX_CAMERA_KANNALA_BRANDT_4: return vjp_kb4(J, mean_c, cov_c, u, vcov, vmx, vmy, u.kp);
+        case BSX_CAMERA_RADIAL_TANGENTIAL_8: return vjp_rt8(mean_c, cov_c, u, vcov, vmx, vmy, u.kp);
+        case BSX_CAMERA_THIN_PRISM_FISHEYE: return vjp_tpf(J, mean_c, cov_c, u, vcov, vmx, vmy, u.kp);
+        default: return vjp_pinhole(J, mean_c, cov_c, u, vcov, vmx, vmy);
+    }
 }
 
 // Row index of element i of a staged block (i < 2^15, cols <= 80).
@@ -71,7 +106,9 @@ struct PbShape {
     static constexpr int GS = 13;                  // gradient row stride (odd)
 };
 
-template <int DEG>
+// PINHOLE: the launch's camera is a pinhole, fixed at compile time so the
+// fisheye models' code stays out of the common kernel.
+template <int DEG, bool PINHOLE>
 __global__ void __launch_bounds__(PbShape<DEG>::R) project_bwd_kernel(const PbArgs a) {
     using S = PbShape<DEG>;
     constexpr int C3 = S::C3;
@@ -101,7 +138,8 @@ __global__ void __launch_bounds__(PbShape<DEG>::R) project_bwd_kernel(const PbAr
             a.v_opac[g] = 0.0f;
             a.v_refine[g] = 0.0f;
         } else {
-            const Uni& u = a.u;
+            Uni u = a.u;
+            if (PINHOLE) u.model = BSX_CAMERA_PINHOLE;
             const float vmx = rg[0], vmy = rg[1], vcx = rg[2], vcy = rg[3], vcz = rg[4];
             const V3 vcol = v3(rg[5], rg[6], rg[7]);
             const float valpha = rg[8], vref = rg[9], vdep = rg[10];
@@ -145,19 +183,7 @@ __global__ void __launch_bounds__(PbShape<DEG>::R) project_bwd_kernel(const PbAr
             const V3 sr0 = s3mul(covar, vr0), sr1 = s3mul(covar, vr1), sr2 = s3mul(covar, vr2);
             const S3 cov_c{vdot(vr0, sr0), vdot(vr0, sr1), vdot(vr0, sr2),
                            vdot(vr1, sr1), vdot(vr1, sr2), vdot(vr2, sr2)};
-            const M23 J = pinhole_jacobian(mean_c, u);
-
-            // pinhole projection VJP (pinhole.rs:180-245)
-            const float mx = mean_c.x, my = mean_c.y, mz = mean_c.z;
-            const float inv_z = 1.0f / mz;
-            const float mxr = mx * inv_z, myr = my * inv_z;
-            const float mxc = bsx_clamp(mxr, u.lnx, u.lpx), myc = bsx_clamp(myr, u.lny, u.lpy);
-            const bool in_x = mxr <= u.lpx && mxr >= u.lnx;
-            const bool in_y = myr <= u.lpy && myr >= u.lny;
-            const float iz2 = inv_z * inv_z, iz3 = iz2 * inv_z;
-            float v_mx = u.fx * inv_z * vmx;
-            float v_my = u.fy * inv_z * vmy;
-            float v_mz = -(u.fx * mx * vmx + u.fy * my * vmy) * iz2;
+            const M23 J = project_jacobian(mean_c, u);
             const float jc[3][2] = {{J.c0x, J.c0y}, {J.c1x, J.c1y}, {J.c2x, J.c2y}};
             float tmp[3][2];
 #pragma unroll
@@ -165,20 +191,8 @@ __global__ void __launch_bounds__(PbShape<DEG>::R) project_bwd_kernel(const PbAr
                 tmp[c][0] = vcov.c00 * jc[c][0] + vcov.c01 * jc[c][1];
                 tmp[c][1] = vcov.c01 * jc[c][0] + vcov.c11 * jc[c][1];
             }
-            const V3 tr0 = v3(tmp[0][0], tmp[1][0], tmp[2][0]), tr1 = v3(tmp[0][1], tmp[1][1], tmp[2][1]);
-            const V3 cr0 = v3(cov_c.c00, cov_c.c01, cov_c.c02), cr1 = v3(cov_c.c01, cov_c.c11, cov_c.c12),
-                     cr2 = v3(cov_c.c02, cov_c.c12, cov_c.c22);
-            const float vj00 = 2.0f * vdot(tr0, cr0);
-            const float vj11 = 2.0f * vdot(tr1, cr1);
-            const float vj20 = 2.0f * vdot(tr0, cr2);
-            const float vj21 = 2.0f * vdot(tr1, cr2);
-            const float txv = mz * mxc, tyv = mz * myc;
-            if (in_x) v_mx += -u.fx * iz2 * vj20;
-            else v_mz += -u.fx * iz3 * vj20 * txv;
-            if (in_y) v_my += -u.fy * iz2 * vj21;
-            else v_mz += -u.fy * iz3 * vj21 * tyv;
-            v_mz += -u.fx * iz2 * vj00 - u.fy * iz2 * vj11 + 2.0f * u.fx * txv * iz3 * vj20 +
-                    2.0f * u.fy * tyv * iz3 * vj21;
+            const V3 pv = projection_vjp(J, mean_c, cov_c, u, vcov, vmx, vmy);
+            const float v_mx = pv.x, v_my = pv.y, v_mz = pv.z;
             const V3 v_mean_c = v3(v_mx, v_my, v_mz + vdep);
 
             // J^T v_cov2d J (Mat2x3::transpose_congruence_sym2)
@@ -231,7 +245,8 @@ __global__ void __launch_bounds__(PbShape<DEG>::R) project_bwd_kernel(const PbAr
 template <int DEG>
 void launch_deg(const PbArgs& a, cudaStream_t st) {
     constexpr int R = PbShape<DEG>::R;
-    project_bwd_kernel<DEG><<<(a.n + R - 1) / R, R, 0, st>>>(a);
+    if (a.u.model == BSX_CAMERA_PINHOLE) project_bwd_kernel<DEG, true><<<(a.n + R - 1) / R, R, 0, st>>>(a);
+    else project_bwd_kernel<DEG, false><<<(a.n + R - 1) / R, R, 0, st>>>(a);
 }
 
 }  // namespace

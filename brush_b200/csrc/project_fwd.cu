@@ -80,7 +80,12 @@ __global__ void __launch_bounds__(kProjThreads) project_fwd_kernel(const __grid_
             mean = v3(t[0], t[1], t[2]);
             V3 mean_c = vadd(mmul(u.rot, mean), u.trans);
             if (!(vfinite(mean_c) && mean_c.z <= 1.0e10f)) break;
-            if (mean_c.z < 0.01f) break;
+            if (u.model == BSX_CAMERA_PINHOLE) {
+                if (mean_c.z < 0.01f) break;
+            } else {  // fisheye-capable models cull by the ray angle (project_forward.rs:49-64)
+                const float rr = sqrtf(mean_c.x * mean_c.x + mean_c.y * mean_c.y);
+                if (bsx_atan2f(rr, mean_c.z) > u.half_max_fov) break;
+            }
             V3 scl = v3(bsx_expf(t[7]), bsx_expf(t[8]), bsx_expf(t[9]));
             if (!vfinite(scl)) break;
             Q4 qu{t[3], t[4], t[5], t[6]};
@@ -94,9 +99,8 @@ __global__ void __launch_bounds__(kProjThreads) project_fwd_kernel(const __grid_
             S2 cov = compensate_cov2d(raw, a.mip != 0, &fc);
             opac = bsx_sigmoid(ro) * fc;
             if (!s2finite(cov)) break;
-            float inv_z = 1.0f / mean_c.z;
-            float m2x = u.fx * mean_c.x * inv_z + u.cx;
-            float m2y = u.fy * mean_c.y * inv_z + u.cy;
+            float m2x, m2y;
+            project_mean(mean_c, u, &m2x, &m2y);
             if (!(opac >= 1.0f / 255.0f)) break;
             float pt = bsx_logf(opac * 255.0f);
             S2 conic = sym2_inverse(cov);

@@ -76,6 +76,9 @@ struct Uni {
     float lpx, lpy, lnx, lny;
     V3 cam;
     uint32_t w, h, tbw, tbh;
+    float half_max_fov;
+    int model;       // bsx_camera_model
+    float kp[BSX_CAMERA_PARAMS];
 };
 
 inline Uni make_uni(const bsx_project_uniforms& u) {
@@ -89,6 +92,9 @@ inline Uni make_uni(const bsx_project_uniforms& u) {
     r.lpx = u.lim_pos_x; r.lpy = u.lim_pos_y; r.lnx = u.lim_neg_x; r.lny = u.lim_neg_y;
     r.cam = V3{u.camera_pos[0], u.camera_pos[1], u.camera_pos[2]};
     r.w = u.img_w; r.h = u.img_h; r.tbw = u.tile_bw; r.tbh = u.tile_bh;
+    r.half_max_fov = u.half_max_render_fov;
+    r.model = u.camera_model;
+    for (int k = 0; k < BSX_CAMERA_PARAMS; ++k) r.kp[k] = u.model_params[k];
     return r;
 }
 
@@ -102,10 +108,12 @@ __device__ __forceinline__ M23 pinhole_jacobian(V3 p, const Uni& u) {
     return M23{dx, 0.0f, 0.0f, dy, -dx * cx, -dy * cy};
 }
 
-// calc_cov2d (helpers.rs:297-330)
+__device__ __forceinline__ M23 project_jacobian(V3 p, const Uni& u);  // camera_models.cuh
+
+// calc_cov2d (helpers.rs:297-330) with the camera model's projection Jacobian
 __device__ __forceinline__ S2 calc_cov2d(V3 scl, Q4 q, V3 mean_c, const Uni& u) {
     M3 ns = mdiag(mmulm(u.rot, quat_to_mat3(q)), scl);
-    M23 j = pinhole_jacobian(mean_c, u);
+    M23 j = project_jacobian(mean_c, u);
     // V = J * ns, column i = (J.c0*n.x + J.c1*n.y) + J.c2*n.z
     float v0x = (j.c0x * ns.c0.x + j.c1x * ns.c0.y) + j.c2x * ns.c0.z;
     float v0y = (j.c0y * ns.c0.x + j.c1y * ns.c0.y) + j.c2y * ns.c0.z;
@@ -190,3 +198,5 @@ __device__ __forceinline__ bool tile_contrib(uint32_t tx, uint32_t ty, float mx,
 }
 
 }  // namespace bsx
+
+#include "camera_models.cuh"

@@ -13,6 +13,7 @@ import os
 from dataclasses import dataclass
 from typing import BinaryIO, Optional, Sequence, Union
 
+import numpy as np
 import torch
 
 from . import _lib
@@ -37,27 +38,41 @@ class SplatMessage:
     compressed: bool = False
 
 
-def _read_bytes(source) -> bytes:
-    if isinstance(source, (bytes, bytearray, memoryview)):
-        return bytes(source)
+def _host_view(source):
+    """(keep-alive object, address, length) of the file bytes without copying them
+    where possible: bytes, bytearray, a uint8 numpy array or a CPU uint8 tensor (pinned
+    memory makes the upload asynchronous); paths and readers are read once."""
     if isinstance(source, (str, os.PathLike)):
         with open(source, "rb") as fh:
-            return fh.read()
-    return source.read()
+            source = fh.read()
+    elif hasattr(source, "read"):
+        source = source.read()
+    if isinstance(source, memoryview):
+        source = source.tobytes()
+    if isinstance(source, bytes):
+        return source, C.cast(C.c_char_p(source), C.c_void_p).value, len(source)
+    if isinstance(source, bytearray):
+        buf = (C.c_uint8 * max(len(source), 1)).from_buffer(source) if source else None
+        return (source, buf), (C.addressof(buf) if buf is not None else None), len(source)
+    if isinstance(source, torch.Tensor):
+        if source.device.type != "cpu" or source.dtype != torch.uint8 or not source.is_contiguous():
+            raise ValueError("expected a contiguous CPU uint8 tensor of file bytes")
+        return source, source.data_ptr(), source.numel()
+    arr = np.ascontiguousarray(np.asarray(source, dtype=np.uint8))
+    return arr, arr.ctypes.data, arr.size
 
 
 def load_splat_from_ply(source: Union[bytes, str, os.PathLike, BinaryIO], subsample_points: Optional[int] = None,
                         device: Union[str, torch.device] = "cuda") -> SplatMessage:
     """Decode a PLY (standard 3DGS properties, RGB colours, or the SuperSplat compressed
     layout) into device-resident Splats. ``subsample_points`` keeps every k-th row."""
-    data = _read_bytes(source)
+    keep, addr, size = _host_view(source)
     sub = 1 if subsample_points is None else int(subsample_points)
-    buf = (C.c_uint8 * max(len(data), 1)).from_buffer_copy(data if data else b"\0")
     info = _lib.PlyInfo()
     handle = C.c_void_p()
     err = C.create_string_buffer(512)
     L = _lib.lib()
-    status = L.bsx_ply_parse(buf, len(data), sub, C.byref(handle), C.byref(info), err, len(err))
+    status = L.bsx_ply_parse(addr, size, sub, C.byref(handle), C.byref(info), err, len(err))
     if status != 0:
         msg = err.value.decode() or L.bsx_status_string(status).decode()
         raise _lib.BsxError(status, msg)
@@ -72,7 +87,7 @@ def load_splat_from_ply(source: Union[bytes, str, os.PathLike, BinaryIO], subsam
         ctx = context(dev)
         ctx.bind_stream()
         ctx.check(L.bsx_ply_load(ctx.handle, handle, ptr(t), ptr(sh), ptr(op)))
-        ctx.sync()  # the upload reads `buf`
+        ctx.sync()  # the upload reads the caller's bytes
     finally:
         L.bsx_ply_free(handle)
     up = tuple(float(v) for v in info.up_axis) if info.has_up_axis else None
@@ -84,6 +99,27 @@ def load_splat_from_ply(source: Union[bytes, str, os.PathLike, BinaryIO], subsam
 def splat_to_ply(splats: Splats, up_axis: Optional[Sequence[float]] = None, mip: Optional[bool] = None) -> bytes:
     """The binary little-endian PLY of ``splats`` (quaternions normalised, SH rest in the
     3DGS channel-major order), with the reference's header comments."""
+    size = export_size(splats, up_axis, mip)
+    out = bytearray(size)
+    n = export_into(splats, out, up_axis, mip)
+    return bytes(memoryview(out)[:n])
+
+
+def export_size(splats: Splats, up_axis: Optional[Sequence[float]] = None, mip: Optional[bool] = None) -> int:
+    """Bytes of ``splat_to_ply(splats, ...)``."""
+    c = int(splats.sh_coeffs.shape[1])
+    render_mip = bool(splats.render_mode == _lib.RENDER_MIP) if mip is None else bool(mip)
+    up = (C.c_float * 3)(*[float(v) for v in up_axis]) if up_axis is not None else None
+    size = C.c_uint64()
+    status = _lib.lib().bsx_ply_export_size(splats.num_splats, c, int(render_mip), up, C.byref(size))
+    if status != 0:
+        raise _lib.BsxError(status, f"cannot export {c} SH coefficients per channel (degrees 0-3)")
+    return int(size.value)
+
+
+def export_into(splats: Splats, out, up_axis: Optional[Sequence[float]] = None, mip: Optional[bool] = None) -> int:
+    """Writes the PLY into ``out`` (a bytearray, uint8 numpy array or CPU uint8 tensor,
+    pinned memory for an asynchronous read-back) and returns its length."""
     t = splats.transforms.detach().float().contiguous()
     sh = splats.sh_coeffs.detach().float().contiguous()
     op = splats.raw_opacities.detach().float().contiguous()
@@ -92,15 +128,10 @@ def splat_to_ply(splats: Splats, up_axis: Optional[Sequence[float]] = None, mip:
     n, c = int(t.shape[0]), int(sh.shape[1])
     render_mip = bool(splats.render_mode == _lib.RENDER_MIP) if mip is None else bool(mip)
     up = (C.c_float * 3)(*[float(v) for v in up_axis]) if up_axis is not None else None
-    L = _lib.lib()
-    size = C.c_uint64()
-    status = L.bsx_ply_export_size(n, c, int(render_mip), up, C.byref(size))
-    if status != 0:
-        raise _lib.BsxError(status, f"cannot export {c} SH coefficients per channel (degrees 0-3)")
-    out = (C.c_uint8 * int(size.value))()
+    keep, addr, cap = _host_view(out)
     written = C.c_uint64()
     ctx = context(t.device)
     ctx.bind_stream()
-    ctx.check(L.bsx_ply_export(ctx.handle, ptr(t), ptr(sh), ptr(op), n, c, int(render_mip), up, out,
-                               size.value, C.byref(written)))
-    return bytes(out)[: int(written.value)]
+    ctx.check(_lib.lib().bsx_ply_export(ctx.handle, ptr(t), ptr(sh), ptr(op), n, c, int(render_mip), up, addr,
+                                        cap, C.byref(written)))
+    return int(written.value)

@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define BSX_ABI_VERSION 2
+#define BSX_ABI_VERSION 3
 /* Gradient lanes per splat written by the raster backward:
  * xy(2) conic(3) rgb(3) alpha refine depth. Reference:
  * crates/brush-render-bwd/src/kernels/rasterize_backwards.rs:40 */
@@ -68,7 +68,18 @@ typedef enum bsx_raster_pass {
     BSX_PASS_BACKWARD_SMOOTH_CUTOFF = 2 /* as BACKWARD with the C^1 alpha-cutoff ramp */
 } bsx_raster_pass;
 
-typedef enum bsx_camera_model { BSX_CAMERA_PINHOLE = 0 } bsx_camera_model;
+/* crates/brush-render/src/kernels/camera_model/mod.rs:30-37; the distortion
+ * coefficients travel in model_params (unused entries ignored):
+ *   KANNALA_BRANDT_4   k1 k2 k3 k4                    (kannala_brandt_4.rs:11-16)
+ *   RADIAL_TANGENTIAL_8 k1 k2 k3 k4 k5 k6 p1 p2       (radial_tangential_8.rs:11-20)
+ *   THIN_PRISM_FISHEYE k1 k2 k3 k4 p1 p2 sx1 sy1      (thin_prism_fisheye.rs:22-29) */
+typedef enum bsx_camera_model {
+    BSX_CAMERA_PINHOLE = 0,
+    BSX_CAMERA_KANNALA_BRANDT_4 = 1,
+    BSX_CAMERA_RADIAL_TANGENTIAL_8 = 2,
+    BSX_CAMERA_THIN_PRISM_FISHEYE = 3
+} bsx_camera_model;
+#define BSX_CAMERA_PARAMS 8
 
 /* crates/brush-render/src/camera.rs:11-19 */
 typedef struct bsx_camera {
@@ -78,6 +89,7 @@ typedef struct bsx_camera {
     float position[3];     /* camera centre, world space */
     float rotation[4];     /* camera-to-world rotation quaternion (x, y, z, w) */
     int32_t camera_model;  /* bsx_camera_model */
+    float model_params[BSX_CAMERA_PARAMS];
 } bsx_camera;
 
 /* crates/brush-render/src/kernels/types.rs:53-83 (ProjectUniforms). */
@@ -92,6 +104,8 @@ typedef struct bsx_project_uniforms {
     uint32_t sh_degree;
     uint32_t total_splats;
     uint32_t num_visible;
+    int32_t camera_model;  /* bsx_camera_model */
+    float model_params[BSX_CAMERA_PARAMS];
 } bsx_project_uniforms;
 
 /* Device outputs of one forward render (crates/brush-render/src/render_aux.rs:16-68).

@@ -179,6 +179,59 @@ BSX_HD float bsx_logf(float x) {
     return bsx_fma(ef, 0.693145751953125f, bsx_fma(ef, 1.428606765330187e-06f, lnm));
 }
 
+/* atan(t) for t in [0, 1]. Above tan(pi/12) the argument is reduced by the
+ * addition formula atan(t) = pi/6 + atan((t - c) / (1 + t c)), c = 1/sqrt(3),
+ * which leaves |t'| <= tan(pi/12) = 0.268; then the Maclaurin series
+ * t - t^3/3 + t^5/5 - ... to t^17/17 (truncation < 8e-13). */
+BSX_HD float bsx_atan_unit(float t) {
+    const float kTanPi12 = 0.2679491937160492f;
+    const float kInvSqrt3 = 0.5773502588272095f;
+    const float kPi6Hi = 0.5235987901687622f;     /* float(pi/6) */
+    const float kPi6Lo = -2.2841566377645488e-08f; /* pi/6 - kPi6Hi */
+    int reduced = t > kTanPi12;
+    float x = reduced ? (t - kInvSqrt3) / bsx_fma(t, kInvSqrt3, 1.0f) : t;
+    float x2 = x * x;
+    float p = 0.05882352963089943f;             /* 1/17 */
+    p = bsx_fma(p, x2, -0.06666667014360428f);  /* -1/15 */
+    p = bsx_fma(p, x2, 0.07692307978868484f);   /* 1/13 */
+    p = bsx_fma(p, x2, -0.09090909361839294f);  /* -1/11 */
+    p = bsx_fma(p, x2, 0.1111111119389534f);    /* 1/9 */
+    p = bsx_fma(p, x2, -0.1428571492433548f);   /* -1/7 */
+    p = bsx_fma(p, x2, 0.20000000298023224f);   /* 1/5 */
+    p = bsx_fma(p, x2, -0.3333333432674408f);   /* -1/3 */
+    float r = bsx_fma(x * x2, p, x);
+    return reduced ? (kPi6Hi + (r + kPi6Lo)) : r;
+}
+
+/* atan2(y, x) in float32 with the C library's quadrant and special-value
+ * conventions: the ratio of the smaller to the larger magnitude goes through
+ * bsx_atan_unit, then pi/2 - r, pi - r and the sign of y place it. */
+BSX_HD float bsx_atan2f(float y, float x) {
+    const float kPi2Hi = 1.5707963705062866f, kPi2Lo = -4.371139000186243e-08f;
+    const float kPiHi = 3.1415927410125732f, kPiLo = -8.742278000372485e-08f;
+    if (x != x || y != y) return x + y;
+    float ax = x < 0.0f ? -x : x, ay = y < 0.0f ? -y : y;
+    int neg_x = (bsx_f32_to_bits(x) >> 31) != 0;
+    int neg_y = (bsx_f32_to_bits(y) >> 31) != 0;
+    float r;
+    if (ay == 0.0f) {
+        r = neg_x ? kPiHi : 0.0f;
+    } else if (ax == bsx_bits_to_f32(0x7f800000u) && ay == ax) {
+        r = neg_x ? 2.356194496154785f : 0.7853981852531433f; /* 3pi/4, pi/4 */
+    } else if (ax == bsx_bits_to_f32(0x7f800000u)) {
+        r = neg_x ? kPiHi : 0.0f;
+    } else if (ay == bsx_bits_to_f32(0x7f800000u) || ax == 0.0f) {
+        r = kPi2Hi;
+    } else {
+        int swap = ay > ax;
+        float t = swap ? ax / ay : ay / ax;
+        r = bsx_atan_unit(t);
+        if (swap) r = kPi2Hi + (kPi2Lo - r);
+        if (neg_x) r = kPiHi + (kPiLo - r);
+    }
+    return neg_y ? -r : r;
+}
+
 /* Logistic sigmoid, same expression as the reference: 1 / (1 + e^-x). */
 BSX_HD float bsx_sigmoid(float x) { return 1.0f / (1.0f + bsx_expf(-x)); }
 

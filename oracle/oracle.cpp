@@ -111,6 +111,9 @@ struct Uni {
     float lpx, lpy, lnx, lny;
     V3 cam;
     uint32_t w, h, tbw, tbh;
+    float half_max_fov;
+    int model;
+    float kp[8];
 };
 
 Uni uni_from(const bsx_project_uniforms& u) {
@@ -122,6 +125,9 @@ Uni uni_from(const bsx_project_uniforms& u) {
     r.lpx = u.lim_pos_x; r.lpy = u.lim_pos_y; r.lnx = u.lim_neg_x; r.lny = u.lim_neg_y;
     r.cam = v3(u.camera_pos[0], u.camera_pos[1], u.camera_pos[2]);
     r.w = u.img_w; r.h = u.img_h; r.tbw = u.tile_bw; r.tbh = u.tile_bh;
+    r.half_max_fov = u.half_max_render_fov;
+    r.model = u.camera_model;
+    for (int k = 0; k < 8; ++k) r.kp[k] = u.model_params[k];
     return r;
 }
 
@@ -138,6 +144,32 @@ inline M23 pinhole_jacobian(V3 p, const Uni& u) {
     j.c[2][0] = -dx * cxv; j.c[2][1] = -dy * cyv;
     return j;
 }
+#include "camera_models.h"
+
+inline cam::Intr intr_of(const Uni& u) { return cam::Intr{u.fx, u.fy, u.cx, u.cy, u.lpx, u.lpy, u.lnx, u.lny, u.kp}; }
+
+// camera_model/mod.rs:48-85: projection and its Jacobian per model
+inline void project_point(V3 p, const Uni& u, float* px, float* py) {
+    switch (u.model) {
+        case 1: cam::kb4_project(p, intr_of(u), px, py); return;
+        case 2: cam::rt8_project(p, intr_of(u), px, py); return;
+        case 3: cam::tpf_project(p, intr_of(u), px, py); return;
+        default: {  // pinhole.rs:24-30
+            float inv_z = 1.0f / p.z;
+            *px = u.fx * p.x * inv_z + u.cx;
+            *py = u.fy * p.y * inv_z + u.cy;
+        }
+    }
+}
+inline M23 model_jacobian(V3 p, const Uni& u) {
+    switch (u.model) {
+        case 1: return cam::kb4_jacobian(p, intr_of(u));
+        case 2: return cam::rt8_jacobian(p, intr_of(u));
+        case 3: return cam::tpf_jacobian(p, intr_of(u));
+        default: return pinhole_jacobian(p, u);
+    }
+}
+
 // brush-cube/src/lib.rs:333-347  Mat2x3 * v = (c0*x + c1*y) + c2*z
 inline void m23_mul_vec3(const M23& m, V3 v, float out[2]) {
     out[0] = (m.c[0][0] * v.x + m.c[1][0] * v.y) + m.c[2][0] * v.z;
@@ -147,7 +179,7 @@ inline void m23_mul_vec3(const M23& m, V3 v, float out[2]) {
 // kernels/helpers.rs:297-330
 S2 calc_cov2d(V3 scl, Q4 quat, V3 mean_c, const Uni& u) {
     M3 ns = mul_diag(mul_mat3(u.rot, quat_to_mat3(quat)), scl);
-    M23 j = pinhole_jacobian(mean_c, u);
+    M23 j = model_jacobian(mean_c, u);
     M23 v;
     for (int c = 0; c < 3; ++c) m23_mul_vec3(j, col(ns, c), v.c[c]);
     S2 raw;
@@ -462,9 +494,54 @@ int orc_get_threads(void) {
 // camera.rs:49-101,200-254 and render.rs:116-136. glam's Affine3A
 // from_rotation_translation(q, p).inverse(): rotation matrix from the
 // quaternion, general 3x3 inverse via cross products, translation -(M^-1 p).
+// camera.rs:85-198: per-model focal length (f64) and the RT8 clamp-bound undistortion.
+static double o_kb4_d(double theta, const float* p) {
+    double t2 = theta * theta;
+    double t3 = t2 * theta;
+    double t5 = t3 * t2;
+    double t7 = t5 * t2;
+    double t9 = t7 * t2;
+    return theta + (double)p[0] * t3 + (double)p[1] * t5 + (double)p[2] * t7 + (double)p[3] * t9;
+}
+static double o_rt8_radial(double r, const float* p) {
+    double r2 = r * r;
+    double r4 = r2 * r2;
+    double r6 = r4 * r2;
+    double num = 1.0 + (double)p[0] * r2 + (double)p[1] * r4 + (double)p[2] * r6;
+    double den = 1.0 + (double)p[3] * r2 + (double)p[4] * r4 + (double)p[5] * r6;
+    return num / den;
+}
+static double o_rt8_undistort(double r_d, const float* p) {
+    double r = r_d;
+    for (int i = 0; i < 30; ++i) {
+        double factor = o_rt8_radial(r, p);
+        if (std::fabs(factor) < 1e-12) break;
+        double r_new = r_d / factor;
+        if (std::fabs(r_new - r) < 1e-12) {
+            r = r_new;
+            break;
+        }
+        r = r_new;
+    }
+    return r;
+}
+static double o_fov_to_focal(double fov, uint32_t pixels, int model, const float* p) {
+    double half_fov = fov / 2.0;
+    double r_pix = (double)pixels / 2.0;
+    double projected;
+    switch (model) {
+        case 1: case 3: projected = o_kb4_d(half_fov, p); break;
+        case 2: { double r = std::tan(half_fov); projected = r * o_rt8_radial(r, p); break; }
+        default: projected = std::tan(half_fov);
+    }
+    return r_pix / projected;
+}
+
 int orc_make_project_uniforms(const bsx_camera* cam, uint32_t w, uint32_t h, uint32_t sh_degree,
                               uint32_t total, bsx_project_uniforms* out) {
-    if (!cam || !out || cam->camera_model != 0) return 1;
+    if (!cam || !out || cam->camera_model < 0 || cam->camera_model > 3) return 1;
+    const int model = cam->camera_model;
+    const float* mpar = cam->model_params;
     // glam Mat3A::from_quat (quaternion stored x, y, z, w).
     float qx = cam->rotation[0], qy = cam->rotation[1], qz = cam->rotation[2], qw = cam->rotation[3];
     float x2 = qx + qx, y2 = qy + qy, z2 = qz + qz;
@@ -491,8 +568,8 @@ int orc_make_project_uniforms(const bsx_camera* cam, uint32_t w, uint32_t h, uin
     vm[6] = ic2.x; vm[7] = ic2.y; vm[8] = ic2.z;
     vm[9] = tr.x; vm[10] = tr.y; vm[11] = tr.z;
     // fov_to_focal (f64) then cast to f32; centre = uv * size (f32)
-    double fx = ((double)w / 2.0) / std::tan(cam->fov_x / 2.0);
-    double fy = ((double)h / 2.0) / std::tan(cam->fov_y / 2.0);
+    double fx = o_fov_to_focal(cam->fov_x, w, model, mpar);
+    double fy = o_fov_to_focal(cam->fov_y, h, model, mpar);
     out->fx = (float)fx;
     out->fy = (float)fy;
     out->cx = cam->center_uv[0] * (float)w;
@@ -501,10 +578,22 @@ int orc_make_project_uniforms(const bsx_camera* cam, uint32_t w, uint32_t h, uin
     float hyp = std::hypot((float)cam->fov_x, (float)cam->fov_y);
     out->half_max_render_fov = bsx_min(hyp * 1.05f, 2.0f * 3.14159265358979323846f - 1e-6f) * 0.5f;
     float wf = (float)w, hf = (float)h;
-    out->lim_pos_x = (1.15f * wf - out->cx) / out->fx;
-    out->lim_pos_y = (1.15f * hf - out->cy) / out->fy;
-    out->lim_neg_x = (-0.15f * wf - out->cx) / out->fx;
-    out->lim_neg_y = (-0.15f * hf - out->cy) / out->fy;
+    if (model == 0 || model == 2) {
+        out->lim_pos_x = (1.15f * wf - out->cx) / out->fx;
+        out->lim_pos_y = (1.15f * hf - out->cy) / out->fy;
+        out->lim_neg_x = (-0.15f * wf - out->cx) / out->fx;
+        out->lim_neg_y = (-0.15f * hf - out->cy) / out->fy;
+        if (model == 2) {
+            float* lims[4] = {&out->lim_pos_x, &out->lim_pos_y, &out->lim_neg_x, &out->lim_neg_y};
+            for (float* e : lims) {
+                float edge = *e;
+                float sign = std::signbit(edge) ? -1.0f : 1.0f;  // f32::signum
+                *e = (float)o_rt8_undistort((double)std::fabs(edge), mpar) * sign;
+            }
+        }
+    }
+    out->camera_model = model;
+    for (int k = 0; k < 8; ++k) out->model_params[k] = mpar[k];
     out->img_w = w; out->img_h = h;
     out->tile_bw = (w + 15) / 16; out->tile_bh = (h + 15) / 16;
     out->sh_degree = sh_degree;
@@ -543,7 +632,13 @@ void* orc_render(const bsx_project_uniforms* up, const float* transforms, const 
         V3 mean = v3(t[0], t[1], t[2]);
         V3 mean_c = add(mul_vec3(u.rot, mean), u.trans);
         if (!(finite3(mean_c) && mean_c.z <= 1.0e10f)) continue;
-        if (mean_c.z < 0.01f) continue;
+        if (u.model == 0) {
+            if (mean_c.z < 0.01f) continue;
+        } else {  // project_forward.rs:49-64
+            float rr = std::sqrt(mean_c.x * mean_c.x + mean_c.y * mean_c.y);
+            float theta = bsx_atan2f(rr, mean_c.z);
+            if (theta > u.half_max_fov) continue;
+        }
         V3 scl = v3(bsx_expf(t[7]), bsx_expf(t[8]), bsx_expf(t[9]));
         if (!finite3(scl)) continue;
         Q4 qu{t[3], t[4], t[5], t[6]};
@@ -557,9 +652,8 @@ void* orc_render(const bsx_project_uniforms* up, const float* transforms, const 
         S2 cov = compensate_cov2d(raw, mip != 0, &fc);
         float opac = bsx_sigmoid(ro) * fc;
         if (!sym2_finite(cov)) continue;
-        float inv_z = 1.0f / mean_c.z;
-        float m2x = u.fx * mean_c.x * inv_z + u.cx;
-        float m2y = u.fy * mean_c.y * inv_z + u.cy;
+        float m2x, m2y;
+        project_point(mean_c, u, &m2x, &m2y);
         if (!(opac >= 1.0f / 255.0f)) continue;
         float pt = bsx_logf(opac * 255.0f);
         S2 conic = sym2_inverse(cov);
@@ -932,8 +1026,8 @@ void orc_project_bwd(const bsx_project_uniforms* up, const float* transforms, co
         V3 vr0 = row(u.rot, 0), vr1 = row(u.rot, 1), vr2 = row(u.rot, 2);
         V3 sr0 = s3mul(covar, vr0), sr1 = s3mul(covar, vr1), sr2 = s3mul(covar, vr2);
         S3 cov_c{dot(vr0, sr0), dot(vr0, sr1), dot(vr0, sr2), dot(vr1, sr1), dot(vr1, sr2), dot(vr2, sr2)};
-        M23 J = pinhole_jacobian(mean_c, u);
-        // calculate_projection_vjp_pinhole (pinhole.rs:58-123)
+        M23 J = model_jacobian(mean_c, u);
+        // calculate_projection_vjp_pinhole (pinhole.rs:58-123); other models below
         float mx = mean_c.x, my = mean_c.y, mz = mean_c.z;
         float inv_z = 1.0f / mz;
         float mxr = mx * inv_z, myr = my * inv_z;
@@ -965,6 +1059,14 @@ void orc_project_bwd(const bsx_project_uniforms* up, const float* transforms, co
         else v_mz += -u.fy * iz3 * vj21 * tyv;
         v_mz += -u.fx * iz2 * vj00 - u.fy * iz2 * vj11 + 2.0f * u.fx * txv * iz3 * vj20 +
                 2.0f * u.fy * tyv * iz3 * vj21;
+        if (u.model != 0) {  // camera_model/mod.rs:88-136
+            V3 g = u.model == 1 ? cam::kb4_vjp(J, mean_c, cov_c, intr_of(u), vcov, vmx, vmy)
+                 : u.model == 2 ? cam::rt8_vjp(mean_c, cov_c, intr_of(u), vcov, vmx, vmy)
+                                : cam::tpf_vjp(J, mean_c, cov_c, intr_of(u), vcov, vmx, vmy);
+            v_mx = g.x;
+            v_my = g.y;
+            v_mz = g.z;
+        }
         V3 v_mean_c = v3(v_mx, v_my, v_mz + vdep);
         // vcc = J^T v_cov2d J (Mat2x3::transpose_congruence_sym2, lib.rs:358-370)
         float sc[3][2];
@@ -1386,6 +1488,7 @@ void orc_rasterize_rows(const float* rows10, uint32_t count, uint32_t w, uint32_
 // Deterministic float32 exp / ln used on both processors (exposed for tests).
 float orc_expf(float x) { return bsx_expf(x); }
 float orc_logf(float x) { return bsx_logf(x); }
+float orc_atan2f(float y, float x) { return bsx_atan2f(y, x); }
 
 // Number of floats in [-|lo|, 0] (every bit pattern from -0 to lo) where the
 // rasterizers' bsx_expf_neg differs in any bit from bsx_expf.

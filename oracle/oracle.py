@@ -19,7 +19,8 @@ _lib = None
 
 class _Camera(C.Structure):
     _fields_ = [("fov_x", C.c_double), ("fov_y", C.c_double), ("center_uv", C.c_float * 2),
-                ("position", C.c_float * 3), ("rotation", C.c_float * 4), ("camera_model", C.c_int32)]
+                ("position", C.c_float * 3), ("rotation", C.c_float * 4), ("camera_model", C.c_int32),
+                ("model_params", C.c_float * 8)]
 
 
 class Uniforms(C.Structure):
@@ -28,7 +29,8 @@ class Uniforms(C.Structure):
                 ("lim_pos_x", C.c_float), ("lim_pos_y", C.c_float), ("lim_neg_x", C.c_float),
                 ("lim_neg_y", C.c_float), ("img_w", C.c_uint32), ("img_h", C.c_uint32),
                 ("tile_bw", C.c_uint32), ("tile_bh", C.c_uint32), ("sh_degree", C.c_uint32),
-                ("total_splats", C.c_uint32), ("num_visible", C.c_uint32)]
+                ("total_splats", C.c_uint32), ("num_visible", C.c_uint32), ("camera_model", C.c_int32),
+                ("model_params", C.c_float * 8)]
 
 
 class LossCfg(C.Structure):
@@ -102,6 +104,8 @@ def lib() -> C.CDLL:
         _lib.orc_expf.restype = C.c_float
         _lib.orc_expf.argtypes = [C.c_float]
         _lib.orc_logf.restype = C.c_float
+        _lib.orc_atan2f.restype = C.c_float
+        _lib.orc_atan2f.argtypes = [C.c_float, C.c_float]
         _lib.orc_ply_decode.restype = C.c_int
         _lib.orc_ply_decode.argtypes = [C.c_char_p, C.c_size_t, C.c_uint32, C.POINTER(C.c_uint32),
                                         C.POINTER(C.c_uint32), C.c_void_p, C.c_void_p, C.c_void_p, C.c_char_p,
@@ -142,6 +146,8 @@ def camera_c(cam) -> _Camera:
     c.position[:] = [float(v) for v in cam.position]
     c.rotation[:] = [float(v) for v in cam.rotation]
     c.camera_model = int(cam.camera_model)
+    mp = list(getattr(cam, "model_params", ())) + [0.0] * 8
+    c.model_params[:] = [float(v) for v in mp[:8]]
     return c
 
 
@@ -318,6 +324,10 @@ def ply_encode_rows(t, sh, op) -> bytes:
     out = np.zeros(size, np.uint8)
     lib().orc_ply_encode_rows(t.ctypes.data, sh.ctypes.data, op.ctypes.data, n, c, out.ctypes.data)
     return out.tobytes()
+
+
+def atan2f(y: float, x: float) -> float:
+    return float(lib().orc_atan2f(float(y), float(x)))
 
 
 def expf_neg_mismatches(lo: float) -> int:

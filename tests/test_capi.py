@@ -30,7 +30,7 @@ def test_library_exports_every_declared_symbol(bsx_lib):
 
 def test_status_strings_and_abi(bsx_lib):
     lib = bsx_lib.lib()
-    assert lib.bsx_abi_version() == 2
+    assert lib.bsx_abi_version() == 3
     assert lib.bsx_status_string(0) == b"ok"
     assert lib.bsx_status_string(4) == b"device wait timed out"
     assert lib.bsx_status_string(8) == b"malformed file"
@@ -46,6 +46,42 @@ def test_uniforms_match_oracle_bit_exact(bsx_lib, orc):
         u = cam.project_uniforms(1297, 840, 3, 12345)
         o = orc.make_uniforms(cam, 1297, 840, 3, 12345)
         assert bytes(u) == bytes(o), k
+
+
+# distortion coefficients of the camera-model tests (camera.rs tests use the same kinds)
+MODEL_PARAMS = {1: (0.05, -0.01, 0.002, -0.0004, 0, 0, 0, 0),
+                2: (-0.12, 0.03, -0.002, 0.01, -0.004, 0.0005, 0.001, -0.0015),
+                3: (0.04, -0.008, 0.001, -0.0002, 0.0008, -0.0006, 0.0009, -0.0007)}
+
+
+def test_camera_model_uniforms_match_oracle(bsx_lib, orc):
+    """Per-model focal length (camera.rs:85-101) and clamp limits (camera.rs:200-254)."""
+    import dataclasses
+
+    from brush_b200.camera import Camera, focal_to_fov, fov_to_focal
+
+    rng = np.random.default_rng(1)
+    for model, kp in MODEL_PARAMS.items():
+        for k in range(6):
+            cam = Camera.look_at(tuple(rng.normal(0, 5, 3)), (0.0, 0.0, 0.0), math.radians(rng.uniform(40, 150)),
+                                 640, 480)
+            cam = dataclasses.replace(cam, camera_model=model, model_params=kp, center_uv=(0.47, 0.53))
+            u = cam.project_uniforms(640, 480, 3, 99)
+            assert bytes(u) == bytes(orc.make_uniforms(cam, 640, 480, 3, 99)), (model, k)
+            assert u.camera_model == model and np.allclose(list(u.model_params), kp)
+            f = fov_to_focal(cam.fov_x, 640, model, kp)
+            assert abs(u.fx - f) <= 1e-6 * f
+            assert abs(focal_to_fov(f, 640, model, kp) - cam.fov_x) < 1e-9
+            if model == 2:
+                # clamp bounds are the undistorted edges, r * radial(r) = distorted edge, where the
+                # fixed-point inverse converges (moderate fields of view)
+                from brush_b200.camera import _rt8_radial
+                edge = (1.15 * 640 - u.cx) / u.fx
+                r = u.lim_pos_x
+                if edge < 1.0:
+                    assert abs(r * _rt8_radial(r, kp) - edge) < 1e-5
+            else:
+                assert u.lim_pos_x == 0.0 and u.lim_neg_y == 0.0
 
 
 def test_invalid_arguments_rejected_without_gpu(bsx_lib):

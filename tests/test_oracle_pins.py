@@ -110,6 +110,22 @@ def test_raster_exp_bit_identical_on_its_domain(orc):
     assert orc.expf_neg_mismatches(-80.0) == 0
 
 
+def test_shared_atan2_accuracy_and_special_values(orc):
+    """bsx_atan2f (the camera models' angle) within 2 ulp of the C library, with its
+    quadrant and signed-zero conventions."""
+    rng = np.random.default_rng(1)
+    pts = np.concatenate([rng.normal(size=(20000, 2)), rng.uniform(-1e-4, 1e-4, (2000, 2)),
+                          rng.uniform(-1e4, 1e4, (2000, 2))]).astype(np.float32)
+    for y, x in pts[::3]:
+        a = np.float32(orc.atan2f(y, x))
+        ref = np.float32(math.atan2(float(y), float(x)))
+        assert abs(np.int64(a.view(np.int32)) - np.int64(ref.view(np.int32))) <= 2, (y, x)
+    inf = float("inf")
+    for y, x in [(0.0, 1.0), (0.0, -1.0), (-0.0, -1.0), (1.0, 0.0), (-1.0, -0.0), (0.0, -0.0), (inf, 1.0),
+                 (1.0, -inf), (-inf, -inf), (inf, inf)]:
+        assert np.float32(orc.atan2f(y, x)) == np.float32(math.atan2(y, x)), (y, x)
+
+
 def test_gauss_taps_normalised(orc):
     w = orc.gauss_taps()
     assert abs(float(w.sum()) - 1.0) < 1e-6 and np.allclose(w, w[::-1])
