@@ -296,6 +296,7 @@ SIGNATURES = {
     "bsx_trainer_stats_buffers": (
         C.c_int, [C.c_void_p, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), C.POINTER(C.c_void_p)]
     ),
+    "bsx_trainer_keep_gradients": (C.c_int, [C.c_void_p, C.c_int32]),
     "bsx_trainer_grad_buffers": (
         C.c_int,
         [C.c_void_p, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), C.POINTER(C.c_void_p)],

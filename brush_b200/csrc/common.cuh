@@ -68,6 +68,32 @@ __device__ __forceinline__ void st_relaxed_u32(uint32_t* p, uint32_t v) {
     asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// AdamScaled applied inside the projection backward (single-GPU trainer): the
+// moments, rates and per-column scales of the three parameter groups, with
+// the same arithmetic as bsx_adam_step (adam.cu).
+struct FusedAdam {
+    float* m_t;   // [N,10]
+    float* m_sh;  // [N,3C]
+    float* m_o;   // [N]
+    float* v_t;   // [N,10]
+    float* v_sh;  // [N] (second moment per row)
+    float* v_o;   // [N]
+    float lr_t, lr_sh, lr_op;
+    int has_t_scale, has_sh_scale;
+    float t_scale[10];
+    float sh_scale[80];
+    float b1, b2, eps, inv_bc1, inv_bc2, gscale;
+    int first;
+    int keep_grads;  // also write the dense gradients
+};
+
+// 1 / (1 - beta^step) in float, by repeated multiplication (adam.cu fill_cfg).
+inline float adam_inv_bias_correction(float beta, uint32_t step) {
+    float r = 1.0f;
+    for (uint32_t i = 0; i < step; ++i) r *= beta;
+    return 1.0f / (1.0f - r);
+}
+
 // Grow-only device buffer owned by a context.
 struct DevBuf {
     void* p = nullptr;

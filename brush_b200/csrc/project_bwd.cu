@@ -20,6 +20,7 @@ namespace bsx {
 namespace {
 
 struct PbArgs {
+    FusedAdam adam;
     const float* transforms;
     const float* sh;
     const float* raw_opac;
@@ -108,13 +109,80 @@ struct PbShape {
 
 // PINHOLE: the launch's camera is a pinhole, fixed at compile time so the
 // fisheye models' code stays out of the common kernel.
-template <int DEG, bool PINHOLE>
+// AdamScaled element update, the expressions of adam.cu's adam_tile.
+__device__ __forceinline__ void adam_elem(const FusedAdam& A, float p, float g, float m_old, float v_old,
+                                          bool reduce, float v_row, float sc, float* po, float* mo, float* vo) {
+    const float one_m_b1 = 1.0f - A.b1, one_m_b2 = 1.0f - A.b2;
+    const float mm = A.first ? g * one_m_b1 : m_old * A.b1 + g * one_m_b1;
+    const float vv = reduce ? v_row : (A.first ? (g * g) * one_m_b2 : v_old * A.b2 + (g * g) * one_m_b2);
+    const float u = __fdividef(mm * A.inv_bc1, sqrtf(vv * A.inv_bc2) + A.eps);
+    *po = p - u * sc;
+    *mo = mm;
+    *vo = vv;
+}
+
+// Adam over the block's rows [g0, g0 + rows) of one group: flat and coalesced
+// over parameters and moments; 16-byte words (two per thread in flight) when
+// every stream of the range is 16-byte aligned (arrays of any row count and
+// views at any offset are accepted, so this is checked), else single floats;
+// gradients from the staged rows (stride gs).
+__device__ __forceinline__ void adam_rows(const FusedAdam& A, float* __restrict__ param, float* __restrict__ m,
+                                          float* __restrict__ v, const float* sg, uint32_t gs, uint32_t g0,
+                                          uint32_t rows, uint32_t cols, float lr, const float* scale,
+                                          bool reduce, const float* s_vrow) {
+    const float inv = 1.0f / (float)cols;
+    const size_t base = (size_t)g0 * cols;
+    const bool aligned = ((reinterpret_cast<uintptr_t>(param + base) | reinterpret_cast<uintptr_t>(m + base) |
+                           (reduce ? 0u : reinterpret_cast<uintptr_t>(v + base))) & 15u) == 0;
+    const uint32_t n = rows * cols, n4 = aligned ? n / 4 : 0;
+    float4* p4 = reinterpret_cast<float4*>(param + base);
+    float4* m4 = reinterpret_cast<float4*>(m + base);
+    float4* v4 = reinterpret_cast<float4*>(v + base);
+    const float4 zero = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    auto upd4 = [&](uint32_t q, float4 p, float4 mo, float4 vo) {
+        float pe[4] = {p.x, p.y, p.z, p.w}, me[4] = {mo.x, mo.y, mo.z, mo.w}, ve[4] = {vo.x, vo.y, vo.z, vo.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t e = 4 * q + i, r = row_of(e, inv), c = e - r * cols;
+            const float g = sg[r * gs + c] * A.gscale;
+            const float sc = scale ? scale[c] * lr : lr;
+            adam_elem(A, pe[i], g, me[i], ve[i], reduce, reduce ? s_vrow[r] : 0.0f, sc, &pe[i], &me[i], &ve[i]);
+        }
+        p4[q] = make_float4(pe[0], pe[1], pe[2], pe[3]);
+        m4[q] = make_float4(me[0], me[1], me[2], me[3]);
+        if (!reduce) v4[q] = make_float4(ve[0], ve[1], ve[2], ve[3]);
+    };
+    for (uint32_t q0 = threadIdx.x; q0 < n4; q0 += 2 * blockDim.x) {
+        const uint32_t q1 = q0 + blockDim.x;
+        const bool in1 = q1 < n4;
+        const float4 pa = p4[q0], pb = in1 ? p4[q1] : zero;
+        const float4 ma = A.first ? zero : m4[q0], mb = (A.first || !in1) ? zero : m4[q1];
+        const float4 va = (reduce || A.first) ? zero : v4[q0], vb = (reduce || A.first || !in1) ? zero : v4[q1];
+        upd4(q0, pa, ma, va);
+        if (in1) upd4(q1, pb, mb, vb);
+    }
+    for (uint32_t e = 4 * n4 + threadIdx.x; e < n; e += blockDim.x) {
+        const uint32_t r = row_of(e, inv), c = e - r * cols;
+        const float g = sg[r * gs + c] * A.gscale;
+        const float sc = scale ? scale[c] * lr : lr;
+        float po, mo, vo;
+        adam_elem(A, param[base + e], g, A.first ? 0.0f : m[base + e], (reduce || A.first) ? 0.0f : v[base + e],
+                  reduce, reduce ? s_vrow[r] : 0.0f, sc, &po, &mo, &vo);
+        param[base + e] = po;
+        m[base + e] = mo;
+        if (!reduce) v[base + e] = vo;
+    }
+}
+
+template <int DEG, bool PINHOLE, bool FUSE>
 __global__ void __launch_bounds__(PbShape<DEG>::R) project_bwd_kernel(const PbArgs a) {
     using S = PbShape<DEG>;
     constexpr int C3 = S::C3;
     __shared__ float s_t[S::R * S::TS];
     __shared__ float s_sh[S::R * S::SS];
     __shared__ float s_g[S::R * S::GS];
+    __shared__ float s_op[FUSE ? S::R : 1];    // opacity gradients (fused Adam)
+    __shared__ float s_vrow[FUSE ? S::R : 1];  // SH second moment per row (fused Adam)
     const uint32_t g0 = blockIdx.x * S::R;
     const uint32_t rows = min((uint32_t)S::R, a.n - g0);
     stage_in(s_t, a.transforms + (size_t)g0 * 10, rows, 10, S::TS);
@@ -135,7 +203,8 @@ __global__ void __launch_bounds__(PbShape<DEG>::R) project_bwd_kernel(const PbAr
             for (int k = 0; k < 10; ++k) t[k] = 0.0f;
 #pragma unroll
             for (int k = 0; k < C3; ++k) shr[k] = 0.0f;
-            a.v_opac[g] = 0.0f;
+            if (FUSE) s_op[r] = 0.0f;
+            if (!FUSE || a.adam.keep_grads) a.v_opac[g] = 0.0f;
             a.v_refine[g] = 0.0f;
         } else {
             Uni u = a.u;
@@ -164,7 +233,9 @@ __global__ void __launch_bounds__(PbShape<DEG>::R) project_bwd_kernel(const PbAr
             float fc;
             const S2 cov = compensate_cov2d(raw, a.mip != 0, &fc);
             const float os = bsx_sigmoid(__ldg(a.raw_opac + g));
-            a.v_opac[g] = fc * valpha * os * (1.0f - os);
+            const float vop = fc * valpha * os * (1.0f - os);
+            if (FUSE) s_op[r] = vop;
+            if (!FUSE || a.adam.keep_grads) a.v_opac[g] = vop;
             const float rc = bsx_is_finite(vref) ? vref : 0.0f;
             a.v_refine[g] = bsx_clamp(rc, 0.0f, 1.0e32f);
 
@@ -238,24 +309,61 @@ __global__ void __launch_bounds__(PbShape<DEG>::R) project_bwd_kernel(const PbAr
         }
     }
     __syncthreads();
-    stage_out(a.v_transforms + (size_t)g0 * 10, s_t, rows, 10, S::TS);
-    stage_out(a.v_sh + (size_t)g0 * C3, s_sh, rows, C3, S::SS);
+    if (!FUSE || a.adam.keep_grads) {
+        stage_out(a.v_transforms + (size_t)g0 * 10, s_t, rows, 10, S::TS);
+        stage_out(a.v_sh + (size_t)g0 * C3, s_sh, rows, C3, S::SS);
+    }
+    if (FUSE) {
+        const FusedAdam& A = a.adam;
+        // SH rows: second moment from the mean square of the row (reduce_moment_2),
+        // summed in adam.cu's fixed order (quads of the row in column order)
+        if (r < rows) {
+            const float* gr = s_sh + r * S::SS;
+            float s2 = 0.0f;
+            if (C3 % 4 == 0) {
+                for (int i = 0; i < C3 / 4; ++i) {
+                    const float x = gr[4 * i] * A.gscale, y = gr[4 * i + 1] * A.gscale, z = gr[4 * i + 2] * A.gscale,
+                                w = gr[4 * i + 3] * A.gscale;
+                    s2 += x * x + y * y + z * z + w * w;
+                }
+            } else {
+                for (int c = 0; c < C3; ++c) {
+                    const float gg = gr[c] * A.gscale;
+                    s2 += gg * gg;
+                }
+            }
+            const float gsq = s2 * (1.0f / (float)C3);
+            const uint32_t row = g0 + r;
+            const float vr = A.first ? gsq * (1.0f - A.b2) : A.v_sh[row] * A.b2 + gsq * (1.0f - A.b2);
+            A.v_sh[row] = vr;
+            s_vrow[r] = vr;
+        }
+        __syncthreads();
+        adam_rows(A, const_cast<float*>(a.transforms), A.m_t, A.v_t, s_t, S::TS, g0, rows, 10, A.lr_t,
+                  A.has_t_scale ? A.t_scale : nullptr, false, nullptr);
+        adam_rows(A, const_cast<float*>(a.sh), A.m_sh, A.v_sh, s_sh, S::SS, g0, rows, C3, A.lr_sh,
+                  A.has_sh_scale ? A.sh_scale : nullptr, true, s_vrow);
+        adam_rows(A, const_cast<float*>(a.raw_opac), A.m_o, A.v_o, s_op, 1, g0, rows, 1, A.lr_op, nullptr, false,
+                  nullptr);
+    }
 }
 
-template <int DEG>
+template <int DEG, bool FUSE>
 void launch_deg(const PbArgs& a, cudaStream_t st) {
     constexpr int R = PbShape<DEG>::R;
-    if (a.u.model == BSX_CAMERA_PINHOLE) project_bwd_kernel<DEG, true><<<(a.n + R - 1) / R, R, 0, st>>>(a);
-    else project_bwd_kernel<DEG, false><<<(a.n + R - 1) / R, R, 0, st>>>(a);
+    if (a.u.model == BSX_CAMERA_PINHOLE) project_bwd_kernel<DEG, true, FUSE><<<(a.n + R - 1) / R, R, 0, st>>>(a);
+    else project_bwd_kernel<DEG, false, FUSE><<<(a.n + R - 1) / R, R, 0, st>>>(a);
 }
 
 }  // namespace
 
 bsx_status launch_project_bwd(bsx_ctx* ctx, const bsx_project_uniforms& uni, const float* transforms, const float* sh,
                               const float* raw_opac, uint32_t n, uint32_t coeffs, int degree, int mip,
-                              const float* v_grad, float* v_transforms, float* v_sh, float* v_opac, float* v_refine) {
+                              const float* v_grad, float* v_transforms, float* v_sh, float* v_opac, float* v_refine,
+                              const FusedAdam* adam) {
     if (n == 0) return BSX_OK;
     PbArgs a;
+    if (adam) a.adam = *adam;
     a.transforms = transforms;
     a.sh = sh;
     a.raw_opac = raw_opac;
@@ -270,12 +378,22 @@ bsx_status launch_project_bwd(bsx_ctx* ctx, const bsx_project_uniforms& uni, con
     a.v_refine = v_refine;
     if (degree < 0 || degree > 4) return fail(ctx, BSX_ERR_SHAPE, "unsupported SH degree");
     prof_begin(ctx);
-    switch (degree) {
-        case 0: launch_deg<0>(a, ctx->stream); break;
-        case 1: launch_deg<1>(a, ctx->stream); break;
-        case 2: launch_deg<2>(a, ctx->stream); break;
-        case 3: launch_deg<3>(a, ctx->stream); break;
-        default: launch_deg<4>(a, ctx->stream); break;
+    if (adam) {
+        switch (degree) {
+            case 0: launch_deg<0, true>(a, ctx->stream); break;
+            case 1: launch_deg<1, true>(a, ctx->stream); break;
+            case 2: launch_deg<2, true>(a, ctx->stream); break;
+            case 3: launch_deg<3, true>(a, ctx->stream); break;
+            default: launch_deg<4, true>(a, ctx->stream); break;
+        }
+    } else {
+        switch (degree) {
+            case 0: launch_deg<0, false>(a, ctx->stream); break;
+            case 1: launch_deg<1, false>(a, ctx->stream); break;
+            case 2: launch_deg<2, false>(a, ctx->stream); break;
+            case 3: launch_deg<3, false>(a, ctx->stream); break;
+            default: launch_deg<4, false>(a, ctx->stream); break;
+        }
     }
     return post_launch(ctx, "project_bwd_kernel");
 }

@@ -29,7 +29,19 @@ bsx_status launch_raster_bwd(bsx_ctx* ctx, const uint32_t* isect_gid, const uint
                              const bsx_project_uniforms& u, const float bg[3], int smooth, int refine);
 bsx_status launch_project_bwd(bsx_ctx* ctx, const bsx_project_uniforms& uni, const float* transforms, const float* sh,
                               const float* raw_opac, uint32_t n, uint32_t coeffs, int degree, int mip,
-                              const float* v_grad, float* v_transforms, float* v_sh, float* v_opac, float* v_refine);
+                              const float* v_grad, float* v_transforms, float* v_sh, float* v_opac, float* v_refine,
+                              const FusedAdam* adam);
+
+// Projection backward of the last forward render with AdamScaled applied to
+// the splats in the same kernel (single-GPU trainer step).
+bsx_status project_bwd_fused(bsx_ctx* ctx, const float* d_v_combined, float* d_v_transforms, float* d_v_sh,
+                             float* d_v_raw_opac, float* d_v_refine, const FusedAdam& adam) {
+    const bsx_fwd_state& f = ctx->fwd;
+    if (!f.valid) return fail(ctx, BSX_ERR_STATE, "project_bwd needs a preceding render");
+    if (3 * f.coeffs > 80) return fail(ctx, BSX_ERR_SHAPE, "fused Adam supports at most 80 SH columns");
+    return launch_project_bwd(ctx, f.uni, f.transforms, f.sh, f.raw_opac, f.n, f.coeffs, (int)f.degree, f.mip,
+                              d_v_combined, d_v_transforms, d_v_sh, d_v_raw_opac, d_v_refine, &adam);
+}
 
 namespace {
 int degree_from_coeffs(uint32_t c) {
@@ -197,7 +209,7 @@ bsx_status bsx_project_bwd(bsx_ctx* ctx, const float* d_v_combined, float* d_v_t
     if ((uintptr_t)d_v_combined % 16) return fail(ctx, BSX_ERR_INVALID_ARG, "v_combined must be 16-byte aligned");
     cudaSetDevice(ctx->device);
     return launch_project_bwd(ctx, f.uni, f.transforms, f.sh, f.raw_opac, f.n, f.coeffs, (int)f.degree, f.mip,
-                              d_v_combined, d_v_transforms, d_v_sh, d_v_raw_opac, d_v_refine);
+                              d_v_combined, d_v_transforms, d_v_sh, d_v_raw_opac, d_v_refine, nullptr);
 }
 
 }  // extern "C"

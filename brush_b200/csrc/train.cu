@@ -25,6 +25,9 @@
 
 namespace bsx {
 
+bsx_status project_bwd_fused(bsx_ctx* ctx, const float* d_v_combined, float* d_v_transforms, float* d_v_sh,
+                             float* d_v_raw_opac, float* d_v_refine, const FusedAdam& adam);
+
 namespace {
 
 constexpr int kStatsThreads = 256;
@@ -84,12 +87,11 @@ Rates next_rates(bsx_trainer* tr) {
 
 // Moments for `rows` rows (zeroed when the layout changes).
 bsx_status ensure_moments(bsx_trainer* tr, uint32_t rows, int world, int rank, float** m, float** v) {
-    const size_t c3 = 3 * (size_t)tr->coeffs;
-    const size_t mf = (size_t)rows * (10 + c3 + 1), vf = (size_t)rows * (10 + 1 + 1);
+    const size_t mv = moment_floats(rows, tr->coeffs);
     if (tr->moment_rows != rows || tr->moment_world != world || tr->moment_rank != rank) {
-        bsx_status s = ensure(tr->ctx, tr->moments, (mf + vf) * 4 + 64);
+        bsx_status s = ensure(tr->ctx, tr->moments, mv * 4 + 64);
         if (s != BSX_OK) return s;
-        s = check_cuda(tr->ctx, cudaMemsetAsync(tr->moments.p, 0, (mf + vf) * 4, tr->ctx->stream), "memset moments");
+        s = check_cuda(tr->ctx, cudaMemsetAsync(tr->moments.p, 0, mv * 4, tr->ctx->stream), "memset moments");
         if (s != BSX_OK) return s;
         tr->moment_rows = rows;
         tr->moment_world = world;
@@ -117,7 +119,8 @@ bsx_loss_cfg loss_cfg_of(const bsx_train_config& c) {
 // Render -> loss -> raster backward -> projection backward, into the given gradient buffers.
 bsx_status forward_backward(bsx_trainer* tr, const bsx_camera* cam, uint32_t w, uint32_t h, const uint32_t* gt,
                             const float* transforms, const float* sh, const float* opac, float* vt, float* vs,
-                            float* vo, float* vr, int refine, float* d_loss, bsx_render_out* out) {
+                            float* vo, float* vr, int refine, float* d_loss, bsx_render_out* out,
+                            const FusedAdam* adam = nullptr) {
     bsx_ctx* ctx = tr->ctx;
     bsx_status s = bsx_render_fwd(ctx, cam, w, h, transforms, sh, opac, tr->n, tr->coeffs, tr->cfg.render_mode,
                                   BSX_PASS_BACKWARD, tr->cfg.background, out);
@@ -129,6 +132,7 @@ bsx_status forward_backward(bsx_trainer* tr, const bsx_camera* cam, uint32_t w, 
     if (s != BSX_OK) return s;
     s = bsx_rasterize_bwd(ctx, tr->v_output.as<float>(), refine, tr->v_combined.as<float>());
     if (s != BSX_OK) return s;
+    if (adam) return project_bwd_fused(ctx, tr->v_combined.as<float>(), vt, vs, vo, vr, *adam);
     return bsx_project_bwd(ctx, tr->v_combined.as<float>(), vt, vs, vo, vr);
 }
 
@@ -322,6 +326,12 @@ bsx_status bsx_trainer_grad_buffers(bsx_trainer* tr, float** vt, float** vs, flo
     return BSX_OK;
 }
 
+bsx_status bsx_trainer_keep_gradients(bsx_trainer* tr, int32_t on) {
+    if (!tr) return BSX_ERR_INVALID_ARG;
+    tr->keep_grads = on ? 1 : 0;
+    return BSX_OK;
+}
+
 bsx_status bsx_train_step(bsx_trainer* tr, const bsx_camera* cam, uint32_t w, uint32_t h, const uint32_t* gt,
                           float* transforms, float* sh, float* opac, int32_t refine, float* d_loss,
                           bsx_train_stats* stats) {
@@ -332,25 +342,40 @@ bsx_status bsx_train_step(bsx_trainer* tr, const bsx_camera* cam, uint32_t w, ui
     float *vt, *vs, *vo, *vr;
     bsx_status s0 = bsx_trainer_grad_buffers(tr, &vt, &vs, &vo, &vr);
     if (s0 != BSX_OK) return s0;
-    bsx_render_out out{};
-    bsx_status s = forward_backward(tr, cam, w, h, gt, transforms, sh, opac, vt, vs, vo, vr, refine, d_loss, &out);
-    if (s != BSX_OK) return s;
+    // The moments and this step's rates are settled before the backward, which
+    // applies AdamScaled to every splat row as soon as its gradient exists
+    // (no dense gradient round trip through memory; bsx_adam_step arithmetic).
     float* m[3];
     float* v[3];
-    s = ensure_moments(tr, tr->n, 1, 0, m, v);
+    bsx_status s = ensure_moments(tr, tr->n, 1, 0, m, v);
     if (s != BSX_OK) return s;
     const Rates r = next_rates(tr);
     tr->step++;
-    const uint32_t c3 = 3 * tr->coeffs;
-    bsx_adam_group g[3];
-    g[0] = {transforms, vt, m[0], v[0], tr->n, 10, r.lr_t, r.scaled ? r.t_scale : nullptr, 0};
-    g[1] = {sh, vs, m[1], v[1], tr->n, c3, r.lr_sh, r.scaled ? r.sh_scale.data() : nullptr, 1};
-    g[2] = {opac, vo, m[2], v[2], tr->n, 1, r.lr_op, nullptr, 0};
-    const bsx_adam_cfg ac{0.9f, 0.999f, 1e-15f, tr->step, 1.0f};
-    if (tr->n) {
-        s = bsx_adam_step(ctx, g, 3, &ac);
-        if (s != BSX_OK) return s;
-    }
+    FusedAdam fa;
+    fa.m_t = m[0];
+    fa.m_sh = m[1];
+    fa.m_o = m[2];
+    fa.v_t = v[0];
+    fa.v_sh = v[1];
+    fa.v_o = v[2];
+    fa.lr_t = r.lr_t;
+    fa.lr_sh = r.lr_sh;
+    fa.lr_op = r.lr_op;
+    fa.has_t_scale = r.scaled;
+    fa.has_sh_scale = r.scaled;
+    for (int k = 0; k < 10; ++k) fa.t_scale[k] = r.scaled ? r.t_scale[k] : 1.0f;
+    for (int k = 0; k < 80; ++k) fa.sh_scale[k] = (r.scaled && k < (int)r.sh_scale.size()) ? r.sh_scale[k] : 1.0f;
+    fa.b1 = 0.9f;
+    fa.b2 = 0.999f;
+    fa.eps = 1e-15f;
+    fa.inv_bc1 = adam_inv_bias_correction(0.9f, tr->step);
+    fa.inv_bc2 = adam_inv_bias_correction(0.999f, tr->step);
+    fa.gscale = 1.0f;
+    fa.first = tr->step == 1;
+    fa.keep_grads = tr->keep_grads;
+    bsx_render_out out{};
+    s = forward_backward(tr, cam, w, h, gt, transforms, sh, opac, vt, vs, vo, vr, refine, d_loss, &out, &fa);
+    if (s != BSX_OK) return s;
     s = gather_stats(tr, refine ? vr : nullptr, out);
     if (s != BSX_OK) return s;
     if (stats) {

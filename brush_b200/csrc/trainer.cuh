@@ -12,6 +12,7 @@ struct bsx_trainer {
     uint32_t step = 0;
     double mean_prev = 0.0, mean_gamma = 1.0, scale_prev = 0.0, scale_gamma = 1.0;
     uint32_t dp_epoch = 0;
+    int keep_grads = 0;  // bsx_train_step also writes the dense gradients
     // densification: the plan of the last bsx_trainer_refine_plan
     bool planned = false;
     uint32_t plan_n = 0, plan_kept = 0, plan_split_count = 0, refines = 0;
@@ -22,19 +23,23 @@ struct bsx_trainer {
 namespace bsx {
 
 // Moment views over one buffer of `rows` rows:
-// m: [rows,10] | [rows,3C] | [rows,1]; v: [rows,10] | [rows] | [rows,1].
+// m: [rows,10] | [rows,3C] | [rows,1]; v: [rows,10] | [rows] | [rows,1],
+// each array starting on a 16-byte boundary (vector loads in the updates).
+inline size_t round4(size_t x) { return (x + 3) / 4 * 4; }
 inline void moment_views(float* base, uint32_t rows, uint32_t coeffs, float** m, float** v) {
     const size_t c3 = 3 * (size_t)coeffs;
     m[0] = base;
-    m[1] = m[0] + (size_t)rows * 10;
-    m[2] = m[1] + (size_t)rows * c3;
-    v[0] = m[2] + rows;
-    v[1] = v[0] + (size_t)rows * 10;
-    v[2] = v[1] + rows;
+    m[1] = m[0] + round4((size_t)rows * 10);
+    m[2] = m[1] + round4((size_t)rows * c3);
+    v[0] = m[2] + round4(rows);
+    v[1] = v[0] + round4((size_t)rows * 10);
+    v[2] = v[1] + round4(rows);
 }
 
 inline size_t moment_floats(uint32_t rows, uint32_t coeffs) {
-    return (size_t)rows * (10 + 3 * (size_t)coeffs + 1) + (size_t)rows * (10 + 1 + 1);
+    const size_t c3 = 3 * (size_t)coeffs;
+    return round4((size_t)rows * 10) + round4((size_t)rows * c3) + round4(rows) + round4((size_t)rows * 10) +
+           round4(rows) + round4(rows);
 }
 
 }  // namespace bsx

@@ -186,8 +186,11 @@ class _NativeTrainer:
 
 class SplatTrainer:
     def __init__(self, config: TrainConfig, splats: Splats, process_group=None, gather_stats: bool = True,
-                 shard_optimizer: bool = True, exchange: str = "peer"):
+                 shard_optimizer: bool = True, exchange: str = "peer", keep_gradients: bool = False):
         self.config = config
+        # The single-GPU step applies AdamScaled inside the projection backward;
+        # keep_gradients also writes the dense gradients to ``grads``.
+        self.keep_gradients = keep_gradients
         # Data-parallel exchange with several ranks:
         #   "peer": one fused kernel over peer memory (brush_b200.peer); the
         #           splat parameters then live in the exchange region and the
@@ -231,6 +234,8 @@ class SplatTrainer:
         if self.world == 1 or self.exchange == "peer":
             self.native = _NativeTrainer(dev.index, n, c, self.config.to_c(self.median_scale, splats.render_mode,
                                                                           self.gather_stats))
+            self.native.ctx.check(_lib.lib().bsx_trainer_keep_gradients(self.native.handle,
+                                                                        int(self.keep_gradients)))
             self.record = self.native.record()
             if self.world > 1:
                 from .peer import PeerExchange

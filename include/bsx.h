@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define BSX_ABI_VERSION 3
+#define BSX_ABI_VERSION 4
 /* Gradient lanes per splat written by the raster backward:
  * xy(2) conic(3) rgb(3) alpha refine depth. Reference:
  * crates/brush-render-bwd/src/kernels/rasterize_backwards.rs:40 */
@@ -338,7 +338,11 @@ BSX_API bsx_status bsx_trainer_destroy(bsx_trainer* tr);
  * zeroed at creation; valid while the trainer lives. */
 BSX_API bsx_status bsx_trainer_stats_buffers(bsx_trainer* tr, float** d_refine_weight_norm, float** d_vis_weight,
                                              float** d_max_screen_size);
-/* Dense gradients of the last step ([N,10], [N,C,3], [N], refine weight [N]). */
+/* Dense gradients of the last step ([N,10], [N,C,3], [N], refine weight [N]).
+ * bsx_train_step applies AdamScaled inside the projection backward, so it
+ * writes the dense gradients only after bsx_trainer_keep_gradients(tr, 1);
+ * the refine weight is always written. */
+BSX_API bsx_status bsx_trainer_keep_gradients(bsx_trainer* tr, int32_t on);
 BSX_API bsx_status bsx_trainer_grad_buffers(bsx_trainer* tr, float** d_v_transforms, float** d_v_sh_coeffs,
                                             float** d_v_raw_opac, float** d_v_refine_weight);
 /* One step in place on the splats. d_loss receives the step's mean loss (one float, device). */
