@@ -117,8 +117,13 @@ class ClockSampler:
 # Algorithmic bytes moved by each kernel per launch (fp32 = 4 B). N splats,
 # V visible, M intersections, Mp intersections surviving the forward early-out,
 # P pixels, T tiles, C SH coefficients per splat.
-def kernel_bytes(name, N, V, M, Mp, P, T, C, W=1):
+def kernel_bytes(name, N, V, M, Mp, P, T, C, W=1, fused_adam=False):
     row = 4 * (11 + 3 * C)  # bytes of one splat's parameters (or gradients)
+    if name == "project_bwd_kernel" and fused_adam:
+        # single-GPU step: projection backward + AdamScaled in one kernel. Per splat:
+        # v_combined 48 + refine 4 + parameters read and written 2 (44 + 12C) +
+        # first moment read and written 2 (44 + 12C) + second moments 2 * 48
+        return (324 + 48 * C) * N
     table = {
         "project_fwd_kernel": 44 * N + 8 * N + N // 8 + V * (12 * C + 48 + 4),
         "compact_visible_kernel": 4 * N + N // 8 + 12 * V,
@@ -381,7 +386,7 @@ def run_ours(args, rank, world, local_rank):
     total_prof = max(sum(v[0] for v in prof.values()), 1e-9)
     for name, (tot, cnt) in prof.items():
         avg_ms = tot / max(cnt, 1)
-        b = kernel_bytes(name, N, V, M, Mp, P, T, C, world)
+        b = kernel_bytes(name, N, V, M, Mp, P, T, C, world, fused_adam=train and world == 1)
         if name in ("sort_pass_kernel", "sort_hist_kernel"):
             # two sorts per step: V depth keys (4 passes) and M tile keys
             per_step = (4 * 16 * V + tile_passes * 16 * M) if name == "sort_pass_kernel" else 4 * V + 4 * M

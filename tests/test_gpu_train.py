@@ -26,14 +26,20 @@ def _burn_rates(cfg, k, median):
     return pm * median, ps
 
 
-def test_native_step_matches_composed_step(cuda):
+@pytest.mark.parametrize("camera_model", [0, 1])
+def test_native_step_matches_composed_step(cuda, camera_model):
+    """camera_model 1: Kannala-Brandt 4, which takes the fused step's non-pinhole kernel."""
+    import dataclasses
+
     import brush_b200 as bsx
     from brush_b200.adam import AdamGroup, AdamScaled
     from brush_b200.splats import clustered_scene, orbit_camera, random_gt
 
     splats = clustered_scene(20000, 3, "cpu", seed=11).to("cuda")
     w, h = 192, 128
-    cams = [orbit_camera(i, 3, 8.0, w, h) for i in range(3)]
+    kp = (0.05, -0.01, 0.002, -0.0004, 0.0, 0.0, 0.0, 0.0)
+    cams = [dataclasses.replace(orbit_camera(i, 3, 8.0, w, h), camera_model=camera_model, model_params=kp)
+            for i in range(3)]
     gts = [random_gt(h, w, 40 + i, "cpu").cuda() for i in range(3)]
     cfg = bsx.TrainConfig()
     comp = splats.clone()
