@@ -61,8 +61,11 @@ struct CompactArgs {
     int* err;
 };
 
+// Register-bounded to four resident blocks per SM: the kernel is latency-bound
+// (long dependent chains of exp / log / sqrt / division per splat), and the
+// extra warps outweigh the few spilled registers of the degree-3 instance.
 template <int DEG>
-__global__ void __launch_bounds__(kProjThreads) project_fwd_kernel(const __grid_constant__ ProjArgs a) {
+__global__ void __launch_bounds__(kProjThreads, 4) project_fwd_kernel(const __grid_constant__ ProjArgs a) {
     const uint32_t g = blockIdx.x * kProjThreads + threadIdx.x;
     const Uni& u = a.u;
 
