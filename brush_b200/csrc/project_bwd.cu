@@ -174,8 +174,9 @@ __device__ __forceinline__ void adam_rows(const FusedAdam& A, float* __restrict_
     }
 }
 
+// Six resident blocks per SM (the shared-memory limit) at 80 registers, no spills.
 template <int DEG, bool PINHOLE, bool FUSE>
-__global__ void __launch_bounds__(PbShape<DEG>::R) project_bwd_kernel(const PbArgs a) {
+__global__ void __launch_bounds__(PbShape<DEG>::R, 6) project_bwd_kernel(const PbArgs a) {
     using S = PbShape<DEG>;
     constexpr int C3 = S::C3;
     __shared__ float s_t[S::R * S::TS];
