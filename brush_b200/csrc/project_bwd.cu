@@ -80,11 +80,38 @@ __device__ __forceinline__ uint32_t row_of(uint32_t i, float inv_cols) {
 }
 
 // Copy `rows` rows of `cols` floats (contiguous in global memory) into shared
-// memory rows of stride `stride`, or back.
+// memory rows of stride `stride`, or back. Loads are 16-byte words, B of them
+// per thread issued before any is stored, when `src` is 16-byte aligned (a
+// block's first row is, for the arrays this kernel is given; views at any
+// offset are accepted, so it is checked), else single floats.
+template <int B>
 __device__ __forceinline__ void stage_in(float* dst, const float* __restrict__ src, uint32_t rows, uint32_t cols,
                                          uint32_t stride) {
     const float inv = 1.0f / (float)cols;
-    for (uint32_t i = threadIdx.x; i < rows * cols; i += blockDim.x) {
+    const uint32_t n = rows * cols;
+    const uint32_t n4 = (reinterpret_cast<uintptr_t>(src) & 15u) == 0 ? n / 4 : 0;
+    const float4* s4 = reinterpret_cast<const float4*>(src);
+    for (uint32_t q0 = threadIdx.x; q0 < n4; q0 += B * blockDim.x) {
+        float4 w[B];
+#pragma unroll
+        for (int k = 0; k < B; ++k) {
+            const uint32_t q = q0 + k * blockDim.x;
+            if (q < n4) w[k] = __ldg(s4 + q);
+        }
+#pragma unroll
+        for (int k = 0; k < B; ++k) {
+            const uint32_t q = q0 + k * blockDim.x;
+            if (q < n4) {
+                const float e[4] = {w[k].x, w[k].y, w[k].z, w[k].w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const uint32_t idx = 4 * q + i, r = row_of(idx, inv);
+                    dst[r * stride + (idx - r * cols)] = e[i];
+                }
+            }
+        }
+    }
+    for (uint32_t i = 4 * n4 + threadIdx.x; i < n; i += blockDim.x) {
         const uint32_t r = row_of(i, inv);
         dst[r * stride + (i - r * cols)] = __ldg(src + i);
     }
@@ -122,10 +149,11 @@ __device__ __forceinline__ void adam_elem(const FusedAdam& A, float p, float g, 
 }
 
 // Adam over the block's rows [g0, g0 + rows) of one group: flat and coalesced
-// over parameters and moments; 16-byte words (two per thread in flight) when
-// every stream of the range is 16-byte aligned (arrays of any row count and
-// views at any offset are accepted, so this is checked), else single floats;
-// gradients from the staged rows (stride gs).
+// over parameters and moments; 16-byte words (B per stream and thread in
+// flight) when every stream of the range is 16-byte aligned (arrays of any row
+// count and views at any offset are accepted, so this is checked), else single
+// floats; gradients from the staged rows (stride gs).
+template <int B>
 __device__ __forceinline__ void adam_rows(const FusedAdam& A, float* __restrict__ param, float* __restrict__ m,
                                           float* __restrict__ v, const float* sg, uint32_t gs, uint32_t g0,
                                           uint32_t rows, uint32_t cols, float lr, const float* scale,
@@ -152,14 +180,21 @@ __device__ __forceinline__ void adam_rows(const FusedAdam& A, float* __restrict_
         m4[q] = make_float4(me[0], me[1], me[2], me[3]);
         if (!reduce) v4[q] = make_float4(ve[0], ve[1], ve[2], ve[3]);
     };
-    for (uint32_t q0 = threadIdx.x; q0 < n4; q0 += 2 * blockDim.x) {
-        const uint32_t q1 = q0 + blockDim.x;
-        const bool in1 = q1 < n4;
-        const float4 pa = p4[q0], pb = in1 ? p4[q1] : zero;
-        const float4 ma = A.first ? zero : m4[q0], mb = (A.first || !in1) ? zero : m4[q1];
-        const float4 va = (reduce || A.first) ? zero : v4[q0], vb = (reduce || A.first || !in1) ? zero : v4[q1];
-        upd4(q0, pa, ma, va);
-        if (in1) upd4(q1, pb, mb, vb);
+    for (uint32_t q0 = threadIdx.x; q0 < n4; q0 += B * blockDim.x) {
+        float4 pw[B], mw[B], vw[B];
+#pragma unroll
+        for (int k = 0; k < B; ++k) {
+            const uint32_t q = q0 + k * blockDim.x;
+            const bool in = q < n4;
+            pw[k] = in ? p4[q] : zero;
+            mw[k] = (A.first || !in) ? zero : m4[q];
+            vw[k] = (reduce || A.first || !in) ? zero : v4[q];
+        }
+#pragma unroll
+        for (int k = 0; k < B; ++k) {
+            const uint32_t q = q0 + k * blockDim.x;
+            if (q < n4) upd4(q, pw[k], mw[k], vw[k]);
+        }
     }
     for (uint32_t e = 4 * n4 + threadIdx.x; e < n; e += blockDim.x) {
         const uint32_t r = row_of(e, inv), c = e - r * cols;
@@ -186,11 +221,14 @@ __global__ void __launch_bounds__(PbShape<DEG>::R, 6) project_bwd_kernel(const P
     __shared__ float s_vrow[FUSE ? S::R : 1];  // SH second moment per row (fused Adam)
     const uint32_t g0 = blockIdx.x * S::R;
     const uint32_t rows = min((uint32_t)S::R, a.n - g0);
-    stage_in(s_t, a.transforms + (size_t)g0 * 10, rows, 10, S::TS);
-    stage_in(s_sh, a.sh + (size_t)g0 * C3, rows, C3, S::SS);
-    stage_in(s_g, a.v_grad + (size_t)g0 * kGradStride, rows, kGradStride, S::GS);
-    __syncthreads();
     const uint32_t r = threadIdx.x;
+    // the row's scalar inputs, issued with the staged rows rather than after them
+    const float raw_op = r < rows ? __ldg(a.raw_opac + g0 + r) : 0.0f;
+    const float v_sh_old = (FUSE && r < rows && !a.adam.first) ? a.adam.v_sh[g0 + r] : 0.0f;
+    stage_in<2>(s_t, a.transforms + (size_t)g0 * 10, rows, 10, S::TS);
+    stage_in<2>(s_g, a.v_grad + (size_t)g0 * kGradStride, rows, kGradStride, S::GS);
+    stage_in<(S::C3 >= 48 ? 6 : 2)>(s_sh, a.sh + (size_t)g0 * C3, rows, C3, S::SS);
+    __syncthreads();
     if (r < rows) {
         const uint32_t g = g0 + r;
         float* t = s_t + r * S::TS;   // transform in, transform gradient out
@@ -233,7 +271,7 @@ __global__ void __launch_bounds__(PbShape<DEG>::R, 6) project_bwd_kernel(const P
             const S2 raw = calc_cov2d(scl, q, mean_c, u);
             float fc;
             const S2 cov = compensate_cov2d(raw, a.mip != 0, &fc);
-            const float os = bsx_sigmoid(__ldg(a.raw_opac + g));
+            const float os = bsx_sigmoid(raw_op);
             const float vop = fc * valpha * os * (1.0f - os);
             if (FUSE) s_op[r] = vop;
             if (!FUSE || a.adam.keep_grads) a.v_opac[g] = vop;
@@ -335,17 +373,17 @@ __global__ void __launch_bounds__(PbShape<DEG>::R, 6) project_bwd_kernel(const P
             }
             const float gsq = s2 * (1.0f / (float)C3);
             const uint32_t row = g0 + r;
-            const float vr = A.first ? gsq * (1.0f - A.b2) : A.v_sh[row] * A.b2 + gsq * (1.0f - A.b2);
+            const float vr = A.first ? gsq * (1.0f - A.b2) : v_sh_old * A.b2 + gsq * (1.0f - A.b2);
             A.v_sh[row] = vr;
             s_vrow[r] = vr;
         }
         __syncthreads();
-        adam_rows(A, const_cast<float*>(a.transforms), A.m_t, A.v_t, s_t, S::TS, g0, rows, 10, A.lr_t,
-                  A.has_t_scale ? A.t_scale : nullptr, false, nullptr);
-        adam_rows(A, const_cast<float*>(a.sh), A.m_sh, A.v_sh, s_sh, S::SS, g0, rows, C3, A.lr_sh,
-                  A.has_sh_scale ? A.sh_scale : nullptr, true, s_vrow);
-        adam_rows(A, const_cast<float*>(a.raw_opac), A.m_o, A.v_o, s_op, 1, g0, rows, 1, A.lr_op, nullptr, false,
-                  nullptr);
+        adam_rows<3>(A, const_cast<float*>(a.transforms), A.m_t, A.v_t, s_t, S::TS, g0, rows, 10, A.lr_t,
+                     A.has_t_scale ? A.t_scale : nullptr, false, nullptr);
+        adam_rows<4>(A, const_cast<float*>(a.sh), A.m_sh, A.v_sh, s_sh, S::SS, g0, rows, C3, A.lr_sh,
+                     A.has_sh_scale ? A.sh_scale : nullptr, true, s_vrow);
+        adam_rows<1>(A, const_cast<float*>(a.raw_opac), A.m_o, A.v_o, s_op, 1, g0, rows, 1, A.lr_op, nullptr, false,
+                     nullptr);
     }
 }
 
