@@ -103,10 +103,14 @@ __device__ __forceinline__ void stage_in(float* dst, const float* __restrict__ s
             const uint32_t q = q0 + k * blockDim.x;
             if (q < n4) {
                 const float e[4] = {w[k].x, w[k].y, w[k].z, w[k].w};
+                uint32_t r = row_of(4 * q, inv), c = 4 * q - r * cols;
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
-                    const uint32_t idx = 4 * q + i, r = row_of(idx, inv);
-                    dst[r * stride + (idx - r * cols)] = e[i];
+                    dst[r * stride + c] = e[i];
+                    if (++c == cols) {
+                        c = 0;
+                        ++r;
+                    }
                 }
             }
         }
@@ -134,30 +138,34 @@ struct PbShape {
     static constexpr int GS = 13;                  // gradient row stride (odd)
 };
 
-// PINHOLE: the launch's camera is a pinhole, fixed at compile time so the
-// fisheye models' code stays out of the common kernel.
-// AdamScaled element update, the expressions of adam.cu's adam_tile.
-__device__ __forceinline__ void adam_elem(const FusedAdam& A, float p, float g, float m_old, float v_old,
-                                          bool reduce, float v_row, float sc, float* po, float* mo, float* vo) {
-    const float one_m_b1 = 1.0f - A.b1, one_m_b2 = 1.0f - A.b2;
+// AdamScaled element update, the expressions of adam.cu's adam_tile, in three
+// parts: the second moment, its denominator sqrt(v * inv_bc2) + eps (computed
+// once per row where the moment is per row) and the first-moment step.
+__device__ __forceinline__ float adam_v(const FusedAdam& A, float g, float v_old) {
+    const float one_m_b2 = 1.0f - A.b2;
+    return A.first ? (g * g) * one_m_b2 : v_old * A.b2 + (g * g) * one_m_b2;
+}
+__device__ __forceinline__ float adam_den(const FusedAdam& A, float vv) { return sqrtf(vv * A.inv_bc2) + A.eps; }
+__device__ __forceinline__ void adam_step(const FusedAdam& A, float p, float g, float m_old, float den, float sc,
+                                          float* po, float* mo) {
+    const float one_m_b1 = 1.0f - A.b1;
     const float mm = A.first ? g * one_m_b1 : m_old * A.b1 + g * one_m_b1;
-    const float vv = reduce ? v_row : (A.first ? (g * g) * one_m_b2 : v_old * A.b2 + (g * g) * one_m_b2);
-    const float u = __fdividef(mm * A.inv_bc1, sqrtf(vv * A.inv_bc2) + A.eps);
+    const float u = __fdividef(mm * A.inv_bc1, den);
     *po = p - u * sc;
     *mo = mm;
-    *vo = vv;
 }
 
 // Adam over the block's rows [g0, g0 + rows) of one group: flat and coalesced
 // over parameters and moments; 16-byte words (B per stream and thread in
 // flight) when every stream of the range is 16-byte aligned (arrays of any row
 // count and views at any offset are accepted, so this is checked), else single
-// floats; gradients from the staged rows (stride gs).
+// floats; gradients from the staged rows (stride gs). With `reduce` the second
+// moment is per row (already updated) and `s_den` holds its denominators.
 template <int B>
 __device__ __forceinline__ void adam_rows(const FusedAdam& A, float* __restrict__ param, float* __restrict__ m,
                                           float* __restrict__ v, const float* sg, uint32_t gs, uint32_t g0,
                                           uint32_t rows, uint32_t cols, float lr, const float* scale,
-                                          bool reduce, const float* s_vrow) {
+                                          bool reduce, const float* s_den) {
     const float inv = 1.0f / (float)cols;
     const size_t base = (size_t)g0 * cols;
     const bool aligned = ((reinterpret_cast<uintptr_t>(param + base) | reinterpret_cast<uintptr_t>(m + base) |
@@ -167,14 +175,28 @@ __device__ __forceinline__ void adam_rows(const FusedAdam& A, float* __restrict_
     float4* m4 = reinterpret_cast<float4*>(m + base);
     float4* v4 = reinterpret_cast<float4*>(v + base);
     const float4 zero = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    auto elem = [&](uint32_t r, uint32_t c, float& p, float& mo, float& vo) {
+        const float g = sg[r * gs + c] * A.gscale;
+        const float sc = scale ? scale[c] * lr : lr;
+        float den;
+        if (reduce) {
+            den = s_den[r];
+        } else {
+            vo = adam_v(A, g, vo);
+            den = adam_den(A, vo);
+        }
+        adam_step(A, p, g, mo, den, sc, &p, &mo);
+    };
     auto upd4 = [&](uint32_t q, float4 p, float4 mo, float4 vo) {
         float pe[4] = {p.x, p.y, p.z, p.w}, me[4] = {mo.x, mo.y, mo.z, mo.w}, ve[4] = {vo.x, vo.y, vo.z, vo.w};
+        uint32_t r = row_of(4 * q, inv), c = 4 * q - r * cols;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            const uint32_t e = 4 * q + i, r = row_of(e, inv), c = e - r * cols;
-            const float g = sg[r * gs + c] * A.gscale;
-            const float sc = scale ? scale[c] * lr : lr;
-            adam_elem(A, pe[i], g, me[i], ve[i], reduce, reduce ? s_vrow[r] : 0.0f, sc, &pe[i], &me[i], &ve[i]);
+            elem(r, c, pe[i], me[i], ve[i]);
+            if (++c == cols) {
+                c = 0;
+                ++r;
+            }
         }
         p4[q] = make_float4(pe[0], pe[1], pe[2], pe[3]);
         m4[q] = make_float4(me[0], me[1], me[2], me[3]);
@@ -198,17 +220,16 @@ __device__ __forceinline__ void adam_rows(const FusedAdam& A, float* __restrict_
     }
     for (uint32_t e = 4 * n4 + threadIdx.x; e < n; e += blockDim.x) {
         const uint32_t r = row_of(e, inv), c = e - r * cols;
-        const float g = sg[r * gs + c] * A.gscale;
-        const float sc = scale ? scale[c] * lr : lr;
-        float po, mo, vo;
-        adam_elem(A, param[base + e], g, A.first ? 0.0f : m[base + e], (reduce || A.first) ? 0.0f : v[base + e],
-                  reduce, reduce ? s_vrow[r] : 0.0f, sc, &po, &mo, &vo);
+        float po = param[base + e], mo = A.first ? 0.0f : m[base + e], vo = (reduce || A.first) ? 0.0f : v[base + e];
+        elem(r, c, po, mo, vo);
         param[base + e] = po;
         m[base + e] = mo;
         if (!reduce) v[base + e] = vo;
     }
 }
 
+// PINHOLE: the launch's camera is a pinhole, fixed at compile time so the
+// fisheye models' code stays out of the common kernel.
 // Six resident blocks per SM (the shared-memory limit) at 80 registers, no spills.
 template <int DEG, bool PINHOLE, bool FUSE>
 __global__ void __launch_bounds__(PbShape<DEG>::R, 6) project_bwd_kernel(const PbArgs a) {
@@ -218,7 +239,7 @@ __global__ void __launch_bounds__(PbShape<DEG>::R, 6) project_bwd_kernel(const P
     __shared__ float s_sh[S::R * S::SS];
     __shared__ float s_g[S::R * S::GS];
     __shared__ float s_op[FUSE ? S::R : 1];    // opacity gradients (fused Adam)
-    __shared__ float s_vrow[FUSE ? S::R : 1];  // SH second moment per row (fused Adam)
+    __shared__ float s_den[FUSE ? S::R : 1];   // SH Adam denominator per row (fused Adam)
     const uint32_t g0 = blockIdx.x * S::R;
     const uint32_t rows = min((uint32_t)S::R, a.n - g0);
     const uint32_t r = threadIdx.x;
@@ -375,13 +396,13 @@ __global__ void __launch_bounds__(PbShape<DEG>::R, 6) project_bwd_kernel(const P
             const uint32_t row = g0 + r;
             const float vr = A.first ? gsq * (1.0f - A.b2) : v_sh_old * A.b2 + gsq * (1.0f - A.b2);
             A.v_sh[row] = vr;
-            s_vrow[r] = vr;
+            s_den[r] = adam_den(A, vr);
         }
         __syncthreads();
         adam_rows<3>(A, const_cast<float*>(a.transforms), A.m_t, A.v_t, s_t, S::TS, g0, rows, 10, A.lr_t,
                      A.has_t_scale ? A.t_scale : nullptr, false, nullptr);
         adam_rows<4>(A, const_cast<float*>(a.sh), A.m_sh, A.v_sh, s_sh, S::SS, g0, rows, C3, A.lr_sh,
-                     A.has_sh_scale ? A.sh_scale : nullptr, true, s_vrow);
+                     A.has_sh_scale ? A.sh_scale : nullptr, true, s_den);
         adam_rows<1>(A, const_cast<float*>(a.raw_opac), A.m_o, A.v_o, s_op, 1, g0, rows, 1, A.lr_op, nullptr, false,
                      nullptr);
     }
