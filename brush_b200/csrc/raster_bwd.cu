@@ -106,14 +106,14 @@ __device__ __forceinline__ void pixel_init(PixelBwd& P, const BwdArgs& a, uint32
 // One pixel's step of the replay for one splat: exact forward arithmetic for
 // sigma / alpha / T, then the pixel's gradient contribution added into gv.
 template <bool SMOOTH, bool REFINE>
-__device__ __forceinline__ bool pixel_step(PixelBwd& P, float pcx, float dx0, float xx, float xy, float sx, float sy,
+__device__ __forceinline__ bool pixel_step(PixelBwd& P, float pcx, float dx0, float hxx, float xy, float sx, float sy,
                                            float c00, float c01, float c11, float ca, float thr, float clr,
                                            float clg, float clb, float wf, float hf, float (&gv)[10]) {
     if (P.done) return false;
     const float dyp = P.pcy - sy;
-    const float sigma = 0.5f * (xx + c11 * dyp * dyp) + xy * dyp;
+    const float sigma = bsx_sigma_row(hxx, xy, 0.5f * c11, dyp);
     if (!(sigma >= 0.0f) || sigma > thr) return false;
-    const float gauss = bsx_expf_neg(-sigma);
+    const float gauss = bsx_expf_raster(-sigma);
     const float alpha = bsx_min(0.999f, ca * gauss);
     const float wc = SMOOTH ? cutoff_weight(alpha) : (alpha >= 1.0f / 255.0f ? 1.0f : 0.0f);
     if (!(wc > 0.0f)) return false;
@@ -216,14 +216,14 @@ __global__ void __launch_bounds__(kBwdPixThreads, 8) raster_bwd_kernel(const Bwd
             const float4 B = s_b[t];
             const float2 Cc = s_c[t];
             const float dx0 = pcx - A.x;
-            const float xx = A.z * dx0 * dx0;
+            const float hxx = bsx_sigma_hxx(A.z, dx0);
             const float xy = A.w * dx0;
             float gv[kGradLanes];
 #pragma unroll
             for (int k = 0; k < kGradLanes; ++k) gv[k] = 0.0f;
-            bool contrib = pixel_step<SMOOTH, REFINE>(PA, pcx, dx0, xx, xy, A.x, A.y, A.z, A.w, B.x, B.y, Cc.y, B.z,
+            bool contrib = pixel_step<SMOOTH, REFINE>(PA, pcx, dx0, hxx, xy, A.x, A.y, A.z, A.w, B.x, B.y, Cc.y, B.z,
                                                       B.w, Cc.x, wf, hf, gv);
-            contrib |= pixel_step<SMOOTH, REFINE>(PB, pcx, dx0, xx, xy, A.x, A.y, A.z, A.w, B.x, B.y, Cc.y, B.z, B.w,
+            contrib |= pixel_step<SMOOTH, REFINE>(PB, pcx, dx0, hxx, xy, A.x, A.y, A.z, A.w, B.x, B.y, Cc.y, B.z, B.w,
                                                   Cc.x, wf, hf, gv);
             if (__any_sync(0xffffffffu, contrib)) {
                 const float tot = warp_sum10(gv, lane);

@@ -12,8 +12,11 @@
 // pixels it can reach (exact minimum of sigma over each warp's footprint), so
 // a warp skips splats none of its pixels can accept; pairs whose sigma
 // exceeds ln(255*o) + margin (where alpha < 1/255 is certain) skip the
-// exponential; colours are clamped once per splat while staging. Every
-// decision and every accumulated value stays bit-identical. Visibility marks
+// exponential; colours are clamped once per splat while staging. sigma is
+// evaluated with fused products (bsx_raster_sigma), e^-sigma by the bounded-
+// domain bsx_expf_raster and the colour sums by fused multiply-adds; the CPU
+// restatement performs the same operations, so every decision and every
+// accumulated value is bit-identical between the two. Visibility marks
 // are collected per batch in shared memory and written once per splat instead
 // of once per pixel.
 #include "raster_common.cuh"
@@ -40,7 +43,7 @@ constexpr int kFwdThreads = 128;
 template <bool BWD, bool SMOOTH>
 __global__ void __launch_bounds__(kFwdThreads) raster_fwd_kernel(const FwdArgs a) {
     __shared__ float4 s_a[kFwdThreads];  // x, y, c00, c01
-    __shared__ float4 s_b[kFwdThreads];  // c11, opacity, max(r,0), max(g,0)
+    __shared__ float4 s_b[kFwdThreads];  // c11 / 2, opacity, max(r,0), max(g,0)
     __shared__ float2 s_c[kFwdThreads];  // max(b,0), ln(255 o) + margin
     __shared__ uint32_t s_mask[kFwdThreads];
     __shared__ uint32_t s_gid[BWD ? kFwdThreads : 1];
@@ -73,7 +76,7 @@ __global__ void __launch_bounds__(kFwdThreads) raster_fwd_kernel(const FwdArgs a
             const float4* row = reinterpret_cast<const float4*>(a.projected + (size_t)g * BSX_PROJECTED_LANES);
             const float4 ra = __ldg(row), rb = __ldg(row + 1), rc = __ldg(row + 2);
             s_a[threadIdx.x] = ra;
-            s_b[threadIdx.x] = make_float4(rb.x, rb.y, bsx_max(rb.z, 0.0f), bsx_max(rb.w, 0.0f));
+            s_b[threadIdx.x] = make_float4(0.5f * rb.x, rb.y, bsx_max(rb.z, 0.0f), bsx_max(rb.w, 0.0f));
             s_c[threadIdx.x] = make_float2(bsx_max(rc.x, 0.0f), rc.z + margin);
             s_mask[threadIdx.x] =
                 warp_visit_mask(ra.x, ra.y, ra.z, ra.w, rb.x, rc.z + margin, tx * kTile, ty * kTile);
@@ -86,11 +89,11 @@ __global__ void __launch_bounds__(kFwdThreads) raster_fwd_kernel(const FwdArgs a
         for (uint32_t t = 0; t < n && !(doneA && doneB); ++t) {
             if (!(s_mask[t] & wbit)) continue;
             const float4 A = s_a[t];
-            const float c11 = s_b[t].x;
+            const float hc11 = s_b[t].x;
             const float thr = s_c[t].y;
-            // calc_sigma(px, py, conic, x, y) with dx shared by both pixels
+            // sigma (bsx_raster_sigma) with the column terms shared by both pixels
             const float dx = pcx - A.x;
-            const float xx = A.z * dx * dx;
+            const float hxx = bsx_sigma_hxx(A.z, dx);
             const float xy = A.w * dx;
             bool used = false;
 #pragma unroll
@@ -98,10 +101,10 @@ __global__ void __launch_bounds__(kFwdThreads) raster_fwd_kernel(const FwdArgs a
                 bool& done = q ? doneB : doneA;
                 if (done) continue;
                 const float dy = (q ? pcyB : pcyA) - A.y;
-                const float sigma = 0.5f * (xx + c11 * dy * dy) + xy * dy;
+                const float sigma = bsx_sigma_row(hxx, xy, hc11, dy);
                 if (!(sigma >= 0.0f) || sigma > thr) continue;
                 const float4 B = s_b[t];
-                const float alpha = bsx_min(0.999f, B.y * bsx_expf_neg(-sigma));
+                const float alpha = bsx_min(0.999f, B.y * bsx_expf_raster(-sigma));
                 const float wc = SMOOTH ? cutoff_weight(alpha) : (alpha >= 1.0f / 255.0f ? 1.0f : 0.0f);
                 if (!(wc > 0.0f)) continue;
                 float& T = q ? TB : TA;
@@ -114,13 +117,13 @@ __global__ void __launch_bounds__(kFwdThreads) raster_fwd_kernel(const FwdArgs a
                 const float vis = ae * T;
                 const float cb = s_c[t].x;
                 if (q) {
-                    rB += B.z * vis;
-                    gB += B.w * vis;
-                    bB += cb * vis;
+                    rB = bsx_fma(B.z, vis, rB);
+                    gB = bsx_fma(B.w, vis, gB);
+                    bB = bsx_fma(cb, vis, bB);
                 } else {
-                    rA += B.z * vis;
-                    gA += B.w * vis;
-                    bA += cb * vis;
+                    rA = bsx_fma(B.z, vis, rA);
+                    gA = bsx_fma(B.w, vis, gA);
+                    bA = bsx_fma(cb, vis, bA);
                 }
                 T = next_t;
                 used = true;

@@ -19,7 +19,9 @@
  *  - exp: Cody & Waite argument reduction x = k*ln2 + r with ln2 split into
  *    a 15-bit head (exact products for |k| <= 255) and a tail, followed by
  *    the degree-7 Taylor polynomial of e^r on |r| <= ln2/2 (truncation error
- *    r^8/8! < 5.3e-9 relative), then exact scaling by 2^k.
+ *    r^8/8! < 5.3e-9 relative), then exact scaling by 2^k. The rasterizers'
+ *    exp (bsx_expf_raster) trades a little accuracy for fewer operations on
+ *    its bounded domain.
  *  - ln: x = m * 2^e with m in [sqrt(1/2), sqrt(2)), s = (m-1)/(m+1),
  *    ln(m) = 2*atanh(s) = 2s(1 + s^2/3 + s^4/5 + ... + s^10/11)
  *    (|s| <= 0.1716, truncation < 2e-10 relative), plus e*ln2.
@@ -116,35 +118,50 @@ BSX_HD float bsx_expf(float x) {
     return (p * bsx_pow2i(ki + 64)) * 5.421010862427522e-20f; /* 2^-64 */
 }
 
-/* bsx_expf for arguments known to lie in [-80, 0] (no NaN, overflow or
- * subnormal handling needed), bit-identical to bsx_expf there, in fewer
- * operations and without conversion instructions:
- *  - k = rint(x*log2e) by the round-to-integer constant 1.5*2^23: adding it
- *    to t = x*log2e (|t| < 2^22) rounds t to an integer with the same
- *    ties-to-even rule, and subtracting it again is exact;
- *  - p*2^k by adding k to p's exponent field: the low bits of t + 1.5*2^23
- *    hold k in two's complement, and the constant's own mantissa bits vanish
- *    when shifted left by 23. p is in [0.7, 1.42] and k >= -116, so the
- *    result is a normal number and the integer add equals the exact product.
- * The CPU test-suite sweeps every float in [-80, 0] against bsx_expf. */
-BSX_HD float bsx_expf_neg(float x) {
+/* exp(x) for the rasterizers' Gaussian falloff, x in [-87, 0] (there e^x is
+ * a normal float; the rasterizers only evaluate x >= -(ln(255) + 1)):
+ *  - k = rint(x*log2e) by the round-to-integer constant 1.5*2^23 added in the
+ *    same fused multiply-add, then r = x - k*ln2 with one float ln2 (for
+ *    |k| <= 24, i.e. x >= -16, the reduction error is below 0.4 ulp);
+ *  - e^r on |r| <= ln2/2 by a degree-6 polynomial whose coefficients come
+ *    from a Remez exchange for relative error, rounded to float (minimax
+ *    error 1.9e-9 before rounding);
+ *  - p*2^k by adding k to p's exponent field: the low bits of
+ *    x*log2e + 1.5*2^23 hold k in two's complement, and the constant's own
+ *    mantissa bits vanish when shifted left by 23; the result is normal on
+ *    the domain, so the integer add equals the exact product.
+ * Error against the exact exponential: at most 1.4 ulp on [-16, 0] (every
+ * float checked; 99% of them below 0.5 ulp), at most 4.5 ulp on [-87, -16].
+ * The CPU test-suite checks a sweep of the domain against the C library. */
+BSX_HD float bsx_expf_raster(float x) {
     const float kLog2e = 1.4426950216293335f;
-    const float kLn2Hi = 0.693145751953125f;
-    const float kLn2Lo = 1.428606765330187e-06f;
+    const float kLn2 = 0.693147182464599609375f;
     const float kRound = 12582912.0f; /* 1.5 * 2^23 */
-    const float tk = x * kLog2e + kRound;
+    const float tk = bsx_fma(x, kLog2e, kRound);
     const float k = tk - kRound;
-    float r = bsx_fma(-k, kLn2Hi, x);
-    r = bsx_fma(-k, kLn2Lo, r);
-    float p = 0.00019841270113829523f;
-    p = bsx_fma(p, r, 0.0013888889225199819f);
-    p = bsx_fma(p, r, 0.008333333767950535f);
-    p = bsx_fma(p, r, 0.0416666679084301f);
-    p = bsx_fma(p, r, 0.1666666716337204f);
-    p = bsx_fma(p, r, 0.5f);
+    const float r = bsx_fma(-k, kLn2, x);
+    float p = 0.0013836835278198123f;
+    p = bsx_fma(p, r, 0.008374824188649654f);
+    p = bsx_fma(p, r, 0.04166822507977486f);
+    p = bsx_fma(p, r, 0.16666419804096222f);
+    p = bsx_fma(p, r, 0.49999991059303284f);
     p = bsx_fma(p, r, 1.0f);
     p = bsx_fma(p, r, 1.0f);
     return bsx_bits_to_f32(bsx_f32_to_bits(p) + (bsx_f32_to_bits(tk) << 23));
+}
+
+/* The rasterizers' sigma = 0.5 (c00 dx^2 + c11 dy^2) + c01 dx dy
+ * (brush-cube/src/lib.rs:634-638) as one fixed sequence of roundings, shared
+ * by the forward and backward kernels and their CPU restatement:
+ *   hxx = 0.5 ((c00 dx) dx),  sigma = fma(c01 dx, dy, fma((0.5 c11) dy, dy, hxx)).
+ * Halving is exact, so this is the expression with fused products; hxx and
+ * c01 dx depend only on the column and are shared by pixels that have it. */
+BSX_HD float bsx_sigma_hxx(float c00, float dx) { return 0.5f * ((c00 * dx) * dx); }
+BSX_HD float bsx_sigma_row(float hxx, float xy, float hc11, float dy) {
+    return bsx_fma(xy, dy, bsx_fma(hc11 * dy, dy, hxx));
+}
+BSX_HD float bsx_raster_sigma(float c00, float c01, float c11, float dx, float dy) {
+    return bsx_sigma_row(bsx_sigma_hxx(c00, dx), c01 * dx, 0.5f * c11, dy);
 }
 
 /* Natural logarithm in float32. */

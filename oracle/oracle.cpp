@@ -91,6 +91,13 @@ inline float calc_sigma(float px, float py, S2 c, float x, float y) {
     return 0.5f * (c.c00 * dx * dx + c.c11 * dy * dy) + c.c01 * dx * dy;
 }
 
+// e^-sigma of the tile rasterizers (rasterize.rs:120-135): bsx_expf_raster,
+// whose domain is [-87, 0]. The kernels evaluate it only for 0 <= sigma <=
+// ln(255) + 1 (other pairs are rejected before); here every pair is
+// evaluated, so sigma is clamped to the domain first, which changes no
+// accepted pair (sigma < 0 and alpha < 1/255 are rejected either way).
+inline float raster_gauss(float sigma) { return bsx_expf_raster(-bsx_clamp(sigma, 0.0f, 87.0f)); }
+
 // kernels/helpers.rs:166-190 (smooth alpha cutoff)
 const float kCutMid = 1.0f / 255.0f;
 const float kCutBand = 1.0e-3f;
@@ -784,9 +791,8 @@ void* orc_render(const bsx_project_uniforms* up, const float* transforms, const 
                 for (uint32_t k = lo; k < hi; ++k) {
                     uint32_t g = r->isect_gid[k];
                     const float* p = &r->projected[(size_t)g * 12];
-                    S2 conic{p[2], p[3], p[4]};
-                    float sigma = calc_sigma(pcx, pcy, conic, p[0], p[1]);
-                    float alpha = bsx_min(0.999f, p[5] * bsx_expf(-sigma));
+                    float sigma = bsx_raster_sigma(p[2], p[3], p[4], pcx - p[0], pcy - p[1]);
+                    float alpha = bsx_min(0.999f, p[5] * raster_gauss(sigma));
                     float w_cut = r->smooth ? alpha_cutoff_weight(alpha) : (alpha >= kCutMid ? 1.0f : 0.0f);
                     if (sigma >= 0.0f && w_cut > 0.0f) {
                         float ae = alpha * w_cut;
@@ -797,9 +803,9 @@ void* orc_render(const bsx_project_uniforms* up, const float* transforms, const 
                             r->visible[g] = 1.0f;
                         }
                         float v = ae * T_acc;
-                        pr += bsx_max(p[6], 0.0f) * v;
-                        pg += bsx_max(p[7], 0.0f) * v;
-                        pb += bsx_max(p[8], 0.0f) * v;
+                        pr = bsx_fma(bsx_max(p[6], 0.0f), v, pr);
+                        pg = bsx_fma(bsx_max(p[7], 0.0f), v, pg);
+                        pb = bsx_fma(bsx_max(p[8], 0.0f), v, pb);
                         T_acc = next_t;
                         last = k + 1;
                     }
@@ -903,8 +909,8 @@ void orc_rasterize_bwd(void* h, const float* v_output, int compute_refine, float
                 uint32_t px = ox + p % 16, py = oy + p / 16;
                 float pcx = (float)px + 0.5f, pcy = (float)py + 0.5f;
                 float dx = sx - pcx, dy = sy - pcy;
-                float sigma = 0.5f * (c00 * dx * dx + c11 * dy * dy) + c01 * dx * dy;
-                float gauss = bsx_expf(-sigma);
+                float sigma = bsx_raster_sigma(c00, c01, c11, dx, dy);
+                float gauss = raster_gauss(sigma);
                 float alpha = bsx_min(0.999f, ca * gauss);
                 float w_cut = r->smooth ? alpha_cutoff_weight(alpha) : (alpha >= kCutMid ? 1.0f : 0.0f);
                 if (!(sigma >= 0.0f && w_cut > 0.0f)) continue;
@@ -1490,17 +1496,27 @@ float orc_expf(float x) { return bsx_expf(x); }
 float orc_logf(float x) { return bsx_logf(x); }
 float orc_atan2f(float y, float x) { return bsx_atan2f(y, x); }
 
-// Number of floats in [-|lo|, 0] (every bit pattern from -0 to lo) where the
-// rasterizers' bsx_expf_neg differs in any bit from bsx_expf.
-uint64_t orc_expf_neg_mismatches(float lo) {
+// Largest error in ulp of the rasterizers' bsx_expf_raster against the
+// exponential evaluated in double precision, over every `stride`-th float in
+// [lo, 0] (lo <= 0, bit patterns from -0 downwards); -1 if any result is not
+// finite and positive.
+double orc_expf_raster_max_ulp(float lo, uint32_t stride) {
     const uint32_t last = bsx_f32_to_bits(-fabsf(lo));
-    uint64_t bad = 0;
-#pragma omp parallel for reduction(+ : bad) schedule(static)
-    for (int64_t b = 0x80000000ll; b <= (int64_t)last; ++b) {
+    const int64_t step = stride ? stride : 1;
+    double worst = 0.0;
+#pragma omp parallel for reduction(max : worst) schedule(static)
+    for (int64_t b = 0x80000000ll; b <= (int64_t)last; b += step) {
         const float x = bsx_bits_to_f32((uint32_t)b);
-        bad += bsx_f32_to_bits(bsx_expf_neg(x)) != bsx_f32_to_bits(bsx_expf(x));
+        const float y = bsx_expf_raster(x);
+        const double ref = exp((double)x);
+        if (!(y > 0.0f) || !bsx_is_finite(y)) {
+            worst = 1e30;
+            continue;
+        }
+        const double ulp = ldexp(1.0, ilogbf((float)ref) - 23);
+        worst = fmax(worst, fabs((double)y - ref) / ulp);
     }
-    return bad;
+    return worst >= 1e30 ? -1.0 : worst;
 }
 
 }  // extern "C"

@@ -112,8 +112,8 @@ def lib() -> C.CDLL:
                                         C.c_size_t]
         _lib.orc_ply_encode_rows.restype = C.c_uint64
         _lib.orc_ply_encode_rows.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p]
-        _lib.orc_expf_neg_mismatches.restype = C.c_uint64
-        _lib.orc_expf_neg_mismatches.argtypes = [C.c_float]
+        _lib.orc_expf_raster_max_ulp.restype = C.c_double
+        _lib.orc_expf_raster_max_ulp.argtypes = [C.c_float, C.c_uint32]
         _lib.orc_logf.argtypes = [C.c_float]
         _lib.orc_set_threads.argtypes = [C.c_int]
         _lib.orc_get_threads.restype = C.c_int
@@ -330,9 +330,10 @@ def atan2f(y: float, x: float) -> float:
     return float(lib().orc_atan2f(float(y), float(x)))
 
 
-def expf_neg_mismatches(lo: float) -> int:
-    """Floats in [lo, 0] where the rasterizers' exp differs from bsx_expf (full sweep)."""
-    return int(lib().orc_expf_neg_mismatches(float(lo)))
+def expf_raster_max_ulp(lo: float, stride: int = 1) -> float:
+    """Largest ulp error of bsx_expf_raster over every stride-th float in [lo, 0]
+    against the double-precision exponential (-1 if a result is not finite and positive)."""
+    return float(lib().orc_expf_raster_max_ulp(float(lo), int(stride)))
 
 
 def refine_cfg(**kw) -> RefineCfg:

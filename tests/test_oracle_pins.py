@@ -105,9 +105,11 @@ def test_shared_exp_log_accuracy(orc):
         assert abs(np.int64(np.float32(lg).view(np.int32)) - np.int64(ref.view(np.int32))) <= 2
 
 
-def test_raster_exp_bit_identical_on_its_domain(orc):
-    """bsx_expf_neg (the rasterizers' exp) equals bsx_expf on every float in [-80, 0]."""
-    assert orc.expf_neg_mismatches(-80.0) == 0
+def test_raster_exp_accuracy_on_its_domain(orc):
+    """bsx_expf_raster (the rasterizers' exp): within 1.4 ulp of the exact exponential on
+    [-16, 0] (every float there measures 1.37 at most), within 4.5 ulp down to -87."""
+    assert 0.0 <= orc.expf_raster_max_ulp(-16.0, 7) <= 1.4
+    assert 0.0 <= orc.expf_raster_max_ulp(-87.0, 101) <= 4.5
 
 
 def test_shared_atan2_accuracy_and_special_values(orc):
