@@ -16,7 +16,9 @@
 // into the [H,W,4] v_output layout the raster backward consumes (alpha lane
 // 0), and emits per-block loss sums that a second tiny kernel reduces in a
 // fixed order. This removes the reference's permute/contiguous copies, the
-// separate mean kernel and the zero-fill of the gradient image.
+// separate mean kernel and the zero-fill of the gradient image. Its blur taps
+// accumulate by fused multiply-adds (same tap order; the loss map and gradient
+// are checked against the CPU restatement to 1e-5 relative, not bit for bit).
 #include "common.cuh"
 
 namespace bsx {
@@ -385,8 +387,8 @@ __device__ __forceinline__ void blur_window(const float* v, const float* w, floa
     for (int j = 0; j < N; ++j) {
         float acc = 0.0f;
 #pragma unroll
-        for (int d = 1; d < 6; ++d) acc += (v[j + 5 - d] + v[j + 5 + d]) * w[5 - d];
-        out[j] = acc + v[j + 5] * w[5];
+        for (int d = 1; d < 6; ++d) acc = __fmaf_rn(v[j + 5 - d] + v[j + 5 + d], w[5 - d], acc);
+        out[j] = __fmaf_rn(v[j + 5], w[5], acc);
     }
 }
 
@@ -467,18 +469,18 @@ __global__ void __launch_bounds__(kFusedThreads) loss_fused_kernel(const __grid_
                     for (int d = 1; d < 6; ++d) {
                         const float wd = w[5 - d];
                         const float xl = xv[j + 5 - d], yl = yv[j + 5 - d], xr = xv[j + 5 + d], yr = yv[j + 5 + d];
-                        sx += (xl + xr) * wd;
-                        sx2 += (xl * xl + xr * xr) * wd;
-                        sy += (yl + yr) * wd;
-                        sy2 += (yl * yl + yr * yr) * wd;
-                        sxy += (xl * yl + xr * yr) * wd;
+                        sx = __fmaf_rn(xl + xr, wd, sx);
+                        sx2 = __fmaf_rn(__fmaf_rn(xl, xl, xr * xr), wd, sx2);
+                        sy = __fmaf_rn(yl + yr, wd, sy);
+                        sy2 = __fmaf_rn(__fmaf_rn(yl, yl, yr * yr), wd, sy2);
+                        sxy = __fmaf_rn(__fmaf_rn(xl, yl, xr * yr), wd, sxy);
                     }
                     const float xc = xv[j + 5], yc = yv[j + 5], wc = w[5];
-                    m[0][j] = sx + xc * wc;
-                    m[1][j] = sx2 + xc * xc * wc;
-                    m[2][j] = sy + yc * wc;
-                    m[3][j] = sy2 + yc * yc * wc;
-                    m[4][j] = sxy + xc * yc * wc;
+                    m[0][j] = __fmaf_rn(xc, wc, sx);
+                    m[1][j] = __fmaf_rn(xc * xc, wc, sx2);
+                    m[2][j] = __fmaf_rn(yc, wc, sy);
+                    m[3][j] = __fmaf_rn(yc * yc, wc, sy2);
+                    m[4][j] = __fmaf_rn(xc * yc, wc, sxy);
                 }
 #pragma unroll
                 for (int j = 0; j < kSeg; ++j)
