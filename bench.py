@@ -311,6 +311,25 @@ def run_ours(args, rank, world, local_rank):
     ctx.profile(False)
     prof = ctx.profile_read()
 
+    # ---- per-step distribution: an event after every step on the launching
+    # stream (no host synchronisation added), the max over ranks per step -----
+    restart()
+    marks = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+
+    def per_step():
+        marks[0].record()
+        for i in range(args.steps):
+            step(args.warmup + i)
+            marks[i + 1].record()
+
+    _time_region(args, world, per_step)
+    step_times = torch.tensor([marks[i].elapsed_time(marks[i + 1]) for i in range(args.steps)], device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(step_times, op=torch.distributed.ReduceOp.MAX)
+    q = torch.quantile(step_times.double().cpu(), torch.tensor([0.1, 0.5, 0.9], dtype=torch.float64)).tolist()
+    step_ms = {"p10": round(q[0], 4), "median": round(q[1], 4), "p90": round(q[2], 4),
+               "note": "per-step CUDA-event times of a separate pass over the same steps (max over ranks)"}
+
     # ---- e2e: public API with host buffers ----------------------------------
     # Training: every step uploads its ground truth from pinned host memory and
     # reads its loss back into pinned host memory, inside the timed region; the
@@ -428,6 +447,7 @@ def run_ours(args, rank, world, local_rank):
                    "num_visible": V, "num_intersections": M, "intersections_after_early_out": Mp},
         "e2e": {"value": round(e2e_value, 3), "unit": unit, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": int(launches),
+        "step_ms": step_ms,
         "roofline": roof,
         "kernels": kernels,
         "clocks": clocks,
@@ -441,6 +461,8 @@ def run_ours(args, rank, world, local_rank):
                                   for r in timed_refines]}
     if train:
         line["fwd_bwd_ms"] = round(sum(v[0] for n, v in prof.items() if n not in not_fwdbwd) / args.steps, 4)
+        if world == 1:
+            line["fwd_bwd_note"] = "includes the Adam update fused into project_bwd_kernel"
         live["trainer"].close()
     else:
         stage = {"project": ("project_fwd_kernel", "compact_visible_kernel"), "scan": ("scan_kernel",),
@@ -675,7 +697,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=100)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
