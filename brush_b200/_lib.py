@@ -162,6 +162,7 @@ class DpExchange(C.Structure):
         ("refine_rows", C.c_uint32),
         ("epoch", C.c_uint32),
         ("timeout_ns", C.c_uint64),
+        ("grad_slot_rows", C.c_uint32),
     ]
 
 

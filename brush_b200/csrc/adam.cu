@@ -13,8 +13,9 @@
 //
 // Data-parallel form (bsx_dp_adam_step): each rank owns a row shard. The
 // block reads its tile's gradient from every rank's buffer (peer loads over
-// NVLink, summed in rank order), updates, and writes the new rows into every
-// rank's parameters (peer stores). Arrival / departure flags in each rank's
+// NVLink, summed in rank order) or, when the ranks pushed their rows into this
+// rank's gradient slots, from those local slots in the same order; updates;
+// and writes the new rows into every rank's parameters (peer stores). Arrival / departure flags in each rank's
 // flag words order the exchange against the ranks' neighbouring steps; every
 // wait is bounded by a wall-clock timeout.
 #include <algorithm>
@@ -473,10 +474,15 @@ extern "C" bsx_status bsx_dp_adam_step(bsx_ctx* ctx, const bsx_dp_exchange* ex, 
             g.peer_param[q] = nullptr;
             g.peer_grad[q] = nullptr;
         }
+        if (ex->grad_slot_rows && (ex->grad_slot_rows < re - rb || !s.d_grad[rank]))
+            return fail(ctx, BSX_ERR_INVALID_ARG, "gradient slots smaller than the shard");
         for (int q = 0; q < world; ++q) {
-            if (!s.d_param[q] || !s.d_grad[q]) return fail(ctx, BSX_ERR_INVALID_ARG, "null parameter / gradient");
+            if (!s.d_param[q] || (!ex->grad_slot_rows && !s.d_grad[q]))
+                return fail(ctx, BSX_ERR_INVALID_ARG, "null parameter / gradient");
             g.peer_param[q] = s.d_param[q] + (size_t)rb * s.cols;
-            g.peer_grad[q] = s.d_grad[q] + (size_t)rb * s.cols;
+            // slots: rank q's rows of this shard sit in this rank's own buffer
+            g.peer_grad[q] = ex->grad_slot_rows ? s.d_grad[rank] + (size_t)q * ex->grad_slot_rows * s.cols
+                                                : s.d_grad[q] + (size_t)rb * s.cols;
             vec = vec && aligned16(g.peer_param[q]) && aligned16(g.peer_grad[q]);
         }
         g.param = g.peer_param[rank];

@@ -87,6 +87,27 @@ struct FusedAdam {
     int keep_grads;  // also write the dense gradients
 };
 
+// Data-parallel gradient push from the projection backward. Rank q owns rows
+// [n q / world, n (q + 1) / world); owner q's gradient region of group k
+// (transforms, SH rows, opacities) holds `world` slots of its shard, and the
+// gradient that rank s computed for global row g (owned by q) goes to
+// dst[k][q] + (s * slot_rows + g - shard_begin(q)) * cols. world == 0: no push.
+struct GradPush {
+    float* dst[3][BSX_MAX_RANKS];
+    uint32_t n, slot_rows;
+    int world, rank;
+};
+
+__host__ __device__ inline uint32_t shard_begin(uint32_t n, int q, int world) {
+    return (uint32_t)((uint64_t)n * (uint32_t)q / (uint32_t)world);
+}
+// Owner of row g: floor(g world / n) never exceeds it and is at most one below.
+__host__ __device__ inline int shard_owner(uint32_t n, uint32_t g, int world) {
+    int q = (int)(((uint64_t)g * (uint32_t)world) / n);
+    if (q + 1 < world && shard_begin(n, q + 1, world) <= g) ++q;
+    return q;
+}
+
 // 1 / (1 - beta^step) in float, by repeated multiplication (adam.cu fill_cfg).
 inline float adam_inv_bias_correction(float beta, uint32_t step) {
     float r = 1.0f;

@@ -21,6 +21,7 @@ namespace {
 
 struct PbArgs {
     FusedAdam adam;
+    GradPush push;
     const float* transforms;
     const float* sh;
     const float* raw_opac;
@@ -127,6 +128,51 @@ __device__ __forceinline__ void stage_out(float* __restrict__ dst, const float* 
         const uint32_t r = row_of(i, inv);
         dst[i] = src[r * stride + (i - r * cols)];
     }
+}
+
+// Data-parallel push of the block's staged gradient rows [g0, g0 + rows) of
+// group k: into slot `rank` of their owners. A block spans at most two owners
+// (every shard has at least a block of rows, which the host checks); rows
+// before the second owner's first row form one contiguous run, the rest a
+// second one.
+__device__ __forceinline__ void push_out(const GradPush& P, int k, const float* src, uint32_t g0, uint32_t rows,
+                                         uint32_t cols, uint32_t stride) {
+    const int q0 = shard_owner(P.n, g0, P.world);
+    const uint32_t b1 = q0 + 1 < P.world ? shard_begin(P.n, q0 + 1, P.world) : P.n;
+    const uint32_t split = min(rows, b1 - g0);
+    float* d0 = P.dst[k][q0] + ((size_t)P.rank * P.slot_rows + (g0 - shard_begin(P.n, q0, P.world))) * cols;
+    float* d1 = split < rows ? P.dst[k][q0 + 1] + (size_t)P.rank * P.slot_rows * cols : nullptr;
+    const uint32_t n0 = split * cols, total = rows * cols;
+    const float inv = 1.0f / (float)cols;
+    // 16-byte stores (NVLink moves whole words far faster than single floats)
+    // when both runs start 16-byte aligned and the first ends on a word
+    const bool vec = ((reinterpret_cast<uintptr_t>(d0) | reinterpret_cast<uintptr_t>(d1)) & 15u) == 0 && n0 % 4 == 0;
+    const uint32_t n4 = vec ? total / 4 : 0;
+    for (uint32_t j = threadIdx.x; j < n4; j += blockDim.x) {
+        uint32_t r = row_of(4 * j, inv), c = 4 * j - r * cols;
+        float v[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            v[i] = src[r * stride + c];
+            if (++c == cols) {
+                c = 0;
+                ++r;
+            }
+        }
+        const float4 w = make_float4(v[0], v[1], v[2], v[3]);
+        if (4 * j < n0) reinterpret_cast<float4*>(d0)[j] = w;
+        else reinterpret_cast<float4*>(d1)[j - n0 / 4] = w;
+    }
+    for (uint32_t i = 4 * n4 + threadIdx.x; i < total; i += blockDim.x) {
+        const uint32_t r = row_of(i, inv);
+        const float v = src[r * stride + (i - r * cols)];
+        if (i < n0) d0[i] = v;
+        else d1[i - n0] = v;
+    }
+}
+__device__ __forceinline__ float* push_scalar(const GradPush& P, uint32_t g) {
+    const int q = shard_owner(P.n, g, P.world);
+    return P.dst[2][q] + (size_t)P.rank * P.slot_rows + (g - shard_begin(P.n, q, P.world));
 }
 
 template <int DEG>
@@ -240,7 +286,16 @@ __global__ void __launch_bounds__(PbShape<DEG>::R, 6) project_bwd_kernel(const P
     __shared__ float s_g[S::R * S::GS];
     __shared__ float s_op[FUSE ? S::R : 1];    // opacity gradients (fused Adam)
     __shared__ float s_den[FUSE ? S::R : 1];   // SH Adam denominator per row (fused Adam)
-    const uint32_t g0 = blockIdx.x * S::R;
+    // With the gradient push, block b takes row block (b % world) K + b / world
+    // (K = row blocks per owner, rounded up): any `world` consecutive blocks
+    // write to different owners, so the peer stores spread over the launch.
+    uint32_t blk = blockIdx.x;
+    if (a.push.world) {
+        const uint32_t nb = (a.n + S::R - 1) / S::R, per = (nb + a.push.world - 1) / a.push.world;
+        blk = (blockIdx.x % a.push.world) * per + blockIdx.x / a.push.world;
+        if (blk >= nb) return;
+    }
+    const uint32_t g0 = blk * S::R;
     const uint32_t rows = min((uint32_t)S::R, a.n - g0);
     const uint32_t r = threadIdx.x;
     // the row's scalar inputs, issued with the staged rows rather than after them
@@ -264,7 +319,7 @@ __global__ void __launch_bounds__(PbShape<DEG>::R, 6) project_bwd_kernel(const P
 #pragma unroll
             for (int k = 0; k < C3; ++k) shr[k] = 0.0f;
             if (FUSE) s_op[r] = 0.0f;
-            if (!FUSE || a.adam.keep_grads) a.v_opac[g] = 0.0f;
+            if (!FUSE || a.adam.keep_grads) *(a.push.world ? push_scalar(a.push, g) : a.v_opac + g) = 0.0f;
             a.v_refine[g] = 0.0f;
         } else {
             Uni u = a.u;
@@ -295,7 +350,7 @@ __global__ void __launch_bounds__(PbShape<DEG>::R, 6) project_bwd_kernel(const P
             const float os = bsx_sigmoid(raw_op);
             const float vop = fc * valpha * os * (1.0f - os);
             if (FUSE) s_op[r] = vop;
-            if (!FUSE || a.adam.keep_grads) a.v_opac[g] = vop;
+            if (!FUSE || a.adam.keep_grads) *(a.push.world ? push_scalar(a.push, g) : a.v_opac + g) = vop;
             const float rc = bsx_is_finite(vref) ? vref : 0.0f;
             a.v_refine[g] = bsx_clamp(rc, 0.0f, 1.0e32f);
 
@@ -369,7 +424,12 @@ __global__ void __launch_bounds__(PbShape<DEG>::R, 6) project_bwd_kernel(const P
         }
     }
     __syncthreads();
-    if (!FUSE || a.adam.keep_grads) {
+    if (!FUSE && a.push.world) {
+        push_out(a.push, 0, s_t, g0, rows, 10, S::TS);
+        push_out(a.push, 1, s_sh, g0, rows, C3, S::SS);
+        // the peer stores are made visible before the exchange kernel's release
+        __threadfence_system();
+    } else if (!FUSE || a.adam.keep_grads) {
         stage_out(a.v_transforms + (size_t)g0 * 10, s_t, rows, 10, S::TS);
         stage_out(a.v_sh + (size_t)g0 * C3, s_sh, rows, C3, S::SS);
     }
@@ -411,8 +471,10 @@ __global__ void __launch_bounds__(PbShape<DEG>::R, 6) project_bwd_kernel(const P
 template <int DEG, bool FUSE>
 void launch_deg(const PbArgs& a, cudaStream_t st) {
     constexpr int R = PbShape<DEG>::R;
-    if (a.u.model == BSX_CAMERA_PINHOLE) project_bwd_kernel<DEG, true, FUSE><<<(a.n + R - 1) / R, R, 0, st>>>(a);
-    else project_bwd_kernel<DEG, false, FUSE><<<(a.n + R - 1) / R, R, 0, st>>>(a);
+    uint32_t grid = (a.n + R - 1) / R;
+    if (a.push.world) grid = (grid + a.push.world - 1) / a.push.world * a.push.world;  // whole rounds of owners
+    if (a.u.model == BSX_CAMERA_PINHOLE) project_bwd_kernel<DEG, true, FUSE><<<grid, R, 0, st>>>(a);
+    else project_bwd_kernel<DEG, false, FUSE><<<grid, R, 0, st>>>(a);
 }
 
 }  // namespace
@@ -420,10 +482,15 @@ void launch_deg(const PbArgs& a, cudaStream_t st) {
 bsx_status launch_project_bwd(bsx_ctx* ctx, const bsx_project_uniforms& uni, const float* transforms, const float* sh,
                               const float* raw_opac, uint32_t n, uint32_t coeffs, int degree, int mip,
                               const float* v_grad, float* v_transforms, float* v_sh, float* v_opac, float* v_refine,
-                              const FusedAdam* adam) {
+                              const FusedAdam* adam, const GradPush* push) {
     if (n == 0) return BSX_OK;
     PbArgs a;
     if (adam) a.adam = *adam;
+    a.push.world = 0;
+    if (push && push->world > 1) {
+        if (adam) return fail(ctx, BSX_ERR_INVALID_ARG, "gradient push and fused Adam are exclusive");
+        a.push = *push;
+    }
     a.transforms = transforms;
     a.sh = sh;
     a.raw_opac = raw_opac;

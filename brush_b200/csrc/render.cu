@@ -30,7 +30,7 @@ bsx_status launch_raster_bwd(bsx_ctx* ctx, const uint32_t* isect_gid, const uint
 bsx_status launch_project_bwd(bsx_ctx* ctx, const bsx_project_uniforms& uni, const float* transforms, const float* sh,
                               const float* raw_opac, uint32_t n, uint32_t coeffs, int degree, int mip,
                               const float* v_grad, float* v_transforms, float* v_sh, float* v_opac, float* v_refine,
-                              const FusedAdam* adam);
+                              const FusedAdam* adam, const GradPush* push = nullptr);
 
 // Projection backward of the last forward render with AdamScaled applied to
 // the splats in the same kernel (single-GPU trainer step).
@@ -41,6 +41,15 @@ bsx_status project_bwd_fused(bsx_ctx* ctx, const float* d_v_combined, float* d_v
     if (3 * f.coeffs > 80) return fail(ctx, BSX_ERR_SHAPE, "fused Adam supports at most 80 SH columns");
     return launch_project_bwd(ctx, f.uni, f.transforms, f.sh, f.raw_opac, f.n, f.coeffs, (int)f.degree, f.mip,
                               d_v_combined, d_v_transforms, d_v_sh, d_v_raw_opac, d_v_refine, &adam);
+}
+
+// Projection backward of the last forward render whose gradient rows go
+// straight into their owners' exchange slots (data-parallel trainer step).
+bsx_status project_bwd_push(bsx_ctx* ctx, const float* d_v_combined, float* d_v_refine, const GradPush& push) {
+    const bsx_fwd_state& f = ctx->fwd;
+    if (!f.valid) return fail(ctx, BSX_ERR_STATE, "project_bwd needs a preceding render");
+    return launch_project_bwd(ctx, f.uni, f.transforms, f.sh, f.raw_opac, f.n, f.coeffs, (int)f.degree, f.mip,
+                              d_v_combined, nullptr, nullptr, nullptr, d_v_refine, nullptr, &push);
 }
 
 namespace {

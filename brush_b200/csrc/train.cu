@@ -27,6 +27,7 @@ namespace bsx {
 
 bsx_status project_bwd_fused(bsx_ctx* ctx, const float* d_v_combined, float* d_v_transforms, float* d_v_sh,
                              float* d_v_raw_opac, float* d_v_refine, const FusedAdam& adam);
+bsx_status project_bwd_push(bsx_ctx* ctx, const float* d_v_combined, float* d_v_refine, const GradPush& push);
 
 namespace {
 
@@ -120,7 +121,7 @@ bsx_loss_cfg loss_cfg_of(const bsx_train_config& c) {
 bsx_status forward_backward(bsx_trainer* tr, const bsx_camera* cam, uint32_t w, uint32_t h, const uint32_t* gt,
                             const float* transforms, const float* sh, const float* opac, float* vt, float* vs,
                             float* vo, float* vr, int refine, float* d_loss, bsx_render_out* out,
-                            const FusedAdam* adam = nullptr) {
+                            const FusedAdam* adam = nullptr, const GradPush* push = nullptr) {
     bsx_ctx* ctx = tr->ctx;
     bsx_status s = bsx_render_fwd(ctx, cam, w, h, transforms, sh, opac, tr->n, tr->coeffs, tr->cfg.render_mode,
                                   BSX_PASS_BACKWARD, tr->cfg.background, out);
@@ -133,6 +134,7 @@ bsx_status forward_backward(bsx_trainer* tr, const bsx_camera* cam, uint32_t w, 
     s = bsx_rasterize_bwd(ctx, tr->v_output.as<float>(), refine, tr->v_combined.as<float>());
     if (s != BSX_OK) return s;
     if (adam) return project_bwd_fused(ctx, tr->v_combined.as<float>(), vt, vs, vo, vr, *adam);
+    if (push) return project_bwd_push(ctx, tr->v_combined.as<float>(), vr, *push);
     return bsx_project_bwd(ctx, tr->v_combined.as<float>(), vt, vs, vo, vr);
 }
 
@@ -398,10 +400,33 @@ bsx_status bsx_train_step_dp(bsx_trainer* tr, const bsx_camera* cam, uint32_t w,
         return fail(ctx, BSX_ERR_INVALID_ARG, "rank / world out of range (world <= 8)");
     if (!ex->d_refine[rank]) return fail(ctx, BSX_ERR_INVALID_ARG, "the exchange needs refine-weight buffers");
     cudaSetDevice(ctx->device);
+    // Gradient push into the owners' slots: needs slots for every shard row,
+    // 16-byte aligned slot starts, and shards of at least one projection block
+    // (128 rows) so that a block's rows span at most two owners.
+    const uint32_t slot = ex->grad_slot_rows;
+    bool push = world > 1 && slot > 0 && !tr->keep_grads;
+    for (int q = 0; push && q < world; ++q) {
+        const uint32_t rows = shard_begin(tr->n, q + 1, world) - shard_begin(tr->n, q, world);
+        push = rows >= 128 && rows <= slot && slot % 4 == 0 && sp->d_v_transforms[q] && sp->d_v_sh_coeffs[q] &&
+               sp->d_v_raw_opac[q];
+    }
+    GradPush gp{};
+    if (push) {
+        for (int q = 0; q < world; ++q) {
+            gp.dst[0][q] = sp->d_v_transforms[q];
+            gp.dst[1][q] = sp->d_v_sh_coeffs[q];
+            gp.dst[2][q] = sp->d_v_raw_opac[q];
+        }
+        gp.n = tr->n;
+        gp.slot_rows = slot;
+        gp.world = world;
+        gp.rank = rank;
+    }
     bsx_render_out out{};
     bsx_status s = forward_backward(tr, cam, w, h, gt, sp->d_transforms[rank], sp->d_sh_coeffs[rank],
                                     sp->d_raw_opac[rank], sp->d_v_transforms[rank], sp->d_v_sh_coeffs[rank],
-                                    sp->d_v_raw_opac[rank], ex->d_refine[rank], refine, d_loss, &out);
+                                    sp->d_v_raw_opac[rank], ex->d_refine[rank], refine, d_loss, &out, nullptr,
+                                    push ? &gp : nullptr);
     if (s != BSX_OK) return s;
     const uint32_t rb = (uint32_t)((uint64_t)tr->n * rank / world), re = (uint32_t)((uint64_t)tr->n * (rank + 1) / world);
     float* m[3];
@@ -431,6 +456,7 @@ bsx_status bsx_train_step_dp(bsx_trainer* tr, const bsx_camera* cam, uint32_t w,
     bsx_dp_exchange e = *ex;
     e.refine_rows = refine ? tr->n : 0;
     e.epoch = ++tr->dp_epoch;
+    e.grad_slot_rows = push ? slot : 0;
     const bsx_adam_cfg ac{0.9f, 0.999f, 1e-15f, tr->step, 1.0f / (float)world};
     s = bsx_dp_adam_step(ctx, &e, g, 3, &ac);
     if (s != BSX_OK) return s;

@@ -35,17 +35,25 @@ def shard_rows(rows: int, rank: int, world: int) -> tuple[int, int]:
 
 
 class ExchangeLayout:
-    """Float offsets of the sub-buffers of one rank's exchange region."""
+    """Float offsets of the sub-buffers of one rank's exchange region.
 
-    def __init__(self, n: int, c: int):
+    The gradient sub-buffers hold ``world`` slots of ``slot_rows`` rows (the
+    largest shard, rounded up to 4 rows so that every slot starts 16-byte
+    aligned): the training step's projection backward stores the rows of the
+    shard that rank q owns into slot ``rank`` of rank q's region. Their first
+    ``n`` rows double as a dense [n, cols] gradient for the paths that write one."""
+
+    def __init__(self, n: int, c: int, world: int = 1):
         self.n, self.c = n, c
         widths = {"transforms": 10, "sh": 3 * c, "opac": 1}
+        self.slot_rows = (-(-n // world) + 3) // 4 * 4
+        grad_rows = max(n, world * self.slot_rows)
         off = 0
         self.offsets = {}
         for kind in ("param", "grad"):
             for name, w in widths.items():
                 self.offsets[(kind, name)] = off
-                off = _up(off + n * w)
+                off = _up(off + (n if kind == "param" else grad_rows) * w)
         self.offsets["refine"] = off
         off = _up(off + n)
         self.offsets["flags"] = off
@@ -69,7 +77,7 @@ class PeerExchange:
             raise ValueError(f"the peer exchange supports at most {_lib.BSX_MAX_RANKS} ranks")
         self.device = device
         self.ctx = context(device)
-        self.layout = ExchangeLayout(n, c)
+        self.layout = ExchangeLayout(n, c, self.world)
         self.timeout_ns = int(timeout_s * 1e9)
         self.epoch = 0
         L = _lib.lib()
@@ -169,6 +177,7 @@ class PeerExchange:
             sp.d_v_raw_opac[q] = self._ptr(q, ("grad", "opac"))
         ex.refine_rows = self.layout.n
         ex.timeout_ns = self.timeout_ns
+        ex.grad_slot_rows = self.layout.slot_rows
         return ex, sp
 
     def close(self) -> None:

@@ -243,6 +243,8 @@ class SplatTrainer:
                 self.peer = PeerExchange(n, c, dev.index, self.pg)
                 self.peer.load(splats.transforms, splats.sh_coeffs, splats.raw_opacities)
                 splats.transforms, splats.sh_coeffs, splats.raw_opacities = self.peer.params
+                # dense gradients of this rank's view only with keep_gradients; otherwise
+                # these buffers hold the exchange slots the ranks push their rows into
                 self.grads = SplatGrads(*self.peer.grads, v_refine_weight=self.peer.refine)
                 self._dp = self.peer.train_structs()
             else:

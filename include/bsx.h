@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define BSX_ABI_VERSION 4
+#define BSX_ABI_VERSION 5
 /* Gradient lanes per splat written by the raster backward:
  * xy(2) conic(3) rgb(3) alpha refine depth. Reference:
  * crates/brush-render-bwd/src/kernels/rasterize_backwards.rs:40 */
@@ -272,6 +272,11 @@ typedef struct bsx_dp_exchange {
     uint32_t refine_rows;
     uint32_t epoch;                      /* 1, 2, 3, ... one per call, equal on every rank */
     uint64_t timeout_ns;                 /* bound on each wait for the other ranks (0: 5 s) */
+    uint32_t grad_slot_rows;             /* 0: d_grad[q] is rank q's dense gradient [rows, cols].
+                                          * > 0 (a multiple of 4, >= every shard's rows): d_grad[rank]
+                                          * holds world slots of this rank's shard, the gradient of
+                                          * rank s for shard row i at row s * grad_slot_rows + i
+                                          * (filled by the ranks themselves; see bsx_train_step_dp) */
 } bsx_dp_exchange;
 
 /* One kernel in place of "all-reduce the gradients, then bsx_adam_step": rank
@@ -351,8 +356,14 @@ BSX_API bsx_status bsx_train_step(bsx_trainer* tr, const bsx_camera* cam, uint32
                                   float* d_raw_opac, int32_t compute_refine_weight, float* d_loss,
                                   bsx_train_stats* stats);
 /* Data-parallel step: this rank renders its view from its own copy of the
- * splats, writes its gradients into sp->d_v_*[rank] and ex->d_refine[rank],
- * then bsx_dp_adam_step (gradient scale 1/world) updates every rank's copy.
+ * splats, writes its gradients and ex->d_refine[rank], then bsx_dp_adam_step
+ * (gradient scale 1/world) updates every rank's copy. With
+ * ex->grad_slot_rows > 0 the buffers sp->d_v_*[q] hold world * grad_slot_rows
+ * rows and the projection backward stores each gradient row straight into
+ * slot `rank` of the row's owner (peer stores overlapped with its compute),
+ * so the exchange reads only local memory; otherwise, and after
+ * bsx_trainer_keep_gradients(tr, 1), sp->d_v_*[rank] receives this rank's
+ * dense gradient and the exchange pulls the peers' rows.
  * The trainer numbers the exchange epochs itself (ex->epoch is ignored), so
  * every rank's trainer must take the same data-parallel steps on flag words
  * that no other exchange uses. */

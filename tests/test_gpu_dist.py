@@ -1,10 +1,14 @@
 """Data-parallel training step on 2 GPUs (skipped with fewer GPUs), and the
 peer-exchange kernel's single-GPU forms.
 
-Each rank trains its own view; after one step (the fused peer-memory exchange,
-NCCL reduce-scatter -> sharded fused Adam -> all-gather, or NCCL all-reduce ->
-fused Adam) every rank holds identical splats, equal to one single-GPU Adam
-step on the mean of the two views' gradients computed with the same library.
+Each rank trains its own view; after one step (the fused peer-memory exchange
+with the gradient rows pushed into their owners' slots, the same exchange
+pulling dense gradients (keep_gradients), NCCL reduce-scatter -> sharded fused
+Adam -> all-gather, or NCCL all-reduce -> fused Adam) every rank holds
+identical splats, equal to one single-GPU Adam step on the mean of the two
+views' gradients computed with the same library. The peer modes use an odd
+splat count, so the shards differ in size and a projection block straddles
+the owner boundary.
 """
 import datetime
 import multiprocessing as mp
@@ -27,10 +31,10 @@ def _port():
         return s.getsockname()[1]
 
 
-def _scene(dev):
+def _scene(dev, n=40000):
     from brush_b200.splats import clustered_scene, orbit_camera, random_gt
 
-    splats = clustered_scene(40000, 3, "cpu", seed=77).to(dev)
+    splats = clustered_scene(n, 3, "cpu", seed=77).to(dev)
     w, h = 320, 256
     cams = [orbit_camera(i, 4, 8.0, w, h) for i in range(4)]
     gts = [random_gt(h, w, 90 + i, "cpu").to(dev) for i in range(4)]
@@ -48,10 +52,11 @@ def _worker(rank, world, port, q, mode):
     torch.distributed.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
                                          timeout=datetime.timedelta(seconds=60))
     try:
-        splats, cams, size, gts = _scene(dev)
+        splats, cams, size, gts = _scene(dev, _n_of(mode))
         tr = bsx.SplatTrainer(bsx.TrainConfig(uniform_lr=1e-3), splats, process_group=torch.distributed.group.WORLD,
                               gather_stats=False, shard_optimizer=mode == "sharded_adam",
-                              exchange="peer" if mode == "peer" else "nccl")
+                              exchange="peer" if mode.startswith("peer") else "nccl",
+                              keep_gradients=mode == "peer_keep")
         v = view_for(0, rank, world, len(cams))
         tr.step(cams[v], size, gts[v], splats)
         torch.cuda.synchronize()
@@ -65,14 +70,18 @@ def _worker(rank, world, port, q, mode):
         torch.distributed.destroy_process_group()
 
 
-def _single_gpu_mean_of_views():
+def _n_of(mode):
+    return 40001 if mode.startswith("peer") else 40000
+
+
+def _single_gpu_mean_of_views(n):
     import brush_b200 as bsx
     from brush_b200.adam import AdamGroup, AdamScaled
     from brush_b200.dist import view_for
     from brush_b200.loss import ImageLossConfig
 
     dev = torch.device("cuda", 0)
-    splats, cams, size, gts = _scene(dev)
+    splats, cams, size, gts = _scene(dev, n)
     n, c = splats.num_splats, splats.sh_coeffs_per_splat
     acc = None
     for r in range(2):
@@ -90,7 +99,7 @@ def _single_gpu_mean_of_views():
     return splats.transforms.cpu().numpy(), splats.sh_coeffs.cpu().numpy(), splats.raw_opacities.cpu().numpy()
 
 
-@pytest.mark.parametrize("mode", ["peer", "sharded_adam", "allreduce"])
+@pytest.mark.parametrize("mode", ["peer", "peer_keep", "sharded_adam", "allreduce"])
 def test_two_gpu_step_matches_mean_of_views(cuda, mode):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
@@ -104,10 +113,10 @@ def test_two_gpu_step_matches_mean_of_views(cuda, mode):
     for p in procs:
         p.join(timeout=60)
     assert all(r[1] == "ok" for r in res), res
-    assert res[0][5] == (mode == "peer", mode == "sharded_adam")
+    assert res[0][5] == (mode.startswith("peer"), mode == "sharded_adam")
     for k in (2, 3, 4):
         np.testing.assert_array_equal(res[0][k], res[1][k])
-    ref = _single_gpu_mean_of_views()
+    ref = _single_gpu_mean_of_views(_n_of(mode))
     for k, r in zip((2, 3, 4), ref):
         # Adam's first step moves each element by ~lr; differences come only from
         # the order of float atomics in the raster backward.
