@@ -172,7 +172,7 @@ __global__ void __launch_bounds__(kBwdPixThreads, 8) raster_bwd_kernel(const Bwd
     __shared__ float4 s_a[kBwdPixThreads];  // x, y, c00, c01
     __shared__ float4 s_b[kBwdPixThreads];  // c11, opacity, max(r,0), max(g,0)
     __shared__ float2 s_c[kBwdPixThreads];  // max(b,0), ln(255 o) + margin
-    __shared__ uint32_t s_mask[kBwdPixThreads];  // bits 0-3 warps, 4-6 colour gates
+    __shared__ uint32_t s_mask[kBwdPixThreads];  // bits 0-7 warp row bands, 8-10 colour gates
     __shared__ uint32_t s_gid[kBwdPixThreads];
     __shared__ float s_grad[kBwdPixThreads][kGradLanes + 1];
 
@@ -183,7 +183,7 @@ __global__ void __launch_bounds__(kBwdPixThreads, 8) raster_bwd_kernel(const Bwd
     if (hi <= lo) return;
     const uint32_t ox = (tile % a.tbw) * kTile, oy = (tile / a.tbw) * kTile;
     const uint32_t lx = compact_bits_16(threadIdx.x), ly = compact_bits_16(threadIdx.x >> 1);
-    const uint32_t wbit = 1u << warp;
+    const uint32_t wshift = 2 * warp;  // this warp's two band bits in s_mask
     const uint32_t px = ox + lx;
     const float pcx = (float)px + 0.5f;
     const float margin = SMOOTH ? kMarginSmooth : kMarginHard;
@@ -202,7 +202,7 @@ __global__ void __launch_bounds__(kBwdPixThreads, 8) raster_bwd_kernel(const Bwd
             s_a[threadIdx.x] = ra;
             s_b[threadIdx.x] = make_float4(rb.x, rb.y, bsx_max(rb.z, 0.0f), bsx_max(rb.w, 0.0f));
             s_c[threadIdx.x] = make_float2(bsx_max(rc.x, 0.0f), rc.z + margin);
-            const uint32_t gates = (rb.z >= 0.0f ? 16u : 0u) | (rb.w >= 0.0f ? 32u : 0u) | (rc.x >= 0.0f ? 64u : 0u);
+            const uint32_t gates = (rb.z >= 0.0f ? 256u : 0u) | (rb.w >= 0.0f ? 512u : 0u) | (rc.x >= 0.0f ? 1024u : 0u);
             s_mask[threadIdx.x] = warp_visit_mask(ra.x, ra.y, ra.z, ra.w, rb.x, rc.z + margin, ox, oy) | gates;
             s_gid[threadIdx.x] = g;
 #pragma unroll
@@ -210,7 +210,8 @@ __global__ void __launch_bounds__(kBwdPixThreads, 8) raster_bwd_kernel(const Bwd
         }
         __syncthreads();
         for (uint32_t t = 0; t < n; ++t) {
-            if (!(s_mask[t] & wbit)) continue;                      // warp-uniform
+            const uint32_t bands = (s_mask[t] >> wshift) & 3u;       // warp-uniform
+            if (!bands) continue;
             if (__all_sync(0xffffffffu, PA.done && PB.done)) break;  // warp-uniform
             const float4 A = s_a[t];
             const float4 B = s_b[t];
@@ -221,10 +222,12 @@ __global__ void __launch_bounds__(kBwdPixThreads, 8) raster_bwd_kernel(const Bwd
             float gv[kGradLanes];
 #pragma unroll
             for (int k = 0; k < kGradLanes; ++k) gv[k] = 0.0f;
-            bool contrib = pixel_step<SMOOTH, REFINE>(PA, pcx, dx0, hxx, xy, A.x, A.y, A.z, A.w, B.x, B.y, Cc.y, B.z,
+            // a band the splat cannot reach has every sigma > thr: its pixel step is a no-op
+            bool contrib = (bands & 1u) && pixel_step<SMOOTH, REFINE>(PA, pcx, dx0, hxx, xy, A.x, A.y, A.z, A.w, B.x,
+                                                                      B.y, Cc.y, B.z, B.w, Cc.x, wf, hf, gv);
+            if (bands & 2u)
+                contrib |= pixel_step<SMOOTH, REFINE>(PB, pcx, dx0, hxx, xy, A.x, A.y, A.z, A.w, B.x, B.y, Cc.y, B.z,
                                                       B.w, Cc.x, wf, hf, gv);
-            contrib |= pixel_step<SMOOTH, REFINE>(PB, pcx, dx0, hxx, xy, A.x, A.y, A.z, A.w, B.x, B.y, Cc.y, B.z, B.w,
-                                                  Cc.x, wf, hf, gv);
             if (__any_sync(0xffffffffu, contrib)) {
                 const float tot = warp_sum10(gv, lane);
                 if (!(lane & 1) && sum_idx < kGradLanes) atomicAdd(&s_grad[t][sum_idx], tot);
@@ -234,8 +237,8 @@ __global__ void __launch_bounds__(kBwdPixThreads, 8) raster_bwd_kernel(const Bwd
         if (threadIdx.x < n) {
             const float* sgr = s_grad[threadIdx.x];
             const uint32_t gates = s_mask[threadIdx.x];
-            const float vr = (gates & 16u) ? sgr[5] : 0.0f, vg = (gates & 32u) ? sgr[6] : 0.0f,
-                        vb = (gates & 64u) ? sgr[7] : 0.0f;
+            const float vr = (gates & 256u) ? sgr[5] : 0.0f, vg = (gates & 512u) ? sgr[6] : 0.0f,
+                        vb = (gates & 1024u) ? sgr[7] : 0.0f;
             bool any = false;
 #pragma unroll
             for (int k = 0; k < kGradLanes; ++k) any = any || sgr[k] != 0.0f;

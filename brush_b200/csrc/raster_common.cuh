@@ -64,9 +64,10 @@ __device__ __forceinline__ float rect_min_sigma(float ax, float bx, float ay, fl
     return fminf(q1, q2);
 }
 
-// Bit w set: warp w of the tile block at (ox, oy) covers a pixel centre whose
-// sigma can be <= thr. The test is the exact minimum of sigma over each of the
-// warp's two 8x4 pixel-centre rectangles, less a rounding allowance of 1e-5 of
+// Bit 2w + b set: row band b of warp w of the tile block at (ox, oy) (band 0
+// holds the warp's first pixels, band 1 its pixels 8 rows lower) has a pixel
+// centre whose sigma can be <= thr. The test is the exact minimum of sigma over
+// each of the warp's two 8x4 pixel-centre rectangles, less a rounding allowance of 1e-5 of
 // the largest term magnitude over the tile (the float evaluation of sigma at a
 // pixel and of the rectangle minimum each err by well under 1e-6 of it), so a
 // cleared bit means no pixel of that warp passes the per-pixel pre-filter
@@ -75,7 +76,7 @@ __device__ __forceinline__ float rect_min_sigma(float ax, float bx, float ay, fl
 __device__ __forceinline__ uint32_t warp_visit_mask(float sx, float sy, float c00, float c01, float c11, float thr,
                                                     uint32_t ox, uint32_t oy) {
     const float det = c00 * c11 - c01 * c01;
-    if (!(c00 > 0.0f && c11 > 0.0f && det > 0.0f)) return 0xfu;
+    if (!(c00 > 0.0f && c11 > 0.0f && det > 0.0f)) return 0xffu;
     const float r01 = __fdividef(c01, c11), s01 = __fdividef(c01, c00);
     const float x0 = (float)ox + 0.5f - sx, y0 = (float)oy + 0.5f - sy;
     const float dxm = fmaxf(fabsf(x0), fabsf(x0 + 15.0f)), dym = fmaxf(fabsf(y0), fabsf(y0 + 15.0f));
@@ -89,8 +90,8 @@ __device__ __forceinline__ uint32_t warp_visit_mask(float sx, float sy, float c0
         for (int band = 0; band < 2; ++band) {
             const float ay = y0 + (float)(4 * (w & 1) + 8 * band), by = ay + 3.0f;
             const float q = rect_min_sigma(ax, bx, ay, by, c00, c01, c11, r01, s01);
-            // NaN compares false: the warp is kept
-            if (!(q > bound)) mask |= 1u << w;
+            // NaN compares false: the band is kept
+            if (!(q > bound)) mask |= 1u << (2 * w + band);
         }
     }
     return mask;

@@ -8,9 +8,11 @@
 //   accept iff sigma >= 0 and alpha >= 1/255; stop before accumulating once
 //   T*(1-alpha) <= 1e-4.
 // B200 specifics: the block-wide early-out is a __syncthreads_count vote;
-// while a batch is staged, each splat gets a 4-bit mask of the warps whose
-// pixels it can reach (exact minimum of sigma over each warp's footprint), so
-// a warp skips splats none of its pixels can accept; pairs whose sigma
+// while a batch is staged, each splat gets a mask of the warp row bands whose
+// pixels it can reach (exact minimum of sigma over each band's 8x4 footprint),
+// so a warp skips splats none of its pixels can accept (a per-pixel band test
+// measured no faster here: the sigma test already rejects those pixels
+// cheaply); pairs whose sigma
 // exceeds ln(255*o) + margin (where alpha < 1/255 is certain) skip the
 // exponential; colours are clamped once per splat while staging. sigma is
 // evaluated with fused products (bsx_raster_sigma), e^-sigma by the bounded-
@@ -53,7 +55,7 @@ __global__ void __launch_bounds__(kFwdThreads) raster_fwd_kernel(const FwdArgs a
     const uint32_t tile = blockIdx.x;
     const uint32_t tx = tile % a.tbw, ty = tile / a.tbw;
     const uint32_t lx = compact_bits_16(threadIdx.x), ly = compact_bits_16(threadIdx.x >> 1);
-    const uint32_t wbit = 1u << (threadIdx.x >> 5);
+    const uint32_t wshift = 2 * (threadIdx.x >> 5);  // this warp's two band bits in s_mask
     const uint32_t px = tx * kTile + lx, pyA = ty * kTile + ly, pyB = pyA + 8;
     const bool inA = px < a.w && pyA < a.h, inB = px < a.w && pyB < a.h;
     const float pcx = (float)px + 0.5f, pcyA = (float)pyA + 0.5f, pcyB = (float)pyB + 0.5f;
@@ -87,7 +89,8 @@ __global__ void __launch_bounds__(kFwdThreads) raster_fwd_kernel(const FwdArgs a
         }
         __syncthreads();
         for (uint32_t t = 0; t < n && !(doneA && doneB); ++t) {
-            if (!(s_mask[t] & wbit)) continue;
+            const uint32_t bands = (s_mask[t] >> wshift) & 3u;  // warp-uniform
+            if (!bands) continue;
             const float4 A = s_a[t];
             const float hc11 = s_b[t].x;
             const float thr = s_c[t].y;
