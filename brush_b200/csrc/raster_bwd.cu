@@ -9,8 +9,9 @@
 // forward bit-for-bit), carrying the residual colour C - T_final*bg - (front
 // contributions) in registers as the reference does. Per splat, a warp that
 // none of the splat's acceptable pixels reach (the forward's exact footprint
-// test, raster_common.cuh) skips it uniformly; otherwise each lane forms its
-// pixels' contribution to the splat's 10
+// test per row band, raster_common.cuh) skips it uniformly, and a warp skips
+// the pixel step of a band the splat cannot reach; otherwise each lane forms
+// its pixels' contribution to the splat's 10
 // gradient lanes, the warp sums them with a 10-value butterfly (12 shuffles),
 // the sums are accumulated per splat in shared memory across the tile's 4
 // warps, and each (splat, tile) leaves with three 16-byte vector atomics
