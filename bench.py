@@ -132,6 +132,7 @@ def kernel_bytes(name, N, V, M, Mp, P, T, C, W=1, fused_adam=False):
         "scan_kernel": 12 * V,
         "emit_kernel": V * (4 + 48 + 8) + 8 * M,
         "tile_offsets_kernel": 8 * M + 8 * T,
+        "tile_order_kernel": 16 * T + 4 * T,  # ranges read twice, order written
         "raster_fwd_kernel": 52 * Mp + 16 * P + 8 * T + 4 * V,
         "loss_fused_kernel": 36 * P,
         "loss_mean_kernel": 0,

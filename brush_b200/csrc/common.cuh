@@ -151,7 +151,7 @@ struct bsx_ctx {
     // workspace
     bsx::DevBuf projected, counts, depth_keys, vis_gid, depth_order, cum, isect_tile, isect_gid, tile_offsets,
         image, image_packed, visible, max_radius, sort_tmp_k, sort_tmp_v, sort_hist, sort_lookback, scan_status,
-        scalars, grad, loss_partials, sort_keys_b, sort_vals_b;
+        scalars, grad, loss_partials, sort_keys_b, sort_vals_b, tile_order;
     bsx_fwd_state fwd;
     // optional per-launch timing (bsx_profile_*)
     int profiling = 0;
@@ -190,6 +190,8 @@ bsx_status scan_inclusive_u32(bsx_ctx* ctx, const uint32_t* d_in, const uint32_t
 bsx_status radix_sort_pairs(bsx_ctx* ctx, const uint32_t* d_keys, const uint32_t* d_vals, uint32_t n,
                             uint32_t bits, uint32_t* d_keys_out, uint32_t* d_vals_out);
 bsx_status tile_offsets(bsx_ctx* ctx, const uint32_t* d_ids, uint32_t n, uint32_t num_tiles, uint32_t* d_off);
+// Launch order of the tiles for the rasterizers (descending intersection count).
+bsx_status tile_order(bsx_ctx* ctx, const uint32_t* d_off, uint32_t num_tiles, uint32_t* d_order);
 
 // Lookback state for the scan family: per-tile status words plus a ticket.
 size_t scan_status_words(uint32_t n_tiles);

@@ -92,7 +92,58 @@ __global__ void __launch_bounds__(256) tile_offsets_kernel(const uint32_t* __res
     }
 }
 
+// Launch order of the tiles for the rasterizers: by descending intersection
+// count, so the longest tiles start first and the short ones fill the tail
+// (in tile order, clustered scenes leave long tiles running alone at the end).
+// A counting sort into 256 buckets of count >> shift (shift fits the largest
+// count into 8 bits); the order within a bucket is arbitrary, which no output
+// depends on (tiles are independent). One block.
+constexpr int kOrderThreads = 1024;
+constexpr int kOrderBuckets = 256;
+
+__global__ void __launch_bounds__(kOrderThreads) tile_order_kernel(const uint32_t* __restrict__ off, uint32_t num_tiles,
+                                                                   uint32_t* __restrict__ order) {
+    __shared__ uint32_t s_cur[kOrderBuckets];
+    __shared__ uint32_t s_max;
+    if (threadIdx.x < kOrderBuckets) s_cur[threadIdx.x] = 0;
+    if (threadIdx.x == 0) s_max = 0;
+    __syncthreads();
+    auto count = [&](uint32_t t) {
+        const uint32_t b = __ldg(off + 2 * t), e = __ldg(off + 2 * t + 1);
+        return e > b ? e - b : 0u;
+    };
+    uint32_t m = 0;
+    for (uint32_t t = threadIdx.x; t < num_tiles; t += kOrderThreads) m = max(m, count(t));
+    for (int o = 16; o; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) atomicMax(&s_max, m);
+    __syncthreads();
+    const uint32_t shift = s_max >= (uint32_t)kOrderBuckets ? 32 - __clz(s_max) - 8 : 0;
+    auto bucket = [&](uint32_t t) { return (uint32_t)(kOrderBuckets - 1) - (count(t) >> shift); };
+    for (uint32_t t = threadIdx.x; t < num_tiles; t += kOrderThreads) atomicAdd(&s_cur[bucket(t)], 1u);
+    __syncthreads();
+    // exclusive prefix over the buckets (Hillis-Steele on the first 256 threads)
+    uint32_t v = threadIdx.x < kOrderBuckets ? s_cur[threadIdx.x] : 0u;
+    const uint32_t own = v;
+    for (int d = 1; d < kOrderBuckets; d <<= 1) {
+        const uint32_t add = (threadIdx.x < kOrderBuckets && (int)threadIdx.x >= d) ? s_cur[threadIdx.x - d] : 0u;
+        __syncthreads();
+        v += add;
+        if (threadIdx.x < kOrderBuckets) s_cur[threadIdx.x] = v;
+        __syncthreads();
+    }
+    if (threadIdx.x < kOrderBuckets) s_cur[threadIdx.x] = v - own;
+    __syncthreads();
+    for (uint32_t t = threadIdx.x; t < num_tiles; t += kOrderThreads) order[atomicAdd(&s_cur[bucket(t)], 1u)] = t;
+}
+
 }  // namespace
+
+bsx_status tile_order(bsx_ctx* ctx, const uint32_t* d_off, uint32_t num_tiles, uint32_t* d_order) {
+    if (num_tiles == 0) return BSX_OK;
+    prof_begin(ctx);
+    tile_order_kernel<<<1, kOrderThreads, 0, ctx->stream>>>(d_off, num_tiles, d_order);
+    return post_launch(ctx, "tile_order_kernel");
+}
 
 bsx_status launch_emit(bsx_ctx* ctx, const float* projected, const uint32_t* depth_order, const uint32_t* cum,
                        uint32_t num_visible, uint32_t tbw, uint32_t tbh, uint32_t* tile_out, uint32_t* gid_out,

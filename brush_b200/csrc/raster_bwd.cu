@@ -35,6 +35,7 @@ struct BwdArgs {
     const float* image;     // [H,W,4]
     const float* v_output;  // [H,W,4]
     float* v_grad;          // [N,12]
+    const uint32_t* order;  // launch order of the tiles (block b replays tile order[b])
     uint32_t tbw, num_tiles, w, h;
     float bg_r, bg_g, bg_b;
 };
@@ -179,7 +180,7 @@ __global__ void __launch_bounds__(kBwdPixThreads, 8) raster_bwd_kernel(const Bwd
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int sum_idx = warp_sum10_index(lane);
-    const uint32_t tile = blockIdx.x;
+    const uint32_t tile = __ldg(a.order + blockIdx.x);
     const uint32_t lo = __ldg(a.tile_offsets + tile * 2), hi = __ldg(a.tile_offsets + tile * 2 + 1);
     if (hi <= lo) return;
     const uint32_t ox = (tile % a.tbw) * kTile, oy = (tile / a.tbw) * kTile;
@@ -273,6 +274,11 @@ bsx_status launch_raster_bwd(bsx_ctx* ctx, const uint32_t* isect_gid, const uint
     a.bg_g = bg[1];
     a.bg_b = bg[2];
     const uint32_t blocks = a.num_tiles;
+    // launch order from the tile ranges as the forward shortened them
+    bsx_status s = ensure(ctx, ctx->tile_order, (size_t)blocks * 4);
+    if (s == BSX_OK) s = tile_order(ctx, tile_offsets, blocks, ctx->tile_order.as<uint32_t>());
+    if (s != BSX_OK) return s;
+    a.order = ctx->tile_order.as<uint32_t>();
     prof_begin(ctx);
     if (smooth) {
         if (refine) raster_bwd_kernel<true, true><<<blocks, kBwdPixThreads, 0, ctx->stream>>>(a);

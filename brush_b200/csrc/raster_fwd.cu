@@ -34,6 +34,7 @@ struct FwdArgs {
     float* image;            // [H,W,4] when bwd_info
     uint32_t* image_packed;  // [H,W] otherwise
     float* visible;          // [N] when bwd_info
+    const uint32_t* order;   // launch order of the tiles (block b renders tile order[b])
     uint32_t tbw, w, h;
     float bg_r, bg_g, bg_b;
 };
@@ -52,7 +53,7 @@ __global__ void __launch_bounds__(kFwdThreads) raster_fwd_kernel(const FwdArgs a
     __shared__ int s_used[BWD ? kFwdThreads : 1];
     __shared__ uint32_t s_max_useful;
 
-    const uint32_t tile = blockIdx.x;
+    const uint32_t tile = __ldg(a.order + blockIdx.x);
     const uint32_t tx = tile % a.tbw, ty = tile / a.tbw;
     const uint32_t lx = compact_bits_16(threadIdx.x), ly = compact_bits_16(threadIdx.x >> 1);
     const uint32_t wshift = 2 * (threadIdx.x >> 5);  // this warp's two band bits in s_mask
@@ -185,6 +186,10 @@ bsx_status launch_raster_fwd(bsx_ctx* ctx, const uint32_t* isect_gid, uint32_t* 
     a.bg_g = bg[1];
     a.bg_b = bg[2];
     const uint32_t tiles = u.tile_bw * u.tile_bh;
+    bsx_status s = ensure(ctx, ctx->tile_order, (size_t)tiles * 4);
+    if (s == BSX_OK) s = tile_order(ctx, tile_offsets, tiles, ctx->tile_order.as<uint32_t>());
+    if (s != BSX_OK) return s;
+    a.order = ctx->tile_order.as<uint32_t>();
     prof_begin(ctx);
     if (!bwd_info) raster_fwd_kernel<false, false><<<tiles, kFwdThreads, 0, ctx->stream>>>(a);
     else if (!smooth) raster_fwd_kernel<true, false><<<tiles, kFwdThreads, 0, ctx->stream>>>(a);
