@@ -97,9 +97,12 @@ __global__ void __launch_bounds__(256) tile_offsets_kernel(const uint32_t* __res
 // (in tile order, clustered scenes leave long tiles running alone at the end).
 // A counting sort into 256 buckets of count >> shift (shift fits the largest
 // count into 8 bits); the order within a bucket is arbitrary, which no output
-// depends on (tiles are independent). One block.
+// depends on (tiles are independent). One block; each pass over the tile
+// ranges loads kOrderPer tiles per thread at once (one memory round trip per
+// 8192 tiles instead of one per tile and thread).
 constexpr int kOrderThreads = 1024;
 constexpr int kOrderBuckets = 256;
+constexpr int kOrderPer = 8;
 
 __global__ void __launch_bounds__(kOrderThreads) tile_order_kernel(const uint32_t* __restrict__ off, uint32_t num_tiles,
                                                                    uint32_t* __restrict__ order) {
@@ -108,18 +111,30 @@ __global__ void __launch_bounds__(kOrderThreads) tile_order_kernel(const uint32_
     if (threadIdx.x < kOrderBuckets) s_cur[threadIdx.x] = 0;
     if (threadIdx.x == 0) s_max = 0;
     __syncthreads();
-    auto count = [&](uint32_t t) {
-        const uint32_t b = __ldg(off + 2 * t), e = __ldg(off + 2 * t + 1);
-        return e > b ? e - b : 0u;
+    // fn(t, count) for every tile, kOrderPer independent loads per thread per round
+    auto for_tiles = [&](auto fn) {
+        for (uint32_t base = 0; base < num_tiles; base += kOrderThreads * kOrderPer) {
+            uint2 r[kOrderPer];
+#pragma unroll
+            for (int k = 0; k < kOrderPer; ++k) {
+                const uint32_t t = base + k * kOrderThreads + threadIdx.x;
+                r[k] = t < num_tiles ? __ldg(reinterpret_cast<const uint2*>(off) + t) : make_uint2(0u, 0u);
+            }
+#pragma unroll
+            for (int k = 0; k < kOrderPer; ++k) {
+                const uint32_t t = base + k * kOrderThreads + threadIdx.x;
+                if (t < num_tiles) fn(t, r[k].y > r[k].x ? r[k].y - r[k].x : 0u);
+            }
+        }
     };
     uint32_t m = 0;
-    for (uint32_t t = threadIdx.x; t < num_tiles; t += kOrderThreads) m = max(m, count(t));
+    for_tiles([&](uint32_t, uint32_t c) { m = max(m, c); });
     for (int o = 16; o; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
     if ((threadIdx.x & 31) == 0) atomicMax(&s_max, m);
     __syncthreads();
     const uint32_t shift = s_max >= (uint32_t)kOrderBuckets ? 32 - __clz(s_max) - 8 : 0;
-    auto bucket = [&](uint32_t t) { return (uint32_t)(kOrderBuckets - 1) - (count(t) >> shift); };
-    for (uint32_t t = threadIdx.x; t < num_tiles; t += kOrderThreads) atomicAdd(&s_cur[bucket(t)], 1u);
+    auto bucket = [&](uint32_t c) { return (uint32_t)(kOrderBuckets - 1) - (c >> shift); };
+    for_tiles([&](uint32_t, uint32_t c) { atomicAdd(&s_cur[bucket(c)], 1u); });
     __syncthreads();
     // exclusive prefix over the buckets (Hillis-Steele on the first 256 threads)
     uint32_t v = threadIdx.x < kOrderBuckets ? s_cur[threadIdx.x] : 0u;
@@ -133,7 +148,7 @@ __global__ void __launch_bounds__(kOrderThreads) tile_order_kernel(const uint32_
     }
     if (threadIdx.x < kOrderBuckets) s_cur[threadIdx.x] = v - own;
     __syncthreads();
-    for (uint32_t t = threadIdx.x; t < num_tiles; t += kOrderThreads) order[atomicAdd(&s_cur[bucket(t)], 1u)] = t;
+    for_tiles([&](uint32_t t, uint32_t c) { order[atomicAdd(&s_cur[bucket(c)], 1u)] = t; });
 }
 
 }  // namespace

@@ -10,7 +10,7 @@ Differences of representation (same meaning):
 from __future__ import annotations
 
 import ctypes as C
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 
 import torch
 
@@ -51,7 +51,16 @@ class RenderOutput:
     tile_counts: torch.Tensor             # [N] int32
     cum_counts: torch.Tensor              # [V] int32 inclusive scan of counts in depth order
     project_uniforms: _lib.ProjectUniforms
-    global_from_compact_gid: torch.Tensor  # identity [N] (global-id indexing)
+    num_splats: int = 0
+    _gid: torch.Tensor | None = field(default=None, repr=False)
+
+    @property
+    def global_from_compact_gid(self) -> torch.Tensor:
+        """Identity [N] int32 (global-id indexing), built on first access so that a render
+        loop does not allocate and fill N ids per frame."""
+        if self._gid is None:
+            self._gid = torch.arange(self.num_splats, device=self.projected_splats.device, dtype=torch.int32)
+        return self._gid
 
 
 def _check_splats(transforms, sh_coeffs, raw_opacities):
@@ -99,7 +108,7 @@ def render(camera: Camera, img_size: tuple, transforms: torch.Tensor, sh_coeffs:
     aux = RenderAux(
         num_visible=V,
         num_intersections=M,
-        visible=device_view(out.d_visible, (n,), f32, dev) if bwd else torch.zeros(1, device=transforms.device),
+        visible=device_view(out.d_visible, (n,), f32, dev) if bwd else torch.empty(0, device=transforms.device),
         max_radius=device_view(out.d_max_radius, (n,), f32, dev),
         tile_offsets=device_view(out.d_tile_offsets, (out.tile_bh, out.tile_bw, 2), i32, dev),
         img_size=(w, h),
@@ -114,7 +123,7 @@ def render(camera: Camera, img_size: tuple, transforms: torch.Tensor, sh_coeffs:
         tile_counts=device_view(out.d_tile_counts, (n,), i32, dev),
         cum_counts=device_view(out.d_cum_counts, (V,), i32, dev),
         project_uniforms=out.uniforms,
-        global_from_compact_gid=torch.arange(n, device=transforms.device, dtype=i32),
+        num_splats=n,
     )
 
 

@@ -80,6 +80,31 @@ def test_forward_packed_pass(cuda, orc):
     _assert_pipeline_equal(r, out, bwd=False)
 
 
+@pytest.mark.parametrize("raster_pass", [0, 1])
+def test_many_tiles_bit_exact(cuda, orc, raster_pass):
+    """4096x2304 (36 864 tiles): the rasterizers launch tiles in an order computed from
+    their intersection counts, beyond the counts that order keeps in shared memory; every
+    tile is rendered exactly once (forward bit-exact) and replayed once (backward)."""
+    import brush_b200 as bsx
+    from brush_b200.splats import clustered_scene, orbit_camera
+
+    from test_gpu_backward import _rel
+
+    splats = clustered_scene(30000, 1, "cpu", seed=23)
+    size = (4096, 2304)
+    cam = orbit_camera(3, 5, 8.0, *size)
+    r, out = _render_both(orc, splats, cam, size, raster_pass=raster_pass)
+    assert r.num_intersections > 0
+    _assert_pipeline_equal(r, out, bwd=raster_pass != 0)
+    if raster_pass:
+        rng = np.random.default_rng(4)
+        v_output = rng.normal(0, 1e-3, (size[1], size[0], 4)).astype(np.float32)
+        vc_gpu = bsx.rasterize_bwd(torch.from_numpy(v_output).cuda(), False).cpu().numpy()[:, :11]
+        vc_orc = r.rasterize_bwd(v_output, False)
+        for lanes in [(0, 1), (2, 3, 4), (5, 6, 7), (8,)]:
+            assert _rel(vc_gpu[:, lanes], vc_orc[:, lanes]) <= 1e-3, lanes
+
+
 def test_mip_and_smooth_cutoff(cuda, orc):
     from brush_b200.splats import clustered_scene, orbit_camera
 
