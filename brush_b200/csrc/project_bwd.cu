@@ -8,11 +8,12 @@
 // One thread per splat over all N rows; rows without gradient are written as
 // zeros, so no separate zero-fill of the dense outputs is needed.
 //
-// Memory: a block owns R consecutive splats. Their transform, SH and gradient
-// rows (contiguous in global memory) are copied into shared memory with
-// coalesced loads, each thread works on its own rows there (odd row strides
-// keep the per-thread accesses free of bank conflicts), and the gradient rows
-// go back to global memory with coalesced stores.
+// Memory: a block owns R consecutive splats. Their transform and SH rows
+// (contiguous in global memory) are copied into shared memory with coalesced
+// loads, each thread works on its own rows there (odd row strides keep the
+// per-thread accesses free of bank conflicts) with its raster-gradient row in
+// registers, and the gradient rows go back to global memory with coalesced
+// stores.
 #include "sh.cuh"
 
 namespace bsx {
@@ -181,7 +182,6 @@ struct PbShape {
     static constexpr int R = DEG >= 4 ? 64 : 128;  // splats per block
     static constexpr int TS = 11;                  // transform row stride (odd)
     static constexpr int SS = C3 | 1;              // SH row stride (odd)
-    static constexpr int GS = 13;                  // gradient row stride (odd)
 };
 
 // AdamScaled element update, the expressions of adam.cu's adam_tile, in three
@@ -283,7 +283,6 @@ __global__ void __launch_bounds__(PbShape<DEG>::R, 6) project_bwd_kernel(const P
     constexpr int C3 = S::C3;
     __shared__ float s_t[S::R * S::TS];
     __shared__ float s_sh[S::R * S::SS];
-    __shared__ float s_g[S::R * S::GS];
     __shared__ float s_op[FUSE ? S::R : 1];    // opacity gradients (fused Adam)
     __shared__ float s_den[FUSE ? S::R : 1];   // SH Adam denominator per row (fused Adam)
     // With the gradient push, block b takes row block (b % world) K + b / world
@@ -301,15 +300,23 @@ __global__ void __launch_bounds__(PbShape<DEG>::R, 6) project_bwd_kernel(const P
     // the row's scalar inputs, issued with the staged rows rather than after them
     const float raw_op = r < rows ? __ldg(a.raw_opac + g0 + r) : 0.0f;
     const float v_sh_old = (FUSE && r < rows && !a.adam.first) ? a.adam.v_sh[g0 + r] : 0.0f;
+    // the row's raster gradients: three 16-byte words per thread straight into
+    // registers (a warp reads 1.5 KB contiguous; no shared-memory staging)
+    float rg[kGradStride];
+    {
+        const float4* gp = reinterpret_cast<const float4*>(a.v_grad + (size_t)(g0 + min(r, rows - 1)) * kGradStride);
+        const float4 q0 = __ldg(gp), q1 = __ldg(gp + 1), q2 = __ldg(gp + 2);
+        const float w[kGradStride] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w, q2.x, q2.y, q2.z, q2.w};
+#pragma unroll
+        for (int k = 0; k < kGradStride; ++k) rg[k] = w[k];
+    }
     stage_in<2>(s_t, a.transforms + (size_t)g0 * 10, rows, 10, S::TS);
-    stage_in<2>(s_g, a.v_grad + (size_t)g0 * kGradStride, rows, kGradStride, S::GS);
     stage_in<(S::C3 >= 48 ? 6 : 2)>(s_sh, a.sh + (size_t)g0 * C3, rows, C3, S::SS);
     __syncthreads();
     if (r < rows) {
         const uint32_t g = g0 + r;
         float* t = s_t + r * S::TS;   // transform in, transform gradient out
         float* shr = s_sh + r * S::SS;  // SH in, SH gradient out
-        const float* rg = s_g + r * S::GS;
         bool any = false;
 #pragma unroll
         for (int k = 0; k < BSX_COMPACT_GRAD_LANES; ++k) any = any || rg[k] != 0.0f;
