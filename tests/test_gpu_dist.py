@@ -1,14 +1,14 @@
-"""Data-parallel training step on 2 GPUs (skipped with fewer GPUs), and the
+"""Data-parallel training step on 2 and 4 GPUs (skipped with fewer GPUs), and the
 peer-exchange kernel's single-GPU forms.
 
 Each rank trains its own view; after one step (the fused peer-memory exchange
 with the gradient rows pushed into their owners' slots, the same exchange
 pulling dense gradients (keep_gradients), NCCL reduce-scatter -> sharded fused
 Adam -> all-gather, or NCCL all-reduce -> fused Adam) every rank holds
-identical splats, equal to one single-GPU Adam step on the mean of the two
+identical splats, equal to one single-GPU Adam step on the mean of the ranks'
 views' gradients computed with the same library. The peer modes use an odd
-splat count, so the shards differ in size and a projection block straddles
-the owner boundary.
+splat count, so the shards differ in size and projection blocks straddle owner
+boundaries; on 4 GPUs the gradient push is checked the same way.
 """
 import datetime
 import multiprocessing as mp
@@ -74,7 +74,7 @@ def _n_of(mode):
     return 40001 if mode.startswith("peer") else 40000
 
 
-def _single_gpu_mean_of_views(n):
+def _single_gpu_mean_of_views(n, world=2):
     import brush_b200 as bsx
     from brush_b200.adam import AdamGroup, AdamScaled
     from brush_b200.dist import view_for
@@ -84,8 +84,8 @@ def _single_gpu_mean_of_views(n):
     splats, cams, size, gts = _scene(dev, n)
     n, c = splats.num_splats, splats.sh_coeffs_per_splat
     acc = None
-    for r in range(2):
-        v = view_for(0, r, 2, len(cams))
+    for r in range(world):
+        v = view_for(0, r, world, len(cams))
         out = bsx.render(cams[v], size, splats.transforms, splats.sh_coeffs, splats.raw_opacities)
         _, vo = bsx.image_loss_fused(out.out_img, gts[v], ImageLossConfig())
         vc = bsx.rasterize_bwd(vo, False)
@@ -95,28 +95,32 @@ def _single_gpu_mean_of_views(n):
     groups = [AdamGroup(splats.transforms, acc[0], 1e-3), AdamGroup(splats.sh_coeffs.view(n, 3 * c), acc[1], 1e-3,
                                                                      reduce_moment_2=True),
               AdamGroup(splats.raw_opacities.view(n, 1), acc[2], 1e-3)]
-    AdamScaled().step(groups, grad_scale=0.5)
+    AdamScaled().step(groups, grad_scale=1.0 / world)
     return splats.transforms.cpu().numpy(), splats.sh_coeffs.cpu().numpy(), splats.raw_opacities.cpu().numpy()
 
 
+@pytest.mark.parametrize("world", [2, 4])
 @pytest.mark.parametrize("mode", ["peer", "peer_keep", "sharded_adam", "allreduce"])
-def test_two_gpu_step_matches_mean_of_views(cuda, mode):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+def test_multi_gpu_step_matches_mean_of_views(cuda, mode, world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    if world > 2 and mode != "peer":
+        pytest.skip("the other exchanges are checked on 2 GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, mode)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, mode)) for r in range(world)]
     for p in procs:
         p.start()
-    res = sorted([q.get(timeout=300) for _ in range(2)], key=lambda r: r[0])
+    res = sorted([q.get(timeout=300) for _ in range(world)], key=lambda r: r[0])
     for p in procs:
         p.join(timeout=60)
     assert all(r[1] == "ok" for r in res), res
     assert res[0][5] == (mode.startswith("peer"), mode == "sharded_adam")
-    for k in (2, 3, 4):
-        np.testing.assert_array_equal(res[0][k], res[1][k])
-    ref = _single_gpu_mean_of_views(_n_of(mode))
+    for r in res[1:]:
+        for k in (2, 3, 4):
+            np.testing.assert_array_equal(res[0][k], r[k])
+    ref = _single_gpu_mean_of_views(_n_of(mode), world)
     for k, r in zip((2, 3, 4), ref):
         # Adam's first step moves each element by ~lr; differences come only from
         # the order of float atomics in the raster backward.
