@@ -351,8 +351,9 @@ __global__ void __launch_bounds__(256) loss_bwd_kernel(const __grid_constant__ L
 // in and out. The larger tile cuts the halo recomputation of the 16x16
 // operator form (SSIM evaluated on 42x42 = 1.7x the outputs instead of 26x26 =
 // 2.6x). Each blur pass runs as a register sliding window: a thread loads a
-// run of 14 (or 12) samples once and produces 4 (or 2) neighbouring outputs,
-// about a third of the shared-memory loads of one-output-per-thread. Planes
+// run of 15, 14 or 12 samples once and produces 5 (first pass: 52 rows x 9
+// runs fill one round of the 512 threads), 4 or 2 neighbouring outputs, about
+// a third of the shared-memory loads of one-output-per-thread. Planes
 // have odd pitches so that lanes walking down a column (horizontal passes,
 // one row per lane) and lanes walking along a row (vertical passes, one
 // column per lane) both hit distinct banks. Tap and summation order per output
@@ -365,7 +366,8 @@ constexpr int kPX = kF1 + 1;               // 53: pitch of the staged planes
 constexpr int kPH = kF2 + 1;               // 43: pitch of the moment / partial planes
 constexpr int kPQ = kFT + 1;               // 33: pitch of the second horizontal blur
 constexpr int kFusedThreads = 512;
-constexpr int kSeg = 4;                    // outputs per thread in passes 1-3
+constexpr int kSeg = 4;                    // outputs per thread in passes 2-3
+constexpr int kSeg1 = 5;                   // outputs per thread in pass 1: 52 rows x 9 runs fill one round
 constexpr int kSeg4 = 2;                   // outputs per thread in pass 4 (32 x 16 threads)
 static_assert(kFT * kFT == kSeg4 * kFusedThreads, "pass 4 covers the tile once");
 
@@ -450,20 +452,22 @@ __global__ void __launch_bounds__(kFusedThreads) loss_fused_kernel(const __grid_
                 S.y[ly * kPX + lx] = ge;
             }
             __syncthreads();
-            // pass 1: horizontal moment blur, 52 rows x 42 output columns (one row per lane)
-            for (int i = threadIdx.x; i < kF1 * 11; i += kFusedThreads) {
+            // pass 1: horizontal moment blur, 52 rows x 42 output columns (one row
+            // per lane, runs of kSeg1 outputs: 468 runs, one round of the block)
+            constexpr int kRuns1 = (kF2 + kSeg1 - 1) / kSeg1;
+            static_assert(kF1 * kRuns1 <= kFusedThreads, "pass 1 fits one round");
+            for (int i = threadIdx.x; i < kF1 * kRuns1; i += kFusedThreads) {
                 const int seg = i / kF1, r = i - seg * kF1;
-                const int c0 = seg * kSeg;
-                float xv[kSeg + 10], yv[kSeg + 10];
+                const int c0 = seg * kSeg1;
+                float xv[kSeg1 + 10], yv[kSeg1 + 10];
 #pragma unroll
-                for (int k = 0; k < kSeg + 10; ++k) {
+                for (int k = 0; k < kSeg1 + 10; ++k) {
                     const bool ok = c0 + k < kF1;
                     xv[k] = ok ? S.x[r * kPX + c0 + k] : 0.0f;
                     yv[k] = ok ? S.y[r * kPX + c0 + k] : 0.0f;
                 }
-                float m[5][kSeg];
 #pragma unroll
-                for (int j = 0; j < kSeg; ++j) {
+                for (int j = 0; j < kSeg1; ++j) {
                     float sx = 0.f, sx2 = 0.f, sy = 0.f, sy2 = 0.f, sxy = 0.f;
 #pragma unroll
                     for (int d = 1; d < 6; ++d) {
@@ -476,17 +480,15 @@ __global__ void __launch_bounds__(kFusedThreads) loss_fused_kernel(const __grid_
                         sxy = __fmaf_rn(__fmaf_rn(xl, yl, xr * yr), wd, sxy);
                     }
                     const float xc = xv[j + 5], yc = yv[j + 5], wc = w[5];
-                    m[0][j] = __fmaf_rn(xc, wc, sx);
-                    m[1][j] = __fmaf_rn(xc * xc, wc, sx2);
-                    m[2][j] = __fmaf_rn(yc, wc, sy);
-                    m[3][j] = __fmaf_rn(yc * yc, wc, sy2);
-                    m[4][j] = __fmaf_rn(xc * yc, wc, sxy);
+                    if (c0 + j < kF2) {  // stored at once: five live sums, not 5 x kSeg1
+                        float* hp = S.h + r * kPH + c0 + j;
+                        hp[0] = __fmaf_rn(xc, wc, sx);
+                        hp[kH1] = __fmaf_rn(xc * xc, wc, sx2);
+                        hp[2 * kH1] = __fmaf_rn(yc, wc, sy);
+                        hp[3 * kH1] = __fmaf_rn(yc * yc, wc, sy2);
+                        hp[4 * kH1] = __fmaf_rn(xc * yc, wc, sxy);
+                    }
                 }
-#pragma unroll
-                for (int j = 0; j < kSeg; ++j)
-                    if (c0 + j < kF2)
-#pragma unroll
-                        for (int k = 0; k < 5; ++k) S.h[k * kH1 + r * kPH + c0 + j] = m[k][j];
             }
             __syncthreads();
             // pass 2: vertical blur + SSIM partials on the 42x42 grid (one column per lane)
