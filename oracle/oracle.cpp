@@ -1493,6 +1493,9 @@ void orc_rasterize_rows(const float* rows10, uint32_t count, uint32_t w, uint32_
 
 // Deterministic float32 exp / ln used on both processors (exposed for tests).
 float orc_expf(float x) { return bsx_expf(x); }
+float orc_raster_sigma(float c00, float c01, float c11, float dx, float dy) {
+    return bsx_raster_sigma(c00, c01, c11, dx, dy);
+}
 float orc_logf(float x) { return bsx_logf(x); }
 float orc_atan2f(float y, float x) { return bsx_atan2f(y, x); }
 

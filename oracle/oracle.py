@@ -112,6 +112,8 @@ def lib() -> C.CDLL:
                                         C.c_size_t]
         _lib.orc_ply_encode_rows.restype = C.c_uint64
         _lib.orc_ply_encode_rows.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p]
+        _lib.orc_raster_sigma.restype = C.c_float
+        _lib.orc_raster_sigma.argtypes = [C.c_float] * 5
         _lib.orc_expf_raster_max_ulp.restype = C.c_double
         _lib.orc_expf_raster_max_ulp.argtypes = [C.c_float, C.c_uint32]
         _lib.orc_logf.argtypes = [C.c_float]
@@ -328,6 +330,11 @@ def ply_encode_rows(t, sh, op) -> bytes:
 
 def atan2f(y: float, x: float) -> float:
     return float(lib().orc_atan2f(float(y), float(x)))
+
+
+def raster_sigma(c00: float, c01: float, c11: float, dx: float, dy: float) -> float:
+    """The rasterizers' sigma (bsx_raster_sigma) as the kernels and this restatement evaluate it."""
+    return float(lib().orc_raster_sigma(c00, c01, c11, dx, dy))
 
 
 def expf_raster_max_ulp(lo: float, stride: int = 1) -> float:

@@ -112,6 +112,23 @@ def test_raster_exp_accuracy_on_its_domain(orc):
     assert 0.0 <= orc.expf_raster_max_ulp(-87.0, 101) <= 4.5
 
 
+def test_raster_sigma_symmetric_and_close_to_reference_expression(orc):
+    """bsx_raster_sigma gives the same bits for (dx, dy) and (-dx, -dy) (the forward takes
+    pixel - splat, the backward's restatement splat - pixel), and stays within a few ulp of
+    the reference's unfused 0.5 (c00 dx^2 + c11 dy^2) + c01 dx dy."""
+    rng = np.random.default_rng(5)
+    for _ in range(3000):
+        c00, c11 = (float(v) for v in np.float32(rng.uniform(1e-3, 2.0, 2)))
+        c01 = float(np.float32(rng.uniform(-0.9, 0.9) * math.sqrt(c00 * c11)))
+        dx, dy = (float(v) for v in np.float32(rng.uniform(-20.0, 20.0, 2)))
+        a = orc.raster_sigma(c00, c01, c11, dx, dy)
+        b = orc.raster_sigma(c00, c01, c11, -dx, -dy)
+        assert np.float32(a).view(np.uint32) == np.float32(b).view(np.uint32)
+        exact = 0.5 * (c00 * dx * dx + c11 * dy * dy) + c01 * dx * dy
+        scale = 0.5 * (c00 * dx * dx + c11 * dy * dy) + abs(c01 * dx * dy)
+        assert abs(a - exact) <= 4e-7 * scale + 1e-30
+
+
 def test_shared_atan2_accuracy_and_special_values(orc):
     """bsx_atan2f (the camera models' angle) within 2 ulp of the C library, with its
     quadrant and signed-zero conventions."""
