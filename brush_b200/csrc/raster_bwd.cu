@@ -168,7 +168,8 @@ __device__ __forceinline__ bool pixel_step(PixelBwd& P, float pcx, float dx0, fl
 constexpr int kBwdPixThreads = 128;
 
 // Bounded to 64 registers (eight resident blocks per SM, no spills): measured
-// faster than the unbounded 68-72 registers at seven blocks.
+// faster than the unbounded 68-72 registers at seven blocks, and than nine
+// blocks at 56 registers (which spills; 6 % slower).
 template <bool SMOOTH, bool REFINE>
 __global__ void __launch_bounds__(kBwdPixThreads, 8) raster_bwd_kernel(const BwdArgs a) {
     __shared__ float4 s_a[kBwdPixThreads];  // x, y, c00, c01
