@@ -6,6 +6,7 @@ the shapes and value distributions the benchmark configurations name.
 """
 from __future__ import annotations
 
+import logging
 import math
 from dataclasses import dataclass
 
@@ -13,6 +14,47 @@ import numpy as np
 import torch
 
 from .camera import Camera
+
+_log = logging.getLogger(__name__)
+
+
+class SplatValidationError(ValueError):
+    """A splat (or gradient) tensor holds NaN or Inf values, or has inconsistent shapes."""
+
+
+def validate_tensor_val(t: torch.Tensor, name: str, min_val=None, max_val=None, strict: bool = True) -> dict:
+    """NaN / Inf and out-of-range counts of a tensor (crates/brush-render/src/validation.rs:6-81).
+
+    Range violations are logged. NaN and Inf are logged and, with ``strict`` (the
+    reference promotes them to panics in its test and debug-validation builds), raise
+    SplatValidationError naming the tensor and the first offending flat index."""
+    v = t.detach().reshape(-1).float()
+    nan = torch.isnan(v)
+    inf = torch.isinf(v)
+    finite = ~(nan | inf)
+    counts = {"nan": int(nan.sum()), "inf": int(inf.sum()), "below_min": 0, "above_max": 0}
+    if min_val is not None:
+        counts["below_min"] = int((finite & (v < min_val)).sum())
+    if max_val is not None:
+        counts["above_max"] = int((finite & (v > max_val)).sum())
+    first = {k: (int(torch.nonzero(m)[0, 0]) if c else None) for k, m, c in
+             (("nan", nan, counts["nan"]), ("inf", inf, counts["inf"]))}
+    if counts["nan"] or counts["inf"]:
+        _log.error("tensor '%s': %d NaN (first @ %s), %d Inf (first @ %s) of %d total", name, counts["nan"],
+                   first["nan"], counts["inf"], first["inf"], v.numel())
+    if counts["below_min"]:
+        _log.error("tensor '%s': %d values < %s of %d", name, counts["below_min"], min_val, v.numel())
+    if counts["above_max"]:
+        _log.error("tensor '%s': %d values > %s of %d", name, counts["above_max"], max_val, v.numel())
+    if strict and (counts["nan"] or counts["inf"]):
+        raise SplatValidationError(f"tensor '{name}' has {counts['nan']} NaNs (first @ {first['nan']}) and "
+                                   f"{counts['inf']} Infs (first @ {first['inf']})")
+    return counts
+
+
+def validate_gradient(gradient: torch.Tensor, name: str, strict: bool = True) -> dict:
+    """validate_gradient (validation.rs:83-85): NaN / Inf in a parameter gradient."""
+    return validate_tensor_val(gradient, f"gradient_{name}", strict=strict)
 
 
 @dataclass
@@ -36,6 +78,38 @@ class Splats:
 
     def means(self) -> torch.Tensor:
         return self.transforms[:, 0:3]
+
+    def validate_values(self, strict: bool = True) -> dict:
+        """Splats::validate_values (gaussian_splats.rs:323-379): every parameter free of
+        NaN / Inf (raises with ``strict``), the reference's plausibility ranges logged
+        (log-scales [-10, 10], scales [1e-20, 1e4] and [1e-6, 100], SH [-5, 5], raw
+        opacity [-20, 20], opacity [0, 1]), and consistent shapes. The render path never
+        calls it (as in the reference, where it is compiled only into test and debug
+        builds): the kernels cull non-finite splats instead."""
+        n = self.num_splats
+        if self.transforms.dim() != 2 or self.transforms.shape[1] != 10:
+            raise SplatValidationError("Transforms must be 10D (means(3) + quats(4) + log_scales(3))")
+        if self.raw_opacities.shape != (n,):
+            raise SplatValidationError("Inconsistent number of splats in opacity")
+        if self.sh_coeffs.dim() != 3 or self.sh_coeffs.shape[2] != 3:
+            raise SplatValidationError("SH coeffs must have 3 color channels")
+        if self.sh_coeffs.shape[0] != n:
+            raise SplatValidationError("Inconsistent number of splats in SH coeffs")
+        t = self.transforms.detach().float()
+        log_scales = t[:, 7:10]
+        scales = torch.exp(log_scales)
+        out = {
+            "means": validate_tensor_val(t[:, 0:3], "means", strict=strict),
+            "rotations": validate_tensor_val(t[:, 3:7], "rotations", strict=strict),
+            "log_scales": validate_tensor_val(log_scales, "log_scales", -10.0, 10.0, strict),
+            "scales": validate_tensor_val(scales, "scales", 1e-20, 10000.0, strict),
+            "sh_coeffs": validate_tensor_val(self.sh_coeffs, "sh_coeffs", -5.0, 5.0, strict),
+            "raw_opacity": validate_tensor_val(self.raw_opacities, "raw_opacity", -20.0, 20.0, strict),
+            "opacities": validate_tensor_val(torch.sigmoid(self.raw_opacities.detach().float()), "opacities",
+                                             0.0, 1.0, strict),
+        }
+        out["scales_plausible"] = validate_tensor_val(scales, "scales", 1e-6, 100.0, strict)
+        return out
 
     def to(self, device) -> "Splats":
         return Splats(self.transforms.to(device), self.sh_coeffs.to(device), self.raw_opacities.to(device),
