@@ -267,3 +267,75 @@ def test_oracle_adam_matches_numpy_restatement(orc, reduce, scaled):
     np.testing.assert_allclose(p, pn, rtol=1e-6, atol=1e-7)
     assert np.abs(p - p0).max() > 1e-4  # three steps of about lr each moved the parameters
 
+
+
+def _lcg_weights(h, w, c=4, seed=0xCAFEF00D):
+    """Deterministic weights in [0, 1) from a 64-bit LCG (the generator of finite_diff.rs:803-812)."""
+    out = np.empty(h * w * c, np.float32)
+    state = seed
+    for i in range(out.size):
+        state = (state * 6364136223846793005 + 1442695040888963407) & (2**64 - 1)
+        out[i] = np.float32((state >> 33) / 0xFFFFFFFF)
+    return out.reshape(h, w, c)
+
+
+@pytest.mark.parametrize("lane,splat,comp", [("mean", 0, 0), ("mean", 1, 1), ("scale", 0, 0), ("sh", 1, 1),
+                                             ("opac", 0, 0), ("opac", 2, 0), ("rot", 2, 1)])
+def test_oracle_weighted_loss_gradient_matches_central_difference(orc, lane, splat, comp):
+    """sum(image * W) for a fixed random weight map W (finite_diff.rs:794-917): a per-pixel
+    asymmetry between forward and backward that a uniform mean would hide shows here.
+    Tolerance 0.5 + 2 % as the reference's (sum-loss values are in the hundreds)."""
+    cam = _camera()
+    t, sh, op = _scene(0)
+    wts = _lcg_weights(SIZE[1], SIZE[0])
+    r = orc.RenderResult(cam, SIZE, t, sh, op, raster_pass=SMOOTH)
+    vt, vs, vo, _ = r.project_bwd(r.rasterize_bwd(wts, False))
+    an = _pick(vt, vs, vo, lane, splat, comp)
+
+    def value(h):
+        img = orc.RenderResult(cam, SIZE, *_perturbed(t, sh, op, lane, splat, comp, h), raster_pass=SMOOTH).image
+        return float((img.astype(np.float64) * wts).sum())
+
+    num = _central(value)
+    scale = max(abs(num), abs(an), 1e-8)
+    assert abs(num - an) <= 0.5 + 0.02 * scale, f"weighted {lane}[{splat},{comp}]: {num:.6e} vs {an:.6e}"
+    assert abs(num - an) <= 0.05 + 0.01 * scale  # the oracle also meets a ten times tighter bound
+
+
+def test_oracle_early_out_back_splats_gradient(orc):
+    """Thirty opaque splats stacked in depth: the front few drive transmittance below 1e-4,
+    the rest are skipped where the stack covers a pixel, and their opacity gradient is
+    near zero on both sides (finite_diff.rs:1020-1075, |diff| < 5e-4)."""
+    cam = _camera()
+    n = 30
+    t = np.zeros((n, 10), np.float32)
+    t[:, 2] = np.arange(n) * 0.3
+    t[:, 3] = 1.0
+    t[:, 7:10] = -0.3
+    c = 0.3 + 0.4 * (np.arange(n) / n)
+    sh = np.repeat(c[:, None, None], 3, axis=2).astype(np.float32)
+    op = np.full(n, 4.0, np.float32)
+    _, _, vo = _analytic(orc, cam, t, sh, op)
+    eps = 1e-3
+    for s in (1, 5, 10, 15, 20, 25, 29):
+        p, m = op.copy(), op.copy()
+        p[s] += eps
+        m[s] -= eps
+        num = (_mean_image(orc, cam, t, sh, p) - _mean_image(orc, cam, t, sh, m)) / (2 * eps)
+        assert abs(num - float(vo[s])) < 5e-4, (s, num, float(vo[s]))
+    assert abs(float(vo[1])) > 1e-4 and abs(float(vo[25])) < 1e-6 and abs(float(vo[29])) < 1e-6
+
+
+@pytest.mark.parametrize("comp", [0, 5, 13, 26, 40, 52, 61, 74])
+def test_oracle_sh4_coefficient_gradient(orc, comp):
+    """Coefficient gradients in every band up to degree 4 (25 coefficients;
+    finite_diff.rs:1748-1830 exercises each band)."""
+    cam = _camera()
+    t, sh, op = _scene(0)
+    sh4 = np.zeros((4, 25, 3), np.float32)
+    sh4[:, :1] = sh
+    sh4[:, 1:] = np.random.default_rng(23).normal(0.0, 0.2, (4, 24, 3))
+    for splat in (0, 3):
+        an = _pick(*_analytic(orc, cam, t, sh4, op), "sh", splat, comp)
+        num = _central(lambda h: _mean_image(orc, cam, *_perturbed(t, sh4, op, "sh", splat, comp, h)))
+        _check(num, an, f"sh4[{splat},{comp}]")
