@@ -1,4 +1,4 @@
-"""Data-parallel host logic on CPU (gloo, world size 2), with the oracle as the compute.
+"""Data-parallel host logic on CPU (gloo, world sizes 2 and 4), with the oracle as the compute.
 
 - every rank trains its own view; after the exchange all ranks hold identical
   splats equal to a single-process Adam step on the mean-of-views gradient;
@@ -141,27 +141,32 @@ def _run(world, die_rank=-1, timeout=120, sharded=False):
     return sorted(out, key=lambda r: r[0])
 
 
+@pytest.mark.parametrize("world", [2, 4])
 @pytest.mark.parametrize("sharded", [False, True], ids=["allreduce", "reduce_scatter"])
-def test_two_ranks_match_mean_of_views_step(orc, sharded):
-    res = _run(2, sharded=sharded)
+def test_ranks_match_mean_of_views_step(orc, sharded, world):
+    res = _run(world, sharded=sharded)
     assert all(r[1] == "ok" for r in res), res
-    (_, _, t0, s0, o0, sc0, ag0, r0), (_, _, t1, s1, o1, sc1, ag1, r1) = res
-    assert sc0 == sc1 == 0.5 and ag0 and ag1
-    np.testing.assert_array_equal(t0, t1)
-    np.testing.assert_array_equal(s0, s1)
-    np.testing.assert_array_equal(r0, r1)
-    # single process: both views' gradients summed, scaled by 1/2
+    _, _, t0, s0, o0, _, _, r0 = res[0]
+    for (_, _, t, sh, op, sc, ag, rw) in res:
+        assert sc == 1.0 / world and ag
+        np.testing.assert_array_equal(t, t0)
+        np.testing.assert_array_equal(sh, s0)
+        np.testing.assert_array_equal(op, o0)
+        np.testing.assert_array_equal(rw, r0)
+    # single process: every rank's view gradient summed, scaled by 1/world
     from brush_b200.dist import view_for
 
     splats, cams, size, gts = _scene()
-    flats = [_view_grad(orc, splats, cams[view_for(0, r, 2, 4)], size, gts[view_for(0, r, 2, 4)]) for r in range(2)]
-    t, sh, op = _apply(orc, splats, flats[0][0] + flats[1][0], 0.5)
+    views = [view_for(0, r, world, len(cams)) for r in range(world)]
+    assert sorted(views) == list(range(world))
+    flats = [_view_grad(orc, splats, cams[v], size, gts[v]) for v in views]
+    t, sh, op = _apply(orc, splats, np.sum([f[0] for f in flats], axis=0, dtype=np.float32), 1.0 / world)
     np.testing.assert_allclose(t0, t, rtol=0, atol=2e-6)
     np.testing.assert_allclose(s0, sh, rtol=0, atol=2e-6)
     np.testing.assert_allclose(o0, op, rtol=0, atol=2e-6)
     # the oracle's raster backward sums with OpenMP atomics, so an independent
     # recomputation agrees to rounding, not bit-for-bit
-    np.testing.assert_allclose(r0, np.maximum(flats[0][1], flats[1][1]), rtol=1e-4, atol=1e-9)
+    np.testing.assert_allclose(r0, np.max([f[1] for f in flats], axis=0), rtol=1e-4, atol=1e-9)
 
 
 def test_dead_rank_fails_fast_instead_of_hanging():
