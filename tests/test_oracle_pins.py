@@ -5,6 +5,8 @@
 - the raster-oracle KATs (crates/brush-render/src/tests/raster_oracle.rs:111-159);
 - sort / prefix-sum / tile-offset KATs (brush-sort/src/lib.rs:170-429,
   brush-prefix-sum/src/lib.rs:109-191, get_tile_offset.rs:88-129);
+- the loss KATs: the L1 formula on the reference's 2x2 vectors, SSIM(x, x) = 1 and the
+  SSIM clamp range on its byte patterns (crates/brush-loss/tests/reference.rs:133-256, 363-412);
 - the shared elementary functions against the C library.
 """
 import math
@@ -148,3 +150,58 @@ def test_shared_atan2_accuracy_and_special_values(orc):
 def test_gauss_taps_normalised(orc):
     w = orc.gauss_taps()
     assert abs(float(w.sum()) - 1.0) < 1e-6 and np.allclose(w, w[::-1])
+
+
+def _pattern(h, w, scale, offset):
+    """The reference loss tests' deterministic RGBA byte pattern (brush-loss/tests/reference.rs:27-31)."""
+    i = np.arange(h * w * 4, dtype=np.uint64)
+    return ((i * scale + offset) % 251).astype(np.uint8).reshape(h, w, 4)
+
+
+def _packed(b):
+    b = b.astype(np.uint32)
+    return b[..., 0] | (b[..., 1] << 8) | (b[..., 2] << 16) | (b[..., 3] << 24)
+
+
+@pytest.mark.parametrize("channels,l1,bg,mask", [(3, 0.73, None, False), (3, 0.41, (0.1, 0.25, 0.8), True),
+                                                 (4, 0.19, None, False)])
+def test_loss_l1_kat(orc, channels, l1, bg, mask):
+    """L1-only loss map against the reference's CPU formula and its own 2x2 vectors
+    (brush-loss/tests/reference.rs:133-175, 363-412): weight * |pred - gt| * (mask ? alpha : 1),
+    gt = byte / 255 (+ (1 - alpha) * bg when compositing), the alpha channel weighted 1."""
+    gt = np.array([10, 100, 200, 0, 250, 50, 25, 64, 30, 90, 150, 192, 240, 180, 60, 255], np.uint8).reshape(2, 2, 4)
+    if channels == 3:
+        pred = np.array([0.9, 0.1, 0.4, 0.2, 0.8, 0.5, 0.7, 0.3, 0.05, 0.4, 0.6, 0.95], np.float32).reshape(2, 2, 3)
+    else:
+        pred = np.array([0.9, 0.1, 0.4, 0.8, 0.2, 0.8, 0.5, 0.1, 0.7, 0.3, 0.05, 0.9, 0.4, 0.6, 0.95, 0.2],
+                        np.float32).reshape(2, 2, 4)
+    cfg = orc.loss_cfg(l1_weight=l1, ssim_weight=0.0, composite_bg=bg, mask=mask)
+    got = orc.loss_fwd(np.ascontiguousarray(pred.transpose(2, 0, 1)), _packed(gt), cfg).transpose(1, 2, 0)
+    alpha = gt[..., 3].astype(np.float32) / 255.0
+    for c in range(channels):
+        if c == 3:
+            ref, wgt = alpha, 1.0
+        else:
+            ref = gt[..., c].astype(np.float32) / 255.0
+            if bg is not None:
+                ref = ref + (1.0 - alpha) * np.float32(bg[c])
+            wgt = l1
+        exp = wgt * np.abs(pred[..., c] - ref) * (alpha if mask else 1.0)
+        assert np.abs(got[..., c] - exp).max() < 2e-6, (c, got[..., c], exp)
+
+
+def test_loss_ssim_of_identical_pattern_is_one(orc):
+    """SSIM(x, x) = 1 on the reference's 40x56 pattern (reference.rs:210-232, |mean - 1| < 1e-4)."""
+    b = _pattern(40, 56, 11, 13)
+    pred = np.ascontiguousarray((b[..., :3].astype(np.float32) / 255.0).transpose(2, 0, 1))
+    m = orc.loss_fwd(pred, _packed(b), orc.loss_cfg(l1_weight=0.0, ssim_weight=1.0))
+    assert abs(float(m.astype(np.float64).mean()) - 1.0) < 1e-4
+    assert np.abs(m - 1.0).max() <= 1e-5
+
+
+def test_loss_ssim_stays_in_clamp_range(orc):
+    """SSIM of two different patterns stays inside [-1, 1] (reference.rs:234-256)."""
+    a, b = _pattern(40, 56, 7, 19), _pattern(40, 56, 13, 7)
+    pred = np.ascontiguousarray((a[..., :3].astype(np.float32) / 255.0).transpose(2, 0, 1))
+    m = orc.loss_fwd(pred, _packed(b), orc.loss_cfg(l1_weight=0.0, ssim_weight=1.0))
+    assert m.min() >= -1.0 and m.max() <= 1.0 and m.min() < 0.9
