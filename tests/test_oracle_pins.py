@@ -7,6 +7,8 @@
   brush-prefix-sum/src/lib.rs:109-191, get_tile_offset.rs:88-129);
 - the loss KATs: the L1 formula on the reference's 2x2 vectors, SSIM(x, x) = 1 and the
   SSIM clamp range on its byte patterns (crates/brush-loss/tests/reference.rs:133-256, 363-412);
+- the render invariance tests: culled splats appended or prepended change nothing, and a
+  repeated render is bit-identical (crates/brush-render/src/tests/mod.rs:302-410);
 - the shared elementary functions against the C library.
 """
 import math
@@ -205,3 +207,50 @@ def test_loss_ssim_stays_in_clamp_range(orc):
     pred = np.ascontiguousarray((a[..., :3].astype(np.float32) / 255.0).transpose(2, 0, 1))
     m = orc.loss_fwd(pred, _packed(b), orc.loss_cfg(l1_weight=0.0, ssim_weight=1.0))
     assert m.min() >= -1.0 and m.max() <= 1.0 and m.min() < 0.9
+
+
+def _rng_scene(n, spread, log_scale, opac, seed):
+    """Random splats: means in [-spread, spread]^3, log-scales and opacity logits uniform in the
+    given ranges, random rotations, DC colours in [0, 1] (the shape of the reference's
+    invariance scenes, crates/brush-render/src/tests/mod.rs:250-290)."""
+    rng = np.random.default_rng(seed)
+    means = rng.uniform(-spread, spread, (n, 3))
+    q = rng.normal(size=(n, 4))
+    ls = rng.uniform(*log_scale, (n, 3))
+    t = np.concatenate([means, q, ls], 1).astype(np.float32)
+    sh = rng.uniform(0.0, 1.0, (n, 1, 3)).astype(np.float32)
+    op = rng.uniform(*opac, n).astype(np.float32)
+    return t, sh, op
+
+
+def _invariance_render(orc, t, sh, op):
+    from brush_b200.camera import Camera
+
+    cam = Camera(fov_x=0.5, fov_y=0.5, position=(0.0, 0.0, -5.0), rotation=(0.0, 0.0, 0.0, 1.0))
+    return orc.RenderResult(cam, (256, 256), t, sh, op).image
+
+
+def test_invariance_hidden_splats_do_not_perturb_render(orc):
+    """Appending culled splats (opacity far below 1/255, behind the camera, far off-screen)
+    leaves the render unchanged (crates/brush-render/src/tests/mod.rs:333-378, < 1e-5)."""
+    t, sh, op = _rng_scene(5000, 1.5, (-3.0, -0.5), (0.0, 3.0), 0xBEEF)
+    ht, hsh, hop = _rng_scene(20000, 1.0, (-1.0, 1.0), (-20.0, -20.0), 0xDEAD)
+    ht[1::3, 0:3] = [0.0, 0.0, -1000.0]  # behind the camera (it looks along +z from z = -5)
+    ht[2::3, 0:3] = [1e6, 1e6, 10.0]     # far off-screen
+    hop[1::3] = 2.0
+    hop[2::3] = 2.0
+    a = _invariance_render(orc, t, sh, op)
+    b = _invariance_render(orc, np.concatenate([t, ht]), np.concatenate([sh, hsh]), np.concatenate([op, hop]))
+    assert a[..., 3].max() > 0.5
+    assert np.abs(a - b).max() < 1e-5
+
+
+def test_invariance_culled_prefix_and_determinism(orc):
+    """A culled prefix shifts every splat's id without changing the render (mod.rs:380-410),
+    and rendering twice is bit-identical (mod.rs:302-330)."""
+    t, sh, op = _rng_scene(4000, 1.5, (-3.0, -0.5), (0.0, 3.0), 0xC0FFEE)
+    pt, psh, pop = _rng_scene(50000, 1.0, (-1.0, 1.0), (-20.0, -20.0), 0xF00D)
+    a = _invariance_render(orc, t, sh, op)
+    b = _invariance_render(orc, np.concatenate([pt, t]), np.concatenate([psh, sh]), np.concatenate([pop, op]))
+    assert np.abs(a - b).max() < 1e-5
+    np.testing.assert_array_equal(a, _invariance_render(orc, t, sh, op))
