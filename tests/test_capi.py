@@ -88,3 +88,50 @@ def test_invalid_arguments_rejected_without_gpu(bsx_lib):
     lib = bsx_lib.lib()
     assert lib.bsx_render_fwd(None, None, 0, 0, None, None, None, 0, 0, 0, 0, None, None) == 1
     assert lib.bsx_make_project_uniforms(None, 1, 1, 0, 0, None) == 1
+
+
+def _c_category(decl: str) -> str:
+    decl = decl.strip()
+    if "*" in decl or "[" in decl:
+        return "ptr"
+    base = re.sub(r"\b(const|unsigned|signed|struct)\b", "", decl).split()[0]
+    if base == "void":
+        return "void"
+    table = {"uint32_t": "u32", "int32_t": "i32", "int": "i32", "float": "f32", "double": "f64",
+             "uint64_t": "u64", "size_t": "u64", "int64_t": "i64"}
+    if base in table:
+        return table[base]
+    if base in ("bsx_status", "bsx_render_mode", "bsx_raster_pass", "bsx_camera_model"):
+        return "i32"  # C enums are int-sized
+    raise AssertionError(f"unmapped C type {decl!r}")
+
+
+def _ctypes_category(t) -> str:
+    import ctypes as C
+
+    if t is None:
+        return "void"
+    if t in (C.c_void_p, C.c_char_p) or (isinstance(t, type) and issubclass(t, C._Pointer)):
+        return "ptr"
+    for cats, name in (((C.c_uint32, C.c_uint), "u32"), ((C.c_int32, C.c_int), "i32"), ((C.c_float,), "f32"),
+                       ((C.c_double,), "f64"), ((C.c_uint64, C.c_size_t), "u64"), ((C.c_int64,), "i64")):
+        if t in cats:
+            return name
+    raise AssertionError(f"unmapped ctypes type {t!r}")
+
+
+def test_bindings_match_header_signatures(bsx_lib):
+    """Every ctypes binding has the header's parameter count and, per parameter, the same
+    kind (pointer, 32/64-bit integer, float) and return kind: a mismatch would pass wrong
+    arguments across the ABI without any error."""
+    text = (ROOT / "include" / "bsx.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    decls = re.findall(r"BSX_API\s+([\w\s\*]+?)\b(bsx_\w+)\s*\(([^;]*?)\)\s*;", text, flags=re.S)
+    assert len(decls) == len(_declared())
+    for ret, name, params in decls:
+        params = " ".join(params.split())
+        cats = [] if params in ("", "void") else [_c_category(p) for p in params.split(",")]
+        restype, argtypes = bsx_lib.SIGNATURES[name]
+        got = [_ctypes_category(t) for t in argtypes]
+        assert got == cats, f"{name}: header {cats} vs binding {got}"
+        assert _ctypes_category(restype) == _c_category(ret), name
