@@ -135,3 +135,9 @@ def test_bindings_match_header_signatures(bsx_lib):
         got = [_ctypes_category(t) for t in argtypes]
         assert got == cats, f"{name}: header {cats} vs binding {got}"
         assert _ctypes_category(restype) == _c_category(ret), name
+
+
+def test_integration_binding_declares_every_entry_point():
+    """The Rust FFI block a maintainer would add names exactly the header's entry points."""
+    doc = set(re.findall(r"pub fn (bsx_\w+)", (ROOT / "INTEGRATION.md").read_text()))
+    assert doc == set(_declared())
