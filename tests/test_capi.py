@@ -138,6 +138,6 @@ def test_bindings_match_header_signatures(bsx_lib):
 
 
 def test_integration_binding_declares_every_entry_point():
-    """The Rust FFI block a maintainer would add names exactly the header's entry points."""
+    """The Rust FFI block of the integration guide names exactly the header's entry points."""
     doc = set(re.findall(r"pub fn (bsx_\w+)", (ROOT / "INTEGRATION.md").read_text()))
     assert doc == set(_declared())
