@@ -10,6 +10,6 @@ from .camera import Camera, focal_to_fov, fov_to_focal  # noqa: F401
 from .loss import ImageLossConfig, image_loss_backward, image_loss_forward, image_loss_fused  # noqa: F401
 from .primitives import get_tile_offsets, prefix_sum, radix_argsort  # noqa: F401
 from .render import RasterPass, RenderOutput, SplatRenderMode, render, render_splats  # noqa: F401
-from .render_bwd import SplatGrads, project_bwd, rasterize_bwd  # noqa: F401
+from .render_bwd import SplatGrads, project_bwd, project_bwd_ref, rasterize_bwd, rasterize_bwd_ref  # noqa: F401
 from .splats import Splats  # noqa: F401
 from .train import RefineConfig, SplatTrainer, TrainConfig  # noqa: F401

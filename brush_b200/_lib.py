@@ -269,6 +269,16 @@ SIGNATURES = {
     ),
     "bsx_rasterize_bwd": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p]),
     "bsx_project_bwd": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "bsx_rasterize_bwd_ref": (
+        C.c_int,
+        [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_void_p, C.c_uint32, C.c_void_p, C.POINTER(C.c_float),
+         C.c_uint32, C.c_uint32, C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p],
+    ),
+    "bsx_project_bwd_ref": (
+        C.c_int,
+        [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p, C.c_uint32,
+         C.POINTER(ProjectUniforms), C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p],
+    ),
     "bsx_loss_fwd": (
         C.c_int,
         [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32, C.POINTER(LossCfg), C.c_void_p],
@@ -298,6 +308,7 @@ SIGNATURES = {
         C.c_int, [C.c_void_p, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), C.POINTER(C.c_void_p)]
     ),
     "bsx_trainer_keep_gradients": (C.c_int, [C.c_void_p, C.c_int32]),
+    "bsx_trainer_raster_grads": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
     "bsx_trainer_grad_buffers": (
         C.c_int,
         [C.c_void_p, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), C.POINTER(C.c_void_p)],

@@ -25,6 +25,7 @@ enum DeviceError : int {
     kDevLookbackTimeout = 1,
     kDevOutOfRange = 2,
     kDevPeerTimeout = 3,
+    kDevBadIndex = 4,  // a caller-supplied index or range was out of bounds (entry skipped)
 };
 
 // Bounded spin for device-side waits on another block's published state.
@@ -151,7 +152,9 @@ struct bsx_ctx {
     // workspace
     bsx::DevBuf projected, counts, depth_keys, vis_gid, depth_order, cum, isect_tile, isect_gid, tile_offsets,
         image, image_packed, visible, max_radius, sort_tmp_k, sort_tmp_v, sort_hist, sort_lookback, scan_status,
-        scalars, grad, loss_partials, sort_keys_b, sort_vals_b, tile_order;
+        scalars, grad, loss_partials, sort_keys_b, sort_vals_b, tile_order,
+        // reference-layout backward operators (ref_bwd.cu)
+        ref_rows, ref_ids, ref_offsets, ref_grad;
     bsx_fwd_state fwd;
     // optional per-launch timing (bsx_profile_*)
     int profiling = 0;

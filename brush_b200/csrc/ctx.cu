@@ -86,6 +86,8 @@ bsx_status check_device_error(bsx_ctx* ctx) {
         return fail(ctx, BSX_ERR_DEVICE_TIMEOUT, "a bounded device-side lookback wait expired");
     if (code == kDevPeerTimeout)
         return fail(ctx, BSX_ERR_DEVICE_TIMEOUT, "a data-parallel peer did not reach the exchange within the timeout");
+    if (code == kDevBadIndex)
+        return fail(ctx, BSX_ERR_INVALID_ARG, "an intersection id, tile range or global id was out of bounds (skipped)");
     return fail(ctx, BSX_ERR_CAPACITY, "device-side range check failed (code " + std::to_string(code) + ")");
 }
 
@@ -147,7 +149,8 @@ bsx_status bsx_destroy(bsx_ctx* ctx) {
                       &ctx->cum, &ctx->isect_tile, &ctx->isect_gid, &ctx->tile_offsets, &ctx->image,
                       &ctx->image_packed, &ctx->visible, &ctx->max_radius, &ctx->sort_tmp_k, &ctx->sort_tmp_v,
                       &ctx->sort_hist, &ctx->sort_lookback, &ctx->scan_status, &ctx->scalars, &ctx->grad,
-                      &ctx->loss_partials, &ctx->sort_keys_b, &ctx->sort_vals_b, &ctx->tile_order};
+                      &ctx->loss_partials, &ctx->sort_keys_b, &ctx->sort_vals_b, &ctx->tile_order,
+                      &ctx->ref_rows,      &ctx->ref_ids,     &ctx->ref_offsets, &ctx->ref_grad};
     for (DevBuf* b : bufs) release(ctx, *b);
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
     else cudaDeviceSynchronize();
@@ -171,7 +174,8 @@ bsx_status bsx_trim(bsx_ctx* ctx) {
                       &ctx->cum, &ctx->isect_tile, &ctx->isect_gid, &ctx->tile_offsets, &ctx->image,
                       &ctx->image_packed, &ctx->visible, &ctx->max_radius, &ctx->sort_tmp_k, &ctx->sort_tmp_v,
                       &ctx->sort_hist, &ctx->sort_lookback, &ctx->scan_status, &ctx->scalars, &ctx->grad,
-                      &ctx->loss_partials, &ctx->sort_keys_b, &ctx->sort_vals_b, &ctx->tile_order};
+                      &ctx->loss_partials, &ctx->sort_keys_b, &ctx->sort_vals_b, &ctx->tile_order,
+                      &ctx->ref_rows,      &ctx->ref_ids,     &ctx->ref_offsets, &ctx->ref_grad};
     for (DevBuf* b : bufs) release(ctx, *b);
     ctx->fwd.valid = 0;
     e = ctx->stream ? cudaStreamSynchronize(ctx->stream) : cudaDeviceSynchronize();

@@ -76,7 +76,11 @@ extern "C" {
 bsx_status bsx_render_fwd(bsx_ctx* ctx, const bsx_camera* cam, uint32_t w, uint32_t h, const float* d_transforms,
                           const float* d_sh, const float* d_raw_opac, uint32_t n, uint32_t coeffs, int32_t render_mode,
                           int32_t raster_pass, const float background[3], bsx_render_out* out) {
-    if (!ctx || !cam || !out || !background) return BSX_ERR_INVALID_ARG;
+    if (!ctx) return BSX_ERR_INVALID_ARG;
+    // A render that fails part way leaves no state a backward could consume:
+    // the previous render's rows and ranges may already be overwritten.
+    ctx->fwd.valid = 0;
+    if (!cam || !out || !background) return BSX_ERR_INVALID_ARG;
     if (w == 0 || h == 0) return fail(ctx, BSX_ERR_INVALID_ARG, "Can't render images with 0 size.");
     if (w > 16384 || h > 16384) return fail(ctx, BSX_ERR_CAPACITY, "image side limited to 16384 pixels");
     if (n && (!d_transforms || !d_sh || !d_raw_opac)) return fail(ctx, BSX_ERR_INVALID_ARG, "null splat tensor");

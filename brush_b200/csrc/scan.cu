@@ -183,6 +183,9 @@ extern "C" bsx_status bsx_prefix_sum_u32(bsx_ctx* ctx, const uint32_t* d_in, uin
 //  - Every call shares the array, so calls whose execution overlaps on the
 //    GPU (different streams, or different host threads on the same device)
 //    race and produce wrong results; serialise them.
+//  - The stream must belong to the current device (another device's stream
+//    is rejected with BSX_ERR_INVALID_ARG); the null stream means the
+//    current device's default stream.
 //  - The first call on a device looks up the array's device address (with
 //    that device current); make that first call before any stream capture.
 //  - Device-side look-back waits are bounded; a timed-out wait is not
@@ -206,6 +209,14 @@ extern "C" bsx_status bsx_prefix_sum_u32_noalloc(const uint32_t* d_in, uint32_t 
     if (n == 0) return BSX_OK;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 256) return BSX_ERR_CUDA;
+    cudaStream_t stream = (cudaStream_t)cuda_stream;
+    // The scratch address below is the current device's copy of the array, so
+    // a stream of another device would run the scan against the wrong memory.
+    if (stream) {
+        int stream_dev = -1;
+        if (cudaStreamGetDevice(stream, &stream_dev) != cudaSuccess) return BSX_ERR_CUDA;
+        if (stream_dev != dev) return BSX_ERR_INVALID_ARG;
+    }
     void* state = nullptr;
     {
         std::lock_guard<std::mutex> lock(g_noalloc_mu);
@@ -218,7 +229,6 @@ extern "C" bsx_status bsx_prefix_sum_u32_noalloc(const uint32_t* d_in, uint32_t 
         }
         state = g_noalloc_ptr[dev];
     }
-    cudaStream_t stream = (cudaStream_t)cuda_stream;
     const uint32_t tiles = (uint32_t)(((uint64_t)n + bsx::kScanTile - 1) / bsx::kScanTile);
     uint64_t* status = static_cast<uint64_t*>(state);
     // The look-back words and the ticket must start at zero on every call.
@@ -227,7 +237,14 @@ extern "C" bsx_status bsx_prefix_sum_u32_noalloc(const uint32_t* d_in, uint32_t 
     uint32_t* ticket = reinterpret_cast<uint32_t*>(status + tiles);
     const int vec_in = ((uintptr_t)d_in % 16) == 0;
     const int vec_out = ((uintptr_t)d_out % 16) == 0;
-    bsx::scan_kernel<<<tiles, bsx::kScanThreads, 0, stream>>>(d_in, nullptr, n, d_out, status, ticket, nullptr,
-                                                                nullptr, vec_in, vec_out);
-    return cudaGetLastError() == cudaSuccess ? BSX_OK : BSX_ERR_CUDA;
+    // cudaLaunchKernel reports this launch's own error; an error left by the
+    // caller's earlier CUDA calls is neither reported here nor cleared.
+    const uint32_t* gather = nullptr;
+    uint32_t* total = nullptr;
+    int* err = nullptr;
+    void* args[] = {(void*)&d_in, (void*)&gather, (void*)&n,      (void*)&d_out,  (void*)&status,
+                    (void*)&ticket, (void*)&total, (void*)&err, (void*)&vec_in, (void*)&vec_out};
+    const cudaError_t e = cudaLaunchKernel((const void*)bsx::scan_kernel, dim3(tiles), dim3(bsx::kScanThreads), args,
+                                           0, stream);
+    return e == cudaSuccess ? BSX_OK : BSX_ERR_CUDA;
 }

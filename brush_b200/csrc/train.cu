@@ -328,6 +328,12 @@ bsx_status bsx_trainer_grad_buffers(bsx_trainer* tr, float** vt, float** vs, flo
     return BSX_OK;
 }
 
+bsx_status bsx_trainer_raster_grads(bsx_trainer* tr, float** d_v_combined) {
+    if (!tr || !d_v_combined) return BSX_ERR_INVALID_ARG;
+    *d_v_combined = tr->v_combined.as<float>();
+    return BSX_OK;
+}
+
 bsx_status bsx_trainer_keep_gradients(bsx_trainer* tr, int32_t on) {
     if (!tr) return BSX_ERR_INVALID_ARG;
     tr->keep_grads = on ? 1 : 0;

@@ -118,7 +118,10 @@ def train_stream(splats: Splats, views: Sequence, config: TrainConfig, refine: O
         for it in range(process.start_iter, total):
             t0 = time.perf_counter()
             cam, size, gt = views[loader.next_index()]
-            st = trainer.step(cam, size, gt.to(dev, non_blocking=True), splats)
+            # the refine weight only feeds high-gradient growth, which stops at
+            # growth_stop_iter (refinement_weight_needed, train.rs:428-430; train_stream.rs:458)
+            need_weight = refine is not None and it < refine.growth_stop_iter
+            st = trainer.step(cam, size, gt.to(dev, non_blocking=True), splats, compute_refine_weight=need_weight)
             # refine gate on the phase iteration just completed (train_stream.rs:475-498)
             if refine is not None and refine.due(it, total):
                 rs = trainer.refine(splats, it, it, total, refine)

@@ -6,6 +6,7 @@ autodiff node, ``GaussianBackwardState``, burn_glue.rs:264-284).
 """
 from __future__ import annotations
 
+import ctypes as C
 from dataclasses import dataclass
 
 import torch
@@ -50,4 +51,49 @@ def project_bwd(v_combined: torch.Tensor, num_splats: int, sh_coeffs_per_splat: 
         )
     ctx.check(_lib.lib().bsx_project_bwd(ctx.handle, ptr(v_combined), ptr(out.v_transforms), ptr(out.v_coeffs),
                                          ptr(out.v_raw_opac), ptr(out.v_refine_weight)))
+    return out
+
+
+def rasterize_bwd_ref(out_img: torch.Tensor, projected_splats: torch.Tensor, compact_gid_from_isect: torch.Tensor,
+                      tile_offsets: torch.Tensor, background, img_size: tuple, v_output: torch.Tensor,
+                      smooth_cutoff: bool = False, render_depth: bool = False,
+                      compute_refine_weight: bool = True) -> torch.Tensor:
+    """``SplatBwdOps::rasterize_bwd`` / ``rasterize_bwd_with_refine_weight`` with the reference's
+    compact layouts (burn_glue.rs:84-121), stateless: ``projected_splats`` [V,10] by compact id,
+    ``compact_gid_from_isect`` [M] compact ids, ``tile_offsets`` [ty,tx,2] -> ``v_combined`` [V,11]."""
+    dev = out_img.device.index
+    ctx = context(dev)
+    v = int(projected_splats.shape[0])
+    if projected_splats.dim() != 2 or projected_splats.shape[1] != 10:
+        raise ValueError("projected_splats must be [V,10]")
+    w, h = int(img_size[0]), int(img_size[1])
+    v_combined = torch.empty((v, _lib.BSX_COMPACT_GRAD_LANES), device=out_img.device, dtype=torch.float32)
+    bg = (C.c_float * 3)(*[float(x) for x in background])
+    ids = compact_gid_from_isect.contiguous()
+    ctx.check(_lib.lib().bsx_rasterize_bwd_ref(ctx.handle, ptr(out_img.contiguous()), ptr(projected_splats.contiguous()),
+                                               v, ptr(ids), int(ids.numel()), ptr(tile_offsets.contiguous()), bg, w, h,
+                                               ptr(v_output.contiguous()), int(smooth_cutoff),
+                                               int(compute_refine_weight), int(render_depth), ptr(v_combined)))
+    return v_combined
+
+
+def project_bwd_ref(transforms: torch.Tensor, sh_coeffs: torch.Tensor, raw_opac: torch.Tensor,
+                    global_from_compact_gid: torch.Tensor, project_uniforms, render_mode: int,
+                    v_combined: torch.Tensor) -> SplatGrads:
+    """``SplatBwdOps::project_bwd`` with the reference's compact ``v_combined`` [V,11] and
+    ``global_from_compact_gid`` [V] (burn_glue.rs:127-141), stateless; dense gradients for all N splats."""
+    dev = transforms.device.index
+    ctx = context(dev)
+    n, c = int(transforms.shape[0]), int(sh_coeffs.shape[1])
+    v = int(global_from_compact_gid.numel())
+    if v_combined.shape != (v, _lib.BSX_COMPACT_GRAD_LANES):
+        raise ValueError("v_combined must be [V,11] with V = len(global_from_compact_gid)")
+    d = transforms.device
+    out = SplatGrads(torch.empty((n, 10), device=d), torch.empty((n, c, 3), device=d), torch.empty((n,), device=d),
+                     torch.empty((n,), device=d))
+    ctx.check(_lib.lib().bsx_project_bwd_ref(ctx.handle, ptr(transforms.contiguous()), ptr(sh_coeffs.contiguous()),
+                                             ptr(raw_opac.contiguous()), n, c, ptr(global_from_compact_gid.contiguous()),
+                                             v, C.byref(project_uniforms), int(render_mode),
+                                             ptr(v_combined.contiguous()), ptr(out.v_transforms), ptr(out.v_coeffs),
+                                             ptr(out.v_raw_opac), ptr(out.v_refine_weight)))
     return out

@@ -152,6 +152,12 @@ class _NativeTrainer:
                           device_view(p[2].value, (n,), torch.float32, d),
                           device_view(p[3].value, (n,), torch.float32, d))
 
+    def raster_grads(self) -> torch.Tensor:
+        """The last step's raster-backward rows [N, 12] (the projection backward's input)."""
+        p = C.c_void_p()
+        self.ctx.check(_lib.lib().bsx_trainer_raster_grads(self.handle, C.byref(p)))
+        return device_view(p.value, (self.n, _lib.BSX_GRAD_STRIDE), torch.float32, self.device)
+
     def record(self) -> RefineRecord | None:
         if not self.gather:
             return None

@@ -217,6 +217,38 @@ BSX_API bsx_status bsx_rasterize_bwd(bsx_ctx* ctx, const float* d_v_output, int3
 BSX_API bsx_status bsx_project_bwd(bsx_ctx* ctx, const float* d_v_combined, float* d_v_transforms,
                            float* d_v_sh_coeffs, float* d_v_raw_opac, float* d_v_refine_weight);
 
+/* The same two operators with the reference's signatures and layouts, for a
+ * backend that keeps its own forward state: stateless, compact-indexed.
+ *   projected   [V,10]  rows by compact id (depth rank): xy, conic (c00 c01 c11),
+ *                       opacity, rgb, depth (crates/brush-render/src/kernels/helpers.rs:48-52)
+ *   compact_gid_from_isect [M] compact ids, tile-major, front to back
+ *   tile_offsets [ty,tx,2] start/end per tile as the backward-pass forward left them
+ *   v_combined  [V,11]  xy(2) conic(3) rgb(3) alpha refine depth
+ *   global_from_compact_gid [V] splat row of each compact id
+ * bsx_rasterize_bwd_ref replaces SplatBwdOps::rasterize_bwd and
+ * rasterize_bwd_with_refine_weight (crates/brush-render-bwd/src/burn_glue.rs:84-121):
+ * d_v_combined is zeroed, then accumulated; compute_refine_weight = 1 is
+ * rasterize_bwd. render_depth = 1 returns BSX_ERR_UNSUPPORTED (depth rendering
+ * is not built). out_img / v_output [H,W,4] must be 16-byte aligned.
+ * bsx_project_bwd_ref replaces SplatBwdOps::project_bwd (burn_glue.rs:127-141) and
+ * writes all N rows of the dense gradients (zeros for splats without a compact id).
+ * An intersection id >= V, a tile range beyond M or a global id >= N is skipped
+ * and reported as BSX_ERR_INVALID_ARG by the next bsx_sync (the reference's
+ * checked launches skip out-of-bounds accesses the same way). Workspace: one
+ * [V+1,12] row copy, the checked ids and ranges, and [max(V+1,N),12] gradient rows. */
+BSX_API bsx_status bsx_rasterize_bwd_ref(bsx_ctx* ctx, const float* d_out_img, const float* d_projected,
+                                         uint32_t num_visible, const uint32_t* d_compact_gid_from_isect,
+                                         uint32_t num_intersections, const uint32_t* d_tile_offsets,
+                                         const float background[3], uint32_t img_w, uint32_t img_h,
+                                         const float* d_v_output, int32_t smooth_cutoff,
+                                         int32_t compute_refine_weight, int32_t render_depth, float* d_v_combined);
+BSX_API bsx_status bsx_project_bwd_ref(bsx_ctx* ctx, const float* d_transforms, const float* d_sh_coeffs,
+                                       const float* d_raw_opac, uint32_t num_splats, uint32_t sh_coeffs_per_splat,
+                                       const uint32_t* d_global_from_compact_gid, uint32_t num_visible,
+                                       const bsx_project_uniforms* uniforms, int32_t render_mode,
+                                       const float* d_v_combined, float* d_v_transforms, float* d_v_sh_coeffs,
+                                       float* d_v_raw_opac, float* d_v_refine_weight);
+
 /* ---- image loss: LossOps (crates/brush-loss/src/lib.rs:955-970) ----
  * pred/map/dl_dpred are [C,H,W] planar like the reference (C = 3, or 4 with
  * alpha matching in channel 3). */
@@ -350,6 +382,9 @@ BSX_API bsx_status bsx_trainer_stats_buffers(bsx_trainer* tr, float** d_refine_w
 BSX_API bsx_status bsx_trainer_keep_gradients(bsx_trainer* tr, int32_t on);
 BSX_API bsx_status bsx_trainer_grad_buffers(bsx_trainer* tr, float** d_v_transforms, float** d_v_sh_coeffs,
                                             float** d_v_raw_opac, float** d_v_refine_weight);
+/* The raster-backward rows of the last step, [N, BSX_GRAD_STRIDE] by global id
+ * (the input of its projection backward); valid until the next step. */
+BSX_API bsx_status bsx_trainer_raster_grads(bsx_trainer* tr, float** d_v_combined);
 /* One step in place on the splats. d_loss receives the step's mean loss (one float, device). */
 BSX_API bsx_status bsx_train_step(bsx_trainer* tr, const bsx_camera* cam, uint32_t img_w, uint32_t img_h,
                                   const uint32_t* d_gt_packed, float* d_transforms, float* d_sh_coeffs,
@@ -461,7 +496,8 @@ BSX_API bsx_status bsx_prefix_sum_u32(bsx_ctx* ctx, const uint32_t* d_in, uint32
  * memory, e.g. inside a foreign memory pool, in a real-time loop that cannot
  * afford cudaMalloc's synchronisation, or in a host that does not let a plugin
  * create a context). Same result as bsx_prefix_sum_u32; runs on the current
- * device and the given stream; needs no context. Its scratch is one fixed
+ * device and the given stream, which must belong to the current device
+ * (BSX_ERR_INVALID_ARG otherwise); needs no context. Its scratch is one fixed
  * device array per GPU (32 KiB, resident until exit) shared by all calls:
  * calls that overlap on the GPU race, so serialise them. n is limited to
  * BSX_PREFIX_SUM_NOALLOC_MAX_N (BSX_ERR_CAPACITY beyond). The first call on a

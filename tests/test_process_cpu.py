@@ -23,11 +23,13 @@ class _FakeTrainer:
 
     def __init__(self, config, splats):
         self.steps, self.refines, self.closed = [], [], False
+        self.weight_flags = []
         self.n = 1000
         _FakeTrainer.instances.append(self)
 
-    def step(self, cam, size, gt, splats):
+    def step(self, cam, size, gt, splats, compute_refine_weight=True):
         self.steps.append(cam)
+        self.weight_flags.append(compute_refine_weight)
         return SimpleNamespace(loss=torch.tensor(1.0 / (len(self.steps) + 1)), num_visible=0, num_intersections=0)
 
     def refine(self, splats, it, phase_iter, phase_total, cfg):
@@ -123,3 +125,14 @@ def test_start_iter_resumes_the_count(fake_trainer):
     msgs = list(proc.train_stream(_splats(), _views(3), TrainConfig(total_train_iters=20),
                                   process=proc.ProcessConfig(start_iter=15)))
     assert [m.iter for m in msgs if isinstance(m, proc.TrainStep)] == [16, 17, 18, 19, 20]
+
+
+def test_refine_weight_only_until_growth_stops(fake_trainer):
+    """compute_refine_weight = iter < growth_stop_iter (refinement_weight_needed, train.rs:428-430),
+    and never without densification."""
+    cfg = TrainConfig(total_train_iters=40)
+    list(proc.train_stream(_splats(), _views(3), cfg, RefineConfig(refine_every=10, growth_stop_iter=25)))
+    flags = fake_trainer.instances[0].weight_flags
+    assert flags == [it < 25 for it in range(40)]
+    list(proc.train_stream(_splats(), _views(3), cfg))
+    assert fake_trainer.instances[1].weight_flags == [False] * 40
