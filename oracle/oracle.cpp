@@ -98,6 +98,26 @@ inline float calc_sigma(float px, float py, S2 c, float x, float y) {
 // accepted pair (sigma < 0 and alpha < 1/255 are rejected either way).
 inline float raster_gauss(float sigma) { return bsx_expf_raster(-bsx_clamp(sigma, 0.0f, 87.0f)); }
 
+// Which per-pixel arithmetic the rasterizers of this restatement evaluate:
+//   0 - the kernels' form: sigma by bsx_raster_sigma (fused products),
+//       e^-sigma by bsx_expf_raster, colour sums by fused multiply-add;
+//   1 - the reference's expression (rasterize.rs:131-155, rasterize_backwards.rs:325-329):
+//       the unfused calc_sigma, e^-sigma correctly rounded from the double
+//       exponential, and pix += max(c, 0) * vis.
+// Mode 1 measures how far the kernels' arithmetic sits from the reference's
+// expression; the parity tests use mode 0.
+int g_raster_expr = 0;
+inline float raster_sigma_mode(int mode, float c00, float c01, float c11, float dx, float dy) {
+    if (mode) return 0.5f * (c00 * dx * dx + c11 * dy * dy) + c01 * dx * dy;
+    return bsx_raster_sigma(c00, c01, c11, dx, dy);
+}
+inline float raster_gauss_mode(int mode, float sigma) {
+    return mode ? (float)std::exp(-(double)sigma) : raster_gauss(sigma);
+}
+inline float raster_accum(int mode, float acc, float c, float v) {
+    return mode ? acc + bsx_max(c, 0.0f) * v : bsx_fma(bsx_max(c, 0.0f), v, acc);
+}
+
 // kernels/helpers.rs:166-190 (smooth alpha cutoff)
 const float kCutMid = 1.0f / 255.0f;
 const float kCutBand = 1.0e-3f;
@@ -475,6 +495,7 @@ struct Render {
     std::vector<uint32_t> image_packed;  // [H,W]
     std::vector<float> visible;          // [N]
     std::vector<uint32_t> last_useful;   // unused by the reference API; kept for debugging
+    int raster_expr = 0;                 // raster arithmetic of this render (g_raster_expr)
 };
 
 int g_threads = 0;
@@ -769,6 +790,8 @@ void* orc_render(const bsx_project_uniforms* up, const float* transforms, const 
 
     // Rasterize (rasterize.rs:118-291), one tile at a time.
     const uint32_t W = u.w, H = u.h;
+    const int mode = g_raster_expr;
+    r->raster_expr = mode;
     if (r->bwd_info) {
         r->image.assign((size_t)W * H * 4, 0.0f);
         r->visible.assign(n, 0.0f);
@@ -791,8 +814,8 @@ void* orc_render(const bsx_project_uniforms* up, const float* transforms, const 
                 for (uint32_t k = lo; k < hi; ++k) {
                     uint32_t g = r->isect_gid[k];
                     const float* p = &r->projected[(size_t)g * 12];
-                    float sigma = bsx_raster_sigma(p[2], p[3], p[4], pcx - p[0], pcy - p[1]);
-                    float alpha = bsx_min(0.999f, p[5] * raster_gauss(sigma));
+                    float sigma = raster_sigma_mode(mode, p[2], p[3], p[4], pcx - p[0], pcy - p[1]);
+                    float alpha = bsx_min(0.999f, p[5] * raster_gauss_mode(mode, sigma));
                     float w_cut = r->smooth ? alpha_cutoff_weight(alpha) : (alpha >= kCutMid ? 1.0f : 0.0f);
                     if (sigma >= 0.0f && w_cut > 0.0f) {
                         float ae = alpha * w_cut;
@@ -803,9 +826,9 @@ void* orc_render(const bsx_project_uniforms* up, const float* transforms, const 
                             r->visible[g] = 1.0f;
                         }
                         float v = ae * T_acc;
-                        pr = bsx_fma(bsx_max(p[6], 0.0f), v, pr);
-                        pg = bsx_fma(bsx_max(p[7], 0.0f), v, pg);
-                        pb = bsx_fma(bsx_max(p[8], 0.0f), v, pb);
+                        pr = raster_accum(mode, pr, p[6], v);
+                        pg = raster_accum(mode, pg, p[7], v);
+                        pb = raster_accum(mode, pb, p[8], v);
                         T_acc = next_t;
                         last = k + 1;
                     }
@@ -876,6 +899,7 @@ void orc_rasterize_bwd(void* h, const float* v_output, int compute_refine, float
     const uint32_t W = u.w, H = u.h, T = u.tbw * u.tbh;
     std::memset(v_combined, 0, sizeof(float) * (size_t)r->n * 11);
     const float bgr = r->bg[0], bgg = r->bg[1], bgb = r->bg[2];
+    const int mode = r->raster_expr;
 #pragma omp parallel for schedule(dynamic, 1)
     for (int64_t ti = 0; ti < (int64_t)T; ++ti) {
         uint32_t tile = (uint32_t)ti;
@@ -909,8 +933,8 @@ void orc_rasterize_bwd(void* h, const float* v_output, int compute_refine, float
                 uint32_t px = ox + p % 16, py = oy + p / 16;
                 float pcx = (float)px + 0.5f, pcy = (float)py + 0.5f;
                 float dx = sx - pcx, dy = sy - pcy;
-                float sigma = bsx_raster_sigma(c00, c01, c11, dx, dy);
-                float gauss = raster_gauss(sigma);
+                float sigma = raster_sigma_mode(mode, c00, c01, c11, dx, dy);
+                float gauss = raster_gauss_mode(mode, sigma);
                 float alpha = bsx_min(0.999f, ca * gauss);
                 float w_cut = r->smooth ? alpha_cutoff_weight(alpha) : (alpha >= kCutMid ? 1.0f : 0.0f);
                 if (!(sigma >= 0.0f && w_cut > 0.0f)) continue;
@@ -1520,6 +1544,62 @@ double orc_expf_raster_max_ulp(float lo, uint32_t stride) {
         worst = fmax(worst, fabs((double)y - ref) / ulp);
     }
     return worst >= 1e30 ? -1.0 : worst;
+}
+
+void orc_set_raster_expr(int mode) { g_raster_expr = mode ? 1 : 0; }
+
+// Decision flips between the two raster arithmetics along one render's
+// trajectory: every pixel walks its tile's whole intersection run (the
+// unshortened range) with the state of the render's own arithmetic, and at
+// each pair evaluates both forms. out = {pairs walked, accept flips (sigma >= 0
+// and alpha >= 1/255 differ), early-out flips (both accept; T (1 - alpha) <=
+// 1e-4 differs), pixels}. Hard alpha cutoff only.
+void orc_raster_decision_flips(void* h, uint64_t out[4]) {
+    Render* r = (Render*)h;
+    const Uni u = uni_from(r->uni);
+    const uint32_t W = u.w, H = u.h, T = u.tbw * u.tbh, M = r->num_intersections;
+    const int mode = r->raster_expr;
+    std::vector<uint32_t> lo(T, 0), hi(T, 0);
+    for (uint32_t k = 0; k < M; ++k) {
+        const uint32_t t = r->isect_tile[k];
+        if (t >= T) continue;
+        if (k == 0 || r->isect_tile[k - 1] != t) lo[t] = k;
+        hi[t] = k + 1;
+    }
+    uint64_t pairs = 0, acc_flip = 0, eo_flip = 0, pixels = 0;
+#pragma omp parallel for schedule(dynamic, 1) reduction(+ : pairs, acc_flip, eo_flip, pixels)
+    for (int64_t ti = 0; ti < (int64_t)T; ++ti) {
+        const uint32_t tile = (uint32_t)ti, tx = tile % u.tbw, ty = tile / u.tbw;
+        for (uint32_t py = ty * 16; py < ty * 16 + 16; ++py)
+            for (uint32_t px = tx * 16; px < tx * 16 + 16; ++px) {
+                if (!(px < W && py < H)) continue;
+                ++pixels;
+                const float pcx = (float)px + 0.5f, pcy = (float)py + 0.5f;
+                float T_acc = 1.0f;
+                for (uint32_t k = lo[tile]; k < hi[tile]; ++k) {
+                    const float* p = &r->projected[(size_t)r->isect_gid[k] * 12];
+                    bool acc[2], eo[2];
+                    float ae[2];
+                    for (int m = 0; m < 2; ++m) {
+                        const float sg = raster_sigma_mode(m, p[2], p[3], p[4], pcx - p[0], pcy - p[1]);
+                        const float al = bsx_min(0.999f, p[5] * raster_gauss_mode(m, sg));
+                        acc[m] = sg >= 0.0f && al >= kCutMid;
+                        ae[m] = al;
+                        eo[m] = T_acc * (1.0f - al) <= 1.0e-4f;
+                    }
+                    ++pairs;
+                    if (acc[0] != acc[1]) ++acc_flip;
+                    else if (acc[0] && eo[0] != eo[1]) ++eo_flip;
+                    if (!acc[mode]) continue;
+                    if (eo[mode]) break;
+                    T_acc = T_acc * (1.0f - ae[mode]);
+                }
+            }
+    }
+    out[0] = pairs;
+    out[1] = acc_flip;
+    out[2] = eo_flip;
+    out[3] = pixels;
 }
 
 }  // extern "C"

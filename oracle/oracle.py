@@ -118,8 +118,25 @@ def lib() -> C.CDLL:
         _lib.orc_expf_raster_max_ulp.argtypes = [C.c_float, C.c_uint32]
         _lib.orc_logf.argtypes = [C.c_float]
         _lib.orc_set_threads.argtypes = [C.c_int]
+        _lib.orc_set_raster_expr.argtypes = [C.c_int]
+        _lib.orc_raster_decision_flips.argtypes = [C.c_void_p, np.ctypeslib.ndpointer(np.uint64,
+                                                                                    flags="C_CONTIGUOUS")]
         _lib.orc_get_threads.restype = C.c_int
     return _lib
+
+
+def set_raster_expr(reference: bool) -> None:
+    """Raster arithmetic of the renders and raster backwards that follow: the kernels' fused
+    form (False, the default) or the reference's expression (True: unfused calc_sigma, e^-sigma
+    correctly rounded, pix += max(c, 0) * vis; rasterize.rs:131-155)."""
+    lib().orc_set_raster_expr(int(bool(reference)))
+
+
+def raster_decision_flips(render: "RenderResult") -> dict:
+    """Pairs where the two raster arithmetics decide differently along ``render``'s trajectory."""
+    out = np.zeros(4, np.uint64)
+    lib().orc_raster_decision_flips(render._h, out)
+    return dict(pairs=int(out[0]), accept_flips=int(out[1]), early_out_flips=int(out[2]), pixels=int(out[3]))
 
 
 def set_threads(n: int) -> None:
