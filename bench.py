@@ -570,6 +570,9 @@ def run_ply(args, rank, world, local_rank):
     return line
 
 
+NATIVE_BUILD = "g++ -O3 -march=native -fopenmp -ffp-contract=off (built on the host that runs it)"
+
+
 def cpu_baseline_sample(workload="cfg2"):
     """One oracle step (all host threads) on the same workload: a full training step, or a
     forward render for the render-only workload. Returns (seconds, threads)."""
@@ -648,9 +651,9 @@ def run_reference(args, rank, world):
         return None
     from oracle import build as obuild
 
-    obuild.build()
     from oracle import oracle as orc
 
+    orc.use_library(obuild.build_native())
     orc.set_threads(os.cpu_count() or 1)
     if args.workload == "cfg3":
         return {"impl": "reference", "unavailable": "cfg3 targets are rendered by the GPU library; no CPU sample"}
@@ -688,6 +691,7 @@ def run_reference(args, rank, world):
         "data": "synthetic (seeded; no dataset)",
         "config": {"workload": WORKLOADS[args.workload]},
         "cpu_baseline": {"value": round(value, 5), "unit": unit, "cores": cores, "kind": "port",
+                         "build": NATIVE_BUILD,
                          "sample": f"one full {args.workload} {what} per timed step (CPU restatement of the "
                                    "reference algorithm; the Rust/wgpu reference cannot be built or run on this box)"},
         "e2e": {"value": round(value, 5), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -737,20 +741,27 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload != "cfg3":
         from oracle import build as obuild
 
-        obuild.build()
         from oracle import oracle as orc
 
+        orc.use_library(obuild.build_native())
         orc.set_threads(os.cpu_count() or 1)
         dt, cores = cpu_baseline_sample(args.workload)
         if args.workload == "ply":
             line["cpu_baseline"] = {"value": round(1_000_000 / dt, 1), "unit": "splats/s", "cores": cores,
-                                    "kind": "port", "sample": "the CPU restatement's decode of a 20 000-row sample "
-                                                              "of the same file, scaled to 1M splats"}
+                                    "kind": "port", "build": NATIVE_BUILD,
+                                    "sample": "the CPU restatement's decode of a 20 000-row sample "
+                                              "of the same file, scaled to 1M splats"}
         else:
             what = "forward render" if args.workload == "cfg5" else "train step"
+            # the same sample on one host thread (the restatement's loops are OpenMP-parallel)
+            orc.set_threads(1)
+            dt1, _ = cpu_baseline_sample(args.workload)
+            orc.set_threads(os.cpu_count() or 1)
             line["cpu_baseline"] = {"value": round(1.0 / dt, 5), "unit": line["unit"], "cores": cores,
-                                    "kind": "port",
-                                    "sample": f"one full {args.workload} {what} on the CPU restatement, all host threads"}
+                                    "kind": "port", "build": NATIVE_BUILD,
+                                    "value_1core": round(1.0 / dt1, 5),
+                                    "sample": f"one full {args.workload} {what} on the CPU restatement, all host "
+                                              f"threads ({cores}); value_1core: the same on one thread"}
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()

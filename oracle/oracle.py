@@ -55,14 +55,27 @@ class RefineStats(C.Structure):
                                                  "num_pruned", "num_pruned_non_finite", "total_splats")]
 
 
+_lib_path = None
+
+
+def use_library(path) -> None:
+    """Load the restatement from ``path`` (e.g. the -march=native timing build) instead of the
+    portable build; must precede the first call into the oracle."""
+    global _lib_path
+    if _lib is not None and Path(path) != Path(_lib_path or LIB):
+        raise RuntimeError("the oracle library is already loaded")
+    _lib_path = Path(path)
+
+
 def lib() -> C.CDLL:
     global _lib
     if _lib is None:
-        if not LIB.exists():
+        path = _lib_path or LIB
+        if path == LIB and not LIB.exists():
             from .build import build
 
             build()
-        _lib = C.CDLL(str(LIB))
+        _lib = C.CDLL(str(path))
         f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
         u32p = np.ctypeslib.ndpointer(np.uint32, flags="C_CONTIGUOUS")
         _lib.orc_make_project_uniforms.argtypes = [C.POINTER(_Camera), C.c_uint32, C.c_uint32, C.c_uint32,
