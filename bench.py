@@ -168,7 +168,8 @@ def build_workload(name, dev, world):
 
     if name == "cfg1":
         splats, cam, size, gt = S.config1_scene(dev, seed=1)
-        return splats, [cam], size, [gt.cpu()], bsx.TrainConfig(uniform_lr=1e-3)
+        # the configuration's step is render, loss, backward and one Adam step: no mean noise
+        return splats, [cam], size, [gt.cpu()], bsx.TrainConfig(uniform_lr=1e-3, mean_noise=False)
     if name == "cfg2":
         splats, _, size, _ = S.config2_scene(dev, seed=2)
         w, h = size
@@ -619,9 +620,13 @@ def cpu_baseline_sample(workload="cfg2"):
     vc = r.rasterize_bwd(vo)
     vt, vs, vop, _ = r.project_bwd(vc)
     n = t.shape[0]
+    new = []
     for p, gr, red in [(t.copy(), vt, False), (sh.reshape(n, -1).copy(), vs.reshape(n, -1), True),
                        (op.reshape(n, 1).copy(), vop.reshape(n, 1), False)]:
         orc.adam(p, gr, np.zeros_like(p), np.zeros(n, np.float32) if red else np.zeros_like(p), 1e-3, None, red)
+        new.append(p)
+    # the mean-noise step after the optimizer (train.rs:1095-1169), gated on this step's visibility
+    orc.mean_noise_step(new[0], new[2], r.visible, 5e-3, 1.0, 42, 1)
     return time.perf_counter() - t0, orc.threads()
 
 

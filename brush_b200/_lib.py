@@ -163,6 +163,8 @@ class DpExchange(C.Structure):
         ("epoch", C.c_uint32),
         ("timeout_ns", C.c_uint64),
         ("grad_slot_rows", C.c_uint32),
+        ("d_gate", C.c_void_p * BSX_MAX_RANKS),
+        ("gate_rows", C.c_uint32),
     ]
 
 
@@ -183,6 +185,10 @@ class TrainConfig(C.Structure):
         ("uniform_lr", C.c_float),
         ("render_mode", C.c_int32),
         ("gather_stats", C.c_int32),
+        ("mean_noise", C.c_int32),
+        ("noise_vis_gate", C.c_int32),
+        ("mean_noise_weight", C.c_float),
+        ("noise_seed", C.c_uint64),
     ]
 
 
@@ -339,6 +345,10 @@ SIGNATURES = {
         C.c_int, [C.c_void_p] + [C.c_void_p] * 6 + [C.c_uint32, C.c_int32, C.c_int32]
     ),
     "bsx_trainer_optimizer_state": (C.c_int, [C.c_void_p] + [C.POINTER(C.c_void_p)] * 6 + [C.POINTER(C.c_uint32)]),
+    "bsx_mean_noise_step": (
+        C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_float, C.c_float, C.c_uint64,
+                  C.c_uint32]
+    ),
     "bsx_radix_argsort_u32": (
         C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p]
     ),

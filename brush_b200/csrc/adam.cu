@@ -55,16 +55,22 @@ struct AdamGroupDev {
     const float* peer_grad[kMaxRanks];
 };
 
+// Rows MAX-combined over the ranks in place (refine weights, noise gate).
+struct MaxRows {
+    float* rows[kMaxRanks];  // shard base of every rank's rows (null: none)
+    uint32_t count;          // rows of this rank's shard
+    uint32_t block_begin;    // first tile of this array
+    int vec;
+};
+
 struct DpDev {
     int rank, world;
     uint32_t epoch;
     uint64_t timeout_ns;
     uint32_t* flags[kMaxRanks];
-    float* refine[kMaxRanks];  // shard base of every rank's refine rows (null: none)
-    uint32_t refine_rows;      // rows of this rank's shard
-    uint32_t refine_block_begin;
+    MaxRows mx[2];             // refine weights, noise gate
+    uint32_t refine_block_begin;  // first MAX tile (the Adam tiles come before)
     uint32_t total_tiles;
-    int refine_vec;
 };
 
 struct AdamArgs {
@@ -116,21 +122,23 @@ __device__ void signal_all_ranks(const DpDev& d, int word0) {
     if ((int)threadIdx.x < d.world) st_release_sys_u32(d.flags[threadIdx.x] + word0 + d.rank, d.epoch);
 }
 
-// MAX over ranks of this rank's refine rows, written back to every rank.
-__device__ void refine_tile(const AdamArgs& a, uint32_t tile) {
+// MAX over ranks of one tile of this rank's shard of a combined array,
+// written back to every rank.
+__device__ void max_tile(const AdamArgs& a, uint32_t t) {
     const DpDev& d = a.dp;
-    const uint32_t r0 = tile * kTileFloats;
-    const uint32_t cnt = min(kTileFloats, d.refine_rows - r0);
-    const uint32_t nvec = d.refine_vec ? cnt / 4 : 0;
+    const MaxRows& x = d.mx[(d.mx[1].count && t >= d.mx[1].block_begin) ? 1 : 0];
+    const uint32_t r0 = (t - x.block_begin) * kTileFloats;
+    const uint32_t cnt = min(kTileFloats, x.count - r0);
+    const uint32_t nvec = x.vec ? cnt / 4 : 0;
     for (uint32_t j = threadIdx.x; j < nvec; j += kAdamThreads) {
-        float4 m = __ldcg(reinterpret_cast<const float4*>(d.refine[0] + r0) + j);
-        for (int q = 1; q < d.world; ++q) m = f4max(m, __ldcg(reinterpret_cast<const float4*>(d.refine[q] + r0) + j));
-        for (int q = 0; q < d.world; ++q) reinterpret_cast<float4*>(d.refine[q] + r0)[j] = m;
+        float4 m = __ldcg(reinterpret_cast<const float4*>(x.rows[0] + r0) + j);
+        for (int q = 1; q < d.world; ++q) m = f4max(m, __ldcg(reinterpret_cast<const float4*>(x.rows[q] + r0) + j));
+        for (int q = 0; q < d.world; ++q) reinterpret_cast<float4*>(x.rows[q] + r0)[j] = m;
     }
     for (uint32_t e = nvec * 4 + threadIdx.x; e < cnt; e += kAdamThreads) {
-        float m = __ldcg(d.refine[0] + r0 + e);
-        for (int q = 1; q < d.world; ++q) m = fmaxf(m, __ldcg(d.refine[q] + r0 + e));
-        for (int q = 0; q < d.world; ++q) d.refine[q][r0 + e] = m;
+        float m = __ldcg(x.rows[0] + r0 + e);
+        for (int q = 1; q < d.world; ++q) m = fmaxf(m, __ldcg(x.rows[q] + r0 + e));
+        for (int q = 0; q < d.world; ++q) x.rows[q][r0 + e] = m;
     }
 }
 
@@ -340,7 +348,7 @@ __global__ void __launch_bounds__(kAdamThreads) dp_adam_kernel(const __grid_cons
             if (t < d.refine_block_begin)
                 adam_tile<true, kW>(a, group_of(a, t), t);
             else
-                refine_tile(a, t - d.refine_block_begin);
+                max_tile(a, t);
             __syncthreads();  // shared staging is reused by the next tile
         }
     }
@@ -447,6 +455,7 @@ extern "C" bsx_status bsx_dp_adam_step(bsx_ctx* ctx, const bsx_dp_exchange* ex, 
     for (int q = 0; q < world; ++q) {
         if (!ex->d_flags[q]) return fail(ctx, BSX_ERR_INVALID_ARG, "null flag words");
         if (ex->refine_rows && !ex->d_refine[q]) return fail(ctx, BSX_ERR_INVALID_ARG, "null refine buffer");
+        if (ex->gate_rows && !ex->d_gate[q]) return fail(ctx, BSX_ERR_INVALID_ARG, "null gate buffer");
     }
     cudaSetDevice(ctx->device);
     AdamArgs a;
@@ -494,21 +503,24 @@ extern "C" bsx_status bsx_dp_adam_step(bsx_ctx* ctx, const bsx_dp_exchange* ex, 
         blocks += nb;
     }
     d.refine_block_begin = blocks;
-    d.refine_rows = 0;
-    d.refine_vec = 1;
-    for (int q = 0; q < kMaxRanks; ++q) {
-        d.flags[q] = q < world ? ex->d_flags[q] : nullptr;
-        d.refine[q] = nullptr;
-    }
-    if (ex->refine_rows) {
+    for (int q = 0; q < kMaxRanks; ++q) d.flags[q] = q < world ? ex->d_flags[q] : nullptr;
+    float* const* srcs[2] = {ex->d_refine, ex->d_gate};
+    const uint32_t counts[2] = {ex->refine_rows, ex->gate_rows};
+    for (int k = 0; k < 2; ++k) {
+        MaxRows& x = d.mx[k];
+        x.count = 0;
+        x.vec = 1;
+        x.block_begin = blocks;
+        for (int q = 0; q < kMaxRanks; ++q) x.rows[q] = nullptr;
+        if (!counts[k]) continue;
         uint32_t rb, re;
-        shard(ex->refine_rows, &rb, &re);
-        d.refine_rows = re - rb;
+        shard(counts[k], &rb, &re);
+        x.count = re - rb;
         for (int q = 0; q < world; ++q) {
-            d.refine[q] = ex->d_refine[q] + rb;
-            d.refine_vec = d.refine_vec && aligned16(d.refine[q]);
+            x.rows[q] = srcs[k][q] + rb;
+            x.vec = x.vec && aligned16(x.rows[q]);
         }
-        blocks += (d.refine_rows + kTileFloats - 1) / kTileFloats;
+        blocks += (x.count + kTileFloats - 1) / kTileFloats;
     }
     d.total_tiles = blocks;
     // Persistent grid: at most one wave of resident blocks; every rank launches

@@ -33,19 +33,69 @@ namespace {
 
 constexpr int kStatsThreads = 256;
 
+// The mean-noise injection of one step (train.rs:1095-1169), applied after
+// AdamScaled: the per-splat arithmetic is bsx_mean_noise (bsx_fmath.h).
+struct NoiseArgs {
+    float* transforms;      // [N,10], means moved in place
+    const float* raw_opac;  // [N], after this step's update
+    const float* gate;      // > 0 where the splat may move; null: the visibility statistic just accumulated
+    float scale, limit;     // f32(lr_mean) * mean_noise_weight, median bounds size
+    uint64_t seed;
+    uint32_t step;
+};
+
+__device__ __forceinline__ void noise_row(const NoiseArgs& z, uint32_t i, float gate_src) {
+    if (!(gate_src > 0.0f)) return;
+    float* m = z.transforms + (size_t)i * 10;
+    float mean[3] = {m[0], m[1], m[2]};
+    if (bsx_mean_noise(__ldg(z.raw_opac + i), 1.0f, z.scale, z.limit, z.seed, z.step, i, mean)) {
+        m[0] = mean[0];
+        m[1] = mean[1];
+        m[2] = mean[2];
+    }
+}
+
 // RefineRecord::gather_stats (stats.rs:111-121): running MAX of the refine
 // weight, SUM of visibility, MAX of the screen-space radius; without a refine
-// weight (refine == null) gather_aux_stats (stats.rs:123-127).
+// weight (refine == null) gather_aux_stats (stats.rs:123-127). With NOISE the
+// same pass applies the mean noise, gated on the visibility sum it has just
+// written (the reference's RefineRecord::vis_mask gate) unless a gate array is
+// given.
+template <bool STATS, bool NOISE>
 __global__ void __launch_bounds__(kStatsThreads)
     gather_stats_kernel(const float* __restrict__ refine, const float* __restrict__ visible,
                         const float* __restrict__ radius, uint32_t n, float* __restrict__ rmax,
-                        float* __restrict__ vsum, float* __restrict__ smax) {
+                        float* __restrict__ vsum, float* __restrict__ smax, const NoiseArgs nz) {
     for (uint32_t i = blockIdx.x * kStatsThreads + threadIdx.x; i < n; i += gridDim.x * kStatsThreads) {
-        if (refine) rmax[i] = bsx_max(rmax[i], refine[i]);
-        vsum[i] = vsum[i] + visible[i];
-        smax[i] = bsx_max(smax[i], radius[i]);
+        float vs = 0.0f;
+        if (STATS) {
+            if (refine) rmax[i] = bsx_max(rmax[i], refine[i]);
+            vs = vsum[i] + visible[i];
+            vsum[i] = vs;
+            smax[i] = bsx_max(smax[i], radius[i]);
+        }
+        if (NOISE) noise_row(nz, i, nz.gate ? __ldg(nz.gate + i) : vs);
     }
 }
+
+// Data-parallel steps: this rank's share of the noise gate, before the ranks'
+// gates are MAX-combined by the exchange: 1 where the splat was visible in this
+// step, or (accum) where the visibility sum including this step is positive.
+__global__ void __launch_bounds__(kStatsThreads)
+    noise_gate_kernel(const float* __restrict__ visible, const float* __restrict__ vsum, uint32_t n,
+                      float* __restrict__ gate) {
+    for (uint32_t i = blockIdx.x * kStatsThreads + threadIdx.x; i < n; i += gridDim.x * kStatsThreads) {
+        const float v = vsum ? vsum[i] + visible[i] : visible[i];
+        gate[i] = v > 0.0f ? 1.0f : 0.0f;
+    }
+}
+
+__global__ void __launch_bounds__(kStatsThreads) mean_noise_kernel(uint32_t n, const NoiseArgs nz) {
+    for (uint32_t i = blockIdx.x * kStatsThreads + threadIdx.x; i < n; i += gridDim.x * kStatsThreads)
+        noise_row(nz, i, __ldg(nz.gate + i));
+}
+
+uint32_t stats_blocks(uint32_t n) { return std::min<uint32_t>((n + kStatsThreads - 1) / kStatsThreads, 148 * 8); }
 
 size_t grad_floats(uint32_t n, uint32_t c) { return (size_t)n * (11 + 3 * (size_t)c); }
 
@@ -138,13 +188,52 @@ bsx_status forward_backward(bsx_trainer* tr, const bsx_camera* cam, uint32_t w, 
     return bsx_project_bwd(ctx, tr->v_combined.as<float>(), vt, vs, vo, vr);
 }
 
-bsx_status gather_stats(bsx_trainer* tr, const float* refine, const bsx_render_out& out) {
-    if (!tr->cfg.gather_stats || tr->n == 0) return BSX_OK;
-    float* st = tr->stats.as<float>();
-    const uint32_t blocks = std::min<uint32_t>((tr->n + kStatsThreads - 1) / kStatsThreads, 148 * 8);
+// Whether this step injects mean noise: configured, and the bounds are valid
+// (train.rs:1098: a finite, positive median size).
+bool noise_on(const bsx_trainer* tr) {
+    const float ms = tr->cfg.median_scale;
+    return tr->cfg.mean_noise && bsx_is_finite(ms) && ms > 0.0f && tr->n > 0;
+}
+
+NoiseArgs noise_args(const bsx_trainer* tr, float* transforms, const float* raw_opac, const float* gate,
+                     float lr_mean) {
+    NoiseArgs z;
+    z.transforms = transforms;
+    z.raw_opac = raw_opac;
+    z.gate = gate;
+    z.scale = lr_mean * tr->cfg.mean_noise_weight;
+    z.limit = tr->cfg.median_scale;
+    z.seed = tr->cfg.noise_seed;
+    z.step = tr->step;
+    return z;
+}
+
+// The step's epilogue: RefineRecord statistics and the mean noise in one pass.
+// gate: the noise gate array (null: the statistic's visibility sum when the
+// accumulated gate is configured, else this step's visible[]).
+bsx_status step_epilogue(bsx_trainer* tr, const float* refine, const bsx_render_out& out, float* transforms,
+                         const float* raw_opac, const float* gate, float lr_mean) {
+    const bool stats = tr->cfg.gather_stats != 0, noise = noise_on(tr);
+    if ((!stats && !noise) || tr->n == 0) return BSX_OK;
+    if (noise && !gate && !(stats && tr->cfg.noise_vis_gate)) gate = out.d_visible;
+    const NoiseArgs nz = noise ? noise_args(tr, transforms, raw_opac, gate, lr_mean) : NoiseArgs{};
+    float* st = stats ? tr->stats.as<float>() : nullptr;
+    const size_t n = tr->n;
+    float* rmax = st;
+    float* vsum = st ? st + n : nullptr;
+    float* smax = st ? st + 2 * n : nullptr;
+    const uint32_t blocks = stats_blocks(tr->n);
+    cudaStream_t s = tr->ctx->stream;
     prof_begin(tr->ctx);
-    gather_stats_kernel<<<blocks, kStatsThreads, 0, tr->ctx->stream>>>(refine, out.d_visible, out.d_max_radius, tr->n,
-                                                                       st, st + tr->n, st + 2 * (size_t)tr->n);
+    if (stats && noise)
+        gather_stats_kernel<true, true><<<blocks, kStatsThreads, 0, s>>>(refine, out.d_visible, out.d_max_radius,
+                                                                         tr->n, rmax, vsum, smax, nz);
+    else if (stats)
+        gather_stats_kernel<true, false><<<blocks, kStatsThreads, 0, s>>>(refine, out.d_visible, out.d_max_radius,
+                                                                          tr->n, rmax, vsum, smax, nz);
+    else
+        gather_stats_kernel<false, true><<<blocks, kStatsThreads, 0, s>>>(refine, out.d_visible, out.d_max_radius,
+                                                                          tr->n, rmax, vsum, smax, nz);
     return post_launch(tr->ctx, "gather_stats_kernel");
 }
 
@@ -384,7 +473,7 @@ bsx_status bsx_train_step(bsx_trainer* tr, const bsx_camera* cam, uint32_t w, ui
     bsx_render_out out{};
     s = forward_backward(tr, cam, w, h, gt, transforms, sh, opac, vt, vs, vo, vr, refine, d_loss, &out, &fa);
     if (s != BSX_OK) return s;
-    s = gather_stats(tr, refine ? vr : nullptr, out);
+    s = step_epilogue(tr, refine ? vr : nullptr, out, transforms, opac, nullptr, r.lr_mean);
     if (s != BSX_OK) return s;
     if (stats) {
         stats->num_visible = out.num_visible;
@@ -463,10 +552,26 @@ bsx_status bsx_train_step_dp(bsx_trainer* tr, const bsx_camera* cam, uint32_t w,
     e.refine_rows = refine ? tr->n : 0;
     e.epoch = ++tr->dp_epoch;
     e.grad_slot_rows = push ? slot : 0;
+    // The noise moves a splat where any rank's gate is set, so that every
+    // replica applies the same update: this rank's gate goes into its exchange
+    // row and the exchange combines the ranks' gates by MAX.
+    const bool noise = noise_on(tr);
+    e.gate_rows = 0;
+    if (noise) {
+        if (!ex->d_gate[rank]) return fail(ctx, BSX_ERR_INVALID_ARG, "the mean noise needs gate buffers");
+        const float* vsum = (tr->cfg.gather_stats && tr->cfg.noise_vis_gate) ? tr->stats.as<float>() + tr->n : nullptr;
+        prof_begin(ctx);
+        noise_gate_kernel<<<stats_blocks(tr->n), kStatsThreads, 0, ctx->stream>>>(out.d_visible, vsum, tr->n,
+                                                                                 ex->d_gate[rank]);
+        s = post_launch(ctx, "noise_gate_kernel");
+        if (s != BSX_OK) return s;
+        e.gate_rows = tr->n;
+    }
     const bsx_adam_cfg ac{0.9f, 0.999f, 1e-15f, tr->step, 1.0f / (float)world};
     s = bsx_dp_adam_step(ctx, &e, g, 3, &ac);
     if (s != BSX_OK) return s;
-    s = gather_stats(tr, refine ? ex->d_refine[rank] : nullptr, out);
+    s = step_epilogue(tr, refine ? ex->d_refine[rank] : nullptr, out, sp->d_transforms[rank], sp->d_raw_opac[rank],
+                      noise ? ex->d_gate[rank] : nullptr, r.lr_mean);
     if (s != BSX_OK) return s;
     if (stats) {
         stats->num_visible = out.num_visible;
@@ -475,6 +580,25 @@ bsx_status bsx_train_step_dp(bsx_trainer* tr, const bsx_camera* cam, uint32_t w,
         stats->step = tr->step;
     }
     return BSX_OK;
+}
+
+bsx_status bsx_mean_noise_step(bsx_ctx* ctx, float* d_transforms, const float* d_raw_opac, const float* d_gate,
+                               uint32_t n, float scale, float limit, uint64_t seed, uint32_t step) {
+    if (!ctx) return BSX_ERR_INVALID_ARG;
+    if (n == 0) return BSX_OK;
+    if (!d_transforms || !d_raw_opac || !d_gate) return BSX_ERR_INVALID_ARG;
+    cudaSetDevice(ctx->device);
+    NoiseArgs z;
+    z.transforms = d_transforms;
+    z.raw_opac = d_raw_opac;
+    z.gate = d_gate;
+    z.scale = scale;
+    z.limit = limit;
+    z.seed = seed;
+    z.step = step;
+    prof_begin(ctx);
+    mean_noise_kernel<<<stats_blocks(n), kStatsThreads, 0, ctx->stream>>>(n, z);
+    return post_launch(ctx, "mean_noise_kernel");
 }
 
 }  // extern "C"

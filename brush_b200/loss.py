@@ -46,8 +46,8 @@ def image_loss_forward(pred_chw: torch.Tensor, gt_packed: torch.Tensor, cfg: Ima
     ctx = context(pred_chw.device.index)
     out = torch.empty_like(pred_chw)
     cfgc = cfg.to_c()
-    ctx.check(_lib.lib().bsx_loss_fwd(ctx.handle, ptr(pred_chw.contiguous()), ptr(gt), w, h, c, C.byref(cfgc),
-                                      ptr(out)))
+    pred = pred_chw.contiguous()  # held until the call returns
+    ctx.check(_lib.lib().bsx_loss_fwd(ctx.handle, ptr(pred), ptr(gt), w, h, c, C.byref(cfgc), ptr(out)))
     return out
 
 
@@ -59,8 +59,9 @@ def image_loss_backward(pred_chw: torch.Tensor, gt_packed: torch.Tensor, dl_dmap
     ctx = context(pred_chw.device.index)
     out = torch.empty_like(pred_chw)
     cfgc = cfg.to_c()
-    ctx.check(_lib.lib().bsx_loss_bwd(ctx.handle, ptr(pred_chw.contiguous()), ptr(gt), w, h, c, C.byref(cfgc),
-                                      ptr(dl_dmap.contiguous()), ptr(out)))
+    # both held until the call returns: a temporary freed early could share memory with the other
+    pred, dl = pred_chw.contiguous(), dl_dmap.contiguous()
+    ctx.check(_lib.lib().bsx_loss_bwd(ctx.handle, ptr(pred), ptr(gt), w, h, c, C.byref(cfgc), ptr(dl), ptr(out)))
     return out
 
 

@@ -2,7 +2,8 @@
 
 Each rank owns one exchange region (library-allocated device memory exported
 with CUDA IPC and mapped by every other rank of the node) holding the splat
-parameters, their gradients, the refine weights and the exchange flag words.
+parameters, their gradients, the refine weights, the mean-noise gate and the
+exchange flag words.
 ``bsx_dp_adam_step`` then replaces "all-reduce gradients, Adam, keep replicas
 in sync": rank ``r`` sums the gradient rows of its shard over every rank in
 rank order, applies AdamScaled with its shard's moments, and stores the new
@@ -55,6 +56,8 @@ class ExchangeLayout:
                 self.offsets[(kind, name)] = off
                 off = _up(off + (n if kind == "param" else grad_rows) * w)
         self.offsets["refine"] = off
+        off = _up(off + n)
+        self.offsets["gate"] = off  # the mean-noise gate (MAX-combined like the refine weights)
         off = _up(off + n)
         self.offsets["flags"] = off
         off = _up(off + _lib.BSX_DP_FLAG_WORDS)
@@ -169,6 +172,7 @@ class PeerExchange:
         for q in range(self.world):
             ex.d_flags[q] = self._ptr(q, "flags")
             ex.d_refine[q] = self._ptr(q, "refine")
+            ex.d_gate[q] = self._ptr(q, "gate")
             sp.d_transforms[q] = self._ptr(q, ("param", "transforms"))
             sp.d_sh_coeffs[q] = self._ptr(q, ("param", "sh"))
             sp.d_raw_opac[q] = self._ptr(q, ("param", "opac"))

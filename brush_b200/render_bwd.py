@@ -31,7 +31,8 @@ def rasterize_bwd(v_output: torch.Tensor, compute_refine_weight: bool = True,
     n = ctx.last_n
     if v_combined is None:
         v_combined = torch.empty((max(n, 1), _lib.BSX_GRAD_STRIDE), device=v_output.device, dtype=torch.float32)
-    ctx.check(_lib.lib().bsx_rasterize_bwd(ctx.handle, ptr(v_output.contiguous()), int(compute_refine_weight),
+    v_output = v_output.contiguous()  # held until the call returns: the kernel reads it asynchronously
+    ctx.check(_lib.lib().bsx_rasterize_bwd(ctx.handle, ptr(v_output), int(compute_refine_weight),
                                            ptr(v_combined)))
     return v_combined
 
@@ -69,10 +70,13 @@ def rasterize_bwd_ref(out_img: torch.Tensor, projected_splats: torch.Tensor, com
     w, h = int(img_size[0]), int(img_size[1])
     v_combined = torch.empty((v, _lib.BSX_COMPACT_GRAD_LANES), device=out_img.device, dtype=torch.float32)
     bg = (C.c_float * 3)(*[float(x) for x in background])
+    # contiguous copies are held in locals until the call returns: freed earlier, the
+    # allocator could hand one's memory to the next before the kernels read it
     ids = compact_gid_from_isect.contiguous()
-    ctx.check(_lib.lib().bsx_rasterize_bwd_ref(ctx.handle, ptr(out_img.contiguous()), ptr(projected_splats.contiguous()),
-                                               v, ptr(ids), int(ids.numel()), ptr(tile_offsets.contiguous()), bg, w, h,
-                                               ptr(v_output.contiguous()), int(smooth_cutoff),
+    img, rows, off, vout = (x.contiguous() for x in (out_img, projected_splats, tile_offsets, v_output))
+    ctx.check(_lib.lib().bsx_rasterize_bwd_ref(ctx.handle, ptr(img), ptr(rows),
+                                               v, ptr(ids), int(ids.numel()), ptr(off), bg, w, h,
+                                               ptr(vout), int(smooth_cutoff),
                                                int(compute_refine_weight), int(render_depth), ptr(v_combined)))
     return v_combined
 
@@ -91,9 +95,11 @@ def project_bwd_ref(transforms: torch.Tensor, sh_coeffs: torch.Tensor, raw_opac:
     d = transforms.device
     out = SplatGrads(torch.empty((n, 10), device=d), torch.empty((n, c, 3), device=d), torch.empty((n,), device=d),
                      torch.empty((n,), device=d))
-    ctx.check(_lib.lib().bsx_project_bwd_ref(ctx.handle, ptr(transforms.contiguous()), ptr(sh_coeffs.contiguous()),
-                                             ptr(raw_opac.contiguous()), n, c, ptr(global_from_compact_gid.contiguous()),
+    t, sh, op, gid, vc = (x.contiguous() for x in (transforms, sh_coeffs, raw_opac, global_from_compact_gid,
+                                                   v_combined))
+    ctx.check(_lib.lib().bsx_project_bwd_ref(ctx.handle, ptr(t), ptr(sh),
+                                             ptr(op), n, c, ptr(gid),
                                              v, C.byref(project_uniforms), int(render_mode),
-                                             ptr(v_combined.contiguous()), ptr(out.v_transforms), ptr(out.v_coeffs),
+                                             ptr(vc), ptr(out.v_transforms), ptr(out.v_coeffs),
                                              ptr(out.v_raw_opac), ptr(out.v_refine_weight)))
     return out

@@ -12,9 +12,9 @@ a native trainer owning gradients, moments, schedules and statistics). The
 NCCL alternative (``exchange="nccl"``) orchestrates the same kernels from
 here around reduce-scatter / all-gather (brush_b200.dist).
 
-Not applied: the reference's random mean-noise injection after Adam
-(train.rs:1095-1169); it draws from a non-reproducible RNG stream and is
-outside the parity contract.
+The reference's mean-noise injection after Adam (train.rs:1095-1169) is
+applied (TrainConfig.mean_noise, on by default) with normals from a
+counter-based generator, so it is reproducible; the parity tests switch it off.
 """
 from __future__ import annotations
 
@@ -53,6 +53,16 @@ class TrainConfig:
     # A single learning rate for every parameter (benchmark configuration 1:
     # "one Adam step, lr 1e-3"); None selects the reference table above.
     uniform_lr: float | None = None
+    # Mean-noise injection after the optimizer step (train.rs:1095-1169), on by default
+    # like the reference: low-opacity splats' means move by N(0,1) * (1-opacity)^150 *
+    # lr_mean * mean_noise_weight (clamped to the median bounds size). With
+    # mrnf_noise_injection (default) only splats visible since the last refine move,
+    # otherwise only those visible in this step. Drawn from a counter-based generator
+    # seeded by noise_seed, so runs are reproducible and data-parallel replicas agree.
+    mean_noise: bool = True
+    mean_noise_weight: float = 50.0
+    mrnf_noise_injection: bool = True
+    noise_seed: int = 42
 
     def to_c(self, median_scale: float, render_mode: int, gather_stats: bool) -> _lib.TrainConfig:
         c = _lib.TrainConfig()
@@ -68,6 +78,10 @@ class TrainConfig:
         c.uniform_lr = float(self.uniform_lr) if self.uniform_lr is not None else 0.0
         c.render_mode = int(render_mode)
         c.gather_stats = int(gather_stats)
+        c.mean_noise = int(self.mean_noise)
+        c.noise_vis_gate = int(self.mrnf_noise_injection)
+        c.mean_noise_weight = float(self.mean_noise_weight)
+        c.noise_seed = int(self.noise_seed)
         return c
 
 
@@ -126,7 +140,9 @@ class RefineRecord:
         return RefineRecord(z(), z(), z())
 
     def gather_stats(self, refine_weight, visible, screen_radius) -> None:
-        torch.maximum(self.refine_weight_norm, refine_weight, out=self.refine_weight_norm)
+        """gather_stats (stats.rs:111-121); without a refine weight gather_aux_stats (:123-127)."""
+        if refine_weight is not None:
+            torch.maximum(self.refine_weight_norm, refine_weight, out=self.refine_weight_norm)
         self.vis_weight.add_(visible)
         torch.maximum(self.max_screen_size, screen_radius, out=self.max_screen_size)
 
@@ -364,9 +380,30 @@ class SplatTrainer:
         self.adam.step(self.groups, grad_scale=grad_scale)
         if self.sharded:
             all_gather_rows(full_params, self.pg, self.rank, self.world)
-        if self.record is not None and compute_refine_weight:
-            self.record.gather_stats(self.grads.v_refine_weight, out.aux.visible, out.aux.max_radius)
+        if self.record is not None:
+            self.record.gather_stats(self.grads.v_refine_weight if compute_refine_weight else None, out.aux.visible,
+                                     out.aux.max_radius)
+        self._mean_noise(splats, out.aux.visible, lr_mean)
         return TrainStepStats(out.aux.num_visible, out.aux.num_intersections, self.loss, lr_mean)
+
+    def _mean_noise(self, splats: Splats, visible: torch.Tensor, lr_mean: float) -> None:
+        """The mean-noise step after the optimizer (train.rs:1095-1169) through the operator
+        bsx_mean_noise_step; every rank gates on the MAX of the ranks' gates, so replicas agree."""
+        cfg = self.config
+        ms = np.float32(self.median_scale)
+        if not cfg.mean_noise or not (np.isfinite(ms) and ms > 0):
+            return
+        if cfg.mrnf_noise_injection and self.record is not None:
+            gate = (self.record.vis_weight > 0).float()
+        else:
+            gate = visible.clone()
+        if self.world > 1:
+            torch.distributed.all_reduce(gate, op=torch.distributed.ReduceOp.MAX, group=self.pg)
+        scale = np.float32(np.float32(lr_mean) * np.float32(cfg.mean_noise_weight))
+        ctx = context(splats.transforms.device)
+        ctx.check(_lib.lib().bsx_mean_noise_step(ctx.handle, ptr(splats.transforms), ptr(splats.raw_opacities),
+                                                 ptr(gate), self.n, float(scale), float(ms), int(cfg.noise_seed),
+                                                 int(self.step_count)))
 
     def reserve(self, max_splats: int, splats: Splats) -> None:
         """Allocate up front for a run that grows to ``max_splats`` (single-GPU native trainer):

@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define BSX_ABI_VERSION 5
+#define BSX_ABI_VERSION 6
 /* Gradient lanes per splat written by the raster backward:
  * xy(2) conic(3) rgb(3) alpha refine depth. Reference:
  * crates/brush-render-bwd/src/kernels/rasterize_backwards.rs:40 */
@@ -309,6 +309,9 @@ typedef struct bsx_dp_exchange {
                                           * holds world slots of this rank's shard, the gradient of
                                           * rank s for shard row i at row s * grad_slot_rows + i
                                           * (filled by the ranks themselves; see bsx_train_step_dp) */
+    float* d_gate[BSX_MAX_RANKS];        /* optional [gate_rows] per rank, MAX-combined in place like
+                                          * d_refine (the mean-noise visibility gate; NULL: none) */
+    uint32_t gate_rows;
 } bsx_dp_exchange;
 
 /* One kernel in place of "all-reduce the gradients, then bsx_adam_step": rank
@@ -332,9 +335,9 @@ BSX_API bsx_status bsx_dp_adam_step(bsx_ctx* ctx, const bsx_dp_exchange* ex, con
  * refine statistics. One bsx_train_step = backward-pass render -> fused
  * SSIM+L1 loss and its gradient -> raster backward -> projection backward ->
  * fused AdamScaled over transforms / SH / opacity with the reference's rate
- * table (train.rs:964-1051) -> refine statistics (stats.rs:111-121), all on
- * the context's stream. The random mean-noise injection after Adam
- * (train.rs:1095-1169) is not applied. */
+ * table (train.rs:964-1051) -> refine statistics (stats.rs:111-121) -> the
+ * mean-noise injection (train.rs:1095-1169, see mean_noise), all on the
+ * context's stream. */
 typedef struct bsx_train_config {        /* TrainConfig subset (crates/brush-train/src/config.rs:15-136) */
     uint32_t total_train_iters;          /* 30000 */
     double lr_mean, lr_mean_end;         /* 2e-5, 2e-7 (scaled by median_scale) */
@@ -349,6 +352,20 @@ typedef struct bsx_train_config {        /* TrainConfig subset (crates/brush-tra
     float uniform_lr;                    /* > 0: this rate for every parameter, no schedule */
     int32_t render_mode;                 /* bsx_render_mode */
     int32_t gather_stats;                /* 1: keep the RefineRecord statistics */
+    /* Mean-noise injection after AdamScaled (train.rs:1095-1169; on by default in
+     * the reference). Each splat's mean moves by clamp(n * w * lr_mean *
+     * mean_noise_weight, +-median_scale), n ~ N(0,1) per coordinate, w =
+     * clamp((1 - opacity)^150, 0, 1) times a visibility gate: with noise_vis_gate
+     * (the reference's default mrnf_noise_injection) the RefineRecord visibility
+     * accumulated since the last refine (this step's visible[] when gather_stats
+     * is off), otherwise this step's visible[]; skipped unless median_scale is
+     * finite and positive. The normals come from a counter-based generator
+     * (SplitMix64 of noise_seed, the optimizer step and the splat index, Box-Muller),
+     * so a step is reproducible and equal on every data-parallel rank. */
+    int32_t mean_noise;                  /* 1: inject */
+    int32_t noise_vis_gate;              /* 1: accumulated visibility (mrnf_noise_injection), 0: this step's */
+    float mean_noise_weight;             /* 50 */
+    uint64_t noise_seed;
 } bsx_train_config;
 
 typedef struct bsx_train_stats {
@@ -483,6 +500,17 @@ BSX_API bsx_status bsx_trainer_load_optimizer_state(bsx_trainer* tr, const float
                                                     int32_t rank);
 /* Rate schedule input after the bounds change (train.rs:656: lr_mean uses bounds.median_size()). */
 BSX_API bsx_status bsx_trainer_set_median_scale(bsx_trainer* tr, float median_scale);
+
+/* The mean-noise step of SplatTrainer::step_with_refine_weight (train.rs:1095-1169)
+ * as an operator, in place on the means of d_transforms [N,10]: for splat i with
+ * d_gate[i] > 0, mean += clamp(n * w * scale, -limit, limit), n ~ N(0,1) from
+ * (seed, step, i) as bsx_train_config describes, w = clamp((1 -
+ * sigmoid(d_raw_opac[i]))^150, 0, 1), scale = f32(lr_mean) * mean_noise_weight,
+ * limit = the median bounds size. The trainer applies the same arithmetic inside
+ * its step; this entry point serves steps composed from the operators. */
+BSX_API bsx_status bsx_mean_noise_step(bsx_ctx* ctx, float* d_transforms, const float* d_raw_opac,
+                                       const float* d_gate, uint32_t num_splats, float scale, float limit,
+                                       uint64_t seed, uint32_t step);
 
 /* ---- primitives: brush-sort / brush-prefix-sum / get_tile_offsets ---- */
 /* Stable argsort by key & mask(bits rounded up to a multiple of 4), as

@@ -252,4 +252,100 @@ BSX_HD float bsx_atan2f(float y, float x) {
 /* Logistic sigmoid, same expression as the reference: 1 / (1 + e^-x). */
 BSX_HD float bsx_sigmoid(float x) { return 1.0f / (1.0f + bsx_expf(-x)); }
 
+/* b^e for an integer exponent by binary exponentiation (square-and-multiply,
+ * least significant bit first): a fixed operation sequence for every e. */
+BSX_HD float bsx_powi(float b, uint32_t e) {
+    float r = 1.0f;
+    while (e) {
+        if (e & 1u) r = r * b;
+        e >>= 1;
+        if (e) b = b * b;
+    }
+    return r;
+}
+
+/* SplitMix64 (Steele, Lea, Flood 2014): a 64-bit counter hash. */
+BSX_HD uint64_t bsx_splitmix64(uint64_t x) {
+    uint64_t z = x + 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+/* sin(2 pi u) and cos(2 pi u) for u in [0, 1). The turn is split into eighths
+ * exactly (8u, its integer part q and fraction f are exact in float); an odd
+ * eighth is mirrored (f -> 1 - f, exact), so the remaining angle a = f pi/4 lies
+ * in [0, pi/4], where the Maclaurin series of sin to a^11 and cos to a^12 are
+ * within 2e-11 of the exact values; the eighth then selects sign and
+ * sin / cos swap. */
+BSX_HD void bsx_sincos_2pi(float u, float* s, float* c) {
+    const float y = u * 8.0f;
+    const int q = (int)y;
+    float f = y - (float)q;
+    if (q & 1) f = 1.0f - f;
+    const float a = f * 0.7853981852531433f; /* pi/4 */
+    const float a2 = a * a;
+    float ps = -2.505210838544172e-08f;          /* -1/11! */
+    ps = bsx_fma(ps, a2, 2.755731922398589e-06f); /* 1/9! */
+    ps = bsx_fma(ps, a2, -1.9841270114481449e-04f); /* -1/7! */
+    ps = bsx_fma(ps, a2, 8.333333767950535e-03f);  /* 1/5! */
+    ps = bsx_fma(ps, a2, -0.1666666716337204f);    /* -1/3! */
+    const float sa = bsx_fma(a * a2, ps, a);
+    float pc = 2.08767569878681e-09f;              /* 1/12! */
+    pc = bsx_fma(pc, a2, -2.755731922398589e-07f); /* -1/10! */
+    pc = bsx_fma(pc, a2, 2.4801587642286904e-05f); /* 1/8! */
+    pc = bsx_fma(pc, a2, -1.3888889225199819e-03f); /* -1/6! */
+    pc = bsx_fma(pc, a2, 0.0416666679084301f);     /* 1/4! */
+    pc = bsx_fma(pc, a2, -0.5f);
+    const float ca = bsx_fma(a2, pc, 1.0f);
+    /* within the quadrant: even eighth -> (sin a, cos a); odd -> (cos a', sin a') */
+    const float sq = (q & 1) ? ca : sa, cq = (q & 1) ? sa : ca;
+    switch ((q >> 1) & 3) {
+        case 0: *s = sq; *c = cq; break;
+        case 1: *s = cq; *c = -sq; break;
+        case 2: *s = -sq; *c = -cq; break;
+        default: *s = -cq; *c = sq; break;
+    }
+}
+
+/* Three standard normal variates for (seed, step, splat index), by the
+ * Box-Muller transform of two counter-hashed uniform pairs
+ * (u1 in (0, 1], u2 in [0, 1), 24 bits each): r = sqrt(-2 ln u1),
+ * (r cos 2 pi u2, r sin 2 pi u2). Deterministic and identical on the host and
+ * the device. */
+BSX_HD void bsx_normal3(uint64_t seed, uint32_t step, uint32_t index, float z[3]) {
+    const uint64_t base = bsx_splitmix64(seed ^ ((uint64_t)step << 32));
+    for (int pair = 0; pair < 2; ++pair) {
+        const uint64_t h = bsx_splitmix64(base ^ bsx_splitmix64(((uint64_t)index << 1) | (uint64_t)pair));
+        const float u1 = (float)((h >> 40) + 1) * 5.9604644775390625e-08f;         /* (0, 1] */
+        const float u2 = (float)((h >> 16) & 0xFFFFFFull) * 5.9604644775390625e-08f; /* [0, 1) */
+        const float r = sqrtf(-2.0f * bsx_logf(u1));
+        float sn, cs;
+        bsx_sincos_2pi(u2, &sn, &cs);
+        if (pair == 0) {
+            z[0] = r * cs;
+            z[1] = r * sn;
+        } else {
+            z[2] = r * cs;
+        }
+    }
+}
+
+/* The mean-noise step of one splat (crates/brush-train/src/train.rs:1095-1169):
+ * w = clamp((1 - sigmoid(raw_opac))^150, 0, 1) * gate, gate in {0, 1};
+ * each mean coordinate moves by clamp(n_k * (w * scale), -limit, limit), with
+ * scale = f32(lr_mean) * mean_noise_weight and limit = the median bounds size.
+ * Returns 0 (means unchanged) where the weight is zero. */
+BSX_HD int bsx_mean_noise(float raw_opac, float gate, float scale, float limit, uint64_t seed, uint32_t step,
+                          uint32_t index, float mean[3]) {
+    const float inv = 1.0f - bsx_sigmoid(raw_opac);
+    const float w = bsx_clamp(bsx_powi(inv, 150u), 0.0f, 1.0f) * gate;
+    if (!(w != 0.0f)) return 0;
+    const float wm = w * scale;
+    float z[3];
+    bsx_normal3(seed, step, index, z);
+    for (int k = 0; k < 3; ++k) mean[k] = mean[k] + bsx_clamp(z[k] * wm, -limit, limit);
+    return 1;
+}
+
 #endif /* BSX_FMATH_H */

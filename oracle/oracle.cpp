@@ -1548,6 +1548,51 @@ double orc_expf_raster_max_ulp(float lo, uint32_t stride) {
 
 void orc_set_raster_expr(int mode) { g_raster_expr = mode ? 1 : 0; }
 
+// The mean-noise injection after the optimizer step (train.rs:1095-1169), in the
+// reference's tensor order over every splat: inv = 1 - sigmoid(raw);
+// noise_weight = clamp(inv^150, 0, 1) * gate (gate = 1 where d_gate > 0);
+// noise_weight_means = noise_weight * scale (scale = f32(lr_mean) *
+// mean_noise_weight); means += clamp(n * noise_weight_means, -limit, limit).
+// The normals n are bsx_normal3(seed, step, i) (the library's counter-based
+// generator; the reference draws from its device RNG).
+void orc_mean_noise_step(float* transforms, const float* raw_opac, const float* gate, uint32_t n, float scale,
+                         float limit, uint64_t seed, uint32_t step) {
+#pragma omp parallel for schedule(static)
+    for (int64_t gi = 0; gi < (int64_t)n; ++gi) {
+        const uint32_t i = (uint32_t)gi;
+        const float inv = 1.0f - bsx_sigmoid(raw_opac[i]);
+        const float nw = bsx_clamp(bsx_powi(inv, 150u), 0.0f, 1.0f) * (gate[i] > 0.0f ? 1.0f : 0.0f);
+        const float nwm = nw * scale;
+        float z[3];
+        bsx_normal3(seed, step, i, z);
+        for (int k = 0; k < 3; ++k) transforms[(size_t)i * 10 + k] += bsx_clamp(z[k] * nwm, -limit, limit);
+    }
+}
+
+void orc_sincos_2pi(float u, float* s, float* c) { bsx_sincos_2pi(u, s, c); }
+// Largest |error| of bsx_sincos_2pi over every u = k / 2^24 (the generator's
+// uniforms) against the double-precision sin / cos: out = {sin, cos}.
+void orc_sincos_2pi_max_err(double out[2]) {
+    double es = 0.0, ec = 0.0;
+#pragma omp parallel for schedule(static) reduction(max : es, ec)
+    for (int64_t k = 0; k < (1 << 24); ++k) {
+        const float u = (float)k * 5.9604644775390625e-08f;
+        float sn, cs;
+        bsx_sincos_2pi(u, &sn, &cs);
+        const double a = 6.283185307179586 * (double)u;
+        es = std::max(es, std::fabs((double)sn - std::sin(a)));
+        ec = std::max(ec, std::fabs((double)cs - std::cos(a)));
+    }
+    out[0] = es;
+    out[1] = ec;
+}
+void orc_normal3_many(uint64_t seed, uint32_t step, uint32_t n, float* z) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < (int64_t)n; ++i) bsx_normal3(seed, step, (uint32_t)i, z + 3 * i);
+}
+void orc_normal3(uint64_t seed, uint32_t step, uint32_t index, float* z) { bsx_normal3(seed, step, index, z); }
+float orc_powi(float b, uint32_t e) { return bsx_powi(b, e); }
+
 // Decision flips between the two raster arithmetics along one render's
 // trajectory: every pixel walks its tile's whole intersection run (the
 // unshortened range) with the state of the render's own arithmetic, and at

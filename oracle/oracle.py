@@ -132,6 +132,14 @@ def lib() -> C.CDLL:
         _lib.orc_logf.argtypes = [C.c_float]
         _lib.orc_set_threads.argtypes = [C.c_int]
         _lib.orc_set_raster_expr.argtypes = [C.c_int]
+        _lib.orc_mean_noise_step.argtypes = [f32p, f32p, f32p, C.c_uint32, C.c_float, C.c_float, C.c_uint64,
+                                             C.c_uint32]
+        _lib.orc_sincos_2pi.argtypes = [C.c_float, C.POINTER(C.c_float), C.POINTER(C.c_float)]
+        _lib.orc_normal3.argtypes = [C.c_uint64, C.c_uint32, C.c_uint32, f32p]
+        _lib.orc_normal3_many.argtypes = [C.c_uint64, C.c_uint32, C.c_uint32, f32p]
+        _lib.orc_sincos_2pi_max_err.argtypes = [np.ctypeslib.ndpointer(np.float64, flags="C_CONTIGUOUS")]
+        _lib.orc_powi.restype = C.c_float
+        _lib.orc_powi.argtypes = [C.c_float, C.c_uint32]
         _lib.orc_raster_decision_flips.argtypes = [C.c_void_p, np.ctypeslib.ndpointer(np.uint64,
                                                                                     flags="C_CONTIGUOUS")]
         _lib.orc_get_threads.restype = C.c_int
@@ -150,6 +158,42 @@ def raster_decision_flips(render: "RenderResult") -> dict:
     out = np.zeros(4, np.uint64)
     lib().orc_raster_decision_flips(render._h, out)
     return dict(pairs=int(out[0]), accept_flips=int(out[1]), early_out_flips=int(out[2]), pixels=int(out[3]))
+
+
+def mean_noise_step(transforms, raw_opac, gate, scale, limit, seed, step):
+    """The mean-noise step (train.rs:1095-1169) on a copy of ``transforms`` [N,10]; returns it."""
+    t = _f32(transforms).reshape(-1, 10).copy()
+    lib().orc_mean_noise_step(t.reshape(-1), _f32(raw_opac).reshape(-1), _f32(gate).reshape(-1), t.shape[0],
+                              float(scale), float(limit), int(seed), int(step))
+    return t
+
+
+def sincos_2pi(u: float):
+    s, c = C.c_float(), C.c_float()
+    lib().orc_sincos_2pi(float(u), C.byref(s), C.byref(c))
+    return s.value, c.value
+
+
+def normal3(seed: int, step: int, index: int) -> np.ndarray:
+    z = np.zeros(3, np.float32)
+    lib().orc_normal3(int(seed), int(step), int(index), z)
+    return z
+
+
+def normal3_many(seed: int, step: int, n: int) -> np.ndarray:
+    z = np.zeros((n, 3), np.float32)
+    lib().orc_normal3_many(int(seed), int(step), int(n), z.reshape(-1))
+    return z
+
+
+def sincos_2pi_max_err():
+    out = np.zeros(2, np.float64)
+    lib().orc_sincos_2pi_max_err(out)
+    return float(out[0]), float(out[1])
+
+
+def powi(b: float, e: int) -> float:
+    return float(lib().orc_powi(float(b), int(e)))
 
 
 def set_threads(n: int) -> None:

@@ -151,7 +151,7 @@ def test_train_step_matches_oracle_chain(cuda, orc):
     splats, cam, size, gt = config1_scene("cpu", seed=1)
     p0 = splats.clone()
     g = splats.to("cuda")
-    trainer = bsx.SplatTrainer(bsx.TrainConfig(uniform_lr=1e-3), g, gather_stats=False)
+    trainer = bsx.SplatTrainer(bsx.TrainConfig(uniform_lr=1e-3, mean_noise=False), g, gather_stats=False)
     stats = trainer.step(cam, size, gt.cuda(), g)
     torch.cuda.synchronize()
     # oracle chain

@@ -100,7 +100,7 @@ def test_fused_training_step_at_config_size(cuda, orc, name):
     p0 = [splats.transforms.numpy().copy(), splats.sh_coeffs.numpy().reshape(n, 3 * c).copy(),
           splats.raw_opacities.numpy().reshape(n, 1).copy()]
     g = splats.to("cuda")
-    cfg = bsx.TrainConfig()
+    cfg = bsx.TrainConfig(mean_noise=False)
     tr = bsx.SplatTrainer(cfg, g, keep_gradients=True)
     st = tr.step(cam, size, gt.cuda(), g)
     torch.cuda.synchronize()

@@ -41,7 +41,7 @@ def test_native_step_matches_composed_step(cuda, camera_model):
     cams = [dataclasses.replace(orbit_camera(i, 3, 8.0, w, h), camera_model=camera_model, model_params=kp)
             for i in range(3)]
     gts = [random_gt(h, w, 40 + i, "cpu").cuda() for i in range(3)]
-    cfg = bsx.TrainConfig()
+    cfg = bsx.TrainConfig(mean_noise=False)
     comp = splats.clone()
     tr = bsx.SplatTrainer(cfg, splats, keep_gradients=True)
     fused = splats.clone()
@@ -96,7 +96,7 @@ def test_native_step_uniform_rate_and_empty_view(cuda):
 
     splats, cam, size, gt = config1_scene("cuda", seed=2)
     before = splats.clone()
-    tr = bsx.SplatTrainer(bsx.TrainConfig(uniform_lr=1e-3), splats, gather_stats=False)
+    tr = bsx.SplatTrainer(bsx.TrainConfig(uniform_lr=1e-3, mean_noise=False), splats, gather_stats=False)
     away = Camera.look_at((0.0, 0.0, 3.0), target=(0.0, 0.0, 10.0), img_w=size[0], img_h=size[1])
     st = tr.step(away, size, gt.cuda(), splats)
     assert st.num_visible == 0 and st.num_intersections == 0 and st.lr_mean == pytest.approx(1e-3)
