@@ -191,6 +191,16 @@ def build_workload(name, dev, world):
     raise ValueError(name)
 
 
+def _exchange_label(args, world, train, trainer):
+    if world == 1 or not train:
+        return None
+    if args.exchange == "nccl":
+        return "NCCL reduce-scatter + sharded Adam + all-gather"
+    if trainer is not None and trainer.peer is not None and trainer.peer.mc_base:
+        return "NVLink multicast fused kernel: in-switch gradient sum + Adam + multicast parameter store"
+    return "peer-memory fused reduce+Adam+broadcast kernel (gradient rows pushed by the projection backward)"
+
+
 def _time_region(args, world, body):
     """Barrier + sync, CUDA events around body(), sync + barrier; returns the max over ranks (ms)."""
     import torch
@@ -443,11 +453,13 @@ def run_ours(args, rank, world, local_rank):
                    "width": w, "height": h, "views": ncam,
                    "views_per_step_per_gpu": 1, "parallelism": f"dp{world}",
                    "l2": "inputs larger than L2" if N * (44 + 12 * C) > 126e6 else "inputs smaller than L2",
-                   "exchange": (None if world == 1 or not train else
-                                "peer-memory fused reduce+Adam+broadcast kernel" if args.exchange == "peer" else
-                                "NCCL reduce-scatter + sharded Adam + all-gather"),
+                   "exchange": _exchange_label(args, world, train, live["trainer"]),
                    "num_visible": V, "num_intersections": M, "intersections_after_early_out": Mp},
         "e2e": {"value": round(e2e_value, 3), "unit": unit, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        # one view per GPU per step: views/s is the whole-job value; an optimizer step
+        # consumes one view per GPU
+        "throughput": {"views_per_s": round(value, 3),
+                       "optimizer_steps_per_s": round(args.steps / (ms * 1e-3), 3)} if train else None,
         "gpu_launches": int(launches),
         "step_ms": step_ms,
         "roofline": roof,
@@ -710,7 +722,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nvls", "nccl"],
                     help="data-parallel gradient exchange with --gpus > 1")
     ap.add_argument("--workload", default="cfg2", choices=sorted(WORKLOADS),
                     help="BASELINE configuration (cfg2 is the headline metric)")

@@ -143,6 +143,8 @@ class DpGroup(C.Structure):
     _fields_ = [
         ("d_param", C.c_void_p * BSX_MAX_RANKS),
         ("d_grad", C.c_void_p * BSX_MAX_RANKS),
+        ("d_param_mc", C.c_void_p),
+        ("d_grad_mc", C.c_void_p),
         ("d_m", C.c_void_p),
         ("d_v", C.c_void_p),
         ("rows", C.c_uint32),
@@ -165,6 +167,8 @@ class DpExchange(C.Structure):
         ("grad_slot_rows", C.c_uint32),
         ("d_gate", C.c_void_p * BSX_MAX_RANKS),
         ("gate_rows", C.c_uint32),
+        ("d_refine_mc", C.c_void_p),
+        ("d_gate_mc", C.c_void_p),
     ]
 
 
@@ -203,7 +207,9 @@ class TrainStats(C.Structure):
 
 class DpSplats(C.Structure):
     _fields_ = [(name, C.c_void_p * BSX_MAX_RANKS) for name in
-                ("d_transforms", "d_sh_coeffs", "d_raw_opac", "d_v_transforms", "d_v_sh_coeffs", "d_v_raw_opac")]
+                ("d_transforms", "d_sh_coeffs", "d_raw_opac", "d_v_transforms", "d_v_sh_coeffs", "d_v_raw_opac")] + \
+               [(name, C.c_void_p) for name in
+                ("mc_transforms", "mc_sh_coeffs", "mc_raw_opac", "mc_v_transforms", "mc_v_sh_coeffs", "mc_v_raw_opac")]
 
 
 class RefineConfig(C.Structure):

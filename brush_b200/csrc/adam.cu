@@ -53,11 +53,14 @@ struct AdamGroupDev {
     float scale[kMaxCols];
     float* peer_param[kMaxRanks];       // data-parallel form: every rank's shard base
     const float* peer_grad[kMaxRanks];
+    float* mc_param;                    // multicast form: the shard base in the multicast mappings
+    const float* mc_grad;
 };
 
 // Rows MAX-combined over the ranks in place (refine weights, noise gate).
 struct MaxRows {
     float* rows[kMaxRanks];  // shard base of every rank's rows (null: none)
+    float* mc;               // multicast form: shard base in the multicast mapping
     uint32_t count;          // rows of this rank's shard
     uint32_t block_begin;    // first tile of this array
     int vec;
@@ -95,6 +98,37 @@ __device__ __forceinline__ float4 f4max(float4 a, float4 b) {
     return make_float4(fmaxf(a.x, b.x), fmaxf(a.y, b.y), fmaxf(a.z, b.z), fmaxf(a.w, b.w));
 }
 
+// NVLink multicast accesses (NVSwitch): a load that returns the sum (or the
+// maximum) of the addressed word over every GPU bound to the multicast object,
+// reduced in the switch, and a store that writes every bound GPU's copy.
+__device__ __forceinline__ float4 mc_ld_add4(const float* p) {
+    float4 r;
+    asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+                 : "l"(p)
+                 : "memory");
+    return r;
+}
+__device__ __forceinline__ float mc_ld_add(const float* p) {
+    float r;
+    asm volatile("multimem.ld_reduce.relaxed.sys.global.add.f32 %0, [%1];" : "=f"(r) : "l"(p) : "memory");
+    return r;
+}
+__device__ __forceinline__ void mc_st4(float* p, float4 v) {
+    asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(v.x), "f"(v.y),
+                 "f"(v.z), "f"(v.w)
+                 : "memory");
+}
+__device__ __forceinline__ void mc_st(float* p, float v) {
+    asm volatile("multimem.st.relaxed.sys.global.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
+}
+// Maximum of non-negative floats as the maximum of their bit patterns.
+__device__ __forceinline__ float mc_ld_max_nonneg(const float* p) {
+    uint32_t r;
+    asm volatile("multimem.ld_reduce.relaxed.sys.global.max.u32 %0, [%1];" : "=r"(r) : "l"(p) : "memory");
+    return __uint_as_float(r);
+}
+
 // Waits until flags[word0 + q] has reached epoch for every rank q (threads
 // 0..world-1 each poll one word). Returns false, with the error recorded,
 // when the wait outlasts the timeout.
@@ -129,6 +163,10 @@ __device__ void max_tile(const AdamArgs& a, uint32_t t) {
     const MaxRows& x = d.mx[(d.mx[1].count && t >= d.mx[1].block_begin) ? 1 : 0];
     const uint32_t r0 = (t - x.block_begin) * kTileFloats;
     const uint32_t cnt = min(kTileFloats, x.count - r0);
+    if (x.mc) {
+        for (uint32_t e = threadIdx.x; e < cnt; e += kAdamThreads) mc_st(x.mc + r0 + e, mc_ld_max_nonneg(x.mc + r0 + e));
+        return;
+    }
     const uint32_t nvec = x.vec ? cnt / 4 : 0;
     for (uint32_t j = threadIdx.x; j < nvec; j += kAdamThreads) {
         float4 m = __ldcg(reinterpret_cast<const float4*>(x.rows[0] + r0) + j);
@@ -157,7 +195,7 @@ __device__ __forceinline__ float4 ld_grad4(const float* p, uint32_t j, bool peer
 // requests in flight per thread: HBM and NVLink are latency-bound otherwise).
 // Every sum is taken in a fixed order, so equal inputs give bit-equal outputs
 // on every run and every data-parallel replica. kW bounds the rank count.
-template <bool kPeers, int kW>
+template <bool kPeers, int kW, bool kMC = false>
 __device__ void adam_tile(const AdamArgs& a, int k, uint32_t tile) {
     __shared__ __align__(16) float s_g[kTileFloats];
     __shared__ float s_v[kTileFloats];
@@ -186,9 +224,10 @@ __device__ void adam_tile(const AdamArgs& a, int k, uint32_t tile) {
 #pragma unroll
             for (int c = 0; c < kChunk; ++c) {
                 const uint32_t j = threadIdx.x + (c0 + c) * kAdamThreads;
-                acc[c] = j < nvec ? ld_grad4((kPeers ? G.peer_grad[0] : G.grad) + base, j, kPeers) : zero;
+                if (kMC) acc[c] = j < nvec ? mc_ld_add4(G.mc_grad + base + 4 * (size_t)j) : zero;
+                else acc[c] = j < nvec ? ld_grad4((kPeers ? G.peer_grad[0] : G.grad) + base, j, kPeers) : zero;
             }
-            if (kPeers) {
+            if (kPeers && !kMC) {
                 float4 t[kW > 1 ? kW - 1 : 1][kChunk];
 #pragma unroll
                 for (int q = 1; q < kW; ++q)
@@ -217,7 +256,9 @@ __device__ void adam_tile(const AdamArgs& a, int k, uint32_t tile) {
     }
     for (uint32_t j = nvec * 4 + threadIdx.x; j < count; j += kAdamThreads) {
         float g;
-        if (kPeers) {
+        if (kMC) {
+            g = mc_ld_add(G.mc_grad + base + j);
+        } else if (kPeers) {
             g = __ldcg(G.peer_grad[0] + base + j);
             for (int q = 1; q < world; ++q) g += __ldcg(G.peer_grad[q] + base + j);
         } else {
@@ -295,8 +336,9 @@ __device__ void adam_tile(const AdamArgs& a, int k, uint32_t tile) {
                 upd(p.z, g.z, m.z, v.z, col, r, po.z, mo.z, vo.z);
                 if (++col == cols) { col = 0; ++r; }
                 upd(p.w, g.w, m.w, v.w, col, r, po.w, mo.w, vo.w);
-                p4[j] = po;
-                if (kPeers)
+                if (kMC) mc_st4(G.mc_param + base + 4 * (size_t)j, po);  // every rank's copy, this one included
+                else p4[j] = po;
+                if (kPeers && !kMC)
 #pragma unroll
                     for (int q = 0; q < kW; ++q)
                         if (q < world && q != a.dp.rank) reinterpret_cast<float4*>(G.peer_param[q] + base)[j] = po;
@@ -312,8 +354,9 @@ __device__ void adam_tile(const AdamArgs& a, int k, uint32_t tile) {
         float po, mo, vo;
         upd(G.param[base + e], s_g[e], a.first ? 0.0f : G.m[base + e], (G.reduce || a.first) ? 0.0f : G.v[base + e],
             c, r, po, mo, vo);
-        G.param[base + e] = po;
-        if (kPeers)
+        if (kMC) mc_st(G.mc_param + base + e, po);
+        else G.param[base + e] = po;
+        if (kPeers && !kMC)
             for (int q = 0; q < world; ++q)
                 if (q != a.dp.rank) G.peer_param[q][base + e] = po;
         G.m[base + e] = mo;
@@ -338,7 +381,7 @@ __global__ void __launch_bounds__(kAdamThreads) adam_kernel(const __grid_constan
 // the last block to finish signals departure and waits until every rank has
 // departed, so the launch ends only when no rank still reads this rank's
 // gradients or writes its parameters.
-template <int kW>
+template <int kW, bool kMC>
 __global__ void __launch_bounds__(kAdamThreads) dp_adam_kernel(const __grid_constant__ AdamArgs a) {
     const DpDev& d = a.dp;
     signal_all_ranks(d, kFlagArrive);
@@ -346,7 +389,7 @@ __global__ void __launch_bounds__(kAdamThreads) dp_adam_kernel(const __grid_cons
     if (arrived) {
         for (uint32_t t = blockIdx.x; t < d.total_tiles; t += gridDim.x) {
             if (t < d.refine_block_begin)
-                adam_tile<true, kW>(a, group_of(a, t), t);
+                adam_tile<true, kW, kMC>(a, group_of(a, t), t);
             else
                 max_tile(a, t);
             __syncthreads();  // shared staging is reused by the next tile
@@ -470,6 +513,12 @@ extern "C" bsx_status bsx_dp_adam_step(bsx_ctx* ctx, const bsx_dp_exchange* ex, 
         *b = (uint32_t)((uint64_t)rows * rank / world);
         *e = (uint32_t)((uint64_t)rows * (rank + 1) / world);
     };
+    // multicast form: every group has both multicast addresses
+    bool mc = true;
+    for (int i = 0; i < num_groups; ++i) mc = mc && groups[i].d_param_mc && groups[i].d_grad_mc;
+    if (mc && ex->grad_slot_rows) return fail(ctx, BSX_ERR_INVALID_ARG, "the multicast form reads dense gradients");
+    if (mc && ((ex->refine_rows && !ex->d_refine_mc) || (ex->gate_rows && !ex->d_gate_mc)))
+        return fail(ctx, BSX_ERR_INVALID_ARG, "the multicast form needs multicast refine / gate addresses");
     uint32_t blocks = 0;
     for (int i = 0; i < num_groups; ++i) {
         const bsx_dp_group& s = groups[i];
@@ -483,9 +532,18 @@ extern "C" bsx_status bsx_dp_adam_step(bsx_ctx* ctx, const bsx_dp_exchange* ex, 
             g.peer_param[q] = nullptr;
             g.peer_grad[q] = nullptr;
         }
+        g.mc_param = nullptr;
+        g.mc_grad = nullptr;
         if (ex->grad_slot_rows && (ex->grad_slot_rows < re - rb || !s.d_grad[rank]))
             return fail(ctx, BSX_ERR_INVALID_ARG, "gradient slots smaller than the shard");
-        for (int q = 0; q < world; ++q) {
+        if (mc) {
+            if (!s.d_param[rank]) return fail(ctx, BSX_ERR_INVALID_ARG, "null parameter");
+            g.peer_param[rank] = s.d_param[rank] + (size_t)rb * s.cols;
+            g.mc_param = s.d_param_mc + (size_t)rb * s.cols;
+            g.mc_grad = s.d_grad_mc + (size_t)rb * s.cols;
+            vec = vec && aligned16(g.peer_param[rank]) && aligned16(g.mc_param) && aligned16(g.mc_grad);
+        }
+        for (int q = 0; q < world && !mc; ++q) {
             if (!s.d_param[q] || (!ex->grad_slot_rows && !s.d_grad[q]))
                 return fail(ctx, BSX_ERR_INVALID_ARG, "null parameter / gradient");
             g.peer_param[q] = s.d_param[q] + (size_t)rb * s.cols;
@@ -505,18 +563,21 @@ extern "C" bsx_status bsx_dp_adam_step(bsx_ctx* ctx, const bsx_dp_exchange* ex, 
     d.refine_block_begin = blocks;
     for (int q = 0; q < kMaxRanks; ++q) d.flags[q] = q < world ? ex->d_flags[q] : nullptr;
     float* const* srcs[2] = {ex->d_refine, ex->d_gate};
+    float* const mcs[2] = {ex->d_refine_mc, ex->d_gate_mc};
     const uint32_t counts[2] = {ex->refine_rows, ex->gate_rows};
     for (int k = 0; k < 2; ++k) {
         MaxRows& x = d.mx[k];
         x.count = 0;
         x.vec = 1;
         x.block_begin = blocks;
+        x.mc = nullptr;
         for (int q = 0; q < kMaxRanks; ++q) x.rows[q] = nullptr;
         if (!counts[k]) continue;
         uint32_t rb, re;
         shard(counts[k], &rb, &re);
         x.count = re - rb;
-        for (int q = 0; q < world; ++q) {
+        if (mc) x.mc = mcs[k] + rb;
+        for (int q = 0; q < world && !mc; ++q) {
             x.rows[q] = srcs[k][q] + rb;
             x.vec = x.vec && aligned16(x.rows[q]);
         }
@@ -525,7 +586,10 @@ extern "C" bsx_status bsx_dp_adam_step(bsx_ctx* ctx, const bsx_dp_exchange* ex, 
     d.total_tiles = blocks;
     // Persistent grid: at most one wave of resident blocks; every rank launches
     // at least one block so that it signals and waits.
-    auto kern = world <= 2 ? dp_adam_kernel<2> : world <= 4 ? dp_adam_kernel<4> : dp_adam_kernel<8>;
+    auto kern = mc ? (world <= 2 ? dp_adam_kernel<2, true> : world <= 4 ? dp_adam_kernel<4, true>
+                                                                       : dp_adam_kernel<8, true>)
+                   : (world <= 2 ? dp_adam_kernel<2, false> : world <= 4 ? dp_adam_kernel<4, false>
+                                                                         : dp_adam_kernel<8, false>);
     int sms = 0, per_sm = 0;
     bsx_status s = check_cuda(ctx, cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ctx->device),
                               "cudaDeviceGetAttribute");

@@ -499,7 +499,10 @@ bsx_status bsx_train_step_dp(bsx_trainer* tr, const bsx_camera* cam, uint32_t w,
     // 16-byte aligned slot starts, and shards of at least one projection block
     // (128 rows) so that a block's rows span at most two owners.
     const uint32_t slot = ex->grad_slot_rows;
-    bool push = world > 1 && slot > 0 && !tr->keep_grads;
+    // multicast form: every rank writes its dense gradient; the exchange reduces in the switch
+    const bool mc = sp->mc_transforms && sp->mc_sh_coeffs && sp->mc_raw_opac && sp->mc_v_transforms &&
+                    sp->mc_v_sh_coeffs && sp->mc_v_raw_opac;
+    bool push = !mc && world > 1 && slot > 0 && !tr->keep_grads;
     for (int q = 0; push && q < world; ++q) {
         const uint32_t rows = shard_begin(tr->n, q + 1, world) - shard_begin(tr->n, q, world);
         push = rows >= 128 && rows <= slot && slot % 4 == 0 && sp->d_v_transforms[q] && sp->d_v_sh_coeffs[q] &&
@@ -540,6 +543,8 @@ bsx_status bsx_train_step_dp(bsx_trainer* tr, const bsx_camera* cam, uint32_t w,
             g[i].d_param[q] = !in ? nullptr : i == 0 ? sp->d_transforms[q] : i == 1 ? sp->d_sh_coeffs[q] : sp->d_raw_opac[q];
             g[i].d_grad[q] = !in ? nullptr : i == 0 ? sp->d_v_transforms[q] : i == 1 ? sp->d_v_sh_coeffs[q] : sp->d_v_raw_opac[q];
         }
+        g[i].d_param_mc = !mc ? nullptr : i == 0 ? sp->mc_transforms : i == 1 ? sp->mc_sh_coeffs : sp->mc_raw_opac;
+        g[i].d_grad_mc = !mc ? nullptr : i == 0 ? sp->mc_v_transforms : i == 1 ? sp->mc_v_sh_coeffs : sp->mc_v_raw_opac;
         g[i].d_m = m[i];
         g[i].d_v = v[i];
         g[i].rows = tr->n;
@@ -552,6 +557,7 @@ bsx_status bsx_train_step_dp(bsx_trainer* tr, const bsx_camera* cam, uint32_t w,
     e.refine_rows = refine ? tr->n : 0;
     e.epoch = ++tr->dp_epoch;
     e.grad_slot_rows = push ? slot : 0;
+    if (!mc) e.d_refine_mc = e.d_gate_mc = nullptr;
     // The noise moves a splat where any rank's gate is set, so that every
     // replica applies the same update: this rank's gate goes into its exchange
     // row and the exchange combines the ranks' gates by MAX.

@@ -72,7 +72,7 @@ class ExchangeLayout:
 class PeerExchange:
     """This rank's exchange region, every rank's mapping of it, and the shard's Adam moments."""
 
-    def __init__(self, n: int, c: int, device: int, group, timeout_s: float = 5.0):
+    def __init__(self, n: int, c: int, device: int, group, timeout_s: float = 5.0, multicast: bool = False):
         self.group = group
         self.world = torch.distributed.get_world_size(group)
         self.rank = torch.distributed.get_rank(group)
@@ -83,23 +83,11 @@ class PeerExchange:
         self.layout = ExchangeLayout(n, c, self.world)
         self.timeout_ns = int(timeout_s * 1e9)
         self.epoch = 0
-        L = _lib.lib()
-        own = C.c_void_p()
-        handle = C.create_string_buffer(_lib.BSX_PEER_HANDLE_BYTES)
-        self.ctx.check(L.bsx_peer_alloc(self.ctx.handle, self.layout.nbytes, C.byref(own), handle))
-        self._own = own.value
-        handles = [None] * self.world
-        torch.distributed.all_gather_object(handles, handle.raw, group=group)
-        self.bases = []
+        self.mc_base = 0
+        self._symm = None
         self._opened = []
-        for q, h in enumerate(handles):
-            if q == self.rank:
-                self.bases.append(self._own)
-                continue
-            p = C.c_void_p()
-            self.ctx.check(L.bsx_peer_open(self.ctx.handle, C.create_string_buffer(h, len(h)), C.byref(p)))
-            self.bases.append(p.value)
-            self._opened.append(p.value)
+        if not (multicast and self.world > 1 and self._alloc_multicast()):
+            self._alloc_ipc()
         self.params = (self._view(("param", "transforms"), (n, 10)), self._view(("param", "sh"), (n, c, 3)),
                        self._view(("param", "opac"), (n,)))
         self.grads = (self._view(("grad", "transforms"), (n, 10)), self._view(("grad", "sh"), (n, c, 3)),
@@ -108,6 +96,60 @@ class PeerExchange:
         self.row0, self.row1 = shard_rows(n, self.rank, self.world)
         self.m = self.v = None  # shard moments of adam_step (the native trainer keeps its own)
         self._closed = False
+
+    def _alloc_ipc(self) -> None:
+        """The region from bsx_peer_alloc, mapped by the other ranks through CUDA IPC handles."""
+        L = _lib.lib()
+        own = C.c_void_p()
+        handle = C.create_string_buffer(_lib.BSX_PEER_HANDLE_BYTES)
+        self.ctx.check(L.bsx_peer_alloc(self.ctx.handle, self.layout.nbytes, C.byref(own), handle))
+        self._own = own.value
+        handles = [None] * self.world
+        torch.distributed.all_gather_object(handles, handle.raw, group=self.group)
+        self.bases = []
+        for q, h in enumerate(handles):
+            if q == self.rank:
+                self.bases.append(self._own)
+                continue
+            p = C.c_void_p()
+            self.ctx.check(L.bsx_peer_open(self.ctx.handle, C.create_string_buffer(h, len(h)), C.byref(p)))
+            self.bases.append(p.value)
+            self._opened.append(p.value)
+
+    def _alloc_multicast(self) -> bool:
+        """The region as PyTorch symmetric memory: every rank's copy mapped on every rank, and
+        one NVLink multicast mapping over all copies (NVSwitch). False, with nothing kept,
+        when some rank's device offers no multicast (every rank then takes the IPC path)."""
+        import torch.distributed._symmetric_memory as symm_mem
+
+        dev = torch.device("cuda", self.device)
+        t = symm_mem.empty(self.layout.floats, dtype=torch.float32, device=dev)
+        hdl = symm_mem.rendezvous(t, self.group)
+
+        def attr(name):
+            v = getattr(hdl, name)
+            return v() if callable(v) else v
+
+        mc = int(attr("multicast_ptr") or 0)
+        ok = torch.tensor([1 if mc else 0], dtype=torch.int32, device=dev)
+        torch.distributed.all_reduce(ok, op=torch.distributed.ReduceOp.MIN, group=self.group)
+        if int(ok.item()) == 0:
+            torch.distributed.barrier(group=self.group)
+            del hdl, t
+            return False
+        t.zero_()  # flag words start at zero
+        torch.cuda.synchronize(self.device)
+        torch.distributed.barrier(group=self.group)
+        self._symm = (t, hdl)
+        self._own = t.data_ptr()
+        self.bases = [int(p) for p in attr("buffer_ptrs")]
+        if self.bases[self.rank] != self._own:
+            raise RuntimeError("symmetric memory: own buffer pointer mismatch")
+        self.mc_base = mc
+        return True
+
+    def _mc(self, key) -> int:
+        return self.mc_base + 4 * self.layout.offsets[key]
 
     def _view(self, key, shape) -> torch.Tensor:
         return device_view(self._own + 4 * self.layout.offsets[key], shape, torch.float32, self.device)
@@ -182,6 +224,14 @@ class PeerExchange:
         ex.refine_rows = self.layout.n
         ex.timeout_ns = self.timeout_ns
         ex.grad_slot_rows = self.layout.slot_rows
+        if self.mc_base:
+            # multicast form: dense gradients, reduced in the switch
+            ex.grad_slot_rows = 0
+            ex.d_refine_mc = self._mc("refine")
+            ex.d_gate_mc = self._mc("gate")
+            for kind, prefix in (("param", "mc_"), ("grad", "mc_v_")):
+                for name, field in (("transforms", "transforms"), ("sh", "sh_coeffs"), ("opac", "raw_opac")):
+                    setattr(sp, prefix + field, self._mc((kind, name)))
         return ex, sp
 
     def close(self) -> None:
@@ -191,6 +241,12 @@ class PeerExchange:
         self._closed = True
         torch.cuda.synchronize(self.device)
         torch.distributed.barrier(group=self.group)
+        if self._symm is not None:
+            # every rank has finished with every copy before any is released
+            self._symm = None
+            torch.cuda.synchronize(self.device)
+            torch.distributed.barrier(group=self.group)
+            return
         L = _lib.lib()
         for p in self._opened:
             self.ctx.check(L.bsx_peer_close(self.ctx.handle, C.c_void_p(p)))

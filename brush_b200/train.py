@@ -220,8 +220,12 @@ class SplatTrainer:
         #   "nccl": with shard_optimizer and N divisible by the world size,
         #           reduce-scatter gradients -> fused Adam on this rank's row
         #           shard -> all-gather; otherwise all-reduce -> full Adam.
-        if exchange not in ("peer", "nccl"):
-            raise ValueError("exchange must be 'peer' or 'nccl'")
+        #   "nvls": the peer exchange over PyTorch symmetric memory with an
+        #           NVLink multicast mapping: the gradient rows are summed in the
+        #           NVSwitch and the updated rows multicast to every rank
+        #           (falls back to "peer" where the devices offer no multicast).
+        if exchange not in ("peer", "nvls", "nccl"):
+            raise ValueError("exchange must be 'peer', 'nvls' or 'nccl'")
         self.exchange = exchange
         self.peer = None
         self.native = None
@@ -253,7 +257,7 @@ class SplatTrainer:
         self.groups = None
         old_peer, self.peer = self.peer, None
         old_native, self.native = self.native, None
-        if self.world == 1 or self.exchange == "peer":
+        if self.world == 1 or self.exchange in ("peer", "nvls"):
             self.native = _NativeTrainer(dev.index, n, c, self.config.to_c(self.median_scale, splats.render_mode,
                                                                           self.gather_stats))
             self.native.ctx.check(_lib.lib().bsx_trainer_keep_gradients(self.native.handle,
@@ -262,7 +266,7 @@ class SplatTrainer:
             if self.world > 1:
                 from .peer import PeerExchange
 
-                self.peer = PeerExchange(n, c, dev.index, self.pg)
+                self.peer = PeerExchange(n, c, dev.index, self.pg, multicast=self.exchange == "nvls")
                 self.peer.load(splats.transforms, splats.sh_coeffs, splats.raw_opacities)
                 splats.transforms, splats.sh_coeffs, splats.raw_opacities = self.peer.params
                 # dense gradients of this rank's view only with keep_gradients; otherwise
@@ -507,7 +511,8 @@ class SplatTrainer:
         from .peer import PeerExchange
 
         old = self.peer
-        self.peer = PeerExchange(self.n, self.c, splats.transforms.device.index, self.pg)
+        self.peer = PeerExchange(self.n, self.c, splats.transforms.device.index, self.pg,
+                                 multicast=self.exchange == "nvls")
         self.peer.load(splats.transforms, splats.sh_coeffs, splats.raw_opacities)
         splats.transforms, splats.sh_coeffs, splats.raw_opacities = self.peer.params
         self.grads = SplatGrads(*self.peer.grads, v_refine_weight=self.peer.refine)

@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define BSX_ABI_VERSION 6
+#define BSX_ABI_VERSION 7
 /* Gradient lanes per splat written by the raster backward:
  * xy(2) conic(3) rgb(3) alpha refine depth. Reference:
  * crates/brush-render-bwd/src/kernels/rasterize_backwards.rs:40 */
@@ -289,6 +289,8 @@ BSX_API bsx_status bsx_peer_close(bsx_ctx* ctx, void* d_ptr);
 typedef struct bsx_dp_group {
     float* d_param[BSX_MAX_RANKS];       /* every rank's copy of the parameter [rows, cols] (own + mapped) */
     const float* d_grad[BSX_MAX_RANKS];  /* every rank's gradient [rows, cols] (own + mapped) */
+    float* d_param_mc;                   /* multicast form (both non-NULL): NVLink multicast addresses of */
+    const float* d_grad_mc;              /* every rank's d_param / dense d_grad buffers (NVSwitch, NVLS) */
     float* d_m;                          /* this rank's first moment for its shard rows [shard_rows, cols] */
     float* d_v;                          /* [shard_rows, cols], or [shard_rows] when reduce_moment_2 */
     uint32_t rows, cols;                 /* full parameter shape; cols <= 80 */
@@ -312,8 +314,21 @@ typedef struct bsx_dp_exchange {
     float* d_gate[BSX_MAX_RANKS];        /* optional [gate_rows] per rank, MAX-combined in place like
                                           * d_refine (the mean-noise visibility gate; NULL: none) */
     uint32_t gate_rows;
+    float* d_refine_mc;                  /* multicast form: multicast addresses of d_refine / d_gate */
+    float* d_gate_mc;
 } bsx_dp_exchange;
 
+/* Multicast form (every group's d_param_mc and d_grad_mc set; grad_slot_rows 0):
+ * the buffers of all ranks are bound to one NVLink multicast object each, at
+ * the same offset, and the *_mc pointers are its mapping on this rank. The
+ * owner of a shard then reads the ranks' summed gradient rows with one
+ * in-switch reduction (multimem.ld_reduce.add) instead of a load per rank, and
+ * writes each updated row once for all ranks (multimem.st), so each GPU's
+ * links carry about S per direction per step (S = the parameter bytes) instead
+ * of 2 (world - 1) / world S. Refine weights and gates (non-negative) take the
+ * in-switch maximum of their bit patterns. The ranks' sums are formed by the
+ * switch, whose order of additions is not specified; every rank still receives
+ * the same rows. */
 /* One kernel in place of "all-reduce the gradients, then bsx_adam_step": rank
  * r owns rows [rows*r/world, rows*(r+1)/world) of every group. After every
  * rank has arrived (a flag barrier), it sums its rows' gradients over all
@@ -382,6 +397,15 @@ typedef struct bsx_dp_splats {
     float* d_v_transforms[BSX_MAX_RANKS];
     float* d_v_sh_coeffs[BSX_MAX_RANKS];
     float* d_v_raw_opac[BSX_MAX_RANKS];
+    /* multicast addresses of the six buffers above (all NULL: no multicast);
+     * with them each rank writes its dense gradient and the exchange takes the
+     * multicast form (see bsx_dp_adam_step) */
+    float* mc_transforms;
+    float* mc_sh_coeffs;
+    float* mc_raw_opac;
+    float* mc_v_transforms;
+    float* mc_v_sh_coeffs;
+    float* mc_v_raw_opac;
 } bsx_dp_splats;
 
 typedef struct bsx_trainer bsx_trainer;

@@ -30,7 +30,7 @@ def test_library_exports_every_declared_symbol(bsx_lib):
 
 def test_status_strings_and_abi(bsx_lib):
     lib = bsx_lib.lib()
-    assert lib.bsx_abi_version() == 6
+    assert lib.bsx_abi_version() == 7
     assert lib.bsx_status_string(0) == b"ok"
     assert lib.bsx_status_string(4) == b"device wait timed out"
     assert lib.bsx_status_string(8) == b"malformed file"

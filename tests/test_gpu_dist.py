@@ -55,14 +55,15 @@ def _worker(rank, world, port, q, mode):
         splats, cams, size, gts = _scene(dev, _n_of(mode))
         tr = bsx.SplatTrainer(bsx.TrainConfig(uniform_lr=1e-3, mean_noise=False), splats, process_group=torch.distributed.group.WORLD,
                               gather_stats=False, shard_optimizer=mode == "sharded_adam",
-                              exchange="peer" if mode.startswith("peer") else "nccl",
+                              exchange="nvls" if mode == "nvls" else "peer" if mode.startswith("peer") else "nccl",
                               keep_gradients=mode == "peer_keep")
         v = view_for(0, rank, world, len(cams))
         tr.step(cams[v], size, gts[v], splats)
         torch.cuda.synchronize()
         tr.peer and tr.peer.ctx.sync()
         q.put((rank, "ok", splats.transforms.cpu().numpy(), splats.sh_coeffs.cpu().numpy(),
-               splats.raw_opacities.cpu().numpy(), (tr.peer is not None, tr.sharded)))
+               splats.raw_opacities.cpu().numpy(), (tr.peer is not None, tr.sharded),
+               bool(tr.peer is not None and tr.peer.mc_base)))
         tr.close()
     except Exception as e:  # noqa: BLE001
         q.put((rank, "error", repr(e)))
@@ -71,7 +72,9 @@ def _worker(rank, world, port, q, mode):
 
 
 def _n_of(mode):
-    return 40001 if mode.startswith("peer") else 40000
+    # odd counts: uneven shards, and (40003) shard starts off the 16-byte grid for the
+    # multicast form's single-float path
+    return 40003 if mode == "nvls" else 40001 if mode.startswith("peer") else 40000
 
 
 def _oracle_mean_of_views(orc, n, world=2):
@@ -125,11 +128,11 @@ def _assert_close_to_oracle_step(got, ref, grads, lr=1e-3):
 
 
 @pytest.mark.parametrize("world", [2, 4])
-@pytest.mark.parametrize("mode", ["peer", "peer_keep", "sharded_adam", "allreduce"])
+@pytest.mark.parametrize("mode", ["peer", "peer_keep", "sharded_adam", "allreduce", "nvls"])
 def test_multi_gpu_step_matches_mean_of_views(cuda, orc, mode, world):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
-    if world > 2 and mode != "peer":
+    if world > 2 and mode not in ("peer", "nvls"):
         pytest.skip("the other exchanges are checked on 2 GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
@@ -141,7 +144,9 @@ def test_multi_gpu_step_matches_mean_of_views(cuda, orc, mode, world):
     for p in procs:
         p.join(timeout=60)
     assert all(r[1] == "ok" for r in res), res
-    assert res[0][5] == (mode.startswith("peer"), mode == "sharded_adam")
+    if mode == "nvls" and not res[0][6]:
+        pytest.skip("the devices offer no NVLink multicast")
+    assert res[0][5] == (mode.startswith("peer") or mode == "nvls", mode == "sharded_adam")
     for r in res[1:]:
         for k in (2, 3, 4):
             np.testing.assert_array_equal(res[0][k], r[k])
@@ -241,7 +246,7 @@ def test_dp_kernel_times_out_when_a_rank_never_arrives(cuda):
     assert torch.isfinite(g["param"][0]).all()
 
 
-def _refine_worker(rank, world, port, q):
+def _refine_worker(rank, world, port, q, exchange="peer"):
     sys.path.insert(0, str(ROOT))
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     import brush_b200 as bsx
@@ -253,7 +258,8 @@ def _refine_worker(rank, world, port, q):
                                          timeout=datetime.timedelta(seconds=60))
     try:
         splats, cams, size, gts = _scene(dev)
-        tr = bsx.SplatTrainer(bsx.TrainConfig(), splats, process_group=torch.distributed.group.WORLD)
+        tr = bsx.SplatTrainer(bsx.TrainConfig(), splats, process_group=torch.distributed.group.WORLD,
+                              exchange=exchange)
         for k in range(4):
             v = view_for(k, rank, world, len(cams))
             tr.step(cams[v], size, gts[v], splats)
@@ -277,7 +283,7 @@ def _refine_worker(rank, world, port, q):
         tr.peer.ctx.sync()
         later = [x.cpu().numpy().copy() for x in (splats.transforms, splats.sh_coeffs, splats.raw_opacities)]
         q.put((rank, "ok", dict(rec=rec, shard=shard, pre=pre, bounds=bounds, post=post, later=later,
-                                total=st.total_splats, added=st.num_added)))
+                                total=st.total_splats, added=st.num_added, mc=bool(tr.peer.mc_base))))
         tr.close()
     except Exception as e:  # noqa: BLE001
         import traceback
@@ -287,13 +293,16 @@ def _refine_worker(rank, world, port, q):
         torch.distributed.destroy_process_group()
 
 
-def test_two_gpu_refine_identical_on_both_ranks_and_matches_oracle(cuda, orc):
+@pytest.mark.parametrize("exchange", ["peer", "nvls"])
+def test_two_gpu_refine_identical_on_both_ranks_and_matches_oracle(cuda, orc, exchange):
+    """Four steps (mean noise on, gated on the combined visibility), a refine, three more steps:
+    both replicas stay bit-identical, and the refine equals the oracle's on the combined state."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_refine_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_refine_worker, args=(r, 2, port, q, exchange)) for r in range(2)]
     for p in procs:
         p.start()
     res = sorted([q.get(timeout=300) for _ in range(2)], key=lambda r: r[0])
@@ -301,6 +310,8 @@ def test_two_gpu_refine_identical_on_both_ranks_and_matches_oracle(cuda, orc):
         p.join(timeout=60)
     assert all(r[1] == "ok" for r in res), res
     a, b = res[0][2], res[1][2]
+    if exchange == "nvls" and not a["mc"]:
+        pytest.skip("the devices offer no NVLink multicast")
     assert a["total"] == b["total"] and a["added"] > 0
     for x, y in zip(a["post"] + a["later"], b["post"] + b["later"]):
         np.testing.assert_array_equal(x, y)
