@@ -241,8 +241,9 @@ def run_ours(args, rank, world, local_rank):
     if args.workload == "cfg4":
         if world > 1:
             raise SystemExit("cfg4 (densification) runs on one GPU")
+        # BASELINE configuration 4's rule: the original 3DGS gradient-threshold densification
         refine_cfg = bsx.RefineConfig(refine_every=100, growth_grad_threshold=2e-4, min_opacity=0.005,
-                                      growth_select_fraction=0.1, max_splats=1_500_000)
+                                      max_splats=1_500_000, rule=bsx.REFINE_GRAD_THRESHOLD, percent_dense=0.01)
     refines = []
 
     def view(step):

@@ -4,7 +4,7 @@ API of debsahu/brush's render / render-bwd / loss / train crates.
 The compute lives in ``libbsx.so`` (C ABI, ``include/bsx.h``); this package is
 the host-side mirror of the reference's operators. There is no CPU path.
 """
-from ._lib import BsxError, lib  # noqa: F401
+from ._lib import REFINE_GRAD_THRESHOLD, REFINE_REFERENCE, BsxError, lib  # noqa: F401
 from .adam import AdamGroup, AdamScaled  # noqa: F401
 from .camera import Camera, focal_to_fov, fov_to_focal  # noqa: F401
 from .loss import ImageLossConfig, image_loss_backward, image_loss_forward, image_loss_fused  # noqa: F401

@@ -13,6 +13,8 @@ from pathlib import Path
 LIB_PATH = Path(__file__).resolve().parent / "libbsx.so"
 
 BSX_COMPACT_GRAD_LANES = 11
+REFINE_REFERENCE = 0
+REFINE_GRAD_THRESHOLD = 1
 BSX_GRAD_STRIDE = 12
 BSX_PROJECTED_LANES = 12
 BSX_TILE_WIDTH = 16
@@ -231,6 +233,8 @@ class RefineConfig(C.Structure):
         ("split_other_axis_scale", C.c_float),
         ("split_opacity_scale", C.c_float),
         ("seed", C.c_uint64),
+        ("rule", C.c_int32),
+        ("percent_dense", C.c_float),
     ]
 
 
@@ -320,6 +324,7 @@ SIGNATURES = {
         C.c_int, [C.c_void_p, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), C.POINTER(C.c_void_p)]
     ),
     "bsx_trainer_keep_gradients": (C.c_int, [C.c_void_p, C.c_int32]),
+    "bsx_trainer_grad2d_accum": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
     "bsx_trainer_raster_grads": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
     "bsx_trainer_grad_buffers": (
         C.c_int,

@@ -289,6 +289,84 @@ __global__ void __launch_bounds__(kRefThreads) decay_kernel(float* __restrict__ 
         }
 }
 
+// ---- gradient-threshold rule (the original 3DGS densify_and_clone / densify_and_split) ----
+
+// Selection of the kept rows: average view-space gradient norm over the
+// visible steps >= threshold; clone where the largest scale is at most `dense`,
+// split otherwise.
+__global__ void __launch_bounds__(kRefThreads)
+    grad_select_kernel(const uint32_t* __restrict__ keep, uint32_t K, const float* __restrict__ t,
+                       const float* __restrict__ vis, const float* __restrict__ grad2d, float threshold, float dense,
+                       uint32_t* __restrict__ clone_flag, uint32_t* __restrict__ split_flag) {
+    const uint32_t j = blockIdx.x * kRefThreads + threadIdx.x;
+    if (j >= K) return;
+    const uint32_t i = keep[j];
+    const float avg = vis[i] > 0.0f ? grad2d[i] / vis[i] : 0.0f;
+    const bool sel = avg >= threshold;
+    const float* r = t + (size_t)i * 10;
+    const float smax = bsx_max(bsx_max(bsx_expf(r[7]), bsx_expf(r[8])), bsx_expf(r[9]));
+    clone_flag[j] = (sel && smax <= dense) ? 1u : 0u;
+    split_flag[j] = (sel && !(smax <= dense)) ? 1u : 0u;
+}
+
+// out[pos[j] - 1] = j for the first `limit` flagged rows; taken[j] marks them.
+__global__ void __launch_bounds__(kRefThreads)
+    take_first_kernel(const uint32_t* __restrict__ flag, const uint32_t* __restrict__ pos, uint32_t K, uint32_t limit,
+                      uint32_t* __restrict__ out, uint32_t* __restrict__ taken) {
+    const uint32_t j = blockIdx.x * kRefThreads + threadIdx.x;
+    if (j >= K) return;
+    const bool t = flag[j] && pos[j] <= limit;
+    if (t) out[pos[j] - 1] = j;
+    if (taken) taken[j] = t ? 0u : 1u;  // 1 = stays (not split)
+}
+
+// idx2[r] = keep[idx[r]] (kept numbering -> original ids).
+__global__ void __launch_bounds__(kRefThreads) compose_kernel(const uint32_t* __restrict__ keep,
+                                                              const uint32_t* __restrict__ idx, uint32_t count,
+                                                              uint32_t* __restrict__ out) {
+    const uint32_t r = blockIdx.x * kRefThreads + threadIdx.x;
+    if (r < count) out[r] = keep[idx[r]];
+}
+
+struct GtSplitArgs {
+    const uint32_t* split;  // split rows (kept numbering) [S]
+    const uint32_t* keep;   // kept original ids
+    const float* t;         // old splats
+    const float* sh;
+    const float* op;
+    float* nt;              // rows `base`.. receive the children
+    float* nsh;
+    float* nop;
+    uint32_t S, c3, base, refine_count;
+    uint64_t seed;
+};
+
+// Child k of split row q at row base + k S + q: mean + R(q) (s * n), log(s / 1.6),
+// rotation, SH and opacity copied (the original 3DGS densify_and_split, N = 2).
+__global__ void __launch_bounds__(kRefThreads) grad_split_kernel(const __grid_constant__ GtSplitArgs a) {
+    const uint32_t e = blockIdx.x * kRefThreads + threadIdx.x;
+    if (e >= 2 * a.S) return;
+    const uint32_t k = e / a.S, q = e - k * a.S;
+    const uint32_t j = a.split[q], i = a.keep[j], r = a.base + e;
+    const float* pr = a.t + (size_t)i * 10;
+    const float mag = bsx_max(sqrtf(pr[3] * pr[3] + pr[4] * pr[4] + pr[5] * pr[5] + pr[6] * pr[6]), 1e-32f);
+    const float qw = pr[3] / mag, qx = pr[4] / mag, qy = pr[5] / mag, qz = pr[6] / mag;
+    float z[3];
+    bsx_normal3(a.seed, (1u << 30) + 2 * a.refine_count + k, j, z);
+    const float vx = bsx_expf(pr[7]) * z[0], vy = bsx_expf(pr[8]) * z[1], vz = bsx_expf(pr[9]) * z[2];
+    const float qw2 = qw * qw, qx2 = qx * qx, qy2 = qy * qy, qz2 = qz * qz;
+    const float xy = qx * qy, xz = qx * qz, yz = qy * qz, wx = qw * qx, wy = qw * qy, wz = qw * qz;
+    const float d[3] = {(qw2 + qx2 - qy2 - qz2) * vx + (xy * vy + xz * vz + wy * vz - wz * vy) * 2.0f,
+                        (qw2 - qx2 + qy2 - qz2) * vy + (xy * vx + yz * vz + wz * vx - wx * vz) * 2.0f,
+                        (qw2 - qx2 - qy2 + qz2) * vz + (xz * vx + yz * vy + wx * vy - wy * vx) * 2.0f};
+    float* cr = a.nt + (size_t)r * 10;
+    for (int c = 0; c < 3; ++c) cr[c] = pr[c] + d[c];
+    for (int c = 0; c < 4; ++c) cr[3 + c] = pr[3 + c];
+    for (int c = 0; c < 3; ++c) cr[7 + c] = bsx_logf(bsx_expf(pr[7 + c]) / 1.6f);
+    for (uint32_t c = 0; c < a.c3; ++c) a.nsh[(size_t)r * a.c3 + c] = a.sh[(size_t)i * a.c3 + c];
+    a.nop[r] = a.op[i];
+}
+
 uint32_t blocks_for(uint64_t n) { return (uint32_t)((n + kRefThreads - 1) / kRefThreads); }
 
 // Reads `count` u32 from the device (synchronises the stream).
@@ -426,6 +504,67 @@ extern "C" bsx_status bsx_trainer_refine_plan(bsx_trainer* tr, const float* t, c
     }
     tr->plan_kept = K;
     const uint32_t pruned = n - K;
+    if (cfg->rule == BSX_REFINE_GRAD_THRESHOLD) {
+        if (!tr->cfg.accumulate_grad2d)
+            return fail(ctx, BSX_ERR_STATE, "the gradient-threshold rule needs a trainer with accumulate_grad2d");
+        // scratch (u32): [0, n) flags, [n, 2n) positions, [2n, 3n) clone rows, [3n, 4n) rows that stay,
+        // [4n, 5n) their positions, counters at 5n, the stay flags at 5n + 32
+        float* st = tr->stats.as<float>();
+        uint32_t* cflag = scratch;
+        uint32_t* cpos = scratch + n;
+        uint32_t* clone_rows = scratch + 2 * (size_t)n;
+        uint32_t* stay_rows = scratch + 3 * (size_t)n;
+        uint32_t* stay_pos = scratch + 4 * (size_t)n;
+        uint32_t* stay = scratch + (size_t)n * 5 + 32;
+        uint32_t* sflag = stay;  // split flags first, then (take_first) the stay flags
+        s = ensure(ctx, tr->plan_split, ((size_t)K + 1) * 4);
+        if (s != BSX_OK) return s;
+        uint32_t* split_rows = tr->plan_split.as<uint32_t>();
+        uint32_t cand[2] = {0, 0};
+        if (K) {
+            const float dense = cfg->percent_dense * max_extent;
+            prof_begin(ctx);
+            grad_select_kernel<<<blocks_for(K), kRefThreads, 0, ctx->stream>>>(
+                keep, K, t, st + tr->n, st + 3 * (size_t)tr->n, cfg->growth_grad_threshold, dense, cflag, sflag);
+            s = post_launch(ctx, "grad_select_kernel");
+            if (s == BSX_OK) s = scan_inclusive_u32(ctx, cflag, nullptr, K, cpos, counters + 2);
+            if (s == BSX_OK) s = scan_inclusive_u32(ctx, sflag, nullptr, K, stay_pos, counters + 3);
+            if (s == BSX_OK) s = read_u32(ctx, counters + 2, 2, cand);
+            if (s != BSX_OK) return s;
+        }
+        uint32_t budget = sat_sub(cfg->max_splats, K);
+        const uint32_t C = std::min(cand[0], budget);
+        budget -= C;
+        const uint32_t S = std::min(cand[1], budget);
+        if (K) {
+            prof_begin(ctx);
+            take_first_kernel<<<blocks_for(K), kRefThreads, 0, ctx->stream>>>(cflag, cpos, K, C, clone_rows, nullptr);
+            s = post_launch(ctx, "take_first_kernel");
+            if (s != BSX_OK) return s;
+            prof_begin(ctx);
+            // split rows in order; the flags become "stays" (1 = not split)
+            take_first_kernel<<<blocks_for(K), kRefThreads, 0, ctx->stream>>>(sflag, stay_pos, K, S, split_rows, stay);
+            s = post_launch(ctx, "take_first_kernel");
+            if (s == BSX_OK) s = scan_inclusive_u32(ctx, stay, nullptr, K, stay_pos, nullptr);
+            if (s != BSX_OK) return s;
+            prof_begin(ctx);
+            scatter_flagged_kernel<<<blocks_for(K), kRefThreads, 0, ctx->stream>>>(stay, stay_pos, K, stay_rows);
+            s = post_launch(ctx, "scatter_flagged_kernel");
+            if (s != BSX_OK) return s;
+        }
+        tr->plan_clone_count = C;
+        tr->plan_split_count = S;
+        tr->planned = true;
+        if (stats) {
+            stats->num_added = C + S;
+            stats->num_split_oversized = 0;
+            stats->num_split_high_grad = S;
+            stats->num_pruned = pruned;
+            stats->num_pruned_non_finite = non_finite;
+            stats->total_splats = K + C + S;
+        }
+        return BSX_OK;
+    }
     const uint32_t stream0 = 2 * tr->refines;
     // split membership of the kept rows; the reference's HashSet (train.rs:1366)
     uint32_t* mark = scratch + (size_t)n * 5 + 32;
@@ -514,10 +653,12 @@ extern "C" bsx_status bsx_trainer_refine_apply(bsx_trainer* tr, const float* t, 
     if (!tr) return BSX_ERR_INVALID_ARG;
     bsx_ctx* ctx = tr->ctx;
     if (!tr->planned) return fail(ctx, BSX_ERR_STATE, "bsx_trainer_refine_apply needs a fresh bsx_trainer_refine_plan");
-    const uint32_t K = tr->plan_kept, S = tr->plan_split_count, N2 = K + S, n = tr->n, c3 = 3 * tr->coeffs;
+    const bsx_refine_config& cfg = tr->plan_cfg;
+    const bool gt_rule = cfg.rule == BSX_REFINE_GRAD_THRESHOLD;
+    const uint32_t C = gt_rule ? tr->plan_clone_count : 0;
+    const uint32_t K = tr->plan_kept, S = tr->plan_split_count, N2 = K + S + C, n = tr->n, c3 = 3 * tr->coeffs;
     if (N2 && (!t || !sh || !op || !nt || !nsh || !nop)) return BSX_ERR_INVALID_ARG;
     cudaSetDevice(ctx->device);
-    const bsx_refine_config& cfg = tr->plan_cfg;
     // old moments (zeros if no optimizer step has been taken yet)
     float* m_old[3];
     float* v_old[3];
@@ -542,7 +683,65 @@ extern "C" bsx_status bsx_trainer_refine_apply(bsx_trainer* tr, const float* t, 
     } gathers[9] = {{t, nt, 10},         {sh, nsh, c3},       {op, nop, 1},
                     {m_old[0], m_new[0], 10}, {m_old[1], m_new[1], c3}, {m_old[2], m_new[2], 1},
                     {v_old[0], v_new[0], 10}, {v_old[1], v_new[1], 1},  {v_old[2], v_new[2], 1}};
-    if (K)
+    if (gt_rule) {
+        // rows: the K - S kept rows that stay, C clones, S first children, S second children;
+        // new rows start with zero moments
+        uint32_t* scratch = tr->plan_scratch.as<uint32_t>();
+        uint32_t* stay_rows = scratch + 3 * (size_t)n;
+        uint32_t* orig = scratch;  // original ids of the stays, then of the clones
+        const uint32_t K2 = K - S;
+        s = check_cuda(ctx, cudaMemsetAsync(tr->moments_next.p, 0, moment_floats(N2, tr->coeffs) * 4, ctx->stream),
+                       "memset new moments");
+        if (s != BSX_OK) return s;
+        if (K2) {
+            prof_begin(ctx);
+            compose_kernel<<<blocks_for(K2), kRefThreads, 0, ctx->stream>>>(keep, stay_rows, K2, orig);
+            s = post_launch(ctx, "compose_kernel");
+            if (s != BSX_OK) return s;
+            for (const G& g : gathers) {
+                prof_begin(ctx);
+                gather_rows_kernel<<<blocks_for((uint64_t)K2 * g.cols), kRefThreads, 0, ctx->stream>>>(g.src, orig, K2,
+                                                                                                       g.cols, g.dst);
+                s = post_launch(ctx, "gather_rows_kernel");
+                if (s != BSX_OK) return s;
+            }
+        }
+        if (C) {
+            prof_begin(ctx);
+            compose_kernel<<<blocks_for(C), kRefThreads, 0, ctx->stream>>>(keep, scratch + 2 * (size_t)n, C, orig);
+            s = post_launch(ctx, "compose_kernel");
+            if (s != BSX_OK) return s;
+            for (int k = 0; k < 3; ++k) {
+                const G& g = gathers[k];
+                prof_begin(ctx);
+                gather_rows_kernel<<<blocks_for((uint64_t)C * g.cols), kRefThreads, 0, ctx->stream>>>(
+                    g.src, orig, C, g.cols, g.dst + (size_t)K2 * g.cols);
+                s = post_launch(ctx, "gather_rows_kernel");
+                if (s != BSX_OK) return s;
+            }
+        }
+        if (S) {
+            GtSplitArgs a;
+            a.split = tr->plan_split.as<uint32_t>();
+            a.keep = keep;
+            a.t = t;
+            a.sh = sh;
+            a.op = op;
+            a.nt = nt;
+            a.nsh = nsh;
+            a.nop = nop;
+            a.S = S;
+            a.c3 = c3;
+            a.base = K2 + C;
+            a.refine_count = tr->refines;
+            a.seed = cfg.seed;
+            prof_begin(ctx);
+            grad_split_kernel<<<blocks_for(2 * (uint64_t)S), kRefThreads, 0, ctx->stream>>>(a);
+            s = post_launch(ctx, "grad_split_kernel");
+            if (s != BSX_OK) return s;
+        }
+    }
+    if (K && !gt_rule)
         for (const G& g : gathers) {
             prof_begin(ctx);
             gather_rows_kernel<<<blocks_for((uint64_t)K * g.cols), kRefThreads, 0, ctx->stream>>>(g.src, keep, K,
@@ -550,7 +749,7 @@ extern "C" bsx_status bsx_trainer_refine_apply(bsx_trainer* tr, const float* t, 
             s = post_launch(ctx, "gather_rows_kernel");
             if (s != BSX_OK) return s;
         }
-    if (S) {
+    if (S && !gt_rule) {
         SplitArgs a;
         a.split = tr->plan_split.as<uint32_t>();
         a.keep = keep;
@@ -575,7 +774,7 @@ extern "C" bsx_status bsx_trainer_refine_apply(bsx_trainer* tr, const float* t, 
         s = post_launch(ctx, "split_kernel");
         if (s != BSX_OK) return s;
     }
-    if (N2) {
+    if (N2 && !gt_rule) {
         const float train_t = bsx_min(bsx_max((float)phase_iter / (float)std::max(phase_total, 1u), 0.0f), 1.0f);
         const float t_shrink = 1.0f - train_t;
         prof_begin(ctx);
@@ -593,9 +792,10 @@ extern "C" bsx_status bsx_trainer_refine_apply(bsx_trainer* tr, const float* t, 
     tr->n = N2;
     const size_t nn = N2 ? N2 : 1;
     s = ensure(ctx, tr->v_combined, nn * BSX_GRAD_STRIDE * 4);
-    if (s == BSX_OK) s = ensure(ctx, tr->stats, 3 * nn * 4);
+    if (s == BSX_OK) s = ensure(ctx, tr->stats, kRecordArrays * nn * 4);
     if (s == BSX_OK)
-        s = check_cuda(ctx, cudaMemsetAsync(tr->stats.p, 0, 3 * nn * 4, ctx->stream), "reset refine record");
+        s = check_cuda(ctx, cudaMemsetAsync(tr->stats.p, 0, kRecordArrays * nn * 4, ctx->stream),
+                       "reset refine record");
     if (s != BSX_OK) return s;
     tr->planned = false;
     tr->refines++;

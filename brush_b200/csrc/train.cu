@@ -61,18 +61,34 @@ __device__ __forceinline__ void noise_row(const NoiseArgs& z, uint32_t i, float 
 // same pass applies the mean noise, gated on the visibility sum it has just
 // written (the reference's RefineRecord::vis_mask gate) unless a gate array is
 // given.
+// View-space gradient statistic of the gradient-threshold densification rule
+// (the classic 3DGS densify_and_clone / densify_and_split): the norm of the
+// step's screen-space mean gradient in normalised device units, summed over
+// the steps in which the splat was visible.
+struct Grad2dArgs {
+    const float* vgrad;  // raster-backward rows [N,12] (lanes 0-1: d loss / d screen mean, pixels); null: off
+    float* accum;        // [N] running sum
+    float half_w, half_h;  // d pixel / d ndc
+};
+
 template <bool STATS, bool NOISE>
 __global__ void __launch_bounds__(kStatsThreads)
     gather_stats_kernel(const float* __restrict__ refine, const float* __restrict__ visible,
                         const float* __restrict__ radius, uint32_t n, float* __restrict__ rmax,
-                        float* __restrict__ vsum, float* __restrict__ smax, const NoiseArgs nz) {
+                        float* __restrict__ vsum, float* __restrict__ smax, const NoiseArgs nz, const Grad2dArgs g2) {
     for (uint32_t i = blockIdx.x * kStatsThreads + threadIdx.x; i < n; i += gridDim.x * kStatsThreads) {
         float vs = 0.0f;
         if (STATS) {
             if (refine) rmax[i] = bsx_max(rmax[i], refine[i]);
-            vs = vsum[i] + visible[i];
+            const float vi = visible[i];
+            vs = vsum[i] + vi;
             vsum[i] = vs;
             smax[i] = bsx_max(smax[i], radius[i]);
+            if (g2.vgrad && vi > 0.0f) {
+                const float2 v = __ldg(reinterpret_cast<const float2*>(g2.vgrad + (size_t)i * kGradStride));
+                const float gx = v.x * g2.half_w, gy = v.y * g2.half_h;
+                g2.accum[i] = g2.accum[i] + sqrtf(gx * gx + gy * gy);
+            }
         }
         if (NOISE) noise_row(nz, i, nz.gate ? __ldg(nz.gate + i) : vs);
     }
@@ -222,18 +238,25 @@ bsx_status step_epilogue(bsx_trainer* tr, const float* refine, const bsx_render_
     float* rmax = st;
     float* vsum = st ? st + n : nullptr;
     float* smax = st ? st + 2 * n : nullptr;
+    Grad2dArgs g2{nullptr, nullptr, 0.0f, 0.0f};
+    if (stats && tr->cfg.accumulate_grad2d) {
+        g2.vgrad = tr->v_combined.as<float>();
+        g2.accum = st + 3 * n;
+        g2.half_w = 0.5f * (float)out.uniforms.img_w;
+        g2.half_h = 0.5f * (float)out.uniforms.img_h;
+    }
     const uint32_t blocks = stats_blocks(tr->n);
     cudaStream_t s = tr->ctx->stream;
     prof_begin(tr->ctx);
     if (stats && noise)
         gather_stats_kernel<true, true><<<blocks, kStatsThreads, 0, s>>>(refine, out.d_visible, out.d_max_radius,
-                                                                         tr->n, rmax, vsum, smax, nz);
+                                                                         tr->n, rmax, vsum, smax, nz, g2);
     else if (stats)
         gather_stats_kernel<true, false><<<blocks, kStatsThreads, 0, s>>>(refine, out.d_visible, out.d_max_radius,
-                                                                          tr->n, rmax, vsum, smax, nz);
+                                                                          tr->n, rmax, vsum, smax, nz, g2);
     else
         gather_stats_kernel<false, true><<<blocks, kStatsThreads, 0, s>>>(refine, out.d_visible, out.d_max_radius,
-                                                                          tr->n, rmax, vsum, smax, nz);
+                                                                          tr->n, rmax, vsum, smax, nz, g2);
     return post_launch(tr->ctx, "gather_stats_kernel");
 }
 
@@ -277,9 +300,10 @@ bsx_status bsx_trainer_create(bsx_ctx* ctx, uint32_t n, uint32_t coeffs, const b
     const size_t nn = n ? n : 1;
     bsx_status s = ensure(ctx, tr->v_combined, nn * BSX_GRAD_STRIDE * 4);
     if (s == BSX_OK && cfg->gather_stats) {
-        s = ensure(ctx, tr->stats, 3 * nn * 4);
+        s = ensure(ctx, tr->stats, kRecordArrays * nn * 4);
         if (s == BSX_OK)
-            s = check_cuda(ctx, cudaMemsetAsync(tr->stats.p, 0, 3 * nn * 4, ctx->stream), "memset refine record");
+            s = check_cuda(ctx, cudaMemsetAsync(tr->stats.p, 0, kRecordArrays * nn * 4, ctx->stream),
+                           "memset refine record");
     }
     if (s != BSX_OK) {
         bsx_trainer_destroy(tr);
@@ -366,7 +390,7 @@ bsx_status bsx_trainer_reserve(bsx_trainer* tr, uint32_t max_splats) {
               {&ctx->visible, m * 4},
               {&tr->grads, (m * (11 + c3) + m) * 4 + 64},
               {&tr->v_combined, m * BSX_GRAD_STRIDE * 4},
-              {&tr->stats, 3 * m * 4},
+              {&tr->stats, kRecordArrays * m * 4},
               {&tr->moments, moment_floats((uint32_t)m, tr->coeffs) * 4 + 64},
               {&tr->moments_next, moment_floats((uint32_t)m, tr->coeffs) * 4 + 64},
               {&tr->plan_keep, (m + 1) * 4},
@@ -391,6 +415,13 @@ bsx_status bsx_trainer_reserve(bsx_trainer* tr, uint32_t max_splats) {
 bsx_status bsx_trainer_set_median_scale(bsx_trainer* tr, float median_scale) {
     if (!tr || !(median_scale > 0.0f)) return BSX_ERR_INVALID_ARG;
     tr->cfg.median_scale = median_scale;
+    return BSX_OK;
+}
+
+bsx_status bsx_trainer_grad2d_accum(bsx_trainer* tr, float** d_accum) {
+    if (!tr || !d_accum) return BSX_ERR_INVALID_ARG;
+    if (!tr->cfg.gather_stats) return fail(tr->ctx, BSX_ERR_STATE, "trainer created without gather_stats");
+    *d_accum = tr->stats.as<float>() + 3 * (size_t)tr->n;
     return BSX_OK;
 }
 

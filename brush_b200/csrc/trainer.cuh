@@ -15,12 +15,16 @@ struct bsx_trainer {
     int keep_grads = 0;  // bsx_train_step also writes the dense gradients
     // densification: the plan of the last bsx_trainer_refine_plan
     bool planned = false;
-    uint32_t plan_n = 0, plan_kept = 0, plan_split_count = 0, refines = 0;
+    uint32_t plan_n = 0, plan_kept = 0, plan_split_count = 0, plan_clone_count = 0, refines = 0;
     bsx_refine_config plan_cfg{};
     bsx::DevBuf plan_keep, plan_split, plan_scratch, moments_next;
 };
 
 namespace bsx {
+
+// RefineRecord arrays per splat: refine-weight MAX, visibility SUM, screen-size
+// MAX, view-space gradient-norm SUM (the gradient-threshold densification rule).
+constexpr size_t kRecordArrays = 4;
 
 // Moment views over one buffer of `rows` rows:
 // m: [rows,10] | [rows,3C] | [rows,1]; v: [rows,10] | [rows] | [rows,1],

@@ -63,6 +63,8 @@ class TrainConfig:
     mean_noise_weight: float = 50.0
     mrnf_noise_injection: bool = True
     noise_seed: int = 42
+    # keep the view-space gradient-norm sum the gradient-threshold densification rule reads
+    accumulate_grad2d: bool = False
 
     def to_c(self, median_scale: float, render_mode: int, gather_stats: bool) -> _lib.TrainConfig:
         c = _lib.TrainConfig()
@@ -82,6 +84,7 @@ class TrainConfig:
         c.noise_vis_gate = int(self.mrnf_noise_injection)
         c.mean_noise_weight = float(self.mean_noise_weight)
         c.noise_seed = int(self.noise_seed)
+        c.accumulate_grad2d = int(self.accumulate_grad2d)
         return c
 
 
@@ -106,6 +109,12 @@ class RefineConfig:
     split_other_axis_scale: float = 0.85
     split_opacity_scale: float = 0.6
     seed: int = 42
+    # _lib.REFINE_REFERENCE: the reference's refine_for_phase; _lib.REFINE_GRAD_THRESHOLD: the
+    # original 3DGS rule (average view-space gradient norm >= growth_grad_threshold: clone
+    # splats whose largest scale is <= percent_dense x the bounds extent, split the others
+    # into two), which needs TrainConfig.accumulate_grad2d
+    rule: int = _lib.REFINE_REFERENCE
+    percent_dense: float = 0.01
 
     def to_c(self) -> _lib.RefineConfig:
         c = _lib.RefineConfig()
@@ -129,10 +138,12 @@ class TrainStepStats:
 
 @dataclass
 class RefineRecord:
-    """``RefineRecord`` statistics (crates/brush-train/src/stats.rs:11-127)."""
+    """``RefineRecord`` statistics (crates/brush-train/src/stats.rs:11-127), plus the
+    view-space gradient-norm sum of the gradient-threshold rule (native trainer)."""
     refine_weight_norm: torch.Tensor
     vis_weight: torch.Tensor
     max_screen_size: torch.Tensor
+    grad2d_accum: torch.Tensor | None = None
 
     @staticmethod
     def new(n: int, device) -> "RefineRecord":
@@ -177,8 +188,9 @@ class _NativeTrainer:
     def record(self) -> RefineRecord | None:
         if not self.gather:
             return None
-        p = [C.c_void_p() for _ in range(3)]
-        self.ctx.check(_lib.lib().bsx_trainer_stats_buffers(self.handle, *[C.byref(x) for x in p]))
+        p = [C.c_void_p() for _ in range(4)]
+        self.ctx.check(_lib.lib().bsx_trainer_stats_buffers(self.handle, *[C.byref(x) for x in p[:3]]))
+        self.ctx.check(_lib.lib().bsx_trainer_grad2d_accum(self.handle, C.byref(p[3])))
         return RefineRecord(*[device_view(x.value, (self.n,), torch.float32, self.device) for x in p])
 
     def optimizer_state(self):
@@ -487,6 +499,8 @@ class SplatTrainer:
         exchange) and give every rank the full optimizer state (all-gather of the row shards)."""
         rec = self.record
         torch.distributed.all_reduce(rec.vis_weight, op=torch.distributed.ReduceOp.SUM, group=self.pg)
+        if self.config.accumulate_grad2d:
+            torch.distributed.all_reduce(rec.grad2d_accum, op=torch.distributed.ReduceOp.SUM, group=self.pg)
         torch.distributed.all_reduce(rec.max_screen_size, op=torch.distributed.ReduceOp.MAX, group=self.pg)
         state = self.native.optimizer_state()
         n, w = self.n, self.world

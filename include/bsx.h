@@ -381,6 +381,10 @@ typedef struct bsx_train_config {        /* TrainConfig subset (crates/brush-tra
     int32_t noise_vis_gate;              /* 1: accumulated visibility (mrnf_noise_injection), 0: this step's */
     float mean_noise_weight;             /* 50 */
     uint64_t noise_seed;
+    /* 1: also sum, over the steps a splat is visible, the norm of its screen-space
+     * mean gradient in normalised device units (|d loss / d xy_pixels * (W/2, H/2)|),
+     * the signal of BSX_REFINE_GRAD_THRESHOLD (bsx_trainer_grad2d_accum) */
+    int32_t accumulate_grad2d;
 } bsx_train_config;
 
 typedef struct bsx_train_stats {
@@ -416,6 +420,8 @@ BSX_API bsx_status bsx_trainer_destroy(bsx_trainer* tr);
  * zeroed at creation; valid while the trainer lives. */
 BSX_API bsx_status bsx_trainer_stats_buffers(bsx_trainer* tr, float** d_refine_weight_norm, float** d_vis_weight,
                                              float** d_max_screen_size);
+/* The view-space gradient-norm sum [N] (accumulate_grad2d); zeroed with the record. */
+BSX_API bsx_status bsx_trainer_grad2d_accum(bsx_trainer* tr, float** d_grad2d_accum);
 /* Dense gradients of the last step ([N,10], [N,C,3], [N], refine weight [N]).
  * bsx_train_step applies AdamScaled inside the projection backward, so it
  * writes the dense gradients only after bsx_trainer_keep_gradients(tr, 1);
@@ -467,6 +473,23 @@ BSX_API bsx_status bsx_train_step_dp(bsx_trainer* tr, const bsx_camera* cam, uin
  * generator (SplitMix64 of seed, refine count and index): deterministic, and
  * the same distribution as the reference's, not the same draws. The growth
  * signal is the gradient norm (error-map / edge-map growth are not built). */
+/* Densification rules:
+ *   BSX_REFINE_REFERENCE: the reference's refine_for_phase (above).
+ *   BSX_REFINE_GRAD_THRESHOLD: the gradient-threshold rule of the original 3D
+ *   Gaussian splatting trainer (Kerbl et al. 2023, densify_and_clone /
+ *   densify_and_split / prune), which the densification benchmark describes:
+ *   after the same prune mask, every kept splat whose view-space gradient norm
+ *   averaged over its visible steps (grad2d_accum / vis_weight) is at least
+ *   growth_grad_threshold is cloned (a copy appended) when its largest scale is
+ *   at most percent_dense times the largest bounds extent, else split: it is
+ *   replaced by two children at mean + R (s * n), n ~ N(0,1)^3 from the
+ *   counter-based generator, with scales s / 1.6 and the other parameters
+ *   copied. New rows have zero Adam moments; no opacity or scale decay. Rows:
+ *   kept splats that are not split (in order), clones, first children, second
+ *   children; clones then splits are cut to max_splats in row order. Needs a
+ *   trainer with accumulate_grad2d. */
+#define BSX_REFINE_REFERENCE 0
+#define BSX_REFINE_GRAD_THRESHOLD 1
 typedef struct bsx_refine_config {       /* refine options (crates/brush-train/src/config.rs:100-330) */
     uint32_t max_splats;                 /* 10,000,000 */
     float growth_grad_threshold;         /* 0.0025 */
@@ -485,6 +508,8 @@ typedef struct bsx_refine_config {       /* refine options (crates/brush-train/s
     float split_other_axis_scale;        /* 0.85 */
     float split_opacity_scale;           /* 0.6 */
     uint64_t seed;
+    int32_t rule;                        /* BSX_REFINE_REFERENCE or BSX_REFINE_GRAD_THRESHOLD */
+    float percent_dense;                 /* 0.01: clone / split boundary (gradient-threshold rule) */
 } bsx_refine_config;
 
 typedef struct bsx_refine_stats {        /* RefineStats (train.rs:1520-1530) */

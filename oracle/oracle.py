@@ -47,7 +47,8 @@ class RefineCfg(C.Structure):
                 ("near_zero_rotation_prune", C.c_int32), ("radial_bounds_prune", C.c_int32),
                 ("min_opacity", C.c_float), ("prune_extent_factor", C.c_float),
                 ("split_long_axis_scale", C.c_float), ("split_other_axis_scale", C.c_float),
-                ("split_opacity_scale", C.c_float), ("seed", C.c_uint64)]
+                ("split_opacity_scale", C.c_float), ("seed", C.c_uint64), ("rule", C.c_int32),
+                ("percent_dense", C.c_float)]
 
 
 class RefineStats(C.Structure):
@@ -107,6 +108,10 @@ def lib() -> C.CDLL:
         _lib.orc_refine_plan.argtypes = [f32p, f32p, f32p, f32p, f32p, f32p, C.c_uint32, C.c_uint32,
                                          C.POINTER(RefineCfg), f32p, f32p, C.c_uint32, C.c_uint32,
                                          C.POINTER(RefineStats)]
+        _lib.orc_refine_plan2.restype = C.c_void_p
+        _lib.orc_refine_plan2.argtypes = [f32p, f32p, f32p, f32p, f32p, f32p, f32p, C.c_uint32, C.c_uint32,
+                                          C.POINTER(RefineCfg), f32p, f32p, C.c_uint32, C.c_uint32,
+                                          C.POINTER(RefineStats)]
         _lib.orc_refine_plan_rows.argtypes = [C.c_void_p, u32p, u32p]
         _lib.orc_refine_apply.argtypes = [C.c_void_p] + [f32p] * 18 + [C.c_uint32, C.c_uint32]
         _lib.orc_refine_free.argtypes = [C.c_void_p]
@@ -423,7 +428,8 @@ def refine_cfg(**kw) -> RefineCfg:
              growth_stop_iter=15000, split_at_screen_size=0.5, opac_decay=0.004, scale_decay=0.002,
              min_scale_prune=1, min_scale_prune_threshold=1e-10, near_zero_rotation_prune=1,
              radial_bounds_prune=0, min_opacity=1.0 / 255.0, prune_extent_factor=100.0,
-             split_long_axis_scale=0.5, split_other_axis_scale=0.85, split_opacity_scale=0.6, seed=42)
+             split_long_axis_scale=0.5, split_other_axis_scale=0.85, split_opacity_scale=0.6, seed=42, rule=0,
+             percent_dense=0.01)
     d.update(kw)
     c = RefineCfg()
     for k, v in d.items():
@@ -441,19 +447,23 @@ def refine_prune_mask(t, sh, op, cfg, center, max_allowed):
 
 
 def refine(t, sh, op, record, moments, cfg, center, extent, global_iter, refine_count, phase_iter, phase_total):
-    """Prune / replace / split / grow (train.rs:1191-1860). record = (refine_norm, vis, screen);
+    """Prune / replace / split / grow (train.rs:1191-1860), or with cfg.rule = 1 the gradient-threshold
+    clone / split rule. record = (refine_norm, vis, screen[, grad2d_accum]);
     moments = ((m_t [n,10], m_s [n,3C], m_o [n]), (v_t [n,10], v_s [n], v_o [n])). Returns
     dict(stats, keep, split, transforms, sh, opac, m, v)."""
     n, c = t.shape[0], sh.shape[1]
     st = RefineStats()
-    h = lib().orc_refine_plan(_f32(t).reshape(-1), _f32(sh).reshape(-1), _f32(op).reshape(-1),
-                              *[_f32(x).reshape(-1) for x in record], n, c, C.byref(cfg), _f32(center),
-                              _f32(extent), int(global_iter), int(refine_count), C.byref(st))
+    grad2d = record[3] if len(record) > 3 else np.zeros(n, np.float32)
+    h = lib().orc_refine_plan2(_f32(t).reshape(-1), _f32(sh).reshape(-1), _f32(op).reshape(-1),
+                               *[_f32(x).reshape(-1) for x in record[:3]], _f32(grad2d).reshape(-1), n, c,
+                               C.byref(cfg), _f32(center), _f32(extent), int(global_iter), int(refine_count),
+                               C.byref(st))
     try:
         K = st.total_splats - st.num_added
         keep = np.empty(max(K, 1), np.uint32)
         split = np.empty(max(st.num_added, 1), np.uint32)
-        lib().orc_refine_plan_rows(h, keep, split)
+        if cfg.rule == 0:
+            lib().orc_refine_plan_rows(h, keep, split)
         n2 = st.total_splats
         nt, nsh, nop = np.empty((n2, 10), np.float32), np.empty((n2, c, 3), np.float32), np.empty(n2, np.float32)
         nm = (np.empty((n2, 10), np.float32), np.empty((n2, 3 * c), np.float32), np.empty(n2, np.float32))

@@ -59,13 +59,110 @@ float clampf(float x, float lo, float hi) { return bsx_min(bsx_max(x, lo), hi); 
 uint32_t sat_sub(uint32_t a, uint32_t b) { return a > b ? a - b : 0u; }
 
 struct Plan {
-    uint32_t n = 0, coeffs = 0;
+    uint32_t n = 0, coeffs = 0, refine_count = 0;
     std::vector<uint32_t> keep;   // kept original indices, ascending
     std::vector<uint32_t> split;  // split rows in the kept numbering, ascending
+    std::vector<uint32_t> clone;  // gradient-threshold rule: cloned rows (kept numbering), ascending
     std::vector<float> screen;    // max_screen_size of the kept rows
     bsx_refine_config cfg{};
     bsx_refine_stats stats{};
 };
+
+// The gradient-threshold rule (the original 3D Gaussian splatting trainer's
+// densify_and_clone / densify_and_split, Kerbl et al. 2023) on the kept rows:
+// average view-space gradient norm = accum / visible steps (0 where never
+// visible) >= threshold selects a row; a selected row whose largest scale is
+// at most percent_dense x the largest bounds extent is cloned, any other is
+// split; clones then splits are cut to the max_splats budget in row order.
+void plan_grad_threshold(Plan* p, const float* t, const float* vis, const float* grad2d, float max_extent) {
+    const bsx_refine_config& c = p->cfg;
+    const uint32_t K = (uint32_t)p->keep.size();
+    const float dense = c.percent_dense * max_extent;
+    std::vector<uint32_t> clone, split;
+    for (uint32_t j = 0; j < K; ++j) {
+        const uint32_t i = p->keep[j];
+        const float avg = vis[i] > 0.0f ? grad2d[i] / vis[i] : 0.0f;
+        if (!(avg >= c.growth_grad_threshold)) continue;
+        const float* r = t + (size_t)i * 10;
+        const float smax = bsx_max(bsx_max(bsx_expf(r[7]), bsx_expf(r[8])), bsx_expf(r[9]));
+        (smax <= dense ? clone : split).push_back(j);
+    }
+    uint32_t budget = sat_sub(c.max_splats, K);
+    if (clone.size() > budget) clone.resize(budget);
+    budget -= (uint32_t)clone.size();
+    if (split.size() > budget) split.resize(budget);
+    p->clone = clone;
+    p->split = split;
+}
+
+// Rows of the gradient-threshold rule: kept rows that are not split (in order),
+// clones, first children, second children. Split children: mean + R(q) (s * n)
+// with n = bsx_normal3(seed, stream, kept row), stream 2^30 + 2 refine_count + k
+// for child k, R the rotation of the normalised quaternion, s = exp(log-scale);
+// log-scale log(s / 1.6); rotation, SH and opacity copied. New rows have zero
+// moments.
+void apply_grad_threshold(const Plan* p, const float* t, const float* sh, const float* op, const float* m_t,
+                          const float* m_s, const float* m_o, const float* v_t, const float* v_s, const float* v_o,
+                          float* nt, float* nsh, float* nop, float* nm_t, float* nm_s, float* nm_o, float* nv_t,
+                          float* nv_s, float* nv_o) {
+    const uint32_t K = (uint32_t)p->keep.size(), C = (uint32_t)p->clone.size(), S = (uint32_t)p->split.size();
+    const uint32_t c3 = 3 * p->coeffs;
+    std::vector<uint8_t> is_split(K, 0);
+    for (uint32_t j : p->split) is_split[j] = 1;
+    auto zero_moments = [&](uint32_t r) {
+        memset(nm_t + (size_t)r * 10, 0, 40);
+        memset(nm_s + (size_t)r * c3, 0, (size_t)c3 * 4);
+        nm_o[r] = 0.0f;
+        memset(nv_t + (size_t)r * 10, 0, 40);
+        nv_s[r] = 0.0f;
+        nv_o[r] = 0.0f;
+    };
+    uint32_t r = 0;
+    for (uint32_t j = 0; j < K; ++j) {
+        if (is_split[j]) continue;
+        const uint32_t i = p->keep[j];
+        memcpy(nt + (size_t)r * 10, t + (size_t)i * 10, 40);
+        memcpy(nsh + (size_t)r * c3, sh + (size_t)i * c3, (size_t)c3 * 4);
+        nop[r] = op[i];
+        memcpy(nm_t + (size_t)r * 10, m_t + (size_t)i * 10, 40);
+        memcpy(nm_s + (size_t)r * c3, m_s + (size_t)i * c3, (size_t)c3 * 4);
+        nm_o[r] = m_o[i];
+        memcpy(nv_t + (size_t)r * 10, v_t + (size_t)i * 10, 40);
+        nv_s[r] = v_s[i];
+        nv_o[r] = v_o[i];
+        ++r;
+    }
+    for (uint32_t q = 0; q < C; ++q, ++r) {
+        const uint32_t i = p->keep[p->clone[q]];
+        memcpy(nt + (size_t)r * 10, t + (size_t)i * 10, 40);
+        memcpy(nsh + (size_t)r * c3, sh + (size_t)i * c3, (size_t)c3 * 4);
+        nop[r] = op[i];
+        zero_moments(r);
+    }
+    for (uint32_t k = 0; k < 2; ++k)
+        for (uint32_t q = 0; q < S; ++q, ++r) {
+            const uint32_t j = p->split[q], i = p->keep[j];
+            const float* pr = t + (size_t)i * 10;
+            const float mag = bsx_max(sqrtf(pr[3] * pr[3] + pr[4] * pr[4] + pr[5] * pr[5] + pr[6] * pr[6]), 1e-32f);
+            const float qw = pr[3] / mag, qx = pr[4] / mag, qy = pr[5] / mag, qz = pr[6] / mag;
+            float z[3];
+            bsx_normal3(p->cfg.seed, (1u << 30) + 2 * p->refine_count + k, j, z);
+            const float vx = bsx_expf(pr[7]) * z[0], vy = bsx_expf(pr[8]) * z[1], vz = bsx_expf(pr[9]) * z[2];
+            const float qw2 = qw * qw, qx2 = qx * qx, qy2 = qy * qy, qz2 = qz * qz;
+            const float xy = qx * qy, xz = qx * qz, yz = qy * qz, wx = qw * qx, wy = qw * qy, wz = qw * qz;
+            const float d[3] = {
+                (qw2 + qx2 - qy2 - qz2) * vx + (xy * vy + xz * vz + wy * vz - wz * vy) * 2.0f,
+                (qw2 - qx2 + qy2 - qz2) * vy + (xy * vx + yz * vz + wz * vx - wx * vz) * 2.0f,
+                (qw2 - qx2 - qy2 + qz2) * vz + (xz * vx + yz * vy + wx * vy - wy * vx) * 2.0f};
+            float* cr = nt + (size_t)r * 10;
+            for (int a = 0; a < 3; ++a) cr[a] = pr[a] + d[a];
+            for (int a = 0; a < 4; ++a) cr[3 + a] = pr[3 + a];
+            for (int a = 0; a < 3; ++a) cr[7 + a] = bsx_logf(bsx_expf(pr[7 + a]) / 1.6f);
+            memcpy(nsh + (size_t)r * c3, sh + (size_t)i * c3, (size_t)c3 * 4);
+            nop[r] = op[i];
+            zero_moments(r);
+        }
+}
 
 }  // namespace
 
@@ -112,14 +209,15 @@ void orc_refine_prune_mask(const float* t, const float* sh, const float* op, uin
 
 // Decide the refine (train.rs:1258-1500). refine_norm / vis / screen are the
 // RefineRecord arrays. Returns a plan handle; stats filled.
-void* orc_refine_plan(const float* t, const float* sh, const float* op, const float* refine_norm, const float* vis,
-                      const float* screen, uint32_t n, uint32_t coeffs, const bsx_refine_config* cfg,
-                      const float center[3], const float extent[3], uint32_t global_iter, uint32_t refine_count,
-                      bsx_refine_stats* stats) {
+void* orc_refine_plan2(const float* t, const float* sh, const float* op, const float* refine_norm, const float* vis,
+                       const float* screen, const float* grad2d, uint32_t n, uint32_t coeffs,
+                       const bsx_refine_config* cfg, const float center[3], const float extent[3],
+                       uint32_t global_iter, uint32_t refine_count, bsx_refine_stats* stats) {
     Plan* p = new Plan();
     p->n = n;
     p->coeffs = coeffs;
     p->cfg = *cfg;
+    p->refine_count = refine_count;
     const float max_extent = bsx_max(bsx_max(extent[0], extent[1]), extent[2]);
     const float max_allowed = max_extent * cfg->prune_extent_factor;
     std::vector<uint8_t> mask(n);
@@ -135,6 +233,19 @@ void* orc_refine_plan(const float* t, const float* sh, const float* op, const fl
         for (uint32_t i = 0; i < n; ++i) p->keep.push_back(i);
     const uint32_t K = (uint32_t)p->keep.size();
     const uint32_t pruned = n - K;
+    if (cfg->rule == BSX_REFINE_GRAD_THRESHOLD) {
+        plan_grad_threshold(p, t, vis, grad2d, max_extent);
+        bsx_refine_stats& st = p->stats;
+        const uint32_t C = (uint32_t)p->clone.size(), S = (uint32_t)p->split.size();
+        st.num_added = C + S;
+        st.num_split_oversized = 0;
+        st.num_split_high_grad = S;
+        st.num_pruned = all_pruned ? 0 : pruned;
+        st.num_pruned_non_finite = non_finite;
+        st.total_splats = K + C + S;
+        if (stats) *stats = st;
+        return p;
+    }
     std::vector<float> vis_k(K), rn_k(K), op_k(K);
     p->screen.resize(K);
     for (uint32_t j = 0; j < K; ++j) {
@@ -187,6 +298,14 @@ void* orc_refine_plan(const float* t, const float* sh, const float* op, const fl
     return p;
 }
 
+void* orc_refine_plan(const float* t, const float* sh, const float* op, const float* refine_norm, const float* vis,
+                      const float* screen, uint32_t n, uint32_t coeffs, const bsx_refine_config* cfg,
+                      const float center[3], const float extent[3], uint32_t global_iter, uint32_t refine_count,
+                      bsx_refine_stats* stats) {
+    return orc_refine_plan2(t, sh, op, refine_norm, vis, screen, nullptr, n, coeffs, cfg, center, extent, global_iter,
+                            refine_count, stats);
+}
+
 // Kept and split rows (kept numbering) of a plan.
 void orc_refine_plan_rows(void* h, uint32_t* keep_out, uint32_t* split_out) {
     const Plan* p = (const Plan*)h;
@@ -203,6 +322,11 @@ void orc_refine_apply(void* h, const float* t, const float* sh, const float* op,
                       uint32_t phase_iter, uint32_t phase_total) {
     const Plan* p = (const Plan*)h;
     const bsx_refine_config& c = p->cfg;
+    if (c.rule == BSX_REFINE_GRAD_THRESHOLD) {
+        apply_grad_threshold(p, t, sh, op, m_t, m_s, m_o, v_t, v_s, v_o, nt, nsh, nop, nm_t, nm_s, nm_o, nv_t, nv_s,
+                             nv_o);
+        return;
+    }
     const uint32_t K = (uint32_t)p->keep.size(), S = (uint32_t)p->split.size(), c3 = 3 * p->coeffs;
     // prune_points: select kept rows of the splats and of both moments
     for (uint32_t j = 0; j < K; ++j) {

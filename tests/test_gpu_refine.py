@@ -39,6 +39,7 @@ def _check(tr, splats, snap, ref, st):
         np.testing.assert_array_equal(a, b)
     rec = tr.record
     assert rec.vis_weight.shape[0] == n2 and not rec.vis_weight.any() and not rec.refine_weight_norm.any()
+    assert rec.grad2d_accum.shape[0] == n2
     assert tr.n == n2 and splats.num_splats == n2
 
 
@@ -92,4 +93,57 @@ def test_refine_refuses_without_statistics(cuda):
     tr.step(cam, size, gt.cuda(), splats)
     with pytest.raises(bsx.BsxError):
         tr.refine(splats, 100)
+    tr.close()
+
+
+def test_gradient_threshold_rule_matches_oracle(cuda, orc):
+    """The original 3DGS densification: the view-space gradient-norm
+    statistic the trainer accumulates, then clone / split / prune, bit-equal to the oracle."""
+    import brush_b200 as bsx
+    from brush_b200.splats import clustered_scene, orbit_camera, random_gt
+
+    splats = clustered_scene(30000, 1, "cpu", seed=24, log_scale_mean=-3.0, log_scale_std=1.0).to("cuda")
+    w, h = 256, 192
+    cams = [orbit_camera(i, 4, 8.0, w, h) for i in range(4)]
+    gts = [random_gt(h, w, 80 + i, "cpu").cuda() for i in range(4)]
+    tr = bsx.SplatTrainer(bsx.TrainConfig(accumulate_grad2d=True), splats)
+    # the statistic after one step: |d loss / d xy * (W/2, H/2)| where visible
+    tr.step(cams[0], (w, h), gts[0], splats)
+    torch.cuda.synchronize()
+    vg = tr.native.raster_grads().cpu().numpy()
+    vis = tr.record.vis_weight.cpu().numpy()
+    gx, gy = vg[:, 0] * np.float32(w / 2), vg[:, 1] * np.float32(h / 2)
+    want = np.where(vis > 0, np.sqrt(gx * gx + gy * gy), np.float32(0)).astype(np.float32)
+    np.testing.assert_array_equal(tr.record.grad2d_accum.cpu().numpy(), want)
+    for k in range(1, 5):
+        tr.step(cams[k % 4], (w, h), gts[k % 4], splats)
+    torch.cuda.synchronize()
+    with torch.no_grad():
+        splats.raw_opacities[:40] = -9.0  # below the 0.005 opacity floor
+    snap = _snapshot(tr, splats)
+    g2 = tr.record.grad2d_accum.cpu().numpy().copy()
+    vis = snap["record"][1]
+    avg = np.where(vis > 0, g2 / np.maximum(vis, 1), 0)
+    thr = float(np.quantile(avg[avg > 0], 0.8))
+    t = snap["t"]
+    smax = np.exp(t[:, 7:10].astype(np.float64)).max(axis=1)
+    ext = float(max(snap["bounds"][1]))
+    dense = float(np.median(smax[avg >= thr])) / ext
+    kw = dict(growth_grad_threshold=thr, min_opacity=0.005, percent_dense=dense, seed=77)
+    cfg = bsx.RefineConfig(rule=bsx.REFINE_GRAD_THRESHOLD, **kw)
+    st = tr.refine(splats, 100, 100, 3000, cfg)
+    ref = orc.refine(t, snap["sh"], snap["op"], snap["record"] + (g2,), snap["moments"],
+                     orc.refine_cfg(rule=1, **kw), snap["bounds"][0], snap["bounds"][1], 100, 0, 100, 3000)
+    torch.cuda.synchronize()
+    _check(tr, splats, snap, ref, st)
+    clones = st.num_added - st.num_split_high_grad
+    assert st.num_pruned >= 40 and clones > 0 and st.num_split_high_grad > 0
+    assert not tr.record.grad2d_accum.any()
+    # split children: scales / 1.6 of their parent, means within a few parent scales
+    n2 = st.total_splats
+    kids = splats.transforms.cpu().numpy()[n2 - 2 * st.num_split_high_grad:]
+    assert np.isfinite(kids).all()
+    for k in range(4):
+        s2 = tr.step(cams[k], (w, h), gts[k], splats)
+        assert np.isfinite(float(s2.loss.item()))
     tr.close()

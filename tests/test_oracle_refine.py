@@ -162,3 +162,64 @@ def test_refine_all_pruned_keeps_everything():
                    _moments(n, c, np.random.default_rng(0)), orc.refine_cfg(), np.zeros(3, np.float32),
                    np.ones(3, np.float32), 0, 0, 0, 100)
     assert r["stats"].num_pruned == 0 and r["stats"].total_splats == n
+
+
+def test_gradient_threshold_rule_clone_split_prune():
+    """The original 3DGS densification (Kerbl et al. 2023) as restated: rows that stay,
+    clones, then the two children of every split row; opacity pruning; new rows have zero
+    moments; children sit at mean + R(q) (s * n) with scales s / 1.6."""
+    n, c = 400, 4
+    rng = np.random.default_rng(5)
+    t, sh, op = _scene(n, c, 5)
+    t[:, 7:10] = -3.0
+    t[::2, 7] = -1.0                      # even rows large (split), odd rows small (clone)
+    op[:] = 1.0
+    op[390:] = -8.0                       # opacity 3e-4 < 0.005: pruned
+    vis = np.full(n, 2.0, np.float32)
+    vis[300:310] = 0.0                    # never visible: never selected
+    g2 = np.zeros(n, np.float32)
+    g2[:320:4] = 2.0 * 3e-4               # average 3e-4 >= 2e-4 (rows 0, 4, 8, ...)
+    g2[1:320:4] = 2.0 * 1e-4              # average 1e-4: below
+    g2[3:320:8] = 2.0 * 5e-4              # odd rows above: cloned
+    moments = _moments(n, c, rng)
+    extent = np.full(3, 10.0, np.float32)
+    # boundary: percent_dense x 10 = 0.1 between e^-3 (0.05) and e^-1 (0.37)
+    cfg = orc.refine_cfg(rule=1, growth_grad_threshold=2e-4, min_opacity=0.005, percent_dense=0.01, seed=3)
+    r = orc.refine(t, sh, op, (np.zeros(n, np.float32), vis, np.zeros(n, np.float32), g2), moments, cfg,
+                   np.zeros(3, np.float32), extent, 0, 0, 0, 100)
+    st = r["stats"]
+    splits = [i for i in range(0, 320, 4) if not (300 <= i < 310)]
+    clones = [i for i in range(3, 320, 8) if not (300 <= i < 310)]
+    assert st.num_pruned == 10 and st.num_split_high_grad == len(splits)
+    assert st.num_added - st.num_split_high_grad == len(clones)
+    K = n - 10
+    assert st.total_splats == K + len(clones) + len(splits)
+    stay = [i for i in range(K) if i not in set(splits)]
+    np.testing.assert_array_equal(r["transforms"][:len(stay)], t[stay])
+    np.testing.assert_array_equal(r["m"][0][:len(stay)], moments[0][0][stay])
+    base = len(stay)
+    np.testing.assert_array_equal(r["transforms"][base:base + len(clones)], t[clones])
+    np.testing.assert_array_equal(r["sh"][base:base + len(clones)], sh[clones])
+    base += len(clones)
+    S = len(splits)
+    for k in range(2):
+        for q, i in enumerate(splits):
+            row = r["transforms"][base + k * S + q]
+            np.testing.assert_allclose(row[7:10], np.log(np.exp(t[i, 7:10].astype(np.float64)) / 1.6), atol=1e-6)
+            np.testing.assert_array_equal(row[3:7], t[i, 3:7])
+            assert r["opac"][base + k * S + q] == op[i]
+            z = orc.normal3(3, (1 << 30) + k, i)
+            qn = t[i, 3:7].astype(np.float64) / np.linalg.norm(t[i, 3:7].astype(np.float64))
+            w, x, y, zz = qn
+            R = np.array([[1 - 2 * (y * y + zz * zz), 2 * (x * y - w * zz), 2 * (x * zz + w * y)],
+                          [2 * (x * y + w * zz), 1 - 2 * (x * x + zz * zz), 2 * (y * zz - w * x)],
+                          [2 * (x * zz - w * y), 2 * (y * zz + w * x), 1 - 2 * (x * x + y * y)]])
+            want = t[i, :3] + R @ (np.exp(t[i, 7:10].astype(np.float64)) * z)
+            np.testing.assert_allclose(row[:3], want, atol=1e-5)
+    for arr in r["m"] + r["v"]:
+        assert not np.any(arr[len(stay):])
+    # the budget cuts clones, then splits, in row order
+    r2 = orc.refine(t, sh, op, (np.zeros(n, np.float32), vis, np.zeros(n, np.float32), g2), moments,
+                    orc.refine_cfg(rule=1, growth_grad_threshold=2e-4, min_opacity=0.005, max_splats=K + 5, seed=3),
+                    np.zeros(3, np.float32), extent, 0, 0, 0, 100)
+    assert r2["stats"].total_splats == K + 5 and r2["stats"].num_split_high_grad == 0
