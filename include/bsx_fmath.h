@@ -342,6 +342,19 @@ BSX_HD int bsx_mean_noise(float raw_opac, float gate, float scale, float limit, 
     const float w = bsx_clamp(bsx_powi(inv, 150u), 0.0f, 1.0f) * gate;
     if (!(w != 0.0f)) return 0;
     const float wm = w * scale;
+    /* Exact shortcut: |n| <= sqrt(-2 ln 2^-24) < 5.77 for these uniforms, so each
+     * move is at most 5.78 |wm|. Below 2^(e-25) for a finite mean in [2^e, 2^(e+1))
+     * (half the float spacing on either side) the rounded sum is the mean itself,
+     * and the normals need not be drawn. */
+    {
+        int noop = 1;
+        const float bound = 5.78f * (wm < 0.0f ? -wm : wm);
+        for (int k = 0; k < 3 && noop; ++k) {
+            const uint32_t e = (bsx_f32_to_bits(mean[k]) >> 23) & 0xFFu;
+            noop = e != 0xFFu && e >= 26u && bound < bsx_bits_to_f32((e - 25u) << 23);
+        }
+        if (noop) return 0;
+    }
     float z[3];
     bsx_normal3(seed, step, index, z);
     for (int k = 0; k < 3; ++k) mean[k] = mean[k] + bsx_clamp(z[k] * wm, -limit, limit);
