@@ -195,6 +195,7 @@ class TrainConfig(C.Structure):
         ("noise_vis_gate", C.c_int32),
         ("mean_noise_weight", C.c_float),
         ("noise_seed", C.c_uint64),
+        ("accumulate_grad2d", C.c_int32),
     ]
 
 

@@ -7,6 +7,7 @@ import subprocess
 from pathlib import Path
 
 import numpy as np
+import pytest
 
 ROOT = Path(__file__).resolve().parent.parent
 
@@ -141,3 +142,51 @@ def test_integration_binding_declares_every_entry_point():
     """The Rust FFI block of the integration guide names exactly the header's entry points."""
     doc = set(re.findall(r"pub fn (bsx_\w+)", (ROOT / "INTEGRATION.md").read_text()))
     assert doc == set(_declared())
+
+
+_STRUCTS = {"Camera": "bsx_camera", "ProjectUniforms": "bsx_project_uniforms", "RenderOut": "bsx_render_out",
+            "LossCfg": "bsx_loss_cfg", "AdamGroup": "bsx_adam_group", "AdamCfg": "bsx_adam_cfg",
+            "DpGroup": "bsx_dp_group", "DpExchange": "bsx_dp_exchange", "TrainConfig": "bsx_train_config",
+            "TrainStats": "bsx_train_stats", "DpSplats": "bsx_dp_splats", "RefineConfig": "bsx_refine_config",
+            "RefineStats": "bsx_refine_stats", "PlyInfo": "bsx_ply_info"}
+
+
+_ORACLE_STRUCTS = {"_Camera": "bsx_camera", "Uniforms": "bsx_project_uniforms", "LossCfg": "bsx_loss_cfg",
+                   "RefineCfg": "bsx_refine_config", "RefineStats": "bsx_refine_stats"}
+
+
+@pytest.mark.parametrize("side", ["library", "oracle"])
+def test_struct_layouts_match_header(bsx_lib, tmp_path, side):
+    """Every ctypes mirror of a header struct (the library's bindings and the oracle's) has the C
+    compiler's size and, field by field, the same name and offset: a missing or misplaced field
+    would make the C side read garbage."""
+    import ctypes as C
+    import subprocess
+
+    if side == "library":
+        mod, structs = bsx_lib, _STRUCTS
+    else:
+        from oracle import oracle as mod
+
+        structs = _ORACLE_STRUCTS
+    lines = ["#include <stdio.h>", "#include <stddef.h>", f'#include "{ROOT / "include" / "bsx.h"}"',
+             "int main(void) {"]
+    for py, cname in structs.items():
+        lines.append(f'  printf("{py} size %zu\\n", sizeof({cname}));')
+        for field, _ in getattr(mod, py)._fields_:
+            lines.append(f'  printf("{py} {field} %zu\\n", offsetof({cname}, {field}));')
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    res = subprocess.run(["gcc", "-std=c11", str(src), "-o", str(exe)], capture_output=True, text=True)
+    assert res.returncode == 0, res.stderr  # a ctypes field missing from the C struct fails here
+    got = {}
+    for ln in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.splitlines():
+        py, key, val = ln.split()
+        got[(py, key)] = int(val)
+    for py in structs:
+        st = getattr(mod, py)
+        assert C.sizeof(st) == got[(py, "size")], py  # a C field missing from ctypes changes the size
+        for field, _ in st._fields_:
+            assert getattr(st, field).offset == got[(py, field)], (py, field)
