@@ -152,7 +152,8 @@ WORKLOADS = {
     "cfg2": WORKLOAD,
     "cfg3": "cfg3: 3M splats SH3 1297x840, 200 hemisphere views, full train step (fwd+SSIM/L1+bwd+Adam)",
     "cfg4": ("cfg4: densification run from 100k splats SH3 1280x720, 100 hemisphere views, refine every 100 "
-             "steps (growth threshold 2e-4, prune opacity < 0.005, growth fraction 0.1, cap 1.5M)"),
+             "steps with the 3DGS rule (average view-space gradient >= 2e-4: clone small / split large, prune "
+             "opacity < 0.005, cap 1.5M)"),
     "cfg5": "cfg5: 6M splats SH3 3840x2160 render-only forward (viewer path, packed RGBA8), 120-frame circle",
     "ply": "ply: 1M splats SH3 (cfg2 scene) as a binary little-endian 3DGS PLY in pinned host memory -> device "
            "splats (import), and back (export)",
@@ -183,7 +184,7 @@ def build_workload(name, dev, world):
         w, h = 1280, 720
         cams = S.hemisphere_cameras(100, 8.0, w, h, seed=4)
         return splats, cams, (w, h), [S.random_gt(h, w, 4000 + i, "cpu") for i in range(100)], \
-            bsx.TrainConfig(total_train_iters=3000)
+            bsx.TrainConfig(total_train_iters=3000, accumulate_grad2d=True)
     if name == "cfg5":
         splats, size = S.config5_scene(dev, seed=5)
         cams = S.circle_cameras(120, 8.0, size[0], size[1])
