@@ -164,7 +164,19 @@ __device__ void max_tile(const AdamArgs& a, uint32_t t) {
     const uint32_t r0 = (t - x.block_begin) * kTileFloats;
     const uint32_t cnt = min(kTileFloats, x.count - r0);
     if (x.mc) {
-        for (uint32_t e = threadIdx.x; e < cnt; e += kAdamThreads) mc_st(x.mc + r0 + e, mc_ld_max_nonneg(x.mc + r0 + e));
+        // every in-switch load of the tile in flight before the first store
+        constexpr int kPer = kTileFloats / kAdamThreads;
+        float v[kPer];
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+            const uint32_t e = threadIdx.x + k * kAdamThreads;
+            v[k] = e < cnt ? mc_ld_max_nonneg(x.mc + r0 + e) : 0.0f;
+        }
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+            const uint32_t e = threadIdx.x + k * kAdamThreads;
+            if (e < cnt) mc_st(x.mc + r0 + e, v[k]);
+        }
         return;
     }
     const uint32_t nvec = x.vec ? cnt / 4 : 0;
@@ -216,7 +228,7 @@ __device__ void adam_tile(const AdamArgs& a, int k, uint32_t tile) {
         // words loaded per batch: the local form keeps one in flight per thread
         // (low registers, six resident blocks per SM measured fastest on HBM);
         // the peer form batches so that NVLink round trips overlap
-        constexpr int kChunk = !kPeers ? 1 : kW > 4 ? kVecPerThread / 2 : kVecPerThread;
+        constexpr int kChunk = !kPeers ? 1 : (kW > 4 && !kMC) ? kVecPerThread / 2 : kVecPerThread;
         constexpr int kUnroll = kPeers ? kVecPerThread / kChunk : 1;
 #pragma unroll kUnroll
         for (int c0 = 0; c0 < kVecPerThread; c0 += kChunk) {
