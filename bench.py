@@ -724,7 +724,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--exchange", default="peer", choices=["peer", "nvls", "nccl"],
+    ap.add_argument("--exchange", default="auto", choices=["auto", "peer", "nvls", "nccl"],
                     help="data-parallel gradient exchange with --gpus > 1")
     ap.add_argument("--workload", default="cfg2", choices=sorted(WORKLOADS),
                     help="BASELINE configuration (cfg2 is the headline metric)")

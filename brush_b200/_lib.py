@@ -352,6 +352,10 @@ SIGNATURES = {
          C.c_uint32],
     ),
     "bsx_trainer_set_median_scale": (C.c_int, [C.c_void_p, C.c_float]),
+    "bsx_splat_bounds": (
+        C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_float, C.POINTER(C.c_float),
+                  C.POINTER(C.c_float)]
+    ),
     "bsx_trainer_reserve": (C.c_int, [C.c_void_p, C.c_uint32]),
     "bsx_trainer_load_optimizer_state": (
         C.c_int, [C.c_void_p] + [C.c_void_p] * 6 + [C.c_uint32, C.c_int32, C.c_int32]

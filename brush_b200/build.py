@@ -4,7 +4,8 @@ Each translation unit is compiled by nvcc in parallel and linked in-tree so the
 library travels with the source tree. Floating-point contraction is disabled
 (``-fmad=false``, ``-ffp-contract=off``): the pipeline's discrete decisions
 (culling, tile counts, alpha cutoffs) must be reproducible bit-for-bit by a
-host restatement compiled the same way.
+host restatement compiled the same way. The image loss, checked by tolerance
+and free of such decisions, is compiled with contraction (``CONTRACTED``).
 """
 from __future__ import annotations
 
@@ -45,11 +46,20 @@ def _stale(target: Path, deps: list[Path]) -> bool:
     return any(d.stat().st_mtime > t for d in deps)
 
 
+# Translation units whose arithmetic is checked by tolerance only and that take no
+# bit-exact decision: there the compiler may contract multiply-adds. Every other
+# unit keeps exact IEEE operations, because the CPU oracle (g++ -ffp-contract=off)
+# restates its decisions (culling, tile counts, alpha and early-out tests, the
+# raster backward's replay of the forward) or its results bit for bit.
+CONTRACTED = {"loss.cu"}
+
+
 def _compile(src: Path, verbose: bool) -> Path:
     obj = BUILD / (src.stem + ".o")
-    if not _stale(obj, [src] + _headers()):
+    if not _stale(obj, [src] + _headers() + [Path(__file__)]):
         return obj
-    cmd = [NVCC, *ARCH, *CFLAGS, "-c", str(src), "-o", str(obj)]
+    flags = [("-fmad=true" if f == "-fmad=false" and src.name in CONTRACTED else f) for f in CFLAGS]
+    cmd = [NVCC, *ARCH, *flags, "-c", str(src), "-o", str(obj)]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     res = subprocess.run(cmd, capture_output=True, text=True)

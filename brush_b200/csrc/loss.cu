@@ -18,7 +18,9 @@
 // fixed order. This removes the reference's permute/contiguous copies, the
 // separate mean kernel and the zero-fill of the gradient image. Its blur taps
 // accumulate by fused multiply-adds (same tap order; the loss map and gradient
-// are checked against the CPU restatement to 1e-5 relative, not bit for bit).
+// are checked against the CPU restatement to 1e-5 relative, not bit for bit),
+// and this file is the one the build compiles with multiply-add contraction:
+// nothing here is a discrete decision another stage must reproduce.
 #include "common.cuh"
 
 namespace bsx {

@@ -126,7 +126,11 @@ class Splats:
 
 def splat_bounds(means: torch.Tensor, percentile: float = 0.8):
     """Robust percentile AABB of the means as (center, extent), f32 as ``bounds_from_pos``
-    computes it (crates/brush-train/src/splat_init.rs:130-158, bounding_box.rs:8-13)."""
+    computes it (crates/brush-train/src/splat_init.rs:130-158, bounding_box.rs:8-13).
+    Device means go through the library (``bsx_splat_bounds``: order statistics by its radix
+    sort under total_cmp); host means are sorted here."""
+    if means.is_cuda:
+        return _device_bounds(means, percentile)
     m = means.detach().float()
     p = np.float32(percentile)
     lo_v, hi_v = [], []
@@ -146,6 +150,21 @@ def splat_bounds(means: torch.Tensor, percentile: float = 0.8):
         hi_v.append(pair[1])
     mn, mx = np.array(lo_v, np.float32), np.array(hi_v, np.float32)
     return (mx + mn) / np.float32(2.0), (mx - mn) / np.float32(2.0)
+
+
+def _device_bounds(means: torch.Tensor, percentile: float):
+    import ctypes as C
+
+    from . import _lib
+    from ._context import context
+
+    if means.dim() != 2 or means.shape[1] != 3 or means.dtype != torch.float32 or means.stride(1) != 1:
+        raise ValueError("means must be a float32 [N,3] view with unit column stride")
+    ctx = context(means.device)
+    center, extent = (C.c_float * 3)(), (C.c_float * 3)()
+    ctx.check(_lib.lib().bsx_splat_bounds(ctx.handle, C.c_void_p(means.data_ptr()), int(means.stride(0)),
+                                          int(means.shape[0]), float(np.float32(percentile)), center, extent))
+    return np.array(center[:], np.float32), np.array(extent[:], np.float32)
 
 
 def median_size(means: torch.Tensor, percentile: float = 0.8) -> float:

@@ -547,6 +547,15 @@ BSX_API bsx_status bsx_trainer_load_optimizer_state(bsx_trainer* tr, const float
                                                     const float* d_v_transforms, const float* d_v_sh_coeffs,
                                                     const float* d_v_raw_opac, uint32_t rows, int32_t world,
                                                     int32_t rank);
+/* The trainer's bounding box: bounds_from_pos (crates/brush-train/src/splat_init.rs:130-158).
+ * Per axis the order statistics trunc(f32((1 - p) / 2) * n) and
+ * min(n - 1, trunc(f32((1 + p) / 2) * n)) of the n finite coordinates under
+ * total_cmp, then center = (max + min) / 2, extent = (max - min) / 2
+ * (BoundingBox::from_min_max); no finite coordinate on some axis: [-1, 1]^3.
+ * d_means: N rows of `stride` floats whose first three are the mean (stride 10
+ * for a transforms tensor). Synchronises the context's stream. */
+BSX_API bsx_status bsx_splat_bounds(bsx_ctx* ctx, const float* d_means, uint32_t stride, uint32_t num_splats,
+                                    float percentile, float center[3], float extent[3]);
 /* Rate schedule input after the bounds change (train.rs:656: lr_mean uses bounds.median_size()). */
 BSX_API bsx_status bsx_trainer_set_median_scale(bsx_trainer* tr, float median_scale);
 

@@ -147,3 +147,46 @@ def test_gradient_threshold_rule_matches_oracle(cuda, orc):
         s2 = tr.step(cams[k], (w, h), gts[k], splats)
         assert np.isfinite(float(s2.loss.item()))
     tr.close()
+
+
+def _bounds_from_pos(means, percentile):
+    """numpy restatement of bounds_from_pos (splat_init.rs:130-158) with total_cmp order."""
+    lo_v, hi_v = [], []
+    p = np.float32(percentile)
+    for k in range(3):
+        v = means[:, k][np.isfinite(means[:, k])]
+        if v.size == 0:
+            return np.zeros(3, np.float32), np.ones(3, np.float32)
+        b = v.view(np.uint32)
+        key = np.where(b & 0x80000000, ~b, b | 0x80000000)  # total_cmp as an unsigned order
+        vs = v[np.argsort(key, kind="stable")]
+        n = v.size
+        lo = int(np.float32(np.float32(np.float32(1) - p) / np.float32(2)) * np.float32(n))
+        hi = min(n - 1, int(np.float32(np.float32(np.float32(1) + p) / np.float32(2)) * np.float32(n)))
+        lo_v.append(vs[lo])
+        hi_v.append(vs[hi])
+    mn, mx = np.array(lo_v, np.float32), np.array(hi_v, np.float32)
+    return (mx + mn) / np.float32(2), (mx - mn) / np.float32(2)
+
+
+@pytest.mark.parametrize("n", [1, 7, 100_003])
+def test_device_bounds_match_restatement(cuda, n):
+    """bsx_splat_bounds (the library's radix sort, no PyTorch kernels) against bounds_from_pos,
+    with non-finite coordinates, signed zeros and the all-non-finite fallback."""
+    from brush_b200.splats import splat_bounds
+
+    rng = np.random.default_rng(n)
+    t = rng.normal(0, 2, (n, 10)).astype(np.float32)
+    if n > 10:
+        t[:5, 0] = np.nan
+        t[5:9, 1] = np.inf
+        t[9:20, 2] = -0.0
+        t[20:30, 2] = 0.0
+    for p in (0.8, 0.0, 1.0):
+        c, e = splat_bounds(torch.from_numpy(t).cuda()[:, 0:3], p)
+        wc, we = _bounds_from_pos(t[:, :3].copy(), p)
+        np.testing.assert_array_equal(c, wc)
+        np.testing.assert_array_equal(e, we)
+    t[:, 1] = np.nan
+    c, e = splat_bounds(torch.from_numpy(t).cuda()[:, 0:3], 0.8)
+    assert c.tolist() == [0, 0, 0] and e.tolist() == [1, 1, 1]
