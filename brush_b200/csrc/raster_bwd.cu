@@ -7,7 +7,8 @@
 // Each thread replays its pixels front to back exactly as the forward did
 // (same float operations, so T and every accept / early-out decision match the
 // forward bit-for-bit), carrying the residual colour C - T_final*bg - (front
-// contributions) in registers as the reference does. Per splat, a warp that
+// contributions) as the reference does, folded into one scalar (its dot
+// product with the pixel's output gradient). Per splat, a warp that
 // none of the splat's acceptable pixels reach (the forward's exact footprint
 // test per row band, raster_common.cuh) skips it uniformly, and a warp skips
 // the pixel step of a band the splat cannot reach; otherwise each lane forms
@@ -17,7 +18,9 @@
 // warps, and each (splat, tile) leaves with three 16-byte vector atomics
 // (red.global.add.v4.f32) into a 12-lane row.
 // The alpha / T chain uses exact IEEE operations; the gradient arithmetic,
-// which is tolerance-checked, uses fused multiply-adds and fast reciprocals.
+// which is tolerance-checked, uses fused multiply-adds and approximate
+// reciprocal and square root, and sums the screen-space offsets weighted by
+// d loss / d sigma so that the conic multiplies them once per (splat, tile).
 // Colours are clamped once per splat while staging; the colour-gradient
 // gates (raw colour >= 0) are per-splat constants applied once at the flush.
 #include "raster_common.cuh"
@@ -74,53 +77,75 @@ __device__ __forceinline__ float warp_sum10(float (&v)[10], int lane) {
 }
 
 // Per-pixel replay state and constants.
+//
+// The colour residual is carried as one scalar. With s_c the residual colour
+// C_c - T_final bg_c - (front contributions) of channel c and vo the pixel's
+// output gradient, the reference's d loss / d alpha is
+//   (sum_c (T cl_c - s_c) vo_c + (vo_a - bg.vo) T_final) / (1 - alpha)
+// = (T (cl . vo) - E) / (1 - alpha),   E = s . vo - (vo_a - bg.vo) T_final,
+// and each splat lowers E by vis (cl . vo). Initially
+// E = C . vo - T_final vo_a (the background terms cancel).
 struct PixelBwd {
-    float T, sr, sg, sb;            // transmittance, residual colour
-    float vor, vog, vob, vow;       // v_out rgb, (v_a - bg.v_out) * T_final
+    float T, E;                     // transmittance, scalar colour residual
+    float vor, vog, vob;            // v_out rgb
     float inv_fa;                   // 1 / max(final alpha, 1e-5)
     float pcy;                      // pixel centre y
     bool done;
 };
 
+__device__ __forceinline__ float rcp_approx(float x) {
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+__device__ __forceinline__ float sqrt_approx(float x) {
+    float r;
+    asm("sqrt.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
 __device__ __forceinline__ void pixel_init(PixelBwd& P, const BwdArgs& a, uint32_t px, uint32_t py) {
     P.T = 1.0f;
-    P.sr = P.sg = P.sb = 0.0f;
-    P.vor = P.vog = P.vob = P.vow = 0.0f;
+    P.E = 0.0f;
+    P.vor = P.vog = P.vob = 0.0f;
     P.inv_fa = 0.0f;
     P.pcy = (float)py + 0.5f;
     P.done = !(px < a.w && py < a.h);
     if (!P.done) {
         const size_t pid = (size_t)py * a.w + px;
         const float4 o = __ldg(reinterpret_cast<const float4*>(a.image) + pid);
-        const float tf = 1.0f - o.w;
-        P.sr = o.x - tf * a.bg_r;
-        P.sg = o.y - tf * a.bg_g;
-        P.sb = o.z - tf * a.bg_b;
         const float4 vo = __ldg(reinterpret_cast<const float4*>(a.v_output) + pid);
         P.vor = vo.x;
         P.vog = vo.y;
         P.vob = vo.z;
-        P.vow = (vo.w - (a.bg_r * vo.x + a.bg_g * vo.y + a.bg_b * vo.z)) * tf;
+        P.E = __fmaf_rn(o.x, vo.x, __fmaf_rn(o.y, vo.y, __fmaf_rn(o.z, vo.z, -(1.0f - o.w) * vo.w)));
         P.inv_fa = __frcp_rn(bsx_max(o.w, 1.0e-5f));
     }
 }
 
 // One pixel's step of the replay for one splat: exact forward arithmetic for
-// sigma / alpha / T, then the pixel's gradient contribution added into gv.
+// sigma / alpha / T, then the pixel's gradient contribution added into gv:
+//   gv[0..1]  sum vsig (dx, dy)        (the conic is applied at the flush)
+//   gv[2..4]  sum vsig (dx dx, dx dy, dy dy)   (halved at the flush)
+//   gv[5..7]  sum vis vo_rgb,  gv[8] sum d loss / d opacity-alpha * gauss,
+//   gv[9]     sum |(w, h) (conic (dx, dy) vsig)| / final alpha
+// with (dx, dy) = pixel centre - splat mean.
 template <bool SMOOTH, bool REFINE>
-__device__ __forceinline__ bool pixel_step(PixelBwd& P, float pcx, float dx0, float hxx, float xy, float sx, float sy,
-                                           float c00, float c01, float c11, float ca, float thr, float clr,
-                                           float clg, float clb, float wf, float hf, float (&gv)[10]) {
+__device__ __forceinline__ bool pixel_step(PixelBwd& P, float dx0, float hxx, float xy, float sy, float hc11,
+                                           float ca, float thr, float clr, float clg, float clb,
+                                           const float4* rr, float (&gv)[10]) {
     if (P.done) return false;
     const float dyp = P.pcy - sy;
-    const float sigma = bsx_sigma_row(hxx, xy, 0.5f * c11, dyp);
+    const float sigma = bsx_sigma_row(hxx, xy, hc11, dyp);
     if (!(sigma >= 0.0f) || sigma > thr) return false;
     const float gauss = bsx_expf_raster(-sigma);
-    const float alpha = bsx_min(0.999f, ca * gauss);
+    const float cg = ca * gauss;
+    const float alpha = bsx_min(0.999f, cg);
     const float wc = SMOOTH ? cutoff_weight(alpha) : (alpha >= 1.0f / 255.0f ? 1.0f : 0.0f);
     if (!(wc > 0.0f)) return false;
     const float ae = alpha * wc;
-    const float next_t = P.T * (1.0f - ae);
+    const float one_m = 1.0f - ae;
+    const float next_t = P.T * one_m;
     if (next_t <= 1.0e-4f) {
         P.done = true;
         return false;
@@ -132,34 +157,26 @@ __device__ __forceinline__ bool pixel_step(PixelBwd& P, float pcx, float dx0, fl
     gv[5] = __fmaf_rn(vis, P.vor, gv[5]);
     gv[6] = __fmaf_rn(vis, P.vog, gv[6]);
     gv[7] = __fmaf_rn(vis, P.vob, gv[7]);
-    const float ra = __fdividef(1.0f, 1.0f - ae);
-    float dot_rgb = __fmaf_rn(T, clr, -P.sr) * P.vor;
-    dot_rgb = __fmaf_rn(__fmaf_rn(T, clg, -P.sg), P.vog, dot_rgb);
-    dot_rgb = __fmaf_rn(__fmaf_rn(T, clb, -P.sb), P.vob, dot_rgb);
-    const float vae = (dot_rgb + P.vow) * ra;
+    const float cv = __fmaf_rn(clr, P.vor, __fmaf_rn(clg, P.vog, clb * P.vob));
+    const float vae = __fmaf_rn(T, cv, -P.E) * rcp_approx(one_m);
     const float valpha = SMOOTH ? vae * (wc + alpha * cutoff_weight_deriv(alpha)) : vae;
-    const float vsig = -alpha * valpha;
-    // the reference's backward uses d = splat - pixel
-    const float dx = -dx0, dy = -dyp;
-    const float vxx = vsig * __fmaf_rn(c00, dx, c01 * dy);
-    const float vxy = vsig * __fmaf_rn(c01, dx, c11 * dy);
-    if (ca * gauss <= 0.999f) {
-        const float hv = 0.5f * vsig;
-        gv[0] += vxx;
-        gv[1] += vxy;
-        gv[2] = __fmaf_rn(hv * dx, dx, gv[2]);
-        gv[3] = __fmaf_rn(vsig * dx, dy, gv[3]);
-        gv[4] = __fmaf_rn(hv * dy, dy, gv[4]);
+    if (cg <= 0.999f) {
+        const float vsig = -alpha * valpha;
+        const float a = vsig * dx0, b = vsig * dyp;
+        gv[0] += a;
+        gv[1] += b;
+        gv[2] = __fmaf_rn(a, dx0, gv[2]);
+        gv[3] = __fmaf_rn(a, dyp, gv[3]);
+        gv[4] = __fmaf_rn(b, dyp, gv[4]);
         gv[8] = __fmaf_rn(valpha, gauss, gv[8]);
         if (REFINE) {
-            const float ax = vxx * wf, ay = vxy * hf;
-            const float q = __fmaf_rn(ax, ax, ay * ay);
-            gv[9] = __fmaf_rn(q * rsqrtf(fmaxf(q, 1e-38f)), P.inv_fa, gv[9]);
+            // the splat's conic rows scaled by the image size: (c00 w, c01 w, c01 h, c11 h)
+            const float4 r = *rr;
+            const float ax = __fmaf_rn(r.x, a, r.y * b), ay = __fmaf_rn(r.z, a, r.w * b);
+            gv[9] = __fmaf_rn(sqrt_approx(__fmaf_rn(ax, ax, ay * ay)), P.inv_fa, gv[9]);
         }
     }
-    P.sr = __fmaf_rn(-vis, clr, P.sr);
-    P.sg = __fmaf_rn(-vis, clg, P.sg);
-    P.sb = __fmaf_rn(-vis, clb, P.sb);
+    P.E = __fmaf_rn(-vis, cv, P.E);
     P.T = next_t;
     return true;
 }
@@ -175,6 +192,7 @@ __global__ void __launch_bounds__(kBwdPixThreads, 8) raster_bwd_kernel(const Bwd
     __shared__ float4 s_a[kBwdPixThreads];  // x, y, c00, c01
     __shared__ float4 s_b[kBwdPixThreads];  // c11, opacity, max(r,0), max(g,0)
     __shared__ float2 s_c[kBwdPixThreads];  // max(b,0), ln(255 o) + margin
+    __shared__ float4 s_d[REFINE ? kBwdPixThreads : 1];  // refine rows (c00 w, c01 w, c01 h, c11 h)
     __shared__ uint32_t s_mask[kBwdPixThreads];  // bits 0-7 warp row bands, 8-10 colour gates
     __shared__ uint32_t s_gid[kBwdPixThreads];
     __shared__ float s_grad[kBwdPixThreads][kGradLanes + 1];
@@ -205,6 +223,7 @@ __global__ void __launch_bounds__(kBwdPixThreads, 8) raster_bwd_kernel(const Bwd
             s_a[threadIdx.x] = ra;
             s_b[threadIdx.x] = make_float4(rb.x, rb.y, bsx_max(rb.z, 0.0f), bsx_max(rb.w, 0.0f));
             s_c[threadIdx.x] = make_float2(bsx_max(rc.x, 0.0f), rc.z + margin);
+            if (REFINE) s_d[threadIdx.x] = make_float4(ra.z * wf, ra.w * wf, ra.w * hf, rb.x * hf);
             const uint32_t gates = (rb.z >= 0.0f ? 256u : 0u) | (rb.w >= 0.0f ? 512u : 0u) | (rc.x >= 0.0f ? 1024u : 0u);
             s_mask[threadIdx.x] = warp_visit_mask(ra.x, ra.y, ra.z, ra.w, rb.x, rc.z + margin, ox, oy) | gates;
             s_gid[threadIdx.x] = g;
@@ -219,18 +238,19 @@ __global__ void __launch_bounds__(kBwdPixThreads, 8) raster_bwd_kernel(const Bwd
             const float4 A = s_a[t];
             const float4 B = s_b[t];
             const float2 Cc = s_c[t];
+            const float4* rr = &s_d[REFINE ? t : 0];
             const float dx0 = pcx - A.x;
             const float hxx = bsx_sigma_hxx(A.z, dx0);
             const float xy = A.w * dx0;
+            const float hc11 = 0.5f * B.x;
             float gv[kGradLanes];
 #pragma unroll
             for (int k = 0; k < kGradLanes; ++k) gv[k] = 0.0f;
             // a band the splat cannot reach has every sigma > thr: its pixel step is a no-op
-            bool contrib = (bands & 1u) && pixel_step<SMOOTH, REFINE>(PA, pcx, dx0, hxx, xy, A.x, A.y, A.z, A.w, B.x,
-                                                                      B.y, Cc.y, B.z, B.w, Cc.x, wf, hf, gv);
+            bool contrib = (bands & 1u) && pixel_step<SMOOTH, REFINE>(PA, dx0, hxx, xy, A.y, hc11, B.y, Cc.y, B.z,
+                                                                      B.w, Cc.x, rr, gv);
             if (bands & 2u)
-                contrib |= pixel_step<SMOOTH, REFINE>(PB, pcx, dx0, hxx, xy, A.x, A.y, A.z, A.w, B.x, B.y, Cc.y, B.z,
-                                                      B.w, Cc.x, wf, hf, gv);
+                contrib |= pixel_step<SMOOTH, REFINE>(PB, dx0, hxx, xy, A.y, hc11, B.y, Cc.y, B.z, B.w, Cc.x, rr, gv);
             if (__any_sync(0xffffffffu, contrib)) {
                 const float tot = warp_sum10(gv, lane);
                 if (!(lane & 1) && sum_idx < kGradLanes) atomicAdd(&s_grad[t][sum_idx], tot);
@@ -246,9 +266,15 @@ __global__ void __launch_bounds__(kBwdPixThreads, 8) raster_bwd_kernel(const Bwd
 #pragma unroll
             for (int k = 0; k < kGradLanes; ++k) any = any || sgr[k] != 0.0f;
             if (any) {
+                // d loss / d mean2d = -conic (sum vsig (dx, dy)) in the reference's
+                // d = mean - pixel convention; the conic lanes take the halving
+                const float4 A = s_a[threadIdx.x];
+                const float c11 = s_b[threadIdx.x].x;
+                const float gx = -__fmaf_rn(A.z, sgr[0], A.w * sgr[1]);
+                const float gy = -__fmaf_rn(A.w, sgr[0], c11 * sgr[1]);
                 float4* dst = reinterpret_cast<float4*>(a.v_grad + (size_t)s_gid[threadIdx.x] * kGradStride);
-                atomicAdd(dst, make_float4(sgr[0], sgr[1], sgr[2], sgr[3]));
-                atomicAdd(dst + 1, make_float4(sgr[4], vr, vg, vb));
+                atomicAdd(dst, make_float4(gx, gy, 0.5f * sgr[2], sgr[3]));
+                atomicAdd(dst + 1, make_float4(0.5f * sgr[4], vr, vg, vb));
                 atomicAdd(dst + 2, make_float4(sgr[8], sgr[9], 0.0f, 0.0f));
             }
         }

@@ -44,11 +44,12 @@ struct NoiseArgs {
     uint32_t step;
 };
 
-__device__ __forceinline__ void noise_row(const NoiseArgs& z, uint32_t i, float gate_src) {
+// raw_op: the splat's opacity logit, loaded by the caller ahead of the gate
+__device__ __forceinline__ void noise_row(const NoiseArgs& z, uint32_t i, float gate_src, float raw_op) {
     if (!(gate_src > 0.0f)) return;
     float* m = z.transforms + (size_t)i * 10;
     float mean[3] = {m[0], m[1], m[2]};
-    if (bsx_mean_noise(__ldg(z.raw_opac + i), 1.0f, z.scale, z.limit, z.seed, z.step, i, mean)) {
+    if (bsx_mean_noise(raw_op, 1.0f, z.scale, z.limit, z.seed, z.step, i, mean)) {
         m[0] = mean[0];
         m[1] = mean[1];
         m[2] = mean[2];
@@ -78,6 +79,8 @@ __global__ void __launch_bounds__(kStatsThreads)
                         float* __restrict__ vsum, float* __restrict__ smax, const NoiseArgs nz, const Grad2dArgs g2) {
     for (uint32_t i = blockIdx.x * kStatsThreads + threadIdx.x; i < n; i += gridDim.x * kStatsThreads) {
         float vs = 0.0f;
+        // issued with the statistics' loads rather than after the gate is known
+        const float raw_op = NOISE ? __ldg(nz.raw_opac + i) : 0.0f;
         if (STATS) {
             if (refine) rmax[i] = bsx_max(rmax[i], refine[i]);
             const float vi = visible[i];
@@ -90,7 +93,7 @@ __global__ void __launch_bounds__(kStatsThreads)
                 g2.accum[i] = g2.accum[i] + sqrtf(gx * gx + gy * gy);
             }
         }
-        if (NOISE) noise_row(nz, i, nz.gate ? __ldg(nz.gate + i) : vs);
+        if (NOISE) noise_row(nz, i, nz.gate ? __ldg(nz.gate + i) : vs, raw_op);
     }
 }
 
@@ -108,7 +111,7 @@ __global__ void __launch_bounds__(kStatsThreads)
 
 __global__ void __launch_bounds__(kStatsThreads) mean_noise_kernel(uint32_t n, const NoiseArgs nz) {
     for (uint32_t i = blockIdx.x * kStatsThreads + threadIdx.x; i < n; i += gridDim.x * kStatsThreads)
-        noise_row(nz, i, __ldg(nz.gate + i));
+        noise_row(nz, i, __ldg(nz.gate + i), __ldg(nz.raw_opac + i));
 }
 
 uint32_t stats_blocks(uint32_t n) { return std::min<uint32_t>((n + kStatsThreads - 1) / kStatsThreads, 148 * 8); }
