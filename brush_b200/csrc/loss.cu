@@ -10,13 +10,14 @@
 // blurred again. Summation order matches the reference (taps d = 1..5 as
 // (left + right) * w[5-d], then the centre tap).
 //
-// The training form (loss_fused_kernel) reads the rasterizer's [H,W,4] image
-// directly, loops over the three colour channels inside one block, uses the
-// constant chain 1/(3HW) of a mean reduction, writes the gradient straight
-// into the [H,W,4] v_output layout the raster backward consumes (alpha lane
-// 0), and emits per-block loss sums that a second tiny kernel reduces in a
-// fixed order. This removes the reference's permute/contiguous copies, the
-// separate mean kernel and the zero-fill of the gradient image. Its blur taps
+// The training form (loss_ssim_kernel, loss_grad_kernel) reads the
+// rasterizer's [H,W,4] image directly, handles the three colour channels in
+// one block, uses the constant chain 1/(3HW) of a mean reduction, writes the
+// gradient straight into the [H,W,4] v_output layout the raster backward
+// consumes (alpha lane 0), and emits per-block loss sums that a tiny kernel
+// reduces in a fixed order. This removes the reference's permute/contiguous
+// copies, the separate mean kernel and the zero-fill of the gradient image.
+// Its blur taps
 // accumulate by fused multiply-adds (same tap order; the loss map and gradient
 // are checked against the CPU restatement to 1e-5 relative, not bit for bit),
 // and this file is the one the build compiles with multiply-add contraction:
@@ -349,42 +350,50 @@ __global__ void __launch_bounds__(256) loss_bwd_kernel(const __grid_constant__ L
     if (in) a.out[idx] = g;
 }
 
-// Training form: 32x32 output tiles, three colour channels per block, [H,W,4]
-// in and out. The larger tile cuts the halo recomputation of the 16x16
-// operator form (SSIM evaluated on 42x42 = 1.7x the outputs instead of 26x26 =
-// 2.6x). Each blur pass runs as a register sliding window: a thread loads a
-// run of 15, 14 or 12 samples once and produces 5 (first pass: 52 rows x 9
-// runs fill one round of the 512 threads), 4 or 2 neighbouring outputs, about
-// a third of the shared-memory loads of one-output-per-thread. Planes
-// have odd pitches so that lanes walking down a column (horizontal passes,
-// one row per lane) and lanes walking along a row (vertical passes, one
-// column per lane) both hit distinct banks. Tap and summation order per output
-// are those of loss_bwd_channel: taps d = 1..5 as (left + right) * w[5-d],
-// then the centre.
-constexpr int kFT = 32;                    // output tile edge
-constexpr int kF2 = kFT + 2 * kHalo;       // 42: SSIM grid
-constexpr int kF1 = kFT + 4 * kHalo;       // 52: staged grid
-constexpr int kPX = kF1 + 1;               // 53: pitch of the staged planes
-constexpr int kPH = kF2 + 1;               // 43: pitch of the moment / partial planes
-constexpr int kPQ = kFT + 1;               // 33: pitch of the second horizontal blur
-constexpr int kFusedThreads = 512;
-constexpr int kSeg = 4;                    // outputs per thread in passes 2-3
-constexpr int kSeg1 = 5;                   // outputs per thread in pass 1: 52 rows x 9 runs fill one round
-constexpr int kSeg4 = 2;                   // outputs per thread in pass 4 (32 x 16 threads)
-static_assert(kFT * kFT == kSeg4 * kFusedThreads, "pass 4 covers the tile once");
+// Training form: two launches over 32x32 output tiles, [H,W,4] in and out.
+//
+// loss_ssim_kernel stages a tile with a 5-pixel halo (42x42 samples, the three
+// colour channels at once), blurs the five moments horizontally over the 42
+// rows x 32 core columns and vertically over the 32x32 core, and writes for
+// every image pixel the chain-weighted SSIM partials (d/d mu_x, d/d sigma_x^2,
+// d/d sigma_xy, each times d loss / d map) as nine planes [c][k][H][pitch]
+// (pitch = W rounded up to 4), with the loss summed per block.
+// loss_grad_kernel stages those planes over the same halo with 16-byte loads,
+// blurs them horizontally then vertically, and forms each core pixel's
+// gradient. Cutting at the partials leaves one halo per blur: each pass
+// evaluates at most 1.31x its outputs, where one kernel doing all four passes
+// needs 52x42 moment blurs and 42x42 SSIM values per 32x32 tile. The planes
+// (36 bytes per pixel) are written once and read back while still largely
+// resident in L2. Blur passes run register sliding windows (a run of 8 outputs
+// per thread horizontally, 4 vertically); planes have odd pitches, so lanes
+// walking down a column (horizontal passes, one row per lane) or along a row
+// (vertical passes) hit distinct banks. Tap and summation order per output are
+// those of loss_bwd_channel: taps d = 1..5 as (left + right) * w[5-d], then
+// the centre.
+constexpr int kFT = 32;                        // output tile edge
+constexpr int kFS = kFT + 2 * kHalo;           // 42: staged grid edge
+constexpr int kFSP = kFS + 1;                  // 43: pitch of the staged planes
+constexpr int kFHP = kFT + 1;                  // 33: pitch of the horizontal-blur planes
+constexpr int kFThreads = 256;
+constexpr int kRunH = 8;                       // outputs per thread, horizontal passes
+constexpr int kRunV = 4;                       // outputs per thread, vertical passes
+constexpr int kItemsH = kFS * (kFT / kRunH);   // 168 (row, run) items of a horizontal pass
+static_assert(kFT * (kFT / kRunV) == kFThreads, "a vertical pass covers the tile once");
+static_assert(kItemsH <= kFThreads, "a horizontal pass is one round");
+constexpr int kFH = kFS * kFHP;                // size of one horizontal-blur plane
 
-struct FusedSmem {
-    float x[kF1 * kPX];           // staged prediction, 52 x 52
-    float y[kF1 * kPX];           // staged effective ground truth
-    float h[5 * kF1 * kPH];       // first horizontal blur: 5 planes 52 x 42;
-                                  // later the second: 3 planes 42 x 32 (pitch 33)
-    float p[3 * kF2 * kPH];       // chain-weighted SSIM partials, 42 x 42
-    float val[kFT * kFT];         // SSIM of the output pixels
-    float w[11];
-    float red[kFusedThreads / 32];
+struct SsimSmem {
+    float x[3][kFS * kFSP];  // staged prediction per channel, 42 x 42
+    float y[3][kFS * kFSP];  // staged effective ground truth
+    float h[5][kFH];         // horizontal moment blur of one channel, 42 x 32
+    float red[kFThreads / 32];
+};
+struct GradSmem {
+    float p[3][kFS * kFSP];  // staged partial planes of one channel, 42 x 42
+    float q[3][kFH];         // their horizontal blur, 42 x 32
 };
 
-// out[j] = blur of window v at output j (centre v[j + 5]), j < n.
+// out[j] = blur of window v at output j (centre v[j + 5]), j < N.
 template <int N>
 __device__ __forceinline__ void blur_window(const float* v, const float* w, float* out) {
 #pragma unroll
@@ -396,206 +405,284 @@ __device__ __forceinline__ void blur_window(const float* v, const float* w, floa
     }
 }
 
-__global__ void __launch_bounds__(kFusedThreads) loss_fused_kernel(const __grid_constant__ LossArgs a) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    FusedSmem& S = *reinterpret_cast<FusedSmem*>(smem_raw);
-    if (threadIdx.x < 11) S.w[threadIdx.x] = a.taps.w[threadIdx.x];
+// Horizontal blur of one row run: window v (kRunH + 10 samples) -> out[0..kRunH).
+__device__ __forceinline__ void blur_row_store(const float* v, const float* w, float* out) {
+    float o[kRunH];
+    blur_window<kRunH>(v, w, o);
+#pragma unroll
+    for (int j = 0; j < kRunH; ++j) out[j] = o[j];
+}
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
     __syncthreads();
+    float sum = 0.0f;
+    if (threadIdx.x == 0)
+        for (int k = 0; k < (int)(blockDim.x / 32); ++k) sum += red[k];
+    return sum;
+}
+
+__global__ void __launch_bounds__(kFThreads, 3)
+    loss_ssim_kernel(const __grid_constant__ LossArgs a, float* __restrict__ planes, uint32_t pitch) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    SsimSmem& S = *reinterpret_cast<SsimSmem*>(smem_raw);
     float w[11];
 #pragma unroll
-    for (int k = 0; k < 11; ++k) w[k] = S.w[k];
-    const int tile_x0 = blockIdx.x * kFT, tile_y0 = blockIdx.y * kFT;
-    // pass-4 ownership: column c4, rows r4 .. r4 + 1 of the tile
-    const int c4 = threadIdx.x % kFT, r4 = (threadIdx.x / kFT) * kSeg4;
-    float g[3][kSeg4];
+    for (int k = 0; k < 11; ++k) w[k] = a.taps.w[k];
+    const int x0 = blockIdx.x * kFT, y0 = blockIdx.y * kFT;
+    // stage the 42x42 samples of all three channels (zero outside the image);
+    // each thread issues all of its loads before its first store
+    constexpr int kStageIters = (kFS * kFS + kFThreads - 1) / kFThreads;  // 7
+    float4 pv[kStageIters];
+    uint32_t gv[kStageIters];
+#pragma unroll
+    for (int i = 0; i < kStageIters; ++i) {
+        const int t = threadIdx.x + i * kFThreads;
+        const int ly = t / kFS, lx = t - ly * kFS;
+        const int gy = y0 + ly - kHalo, gx = x0 + lx - kHalo;
+        pv[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        gv[i] = 0u;
+        if (t < kFS * kFS && gy >= 0 && gx >= 0 && gy < (int)a.h && gx < (int)a.w) {
+            const size_t pid = (size_t)gy * a.w + gx;
+            pv[i] = __ldg(reinterpret_cast<const float4*>(a.pred) + pid);
+            gv[i] = __ldg(a.gt + pid);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < kStageIters; ++i) {
+        const int t = threadIdx.x + i * kFThreads;
+        if (t < kFS * kFS) {
+            const int ly = t / kFS, lx = t - ly * kFS;
+            const uint32_t v = gv[i];
+            float g0 = (float)(v & 0xffu) * kInv255;
+            float g1 = (float)((v >> 8u) & 0xffu) * kInv255;
+            float g2 = (float)((v >> 16u) & 0xffu) * kInv255;
+            if (a.composite) {
+                // (a zero sample outside the image has alpha 0 and stays zero: its
+                // background term is masked by the bounds)
+                const int gy = y0 + ly - kHalo, gx = x0 + lx - kHalo;
+                const bool in = gy >= 0 && gx >= 0 && gy < (int)a.h && gx < (int)a.w;
+                const float ta = in ? 1.0f - (float)(v >> 24u) * kInv255 : 0.0f;
+                g0 = g0 + ta * a.bg[0];
+                g1 = g1 + ta * a.bg[1];
+                g2 = g2 + ta * a.bg[2];
+            }
+            const int o = ly * kFSP + lx;
+            S.x[0][o] = pv[i].x;
+            S.x[1][o] = pv[i].y;
+            S.x[2][o] = pv[i].z;
+            S.y[0][o] = g0;
+            S.y[1][o] = g1;
+            S.y[2][o] = g2;
+        }
+    }
+    __syncthreads();
+    // vertical-pass ownership: column col, rows r0 .. r0 + 3 of the tile
+    const int col = threadIdx.x & (kFT - 1), r0 = (threadIdx.x / kFT) * kRunV;
+    const size_t plane = (size_t)a.h * pitch;
     float loss = 0.0f;
+    for (int c = 0; c < 3; ++c) {
+        // horizontal moment blur: 42 rows x 32 columns, one row per lane
+        if (threadIdx.x < kItemsH) {
+            const int row = threadIdx.x % kFS, run = threadIdx.x / kFS;
+            const float* xr = S.x[c] + row * kFSP + run * kRunH;
+            const float* yr = S.y[c] + row * kFSP + run * kRunH;
+            float xv[kRunH + 10], yv[kRunH + 10], t[kRunH + 10];
 #pragma unroll
-    for (int c = 0; c < 3; ++c)
+            for (int k = 0; k < kRunH + 10; ++k) {
+                xv[k] = xr[k];
+                yv[k] = yr[k];
+            }
+            float* hp = S.h[0] + row * kFHP + run * kRunH;
+            blur_row_store(xv, w, hp);
+            blur_row_store(yv, w, hp + 2 * kFH);
 #pragma unroll
-        for (int k = 0; k < kSeg4; ++k) g[c][k] = 0.0f;
-    if (a.ssim_w == 0.0f) {
+            for (int k = 0; k < kRunH + 10; ++k) t[k] = xv[k] * xv[k];
+            blur_row_store(t, w, hp + kFH);
 #pragma unroll
-        for (int k = 0; k < kSeg4; ++k) {
-            const uint32_t px = tile_x0 + c4, py = tile_y0 + r4 + k;
-            if (px < a.w && py < a.h) {
-                for (int c = 0; c < 3; ++c) {
-                    float ga;
-                    const float ge = gt_eff(a, c, py, px, &ga);
-                    const float diff = read_pred<true>(a, c, py, px) - ge;
-                    const float sign = diff > 0.0f ? 1.0f : (diff < 0.0f ? -1.0f : 0.0f);
-                    float ch = a.chain_const;
-                    float v = a.l1_w * fabsf(diff);
-                    if (a.mask) {
-                        ch = ch * ga;
-                        v = v * ga;
-                    }
-                    g[c][k] = a.l1_w * sign * ch;
-                    loss += v;
+            for (int k = 0; k < kRunH + 10; ++k) t[k] = yv[k] * yv[k];
+            blur_row_store(t, w, hp + 3 * kFH);
+#pragma unroll
+            for (int k = 0; k < kRunH + 10; ++k) t[k] = xv[k] * yv[k];
+            blur_row_store(t, w, hp + 4 * kFH);
+        }
+        __syncthreads();
+        // vertical blur + SSIM partials on the 32x32 core
+        float o[5][kRunV];
+#pragma unroll
+        for (int m = 0; m < 5; ++m) {
+            float v[kRunV + 10];
+#pragma unroll
+            for (int t = 0; t < kRunV + 10; ++t) v[t] = S.h[m][(r0 + t) * kFHP + col];
+            blur_window<kRunV>(v, w, o[m]);
+        }
+#pragma unroll
+        for (int j = 0; j < kRunV; ++j) {
+            const uint32_t gx = x0 + col, gy = y0 + r0 + j;
+            if (gx < a.w && gy < a.h) {
+                const Ssim sm = ssim_terms(o[0][j], o[1][j], o[2][j], o[3][j], o[4][j]);
+                float chain = a.chain_const, ga = 1.0f;
+                if (a.mask) {
+                    ga = (float)(__ldg(a.gt + (size_t)gy * a.w + gx) >> 24u) * kInv255;
+                    chain = chain * ga;
+                }
+                float* pp = planes + 3 * (size_t)c * plane + (size_t)gy * pitch + gx;
+                pp[0] = sm.dmu1 * chain;
+                pp[plane] = sm.dsig1 * chain;
+                pp[2 * plane] = sm.dsig12 * chain;
+                const int ci = (r0 + j + kHalo) * kFSP + col + kHalo;
+                float v = a.l1_w * fabsf(S.x[c][ci] - S.y[c][ci]) + a.ssim_w * sm.val;
+                if (a.mask) v = v * ga;
+                loss += v;
+            }
+        }
+        __syncthreads();  // h is rewritten by the next channel
+    }
+    const float sum = block_sum(loss, S.red);
+    if (threadIdx.x == 0) a.block_loss[blockIdx.y * gridDim.x + blockIdx.x] = sum;
+}
+
+__global__ void __launch_bounds__(kFThreads, 4)
+    loss_grad_kernel(const __grid_constant__ LossArgs a, const float* __restrict__ planes, uint32_t pitch) {
+    __shared__ GradSmem S;
+    float w[11];
+#pragma unroll
+    for (int k = 0; k < 11; ++k) w[k] = a.taps.w[k];
+    const int x0 = blockIdx.x * kFT, y0 = blockIdx.y * kFT;
+    const int col = threadIdx.x & (kFT - 1), r0 = (threadIdx.x / kFT) * kRunV;
+    const size_t plane = (size_t)a.h * pitch;
+    // staging ownership: 16-byte column group q4 of the 48 columns x0-8 .. x0+39
+    constexpr int kQ4 = 12, kRowsPerRound = kFThreads / kQ4;  // 21 rows per round (252 threads)
+    const int q4 = threadIdx.x % kQ4, rr = threadIdx.x / kQ4;
+    const int gx4 = x0 - 8 + 4 * q4;
+    const bool gx4_in = gx4 >= 0 && gx4 < (int)pitch;
+    static_assert(3 * kFS % kRowsPerRound == 0, "staging rounds cover the planes exactly");
+    constexpr int kStageRounds = 3 * kFS / kRowsPerRound;  // 6
+    // ground truth of this thread's four output pixels (shared by the channels)
+    uint32_t gt_px[kRunV];
+#pragma unroll
+    for (int j = 0; j < kRunV; ++j) {
+        const uint32_t gx = x0 + col, gy = y0 + r0 + j;
+        gt_px[j] = gx < a.w && gy < a.h ? __ldg(a.gt + (size_t)gy * a.w + gx) : 0u;
+    }
+    float g[3][kRunV];  // unrolled channel loop: g stays in registers
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+        // stage the three partial planes of channel c over rows y0-5 .. y0+36;
+        // staged column lx holds image column x0 - 5 + lx, zero outside the
+        // image. All loads of a thread are issued before its first store.
+        float4 v[kStageRounds];
+#pragma unroll
+        for (int i = 0; i < kStageRounds; ++i) {
+            const int row = rr + kRowsPerRound * i;
+            const int k = row / kFS, ly = row - k * kFS;
+            const int gy = y0 + ly - kHalo;
+            v[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (rr < kRowsPerRound && gx4_in && gy >= 0 && gy < (int)a.h)
+                v[i] = __ldg(reinterpret_cast<const float4*>(planes + (3 * (size_t)c + k) * plane +
+                                                             (size_t)gy * pitch + gx4));
+        }
+        if (rr < kRowsPerRound) {
+#pragma unroll
+            for (int i = 0; i < kStageRounds; ++i) {
+                const int row = rr + kRowsPerRound * i;
+                const int k = row / kFS, ly = row - k * kFS;
+                const float e[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+                float* dst = S.p[k] + ly * kFSP;
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int lx = 4 * q4 + u - 3;
+                    if (lx >= 0 && lx < kFS) dst[lx] = gx4 + u < (int)a.w ? e[u] : 0.0f;
                 }
             }
         }
-    } else {
-        constexpr int kH1 = kF1 * kPH;  // plane size of the first blur
-        constexpr int kP = kF2 * kPH;   // plane size of the partials
-        constexpr int kQ = kF2 * kPQ;   // plane size of the second blur
+        __syncthreads();
+        // horizontal blur of the partials: 42 rows x 32 columns, one row per lane
+        if (threadIdx.x < kItemsH) {
+            const int row = threadIdx.x % kFS, run = threadIdx.x / kFS;
+#pragma unroll
+            for (int k = 0; k < 3; ++k) {
+                const float* pr = S.p[k] + row * kFSP + run * kRunH;
+                float v[kRunH + 10];
+#pragma unroll
+                for (int t = 0; t < kRunH + 10; ++t) v[t] = pr[t];
+                blur_row_store(v, w, S.q[k] + row * kFHP + run * kRunH);
+            }
+        }
+        __syncthreads();
+        // vertical blur -> gradient of this thread's four pixels (their
+        // prediction is loaded first, so that the loads overlap the blur)
+        float p_px[kRunV];
+#pragma unroll
+        for (int j = 0; j < kRunV; ++j) {
+            const uint32_t gx = x0 + col, gy = y0 + r0 + j;
+            p_px[j] = gx < a.w && gy < a.h ? read_pred<true>(a, c, gy, gx) : 0.0f;
+        }
+        float s3[3][kRunV];
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+            float v[kRunV + 10];
+#pragma unroll
+            for (int t = 0; t < kRunV + 10; ++t) v[t] = S.q[k][(r0 + t) * kFHP + col];
+            blur_window<kRunV>(v, w, s3[k]);
+        }
+#pragma unroll
+        for (int j = 0; j < kRunV; ++j) {
+            g[c][j] = 0.0f;
+            const uint32_t gx = x0 + col, gy = y0 + r0 + j;
+            if (gx < a.w && gy < a.h) {
+                const float p1 = p_px[j];
+                const float ga = (float)(gt_px[j] >> 24u) * kInv255;
+                float ge = (float)((gt_px[j] >> (8u * c)) & 0xffu) * kInv255;
+                if (a.composite) ge = ge + (1.0f - ga) * a.bg[c];
+                const float sg = s3[0][j] + (2.0f * p1) * s3[1][j] + ge * s3[2][j];
+                const float diff = p1 - ge;
+                const float sign = diff > 0.0f ? 1.0f : (diff < 0.0f ? -1.0f : 0.0f);
+                float chc = a.chain_const;
+                if (a.mask) chc = chc * ga;
+                g[c][j] = a.ssim_w * sg + a.l1_w * sign * chc;
+            }
+        }
+        __syncthreads();  // p and q are restaged by the next channel
+    }
+#pragma unroll
+    for (int j = 0; j < kRunV; ++j) {
+        const uint32_t gx = x0 + col, gy = y0 + r0 + j;
+        if (gx < a.w && gy < a.h)
+            reinterpret_cast<float4*>(a.out)[(size_t)gy * a.w + gx] = make_float4(g[0][j], g[1][j], g[2][j], 0.0f);
+    }
+}
+
+// L1-only training form (ssim weight 0): one thread per pixel, all channels.
+constexpr int kL1Threads = 256;
+__global__ void __launch_bounds__(kL1Threads) loss_l1_fused_kernel(const __grid_constant__ LossArgs a) {
+    __shared__ float red[kL1Threads / 32];
+    const size_t pid = (size_t)blockIdx.x * kL1Threads + threadIdx.x;
+    float loss = 0.0f;
+    if (pid < (size_t)a.w * a.h) {
+        const uint32_t py = (uint32_t)(pid / a.w), px = (uint32_t)(pid - (size_t)py * a.w);
+        float g[3];
 #pragma unroll
         for (int c = 0; c < 3; ++c) {
-            // stage pred / gt_eff of the 52x52 region starting 10 pixels before the tile
-            for (int t = threadIdx.x; t < kF1 * kF1; t += kFusedThreads) {
-                const int ly = t / kF1, lx = t - ly * kF1;
-                const int gy = tile_y0 + ly - 2 * kHalo, gx = tile_x0 + lx - 2 * kHalo;
-                float pv = 0.0f, ge = 0.0f;
-                if (gy >= 0 && gx >= 0 && gy < (int)a.h && gx < (int)a.w) {
-                    pv = read_pred<true>(a, c, gy, gx);
-                    float ga;
-                    ge = gt_eff(a, c, gy, gx, &ga);
-                }
-                S.x[ly * kPX + lx] = pv;
-                S.y[ly * kPX + lx] = ge;
+            float ga;
+            const float ge = gt_eff(a, c, py, px, &ga);
+            const float diff = read_pred<true>(a, c, py, px) - ge;
+            const float sign = diff > 0.0f ? 1.0f : (diff < 0.0f ? -1.0f : 0.0f);
+            float ch = a.chain_const;
+            float v = a.l1_w * fabsf(diff);
+            if (a.mask) {
+                ch = ch * ga;
+                v = v * ga;
             }
-            __syncthreads();
-            // pass 1: horizontal moment blur, 52 rows x 42 output columns (one row
-            // per lane, runs of kSeg1 outputs: 468 runs, one round of the block)
-            constexpr int kRuns1 = (kF2 + kSeg1 - 1) / kSeg1;
-            static_assert(kF1 * kRuns1 <= kFusedThreads, "pass 1 fits one round");
-            for (int i = threadIdx.x; i < kF1 * kRuns1; i += kFusedThreads) {
-                const int seg = i / kF1, r = i - seg * kF1;
-                const int c0 = seg * kSeg1;
-                float xv[kSeg1 + 10], yv[kSeg1 + 10];
-#pragma unroll
-                for (int k = 0; k < kSeg1 + 10; ++k) {
-                    const bool ok = c0 + k < kF1;
-                    xv[k] = ok ? S.x[r * kPX + c0 + k] : 0.0f;
-                    yv[k] = ok ? S.y[r * kPX + c0 + k] : 0.0f;
-                }
-#pragma unroll
-                for (int j = 0; j < kSeg1; ++j) {
-                    float sx = 0.f, sx2 = 0.f, sy = 0.f, sy2 = 0.f, sxy = 0.f;
-#pragma unroll
-                    for (int d = 1; d < 6; ++d) {
-                        const float wd = w[5 - d];
-                        const float xl = xv[j + 5 - d], yl = yv[j + 5 - d], xr = xv[j + 5 + d], yr = yv[j + 5 + d];
-                        sx = __fmaf_rn(xl + xr, wd, sx);
-                        sx2 = __fmaf_rn(__fmaf_rn(xl, xl, xr * xr), wd, sx2);
-                        sy = __fmaf_rn(yl + yr, wd, sy);
-                        sy2 = __fmaf_rn(__fmaf_rn(yl, yl, yr * yr), wd, sy2);
-                        sxy = __fmaf_rn(__fmaf_rn(xl, yl, xr * yr), wd, sxy);
-                    }
-                    const float xc = xv[j + 5], yc = yv[j + 5], wc = w[5];
-                    if (c0 + j < kF2) {  // stored at once: five live sums, not 5 x kSeg1
-                        float* hp = S.h + r * kPH + c0 + j;
-                        hp[0] = __fmaf_rn(xc, wc, sx);
-                        hp[kH1] = __fmaf_rn(xc * xc, wc, sx2);
-                        hp[2 * kH1] = __fmaf_rn(yc, wc, sy);
-                        hp[3 * kH1] = __fmaf_rn(yc * yc, wc, sy2);
-                        hp[4 * kH1] = __fmaf_rn(xc * yc, wc, sxy);
-                    }
-                }
-            }
-            __syncthreads();
-            // pass 2: vertical blur + SSIM partials on the 42x42 grid (one column per lane)
-            for (int i = threadIdx.x; i < kF2 * 11; i += kFusedThreads) {
-                const int seg = i / kF2, col = i - seg * kF2;
-                const int r0 = seg * kSeg;
-                float o[5][kSeg];
-#pragma unroll
-                for (int k = 0; k < 5; ++k) {
-                    float v[kSeg + 10];
-#pragma unroll
-                    for (int t = 0; t < kSeg + 10; ++t)
-                        v[t] = r0 + t < kF1 ? S.h[k * kH1 + (r0 + t) * kPH + col] : 0.0f;
-                    blur_window<kSeg>(v, w, o[k]);
-                }
-#pragma unroll
-                for (int j = 0; j < kSeg; ++j) {
-                    const int pyl = r0 + j;
-                    if (pyl >= kF2) continue;
-                    const Ssim sm = ssim_terms(o[0][j], o[1][j], o[2][j], o[3][j], o[4][j]);
-                    const int gy = tile_y0 + pyl - kHalo, gx = tile_x0 + col - kHalo;
-                    float chain = 0.0f;
-                    if (gy >= 0 && gx >= 0 && gy < (int)a.h && gx < (int)a.w) {
-                        chain = a.chain_const;
-                        if (a.mask) {
-                            float gc, ga;
-                            read_gt(a, c, gy, gx, &gc, &ga);
-                            chain = chain * ga;
-                        }
-                    }
-                    const int t = pyl * kPH + col;
-                    S.p[t] = sm.dmu1 * chain;
-                    S.p[kP + t] = sm.dsig1 * chain;
-                    S.p[2 * kP + t] = sm.dsig12 * chain;
-                    if (pyl >= kHalo && pyl < kHalo + kFT && col >= kHalo && col < kHalo + kFT)
-                        S.val[(pyl - kHalo) * kFT + (col - kHalo)] = sm.val;
-                }
-            }
-            __syncthreads();
-            // pass 3: horizontal blur of the partials, 42 rows x 32 output columns (one row per lane)
-            for (int i = threadIdx.x; i < kF2 * (kFT / kSeg); i += kFusedThreads) {
-                const int seg = i / kF2, r = i - seg * kF2;
-                const int c0 = seg * kSeg;
-#pragma unroll
-                for (int k = 0; k < 3; ++k) {
-                    float v[kSeg + 10], o[kSeg];
-#pragma unroll
-                    for (int t = 0; t < kSeg + 10; ++t) v[t] = S.p[k * kP + r * kPH + c0 + t];
-                    blur_window<kSeg>(v, w, o);
-#pragma unroll
-                    for (int j = 0; j < kSeg; ++j) S.h[k * kQ + r * kPQ + c0 + j] = o[j];
-                }
-            }
-            __syncthreads();
-            // pass 4: vertical blur -> gradient of this thread's two output pixels
-            {
-                float s3[3][kSeg4];
-#pragma unroll
-                for (int k = 0; k < 3; ++k) {
-                    float v[kSeg4 + 10];
-#pragma unroll
-                    for (int t = 0; t < kSeg4 + 10; ++t) v[t] = S.h[k * kQ + (r4 + t) * kPQ + c4];
-                    blur_window<kSeg4>(v, w, s3[k]);
-                }
-#pragma unroll
-                for (int j = 0; j < kSeg4; ++j) {
-                    const int ty = r4 + j;
-                    const uint32_t px = tile_x0 + c4, py = tile_y0 + ty;
-                    if (px < a.w && py < a.h) {
-                        const int ci = (ty + 2 * kHalo) * kPX + c4 + 2 * kHalo;
-                        const float p1 = S.x[ci];
-                        const float ge = S.y[ci];
-                        float gc_unused, ga = 1.0f;
-                        if (a.mask) read_gt(a, c, py, px, &gc_unused, &ga);
-                        const float sg = s3[0][j] + (2.0f * p1) * s3[1][j] + ge * s3[2][j];
-                        const float diff = p1 - ge;
-                        const float sign = diff > 0.0f ? 1.0f : (diff < 0.0f ? -1.0f : 0.0f);
-                        float chc = a.chain_const;
-                        if (a.mask) chc = chc * ga;
-                        g[c][j] = a.ssim_w * sg + a.l1_w * sign * chc;
-                        float v = a.l1_w * fabsf(diff) + a.ssim_w * S.val[ty * kFT + c4];
-                        if (a.mask) v = v * ga;
-                        loss += v;
-                    }
-                }
-            }
-            __syncthreads();  // x, y, h and val are restaged by the next channel
+            g[c] = a.l1_w * sign * ch;
+            loss += v;
         }
+        reinterpret_cast<float4*>(a.out)[pid] = make_float4(g[0], g[1], g[2], 0.0f);
     }
-#pragma unroll
-    for (int k = 0; k < kSeg4; ++k) {
-        const uint32_t px = tile_x0 + c4, py = tile_y0 + r4 + k;
-        if (px < a.w && py < a.h)
-            reinterpret_cast<float4*>(a.out)[(size_t)py * a.w + px] = make_float4(g[0][k], g[1][k], g[2][k], 0.0f);
-    }
-    // block loss sum (fixed order)
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) loss += __shfl_xor_sync(0xffffffffu, loss, o);
-    if ((threadIdx.x & 31) == 0) S.red[threadIdx.x >> 5] = loss;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        float sum = 0.0f;
-        for (int k = 0; k < kFusedThreads / 32; ++k) sum += S.red[k];
-        a.block_loss[blockIdx.y * gridDim.x + blockIdx.x] = sum;
-    }
+    const float sum = block_sum(loss, red);
+    if (threadIdx.x == 0) a.block_loss[blockIdx.x] = sum;
 }
 
 __global__ void __launch_bounds__(1024) loss_mean_kernel(const float* partials, uint32_t count, double inv_n, float* out) {
@@ -689,25 +776,39 @@ bsx_status bsx_loss_fused(bsx_ctx* ctx, const float* d_image, const uint32_t* d_
     if (!ctx || !d_image || !d_gt || !cfg || !d_loss_mean || !d_v_output || w == 0 || h == 0) return BSX_ERR_INVALID_ARG;
     if (((uintptr_t)d_image | (uintptr_t)d_v_output) % 16) return fail(ctx, BSX_ERR_INVALID_ARG, "[H,W,4] buffers must be 16-byte aligned");
     cudaSetDevice(ctx->device);
-    dim3 grid((w + kFT - 1) / kFT, (h + kFT - 1) / kFT, 1);
-    const uint32_t blocks = grid.x * grid.y;
-    bsx_status s = ensure(ctx, ctx->loss_partials, (size_t)blocks * 4);
-    if (s != BSX_OK) return s;
-    constexpr size_t kFusedSmem = sizeof(FusedSmem);
-    static_assert(kFusedSmem <= 227 * 1024, "fused loss shared memory");
-    s = check_cuda(ctx, cudaFuncSetAttribute(loss_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)kFusedSmem),
-                   "cudaFuncSetAttribute (fused loss)");
-    if (s != BSX_OK) return s;
     LossArgs a = make_args(cfg, d_image, d_gt, w, h);
     const double n = 3.0 * (double)w * (double)h;
     a.chain_const = (float)(1.0 / n);
     a.out = d_v_output;
-    a.block_loss = ctx->loss_partials.as<float>();
-    prof_begin(ctx);
-    loss_fused_kernel<<<grid, kFusedThreads, kFusedSmem, ctx->stream>>>(a);
-    s = post_launch(ctx, "loss_fused_kernel");
+    const bool ssim = cfg->ssim_weight != 0.0f;
+    const dim3 grid = ssim ? dim3((w + kFT - 1) / kFT, (h + kFT - 1) / kFT, 1)
+                           : dim3((uint32_t)(((size_t)w * h + kL1Threads - 1) / kL1Threads), 1, 1);
+    const uint32_t blocks = grid.x * grid.y;
+    bsx_status s = ensure(ctx, ctx->loss_partials, (size_t)blocks * 4);
     if (s != BSX_OK) return s;
+    a.block_loss = ctx->loss_partials.as<float>();
+    if (ssim) {
+        const uint32_t pitch = (w + 3u) & ~3u;
+        s = ensure(ctx, ctx->loss_planes, 9 * (size_t)h * pitch * 4);
+        if (s != BSX_OK) return s;
+        constexpr size_t kSsimSmem = sizeof(SsimSmem);
+        static_assert(kSsimSmem <= 227 * 1024, "SSIM pass shared memory");
+        s = check_cuda(ctx, cudaFuncSetAttribute(loss_ssim_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)kSsimSmem),
+                       "cudaFuncSetAttribute (SSIM pass)");
+        if (s != BSX_OK) return s;
+        float* planes = ctx->loss_planes.as<float>();
+        prof_begin(ctx);
+        loss_ssim_kernel<<<grid, kFThreads, kSsimSmem, ctx->stream>>>(a, planes, pitch);
+        if ((s = post_launch(ctx, "loss_ssim_kernel")) != BSX_OK) return s;
+        prof_begin(ctx);
+        loss_grad_kernel<<<grid, kFThreads, 0, ctx->stream>>>(a, planes, pitch);
+        if ((s = post_launch(ctx, "loss_grad_kernel")) != BSX_OK) return s;
+    } else {
+        prof_begin(ctx);
+        loss_l1_fused_kernel<<<grid, kL1Threads, 0, ctx->stream>>>(a);
+        if ((s = post_launch(ctx, "loss_l1_fused_kernel")) != BSX_OK) return s;
+    }
     prof_begin(ctx);
     loss_mean_kernel<<<1, 1024, 0, ctx->stream>>>(a.block_loss, blocks, 1.0 / n, d_loss_mean);
     return post_launch(ctx, "loss_mean_kernel");

@@ -96,7 +96,9 @@ def test_loss_alpha_channel(cuda, orc):
     (33, 70, {"composite_bg": (0.2, 0.5, 0.9), "mask": True}),
     (40, 47, {"l1_weight": 1.0, "ssim_weight": 0.0}),
     (1, 1, {}),
-], ids=["aligned", "ragged", "composite_mask", "l1_only", "single_pixel"])
+    (70, 1, {}),
+    (9, 301, {"composite_bg": (0.7, 0.1, 0.3)}),
+], ids=["aligned", "ragged", "composite_mask", "l1_only", "single_pixel", "single_column", "wide_strip"])
 def test_fused_loss_matches_mean_and_gradient(cuda, orc, h, w, cfg):
     from brush_b200.loss import ImageLossConfig, image_loss_fused
 
