@@ -356,20 +356,25 @@ __global__ void __launch_bounds__(256) loss_bwd_kernel(const __grid_constant__ L
 // colour channels at once), blurs the five moments horizontally over the 42
 // rows x 32 core columns and vertically over the 32x32 core, and writes for
 // every image pixel the chain-weighted SSIM partials (d/d mu_x, d/d sigma_x^2,
-// d/d sigma_xy, each times d loss / d map) as nine planes [c][k][H][pitch]
-// (pitch = W rounded up to 4), with the loss summed per block.
-// loss_grad_kernel stages those planes over the same halo with 16-byte loads,
-// blurs them horizontally then vertically, and forms each core pixel's
-// gradient. Cutting at the partials leaves one halo per blur: each pass
-// evaluates at most 1.31x its outputs, where one kernel doing all four passes
-// needs 52x42 moment blurs and 42x42 SSIM values per 32x32 tile. The planes
-// (36 bytes per pixel) are written once and read back while still largely
-// resident in L2. Blur passes run register sliding windows (a run of 8 outputs
-// per thread horizontally, 4 vertically); planes have odd pitches, so lanes
-// walking down a column (horizontal passes, one row per lane) or along a row
-// (vertical passes) hit distinct banks. Tap and summation order per output are
-// those of loss_bwd_channel: taps d = 1..5 as (left + right) * w[5-d], then
-// the centre.
+// d/d sigma_xy, each times d loss / d map) with the loss summed per block.
+// loss_grad_kernel (one channel per block) stages those partials over the same
+// halo with 16-byte loads, blurs them horizontally then vertically, and forms
+// each core pixel's gradient. Cutting at the partials leaves one halo per
+// blur: each pass evaluates at most 1.31x its outputs, where one kernel doing
+// all four passes needs 52x42 moment blurs and 42x42 SSIM values per 32x32
+// tile. The partials (36 bytes per pixel) are written once and read back
+// while still largely resident in L2.
+//
+// Quantities that are blurred alike travel in pairs through Blackwell's
+// two-lane FP32 instructions (add / mul / fma .rn.f32x2, each lane rounded as
+// the scalar instruction): the staged samples as (x, y), the moments as
+// (mu_x, mu_y), (E[x^2], E[y^2]) and E[xy], the partials as
+// (d/d mu_x, d/d sigma_x^2) and d/d sigma_xy. Blur passes run register sliding
+// windows (a run of 8 outputs per thread horizontally, 4 vertically); planes
+// have odd pitches, so lanes walking down a column (horizontal passes, one row
+// per lane) or along a row (vertical passes) hit distinct banks. Tap and
+// summation order per output are those of loss_bwd_channel: taps d = 1..5 as
+// (left + right) * w[5-d], then the centre.
 constexpr int kFT = 32;                        // output tile edge
 constexpr int kFS = kFT + 2 * kHalo;           // 42: staged grid edge
 constexpr int kFSP = kFS + 1;                  // 43: pitch of the staged planes
@@ -380,37 +385,74 @@ constexpr int kRunV = 4;                       // outputs per thread, vertical p
 constexpr int kItemsH = kFS * (kFT / kRunH);   // 168 (row, run) items of a horizontal pass
 static_assert(kFT * (kFT / kRunV) == kFThreads, "a vertical pass covers the tile once");
 static_assert(kItemsH <= kFThreads, "a horizontal pass is one round");
+constexpr int kFStage = kFS * kFSP;            // size of one staged plane
 constexpr int kFH = kFS * kFHP;                // size of one horizontal-blur plane
 
-struct SsimSmem {
-    float x[3][kFS * kFSP];  // staged prediction per channel, 42 x 42
-    float y[3][kFS * kFSP];  // staged effective ground truth
-    float h[5][kFH];         // horizontal moment blur of one channel, 42 x 32
-    float red[kFThreads / 32];
-};
-struct GradSmem {
-    float p[3][kFS * kFSP];  // staged partial planes of one channel, 42 x 42
-    float q[3][kFH];         // their horizontal blur, 42 x 32
-};
-
-// out[j] = blur of window v at output j (centre v[j + 5]), j < N.
-template <int N>
-__device__ __forceinline__ void blur_window(const float* v, const float* w, float* out) {
-#pragma unroll
-    for (int j = 0; j < N; ++j) {
-        float acc = 0.0f;
-#pragma unroll
-        for (int d = 1; d < 6; ++d) acc = __fmaf_rn(v[j + 5 - d] + v[j + 5 + d], w[5 - d], acc);
-        out[j] = __fmaf_rn(v[j + 5], w[5], acc);
-    }
+// Two f32 lanes in one 64-bit register (low lane first).
+typedef unsigned long long f2;
+__device__ __forceinline__ f2 f2_pack(float lo, float hi) {
+    f2 r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ float f2_lo(f2 v) {
+    float lo, hi;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+    return lo;
+}
+__device__ __forceinline__ float f2_hi(f2 v) {
+    float lo, hi;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+    return hi;
+}
+__device__ __forceinline__ f2 f2_add(f2 a, f2 b) {
+    f2 r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ f2 f2_mul(f2 a, f2 b) {
+    f2 r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ f2 f2_fma(f2 a, f2 b, f2 c) {
+    f2 r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
 }
 
-// Horizontal blur of one row run: window v (kRunH + 10 samples) -> out[0..kRunH).
-__device__ __forceinline__ void blur_row_store(const float* v, const float* w, float* out) {
-    float o[kRunH];
-    blur_window<kRunH>(v, w, o);
+// Blur taps as lane pairs (w[k], w[k]).
+struct Taps2 {
+    f2 w[6];  // w[0..5] of the 11 symmetric taps
+};
+__device__ __forceinline__ Taps2 taps2(const LossTaps& t) {
+    Taps2 r;
 #pragma unroll
-    for (int j = 0; j < kRunH; ++j) out[j] = o[j];
+    for (int k = 0; k < 6; ++k) r.w[k] = f2_pack(t.w[k], t.w[k]);
+    return r;
+}
+
+// Output j of the window v (centre v[j + 5]): (v[j+4] + v[j+6]) w4 first, then
+// the taps d = 2..5, then the centre.
+template <int N>
+__device__ __forceinline__ void blur2(const f2* v, const Taps2& w, f2* out) {
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+        f2 acc = f2_mul(f2_add(v[j + 4], v[j + 6]), w.w[4]);
+#pragma unroll
+        for (int d = 2; d < 6; ++d) acc = f2_fma(f2_add(v[j + 5 - d], v[j + 5 + d]), w.w[5 - d], acc);
+        out[j] = f2_fma(v[j + 5], w.w[5], acc);
+    }
+}
+template <int N>
+__device__ __forceinline__ void blur1(const float* v, const Taps2& w, float* out) {
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+        float acc = (v[j + 4] + v[j + 6]) * f2_lo(w.w[4]);
+#pragma unroll
+        for (int d = 2; d < 6; ++d) acc = __fmaf_rn(v[j + 5 - d] + v[j + 5 + d], f2_lo(w.w[5 - d]), acc);
+        out[j] = __fmaf_rn(v[j + 5], f2_lo(w.w[5]), acc);
+    }
 }
 
 __device__ __forceinline__ float block_sum(float v, float* red) {
@@ -424,13 +466,21 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
     return sum;
 }
 
+struct SsimSmem {
+    f2 xy[3][kFStage];  // staged (prediction, effective ground truth) per channel, 42 x 42
+    f2 m01[kFH];        // horizontal blur of one channel: (x, y)
+    f2 m23[kFH];        //                                 (x^2, y^2)
+    float m4[kFH];      //                                 x y
+    float red[kFThreads / 32];
+};
+
+// Partial planes of channel c: (d/d mu_x, d/d sigma_x^2) pairs [H][pitch] at
+// 3c planes, d/d sigma_xy [H][pitch] at 3c + 2 planes (plane = H * pitch floats).
 __global__ void __launch_bounds__(kFThreads, 3)
     loss_ssim_kernel(const __grid_constant__ LossArgs a, float* __restrict__ planes, uint32_t pitch) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     SsimSmem& S = *reinterpret_cast<SsimSmem*>(smem_raw);
-    float w[11];
-#pragma unroll
-    for (int k = 0; k < 11; ++k) w[k] = a.taps.w[k];
+    const Taps2 w = taps2(a.taps);
     const int x0 = blockIdx.x * kFT, y0 = blockIdx.y * kFT;
     // stage the 42x42 samples of all three channels (zero outside the image);
     // each thread issues all of its loads before its first store
@@ -460,8 +510,7 @@ __global__ void __launch_bounds__(kFThreads, 3)
             float g1 = (float)((v >> 8u) & 0xffu) * kInv255;
             float g2 = (float)((v >> 16u) & 0xffu) * kInv255;
             if (a.composite) {
-                // (a zero sample outside the image has alpha 0 and stays zero: its
-                // background term is masked by the bounds)
+                // a zero sample outside the image stays zero
                 const int gy = y0 + ly - kHalo, gx = x0 + lx - kHalo;
                 const bool in = gy >= 0 && gx >= 0 && gy < (int)a.h && gx < (int)a.w;
                 const float ta = in ? 1.0f - (float)(v >> 24u) * kInv255 : 0.0f;
@@ -470,12 +519,9 @@ __global__ void __launch_bounds__(kFThreads, 3)
                 g2 = g2 + ta * a.bg[2];
             }
             const int o = ly * kFSP + lx;
-            S.x[0][o] = pv[i].x;
-            S.x[1][o] = pv[i].y;
-            S.x[2][o] = pv[i].z;
-            S.y[0][o] = g0;
-            S.y[1][o] = g1;
-            S.y[2][o] = g2;
+            S.xy[0][o] = f2_pack(pv[i].x, g0);
+            S.xy[1][o] = f2_pack(pv[i].y, g1);
+            S.xy[2][o] = f2_pack(pv[i].z, g2);
         }
     }
     __syncthreads();
@@ -487,171 +533,195 @@ __global__ void __launch_bounds__(kFThreads, 3)
         // horizontal moment blur: 42 rows x 32 columns, one row per lane
         if (threadIdx.x < kItemsH) {
             const int row = threadIdx.x % kFS, run = threadIdx.x / kFS;
-            const float* xr = S.x[c] + row * kFSP + run * kRunH;
-            const float* yr = S.y[c] + row * kFSP + run * kRunH;
-            float xv[kRunH + 10], yv[kRunH + 10], t[kRunH + 10];
+            const f2* src = S.xy[c] + row * kFSP + run * kRunH;
+            f2 v[kRunH + 10], o[kRunH];
 #pragma unroll
-            for (int k = 0; k < kRunH + 10; ++k) {
-                xv[k] = xr[k];
-                yv[k] = yr[k];
-            }
-            float* hp = S.h[0] + row * kFHP + run * kRunH;
-            blur_row_store(xv, w, hp);
-            blur_row_store(yv, w, hp + 2 * kFH);
+            for (int k = 0; k < kRunH + 10; ++k) v[k] = src[k];
+            const int hb = row * kFHP + run * kRunH;
+            blur2<kRunH>(v, w, o);
 #pragma unroll
-            for (int k = 0; k < kRunH + 10; ++k) t[k] = xv[k] * xv[k];
-            blur_row_store(t, w, hp + kFH);
+            for (int j = 0; j < kRunH; ++j) S.m01[hb + j] = o[j];
+            float t[kRunH + 10], ot[kRunH];
 #pragma unroll
-            for (int k = 0; k < kRunH + 10; ++k) t[k] = yv[k] * yv[k];
-            blur_row_store(t, w, hp + 3 * kFH);
+            for (int k = 0; k < kRunH + 10; ++k) t[k] = f2_lo(v[k]) * f2_hi(v[k]);
 #pragma unroll
-            for (int k = 0; k < kRunH + 10; ++k) t[k] = xv[k] * yv[k];
-            blur_row_store(t, w, hp + 4 * kFH);
+            for (int k = 0; k < kRunH + 10; ++k) v[k] = f2_mul(v[k], v[k]);
+            blur2<kRunH>(v, w, o);
+#pragma unroll
+            for (int j = 0; j < kRunH; ++j) S.m23[hb + j] = o[j];
+            blur1<kRunH>(t, w, ot);
+#pragma unroll
+            for (int j = 0; j < kRunH; ++j) S.m4[hb + j] = ot[j];
         }
         __syncthreads();
         // vertical blur + SSIM partials on the 32x32 core
-        float o[5][kRunV];
+        f2 mu[kRunV], sq[kRunV];
+        float xy[kRunV];
+        {
+            f2 v[kRunV + 10];
 #pragma unroll
-        for (int m = 0; m < 5; ++m) {
-            float v[kRunV + 10];
+            for (int t = 0; t < kRunV + 10; ++t) v[t] = S.m01[(r0 + t) * kFHP + col];
+            blur2<kRunV>(v, w, mu);
 #pragma unroll
-            for (int t = 0; t < kRunV + 10; ++t) v[t] = S.h[m][(r0 + t) * kFHP + col];
-            blur_window<kRunV>(v, w, o[m]);
+            for (int t = 0; t < kRunV + 10; ++t) v[t] = S.m23[(r0 + t) * kFHP + col];
+            blur2<kRunV>(v, w, sq);
+            float u[kRunV + 10];
+#pragma unroll
+            for (int t = 0; t < kRunV + 10; ++t) u[t] = S.m4[(r0 + t) * kFHP + col];
+            blur1<kRunV>(u, w, xy);
         }
 #pragma unroll
         for (int j = 0; j < kRunV; ++j) {
             const uint32_t gx = x0 + col, gy = y0 + r0 + j;
             if (gx < a.w && gy < a.h) {
-                const Ssim sm = ssim_terms(o[0][j], o[1][j], o[2][j], o[3][j], o[4][j]);
+                const Ssim sm = ssim_terms(f2_lo(mu[j]), f2_lo(sq[j]), f2_hi(mu[j]), f2_hi(sq[j]), xy[j]);
                 float chain = a.chain_const, ga = 1.0f;
                 if (a.mask) {
                     ga = (float)(__ldg(a.gt + (size_t)gy * a.w + gx) >> 24u) * kInv255;
                     chain = chain * ga;
                 }
-                float* pp = planes + 3 * (size_t)c * plane + (size_t)gy * pitch + gx;
-                pp[0] = sm.dmu1 * chain;
-                pp[plane] = sm.dsig1 * chain;
-                pp[2 * plane] = sm.dsig12 * chain;
-                const int ci = (r0 + j + kHalo) * kFSP + col + kHalo;
-                float v = a.l1_w * fabsf(S.x[c][ci] - S.y[c][ci]) + a.ssim_w * sm.val;
+                const size_t px = (size_t)gy * pitch + gx;
+                reinterpret_cast<float2*>(planes + 3 * (size_t)c * plane)[px] =
+                    make_float2(sm.dmu1 * chain, sm.dsig1 * chain);
+                planes[(3 * (size_t)c + 2) * plane + px] = sm.dsig12 * chain;
+                const f2 s = S.xy[c][(r0 + j + kHalo) * kFSP + col + kHalo];
+                float v = a.l1_w * fabsf(f2_lo(s) - f2_hi(s)) + a.ssim_w * sm.val;
                 if (a.mask) v = v * ga;
                 loss += v;
             }
         }
-        __syncthreads();  // h is rewritten by the next channel
+        __syncthreads();  // the moment planes are rewritten by the next channel
     }
     const float sum = block_sum(loss, S.red);
     if (threadIdx.x == 0) a.block_loss[blockIdx.y * gridDim.x + blockIdx.x] = sum;
 }
 
-__global__ void __launch_bounds__(kFThreads, 4)
+struct GradSmem {
+    f2 p01[kFStage];   // staged (d/d mu_x, d/d sigma_x^2) partials, 42 x 42
+    float p2[kFStage]; // staged d/d sigma_xy partials
+    f2 q01[kFH];       // their horizontal blur, 42 x 32
+    float q2[kFH];
+};
+
+// Grid (3, tiles x, tiles y): one colour channel per block, the three channel
+// blocks of a tile adjacent in launch order (they read the same image and
+// ground-truth lines); block c writes lane c of the [H,W,4] gradient (block 0
+// also the zero alpha lane).
+__global__ void __launch_bounds__(kFThreads, 5)
     loss_grad_kernel(const __grid_constant__ LossArgs a, const float* __restrict__ planes, uint32_t pitch) {
     __shared__ GradSmem S;
-    float w[11];
-#pragma unroll
-    for (int k = 0; k < 11; ++k) w[k] = a.taps.w[k];
-    const int x0 = blockIdx.x * kFT, y0 = blockIdx.y * kFT;
+    const Taps2 w = taps2(a.taps);
+    const int c = blockIdx.x;
+    const int x0 = blockIdx.y * kFT, y0 = blockIdx.z * kFT;
     const int col = threadIdx.x & (kFT - 1), r0 = (threadIdx.x / kFT) * kRunV;
     const size_t plane = (size_t)a.h * pitch;
-    // staging ownership: 16-byte column group q4 of the 48 columns x0-8 .. x0+39
-    constexpr int kQ4 = 12, kRowsPerRound = kFThreads / kQ4;  // 21 rows per round (252 threads)
-    const int q4 = threadIdx.x % kQ4, rr = threadIdx.x / kQ4;
-    const int gx4 = x0 - 8 + 4 * q4;
-    const bool gx4_in = gx4 >= 0 && gx4 < (int)pitch;
-    static_assert(3 * kFS % kRowsPerRound == 0, "staging rounds cover the planes exactly");
-    constexpr int kStageRounds = 3 * kFS / kRowsPerRound;  // 6
-    // ground truth of this thread's four output pixels (shared by the channels)
+    const float* p01g = planes + 3 * (size_t)c * plane;
+    const float* p2g = planes + (3 * (size_t)c + 2) * plane;
+    // stage rows y0-5 .. y0+36 of both partial planes over the 48 columns
+    // x0-8 .. x0+39 with 16-byte loads; staged column lx holds image column
+    // x0 - 5 + lx, zero outside the image. The loads form 126 segments of 12:
+    // segments 0-83 are the two halves of each row of pairs (two pixels per
+    // load), 84-125 the rows of singles (four pixels per load); a round covers 21
+    // segments, so rounds 0-3 read pairs and rounds 4-5 singles, uniformly per
+    // warp. All loads of a thread are issued before its first store.
+    constexpr int kQ4 = 12, kSegPerRound = kFThreads / kQ4;  // 21 (252 threads)
+    constexpr int kPairSegs = 2 * kFS, kRounds = 3 * kFS / kSegPerRound;  // 84, 6
+    static_assert(kPairSegs % kSegPerRound == 0 && 3 * kFS % kSegPerRound == 0, "uniform staging rounds");
+    const int q4 = threadIdx.x % kQ4, sr = threadIdx.x / kQ4;
+    const bool stager = sr < kSegPerRound;
+    float4 v[kRounds];
+#pragma unroll
+    for (int i = 0; i < kRounds; ++i) {
+        const int seg = sr + kSegPerRound * i;
+        const bool pairs = i < kPairSegs / kSegPerRound;
+        const int ly = pairs ? seg >> 1 : seg - kPairSegs;
+        const int gx = pairs ? x0 - 8 + 24 * (seg & 1) + 2 * q4 : x0 - 8 + 4 * q4;
+        const int gy = y0 + ly - kHalo;
+        v[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (stager && gy >= 0 && gy < (int)a.h && gx >= 0 && gx < (int)pitch)
+            v[i] = pairs ? __ldg(reinterpret_cast<const float4*>(p01g + 2 * ((size_t)gy * pitch + gx)))
+                         : __ldg(reinterpret_cast<const float4*>(p2g + (size_t)gy * pitch + gx));
+    }
+    if (stager) {
+#pragma unroll
+        for (int i = 0; i < kRounds; ++i) {
+            const int seg = sr + kSegPerRound * i;
+            if (i < kPairSegs / kSegPerRound) {
+                const int ly = seg >> 1, lx = 24 * (seg & 1) + 2 * q4 - 3;
+                const int gx = x0 - 5 + lx;
+                f2* dst = S.p01 + ly * kFSP;
+                if (lx >= 0 && lx < kFS) dst[lx] = gx < (int)a.w ? f2_pack(v[i].x, v[i].y) : 0ull;
+                if (lx + 1 >= 0 && lx + 1 < kFS) dst[lx + 1] = gx + 1 < (int)a.w ? f2_pack(v[i].z, v[i].w) : 0ull;
+            } else {
+                const int ly = seg - kPairSegs, lx = 4 * q4 - 3;
+                const int gx = x0 - 5 + lx;
+                const float e[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+                float* dst = S.p2 + ly * kFSP;
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    if (lx + u >= 0 && lx + u < kFS) dst[lx + u] = gx + u < (int)a.w ? e[u] : 0.0f;
+            }
+        }
+    }
+    __syncthreads();
+    // horizontal blur of the partials: 42 rows x 32 columns, one row per lane
+    if (threadIdx.x < kItemsH) {
+        const int row = threadIdx.x % kFS, run = threadIdx.x / kFS;
+        const int sb = row * kFSP + run * kRunH, hb = row * kFHP + run * kRunH;
+        f2 t2[kRunH + 10], o2[kRunH];
+#pragma unroll
+        for (int u = 0; u < kRunH + 10; ++u) t2[u] = S.p01[sb + u];
+        blur2<kRunH>(t2, w, o2);
+#pragma unroll
+        for (int j = 0; j < kRunH; ++j) S.q01[hb + j] = o2[j];
+        float t1[kRunH + 10], o1[kRunH];
+#pragma unroll
+        for (int u = 0; u < kRunH + 10; ++u) t1[u] = S.p2[sb + u];
+        blur1<kRunH>(t1, w, o1);
+#pragma unroll
+        for (int j = 0; j < kRunH; ++j) S.q2[hb + j] = o1[j];
+    }
+    __syncthreads();
+    // vertical blur -> gradient of this thread's four pixels (their prediction
+    // and ground truth are loaded first, so that the loads overlap the blur)
+    float p_px[kRunV];
     uint32_t gt_px[kRunV];
 #pragma unroll
     for (int j = 0; j < kRunV; ++j) {
         const uint32_t gx = x0 + col, gy = y0 + r0 + j;
-        gt_px[j] = gx < a.w && gy < a.h ? __ldg(a.gt + (size_t)gy * a.w + gx) : 0u;
+        const bool in = gx < a.w && gy < a.h;
+        p_px[j] = in ? read_pred<true>(a, c, gy, gx) : 0.0f;
+        gt_px[j] = in ? __ldg(a.gt + (size_t)gy * a.w + gx) : 0u;
     }
-    float g[3][kRunV];  // unrolled channel loop: g stays in registers
+    f2 s01[kRunV];
+    float s2[kRunV];
+    {
+        f2 t2[kRunV + 10];
 #pragma unroll
-    for (int c = 0; c < 3; ++c) {
-        // stage the three partial planes of channel c over rows y0-5 .. y0+36;
-        // staged column lx holds image column x0 - 5 + lx, zero outside the
-        // image. All loads of a thread are issued before its first store.
-        float4 v[kStageRounds];
+        for (int u = 0; u < kRunV + 10; ++u) t2[u] = S.q01[(r0 + u) * kFHP + col];
+        blur2<kRunV>(t2, w, s01);
+        float t1[kRunV + 10];
 #pragma unroll
-        for (int i = 0; i < kStageRounds; ++i) {
-            const int row = rr + kRowsPerRound * i;
-            const int k = row / kFS, ly = row - k * kFS;
-            const int gy = y0 + ly - kHalo;
-            v[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            if (rr < kRowsPerRound && gx4_in && gy >= 0 && gy < (int)a.h)
-                v[i] = __ldg(reinterpret_cast<const float4*>(planes + (3 * (size_t)c + k) * plane +
-                                                             (size_t)gy * pitch + gx4));
-        }
-        if (rr < kRowsPerRound) {
-#pragma unroll
-            for (int i = 0; i < kStageRounds; ++i) {
-                const int row = rr + kRowsPerRound * i;
-                const int k = row / kFS, ly = row - k * kFS;
-                const float e[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
-                float* dst = S.p[k] + ly * kFSP;
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int lx = 4 * q4 + u - 3;
-                    if (lx >= 0 && lx < kFS) dst[lx] = gx4 + u < (int)a.w ? e[u] : 0.0f;
-                }
-            }
-        }
-        __syncthreads();
-        // horizontal blur of the partials: 42 rows x 32 columns, one row per lane
-        if (threadIdx.x < kItemsH) {
-            const int row = threadIdx.x % kFS, run = threadIdx.x / kFS;
-#pragma unroll
-            for (int k = 0; k < 3; ++k) {
-                const float* pr = S.p[k] + row * kFSP + run * kRunH;
-                float v[kRunH + 10];
-#pragma unroll
-                for (int t = 0; t < kRunH + 10; ++t) v[t] = pr[t];
-                blur_row_store(v, w, S.q[k] + row * kFHP + run * kRunH);
-            }
-        }
-        __syncthreads();
-        // vertical blur -> gradient of this thread's four pixels (their
-        // prediction is loaded first, so that the loads overlap the blur)
-        float p_px[kRunV];
-#pragma unroll
-        for (int j = 0; j < kRunV; ++j) {
-            const uint32_t gx = x0 + col, gy = y0 + r0 + j;
-            p_px[j] = gx < a.w && gy < a.h ? read_pred<true>(a, c, gy, gx) : 0.0f;
-        }
-        float s3[3][kRunV];
-#pragma unroll
-        for (int k = 0; k < 3; ++k) {
-            float v[kRunV + 10];
-#pragma unroll
-            for (int t = 0; t < kRunV + 10; ++t) v[t] = S.q[k][(r0 + t) * kFHP + col];
-            blur_window<kRunV>(v, w, s3[k]);
-        }
-#pragma unroll
-        for (int j = 0; j < kRunV; ++j) {
-            g[c][j] = 0.0f;
-            const uint32_t gx = x0 + col, gy = y0 + r0 + j;
-            if (gx < a.w && gy < a.h) {
-                const float p1 = p_px[j];
-                const float ga = (float)(gt_px[j] >> 24u) * kInv255;
-                float ge = (float)((gt_px[j] >> (8u * c)) & 0xffu) * kInv255;
-                if (a.composite) ge = ge + (1.0f - ga) * a.bg[c];
-                const float sg = s3[0][j] + (2.0f * p1) * s3[1][j] + ge * s3[2][j];
-                const float diff = p1 - ge;
-                const float sign = diff > 0.0f ? 1.0f : (diff < 0.0f ? -1.0f : 0.0f);
-                float chc = a.chain_const;
-                if (a.mask) chc = chc * ga;
-                g[c][j] = a.ssim_w * sg + a.l1_w * sign * chc;
-            }
-        }
-        __syncthreads();  // p and q are restaged by the next channel
+        for (int u = 0; u < kRunV + 10; ++u) t1[u] = S.q2[(r0 + u) * kFHP + col];
+        blur1<kRunV>(t1, w, s2);
     }
 #pragma unroll
     for (int j = 0; j < kRunV; ++j) {
         const uint32_t gx = x0 + col, gy = y0 + r0 + j;
-        if (gx < a.w && gy < a.h)
-            reinterpret_cast<float4*>(a.out)[(size_t)gy * a.w + gx] = make_float4(g[0][j], g[1][j], g[2][j], 0.0f);
+        if (gx < a.w && gy < a.h) {
+            const float p1 = p_px[j];
+            const float ga = (float)(gt_px[j] >> 24u) * kInv255;
+            float ge = (float)((gt_px[j] >> (8u * c)) & 0xffu) * kInv255;
+            if (a.composite) ge = ge + (1.0f - ga) * a.bg[c];
+            const float sg = f2_lo(s01[j]) + (2.0f * p1) * f2_hi(s01[j]) + ge * s2[j];
+            const float diff = p1 - ge;
+            const float sign = diff > 0.0f ? 1.0f : (diff < 0.0f ? -1.0f : 0.0f);
+            float chc = a.chain_const;
+            if (a.mask) chc = chc * ga;
+            float* dst = a.out + ((size_t)gy * a.w + gx) * 4;
+            dst[c] = a.ssim_w * sg + a.l1_w * sign * chc;
+            if (c == 0) dst[3] = 0.0f;
+        }
     }
 }
 
@@ -802,7 +872,7 @@ bsx_status bsx_loss_fused(bsx_ctx* ctx, const float* d_image, const uint32_t* d_
         loss_ssim_kernel<<<grid, kFThreads, kSsimSmem, ctx->stream>>>(a, planes, pitch);
         if ((s = post_launch(ctx, "loss_ssim_kernel")) != BSX_OK) return s;
         prof_begin(ctx);
-        loss_grad_kernel<<<grid, kFThreads, 0, ctx->stream>>>(a, planes, pitch);
+        loss_grad_kernel<<<dim3(3, grid.x, grid.y), kFThreads, 0, ctx->stream>>>(a, planes, pitch);
         if ((s = post_launch(ctx, "loss_grad_kernel")) != BSX_OK) return s;
     } else {
         prof_begin(ctx);
