@@ -44,7 +44,9 @@ def test_sort_small_kat(cuda):
         assert (_u(ko) == keys[order]).all() and (_u(vo) == order).all()
 
 
-@pytest.mark.parametrize("n,bits", [(1, 32), (4095, 32), (4097, 16), (1_000_003, 32), (30_000_000, 13),
+# sizes of the benchmark's depth (647,777 visible) and tile (3,140,719 intersections) sorts among them
+@pytest.mark.parametrize("n,bits", [(1, 32), (4095, 32), (4097, 16), (647_777, 32), (1_000_003, 32),
+                                    (1_800_001, 32), (2_400_000, 13), (3_140_719, 13), (30_000_000, 13),
                                     (70_000_000, 32)])
 def test_sort_large_random(cuda, n, bits):
     from brush_b200.primitives import radix_argsort
