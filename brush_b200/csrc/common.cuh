@@ -152,7 +152,7 @@ struct bsx_ctx {
     // workspace
     bsx::DevBuf projected, counts, depth_keys, vis_gid, depth_order, cum, isect_tile, isect_gid, tile_offsets,
         image, image_packed, visible, max_radius, sort_tmp_k, sort_tmp_v, sort_hist, sort_lookback, scan_status,
-        scalars, grad, loss_partials, loss_planes, sort_keys_b, sort_vals_b, tile_order,
+        scalars, grad, loss_partials, loss_planes, sort_keys_b, sort_vals_b, tile_order, isect_mask,
         // reference-layout backward operators (ref_bwd.cu)
         ref_rows, ref_ids, ref_offsets, ref_grad,
         // percentile bounds of the means (bounds.cu)

@@ -150,7 +150,7 @@ bsx_status bsx_destroy(bsx_ctx* ctx) {
                       &ctx->image_packed, &ctx->visible, &ctx->max_radius, &ctx->sort_tmp_k, &ctx->sort_tmp_v,
                       &ctx->sort_hist, &ctx->sort_lookback, &ctx->scan_status, &ctx->scalars, &ctx->grad,
                       &ctx->loss_partials, &ctx->loss_planes, &ctx->sort_keys_b, &ctx->sort_vals_b,
-                      &ctx->tile_order,
+                      &ctx->tile_order, &ctx->isect_mask,
                       &ctx->ref_rows,      &ctx->ref_ids,     &ctx->ref_offsets, &ctx->ref_grad,
                       &ctx->bounds_tmp};
     for (DevBuf* b : bufs) release(ctx, *b);
@@ -177,7 +177,7 @@ bsx_status bsx_trim(bsx_ctx* ctx) {
                       &ctx->image_packed, &ctx->visible, &ctx->max_radius, &ctx->sort_tmp_k, &ctx->sort_tmp_v,
                       &ctx->sort_hist, &ctx->sort_lookback, &ctx->scan_status, &ctx->scalars, &ctx->grad,
                       &ctx->loss_partials, &ctx->loss_planes, &ctx->sort_keys_b, &ctx->sort_vals_b,
-                      &ctx->tile_order,
+                      &ctx->tile_order, &ctx->isect_mask,
                       &ctx->ref_rows,      &ctx->ref_ids,     &ctx->ref_offsets, &ctx->ref_grad,
                       &ctx->bounds_tmp};
     for (DevBuf* b : bufs) release(ctx, *b);

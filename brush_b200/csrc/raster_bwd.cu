@@ -38,6 +38,7 @@ struct BwdArgs {
     const float* image;     // [H,W,4]
     const float* v_output;  // [H,W,4]
     float* v_grad;          // [N,12]
+    const uint8_t* isect_mask;  // [M] band masks the forward computed for these ranges, or null: compute them
     const uint32_t* order;  // launch order of the tiles (block b replays tile order[b])
     uint32_t tbw, num_tiles, w, h;
     float bg_r, bg_g, bg_b;
@@ -225,7 +226,11 @@ __global__ void __launch_bounds__(kBwdPixThreads, 8) raster_bwd_kernel(const Bwd
             s_c[threadIdx.x] = make_float2(bsx_max(rc.x, 0.0f), rc.z + margin);
             if (REFINE) s_d[threadIdx.x] = make_float4(ra.z * wf, ra.w * wf, ra.w * hf, rb.x * hf);
             const uint32_t gates = (rb.z >= 0.0f ? 256u : 0u) | (rb.w >= 0.0f ? 512u : 0u) | (rc.x >= 0.0f ? 1024u : 0u);
-            s_mask[threadIdx.x] = warp_visit_mask(ra.x, ra.y, ra.z, ra.w, rb.x, rc.z + margin, ox, oy) | gates;
+            // the forward's masks of these indices (same splat rows, tile, margin and
+            // arithmetic), when it left them
+            const uint32_t vm = a.isect_mask ? (uint32_t)__ldg(a.isect_mask + batch + threadIdx.x)
+                                             : warp_visit_mask(ra.x, ra.y, ra.z, ra.w, rb.x, rc.z + margin, ox, oy);
+            s_mask[threadIdx.x] = vm | gates;
             s_gid[threadIdx.x] = g;
 #pragma unroll
             for (int k = 0; k <= kGradLanes; ++k) s_grad[threadIdx.x][k] = 0.0f;
@@ -234,7 +239,6 @@ __global__ void __launch_bounds__(kBwdPixThreads, 8) raster_bwd_kernel(const Bwd
         for (uint32_t t = 0; t < n; ++t) {
             const uint32_t bands = (s_mask[t] >> wshift) & 3u;       // warp-uniform
             if (!bands) continue;
-            if (__all_sync(0xffffffffu, PA.done && PB.done)) break;  // warp-uniform
             const float4 A = s_a[t];
             const float4 B = s_b[t];
             const float2 Cc = s_c[t];
@@ -254,6 +258,8 @@ __global__ void __launch_bounds__(kBwdPixThreads, 8) raster_bwd_kernel(const Bwd
             if (__any_sync(0xffffffffu, contrib)) {
                 const float tot = warp_sum10(gv, lane);
                 if (!(lane & 1) && sum_idx < kGradLanes) atomicAdd(&s_grad[t][sum_idx], tot);
+            } else if (__all_sync(0xffffffffu, PA.done && PB.done)) {
+                break;  // warp-uniform: a finished pixel never contributes, so this is tested only here
             }
         }
         __syncthreads();
@@ -285,7 +291,8 @@ __global__ void __launch_bounds__(kBwdPixThreads, 8) raster_bwd_kernel(const Bwd
 
 bsx_status launch_raster_bwd(bsx_ctx* ctx, const uint32_t* isect_gid, const uint32_t* tile_offsets,
                              const float* projected, const float* image, const float* v_output, float* v_grad,
-                             const bsx_project_uniforms& u, const float bg[3], int smooth, int refine) {
+                             const uint8_t* isect_mask, const bsx_project_uniforms& u, const float bg[3], int smooth,
+                             int refine) {
     BwdArgs a;
     a.isect_gid = isect_gid;
     a.tile_offsets = tile_offsets;
@@ -293,6 +300,7 @@ bsx_status launch_raster_bwd(bsx_ctx* ctx, const uint32_t* isect_gid, const uint
     a.image = image;
     a.v_output = v_output;
     a.v_grad = v_grad;
+    a.isect_mask = isect_mask;
     a.tbw = u.tile_bw;
     a.num_tiles = u.tile_bw * u.tile_bh;
     a.w = u.img_w;

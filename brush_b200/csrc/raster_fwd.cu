@@ -34,6 +34,7 @@ struct FwdArgs {
     float* image;            // [H,W,4] when bwd_info
     uint32_t* image_packed;  // [H,W] otherwise
     float* visible;          // [N] when bwd_info
+    uint8_t* isect_mask;     // [M] when bwd_info: each staged intersection's warp band mask, for the backward
     const uint32_t* order;   // launch order of the tiles (block b renders tile order[b])
     uint32_t tbw, w, h;
     float bg_r, bg_g, bg_b;
@@ -81,9 +82,10 @@ __global__ void __launch_bounds__(kFwdThreads) raster_fwd_kernel(const FwdArgs a
             s_a[threadIdx.x] = ra;
             s_b[threadIdx.x] = make_float4(0.5f * rb.x, rb.y, bsx_max(rb.z, 0.0f), bsx_max(rb.w, 0.0f));
             s_c[threadIdx.x] = make_float2(bsx_max(rc.x, 0.0f), rc.z + margin);
-            s_mask[threadIdx.x] =
-                warp_visit_mask(ra.x, ra.y, ra.z, ra.w, rb.x, rc.z + margin, tx * kTile, ty * kTile);
+            const uint32_t vm = warp_visit_mask(ra.x, ra.y, ra.z, ra.w, rb.x, rc.z + margin, tx * kTile, ty * kTile);
+            s_mask[threadIdx.x] = vm;
             if (BWD) {
+                a.isect_mask[batch + threadIdx.x] = (uint8_t)vm;
                 s_gid[threadIdx.x] = g;
                 s_used[threadIdx.x] = 0;
             }
@@ -170,8 +172,8 @@ __global__ void __launch_bounds__(kFwdThreads) raster_fwd_kernel(const FwdArgs a
 }  // namespace
 
 bsx_status launch_raster_fwd(bsx_ctx* ctx, const uint32_t* isect_gid, uint32_t* tile_offsets, const float* projected,
-                             float* image, uint32_t* image_packed, float* visible, const bsx_project_uniforms& u,
-                             const float bg[3], int bwd_info, int smooth) {
+                             float* image, uint32_t* image_packed, float* visible, uint8_t* isect_mask,
+                             const bsx_project_uniforms& u, const float bg[3], int bwd_info, int smooth) {
     FwdArgs a;
     a.isect_gid = isect_gid;
     a.tile_offsets = tile_offsets;
@@ -179,6 +181,7 @@ bsx_status launch_raster_fwd(bsx_ctx* ctx, const uint32_t* isect_gid, uint32_t* 
     a.image = image;
     a.image_packed = image_packed;
     a.visible = visible;
+    a.isect_mask = isect_mask;
     a.tbw = u.tile_bw;
     a.w = u.img_w;
     a.h = u.img_h;

@@ -22,11 +22,12 @@ bsx_status launch_emit(bsx_ctx* ctx, const float* projected, const uint32_t* dep
                        uint32_t num_visible, uint32_t tbw, uint32_t tbh, uint32_t* tile_out, uint32_t* gid_out,
                        uint32_t num_isect);
 bsx_status launch_raster_fwd(bsx_ctx* ctx, const uint32_t* isect_gid, uint32_t* tile_offsets, const float* projected,
-                             float* image, uint32_t* image_packed, float* visible, const bsx_project_uniforms& u,
-                             const float bg[3], int bwd_info, int smooth);
+                             float* image, uint32_t* image_packed, float* visible, uint8_t* isect_mask,
+                             const bsx_project_uniforms& u, const float bg[3], int bwd_info, int smooth);
 bsx_status launch_raster_bwd(bsx_ctx* ctx, const uint32_t* isect_gid, const uint32_t* tile_offsets,
                              const float* projected, const float* image, const float* v_output, float* v_grad,
-                             const bsx_project_uniforms& u, const float bg[3], int smooth, int refine);
+                             const uint8_t* isect_mask, const bsx_project_uniforms& u, const float bg[3], int smooth,
+                             int refine);
 bsx_status launch_project_bwd(bsx_ctx* ctx, const bsx_project_uniforms& uni, const float* transforms, const float* sh,
                               const float* raw_opac, uint32_t n, uint32_t coeffs, int degree, int mip,
                               const float* v_grad, float* v_transforms, float* v_sh, float* v_opac, float* v_refine,
@@ -139,6 +140,7 @@ bsx_status bsx_render_fwd(bsx_ctx* ctx, const bsx_camera* cam, uint32_t w, uint3
     BSX_TRY(ensure(ctx, ctx->sort_vals_b, mm * 4));
     BSX_TRY(ensure(ctx, ctx->isect_tile, mm * 4));
     BSX_TRY(ensure(ctx, ctx->isect_gid, mm * 4));
+    if (bwd_info) BSX_TRY(ensure(ctx, ctx->isect_mask, mm));
     uint32_t* depth_order = ctx->depth_order.as<uint32_t>();
     if (V) {
         BSX_TRY(radix_sort_pairs(ctx, ctx->depth_keys.as<uint32_t>(), ctx->vis_gid.as<uint32_t>(), V, 32,
@@ -157,7 +159,8 @@ bsx_status bsx_render_fwd(bsx_ctx* ctx, const bsx_camera* cam, uint32_t w, uint3
     BSX_TRY(launch_raster_fwd(ctx, ctx->isect_gid.as<uint32_t>(), ctx->tile_offsets.as<uint32_t>(),
                               ctx->projected.as<float>(), bwd_info ? ctx->image.as<float>() : nullptr,
                               bwd_info ? nullptr : ctx->image_packed.as<uint32_t>(),
-                              bwd_info ? ctx->visible.as<float>() : nullptr, uni, background, bwd_info, smooth));
+                              bwd_info ? ctx->visible.as<float>() : nullptr,
+                              bwd_info ? ctx->isect_mask.as<uint8_t>() : nullptr, uni, background, bwd_info, smooth));
 
     uni.num_visible = V;
     std::memset(out, 0, sizeof *out);
@@ -210,8 +213,8 @@ bsx_status bsx_rasterize_bwd(bsx_ctx* ctx, const float* d_v_output, int32_t comp
     BSX_TRY(check_cuda(ctx, cudaMemsetAsync(d_v_combined, 0, nn * kGradStride * 4, ctx->stream), "memset v_combined"));
     if (f.num_intersections == 0) return BSX_OK;
     return launch_raster_bwd(ctx, ctx->isect_gid.as<uint32_t>(), ctx->tile_offsets.as<uint32_t>(),
-                             ctx->projected.as<float>(), ctx->image.as<float>(), d_v_output, d_v_combined, f.uni, f.bg,
-                             f.smooth, compute_refine_weight);
+                             ctx->projected.as<float>(), ctx->image.as<float>(), d_v_output, d_v_combined,
+                             ctx->isect_mask.as<uint8_t>(), f.uni, f.bg, f.smooth, compute_refine_weight);
 }
 
 bsx_status bsx_project_bwd(bsx_ctx* ctx, const float* d_v_combined, float* d_v_transforms, float* d_v_sh,
