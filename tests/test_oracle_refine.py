@@ -49,6 +49,43 @@ def test_sampler_first_draw_proportional_to_weight():
     assert chi2 < 16.3  # 3 dof, p = 0.001
 
 
+def _successive_subset_probs(w, k):
+    """Exact probability of every k-subset under successive weighted sampling without
+    replacement (each draw proportional to the remaining weights): the distribution of
+    rand::seq::index::sample_weighted, which the reference's multinomial_sample calls
+    (crates/brush-train/src/multinomial.rs:1-28), by Efraimidis & Spirakis (2006)."""
+    import itertools
+
+    total = float(sum(w))
+    probs = {}
+    for order in itertools.permutations(range(len(w)), k):
+        p, rest = 1.0, total
+        for i in order:
+            p *= float(w[i]) / rest
+            rest -= float(w[i])
+        key = tuple(sorted(order))
+        probs[key] = probs.get(key, 0.0) + p
+    return probs
+
+
+def test_sampler_subset_distribution_matches_successive_sampling():
+    """Draw-level parity with the reference's sampler is not possible (it runs StdRng);
+    its distribution is: the frequency of each 3-of-6 subset over many seeds against the
+    exact successive-sampling probabilities (chi-square, 19 degrees of freedom)."""
+    w = np.array([0.5, 1.0, 1.5, 2.0, 4.0, 8.0], np.float32)
+    probs = _successive_subset_probs(w, 3)
+    trials = 20000
+    counts = {key: 0 for key in probs}
+    for t in range(trials):
+        counts[tuple(sorted(orc.weighted_sample(w, 3, seed=t, stream=2).tolist()))] += 1
+    chi2 = sum((counts[key] - trials * p) ** 2 / (trials * p) for key, p in probs.items())
+    assert chi2 < 43.8  # 19 dof, p = 0.001
+    # inclusion frequency of the heaviest weight, against its exact value
+    inc = sum(p for key, p in probs.items() if 5 in key)
+    got = sum(c for key, c in counts.items() if 5 in key) / trials
+    assert abs(got - inc) < 4 * math.sqrt(inc * (1 - inc) / trials)
+
+
 def _scene(n=400, c=4, seed=0):
     rng = np.random.default_rng(seed)
     t = np.zeros((n, 10), np.float32)
