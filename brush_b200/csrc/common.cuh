@@ -154,7 +154,7 @@ struct bsx_ctx {
         image, image_packed, visible, max_radius, sort_tmp_k, sort_tmp_v, sort_hist, sort_lookback, scan_status,
         scalars, grad, loss_partials, loss_planes, sort_keys_b, sort_vals_b, tile_order, isect_mask,
         // reference-layout backward operators (ref_bwd.cu)
-        ref_rows, ref_ids, ref_offsets, ref_grad,
+        ref_rows, ref_ids, ref_offsets, ref_grad, ref_order,
         // percentile bounds of the means (bounds.cu)
         bounds_tmp;
     bsx_fwd_state fwd;

@@ -151,7 +151,7 @@ bsx_status bsx_destroy(bsx_ctx* ctx) {
                       &ctx->sort_hist, &ctx->sort_lookback, &ctx->scan_status, &ctx->scalars, &ctx->grad,
                       &ctx->loss_partials, &ctx->loss_planes, &ctx->sort_keys_b, &ctx->sort_vals_b,
                       &ctx->tile_order, &ctx->isect_mask,
-                      &ctx->ref_rows,      &ctx->ref_ids,     &ctx->ref_offsets, &ctx->ref_grad,
+                      &ctx->ref_rows,      &ctx->ref_ids,     &ctx->ref_offsets, &ctx->ref_grad, &ctx->ref_order,
                       &ctx->bounds_tmp};
     for (DevBuf* b : bufs) release(ctx, *b);
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
@@ -178,7 +178,7 @@ bsx_status bsx_trim(bsx_ctx* ctx) {
                       &ctx->sort_hist, &ctx->sort_lookback, &ctx->scan_status, &ctx->scalars, &ctx->grad,
                       &ctx->loss_partials, &ctx->loss_planes, &ctx->sort_keys_b, &ctx->sort_vals_b,
                       &ctx->tile_order, &ctx->isect_mask,
-                      &ctx->ref_rows,      &ctx->ref_ids,     &ctx->ref_offsets, &ctx->ref_grad,
+                      &ctx->ref_rows,      &ctx->ref_ids,     &ctx->ref_offsets, &ctx->ref_grad, &ctx->ref_order,
                       &ctx->bounds_tmp};
     for (DevBuf* b : bufs) release(ctx, *b);
     ctx->fwd.valid = 0;

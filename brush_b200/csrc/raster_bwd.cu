@@ -291,8 +291,8 @@ __global__ void __launch_bounds__(kBwdPixThreads, 8) raster_bwd_kernel(const Bwd
 
 bsx_status launch_raster_bwd(bsx_ctx* ctx, const uint32_t* isect_gid, const uint32_t* tile_offsets,
                              const float* projected, const float* image, const float* v_output, float* v_grad,
-                             const uint8_t* isect_mask, const bsx_project_uniforms& u, const float bg[3], int smooth,
-                             int refine) {
+                             const uint8_t* isect_mask, const uint32_t* order, const bsx_project_uniforms& u,
+                             const float bg[3], int smooth, int refine) {
     BwdArgs a;
     a.isect_gid = isect_gid;
     a.tile_offsets = tile_offsets;
@@ -309,11 +309,16 @@ bsx_status launch_raster_bwd(bsx_ctx* ctx, const uint32_t* isect_gid, const uint
     a.bg_g = bg[1];
     a.bg_b = bg[2];
     const uint32_t blocks = a.num_tiles;
-    // launch order from the tile ranges as the forward shortened them
-    bsx_status s = ensure(ctx, ctx->tile_order, (size_t)blocks * 4);
-    if (s == BSX_OK) s = tile_order(ctx, tile_offsets, blocks, ctx->tile_order.as<uint32_t>());
-    if (s != BSX_OK) return s;
-    a.order = ctx->tile_order.as<uint32_t>();
+    // launch order: the forward's (heaviest tiles first) when given, else from
+    // these ranges into the operator's own buffer (the forward's order stays intact)
+    if (order) {
+        a.order = order;
+    } else {
+        bsx_status s = ensure(ctx, ctx->ref_order, (size_t)blocks * 4);
+        if (s == BSX_OK) s = tile_order(ctx, tile_offsets, blocks, ctx->ref_order.as<uint32_t>());
+        if (s != BSX_OK) return s;
+        a.order = ctx->ref_order.as<uint32_t>();
+    }
     prof_begin(ctx);
     if (smooth) {
         if (refine) raster_bwd_kernel<true, true><<<blocks, kBwdPixThreads, 0, ctx->stream>>>(a);

@@ -28,8 +28,8 @@ namespace bsx {
 
 bsx_status launch_raster_bwd(bsx_ctx* ctx, const uint32_t* isect_gid, const uint32_t* tile_offsets,
                              const float* projected, const float* image, const float* v_output, float* v_grad,
-                             const uint8_t* isect_mask, const bsx_project_uniforms& u, const float bg[3], int smooth,
-                             int refine);
+                             const uint8_t* isect_mask, const uint32_t* order, const bsx_project_uniforms& u,
+                             const float bg[3], int smooth, int refine);
 bsx_status launch_project_bwd(bsx_ctx* ctx, const bsx_project_uniforms& uni, const float* transforms, const float* sh,
                               const float* raw_opac, uint32_t n, uint32_t coeffs, int degree, int mip,
                               const float* v_grad, float* v_transforms, float* v_sh, float* v_opac, float* v_refine,
@@ -172,7 +172,8 @@ bsx_status bsx_rasterize_bwd_ref(bsx_ctx* ctx, const float* d_out_img, const flo
                    "memset gradient rows");
     if (s != BSX_OK) return s;
     s = launch_raster_bwd(ctx, ctx->ref_ids.as<uint32_t>(), ctx->ref_offsets.as<uint32_t>(), ctx->ref_rows.as<float>(),
-                          d_out_img, d_v_output, ctx->ref_grad.as<float>(), nullptr, u, background, smooth_cutoff != 0,
+                          d_out_img, d_v_output, ctx->ref_grad.as<float>(), nullptr, nullptr, u, background,
+                          smooth_cutoff != 0,
                           compute_refine_weight != 0);
     if (s != BSX_OK) return s;
     prof_begin(ctx);

@@ -26,8 +26,8 @@ bsx_status launch_raster_fwd(bsx_ctx* ctx, const uint32_t* isect_gid, uint32_t* 
                              const bsx_project_uniforms& u, const float bg[3], int bwd_info, int smooth);
 bsx_status launch_raster_bwd(bsx_ctx* ctx, const uint32_t* isect_gid, const uint32_t* tile_offsets,
                              const float* projected, const float* image, const float* v_output, float* v_grad,
-                             const uint8_t* isect_mask, const bsx_project_uniforms& u, const float bg[3], int smooth,
-                             int refine);
+                             const uint8_t* isect_mask, const uint32_t* order, const bsx_project_uniforms& u,
+                             const float bg[3], int smooth, int refine);
 bsx_status launch_project_bwd(bsx_ctx* ctx, const bsx_project_uniforms& uni, const float* transforms, const float* sh,
                               const float* raw_opac, uint32_t n, uint32_t coeffs, int degree, int mip,
                               const float* v_grad, float* v_transforms, float* v_sh, float* v_opac, float* v_refine,
@@ -214,7 +214,8 @@ bsx_status bsx_rasterize_bwd(bsx_ctx* ctx, const float* d_v_output, int32_t comp
     if (f.num_intersections == 0) return BSX_OK;
     return launch_raster_bwd(ctx, ctx->isect_gid.as<uint32_t>(), ctx->tile_offsets.as<uint32_t>(),
                              ctx->projected.as<float>(), ctx->image.as<float>(), d_v_output, d_v_combined,
-                             ctx->isect_mask.as<uint8_t>(), f.uni, f.bg, f.smooth, compute_refine_weight);
+                             ctx->isect_mask.as<uint8_t>(), ctx->tile_order.as<uint32_t>(), f.uni, f.bg, f.smooth,
+                             compute_refine_weight);
 }
 
 bsx_status bsx_project_bwd(bsx_ctx* ctx, const float* d_v_combined, float* d_v_transforms, float* d_v_sh,
