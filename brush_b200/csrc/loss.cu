@@ -10,14 +10,13 @@
 // blurred again. Summation order matches the reference (taps d = 1..5 as
 // (left + right) * w[5-d], then the centre tap).
 //
-// The training form (loss_ssim_kernel, loss_grad_kernel) reads the
-// rasterizer's [H,W,4] image directly, handles the three colour channels in
-// one block, uses the constant chain 1/(3HW) of a mean reduction, writes the
-// gradient straight into the [H,W,4] v_output layout the raster backward
-// consumes (alpha lane 0), and emits per-block loss sums that a tiny kernel
-// reduces in a fixed order. This removes the reference's permute/contiguous
-// copies, the separate mean kernel and the zero-fill of the gradient image.
-// Its blur taps
+// The training form (loss_ssim_kernel, loss_grad_kernel; loss_l1_fused_kernel
+// when the SSIM weight is 0) reads the rasterizer's [H,W,4] image directly,
+// uses the constant chain 1/(3HW) of a mean reduction, writes the gradient
+// straight into the [H,W,4] v_output layout the raster backward consumes
+// (alpha lane 0), and emits per-block loss sums that a tiny kernel reduces in
+// a fixed order. This removes the reference's permute/contiguous copies, the
+// separate mean kernel and the zero-fill of the gradient image. Its blur taps
 // accumulate by fused multiply-adds (same tap order; the loss map and gradient
 // are checked against the CPU restatement to 1e-5 relative, not bit for bit),
 // and this file is the one the build compiles with multiply-add contraction:
