@@ -8,12 +8,12 @@
 // (same float operations, so T and every accept / early-out decision match the
 // forward bit-for-bit), carrying the residual colour C - T_final*bg - (front
 // contributions) as the reference does, folded into one scalar (its dot
-// product with the pixel's output gradient). Per splat, a warp that
-// none of the splat's acceptable pixels reach (the forward's exact footprint
-// test per row band, raster_common.cuh) skips it uniformly, and a warp skips
-// the pixel step of a band the splat cannot reach; otherwise each lane forms
-// its pixels' contribution to the splat's 10
-// gradient lanes, the warp sums them with a 10-value butterfly (12 shuffles),
+// product with the pixel's output gradient). Each warp visits only the staged
+// splats that reach one of its two row bands (the forward's exact footprint
+// test per band, kept from the forward as one byte per intersection; the list
+// is built once per batch, raster_common.cuh), and skips the pixel step of a
+// band the splat cannot reach; each lane forms its pixels' contribution to the
+// splat's 10 gradient lanes, the warp sums them with a 10-value butterfly (12 shuffles),
 // the sums are accumulated per splat in shared memory across the tile's 4
 // warps, and each (splat, tile) leaves with three 16-byte vector atomics
 // (red.global.add.v4.f32) into a 12-lane row.
@@ -195,6 +195,7 @@ __global__ void __launch_bounds__(kBwdPixThreads, 8) raster_bwd_kernel(const Bwd
     __shared__ float2 s_c[kBwdPixThreads];  // max(b,0), ln(255 o) + margin
     __shared__ float4 s_d[REFINE ? kBwdPixThreads : 1];  // refine rows (c00 w, c01 w, c01 h, c11 h)
     __shared__ uint32_t s_mask[kBwdPixThreads];  // bits 0-7 warp row bands, 8-10 colour gates
+    __shared__ uint8_t s_list[kBwdPixThreads / 32][kBwdPixThreads];  // per warp: the staged splats it visits
     __shared__ uint32_t s_gid[kBwdPixThreads];
     __shared__ float s_grad[kBwdPixThreads][kGradLanes + 1];
 
@@ -236,9 +237,11 @@ __global__ void __launch_bounds__(kBwdPixThreads, 8) raster_bwd_kernel(const Bwd
             for (int k = 0; k <= kGradLanes; ++k) s_grad[threadIdx.x][k] = 0.0f;
         }
         __syncthreads();
-        for (uint32_t t = 0; t < n; ++t) {
-            const uint32_t bands = (s_mask[t] >> wshift) & 3u;       // warp-uniform
-            if (!bands) continue;
+        uint8_t* list = s_list[warp];
+        const uint32_t nvis = warp_visit_list<kBwdPixThreads>(s_mask, n, wshift, list);
+        for (uint32_t i = 0; i < nvis; ++i) {
+            const uint32_t t = list[i];
+            const uint32_t bands = (s_mask[t] >> wshift) & 3u;  // warp-uniform, non-zero
             const float4 A = s_a[t];
             const float4 B = s_b[t];
             const float2 Cc = s_c[t];

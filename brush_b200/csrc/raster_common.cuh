@@ -97,4 +97,28 @@ __device__ __forceinline__ uint32_t warp_visit_mask(float sx, float sy, float c0
     return mask;
 }
 
+// The staged splats of a batch (indices t < n) that reach one of this warp's
+// two row bands (its two bits at `wshift` in s_mask), in staging order: written
+// to `list`, their count returned (warp-uniform). The warp then visits only
+// these, instead of testing every staged splat's bits in its visit loop.
+template <int kBatch>
+__device__ __forceinline__ uint32_t warp_visit_list(const uint32_t* s_mask, uint32_t n, uint32_t wshift,
+                                                    uint8_t* list) {
+    static_assert(kBatch <= 256, "8-bit list entries");
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint32_t below = (1u << lane) - 1u;
+    uint32_t cnt = 0;
+#pragma unroll
+    for (uint32_t c = 0; c < (uint32_t)kBatch; c += 32) {
+        if (c >= n) break;  // warp-uniform
+        const uint32_t t = c + lane;
+        const bool hit = t < n && ((s_mask[t] >> wshift) & 3u) != 0u;
+        const uint32_t bal = __ballot_sync(0xffffffffu, hit);
+        if (hit) list[cnt + __popc(bal & below)] = (uint8_t)t;
+        cnt += __popc(bal);
+    }
+    __syncwarp();
+    return cnt;
+}
+
 }  // namespace bsx

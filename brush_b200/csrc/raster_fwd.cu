@@ -10,9 +10,11 @@
 // B200 specifics: the block-wide early-out is a __syncthreads_count vote;
 // while a batch is staged, each splat gets a mask of the warp row bands whose
 // pixels it can reach (exact minimum of sigma over each band's 8x4 footprint),
-// so a warp skips splats none of its pixels can accept (a per-pixel band test
-// measured no faster here: the sigma test already rejects those pixels
-// cheaply); pairs whose sigma
+// and each warp then visits only the splats that reach one of its bands, from
+// a list built once per batch by ballots (a per-pixel band test measured no
+// faster here: the sigma test already rejects those pixels cheaply); the
+// training pass keeps each mask (one byte per staged intersection) for the
+// backward; pairs whose sigma
 // exceeds ln(255*o) + margin (where alpha < 1/255 is certain) skip the
 // exponential; colours are clamped once per splat while staging. sigma is
 // evaluated with fused products (bsx_raster_sigma), e^-sigma by the bounded-
@@ -50,6 +52,7 @@ __global__ void __launch_bounds__(kFwdThreads) raster_fwd_kernel(const FwdArgs a
     __shared__ float4 s_b[kFwdThreads];  // c11 / 2, opacity, max(r,0), max(g,0)
     __shared__ float2 s_c[kFwdThreads];  // max(b,0), ln(255 o) + margin
     __shared__ uint32_t s_mask[kFwdThreads];
+    __shared__ uint8_t s_list[kFwdThreads / 32][kFwdThreads];  // per warp: the staged splats it visits
     __shared__ uint32_t s_gid[BWD ? kFwdThreads : 1];
     __shared__ int s_used[BWD ? kFwdThreads : 1];
     __shared__ uint32_t s_max_useful;
@@ -91,9 +94,10 @@ __global__ void __launch_bounds__(kFwdThreads) raster_fwd_kernel(const FwdArgs a
             }
         }
         __syncthreads();
-        for (uint32_t t = 0; t < n && !(doneA && doneB); ++t) {
-            const uint32_t bands = (s_mask[t] >> wshift) & 3u;  // warp-uniform
-            if (!bands) continue;
+        uint8_t* list = s_list[threadIdx.x >> 5];
+        const uint32_t nvis = warp_visit_list<kFwdThreads>(s_mask, n, wshift, list);
+        for (uint32_t i = 0; i < nvis && !(doneA && doneB); ++i) {
+            const uint32_t t = list[i];
             const float4 A = s_a[t];
             const float hc11 = s_b[t].x;
             const float thr = s_c[t].y;
