@@ -123,6 +123,16 @@ __global__ void __launch_bounds__(kProjThreads, 4) project_fwd_kernel(const __gr
         } while (false);
     }
 
+    // The visible splat's SH row (12 C bytes) starts towards L2 now and is read
+    // after the walk below.
+    if (visible) {
+        constexpr uint32_t kRowBytes = (DEG + 1) * (DEG + 1) * 12;
+        const char* srow = reinterpret_cast<const char*>(a.sh + (size_t)g * ((DEG + 1) * (DEG + 1) * 3));
+#pragma unroll
+        for (uint32_t off = 0; off < kRowBytes; off += 128)
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(srow + off));
+    }
+
     // Contributing-tile count: the warp walks its splats' boxes together.
     uint32_t hits = 0;
     warp_tile_walk(ws, [&](const WalkStep& s) { hits += s.own; });

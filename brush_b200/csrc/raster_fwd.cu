@@ -45,16 +45,21 @@ struct FwdArgs {
 // Two pixels per thread: Morton index t < 128 gives (x, y) with y < 8, and
 // the thread also owns (x, y + 8). Both share dx and its products.
 constexpr int kFwdThreads = 128;
+// Splats staged per batch (a multiple of the block size): each thread stages
+// kFwdBatch / kFwdThreads of them (256: fewer barriers per splat, measured 1.5 %
+// faster than 128 here; the backward keeps 128, where 256 measured slower).
+constexpr int kFwdBatch = 256;
+static_assert(kFwdBatch % kFwdThreads == 0 && kFwdBatch <= 256, "whole rounds, 8-bit list entries");
 
 template <bool BWD, bool SMOOTH>
 __global__ void __launch_bounds__(kFwdThreads) raster_fwd_kernel(const FwdArgs a) {
-    __shared__ float4 s_a[kFwdThreads];  // x, y, c00, c01
-    __shared__ float4 s_b[kFwdThreads];  // c11 / 2, opacity, max(r,0), max(g,0)
-    __shared__ float2 s_c[kFwdThreads];  // max(b,0), ln(255 o) + margin
-    __shared__ uint32_t s_mask[kFwdThreads];
-    __shared__ uint8_t s_list[kFwdThreads / 32][kFwdThreads];  // per warp: the staged splats it visits
-    __shared__ uint32_t s_gid[BWD ? kFwdThreads : 1];
-    __shared__ int s_used[BWD ? kFwdThreads : 1];
+    __shared__ float4 s_a[kFwdBatch];  // x, y, c00, c01
+    __shared__ float4 s_b[kFwdBatch];  // c11 / 2, opacity, max(r,0), max(g,0)
+    __shared__ float2 s_c[kFwdBatch];  // max(b,0), ln(255 o) + margin
+    __shared__ uint32_t s_mask[kFwdBatch];
+    __shared__ uint8_t s_list[kFwdThreads / 32][kFwdBatch];  // per warp: the staged splats it visits
+    __shared__ uint32_t s_gid[BWD ? kFwdBatch : 1];
+    __shared__ int s_used[BWD ? kFwdBatch : 1];
     __shared__ uint32_t s_max_useful;
 
     const uint32_t tile = __ldg(a.order + blockIdx.x);
@@ -75,27 +80,30 @@ __global__ void __launch_bounds__(kFwdThreads) raster_fwd_kernel(const FwdArgs a
     uint32_t last = lo;
     const float margin = SMOOTH ? kMarginSmooth : kMarginHard;
 
-    for (uint32_t batch = lo; batch < hi; batch += kFwdThreads) {
+    for (uint32_t batch = lo; batch < hi; batch += kFwdBatch) {
         if (__syncthreads_count(doneA && doneB) == kFwdThreads) break;
-        const uint32_t n = min((uint32_t)kFwdThreads, hi - batch);
-        if (threadIdx.x < n) {
-            const uint32_t g = __ldg(a.isect_gid + batch + threadIdx.x);
+        const uint32_t n = min((uint32_t)kFwdBatch, hi - batch);
+#pragma unroll
+        for (int u = 0; u < kFwdBatch / kFwdThreads; ++u) {
+            const uint32_t j = threadIdx.x + u * kFwdThreads;
+            if (j >= n) break;
+            const uint32_t g = __ldg(a.isect_gid + batch + j);
             const float4* row = reinterpret_cast<const float4*>(a.projected + (size_t)g * BSX_PROJECTED_LANES);
             const float4 ra = __ldg(row), rb = __ldg(row + 1), rc = __ldg(row + 2);
-            s_a[threadIdx.x] = ra;
-            s_b[threadIdx.x] = make_float4(0.5f * rb.x, rb.y, bsx_max(rb.z, 0.0f), bsx_max(rb.w, 0.0f));
-            s_c[threadIdx.x] = make_float2(bsx_max(rc.x, 0.0f), rc.z + margin);
+            s_a[j] = ra;
+            s_b[j] = make_float4(0.5f * rb.x, rb.y, bsx_max(rb.z, 0.0f), bsx_max(rb.w, 0.0f));
+            s_c[j] = make_float2(bsx_max(rc.x, 0.0f), rc.z + margin);
             const uint32_t vm = warp_visit_mask(ra.x, ra.y, ra.z, ra.w, rb.x, rc.z + margin, tx * kTile, ty * kTile);
-            s_mask[threadIdx.x] = vm;
+            s_mask[j] = vm;
             if (BWD) {
-                a.isect_mask[batch + threadIdx.x] = (uint8_t)vm;
-                s_gid[threadIdx.x] = g;
-                s_used[threadIdx.x] = 0;
+                a.isect_mask[batch + j] = (uint8_t)vm;
+                s_gid[j] = g;
+                s_used[j] = 0;
             }
         }
         __syncthreads();
         uint8_t* list = s_list[threadIdx.x >> 5];
-        const uint32_t nvis = warp_visit_list<kFwdThreads>(s_mask, n, wshift, list);
+        const uint32_t nvis = warp_visit_list<kFwdBatch>(s_mask, n, wshift, list);
         for (uint32_t i = 0; i < nvis && !(doneA && doneB); ++i) {
             const uint32_t t = list[i];
             const float4 A = s_a[t];
@@ -145,7 +153,11 @@ __global__ void __launch_bounds__(kFwdThreads) raster_fwd_kernel(const FwdArgs a
         }
         if (BWD) {
             __syncthreads();
-            if (threadIdx.x < n && s_used[threadIdx.x]) a.visible[s_gid[threadIdx.x]] = 1.0f;
+#pragma unroll
+            for (int u = 0; u < kFwdBatch / kFwdThreads; ++u) {
+                const uint32_t j = threadIdx.x + u * kFwdThreads;
+                if (j < n && s_used[j]) a.visible[s_gid[j]] = 1.0f;
+            }
         }
     }
 
