@@ -185,11 +185,11 @@ __device__ __forceinline__ bool pixel_step(PixelBwd& P, float dx0, float hxx, fl
 // Two pixels per thread (rows y and y + 8 of the tile), 128 threads per tile.
 constexpr int kBwdPixThreads = 128;
 
-// Bounded to 64 registers (eight resident blocks per SM, no spills): measured
-// faster than the unbounded 68-72 registers at seven blocks, and than nine
-// blocks at 56 registers (which spills; 6 % slower).
+// Bounded to 56 registers (nine resident blocks per SM; the refine variant
+// spills 8 bytes): with the per-warp visit lists this measured 2 % faster than
+// 64 registers at eight blocks (before the lists, nine blocks were 6 % slower).
 template <bool SMOOTH, bool REFINE>
-__global__ void __launch_bounds__(kBwdPixThreads, 8) raster_bwd_kernel(const BwdArgs a) {
+__global__ void __launch_bounds__(kBwdPixThreads, 9) raster_bwd_kernel(const BwdArgs a) {
     __shared__ float4 s_a[kBwdPixThreads];  // x, y, c00, c01
     __shared__ float4 s_b[kBwdPixThreads];  // c11, opacity, max(r,0), max(g,0)
     __shared__ float2 s_c[kBwdPixThreads];  // max(b,0), ln(255 o) + margin
