@@ -133,14 +133,16 @@ def kernel_bytes(name, N, V, M, Mp, P, T, C, W=1, fused_adam=False):
         "emit_kernel": V * (4 + 48 + 8) + 8 * M,
         "tile_offsets_kernel": 8 * M + 8 * T,
         "tile_order_kernel": 16 * T + 4 * T,  # ranges read twice, order written
-        "raster_fwd_kernel": 52 * Mp + 16 * P + 8 * T + 4 * V,
+        # + Mp: the training pass stores each staged intersection's band mask (1 B),
+        # which the backward reads
+        "raster_fwd_kernel": 52 * Mp + 16 * P + 8 * T + 4 * V + Mp,
         # SSIM pass: image + ground truth in, nine partial planes out; gradient pass:
         # the planes, image and ground truth in, the gradient image out
         "loss_ssim_kernel": 20 * P + 36 * P,
         "loss_grad_kernel": 36 * P + 20 * P + 16 * P,
         "loss_l1_fused_kernel": 36 * P,
         "loss_mean_kernel": 0,
-        "raster_bwd_kernel": 32 * P + 52 * Mp + 48 * V,
+        "raster_bwd_kernel": 32 * P + 52 * Mp + 48 * V + Mp,
         "project_bwd_kernel": 48 * N + V * (44 + 12 * C) + N * (48 + 12 * C),
         "adam_kernel": (316 + 60 * C) * N,
         "gather_stats_kernel": 36 * N,
